@@ -1,0 +1,130 @@
+// Shared helpers for the sm_100a kernels: status handling, launch geometry, the hash-grid
+// index math and the reference's PCG32 generator.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "ngp_b200.h"
+
+namespace ngp {
+
+// ---- status --------------------------------------------------------------------------------
+void set_error(const std::string& message);
+void clear_error();
+
+inline int fail(int code, const std::string& message) {
+    set_error(message);
+    return code;
+}
+
+inline int check_launch(const char* what) {
+    const cudaError_t status = cudaGetLastError();
+    if (status != cudaSuccess) return fail(NGP_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(status));
+    return NGP_OK;
+}
+
+inline int check_cuda(cudaError_t status, const char* what) {
+    if (status != cudaSuccess) return fail(NGP_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(status));
+    return NGP_OK;
+}
+
+#define NGP_TRY(expr)                        \
+    do {                                     \
+        const int ngp_status_ = (expr);      \
+        if (ngp_status_ != NGP_OK) return ngp_status_; \
+    } while (0)
+
+inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+// Number of SMs of the current device (148 on B200), cached per process.
+int sm_count();
+
+// ---- hash grid -----------------------------------------------------------------------------
+// Kernel-parameter copy of ngp_grid_layout (only what the device needs).
+struct GridParams {
+    uint32_t n_levels;
+    uint32_t offsets[NGP_MAX_LEVELS + 1];
+    uint32_t resolution[NGP_MAX_LEVELS];
+    float scale[NGP_MAX_LEVELS];
+};
+
+inline GridParams make_grid_params(const ngp_grid_layout& layout) {
+    GridParams p{};
+    p.n_levels = layout.n_levels;
+    for (uint32_t l = 0; l <= layout.n_levels; ++l) p.offsets[l] = layout.offsets[l];
+    for (uint32_t l = 0; l < layout.n_levels; ++l) {
+        p.resolution[l] = layout.resolution[l];
+        p.scale[l]      = layout.scale[l];
+    }
+    return p;
+}
+
+// Grid index of corner (x, y, z): dense x + y*r + z*r^2 while r <= 0x659 and r^3 fits the
+// level, otherwise the spatial hash x ^ y*2654435761 ^ z*805459861; then modulo the level size.
+// Same integer function as the reference's grid_index / coherent_prime_hash
+// (ngp.train.cu:165-186), which must be reproduced bit for bit.
+__device__ __forceinline__ uint32_t grid_index(uint32_t hashmap_size, uint32_t resolution, uint32_t x,
+                                               uint32_t y, uint32_t z) {
+    uint32_t index;
+    uint32_t stride;
+    if (resolution <= 0x659u) {
+        index  = x + y * resolution + z * (resolution * resolution);
+        stride = resolution * resolution * resolution;
+    } else {
+        index  = 0u;
+        stride = 0xFFFFFFFFu;
+    }
+    if (hashmap_size < stride) index = x ^ (y * 2654435761u) ^ (z * 805459861u);
+    return index % hashmap_size;
+}
+
+// ---- PCG32 ---------------------------------------------------------------------------------
+// The reference's PCG32 (ngp.train.cu:85-143): O'Neill's pcg32 (XSH-RR 64/32) with the
+// default stream constants and the LCG jump-ahead of Brown (1994).  All training randomness
+// must follow it exactly so that sample positions are bit-identical to the reference's.
+struct Pcg32 {
+    uint64_t state;
+    uint64_t inc;
+
+    __host__ __device__ explicit Pcg32(uint64_t initstate, uint64_t initseq = 1u) {
+        state = 0u;
+        inc   = (initseq << 1u) | 1u;
+        next_uint();
+        state += initstate;
+        next_uint();
+    }
+    __host__ __device__ uint32_t next_uint() {
+        const uint64_t old = state;
+        state              = old * 0x5851f42d4c957f2dULL + inc;
+        const uint32_t xs  = static_cast<uint32_t>(((old >> 18u) ^ old) >> 27u);
+        const uint32_t rot = static_cast<uint32_t>(old >> 59u);
+        return (xs >> rot) | (xs << ((~rot + 1u) & 31u));
+    }
+    __host__ __device__ float next_float() {
+        const uint32_t bits = (next_uint() >> 9u) | 0x3f800000u;
+        float value;
+        memcpy(&value, &bits, sizeof(value));
+        return value - 1.0f;
+    }
+    __host__ __device__ void advance(uint64_t delta) {
+        uint64_t cur_mult = 0x5851f42d4c957f2dULL, cur_plus = inc, acc_mult = 1u, acc_plus = 0u;
+        while (delta > 0u) {
+            if (delta & 1u) {
+                acc_mult *= cur_mult;
+                acc_plus = acc_plus * cur_mult + cur_plus;
+            }
+            cur_plus = (cur_mult + 1u) * cur_plus;
+            cur_mult *= cur_mult;
+            delta >>= 1u;
+        }
+        state = acc_mult * state + acc_plus;
+    }
+};
+
+constexpr uint64_t kTrainSeed = 1337u;
+
+}  // namespace ngp

@@ -1,0 +1,231 @@
+// Multiresolution hash-grid encoding, forward and backward, for sm_100a.
+//
+// Thread mapping is level-major: blockIdx.y selects the level, so every resident CTA of a
+// wave gathers from the same level's table and the coarse tables stay L1-resident while the
+// fine ones stream through L2 (the 24 MB table of the BASELINE configuration is L2-resident
+// on B200's 126 MB L2).  A corner's F features are one vector load (F=2: 32-bit half2,
+// F=4: 64-bit), taken through the non-coherent read-only path.  Each thread handles
+// POINTS_PER_THREAD points so that 8 * POINTS_PER_THREAD independent gathers are in flight.
+//
+// Forward follows encode_grid_forward_kernel (ngp.train.cu:876-921) with fp32 accumulation
+// (fmaf in corner order 0..7) instead of fp16 __hfma, rounded once to fp16.
+// Backward follows encode_grid_backward_kernel (ngp.train.cu:923-960) but scatters into an
+// fp32 gradient table with vector atomics (red.global.add.v2/v4.f32) instead of fp16 atomics.
+#include "common.cuh"
+
+namespace ngp {
+namespace {
+
+constexpr uint32_t kEncodeThreads = 256u;
+
+template <uint32_t F>
+struct FeatureVec;
+template <>
+struct FeatureVec<1> {
+    using type = __half;
+};
+template <>
+struct FeatureVec<2> {
+    using type = uint32_t;
+};
+template <>
+struct FeatureVec<4> {
+    using type = uint2;
+};
+template <>
+struct FeatureVec<8> {
+    using type = uint4;
+};
+
+template <uint32_t F>
+__device__ __forceinline__ void unpack(const typename FeatureVec<F>::type& v, float (&out)[F]) {
+    if constexpr (F == 1) {
+        out[0] = __half2float(v);
+    } else {
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (uint32_t k = 0; k < F / 2; ++k) {
+            const float2 f = __half22float2(h[k]);
+            out[2 * k]     = f.x;
+            out[2 * k + 1] = f.y;
+        }
+    }
+}
+
+// pos = fmaf(scale, x, 0.5); cell = floor(pos); frac = pos - cell (ngp.train.cu:188-193).
+__device__ __forceinline__ void position_fraction(float x, float scale, float& frac, uint32_t& cell) {
+    const float pos     = __fmaf_rn(scale, x, 0.5f);
+    const float floored = floorf(pos);
+    cell                = static_cast<uint32_t>(static_cast<int>(floored));
+    frac                = __fsub_rn(pos, floored);
+}
+
+template <uint32_t F, uint32_t PPT>
+__global__ void __launch_bounds__(kEncodeThreads) encode_forward_kernel(const uint32_t n, const float* __restrict__ coords,
+                                                                        const uint32_t coord_stride,
+                                                                        const __half* __restrict__ table,
+                                                                        __half* __restrict__ out, const uint32_t out_stride,
+                                                                        const __grid_constant__ GridParams grid) {
+    using Vec                    = typename FeatureVec<F>::type;
+    const uint32_t level         = blockIdx.y;
+    const uint32_t level_offset  = grid.offsets[level];
+    const uint32_t hashmap_size  = grid.offsets[level + 1] - level_offset;
+    const uint32_t resolution    = grid.resolution[level];
+    const float scale            = grid.scale[level];
+    const Vec* __restrict__ lvl  = reinterpret_cast<const Vec*>(table) + level_offset;
+    const uint32_t base          = blockIdx.x * (kEncodeThreads * PPT) + threadIdx.x;
+
+    float frac[PPT][3];
+    uint32_t cell[PPT][3];
+    bool valid[PPT];
+#pragma unroll
+    for (uint32_t p = 0; p < PPT; ++p) {
+        const uint32_t i = base + p * kEncodeThreads;
+        valid[p]         = i < n;
+        const float* c   = coords + static_cast<uint64_t>(valid[p] ? i : 0u) * coord_stride;
+#pragma unroll
+        for (uint32_t d = 0; d < 3; ++d) position_fraction(__ldg(c + d), scale, frac[p][d], cell[p][d]);
+    }
+
+    // Issue all 8 * PPT gathers before any arithmetic depends on them.
+    Vec v[PPT][8];
+#pragma unroll
+    for (uint32_t p = 0; p < PPT; ++p) {
+#pragma unroll
+        for (uint32_t corner = 0; corner < 8; ++corner) {
+            const uint32_t idx = grid_index(hashmap_size, resolution, cell[p][0] + (corner & 1u), cell[p][1] + ((corner >> 1) & 1u),
+                                            cell[p][2] + ((corner >> 2) & 1u));
+            v[p][corner]       = __ldg(lvl + idx);
+        }
+    }
+
+#pragma unroll
+    for (uint32_t p = 0; p < PPT; ++p) {
+        float acc[F];
+#pragma unroll
+        for (uint32_t f = 0; f < F; ++f) acc[f] = 0.0f;
+#pragma unroll
+        for (uint32_t corner = 0; corner < 8; ++corner) {
+            const float wx = (corner & 1u) ? frac[p][0] : __fsub_rn(1.0f, frac[p][0]);
+            const float wy = (corner & 2u) ? frac[p][1] : __fsub_rn(1.0f, frac[p][1]);
+            const float wz = (corner & 4u) ? frac[p][2] : __fsub_rn(1.0f, frac[p][2]);
+            const float w  = __fmul_rn(__fmul_rn(wx, wy), wz);
+            float val[F];
+            unpack<F>(v[p][corner], val);
+#pragma unroll
+            for (uint32_t f = 0; f < F; ++f) acc[f] = __fmaf_rn(w, val[f], acc[f]);
+        }
+        if (valid[p]) {
+            const uint32_t i = base + p * kEncodeThreads;
+#pragma unroll
+            for (uint32_t f = 0; f < F; ++f) out[static_cast<uint64_t>(level * F + f) * out_stride + i] = __float2half_rn(acc[f]);
+        }
+    }
+}
+
+template <uint32_t F>
+__device__ __forceinline__ void scatter_add(float* dst, const float (&g)[F]) {
+    if constexpr (F == 1) {
+        atomicAdd(dst, g[0]);
+    } else if constexpr (F == 2) {
+        atomicAdd(reinterpret_cast<float2*>(dst), make_float2(g[0], g[1]));
+    } else if constexpr (F == 4) {
+        atomicAdd(reinterpret_cast<float4*>(dst), make_float4(g[0], g[1], g[2], g[3]));
+    } else {
+        atomicAdd(reinterpret_cast<float4*>(dst), make_float4(g[0], g[1], g[2], g[3]));
+        atomicAdd(reinterpret_cast<float4*>(dst + 4), make_float4(g[4], g[5], g[6], g[7]));
+    }
+}
+
+template <uint32_t F>
+__global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const uint32_t n, const float* __restrict__ coords,
+                                                                         const uint32_t coord_stride,
+                                                                         const __half* __restrict__ dy, const uint32_t dy_stride,
+                                                                         float* __restrict__ table_grad,
+                                                                         const __grid_constant__ GridParams grid) {
+    const uint32_t i = blockIdx.x * kEncodeThreads + threadIdx.x;
+    if (i >= n) return;
+    const uint32_t level        = blockIdx.y;
+    const uint32_t level_offset = grid.offsets[level];
+    const uint32_t hashmap_size = grid.offsets[level + 1] - level_offset;
+    const uint32_t resolution   = grid.resolution[level];
+    const float scale           = grid.scale[level];
+    float* __restrict__ lvl     = table_grad + static_cast<uint64_t>(level_offset) * F;
+
+    float g[F];
+#pragma unroll
+    for (uint32_t f = 0; f < F; ++f) g[f] = __half2float(dy[static_cast<uint64_t>(level * F + f) * dy_stride + i]);
+
+    float frac[3];
+    uint32_t cell[3];
+    const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
+#pragma unroll
+    for (uint32_t d = 0; d < 3; ++d) position_fraction(__ldg(c + d), scale, frac[d], cell[d]);
+
+#pragma unroll
+    for (uint32_t corner = 0; corner < 8; ++corner) {
+        const float wx     = (corner & 1u) ? frac[0] : __fsub_rn(1.0f, frac[0]);
+        const float wy     = (corner & 2u) ? frac[1] : __fsub_rn(1.0f, frac[1]);
+        const float wz     = (corner & 4u) ? frac[2] : __fsub_rn(1.0f, frac[2]);
+        const float w      = __fmul_rn(__fmul_rn(wx, wy), wz);
+        const uint32_t idx = grid_index(hashmap_size, resolution, cell[0] + (corner & 1u), cell[1] + ((corner >> 1) & 1u), cell[2] + ((corner >> 2) & 1u));
+        float contrib[F];
+#pragma unroll
+        for (uint32_t f = 0; f < F; ++f) contrib[f] = __fmul_rn(w, g[f]);
+        scatter_add<F>(lvl + static_cast<uint64_t>(idx) * F, contrib);
+    }
+}
+
+int validate_layout(const ngp_grid_layout* layout) {
+    if (layout == nullptr) return fail(NGP_ERR_INVALID, "grid layout is null");
+    if (layout->n_levels == 0 || layout->n_levels > NGP_MAX_LEVELS) return fail(NGP_ERR_INVALID, "grid layout: bad level count");
+    const uint32_t F = layout->features_per_level;
+    if (F != 1 && F != 2 && F != 4 && F != 8) return fail(NGP_ERR_INVALID, "grid layout: features per level must be 1, 2, 4 or 8");
+    return NGP_OK;
+}
+
+}  // namespace
+
+}  // namespace ngp
+
+using namespace ngp;
+
+extern "C" int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n, const float* coords, uint32_t coord_stride,
+                                       const uint16_t* table, uint16_t* out, uint32_t out_stride, void* stream) {
+    clear_error();
+    NGP_TRY(validate_layout(layout));
+    if (n == 0) return NGP_OK;
+    if (coords == nullptr || table == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "encode forward: null pointer");
+    if (coord_stride < 3 || out_stride < n) return fail(NGP_ERR_INVALID, "encode forward: bad stride");
+    const GridParams grid = make_grid_params(*layout);
+    constexpr uint32_t ppt = 2;
+    const dim3 blocks((n + kEncodeThreads * ppt - 1) / (kEncodeThreads * ppt), layout->n_levels);
+    const auto* t = reinterpret_cast<const __half*>(table);
+    auto* o       = reinterpret_cast<__half*>(out);
+    switch (layout->features_per_level) {
+        case 1: encode_forward_kernel<1, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+        case 2: encode_forward_kernel<2, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+        case 4: encode_forward_kernel<4, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+        default: encode_forward_kernel<8, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+    }
+    return check_launch("encode_forward_kernel");
+}
+
+extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t n, const float* coords, uint32_t coord_stride,
+                                        const uint16_t* dy, uint32_t dy_stride, float* table_grad, void* stream) {
+    clear_error();
+    NGP_TRY(validate_layout(layout));
+    if (n == 0) return NGP_OK;
+    if (coords == nullptr || dy == nullptr || table_grad == nullptr) return fail(NGP_ERR_INVALID, "encode backward: null pointer");
+    if (coord_stride < 3 || dy_stride < n) return fail(NGP_ERR_INVALID, "encode backward: bad stride");
+    const GridParams grid = make_grid_params(*layout);
+    const dim3 blocks((n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
+    const auto* g = reinterpret_cast<const __half*>(dy);
+    switch (layout->features_per_level) {
+        case 1: encode_backward_kernel<1><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+        case 2: encode_backward_kernel<2><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+        case 4: encode_backward_kernel<4><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+        default: encode_backward_kernel<8><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+    }
+    return check_launch("encode_backward_kernel");
+}
