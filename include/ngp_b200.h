@@ -91,6 +91,50 @@ NGP_API int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t n, 
                              uint32_t coord_stride, const uint16_t* dy, uint32_t dy_stride,
                              float* table_grad, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Fully fused MLPs (tcgen05 tensor cores, fp32 accumulation in TMEM).
+ *
+ * params: the 10,240 packed fp16 MLP weights [out][in] in the reference order
+ * (ngp.train.h:58-78): density W_in 64x32, density W_out 16x64, rgb W_in 64x32, rgb W_h 64x64,
+ * rgb W_out 16x64.  x: encoded positions, fp16 feature-major [32][x_stride].  coords: sample
+ * records (the view direction is read from floats 4..6).
+ * ------------------------------------------------------------------------------------------ */
+
+/* Degree-4 spherical-harmonics encoding of the view directions -> fp16 [16][out_stride].
+ * Replaces encode_spherical_harmonics_kernel (ngp.train.cu:962-993). */
+NGP_API int ngp_sh_encode(uint32_t n, const float* coords, uint32_t coord_stride, uint16_t* out, uint32_t out_stride, void* stream);
+
+/* Density + colour network forward for n rows -> out fp16 [n][16] (ch 0-2 raw rgb, ch 3 raw
+ * density, as network_output in the reference).  density_rgb_in (optional, may be NULL)
+ * receives the 16 density outputs feature-major [16][x_stride], the reference's rgb_input[0..15].
+ * Replaces evaluate_network / forward_network (ngp.train.cu:1494-1524, 1660-1684): WMMA
+ * kernels K19 and the glue kernels K16, K21. */
+NGP_API int ngp_mlp_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
+                    uint32_t coord_stride, uint16_t* out, uint16_t* density_rgb_in, void* stream);
+
+/* Density network only -> out[n] = raw density (fp16).  Replaces the density-only
+ * mlp_forward_64_relu_kernel launch of update_density_grid (ngp.train.cu:1573). */
+NGP_API int ngp_density_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, uint16_t* out, void* stream);
+
+/* Number of fp32 scratch values ngp_mlp_backward needs (one weight-gradient partial per CTA). */
+NGP_API uint32_t ngp_mlp_backward_scratch_floats(void);
+
+/* Network backward for n rows: dy fp16 [n][16] (ch 0-2 rgb, ch 3 density gradient) ->
+ * dx fp16 [32][dx_stride] (gradient w.r.t. x; may be NULL) and the weight gradient
+ * dw = dw_scale * dL/dW written as fp32 (dw_f32) and/or fp16 (dw_f16) [10240] (either may be
+ * NULL).  The forward activations are recomputed on chip.  scratch: caller-allocated device
+ * buffer of at least ngp_mlp_backward_scratch_floats() floats.  The weight gradient is summed
+ * in a fixed order, so results are deterministic.
+ * Replaces backward_network (ngp.train.cu:1686-1895): WMMA kernel K20, cuBLASLt G1-G7 and the
+ * glue kernels K22, K23. */
+NGP_API int ngp_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
+                     uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, float* scratch,
+                     size_t scratch_floats, float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream);
+
+/* Sticky device status of the MLP kernels: bit 0 = a tensor-core completion wait timed out.
+ * reset != 0 clears it. */
+NGP_API int ngp_mlp_status(uint32_t* out_status, int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,9 +1,8 @@
 // Multiresolution hash-grid encoding, forward and backward, for sm_100a.
 //
-// Thread mapping is level-major: blockIdx.y selects the level, so every resident CTA of a
-// wave gathers from the same level's table and the coarse tables stay L1-resident while the
-// fine ones stream through L2 (the 24 MB table of the BASELINE configuration is L2-resident
-// on B200's 126 MB L2).  A corner's F features are one vector load (F=2: 32-bit half2,
+// Thread mapping is level-major: every CTA serves one level for a chunk of points, so its
+// gathers hit one table; the coarse tables stay L1-resident while the fine ones stream through
+// L2 (the 24 MB table of the BASELINE configuration is L2-resident on B200's 126 MB L2).  A corner's F features are one vector load (F=2: 32-bit half2,
 // F=4: 64-bit), taken through the non-coherent read-only path.  Each thread handles
 // POINTS_PER_THREAD points so that 8 * POINTS_PER_THREAD independent gathers are in flight.
 //
@@ -13,10 +12,45 @@
 // fp32 gradient table with vector atomics (red.global.add.v2/v4.f32) instead of fp16 atomics.
 #include "common.cuh"
 
+// Tuning knobs (compile-time; the defaults are the measured best on B200).
+#ifndef NGP_ENC_FWD_PPT
+#define NGP_ENC_FWD_PPT 1  // points per thread in the forward kernel
+#endif
+#ifndef NGP_ENC_FWD_PAIR
+#define NGP_ENC_FWD_PAIR 0  // 1: one load for an aligned pair of x-neighbour entries (measured slower)
+#endif
+#ifndef NGP_ENC_FWD_INTERLEAVE
+#define NGP_ENC_FWD_INTERLEAVE 0  // 1: consecutive CTAs take consecutive levels; 0: level = blockIdx.y
+#endif
+#ifndef NGP_ENC_BWD_INTERLEAVE
+#define NGP_ENC_BWD_INTERLEAVE 1
+#endif
+#ifndef NGP_ENC_BWD_PAIR
+#define NGP_ENC_BWD_PAIR 1  // 1: merge the x-neighbour corners into one 16-byte atomic when they pair up
+#endif
+
 namespace ngp {
 namespace {
 
 constexpr uint32_t kEncodeThreads = 256u;
+
+// Level and point-chunk of this CTA.  Interleaving the levels across consecutive CTAs spreads
+// the atomic traffic of the small coarse tables over the whole kernel instead of issuing all of
+// a coarse level's updates in the first wave.
+template <bool INTERLEAVE>
+__device__ __forceinline__ void cta_level_chunk(uint32_t n_levels, uint32_t& level, uint32_t& chunk) {
+    if constexpr (INTERLEAVE) {
+        level = blockIdx.x % n_levels;
+        chunk = blockIdx.x / n_levels;
+    } else {
+        level = blockIdx.y;
+        chunk = blockIdx.x;
+    }
+}
+
+inline dim3 encode_grid(bool interleave, uint32_t chunks, uint32_t n_levels) {
+    return interleave ? dim3(chunks * n_levels, 1u) : dim3(chunks, n_levels);
+}
 
 template <uint32_t F>
 struct FeatureVec;
@@ -35,6 +69,10 @@ struct FeatureVec<4> {
 template <>
 struct FeatureVec<8> {
     using type = uint4;
+};
+template <>
+struct FeatureVec<16> {
+    using type = uint4;  // unused: pairs are formed for F <= 4 only
 };
 
 template <uint32_t F>
@@ -66,14 +104,15 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_kernel(const ui
                                                                         const __half* __restrict__ table,
                                                                         __half* __restrict__ out, const uint32_t out_stride,
                                                                         const __grid_constant__ GridParams grid) {
-    using Vec                    = typename FeatureVec<F>::type;
-    const uint32_t level         = blockIdx.y;
+    using Vec = typename FeatureVec<F>::type;
+    uint32_t level, chunk;
+    cta_level_chunk<NGP_ENC_FWD_INTERLEAVE>(grid.n_levels, level, chunk);
     const uint32_t level_offset  = grid.offsets[level];
     const uint32_t hashmap_size  = grid.offsets[level + 1] - level_offset;
     const uint32_t resolution    = grid.resolution[level];
     const float scale            = grid.scale[level];
     const Vec* __restrict__ lvl  = reinterpret_cast<const Vec*>(table) + level_offset;
-    const uint32_t base          = blockIdx.x * (kEncodeThreads * PPT) + threadIdx.x;
+    const uint32_t base          = chunk * (kEncodeThreads * PPT) + threadIdx.x;
 
     float frac[PPT][3];
     uint32_t cell[PPT][3];
@@ -87,15 +126,30 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_kernel(const ui
         for (uint32_t d = 0; d < 3; ++d) position_fraction(__ldg(c + d), scale, frac[p][d], cell[p][d]);
     }
 
-    // Issue all 8 * PPT gathers before any arithmetic depends on them.
+    // Issue all 8 * PPT gathers before any arithmetic depends on them.  For F <= 4 the x-neighbour
+    // corners often share one aligned pair of entries (dense levels: idx and idx + 1 with idx even;
+    // hashed levels: x even, so (x ^ h) and ((x + 1) ^ h) differ in bit 0 only): one load of the
+    // pair containing corner x serves both, and corner x + 1 is loaded separately only otherwise.
     Vec v[PPT][8];
 #pragma unroll
     for (uint32_t p = 0; p < PPT; ++p) {
 #pragma unroll
-        for (uint32_t corner = 0; corner < 8; ++corner) {
-            const uint32_t idx = grid_index(hashmap_size, resolution, cell[p][0] + (corner & 1u), cell[p][1] + ((corner >> 1) & 1u),
-                                            cell[p][2] + ((corner >> 2) & 1u));
-            v[p][corner]       = __ldg(lvl + idx);
+        for (uint32_t yz = 0; yz < 4; ++yz) {
+            const uint32_t cy = cell[p][1] + (yz & 1u), cz = cell[p][2] + (yz >> 1);
+            const uint32_t i0 = grid_index(hashmap_size, resolution, cell[p][0], cy, cz);
+            const uint32_t i1 = grid_index(hashmap_size, resolution, cell[p][0] + 1u, cy, cz);
+#if NGP_ENC_FWD_PAIR
+            if constexpr (F <= 4) {
+                using Pair          = typename FeatureVec<2 * F>::type;
+                const Pair pr       = __ldg(reinterpret_cast<const Pair*>(lvl + (i0 & ~1u)));
+                const Vec* pv       = reinterpret_cast<const Vec*>(&pr);
+                v[p][2 * yz]        = pv[i0 & 1u];
+                v[p][2 * yz + 1]    = ((i0 ^ i1) == 1u) ? pv[i1 & 1u] : __ldg(lvl + i1);
+                continue;
+            }
+#endif
+            v[p][2 * yz]     = __ldg(lvl + i0);
+            v[p][2 * yz + 1] = __ldg(lvl + i1);
         }
     }
 
@@ -143,9 +197,10 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const u
                                                                          const __half* __restrict__ dy, const uint32_t dy_stride,
                                                                          float* __restrict__ table_grad,
                                                                          const __grid_constant__ GridParams grid) {
-    const uint32_t i = blockIdx.x * kEncodeThreads + threadIdx.x;
+    uint32_t level, chunk;
+    cta_level_chunk<NGP_ENC_BWD_INTERLEAVE>(grid.n_levels, level, chunk);
+    const uint32_t i = chunk * kEncodeThreads + threadIdx.x;
     if (i >= n) return;
-    const uint32_t level        = blockIdx.y;
     const uint32_t level_offset = grid.offsets[level];
     const uint32_t hashmap_size = grid.offsets[level + 1] - level_offset;
     const uint32_t resolution   = grid.resolution[level];
@@ -162,17 +217,41 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const u
 #pragma unroll
     for (uint32_t d = 0; d < 3; ++d) position_fraction(__ldg(c + d), scale, frac[d], cell[d]);
 
+    const float wx0 = __fsub_rn(1.0f, frac[0]), wx1 = frac[0];
 #pragma unroll
-    for (uint32_t corner = 0; corner < 8; ++corner) {
-        const float wx     = (corner & 1u) ? frac[0] : __fsub_rn(1.0f, frac[0]);
-        const float wy     = (corner & 2u) ? frac[1] : __fsub_rn(1.0f, frac[1]);
-        const float wz     = (corner & 4u) ? frac[2] : __fsub_rn(1.0f, frac[2]);
-        const float w      = __fmul_rn(__fmul_rn(wx, wy), wz);
-        const uint32_t idx = grid_index(hashmap_size, resolution, cell[0] + (corner & 1u), cell[1] + ((corner >> 1) & 1u), cell[2] + ((corner >> 2) & 1u));
-        float contrib[F];
+    for (uint32_t yz = 0; yz < 4; ++yz) {
+        const uint32_t cy  = cell[1] + (yz & 1u), cz = cell[2] + (yz >> 1);
+        // corner weights in the forward kernel's order: (wx * wy) * wz
+        const float wy     = (yz & 1u) ? frac[1] : __fsub_rn(1.0f, frac[1]);
+        const float wz     = (yz & 2u) ? frac[2] : __fsub_rn(1.0f, frac[2]);
+        const float w0     = __fmul_rn(__fmul_rn(wx0, wy), wz);
+        const float w1     = __fmul_rn(__fmul_rn(wx1, wy), wz);
+        const uint32_t i0  = grid_index(hashmap_size, resolution, cell[0], cy, cz);
+        const uint32_t i1  = grid_index(hashmap_size, resolution, cell[0] + 1u, cy, cz);
+        float c0[F], c1[F];
 #pragma unroll
-        for (uint32_t f = 0; f < F; ++f) contrib[f] = __fmul_rn(w, g[f]);
-        scatter_add<F>(lvl + static_cast<uint64_t>(idx) * F, contrib);
+        for (uint32_t f = 0; f < F; ++f) {
+            c0[f] = __fmul_rn(w0, g[f]);
+            c1[f] = __fmul_rn(w1, g[f]);
+        }
+#if NGP_ENC_BWD_PAIR
+        if constexpr (F <= 2) {
+            // Entries 2k and 2k+1 share one 16-byte (F=2) / 8-byte (F=1) aligned slot: one atomic.
+            if ((i0 ^ i1) == 1u) {
+                const uint32_t lo = i0 < i1 ? i0 : i1;
+                float pair[2 * F];
+#pragma unroll
+                for (uint32_t f = 0; f < F; ++f) {
+                    pair[f]     = i0 < i1 ? c0[f] : c1[f];
+                    pair[F + f] = i0 < i1 ? c1[f] : c0[f];
+                }
+                scatter_add<2 * F>(lvl + static_cast<uint64_t>(lo) * F, pair);
+                continue;
+            }
+        }
+#endif
+        scatter_add<F>(lvl + static_cast<uint64_t>(i0) * F, c0);
+        scatter_add<F>(lvl + static_cast<uint64_t>(i1) * F, c1);
     }
 }
 
@@ -198,8 +277,8 @@ extern "C" int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n
     if (coords == nullptr || table == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "encode forward: null pointer");
     if (coord_stride < 3 || out_stride < n) return fail(NGP_ERR_INVALID, "encode forward: bad stride");
     const GridParams grid = make_grid_params(*layout);
-    constexpr uint32_t ppt = 2;
-    const dim3 blocks((n + kEncodeThreads * ppt - 1) / (kEncodeThreads * ppt), layout->n_levels);
+    constexpr uint32_t ppt = NGP_ENC_FWD_PPT;
+    const dim3 blocks = encode_grid(NGP_ENC_FWD_INTERLEAVE, (n + kEncodeThreads * ppt - 1) / (kEncodeThreads * ppt), layout->n_levels);
     const auto* t = reinterpret_cast<const __half*>(table);
     auto* o       = reinterpret_cast<__half*>(out);
     switch (layout->features_per_level) {
@@ -219,7 +298,7 @@ extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t 
     if (coords == nullptr || dy == nullptr || table_grad == nullptr) return fail(NGP_ERR_INVALID, "encode backward: null pointer");
     if (coord_stride < 3 || dy_stride < n) return fail(NGP_ERR_INVALID, "encode backward: bad stride");
     const GridParams grid = make_grid_params(*layout);
-    const dim3 blocks((n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
+    const dim3 blocks = encode_grid(NGP_ENC_BWD_INTERLEAVE, (n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
     const auto* g = reinterpret_cast<const __half*>(dy);
     switch (layout->features_per_level) {
         case 1: encode_backward_kernel<1><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;

@@ -1,0 +1,675 @@
+// Fully fused 64-wide density + colour MLPs on the sm_100a tensor cores (tcgen05 + TMEM).
+//
+// Replaces the reference's WMMA kernels and cuBLASLt GEMMs (ngp.train.cu:1019-1236,
+// 1494-1524, 1660-1903):
+//   density net  32 -> 64 (ReLU) -> 16           (output 0 = raw density)
+//   colour net   [16 density outputs | 16 SH] -> 64 (ReLU) -> 64 (ReLU) -> 16 (0-2 = raw rgb)
+// fp16 weights [out][in] packed as in ngp.train.h:58-78, no biases, fp32 accumulation in TMEM,
+// one fp16 rounding per layer output.
+//
+// Execution: a persistent CTA of one warpgroup (128 threads) owns a 128-row tile at a time;
+// thread t owns row t, which is TMEM lane t of every accumulator.  All weights stay in shared
+// memory for the CTA's lifetime; activations never leave the SM: each layer's accumulator is
+// read from TMEM (tcgen05.ld), activated, rounded to fp16 and written back into shared memory
+// as the next MMA's operand.  One elected thread issues the MMAs and commits them to an
+// mbarrier that every thread waits on (with a time bound).
+//
+// Backward recomputes the forward activations of its tile on chip instead of reading stored
+// hidden activations from HBM, then runs the input-gradient chain and accumulates all five
+// weight gradients in TMEM across every tile the CTA processes.  Each CTA writes its weight-
+// gradient partial once; a second small kernel sums the partials in a fixed order
+// (deterministic).  Weight-gradient GEMMs use M = 128 with the 64 real rows in lanes 0-63.
+#include "common.cuh"
+#include "umma.cuh"
+
+namespace ngp {
+namespace {
+
+constexpr uint32_t kThreads = 128;
+constexpr uint32_t kRows    = 128;
+
+// packed weight offsets (halves)
+constexpr uint32_t kWdIn = 0, kWdOut = 2048, kWrIn = 3072, kWrH = 5120, kWrOut = 9216, kMlpParams = 10240;
+
+// shared-memory weight tiles (bytes): each [out rows][in] in the interleaved layout
+constexpr uint32_t kSWdIn = 0, kSWdOut = 4096, kSWrIn = 6144, kSWrH = 10240, kSWrOut = 18432, kSWeights = 20480;
+
+// ---- error status --------------------------------------------------------------------------
+// Device status word: set (never cleared by kernels) when an mbarrier wait times out.
+__device__ uint32_t g_mlp_status;
+
+// ---- tile helpers --------------------------------------------------------------------------
+// Byte offset of 16-byte chunk c of row r in a tile with `cpr` chunks per row.
+__device__ __forceinline__ uint32_t tile_off(uint32_t r, uint32_t c, uint32_t cpr) { return (r & 7u) * 16u + (r >> 3) * (128u * cpr) + c * 128u; }
+
+__device__ __forceinline__ void store_chunk(unsigned char* tile, uint32_t r, uint32_t c, uint32_t cpr, uint4 v) {
+    *reinterpret_cast<uint4*>(tile + tile_off(r, c, cpr)) = v;
+}
+__device__ __forceinline__ uint4 load_chunk(const unsigned char* tile, uint32_t r, uint32_t c, uint32_t cpr) {
+    return *reinterpret_cast<const uint4*>(tile + tile_off(r, c, cpr));
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Copy a row-major fp16 matrix [rows][cols] from global memory into an interleaved tile.
+__device__ void load_weight_tile(unsigned char* tile, const __half* W, uint32_t rows, uint32_t cols) {
+    const uint32_t cpr = cols / 8u;
+    for (uint32_t q = threadIdx.x; q < rows * cpr; q += blockDim.x) {
+        const uint32_t r = q / cpr, c = q % cpr;
+        store_chunk(tile, r, c, cpr, *reinterpret_cast<const uint4*>(W + r * cols + c * 8u));
+    }
+}
+
+// Store 8*nchunks fp32 values of this thread's row (ReLU optional) as fp16 into a tile.
+template <uint32_t NCHUNK, bool RELU>
+__device__ __forceinline__ void store_row(unsigned char* tile, uint32_t r, const float* v) {
+#pragma unroll
+    for (uint32_t c = 0; c < NCHUNK; ++c) {
+        float a[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] = RELU ? fmaxf(v[c * 8 + j], 0.0f) : v[c * 8 + j];
+        store_chunk(tile, r, c, NCHUNK, make_uint4(pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7])));
+    }
+}
+
+// Read N fp32 accumulator columns [col, col+N) of this thread's lane.
+template <uint32_t N>
+__device__ __forceinline__ void read_acc(uint32_t tmem, uint32_t col, float* v) {
+    const uint32_t lane_base = (threadIdx.x & ~31u) << 16;
+#pragma unroll
+    for (uint32_t c = 0; c < N; c += 16) {
+        float t[16];
+        umma::tmem_ld16(tmem + lane_base + col + c, t);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[c + j] = t[j];
+    }
+}
+
+// Issue D(+)= A * B^T over K (multiple of 16) from one thread.
+// A: M=128 rows.  K-major A: tile rows = M, cpr chunks per row.  MN-major A: tile rows = K.
+// B: N rows.       K-major B: tile rows = N.                     MN-major B: tile rows = K.
+__device__ __forceinline__ void gemm(uint32_t d_tmem, uint32_t N, uint32_t K, uint32_t a_saddr, bool a_mn, uint32_t a_cpr,
+                                     uint32_t b_saddr, bool b_mn, uint32_t b_cpr, bool accumulate) {
+    const uint32_t a_lbo = a_mn ? 128u * a_cpr : 128u, a_sbo = a_mn ? 128u : 128u * a_cpr;
+    const uint32_t b_lbo = b_mn ? 128u * b_cpr : 128u, b_sbo = b_mn ? 128u : 128u * b_cpr;
+    const uint32_t idesc = umma::make_idesc_f16(128u, N, a_mn, b_mn);
+    for (uint32_t ks = 0; ks < K / 16u; ++ks) {
+        const uint64_t ad = umma::make_desc(a_saddr + ks * 2u * a_lbo, a_lbo, a_sbo);
+        const uint64_t bd = umma::make_desc(b_saddr + ks * 2u * b_lbo, b_lbo, b_sbo);
+        umma::mma_f16(d_tmem, ad, bd, idesc, (accumulate || ks > 0) ? 1u : 0u);
+    }
+}
+
+// Degree-4 SH of dir = 2 * warped - 1 (ngp.train.cu:962-993), one IEEE operation at a time with
+// explicit fused multiply-adds for the a*b+c forms.
+__device__ __forceinline__ void sh16(float wx, float wy, float wz, float (&o)[16]) {
+    const float x = __fsub_rn(__fmul_rn(wx, 2.0f), 1.0f), y = __fsub_rn(__fmul_rn(wy, 2.0f), 1.0f), z = __fsub_rn(__fmul_rn(wz, 2.0f), 1.0f);
+    const float xy = __fmul_rn(x, y), xz = __fmul_rn(x, z), yz = __fmul_rn(y, z);
+    const float x2 = __fmul_rn(x, x), y2 = __fmul_rn(y, y), z2 = __fmul_rn(z, z);
+    o[0]  = 0.28209479177387814f;
+    o[1]  = __fmul_rn(-0.48860251190291987f, y);
+    o[2]  = __fmul_rn(0.48860251190291987f, z);
+    o[3]  = __fmul_rn(-0.48860251190291987f, x);
+    o[4]  = __fmul_rn(1.0925484305920792f, xy);
+    o[5]  = __fmul_rn(-1.0925484305920792f, yz);
+    o[6]  = __fmaf_rn(0.94617469575755997f, z2, -0.31539156525251999f);
+    o[7]  = __fmul_rn(-1.0925484305920792f, xz);
+    o[8]  = __fmaf_rn(0.54627421529603959f, x2, -__fmul_rn(0.54627421529603959f, y2));
+    o[9]  = __fmul_rn(__fmul_rn(0.59004358992664352f, y), __fmaf_rn(-3.0f, x2, y2));
+    o[10] = __fmul_rn(__fmul_rn(2.8906114426405538f, xy), z);
+    o[11] = __fmul_rn(__fmul_rn(0.45704579946446572f, y), __fmaf_rn(-5.0f, z2, 1.0f));
+    o[12] = __fmul_rn(__fmul_rn(0.3731763325901154f, z), __fmaf_rn(5.0f, z2, -3.0f));
+    o[13] = __fmul_rn(__fmul_rn(0.45704579946446572f, x), __fmaf_rn(-5.0f, z2, 1.0f));
+    o[14] = __fmul_rn(__fmul_rn(1.4453057213202769f, z), __fsub_rn(x2, y2));
+    o[15] = __fmul_rn(__fmul_rn(0.59004358992664352f, x), __fmaf_rn(3.0f, y2, -x2));
+}
+
+// CTA-wide step boundary: make this thread's shared-memory writes visible to the tensor core,
+// order its earlier TMEM reads before the barrier, and synchronise.
+__device__ __forceinline__ void stage_sync() {
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+}
+
+// Wait for the MMAs committed to `mbar` (phase parity flips every call).
+__device__ __forceinline__ bool stage_wait(uint64_t* mbar, uint32_t& phase) {
+    const bool ok = umma::mbar_wait(mbar, phase);
+    phase ^= 1u;
+    umma::fence_after_sync();
+    if (!ok) atomicOr(&g_mlp_status, 1u);
+    return ok;
+}
+
+struct MlpForwardParams {
+    uint32_t n;
+    const __half* params;   // packed MLP weights (10,240 halves)
+    const __half* x;        // encoded positions, feature-major [32][x_stride]
+    uint32_t x_stride;
+    const float* coords;    // sample records (view direction at floats 4..6)
+    uint32_t coord_stride;
+    __half* out;            // [n][16] row-major (MODE full) or [n] raw density (MODE density)
+    __half* density_rgb_in; // optional: density outputs, feature-major [16][x_stride]
+};
+
+enum : int { kModeFull = 0, kModeDensity = 1 };
+
+constexpr uint32_t kFwdTmemCols = 128;  // D0: cols 0-63, D1: cols 64-79
+constexpr uint32_t kFwdSmem     = kSWeights + 8192 + 16384 + 1024;
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    unsigned char* sw  = smem;                      // weights
+    unsigned char* sx  = smem + kSWeights;          // 128 x 32 input tile (X, then rgb input)
+    unsigned char* shd = sx + 8192;                 // 128 x 64 hidden tile
+    __shared__ uint64_t mbar;
+    __shared__ uint32_t tmem_slot;
+
+    const uint32_t t = threadIdx.x;
+    load_weight_tile(sw + kSWdIn, p.params + kWdIn, 64, 32);
+    load_weight_tile(sw + kSWdOut, p.params + kWdOut, 16, 64);
+    if (MODE == kModeFull) {
+        load_weight_tile(sw + kSWrIn, p.params + kWrIn, 64, 32);
+        load_weight_tile(sw + kSWrH, p.params + kWrH, 64, 64);
+        load_weight_tile(sw + kSWrOut, p.params + kWrOut, 16, 64);
+    }
+    if (t < 32) umma::tmem_alloc(&tmem_slot, kFwdTmemCols);
+    if (t == 0) umma::mbar_init(&mbar, 1);
+    stage_sync();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t d0 = tmem, d1 = tmem + 64;
+    const uint32_t a_sx = umma::smem_addr(sx), a_shd = umma::smem_addr(shd), a_sw = umma::smem_addr(sw);
+    uint32_t phase  = 0;
+    bool ok         = true;
+    const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
+
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t row   = tile * kRows + t;
+        const bool valid     = row < p.n;
+        // ---- input row: 32 fp16 features (coalesced across the warp per feature) ----
+        {
+            float xv[32];
+#pragma unroll
+            for (uint32_t k = 0; k < 32; ++k) xv[k] = valid ? __half2float(p.x[static_cast<uint64_t>(k) * p.x_stride + row]) : 0.0f;
+            store_row<4, false>(sx, t, xv);
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
+            umma::commit(&mbar);
+        }
+        ok = stage_wait(&mbar, phase);
+        {
+            float h[64];
+            read_acc<64>(tmem, 0, h);
+            store_row<8, true>(shd, t, h);
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(d1, 16, 64, a_shd, false, 8, a_sw + kSWdOut, false, 8, false);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        float dens[16];
+        read_acc<16>(tmem, 64, dens);
+        if (MODE == kModeDensity) {
+            if (valid) p.out[row] = __float2half_rn(dens[0]);
+            umma::fence_before_sync();
+            if (!__syncthreads_and(ok)) break;
+            umma::fence_after_sync();
+            continue;
+        }
+        // ---- colour network input: [16 density outputs | 16 SH of the view direction] ----
+        {
+            float ri[32];
+            float sh[16];
+            const float* c = p.coords + static_cast<uint64_t>(valid ? row : 0u) * p.coord_stride;
+            sh16(c[4], c[5], c[6], sh);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                ri[k]      = dens[k];
+                ri[16 + k] = sh[k];
+            }
+            store_row<4, false>(sx, t, ri);
+            if (p.density_rgb_in != nullptr && valid)
+#pragma unroll
+                for (int k = 0; k < 16; ++k) p.density_rgb_in[static_cast<uint64_t>(k) * p.x_stride + row] = __float2half_rn(dens[k]);
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWrIn, false, 4, false);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float h[64];
+            read_acc<64>(tmem, 0, h);
+            store_row<8, true>(shd, t, h);
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(d0, 64, 64, a_shd, false, 8, a_sw + kSWrH, false, 8, false);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float h[64];
+            read_acc<64>(tmem, 0, h);
+            store_row<8, true>(shd, t, h);  // the layer-2 MMA that read shd has completed
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(d1, 16, 64, a_shd, false, 8, a_sw + kSWrOut, false, 8, false);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        float o[16];
+        read_acc<16>(tmem, 64, o);
+        o[3] = dens[0];
+        if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<uint64_t>(row) * 16u);
+            dst[0]     = make_uint4(pack2(o[0], o[1]), pack2(o[2], o[3]), pack2(o[4], o[5]), pack2(o[6], o[7]));
+            dst[1]     = make_uint4(pack2(o[8], o[9]), pack2(o[10], o[11]), pack2(o[12], o[13]), pack2(o[14], o[15]));
+        }
+        // a timed-out wait anywhere in the CTA ends the loop for every thread together
+        umma::fence_before_sync();
+        if (!__syncthreads_and(ok)) break;
+        umma::fence_after_sync();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (t < 32) umma::tmem_dealloc(tmem, kFwdTmemCols);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------------------------
+struct MlpBackwardParams {
+    uint32_t n;
+    const __half* params;
+    const __half* x;          // encoded positions [32][x_stride]
+    uint32_t x_stride;
+    const float* coords;
+    uint32_t coord_stride;
+    const __half* dy;         // dL/d(network output) [n][16]: ch 0-2 rgb, ch 3 density
+    __half* dx;               // dL/d(encoded positions) [32][dx_stride] (may be null)
+    uint32_t dx_stride;
+    float* dw_partial;        // [gridDim.x][10240] per-CTA weight-gradient partials
+};
+
+// TMEM columns: D0 working accumulator 0-63; weight-gradient accumulators after it.
+constexpr uint32_t kColD0 = 0, kColWrOut = 64, kColWrH = 80, kColWrIn = 144, kColWdOut = 176, kColWdIn = 192;
+constexpr uint32_t kBwdTmemCols = 256;
+// shared memory tiles (bytes)
+constexpr uint32_t kBX = kSWeights, kBHd = kBX + 8192, kBRi = kBHd + 16384, kBH1 = kBRi + 8192, kBH2 = kBH1 + 16384, kBDy = kBH2 + 16384,
+                   kBGuard = kBDy + 4096, kBwdSmem = kBGuard + 4096;
+
+__global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_constant__ MlpBackwardParams p) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    __shared__ uint64_t mbar;
+    __shared__ uint32_t tmem_slot;
+    const uint32_t t = threadIdx.x;
+
+    load_weight_tile(smem + kSWdIn, p.params + kWdIn, 64, 32);
+    load_weight_tile(smem + kSWdOut, p.params + kWdOut, 16, 64);
+    load_weight_tile(smem + kSWrIn, p.params + kWrIn, 64, 32);
+    load_weight_tile(smem + kSWrH, p.params + kWrH, 64, 64);
+    load_weight_tile(smem + kSWrOut, p.params + kWrOut, 16, 64);
+    // the padded (M = 128) weight-gradient GEMMs read up to 2 KB past the last activation tile
+    for (uint32_t i = t; i < 4096 / 16; i += kThreads) reinterpret_cast<uint4*>(smem + kBGuard)[i] = make_uint4(0, 0, 0, 0);
+    if (t < 32) umma::tmem_alloc(&tmem_slot, kBwdTmemCols);
+    if (t == 0) umma::mbar_init(&mbar, 1);
+    stage_sync();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t s0   = umma::smem_addr(smem);
+    uint32_t phase      = 0;
+    bool ok             = true;
+    bool first          = true;
+    const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
+
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t row = tile * kRows + t;
+        const bool valid   = row < p.n;
+        // ---------------- forward recompute ----------------
+        {
+            float xv[32];
+#pragma unroll
+            for (uint32_t k = 0; k < 32; ++k) xv[k] = valid ? __half2float(p.x[static_cast<uint64_t>(k) * p.x_stride + row]) : 0.0f;
+            store_row<4, false>(smem + kBX, t, xv);
+        }
+        float g[16];
+        {
+            // rgb output gradient: channels 0-2 (extract_rgb_gradients, ngp.train.cu:1244-1253)
+            const uint4* src = reinterpret_cast<const uint4*>(p.dy + static_cast<uint64_t>(valid ? row : 0u) * 16u);
+            const uint4 a = valid ? src[0] : make_uint4(0, 0, 0, 0);
+            const __half2* h = reinterpret_cast<const __half2*>(&a);
+            const float2 g01 = __half22float2(h[0]), g23 = __half22float2(h[1]);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) g[k] = 0.0f;
+            g[0] = g01.x;
+            g[1] = g01.y;
+            g[2] = g23.x;
+            g[3] = g23.y;  // density gradient, added to the density-output gradient below
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 64, 32, s0 + kBX, false, 4, s0 + kSWdIn, false, 4, false);
+            umma::commit(&mbar);
+        }
+        ok = stage_wait(&mbar, phase);
+        {
+            float h[64];
+            read_acc<64>(tmem, kColD0, h);
+            store_row<8, true>(smem + kBHd, t, h);
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 16, 64, s0 + kBHd, false, 8, s0 + kSWdOut, false, 8, false);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float ri[32], dens[16], sh[16];
+            read_acc<16>(tmem, kColD0, dens);
+            const float* c = p.coords + static_cast<uint64_t>(valid ? row : 0u) * p.coord_stride;
+            sh16(c[4], c[5], c[6], sh);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                ri[k]      = dens[k];
+                ri[16 + k] = sh[k];
+            }
+            store_row<4, false>(smem + kBRi, t, ri);
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 64, 32, s0 + kBRi, false, 4, s0 + kSWrIn, false, 4, false);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float h[64];
+            read_acc<64>(tmem, kColD0, h);
+            store_row<8, true>(smem + kBH1, t, h);
+        }
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 64, 64, s0 + kBH1, false, 8, s0 + kSWrH, false, 8, false);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float h[64];
+            read_acc<64>(tmem, kColD0, h);
+            store_row<8, true>(smem + kBH2, t, h);
+            // rgb output gradient tile (K = 16): channels 0-2, zeros elsewhere
+            float gy[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) gy[k] = k < 3 ? g[k] : 0.0f;
+            store_row<2, false>(smem + kBDy, t, gy);
+        }
+        // ---------------- backward ----------------
+        // B1: dH2 = dY * Wr_out (N = 64, K = 16);  dWr_out^T[i][o] += sum_m H2[m][i] dY[m][o]
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 64, 16, s0 + kBDy, false, 2, s0 + kSWrOut, true, 8, false);
+            gemm(tmem + kColWrOut, 16, 128, s0 + kBH2, true, 8, s0 + kBDy, true, 2, !first);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float d[64];
+            read_acc<64>(tmem, kColD0, d);
+#pragma unroll
+            for (uint32_t c = 0; c < 8; ++c) {
+                const uint4 hv = load_chunk(smem + kBH2, t, c, 8);
+                const __half* hh = reinterpret_cast<const __half*>(&hv);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) d[c * 8 + j] = __half2float(hh[j]) > 0.0f ? d[c * 8 + j] : 0.0f;
+            }
+            store_row<8, false>(smem + kBH2, t, d);  // dH2 replaces H2 (both MMAs reading H2 are done)
+        }
+        // B2: dH1 = dH2 * Wr_h (N = 64, K = 64);  dWr_h[o][i] += sum_m dH2[m][o] H1[m][i]
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 64, 64, s0 + kBH2, false, 8, s0 + kSWrH, true, 8, false);
+            gemm(tmem + kColWrH, 64, 128, s0 + kBH2, true, 8, s0 + kBH1, true, 8, !first);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float d[64];
+            read_acc<64>(tmem, kColD0, d);
+#pragma unroll
+            for (uint32_t c = 0; c < 8; ++c) {
+                const uint4 hv = load_chunk(smem + kBH1, t, c, 8);
+                const __half* hh = reinterpret_cast<const __half*>(&hv);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) d[c * 8 + j] = __half2float(hh[j]) > 0.0f ? d[c * 8 + j] : 0.0f;
+            }
+            store_row<8, false>(smem + kBH1, t, d);  // dH1 replaces H1
+        }
+        // B3: dRi = dH1 * Wr_in (N = 32, K = 64);  dWr_in[o][i] += sum_m dH1[m][o] Ri[m][i]
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 32, 64, s0 + kBH1, false, 8, s0 + kSWrIn, true, 4, false);
+            gemm(tmem + kColWrIn, 32, 128, s0 + kBH1, true, 8, s0 + kBRi, true, 4, !first);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float d[32];
+            read_acc<32>(tmem, kColD0, d);
+            d[0] += g[3];  // add_density_gradient_kernel (ngp.train.cu:1255-1259)
+            store_row<2, false>(smem + kBDy, t, d);  // dDensityOut (16) replaces dY
+        }
+        // B4: dHd = dDo * Wd_out (N = 64, K = 16);  dWd_out^T[i][o] += sum_m Hd[m][i] dDo[m][o]
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 64, 16, s0 + kBDy, false, 2, s0 + kSWdOut, true, 8, false);
+            gemm(tmem + kColWdOut, 16, 128, s0 + kBHd, true, 8, s0 + kBDy, true, 2, !first);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float d[64];
+            read_acc<64>(tmem, kColD0, d);
+#pragma unroll
+            for (uint32_t c = 0; c < 8; ++c) {
+                const uint4 hv = load_chunk(smem + kBHd, t, c, 8);
+                const __half* hh = reinterpret_cast<const __half*>(&hv);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) d[c * 8 + j] = __half2float(hh[j]) > 0.0f ? d[c * 8 + j] : 0.0f;
+            }
+            store_row<8, false>(smem + kBHd, t, d);  // dHd replaces Hd
+        }
+        // B5: dX = dHd * Wd_in (N = 32, K = 64);  dWd_in[o][i] += sum_m dHd[m][o] X[m][i]
+        stage_sync();
+        if (t == 0) {
+            gemm(tmem + kColD0, 32, 64, s0 + kBHd, false, 8, s0 + kSWdIn, true, 4, false);
+            gemm(tmem + kColWdIn, 32, 128, s0 + kBHd, true, 8, s0 + kBX, true, 4, !first);
+            umma::commit(&mbar);
+        }
+        ok = ok && stage_wait(&mbar, phase);
+        {
+            float d[32];
+            read_acc<32>(tmem, kColD0, d);
+            if (valid && p.dx != nullptr)
+#pragma unroll
+                for (uint32_t k = 0; k < 32; ++k) p.dx[static_cast<uint64_t>(k) * p.dx_stride + row] = __float2half_rn(d[k]);
+        }
+        first = false;
+        umma::fence_before_sync();
+        if (!__syncthreads_and(ok)) break;
+        umma::fence_after_sync();
+    }
+
+    // ---- write this CTA's weight-gradient partial (rows 0-63 of the M = 128 accumulators) ----
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    float* part = p.dw_partial + static_cast<uint64_t>(blockIdx.x) * kMlpParams;
+    if (t < 64) {
+        if (first) {
+            // this CTA processed no tile: its partial is zero
+            for (uint32_t i = 0; i < 64; ++i) {
+                if (i < 32) part[kWdIn + t * 32 + i] = 0.0f, part[kWrIn + t * 32 + i] = 0.0f;
+                part[kWrH + t * 64 + i] = 0.0f;
+                if (i < 16) part[kWrOut + i * 64 + t] = 0.0f, part[kWdOut + i * 64 + t] = 0.0f;
+            }
+        } else {
+            float v[64];
+            read_acc<16>(tmem, kColWrOut, v);  // lane t = hidden unit i, column o: dWr_out[o][i]
+            for (uint32_t o = 0; o < 16; ++o) part[kWrOut + o * 64 + t] = v[o];
+            read_acc<64>(tmem, kColWrH, v);  // lane t = output unit o: dWr_h[o][i]
+            for (uint32_t i = 0; i < 64; ++i) part[kWrH + t * 64 + i] = v[i];
+            read_acc<32>(tmem, kColWrIn, v);
+            for (uint32_t i = 0; i < 32; ++i) part[kWrIn + t * 32 + i] = v[i];
+            read_acc<16>(tmem, kColWdOut, v);
+            for (uint32_t o = 0; o < 16; ++o) part[kWdOut + o * 64 + t] = v[o];
+            read_acc<32>(tmem, kColWdIn, v);
+            for (uint32_t i = 0; i < 32; ++i) part[kWdIn + t * 32 + i] = v[i];
+        }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (t < 32) umma::tmem_dealloc(tmem, kBwdTmemCols);
+}
+
+// dW[j] = scale * sum over CTAs of partial[cta][j], in CTA order (deterministic).
+__global__ void mlp_reduce_partials_kernel(const float* __restrict__ partial, uint32_t n_parts, float scale, float* __restrict__ dw_f32,
+                                           __half* __restrict__ dw_f16) {
+    const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= kMlpParams) return;
+    float acc = 0.0f;
+    for (uint32_t c = 0; c < n_parts; ++c) acc += partial[static_cast<uint64_t>(c) * kMlpParams + j];
+    acc *= scale;
+    if (dw_f32 != nullptr) dw_f32[j] = acc;
+    if (dw_f16 != nullptr) dw_f16[j] = __float2half_rn(acc);
+}
+
+__global__ void sh_encode_kernel(uint32_t n, const float* __restrict__ coords, uint32_t coord_stride, __half* __restrict__ out,
+                                 uint32_t out_stride) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
+    float sh[16];
+    sh16(c[4], c[5], c[6], sh);
+#pragma unroll
+    for (uint32_t k = 0; k < 16; ++k) out[static_cast<uint64_t>(k) * out_stride + i] = __float2half_rn(sh[k]);
+}
+
+int mlp_grid(int smem_bytes, const void* kernel, uint32_t n_tiles, uint32_t tmem_cols) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem_bytes) != cudaSuccess || per_sm < 1) per_sm = 1;
+    const int by_tmem = static_cast<int>(512u / tmem_cols);
+    per_sm            = per_sm < by_tmem ? per_sm : by_tmem;
+    const uint32_t g  = static_cast<uint32_t>(per_sm * sm_count());
+    return static_cast<int>(n_tiles < g ? n_tiles : g);
+}
+
+}  // namespace
+
+uint32_t mlp_backward_max_ctas() {
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mlp_backward_kernel, kThreads, kBwdSmem);
+    if (per_sm < 1) per_sm = 1;
+    const int by_tmem = static_cast<int>(512u / kBwdTmemCols);
+    return static_cast<uint32_t>((per_sm < by_tmem ? per_sm : by_tmem) * sm_count());
+}
+
+}  // namespace ngp
+
+using namespace ngp;
+
+namespace {
+int ensure_attrs() {
+    static int status = [] {
+        cudaError_t e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+        return static_cast<int>(e);
+    }();
+    if (status != 0) return fail(NGP_ERR_CUDA, std::string("mlp: cudaFuncSetAttribute: ") + cudaGetErrorString(static_cast<cudaError_t>(status)));
+    return NGP_OK;
+}
+}  // namespace
+
+extern "C" int ngp_mlp_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
+                               uint32_t coord_stride, uint16_t* out, uint16_t* density_rgb_in, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (params == nullptr || x == nullptr || coords == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "mlp forward: null pointer");
+    if (x_stride < n || coord_stride < 7) return fail(NGP_ERR_INVALID, "mlp forward: bad stride");
+    NGP_TRY(ensure_attrs());
+    MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
+                       reinterpret_cast<__half*>(out), reinterpret_cast<__half*>(density_rgb_in)};
+    const uint32_t n_tiles = (n + kRows - 1) / kRows;
+    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull>), n_tiles, kFwdTmemCols);
+    mlp_forward_kernel<kModeFull><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
+    return check_launch("mlp_forward_kernel");
+}
+
+extern "C" int ngp_density_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, uint16_t* out, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (params == nullptr || x == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "density forward: null pointer");
+    if (x_stride < n) return fail(NGP_ERR_INVALID, "density forward: bad stride");
+    NGP_TRY(ensure_attrs());
+    MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7,
+                       reinterpret_cast<__half*>(out), nullptr};
+    const uint32_t n_tiles = (n + kRows - 1) / kRows;
+    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity>), n_tiles, kFwdTmemCols);
+    mlp_forward_kernel<kModeDensity><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
+    return check_launch("mlp_forward_kernel<density>");
+}
+
+extern "C" uint32_t ngp_mlp_backward_scratch_floats(void) { return mlp_backward_max_ctas() * kMlpParams; }
+
+extern "C" int ngp_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
+                                uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, float* scratch,
+                                size_t scratch_floats, float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream) {
+    clear_error();
+    if (params == nullptr || x == nullptr || coords == nullptr || dy == nullptr || scratch == nullptr)
+        return fail(NGP_ERR_INVALID, "mlp backward: null pointer");
+    if (x_stride < n || coord_stride < 7 || (dx != nullptr && dx_stride < n)) return fail(NGP_ERR_INVALID, "mlp backward: bad stride");
+    NGP_TRY(ensure_attrs());
+    const uint32_t n_tiles = (n + kRows - 1) / kRows;
+    uint32_t grid          = static_cast<uint32_t>(mlp_grid(kBwdSmem, reinterpret_cast<const void*>(mlp_backward_kernel), n_tiles == 0 ? 1 : n_tiles, kBwdTmemCols));
+    if (static_cast<size_t>(grid) * kMlpParams > scratch_floats) {
+        grid = static_cast<uint32_t>(scratch_floats / kMlpParams);
+        if (grid == 0) return fail(NGP_ERR_INVALID, "mlp backward: scratch too small (need ngp_mlp_backward_scratch_floats())");
+    }
+    MlpBackwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
+                        reinterpret_cast<const __half*>(dy), reinterpret_cast<__half*>(dx), dx_stride, scratch};
+    mlp_backward_kernel<<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
+    NGP_TRY(check_launch("mlp_backward_kernel"));
+    mlp_reduce_partials_kernel<<<(kMlpParams + 255) / 256, 256, 0, as_stream(stream)>>>(scratch, grid, dw_scale, dw_f32,
+                                                                                          reinterpret_cast<__half*>(dw_f16));
+    return check_launch("mlp_reduce_partials_kernel");
+}
+
+extern "C" int ngp_mlp_status(uint32_t* out_status, int reset) {
+    clear_error();
+    uint32_t v = 0;
+    NGP_TRY(check_cuda(cudaMemcpyFromSymbol(&v, g_mlp_status, sizeof(v)), "mlp status read"));
+    if (reset) {
+        const uint32_t zero = 0;
+        NGP_TRY(check_cuda(cudaMemcpyToSymbol(g_mlp_status, &zero, sizeof(zero)), "mlp status reset"));
+    }
+    if (out_status != nullptr) *out_status = v;
+    return NGP_OK;
+}
+
+extern "C" int ngp_sh_encode(uint32_t n, const float* coords, uint32_t coord_stride, uint16_t* out, uint32_t out_stride, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (coords == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "sh encode: null pointer");
+    if (coord_stride < 7 || out_stride < n) return fail(NGP_ERR_INVALID, "sh encode: bad stride");
+    sh_encode_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(n, coords, coord_stride, reinterpret_cast<__half*>(out), out_stride);
+    return check_launch("sh_encode_kernel");
+}

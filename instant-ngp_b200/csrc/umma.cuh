@@ -1,0 +1,112 @@
+// Thin wrappers over the sm_100a tensor-core instructions (tcgen05.*) and mbarriers, written
+// from the PTX ISA.  Used by the fused MLP kernels.
+//
+// Shared-memory operand layout: the "interleaved" (no swizzle) canonical layout, built from
+// 8 x 8 fp16 core matrices of 128 contiguous bytes (8 rows of 16 bytes).  For a tile stored with
+// rows r and 16-byte chunks c along the row, element (r, c*8 + j) lives at
+//     (r % 8) * 16 + (r / 8) * ROW_BLOCK + c * 128 + j * 2,   ROW_BLOCK = 128 * chunks_per_row.
+// The same bytes describe the tile as a K-major operand (rows = M/N, K along the row:
+// LBO = 128, SBO = ROW_BLOCK) and as the transposed MN-major operand (rows = K, M/N along the
+// row: LBO = ROW_BLOCK, SBO = 128).  One copy of every activation tile therefore feeds both the
+// forward/input-gradient GEMMs and the weight-gradient GEMMs of the MLP.
+#pragma once
+
+#include <cstdint>
+
+namespace ngp {
+namespace umma {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// Shared-memory matrix descriptor (tcgen05 format): start, LBO and SBO in 16-byte units,
+// version 1 at bits 46-47, no swizzle (layout type 0 at bits 61-63).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    return d;
+}
+
+// Instruction descriptor for kind::f16: fp16 A and B, fp32 accumulator, M x N tile.
+// a_mn / b_mn select MN-major operands (bit 15 / bit 16).
+__host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t M, uint32_t N, bool a_mn, bool b_mn) {
+    return (1u << 4) | (static_cast<uint32_t>(a_mn) << 15) | (static_cast<uint32_t>(b_mn) << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on an mbarrier once all previously issued MMAs of this thread have completed.
+__device__ __forceinline__ void commit(uint64_t* mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(mbar)) : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Make this thread's generic-proxy shared-memory writes visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- TMEM allocation (whole warp) ----------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Read 16 consecutive fp32 columns of this thread's TMEM lane (warp w owns lanes 32w..32w+31).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+          "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- mbarrier ------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(mbar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the mbarrier phase with parity `phase` to complete.  Bounded: gives up after about
+// one second of wall time and returns false, so a lost arrival can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t phase) {
+    const uint32_t addr = smem_addr(mbar);
+    uint64_t start      = 0;
+    for (uint32_t it = 0;; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(addr), "r"(phase)
+            : "memory");
+        if (done) return true;
+        if ((it & 1023u) == 0u) {
+            const uint64_t now = globaltimer_ns();
+            if (start == 0) start = now;
+            else if (now - start > 1000000000ull) return false;
+        }
+    }
+}
+
+}  // namespace umma
+}  // namespace ngp

@@ -125,3 +125,65 @@ def encode_grid_backward(layout: GridLayout, coords, dy, table_grad, n: int | No
     _check(lib().ngp_encode_grid_backward(ctypes.byref(layout), ctypes.c_uint32(n), _ptr(coords), ctypes.c_uint32(coord_stride),
                                           _ptr(dy), ctypes.c_uint32(dy_stride), _ptr(table_grad), _stream(stream)),
            "ngp_encode_grid_backward")
+
+
+# ---------------------------------------------------------------------------------------------
+# Fully fused MLPs (replaces mlp_forward_64_relu_kernel / backward + cuBLASLt, ngp.train.cu:1019-1903)
+# ---------------------------------------------------------------------------------------------
+MLP_PARAMS = 10240
+_scratch = {}
+
+
+def sh_encode(coords, out, n: int | None = None, out_stride: int | None = None, stream=None) -> None:
+    """Degree-4 SH of the sample records' view directions -> fp16 [16][out_stride]."""
+    n = coords.shape[0] if n is None else n
+    out_stride = out.shape[1] if out_stride is None else out_stride
+    _check(lib().ngp_sh_encode(ctypes.c_uint32(n), _ptr(coords), ctypes.c_uint32(coords.shape[1]), _ptr(out),
+                               ctypes.c_uint32(out_stride), _stream(stream)), "ngp_sh_encode")
+
+
+def mlp_forward(params, x, coords, out, n: int | None = None, x_stride: int | None = None, density_rgb_in=None, stream=None) -> None:
+    """Density + colour network forward -> out fp16 [n][16]."""
+    n = coords.shape[0] if n is None else n
+    x_stride = x.shape[1] if x_stride is None else x_stride
+    _check(lib().ngp_mlp_forward(ctypes.c_uint32(n), _ptr(params), _ptr(x), ctypes.c_uint32(x_stride), _ptr(coords),
+                                 ctypes.c_uint32(coords.shape[1]), _ptr(out), _ptr(density_rgb_in), _stream(stream)), "ngp_mlp_forward")
+
+
+def density_forward(params, x, out, n: int | None = None, x_stride: int | None = None, stream=None) -> None:
+    """Density network only -> raw density fp16 [n]."""
+    n = out.shape[0] if n is None else n
+    x_stride = x.shape[1] if x_stride is None else x_stride
+    _check(lib().ngp_density_forward(ctypes.c_uint32(n), _ptr(params), _ptr(x), ctypes.c_uint32(x_stride), _ptr(out), _stream(stream)),
+           "ngp_density_forward")
+
+
+def mlp_backward_scratch(device=None):
+    """The (cached) fp32 scratch buffer ngp_mlp_backward needs on `device`."""
+    import torch
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev not in _scratch:
+        lib().ngp_mlp_backward_scratch_floats.restype = ctypes.c_uint32
+        _scratch[dev] = torch.empty(int(lib().ngp_mlp_backward_scratch_floats()), dtype=torch.float32, device=dev)
+    return _scratch[dev]
+
+
+def mlp_backward(params, x, coords, dy, dx=None, dw_f32=None, dw_f16=None, dw_scale: float = 1.0, n: int | None = None,
+                 x_stride: int | None = None, dx_stride: int | None = None, scratch=None, stream=None) -> None:
+    """Network backward: dy fp16 [n][16] -> dx fp16 [32][dx_stride] and dw (scaled) fp32/fp16 [10240]."""
+    n = coords.shape[0] if n is None else n
+    x_stride = x.shape[1] if x_stride is None else x_stride
+    if dx_stride is None:
+        dx_stride = dx.shape[1] if dx is not None else n
+    scratch = mlp_backward_scratch(x.device) if scratch is None else scratch
+    _check(lib().ngp_mlp_backward(ctypes.c_uint32(n), _ptr(params), _ptr(x), ctypes.c_uint32(x_stride), _ptr(coords),
+                                  ctypes.c_uint32(coords.shape[1]), _ptr(dy), _ptr(dx), ctypes.c_uint32(dx_stride), _ptr(scratch),
+                                  ctypes.c_size_t(scratch.numel()), _ptr(dw_f32), _ptr(dw_f16), ctypes.c_float(dw_scale),
+                                  _stream(stream)), "ngp_mlp_backward")
+
+
+def mlp_status(reset: bool = False) -> int:
+    v = ctypes.c_uint32(0)
+    _check(lib().ngp_mlp_status(ctypes.byref(v), ctypes.c_int(1 if reset else 0)), "ngp_mlp_status")
+    return int(v.value)

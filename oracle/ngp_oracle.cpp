@@ -240,3 +240,174 @@ void oracle_pcg32(uint64_t initstate, uint64_t initseq, uint64_t advance, uint32
 }
 
 }  // extern "C"
+
+// ======================================================================================
+// Spherical harmonics (ngp.train.cu:962-993) and the fully fused MLPs (ngp.train.cu:1019-1236,
+// 1660-1903).  Packed fp16 weights [out][in] at the reference offsets (ngp.train.h:58-78):
+//   density W_in 64x32 @0, density W_out 16x64 @2048, rgb W_in 64x32 @3072,
+//   rgb W_h 64x64 @5120, rgb W_out 16x64 @9216  (10,240 weights, no biases).
+// Arithmetic restated with fp32 accumulation and one fp16 rounding per layer output, which is
+// the CUDA library's arithmetic; the reference accumulates in fp16 (checked with tolerances).
+// ======================================================================================
+namespace {
+
+constexpr uint32_t kWdIn = 0, kWdOut = 2048, kWrIn = 3072, kWrH = 5120, kWrOut = 9216, kMlpParams = 10240;
+
+inline float rh(float v) { return h2f(f2h(v)); }  // round to fp16 and back
+
+// Degree-4 real spherical harmonics of dir = 2 * warped - 1.  The products and sums are written
+// out one IEEE operation at a time; the a*b+c forms use a single fused multiply-add.
+void sh16(float wx, float wy, float wz, float out[16]) {
+    const float x = wx * 2.0f - 1.0f, y = wy * 2.0f - 1.0f, z = wz * 2.0f - 1.0f;
+    const float xy = x * y, xz = x * z, yz = y * z, x2 = x * x, y2 = y * y, z2 = z * z;
+    out[0]  = 0.28209479177387814f;
+    out[1]  = -0.48860251190291987f * y;
+    out[2]  = 0.48860251190291987f * z;
+    out[3]  = -0.48860251190291987f * x;
+    out[4]  = 1.0925484305920792f * xy;
+    out[5]  = -1.0925484305920792f * yz;
+    out[6]  = std::fmaf(0.94617469575755997f, z2, -0.31539156525251999f);
+    out[7]  = -1.0925484305920792f * xz;
+    out[8]  = std::fmaf(0.54627421529603959f, x2, -(0.54627421529603959f * y2));
+    out[9]  = (0.59004358992664352f * y) * std::fmaf(-3.0f, x2, y2);
+    out[10] = (2.8906114426405538f * xy) * z;
+    out[11] = (0.45704579946446572f * y) * std::fmaf(-5.0f, z2, 1.0f);
+    out[12] = (0.3731763325901154f * z) * std::fmaf(5.0f, z2, -3.0f);
+    out[13] = (0.45704579946446572f * x) * std::fmaf(-5.0f, z2, 1.0f);
+    out[14] = (1.4453057213202769f * z) * (x2 - y2);
+    out[15] = (0.59004358992664352f * x) * std::fmaf(3.0f, y2, -x2);
+}
+
+// y[o] = sum_k W[o][k] x[k] with an fp32 fmaf chain in k order.
+template <int OUT, int IN>
+void layer(const uint16_t* W, const float* x, float* y) {
+    for (int o = 0; o < OUT; ++o) {
+        float acc = 0.0f;
+        for (int k = 0; k < IN; ++k) acc = std::fmaf(h2f(W[o * IN + k]), x[k], acc);
+        y[o] = acc;
+    }
+}
+
+struct RowActs {
+    float x[32], hd[64], dout[16], ri[32], h1[64], h2[64], out[16];
+};
+
+void mlp_row_forward(const uint16_t* P, const float x16[32], const float dir[3], RowActs& a) {
+    for (int k = 0; k < 32; ++k) a.x[k] = x16[k];
+    float t[64];
+    layer<64, 32>(P + kWdIn, a.x, t);
+    for (int j = 0; j < 64; ++j) a.hd[j] = rh(std::max(t[j], 0.0f));
+    layer<16, 64>(P + kWdOut, a.hd, t);
+    for (int o = 0; o < 16; ++o) a.dout[o] = rh(t[o]);
+    float sh[16];
+    sh16(dir[0], dir[1], dir[2], sh);
+    for (int k = 0; k < 16; ++k) {
+        a.ri[k]      = a.dout[k];
+        a.ri[16 + k] = rh(sh[k]);
+    }
+    layer<64, 32>(P + kWrIn, a.ri, t);
+    for (int j = 0; j < 64; ++j) a.h1[j] = rh(std::max(t[j], 0.0f));
+    layer<64, 64>(P + kWrH, a.h1, t);
+    for (int j = 0; j < 64; ++j) a.h2[j] = rh(std::max(t[j], 0.0f));
+    layer<16, 64>(P + kWrOut, a.h2, t);
+    for (int o = 0; o < 16; ++o) a.out[o] = rh(t[o]);
+    a.out[3] = a.dout[0];
+}
+
+}  // namespace
+
+extern "C" {
+
+// SH encoding of n sample records (dirs at floats 4..6 of each 7-float record) -> fp16 [16][n].
+void oracle_sh_encode(uint32_t n, const float* coords, uint32_t coord_stride, uint16_t* out) {
+    for (uint32_t i = 0; i < n; ++i) {
+        const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
+        float sh[16];
+        sh16(c[4], c[5], c[6], sh);
+        for (int k = 0; k < 16; ++k) out[static_cast<uint64_t>(k) * n + i] = f2h(sh[k]);
+    }
+}
+
+// Network forward (evaluate_network, ngp.train.cu:1494-1524): x fp16 feature-major [32][x_stride],
+// sample records for the view directions -> out fp16 [n][16] (ch 0-2 rgb raw, ch 3 density raw).
+void oracle_mlp_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords, uint32_t coord_stride,
+                        uint16_t* out, int threads) {
+    parallel_for(n, threads, [&](uint32_t b, uint32_t e) {
+        for (uint32_t i = b; i < e; ++i) {
+            float xr[32];
+            for (int k = 0; k < 32; ++k) xr[k] = h2f(x[static_cast<uint64_t>(k) * x_stride + i]);
+            const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
+            RowActs a;
+            mlp_row_forward(params, xr, c + 4, a);
+            for (int o = 0; o < 16; ++o) out[static_cast<uint64_t>(i) * 16 + o] = f2h(a.out[o]);
+        }
+    });
+}
+
+// Density network only (update_density_grid, ngp.train.cu:1569-1573): raw density (ch 0) -> out[n].
+void oracle_density_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, uint16_t* out) {
+    for (uint32_t i = 0; i < n; ++i) {
+        float xr[32], t[64], hd[64], d[16];
+        for (int k = 0; k < 32; ++k) xr[k] = h2f(x[static_cast<uint64_t>(k) * x_stride + i]);
+        layer<64, 32>(params + kWdIn, xr, t);
+        for (int j = 0; j < 64; ++j) hd[j] = rh(std::max(t[j], 0.0f));
+        layer<16, 64>(params + kWdOut, hd, d);
+        out[i] = f2h(d[0]);
+    }
+}
+
+// Network backward (backward_network, ngp.train.cu:1686-1903) for n rows:
+// dy fp16 [n][16] (ch 0-2 rgb, ch 3 density; others ignored as extract_rgb_gradients does)
+// -> dx fp16 [32][dx_stride] (gradient w.r.t. the encoded input) and dW fp64 [10240] (summed).
+void oracle_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords, uint32_t coord_stride,
+                         const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, double* dW) {
+    const uint16_t* P = params;
+    for (uint32_t i = 0; i < n; ++i) {
+        float xr[32];
+        for (int k = 0; k < 32; ++k) xr[k] = h2f(x[static_cast<uint64_t>(k) * x_stride + i]);
+        RowActs a;
+        mlp_row_forward(P, xr, coords + static_cast<uint64_t>(i) * coord_stride + 4, a);
+        float g[16] = {};
+        for (int o = 0; o < 3; ++o) g[o] = h2f(dy[static_cast<uint64_t>(i) * 16 + o]);
+        const float gd = h2f(dy[static_cast<uint64_t>(i) * 16 + 3]);
+        float dh2[64], dh1[64], dxr[32], ddo[16], dhd[64];
+        for (int j = 0; j < 64; ++j) {
+            float acc = 0.0f;
+            for (int o = 0; o < 16; ++o) acc = std::fmaf(g[o], h2f(P[kWrOut + o * 64 + j]), acc);
+            dh2[j] = a.h2[j] > 0.0f ? rh(acc) : 0.0f;
+        }
+        for (int k = 0; k < 64; ++k) {
+            float acc = 0.0f;
+            for (int j = 0; j < 64; ++j) acc = std::fmaf(dh2[j], h2f(P[kWrH + j * 64 + k]), acc);
+            dh1[k] = a.h1[k] > 0.0f ? rh(acc) : 0.0f;
+        }
+        for (int k = 0; k < 32; ++k) {
+            float acc = 0.0f;
+            for (int j = 0; j < 64; ++j) acc = std::fmaf(dh1[j], h2f(P[kWrIn + j * 32 + k]), acc);
+            dxr[k] = acc;
+        }
+        for (int o = 0; o < 16; ++o) ddo[o] = rh(o == 0 ? dxr[0] + gd : dxr[o]);
+        for (int j = 0; j < 64; ++j) {
+            float acc = 0.0f;
+            for (int o = 0; o < 16; ++o) acc = std::fmaf(ddo[o], h2f(P[kWdOut + o * 64 + j]), acc);
+            dhd[j] = a.hd[j] > 0.0f ? rh(acc) : 0.0f;
+        }
+        for (int k = 0; k < 32; ++k) {
+            float acc = 0.0f;
+            for (int j = 0; j < 64; ++j) acc = std::fmaf(dhd[j], h2f(P[kWdIn + j * 32 + k]), acc);
+            dx[static_cast<uint64_t>(k) * dx_stride + i] = f2h(acc);
+        }
+        for (int o = 0; o < 16; ++o)
+            for (int j = 0; j < 64; ++j) dW[kWrOut + o * 64 + j] += static_cast<double>(g[o]) * a.h2[j];
+        for (int j = 0; j < 64; ++j)
+            for (int k = 0; k < 64; ++k) dW[kWrH + j * 64 + k] += static_cast<double>(dh2[j]) * a.h1[k];
+        for (int j = 0; j < 64; ++j)
+            for (int k = 0; k < 32; ++k) dW[kWrIn + j * 32 + k] += static_cast<double>(dh1[j]) * a.ri[k];
+        for (int o = 0; o < 16; ++o)
+            for (int j = 0; j < 64; ++j) dW[kWdOut + o * 64 + j] += static_cast<double>(ddo[o]) * a.hd[j];
+        for (int j = 0; j < 64; ++j)
+            for (int k = 0; k < 32; ++k) dW[kWdIn + j * 32 + k] += static_cast<double>(dhd[j]) * a.x[k];
+    }
+}
+
+}  // extern "C"

@@ -120,3 +120,48 @@ class RefLib:
         status = getattr(self.lib, name)(*args)
         if status != 0:
             raise RuntimeError(f"{name} failed with CUDA status {status}")
+
+
+def _oracle_mlp_methods():
+    def sh_encode(self, coords):
+        coords = np.ascontiguousarray(coords, np.float32)
+        n = coords.shape[0]
+        out = np.zeros((16, n), np.uint16)
+        self.lib.oracle_sh_encode(ctypes.c_uint32(n), _p(coords), ctypes.c_uint32(coords.shape[1]), _p(out))
+        return out.view(np.float16)
+
+    def mlp_forward(self, params, x, coords, threads: int = 1):
+        params = np.ascontiguousarray(params.view(np.uint16))
+        x = np.ascontiguousarray(x.view(np.uint16))
+        coords = np.ascontiguousarray(coords, np.float32)
+        n = coords.shape[0]
+        out = np.zeros((n, 16), np.uint16)
+        self.lib.oracle_mlp_forward(ctypes.c_uint32(n), _p(params), _p(x), ctypes.c_uint32(x.shape[1]), _p(coords),
+                                    ctypes.c_uint32(coords.shape[1]), _p(out), ctypes.c_int(threads))
+        return out.view(np.float16)
+
+    def density_forward(self, params, x):
+        params = np.ascontiguousarray(params.view(np.uint16))
+        x = np.ascontiguousarray(x.view(np.uint16))
+        n = x.shape[1]
+        out = np.zeros(n, np.uint16)
+        self.lib.oracle_density_forward(ctypes.c_uint32(n), _p(params), _p(x), ctypes.c_uint32(x.shape[1]), _p(out))
+        return out.view(np.float16)
+
+    def mlp_backward(self, params, x, coords, dy):
+        params = np.ascontiguousarray(params.view(np.uint16))
+        x = np.ascontiguousarray(x.view(np.uint16))
+        dy = np.ascontiguousarray(dy.view(np.uint16))
+        coords = np.ascontiguousarray(coords, np.float32)
+        n = coords.shape[0]
+        dx = np.zeros((32, n), np.uint16)
+        dw = np.zeros(10240, np.float64)
+        self.lib.oracle_mlp_backward(ctypes.c_uint32(n), _p(params), _p(x), ctypes.c_uint32(x.shape[1]), _p(coords),
+                                     ctypes.c_uint32(coords.shape[1]), _p(dy), _p(dx), ctypes.c_uint32(n), _p(dw))
+        return dx.view(np.float16), dw
+
+    for f in (sh_encode, mlp_forward, density_forward, mlp_backward):
+        setattr(Oracle, f.__name__, f)
+
+
+_oracle_mlp_methods()

@@ -52,6 +52,32 @@ int ref_encode_backward(uint32_t n, const float* coords, const uint16_t* dy, uin
     return status_of(cudaGetLastError());
 }
 
+// encode_spherical_harmonics_kernel (ngp.train.cu:962-993) -> fp16 [16][n].
+int ref_sh_encode(uint32_t n, const float* coords, uint16_t* out, void* stream) {
+    ref::encode_spherical_harmonics_kernel<<<(n + ref::THREADS_PER_BLOCK - 1u) / ref::THREADS_PER_BLOCK, ref::THREADS_PER_BLOCK, 0,
+                                             static_cast<cudaStream_t>(stream)>>>(n, coords, reinterpret_cast<__half*>(out));
+    return status_of(cudaGetLastError());
+}
+
+// The reference's two MLP launches and density extraction of evaluate_network
+// (ngp.train.cu:1514-1522) on a given encoded input x [32][n] and SH block sh [16][n]:
+// density net -> rgb_in[0..15], rgb net -> out [n][16], out[:,3] = density.  n % 128 == 0.
+int ref_mlp_forward(uint32_t n, const uint16_t* mlp_params, const uint16_t* x, uint16_t* rgb_in, uint16_t* out, void* stream) {
+    const auto s                 = static_cast<cudaStream_t>(stream);
+    constexpr int forward_shmem  = sizeof(__half) * (16u + 16u * ref::MLP_FORWARD_ITERS) * (cfg::MLP_WIDTH + ref::MLP_SKEW);
+    constexpr dim3 threads{32u, ref::MLP_WIDTH_BLOCKS, 1u};
+    if (cudaFuncSetAttribute(ref::mlp_forward_64_relu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, forward_shmem) != cudaSuccess) return 1;
+    const dim3 blocks{n / (16u * ref::MLP_FORWARD_ITERS), 1u, 1u};
+    const auto* P = reinterpret_cast<const __half*>(mlp_params);
+    ref::mlp_forward_64_relu_kernel<<<blocks, threads, forward_shmem, s>>>(n, reinterpret_cast<const __half*>(x), P + cfg::NETWORK_PARAMETER_LAYOUT.density_param_offset,
+                                                                           nullptr, reinterpret_cast<__half*>(rgb_in), false, cfg::DENSITY_HIDDEN_LAYERS);
+    ref::mlp_forward_64_relu_kernel<<<blocks, threads, forward_shmem, s>>>(n, reinterpret_cast<const __half*>(rgb_in), P + cfg::NETWORK_PARAMETER_LAYOUT.rgb_param_offset,
+                                                                           nullptr, reinterpret_cast<__half*>(out), true, cfg::RGB_HIDDEN_LAYERS);
+    ref::extract_density_kernel<<<(n + ref::THREADS_PER_BLOCK - 1u) / ref::THREADS_PER_BLOCK, ref::THREADS_PER_BLOCK, 0, s>>>(
+        n, reinterpret_cast<const __half*>(rgb_in), reinterpret_cast<__half*>(out));
+    return status_of(cudaGetLastError());
+}
+
 // PCG32 as the reference's device code runs it (ngp.train.cu:89-143), for pinning.
 int ref_pcg32(uint64_t initstate, uint64_t initseq, uint64_t advance, uint32_t count, uint32_t* out_uint, float* out_float) {
     ref::Pcg32 a{initstate, initseq};
