@@ -135,6 +135,152 @@ NGP_API int ngp_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t*
  * reset != 0 clears it. */
 NGP_API int ngp_mlp_status(uint32_t* out_status, int reset);
 
+/* ------------------------------------------------------------------------------------------
+ * Occupancy density grid: 128^3 cells in Morton order over the unit cube, fp32 values,
+ * uint8 bitfield (8 cells per byte).  camera: 12 floats per frame (three axis columns, then
+ * the origin), as built by the reference's dataset loader (ngp.dataset.cpp:47-65).
+ * ------------------------------------------------------------------------------------------ */
+
+/* values[c] = 0 if any corner of cell c is seen by some training view, else -1.
+ * Replaces mark_untrained_density_grid_kernel (ngp.train.cu:310-381). */
+NGP_API int ngp_density_grid_mark_untrained(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x,
+                                            float focal_y, float principal_x, float principal_y, float* values, void* stream);
+
+/* n_uniform uniformly chosen cells followed by n_nonuniform cells above the occupancy threshold
+ * (up to 10 hashed tries), jittered positions from PCG32(1337) at ema_step -> 7-float records
+ * and cell indices.  Replaces generate_density_grid_samples_kernel (ngp.train.cu:383-424). */
+NGP_API int ngp_density_grid_samples(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords,
+                                     uint32_t* indices, void* stream);
+
+/* scratch[indices[i]] = max(scratch[indices[i]], exp(density[i]) * sqrt(3)/1024).
+ * Replaces splat_density_grid_samples_kernel (ngp.train.cu:426-432). */
+NGP_API int ngp_density_grid_splat(uint32_t n, const uint32_t* indices, const uint16_t* density, float* scratch, void* stream);
+
+/* Size (floats) of the `partial` buffer of ngp_density_grid_update. */
+NGP_API uint32_t ngp_density_grid_partials(void);
+
+/* EMA (values = v < 0 ? v : max(decay * v, scratch)), mean of max(v, 0) in a fixed order
+ * (deterministic), bitfield = v > min(0.01, mean), occupied-cell count; clears scratch.
+ * Replaces K4-K6 (ngp.train.cu:434-474) and the memsets of update_density_grid. */
+NGP_API int ngp_density_grid_update(float* values, float* scratch, float decay, float* partial, float* mean, uint8_t* bitfield,
+                                    uint32_t* occupied_count, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Ray marching (dt = sqrt(3)/1024, <= 1024 occupied steps, empty-space skipping).  Samples are
+ * placed in ray order: numsteps[2i] = samples of ray i, numsteps[2i+1] = its first sample.
+ * block_totals: ngp_march_block_totals(n_rays) uint32 of scratch.
+ * ------------------------------------------------------------------------------------------ */
+NGP_API uint32_t ngp_march_block_totals(uint32_t max_rays);
+
+/* Training rays of `step` from the cameras (PCG32 pixels, start jitter) -> 7-float sample
+ * records, rays [i][6] (origin, unnormalised direction), ray_indices (identity), numsteps,
+ * *ray_counter = rays, *sample_counter = samples before the limit.  rays_per_batch_dev
+ * (optional) overrides the ray count from device memory (<= rays_per_batch).
+ * Replaces generate_training_samples_kernel / sample_training_batch (ngp.train.cu:476-578,
+ * 1919-1930). */
+NGP_API int ngp_march_training_rays(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x,
+                                    float focal_y, float principal_x, float principal_y, uint32_t step, uint32_t rays_per_batch,
+                                    const uint32_t* rays_per_batch_dev, uint32_t sample_limit, const uint8_t* bitfield, float* coords,
+                                    float* rays, uint32_t* ray_indices, uint32_t* numsteps, uint32_t* block_totals, uint32_t* ray_counter,
+                                    uint32_t* sample_counter, void* stream);
+
+/* Explicit rays [n][6] (origin, unit direction) in the unit-cube frame; jitter != 0 starts at
+ * tmin + U*dt with U the third draw of the training PCG32 stream of ray i at `step` (as
+ * training rays do), else at tmin + dt/2 (the evaluation rule, ngp.train.cu:613). */
+NGP_API int ngp_march_rays(uint32_t n_rays, const float* rays, int jitter, uint32_t step, const uint8_t* bitfield, uint32_t sample_limit,
+                           float* coords, uint32_t* numsteps, uint32_t* block_totals, uint32_t* sample_counter, void* stream);
+
+/* Pixel rays [n][6] (origin, unit direction) of pixels [pixel_offset, pixel_offset + n) of image
+ * `image`.  Replaces the ray set-up of generate_evaluation_samples_kernel (ngp.train.cu:587-614). */
+NGP_API int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,
+                               float principal_x, float principal_y, uint32_t pixel_offset, uint32_t n, float* rays, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Compositing, loss and compaction (batch = 2^18 samples).
+ * ------------------------------------------------------------------------------------------ */
+NGP_API uint32_t ngp_loss_scratch_bytes(uint32_t max_rays);
+
+/* Front-to-back compositing with early stop at transmittance < 1e-4, random background, L2
+ * loss, analytic compositing backward -> dloss_doutput fp16 [2^18][16] (scaled by
+ * 128 / rays_per_batch), compacted samples in ray order, loss_values[ray], numsteps rewritten
+ * to the compacted (count, base), *compacted_counter.  scratch: ngp_loss_scratch_bytes bytes,
+ * 16-byte aligned.  Replaces compute_training_loss_and_compact_kernel (ngp.train.cu:747-860,
+ * 1932-1944). */
+NGP_API int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                          uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                          uint32_t* compacted_counter, const uint32_t* ray_indices, const float* rays, uint32_t* numsteps,
+                                          const float* coords, float* compacted_coords, uint16_t* dloss_doutput, float* loss_values,
+                                          void* scratch, size_t scratch_bytes, void* stream);
+
+/* Wrap-around padding of the compacted batch to 2^18 samples, copied gradients scaled by
+ * count / 2^18.  Replaces K12/K13 (ngp.train.cu:862-874, 1946-1956). */
+NGP_API int ngp_pad_training_batch(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, void* stream);
+
+/* Evaluation compositing of n_pixels pixels: *sse += squared error vs the sRGB target (fp64; no
+ * target when pixels is NULL), optional comparison image [height][2*width][3] (target | render)
+ * and rendered [pixel][3].  Replaces accumulate_evaluation_loss_kernel (ngp.train.cu:676-745). */
+NGP_API int ngp_eval_composite(uint32_t n_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,
+                               const uint32_t* numsteps, const float* coords, const uint16_t* network_output, double* sse,
+                               uint8_t* comparison, float* rendered, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Optimizer.  Parameters [0, n_mlp) dense with L2 regularisation, the rest sparse (zero
+ * gradient = skipped).  gradients are fp32 and divided by loss_scale; clear_grid_gradients != 0
+ * zeroes gradients [n_mlp, n_params) in the same pass.  n_mlp % 4 == 0.
+ * Replaces adam_step_kernel / step_optimizer (ngp.train.cu:1261-1280, 1973-1980).
+ * ------------------------------------------------------------------------------------------ */
+NGP_API int ngp_adam_step(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg, float loss_scale,
+                          float* params_full_precision, uint16_t* params, float* gradients, float* first_moments, float* second_moments,
+                          uint32_t* param_steps, int clear_grid_gradients, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Trainer: the reference's ngp::train::InstantNGP (ngp.train.ixx:40-53) as an opaque handle.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct ngp_trainer ngp_trainer;
+
+typedef struct ngp_trainer_config {
+    uint32_t n_levels, features_per_level, log2_hashmap_size, base_resolution;
+    double log2_per_level_scale;
+    float learning_rate;
+} ngp_trainer_config;
+
+/* One dataset split on the host: RGBA8 pixels [frames][height][width][4], cameras [frames][12]. */
+typedef struct ngp_split {
+    const uint8_t* pixels;
+    const float* camera;
+    uint32_t frame_count, width, height;
+    float focal_x, focal_y, principal_x, principal_y;
+} ngp_split;
+
+/* TrainStats (ngp.train.ixx:8-18). */
+typedef struct ngp_train_stats {
+    uint32_t step, rays_per_batch, measured_sample_count_before_compaction, measured_sample_count, density_grid_occupied_cells;
+    float loss, elapsed_ms, density_grid_update_ms, density_grid_occupancy_ratio;
+} ngp_train_stats;
+
+NGP_API void ngp_trainer_default_config(ngp_trainer_config* cfg);
+/* Upload the splits, allocate and initialise everything (InstantNGP::InstantNGP, ngp.train.cpp:12-100). */
+NGP_API int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split* train, const ngp_split* validation, const ngp_split* test,
+                               ngp_trainer** out);
+NGP_API void ngp_trainer_destroy(ngp_trainer* t);
+/* InstantNGP::train(iters) (ngp.train.cpp:108-155). */
+NGP_API int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats* stats);
+/* Render `image_count` images of split 1 (validation) or 2 (test) and sum the squared error;
+ * comparison_host (optional, one image only) receives [height][2*width][3] RGB8.
+ * InstantNGP::validate / test (ngp.train.cpp:157-229). */
+NGP_API int ngp_trainer_evaluate(ngp_trainer* t, int split, uint32_t image_begin, uint32_t image_count, uint8_t* comparison_host,
+                                 double* out_sse, uint64_t* out_pixels);
+/* Render a novel view (camera: 12 floats, host) into rgb_device [height*width][3] (fp32, [0,1]). */
+NGP_API int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint32_t width, uint32_t height, float fx, float fy, float cx,
+                               float cy, float* rgb_device);
+NGP_API uint32_t ngp_trainer_param_count(const ngp_trainer* t);
+/* fp32 master parameters [MLP | grid] to / from the host (export_weights / load_weights;
+ * loading resets the optimizer and is allowed only before training, ngp.train.cpp:312). */
+NGP_API int ngp_trainer_get_params(const ngp_trainer* t, float* host_out, uint32_t count);
+NGP_API int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_t count);
+/* Occupancy bitfield (2^18 bytes) and density-grid values (2^21 floats) to the host. */
+NGP_API int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host, float* values_host);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,333 @@
+// Volume compositing, training loss, analytic compositing backward and deterministic
+// compaction of the training batch; evaluation compositing (PSNR / comparison image).
+//
+// Replaces K10-K13 (ngp.train.cu:669-874) and the host wrappers
+// compute_training_loss_and_compact_samples / pad_compacted_training_batch (1932-1956).
+//
+// The reference reserves compacted slots with a global atomic (ray order nondeterministic).
+// Here pass 1 composites each ray and counts the samples it keeps (front-to-back until the
+// transmittance drops below 1e-4), one CTA scans the per-CTA totals, and pass 2 writes each
+// ray's compacted samples, network-output gradients and loss at its prefix offset.
+#include "sampler.cuh"
+
+namespace ngp {
+namespace {
+
+constexpr uint32_t kThreads = 128u;
+
+struct LossParams {
+    uint32_t rays_per_batch;        // rays of the step (scales the loss and its gradient)
+    uint32_t step;
+    const uint32_t* ray_counter;    // optional: rays actually marched (<= rays_per_batch)
+    const uint8_t* pixels;
+    uint32_t frame_count, width, height;
+    const __half* network_output;   // [samples][16]
+    const uint32_t* ray_indices;    // optional: batch ray index of each marched ray
+    const float* rays;              // [ray][6]
+    uint32_t* numsteps;             // [ray][2]; rewritten with the compacted (count, base)
+    const float* coords;            // pre-compaction sample records
+    float* coords_out;              // compacted records [NETWORK_BATCH_SIZE][7]
+    __half* dloss_doutput;          // [NETWORK_BATCH_SIZE][16]
+    float* loss_output;             // [ray] (may be null)
+    float4* ray_rgb;                // scratch [ray]: composited colour, pass 1 -> pass 2
+    uint32_t* kept;                 // scratch [ray]: samples kept by compositing
+    uint32_t* block_totals;         // scratch [ray blocks]
+    uint32_t batch;                 // NETWORK_BATCH_SIZE
+};
+
+__device__ __forceinline__ uint32_t loss_rays(const LossParams& p) {
+    const uint32_t n = p.ray_counter != nullptr ? *p.ray_counter : p.rays_per_batch;
+    return min(n, p.rays_per_batch);
+}
+
+// Target pixel and random background of ray `ray_index` in this step (ngp.train.cu:781-796).
+__device__ __forceinline__ void ray_target(const LossParams& p, uint32_t ray_index, float3& bg, float3& target) {
+    Pcg32 rng{kTrainSeed};
+    rng.advance(static_cast<uint64_t>(p.step) << 32u);
+    rng.advance(static_cast<uint64_t>(ray_index) * kRandPerRay);
+    const uint32_t image = static_cast<uint32_t>((static_cast<uint64_t>(ray_index) * p.frame_count) / p.rays_per_batch) % p.frame_count;
+    float u = rng.next_float(), v = rng.next_float();
+    uint32_t px = min(static_cast<uint32_t>(u * static_cast<float>(p.width)), p.width - 1u);
+    uint32_t py = min(static_cast<uint32_t>(v * static_cast<float>(p.height)), p.height - 1u);
+    u           = (static_cast<float>(px) + 0.5f) / static_cast<float>(p.width);
+    v           = (static_cast<float>(py) + 0.5f) / static_cast<float>(p.height);
+    bg          = {rng.next_float(), rng.next_float(), rng.next_float()};
+    px          = min(static_cast<uint32_t>(u * static_cast<float>(p.width)), p.width - 1u);
+    py          = min(static_cast<uint32_t>(v * static_cast<float>(p.height)), p.height - 1u);
+    const float4 texel = read_texel(px, py, image, p.width, p.height, p.pixels);
+    const float3 bgl   = {srgb_to_linear_c(bg.x), srgb_to_linear_c(bg.y), srgb_to_linear_c(bg.z)};
+    target = {linear_to_srgb_c(__fmaf_rn(1.0f - texel.w, bgl.x, texel.x)), linear_to_srgb_c(__fmaf_rn(1.0f - texel.w, bgl.y, texel.y)),
+              linear_to_srgb_c(__fmaf_rn(1.0f - texel.w, bgl.z, texel.z))};
+}
+
+__device__ __forceinline__ void load_output(const __half* o, float& r, float& g, float& b, float& d) {
+    const uint2 v    = *reinterpret_cast<const uint2*>(o);
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    const float2 rg = __half22float2(h[0]), bd = __half22float2(h[1]);
+    r = rg.x, g = rg.y, b = bd.x, d = bd.y;
+}
+
+// Pass 1 (first loop of K11, ngp.train.cu:751-802): composite, count the kept samples.
+__global__ void __launch_bounds__(kThreads) loss_pass1_kernel(const __grid_constant__ LossParams p) {
+    const uint32_t n = loss_rays(p);
+    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+    uint32_t kept    = 0;
+    if (i < n) {
+        const uint32_t steps = p.numsteps[2u * i], base = p.numsteps[2u * i + 1u];
+        const __half* out    = p.network_output + static_cast<uint64_t>(base) * 16u;
+        const float* c       = p.coords + static_cast<uint64_t>(base) * 7u;
+        float T              = 1.0f;
+        float3 rgb           = {0.0f, 0.0f, 0.0f};
+        for (; kept < steps; ++kept) {
+            if (T < kTransmittanceEps) break;
+            float r, g, b, d;
+            load_output(out + static_cast<uint64_t>(kept) * 16u, r, g, b, d);
+            const float alpha  = 1.0f - __expf(-expf(d) * c[static_cast<uint64_t>(kept) * 7u + 3u]);
+            const float weight = alpha * T;
+            rgb.x              = __fmaf_rn(weight, sigmoidf_(r), rgb.x);
+            rgb.y              = __fmaf_rn(weight, sigmoidf_(g), rgb.y);
+            rgb.z              = __fmaf_rn(weight, sigmoidf_(b), rgb.z);
+            T *= 1.0f - alpha;
+        }
+        if (kept == steps) {
+            float3 bg, target;
+            ray_target(p, p.ray_indices != nullptr ? p.ray_indices[i] : i, bg, target);
+            rgb.x = __fmaf_rn(T, bg.x, rgb.x);
+            rgb.y = __fmaf_rn(T, bg.y, rgb.y);
+            rgb.z = __fmaf_rn(T, bg.z, rgb.z);
+        }
+        p.ray_rgb[i] = make_float4(rgb.x, rgb.y, rgb.z, 0.0f);
+        p.kept[i]    = kept;
+    }
+    uint32_t total;
+    block_exclusive_scan(kept, total);
+    if (threadIdx.x == 0) p.block_totals[blockIdx.x] = total;
+}
+
+// Pass 2 (rest of K11, ngp.train.cu:804-859): clamp to the batch, copy the kept samples, write
+// dL/d(raw rgb) and dL/d(raw density) per sample, scaled by 128 / rays_per_batch.
+__global__ void __launch_bounds__(kThreads) loss_pass2_kernel(const __grid_constant__ LossParams p) {
+    const uint32_t n = loss_rays(p);
+    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+    const uint32_t k = i < n ? p.kept[i] : 0u;
+    uint32_t total;
+    const uint32_t cbase = p.block_totals[blockIdx.x] + block_exclusive_scan(k, total);
+    if (i >= n) return;
+    const uint32_t remaining = cbase < p.batch ? p.batch - cbase : 0u;
+    const uint32_t cn        = k < remaining ? k : remaining;
+    const uint32_t base      = p.numsteps[2u * i + 1u];
+    p.numsteps[2u * i]       = cn;
+    p.numsteps[2u * i + 1u]  = cbase;
+    if (cn == 0) return;
+
+    float3 bg, target;
+    ray_target(p, p.ray_indices != nullptr ? p.ray_indices[i] : i, bg, target);
+    const float4 rr   = p.ray_rgb[i];
+    const float3 rgb  = {rr.x, rr.y, rr.z};
+    const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
+    const float3 grad = {2.0f * diff.x, 2.0f * diff.y, 2.0f * diff.z};
+    if (p.loss_output != nullptr)
+        p.loss_output[i] = __fmaf_rn(diff.z, diff.z, __fmaf_rn(diff.x, diff.x, diff.y * diff.y)) / (3.0f * static_cast<float>(p.rays_per_batch));
+    const float scale   = kLossScale / static_cast<float>(p.rays_per_batch);
+    const float* ray    = p.rays + static_cast<uint64_t>(i) * 6u;
+    const float3 origin = {ray[0], ray[1], ray[2]};
+    const float* cin    = p.coords + static_cast<uint64_t>(base) * 7u;
+    const __half* out   = p.network_output + static_cast<uint64_t>(base) * 16u;
+    float* cout         = p.coords_out + static_cast<uint64_t>(cbase) * 7u;
+    __half* dout        = p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u;
+    float T             = 1.0f;
+    float3 acc          = {0.0f, 0.0f, 0.0f};
+    for (uint32_t j = 0; j < cn; ++j) {
+        const float* c = cin + static_cast<uint64_t>(j) * 7u;
+        float* co      = cout + static_cast<uint64_t>(j) * 7u;
+#pragma unroll
+        for (int q = 0; q < 7; ++q) co[q] = c[q];
+        const float depth = norm3df(c[0] - origin.x, c[1] - origin.y, c[2] - origin.z);
+        const float dt    = c[3];
+        float mr, mg, mb, md;
+        load_output(out + static_cast<uint64_t>(j) * 16u, mr, mg, mb, md);
+        const float3 col   = {sigmoidf_(mr), sigmoidf_(mg), sigmoidf_(mb)};
+        const float alpha  = 1.0f - __expf(-expf(md) * dt);
+        const float weight = alpha * T;
+        acc.x              = __fmaf_rn(weight, col.x, acc.x);
+        acc.y              = __fmaf_rn(weight, col.y, acc.y);
+        acc.z              = __fmaf_rn(weight, col.z, acc.z);
+        T *= 1.0f - alpha;
+        const float3 suffix = {rgb.x - acc.x, rgb.y - acc.y, rgb.z - acc.z};
+        const float g0      = scale * (weight * grad.x * (col.x * (1.0f - col.x)));
+        const float g1      = scale * (weight * grad.y * (col.y * (1.0f - col.y)));
+        const float g2      = scale * (weight * grad.z * (col.z * (1.0f - col.z)));
+        const float dd      = expf(fminf(fmaxf(md, -15.0f), 15.0f));
+        const float sum = __fmaf_rn(grad.z, __fmaf_rn(T, col.z, -suffix.z),
+                                    __fmaf_rn(grad.x, __fmaf_rn(T, col.x, -suffix.x), grad.y * __fmaf_rn(T, col.y, -suffix.y)));
+        const float g3  = __fmaf_rn(scale, dd * (dt * sum), (md > -10.0f && depth < 0.1f) ? 1e-4f : 0.0f);
+        uint4* d        = reinterpret_cast<uint4*>(dout + static_cast<uint64_t>(j) * 16u);
+        __half2 h01 = __floats2half2_rn(g0, g1), h23 = __floats2half2_rn(g2, g3);
+        d[0]        = make_uint4(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23), 0u, 0u);
+        d[1]        = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+__global__ void __launch_bounds__(1024) scan_kept_kernel(uint32_t* __restrict__ totals, uint32_t n_blocks, uint32_t* __restrict__ compacted_counter,
+                                                         uint32_t batch) {
+    uint32_t carry = 0;
+    for (uint32_t b = 0; b < n_blocks; b += 1024u) {
+        const uint32_t k = b + threadIdx.x;
+        const uint32_t v = k < n_blocks ? totals[k] : 0u;
+        uint32_t sum;
+        const uint32_t ex = block_exclusive_scan(v, sum);
+        if (k < n_blocks) totals[k] = carry + ex;
+        carry += sum;
+    }
+    if (threadIdx.x == 0) *compacted_counter = carry < batch ? carry : batch;
+}
+
+// K12 + K13 (ngp.train.cu:862-874): fill the batch tail [n, batch) by wrap-around copies of the
+// first n samples; the copied gradients are scaled by n / batch.
+__global__ void pad_batch_kernel(const uint32_t* __restrict__ count, float* __restrict__ coords, __half* __restrict__ dloss, uint32_t batch) {
+    const uint32_t n = *count;
+    const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;  // row of the batch
+    if (n == 0 || r < n || r >= batch) return;
+    const uint32_t src = r % n;
+#pragma unroll
+    for (int q = 0; q < 7; ++q) coords[static_cast<uint64_t>(r) * 7u + q] = coords[static_cast<uint64_t>(src) * 7u + q];
+    const float s = static_cast<float>(n) / static_cast<float>(batch);
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+        dloss[static_cast<uint64_t>(r) * 16u + q] = __float2half(__half2float(dloss[static_cast<uint64_t>(src) * 16u + q]) * s);
+}
+
+// Evaluation compositing (K10, ngp.train.cu:676-745) for a set of pixels of one image: clamp to
+// [0,1], squared error against the sRGB target (fp64 block sums), optional side-by-side
+// comparison pixels (target left, render right) and rendered colours.
+__global__ void __launch_bounds__(kThreads) eval_composite_kernel(uint32_t n_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width,
+                                                                  uint32_t height, const uint8_t* __restrict__ pixels,
+                                                                  const uint32_t* __restrict__ numsteps, const float* __restrict__ coords,
+                                                                  const __half* __restrict__ network_output, double* __restrict__ sse,
+                                                                  uint8_t* __restrict__ comparison, float* __restrict__ rendered) {
+    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+    double se        = 0.0;
+    if (i < n_pixels) {
+        const uint32_t gp = pixel_offset + i, px = gp % width, py = gp / width;
+        const uint32_t steps = numsteps[2u * i], base = numsteps[2u * i + 1u];
+        float T    = 1.0f;
+        float3 rgb = {0.0f, 0.0f, 0.0f};
+        for (uint32_t j = 0; j < steps; ++j) {
+            float r, g, b, d;
+            load_output(network_output + (static_cast<uint64_t>(base) + j) * 16u, r, g, b, d);
+            const float alpha  = 1.0f - __expf(-expf(d) * coords[(static_cast<uint64_t>(base) + j) * 7u + 3u]);
+            const float weight = alpha * T;
+            rgb.x              = __fmaf_rn(weight, sigmoidf_(r), rgb.x);
+            rgb.y              = __fmaf_rn(weight, sigmoidf_(g), rgb.y);
+            rgb.z              = __fmaf_rn(weight, sigmoidf_(b), rgb.z);
+            T *= 1.0f - alpha;
+            if (T < kTransmittanceEps) break;
+        }
+        const float3 pr = {fminf(fmaxf(rgb.x, 0.0f), 1.0f), fminf(fmaxf(rgb.y, 0.0f), 1.0f), fminf(fmaxf(rgb.z, 0.0f), 1.0f)};
+        if (pixels != nullptr) {
+            const float4 tx = read_texel(px, py, image, width, height, pixels);
+            const float3 tg = {fminf(fmaxf(linear_to_srgb_c(tx.x), 0.0f), 1.0f), fminf(fmaxf(linear_to_srgb_c(tx.y), 0.0f), 1.0f),
+                               fminf(fmaxf(linear_to_srgb_c(tx.z), 0.0f), 1.0f)};
+            const double dr = static_cast<double>(pr.x) - tg.x, dg = static_cast<double>(pr.y) - tg.y, db = static_cast<double>(pr.z) - tg.z;
+            se              = dr * dr + dg * dg + db * db;
+            if (comparison != nullptr) {
+                const uint64_t row = static_cast<uint64_t>(py) * width * 6u;
+                uint8_t* t         = comparison + row + px * 3u;
+                uint8_t* q         = comparison + row + (static_cast<uint64_t>(width) + px) * 3u;
+                t[0] = static_cast<uint8_t>(tg.x * 255.0f + 0.5f), t[1] = static_cast<uint8_t>(tg.y * 255.0f + 0.5f),
+                t[2] = static_cast<uint8_t>(tg.z * 255.0f + 0.5f);
+                q[0] = static_cast<uint8_t>(pr.x * 255.0f + 0.5f), q[1] = static_cast<uint8_t>(pr.y * 255.0f + 0.5f),
+                q[2] = static_cast<uint8_t>(pr.z * 255.0f + 0.5f);
+            }
+        }
+        if (rendered != nullptr) {
+            float* o = rendered + static_cast<uint64_t>(gp) * 3u;
+            o[0] = pr.x, o[1] = pr.y, o[2] = pr.z;
+        }
+    }
+#pragma unroll
+    for (uint32_t o = 16; o > 0; o >>= 1) se += __shfl_down_sync(0xFFFFFFFFu, se, o);
+    __shared__ double ws[kThreads / 32];
+    if ((threadIdx.x & 31u) == 0) ws[threadIdx.x >> 5] = se;
+    __syncthreads();
+    if (threadIdx.x == 0 && sse != nullptr) {
+        double tot = 0.0;
+        for (uint32_t w = 0; w < kThreads / 32; ++w) tot += ws[w];
+        atomicAdd(sse, tot);
+    }
+}
+
+}  // namespace
+}  // namespace ngp
+
+using namespace ngp;
+
+extern "C" uint32_t ngp_loss_scratch_bytes(uint32_t max_rays) {
+    const uint32_t blocks = (max_rays + kThreads - 1) / kThreads;
+    return max_rays * (16u + 4u) + blocks * 4u + 256u;
+}
+
+extern "C" int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                             uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                             uint32_t* compacted_counter, const uint32_t* ray_indices, const float* rays, uint32_t* numsteps,
+                                             const float* coords, float* compacted_coords, uint16_t* dloss_doutput, float* loss_values,
+                                             void* scratch, size_t scratch_bytes, void* stream) {
+    clear_error();
+    if (rays_per_batch == 0) return NGP_OK;
+    if (pixels == nullptr || network_output == nullptr || compacted_counter == nullptr || rays == nullptr || numsteps == nullptr ||
+        coords == nullptr || compacted_coords == nullptr || dloss_doutput == nullptr || scratch == nullptr || frame_count == 0 || width == 0 ||
+        height == 0)
+        return fail(NGP_ERR_INVALID, "training loss: invalid input");
+    if (scratch_bytes < ngp_loss_scratch_bytes(rays_per_batch)) return fail(NGP_ERR_INVALID, "training loss: scratch too small");
+    if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "training loss: scratch must be 16-byte aligned");
+    const cudaStream_t s  = as_stream(stream);
+    const uint32_t blocks = (rays_per_batch + kThreads - 1) / kThreads;
+    unsigned char* sc     = static_cast<unsigned char*>(scratch);
+    LossParams p{};
+    p.rays_per_batch = rays_per_batch;
+    p.step           = step;
+    p.ray_counter    = ray_counter;
+    p.pixels         = pixels;
+    p.frame_count    = frame_count;
+    p.width          = width;
+    p.height         = height;
+    p.network_output = reinterpret_cast<const __half*>(network_output);
+    p.ray_indices    = ray_indices;
+    p.rays           = rays;
+    p.numsteps       = numsteps;
+    p.coords         = coords;
+    p.coords_out     = compacted_coords;
+    p.dloss_doutput  = reinterpret_cast<__half*>(dloss_doutput);
+    p.loss_output    = loss_values;
+    p.ray_rgb        = reinterpret_cast<float4*>(sc);
+    p.kept           = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(rays_per_batch) * 16u);
+    p.block_totals   = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(rays_per_batch) * 20u);
+    p.batch          = kNetworkBatch;
+    if (loss_values != nullptr) NGP_TRY(check_cuda(cudaMemsetAsync(loss_values, 0, sizeof(float) * rays_per_batch, s), "training loss: clear"));
+    loss_pass1_kernel<<<blocks, kThreads, 0, s>>>(p);
+    NGP_TRY(check_launch("loss_pass1_kernel"));
+    scan_kept_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, compacted_counter, kNetworkBatch);
+    NGP_TRY(check_launch("scan_kept_kernel"));
+    loss_pass2_kernel<<<blocks, kThreads, 0, s>>>(p);
+    return check_launch("loss_pass2_kernel");
+}
+
+extern "C" int ngp_pad_training_batch(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, void* stream) {
+    clear_error();
+    if (compacted_counter == nullptr || compacted_coords == nullptr || dloss_doutput == nullptr) return fail(NGP_ERR_INVALID, "pad batch: null pointer");
+    pad_batch_kernel<<<kNetworkBatch / 256u, 256, 0, as_stream(stream)>>>(compacted_counter, compacted_coords, reinterpret_cast<__half*>(dloss_doutput),
+                                                                            kNetworkBatch);
+    return check_launch("pad_batch_kernel");
+}
+
+extern "C" int ngp_eval_composite(uint32_t n_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,
+                                  const uint32_t* numsteps, const float* coords, const uint16_t* network_output, double* sse,
+                                  uint8_t* comparison, float* rendered, void* stream) {
+    clear_error();
+    if (n_pixels == 0) return NGP_OK;
+    if (numsteps == nullptr || coords == nullptr || network_output == nullptr) return fail(NGP_ERR_INVALID, "eval composite: null pointer");
+    eval_composite_kernel<<<(n_pixels + kThreads - 1) / kThreads, kThreads, 0, as_stream(stream)>>>(
+        n_pixels, pixel_offset, image, width, height, pixels, numsteps, coords, reinterpret_cast<const __half*>(network_output), sse, comparison,
+        rendered);
+    return check_launch("eval_composite_kernel");
+}

@@ -1,0 +1,413 @@
+// Occupancy density grid (update + bitfield) and ray marching with deterministic compaction.
+//
+// Replaces the reference's K1-K8 (ngp.train.cu:310-667) and the host wrappers
+// update_density_grid / sample_training_batch / run_evaluation's sampling (1526-1595,
+// 1919-1930, 1618-1642).
+//
+// B200 design notes:
+// * Ray marching is count -> scan -> write: the count pass stores each ray's step count and a
+//   per-CTA total, one CTA scans the totals, and the write pass places every ray's samples at
+//   its prefix offset.  Sample order is therefore the ray order (deterministic, and coalesced
+//   for the network that consumes it) instead of the reference's atomic slot order.
+// * The grid mean is a fixed-order two-level reduction (deterministic), fused with the EMA.
+// * The occupancy bitfield (256 KB) stays L2/L1 resident for the marching kernels.
+#include <cmath>
+
+#include "sampler.cuh"
+
+namespace ngp {
+namespace {
+
+constexpr uint32_t kThreads = 128u;
+
+// ------------------------------------------------------------------------------------------
+// density grid
+// ------------------------------------------------------------------------------------------
+
+// K1 (ngp.train.cu:310-381): a cell is "trained" when any corner projects into some training
+// view along a ray that matches the pixel's camera ray; untrained cells get -1.
+__global__ void mark_untrained_kernel(float* __restrict__ values, const CameraSet cam) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= kGridCells) return;
+    const uint32_t x = morton_compact(i), y = morton_compact(i >> 1), z = morton_compact(i >> 2);
+    constexpr float voxel = 1.0f / 128.0f;
+    const float3 cmin     = {static_cast<float>(x) * voxel, static_cast<float>(y) * voxel, static_cast<float>(z) * voxel};
+    bool trained          = false;
+    for (uint32_t frame = 0; frame < cam.frame_count && !trained; ++frame) {
+        const float* f  = cam.camera + static_cast<uint64_t>(frame) * 12u;
+        const float3 cx = {f[0], f[1], f[2]}, cy = {f[3], f[4], f[5]}, cz = {f[6], f[7], f[8]}, o = {f[9], f[10], f[11]};
+        for (uint32_t corner = 0; corner < 8 && !trained; ++corner) {
+            const float3 pos = {cmin.x + ((corner & 1u) ? voxel : 0.0f), cmin.y + ((corner & 2u) ? voxel : 0.0f),
+                                cmin.z + ((corner & 4u) ? voxel : 0.0f)};
+            const float3 rel = {pos.x - o.x, pos.y - o.y, pos.z - o.z};
+            const float dist = norm3df(rel.x, rel.y, rel.z);
+            if (dist <= 0.0f) continue;
+            const float lx = __fmaf_rn(rel.z, cx.z, __fmaf_rn(rel.x, cx.x, rel.y * cx.y));
+            const float ly = __fmaf_rn(rel.z, cy.z, __fmaf_rn(rel.x, cy.x, rel.y * cy.y));
+            const float lz = __fmaf_rn(rel.z, cz.z, __fmaf_rn(rel.x, cz.x, rel.y * cz.y));
+            if (lz / dist < 1e-4f) continue;
+            const float px = lx * cam.focal_x / lz + cam.principal_x;
+            const float py = ly * cam.focal_y / lz + cam.principal_y;
+            if (px <= 0.0f || py <= 0.0f || px >= static_cast<float>(cam.width) || py >= static_cast<float>(cam.height)) continue;
+            const float rx  = (px - cam.principal_x) / cam.focal_x;
+            const float ry  = (py - cam.principal_y) / cam.focal_y;
+            const float3 rd = {__fmaf_rn(cx.x, rx, cy.x * ry) + cz.x, __fmaf_rn(cx.y, rx, cy.y * ry) + cz.y, __fmaf_rn(cx.z, rx, cy.z * ry) + cz.z};
+            const float rl  = norm3df(rd.x, rd.y, rd.z);
+            if (rl <= 0.0f) continue;
+            const float3 rn = {rd.x / rl, rd.y / rl, rd.z / rl};
+            const float3 dn = {rel.x / dist, rel.y / dist, rel.z / dist};
+            trained         = norm3df(rn.x - dn.x, rn.y - dn.y, rn.z - dn.z) < 1e-3f;
+        }
+    }
+    values[i] = trained ? 0.0f : -1.0f;
+}
+
+// K2 (ngp.train.cu:383-424): sample positions for the grid update.  Samples [0, n_uniform) pick
+// cells uniformly; the rest take up to 10 hashed tries for a cell above the occupancy
+// threshold.  Each writes a 7-float record and its cell index.
+__global__ void generate_grid_samples_kernel(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* __restrict__ values,
+                                             float* __restrict__ coords, uint32_t* __restrict__ indices) {
+    const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n_uniform + n_nonuniform) return;
+    const bool uniform   = g < n_uniform;
+    const uint32_t i     = uniform ? g : g - n_uniform;
+    const uint32_t count = uniform ? n_uniform : n_nonuniform;
+    const float thresh   = uniform ? -0.01f : kMinOpticalThick;
+    Pcg32 rng{kTrainSeed};
+    rng.advance(((static_cast<uint64_t>(ema_step) * 2ull + (uniform ? 0ull : 1ull) + 1ull) << 32u) + static_cast<uint64_t>(i) * 4ull);
+    uint32_t idx = 0;
+    for (uint32_t j = 0; j < 10; ++j) {
+        idx = static_cast<uint32_t>(((static_cast<uint64_t>(i) + static_cast<uint64_t>(ema_step) * count) * 56924617ull +
+                                     static_cast<uint64_t>(j) * 19349663ull + 96925573ull) %
+                                    kGridCells);
+        if (values[idx] > thresh) break;
+    }
+    const uint32_t x = morton_compact(idx), y = morton_compact(idx >> 1), z = morton_compact(idx >> 2);
+    float* c   = coords + static_cast<uint64_t>(g) * 7u;
+    c[0]       = (static_cast<float>(x) + rng.next_float()) / 128.0f;
+    c[1]       = (static_cast<float>(y) + rng.next_float()) / 128.0f;
+    c[2]       = (static_cast<float>(z) + rng.next_float()) / 128.0f;
+    c[3]       = kConeStep;
+    c[4]       = 0.5f;
+    c[5]       = 0.5f;
+    c[6]       = 0.5f;
+    indices[g] = idx;
+}
+
+// K3 (ngp.train.cu:426-432): scratch[cell] = max(scratch[cell], exp(raw density) * dt).
+__global__ void splat_kernel(uint32_t n, const uint32_t* __restrict__ indices, const __half* __restrict__ density, float* __restrict__ scratch) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float thickness = expf(__half2float(density[i])) * kConeStep;
+    atomicMax(reinterpret_cast<uint32_t*>(scratch + indices[i]), __float_as_uint(thickness));
+}
+
+// K4 + first level of K5 (ngp.train.cu:434-461): EMA update of every cell, then per-CTA sums of
+// max(v, 0) in a fixed order.  1024 cells per CTA (256 threads x float4).
+__global__ void __launch_bounds__(256) ema_partial_kernel(const float* __restrict__ scratch, float* __restrict__ values, float decay,
+                                                          float* __restrict__ partial) {
+    const uint32_t q = blockIdx.x * 256u + threadIdx.x;  // float4 index
+    const float4 s   = reinterpret_cast<const float4*>(scratch)[q];
+    float4 v         = reinterpret_cast<float4*>(values)[q];
+    v.x              = v.x < 0.0f ? v.x : fmaxf(v.x * decay, s.x);
+    v.y              = v.y < 0.0f ? v.y : fmaxf(v.y * decay, s.y);
+    v.z              = v.z < 0.0f ? v.z : fmaxf(v.z * decay, s.z);
+    v.w              = v.w < 0.0f ? v.w : fmaxf(v.w * decay, s.w);
+    reinterpret_cast<float4*>(values)[q] = v;
+    float sum = ((fmaxf(v.x, 0.0f) + fmaxf(v.y, 0.0f)) + fmaxf(v.z, 0.0f)) + fmaxf(v.w, 0.0f);
+#pragma unroll
+    for (uint32_t o = 16; o > 0; o >>= 1) sum += __shfl_down_sync(0xFFFFFFFFu, sum, o);
+    __shared__ float warp_sum[8];
+    if ((threadIdx.x & 31u) == 0) warp_sum[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float total = 0.0f;
+        for (int w = 0; w < 8; ++w) total += warp_sum[w];
+        partial[blockIdx.x] = total;
+    }
+}
+
+// Rest of K5 + K6 (ngp.train.cu:443-474): the mean (sum of the 2048 partials, fixed order,
+// recomputed by every CTA), threshold = min(0.01, mean), 8 cells per byte in Morton order,
+// and the occupied-cell count.  Zeroes the scratch grid for the next update on the way.
+__global__ void __launch_bounds__(256) bitfield_kernel(const float* __restrict__ values, const float* __restrict__ partial, uint32_t n_partial,
+                                                       float* __restrict__ mean_out, uint8_t* __restrict__ bits, uint32_t* __restrict__ count,
+                                                       float* __restrict__ scratch) {
+    __shared__ float s_mean;
+    __shared__ uint32_t s_count[8];
+    if (threadIdx.x < 32) {
+        float acc = 0.0f;
+        for (uint32_t k = threadIdx.x; k < n_partial; k += 32) acc += partial[k];
+#pragma unroll
+        for (uint32_t o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xFFFFFFFFu, acc, o);
+        if (threadIdx.x == 0) {
+            s_mean = acc / static_cast<float>(kGridCells);
+            if (blockIdx.x == 0) *mean_out = s_mean;
+        }
+    }
+    __syncthreads();
+    const float thresh  = fminf(kMinOpticalThick, s_mean);
+    const uint32_t b    = blockIdx.x * 256u + threadIdx.x;  // byte index: cells 8b .. 8b+7
+    const float4 lo     = reinterpret_cast<const float4*>(values)[2u * b];
+    const float4 hi     = reinterpret_cast<const float4*>(values)[2u * b + 1u];
+    const uint32_t byte = (lo.x > thresh ? 1u : 0u) | (lo.y > thresh ? 2u : 0u) | (lo.z > thresh ? 4u : 0u) | (lo.w > thresh ? 8u : 0u) |
+                          (hi.x > thresh ? 16u : 0u) | (hi.y > thresh ? 32u : 0u) | (hi.z > thresh ? 64u : 0u) | (hi.w > thresh ? 128u : 0u);
+    bits[b] = static_cast<uint8_t>(byte);
+    reinterpret_cast<float4*>(scratch)[2u * b]      = make_float4(0.f, 0.f, 0.f, 0.f);
+    reinterpret_cast<float4*>(scratch)[2u * b + 1u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t c = __popc(byte);
+#pragma unroll
+    for (uint32_t o = 16; o > 0; o >>= 1) c += __shfl_down_sync(0xFFFFFFFFu, c, o);
+    if ((threadIdx.x & 31u) == 0) s_count[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t total = 0;
+        for (int w = 0; w < 8; ++w) total += s_count[w];
+        atomicAdd(count, total);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// marching
+// ------------------------------------------------------------------------------------------
+struct MarchParams {
+    CameraSet cam;                // training rays from cameras, or
+    const float* rays_in;         // explicit rays [n][6] (origin, unit direction)
+    int jitter;                   // explicit rays: 1 = training PCG start jitter, 0 = half step
+    uint32_t step;                // training step (PCG stream)
+    const uint32_t* n_rays_dev;   // optional device-side ray count (<= n_rays)
+    uint32_t n_rays;
+    const uint8_t* bits;
+    uint32_t* numsteps;           // [n][2] (count, base) per ray
+    uint32_t* block_totals;       // per-CTA sample totals
+    float* rays_out;              // training: [n][6] origin + unnormalised direction
+    uint32_t* ray_indices;        // training: identity
+    float* coords;                // sample records
+    uint32_t sample_limit;
+    uint32_t* ray_counter;
+    uint32_t* sample_counter;     // total samples before the limit
+};
+
+__device__ __forceinline__ uint32_t march_ray_count(const MarchParams& p) { return p.n_rays_dev != nullptr ? min(*p.n_rays_dev, p.n_rays) : p.n_rays; }
+
+__device__ __forceinline__ bool setup_ray(const MarchParams& p, uint32_t i, uint32_t n, TrainRay& r) {
+    if (p.rays_in == nullptr) return make_train_ray(i, n, p.step, p.cam, r);
+    const float* q = p.rays_in + static_cast<uint64_t>(i) * 6u;
+    r.origin       = {q[0], q[1], q[2]};
+    r.dir          = {q[3], q[4], q[5]};
+    r.dir_raw      = r.dir;
+    float tmin;
+    if (!intersect_unit_cube(r.origin, r.dir, tmin)) return false;
+    if (p.jitter) {
+        Pcg32 rng{kTrainSeed};
+        rng.advance(static_cast<uint64_t>(p.step) << 32u);
+        rng.advance(static_cast<uint64_t>(i) * kRandPerRay);
+        rng.next_float();
+        rng.next_float();
+        r.start_t = __fmaf_rn(rng.next_float(), kConeStep, tmin);
+    } else {
+        r.start_t = tmin + 0.5f * kConeStep;
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kThreads) march_count_kernel(const __grid_constant__ MarchParams p) {
+    const uint32_t n = march_ray_count(p);
+    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+    uint32_t steps   = 0;
+    if (i < n) {
+        TrainRay r{};
+        if (setup_ray(p, i, n, r)) steps = march_count(r.origin, r.dir, r.start_t, p.bits);
+        p.numsteps[2u * i] = steps;
+        if (p.rays_out != nullptr) {
+            float* o = p.rays_out + static_cast<uint64_t>(i) * 6u;
+            o[0] = r.origin.x, o[1] = r.origin.y, o[2] = r.origin.z, o[3] = r.dir_raw.x, o[4] = r.dir_raw.y, o[5] = r.dir_raw.z;
+        }
+        if (p.ray_indices != nullptr) p.ray_indices[i] = i;
+    }
+    uint32_t total;
+    block_exclusive_scan(steps, total);
+    if (threadIdx.x == 0) p.block_totals[blockIdx.x] = total;
+}
+
+// One CTA: exclusive scan of the per-CTA totals in place; writes the grand total.
+__global__ void __launch_bounds__(1024) scan_totals_kernel(uint32_t* __restrict__ totals, uint32_t n_blocks, const uint32_t* n_rays_dev,
+                                                           uint32_t n_rays, uint32_t* __restrict__ grand_total, uint32_t* __restrict__ ray_counter) {
+    uint32_t carry = 0;
+    for (uint32_t base = 0; base < n_blocks; base += 1024u) {
+        const uint32_t k = base + threadIdx.x;
+        const uint32_t v = k < n_blocks ? totals[k] : 0u;
+        uint32_t sum;
+        const uint32_t ex = block_exclusive_scan(v, sum);
+        if (k < n_blocks) totals[k] = carry + ex;
+        carry += sum;
+    }
+    if (threadIdx.x == 0) {
+        if (grand_total != nullptr) *grand_total = carry;
+        if (ray_counter != nullptr) *ray_counter = n_rays_dev != nullptr ? min(*n_rays_dev, n_rays) : n_rays;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) march_write_kernel(const __grid_constant__ MarchParams p) {
+    const uint32_t n     = march_ray_count(p);
+    const uint32_t i     = blockIdx.x * kThreads + threadIdx.x;
+    const uint32_t steps = i < n ? p.numsteps[2u * i] : 0u;
+    uint32_t total;
+    const uint32_t base = p.block_totals[blockIdx.x] + block_exclusive_scan(steps, total);
+    if (i >= n) return;
+    // rays whose samples would cross the sample limit are dropped (ngp.train.cu:537-538)
+    const uint32_t kept     = base + steps <= p.sample_limit ? steps : 0u;
+    p.numsteps[2u * i]      = kept;
+    p.numsteps[2u * i + 1u] = kept ? base : 0u;
+    if (kept == 0) return;
+    TrainRay r{};
+    setup_ray(p, i, n, r);
+    march_write(r.origin, r.dir, r.start_t, kept, p.bits, p.coords + static_cast<uint64_t>(base) * 7u);
+}
+
+// Evaluation pixel rays (ngp.train.cu:587-614): pixel centre through the pinhole camera,
+// normalised direction.  A degenerate ray gets a NaN origin, which yields no samples.
+__global__ void eval_rays_kernel(const CameraSet cam, uint32_t image, uint32_t pixel_offset, uint32_t n, float* __restrict__ rays) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint32_t gp = pixel_offset + i, px = gp % cam.width, py = gp / cam.width;
+    const float* f    = cam.camera + static_cast<uint64_t>(image) * 12u;
+    const float rx    = (static_cast<float>(px) + 0.5f - cam.principal_x) / cam.focal_x;
+    const float ry    = (static_cast<float>(py) + 0.5f - cam.principal_y) / cam.focal_y;
+    float3 d          = {__fmaf_rn(f[0], rx, f[3] * ry) + f[6], __fmaf_rn(f[1], rx, f[4] * ry) + f[7], __fmaf_rn(f[2], rx, f[5] * ry) + f[8]};
+    if (d.x == 0.0f && d.y == 0.0f && d.z == 0.0f) d = {f[6], f[7], f[8]};
+    const float len = norm3df(d.x, d.y, d.z);
+    float* o        = rays + static_cast<uint64_t>(i) * 6u;
+    if (len == 0.0f) {
+        o[0] = o[1] = o[2] = __int_as_float(0x7fc00000);
+        o[3] = 1.0f, o[4] = 0.0f, o[5] = 0.0f;
+        return;
+    }
+    o[0] = f[9], o[1] = f[10], o[2] = f[11];
+    o[3] = d.x / len, o[4] = d.y / len, o[5] = d.z / len;
+}
+
+int launch_march(const MarchParams& p, cudaStream_t s) {
+    const uint32_t blocks = (p.n_rays + kThreads - 1) / kThreads;
+    march_count_kernel<<<blocks, kThreads, 0, s>>>(p);
+    NGP_TRY(check_launch("march_count_kernel"));
+    scan_totals_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, p.n_rays_dev, p.n_rays, p.sample_counter, p.ray_counter);
+    NGP_TRY(check_launch("scan_totals_kernel"));
+    march_write_kernel<<<blocks, kThreads, 0, s>>>(p);
+    return check_launch("march_write_kernel");
+}
+
+CameraSet camera_set(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float fx, float fy, float cx, float cy) {
+    return CameraSet{camera, frame_count, width, height, fx, fy, cx, cy};
+}
+bool camera_ok(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float fx, float fy, float cx, float cy) {
+    return camera != nullptr && frame_count > 0 && width > 0 && height > 0 && fx > 0.0f && fy > 0.0f && std::isfinite(cx) && std::isfinite(cy);
+}
+
+}  // namespace
+}  // namespace ngp
+
+using namespace ngp;
+
+extern "C" uint32_t ngp_march_block_totals(uint32_t max_rays) { return (max_rays + kThreads - 1) / kThreads; }
+
+extern "C" int ngp_density_grid_mark_untrained(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x,
+                                               float focal_y, float principal_x, float principal_y, float* values, void* stream) {
+    clear_error();
+    if (!camera_ok(camera, frame_count, width, height, focal_x, focal_y, principal_x, principal_y) || values == nullptr)
+        return fail(NGP_ERR_INVALID, "mark untrained: invalid input");
+    mark_untrained_kernel<<<kGridCells / 128u, 128, 0, as_stream(stream)>>>(
+        values, camera_set(camera, frame_count, width, height, focal_x, focal_y, principal_x, principal_y));
+    return check_launch("mark_untrained_kernel");
+}
+
+extern "C" int ngp_density_grid_samples(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords,
+                                        uint32_t* indices, void* stream) {
+    clear_error();
+    const uint32_t n = n_uniform + n_nonuniform;
+    if (n == 0) return NGP_OK;
+    if (values == nullptr || coords == nullptr || indices == nullptr) return fail(NGP_ERR_INVALID, "grid samples: null pointer");
+    generate_grid_samples_kernel<<<(n + 127) / 128, 128, 0, as_stream(stream)>>>(n_uniform, n_nonuniform, ema_step, values, coords, indices);
+    return check_launch("generate_grid_samples_kernel");
+}
+
+extern "C" int ngp_density_grid_splat(uint32_t n, const uint32_t* indices, const uint16_t* density, float* scratch, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (indices == nullptr || density == nullptr || scratch == nullptr) return fail(NGP_ERR_INVALID, "grid splat: null pointer");
+    splat_kernel<<<(n + 127) / 128, 128, 0, as_stream(stream)>>>(n, indices, reinterpret_cast<const __half*>(density), scratch);
+    return check_launch("splat_kernel");
+}
+
+extern "C" uint32_t ngp_density_grid_partials(void) { return kGridCells / 1024u; }
+
+extern "C" int ngp_density_grid_update(float* values, float* scratch, float decay, float* partial, float* mean, uint8_t* bitfield,
+                                       uint32_t* occupied_count, void* stream) {
+    clear_error();
+    if (values == nullptr || scratch == nullptr || partial == nullptr || mean == nullptr || bitfield == nullptr || occupied_count == nullptr)
+        return fail(NGP_ERR_INVALID, "grid update: null pointer");
+    const cudaStream_t s = as_stream(stream);
+    ema_partial_kernel<<<kGridCells / 1024u, 256, 0, s>>>(scratch, values, decay, partial);
+    NGP_TRY(check_launch("ema_partial_kernel"));
+    NGP_TRY(check_cuda(cudaMemsetAsync(occupied_count, 0, sizeof(uint32_t), s), "grid update: clear count"));
+    bitfield_kernel<<<kGridCells / 8u / 256u, 256, 0, s>>>(values, partial, kGridCells / 1024u, mean, bitfield, occupied_count, scratch);
+    return check_launch("bitfield_kernel");
+}
+
+extern "C" int ngp_march_training_rays(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x, float focal_y,
+                                       float principal_x, float principal_y, uint32_t step, uint32_t rays_per_batch,
+                                       const uint32_t* rays_per_batch_dev, uint32_t sample_limit, const uint8_t* bitfield, float* coords,
+                                       float* rays, uint32_t* ray_indices, uint32_t* numsteps, uint32_t* block_totals, uint32_t* ray_counter,
+                                       uint32_t* sample_counter, void* stream) {
+    clear_error();
+    if (rays_per_batch == 0) return NGP_OK;
+    if (!camera_ok(camera, frame_count, width, height, focal_x, focal_y, principal_x, principal_y) || bitfield == nullptr || coords == nullptr ||
+        numsteps == nullptr || block_totals == nullptr || sample_limit == 0)
+        return fail(NGP_ERR_INVALID, "march training rays: invalid input");
+    MarchParams p{};
+    p.cam            = camera_set(camera, frame_count, width, height, focal_x, focal_y, principal_x, principal_y);
+    p.step           = step;
+    p.n_rays_dev     = rays_per_batch_dev;
+    p.n_rays         = rays_per_batch;
+    p.bits           = bitfield;
+    p.numsteps       = numsteps;
+    p.block_totals   = block_totals;
+    p.rays_out       = rays;
+    p.ray_indices    = ray_indices;
+    p.coords         = coords;
+    p.sample_limit   = sample_limit;
+    p.ray_counter    = ray_counter;
+    p.sample_counter = sample_counter;
+    return launch_march(p, as_stream(stream));
+}
+
+extern "C" int ngp_march_rays(uint32_t n_rays, const float* rays, int jitter, uint32_t step, const uint8_t* bitfield, uint32_t sample_limit,
+                              float* coords, uint32_t* numsteps, uint32_t* block_totals, uint32_t* sample_counter, void* stream) {
+    clear_error();
+    if (n_rays == 0) return NGP_OK;
+    if (rays == nullptr || bitfield == nullptr || coords == nullptr || numsteps == nullptr || block_totals == nullptr || sample_limit == 0)
+        return fail(NGP_ERR_INVALID, "march rays: invalid input");
+    MarchParams p{};
+    p.n_rays         = n_rays;
+    p.rays_in        = rays;
+    p.jitter         = jitter;
+    p.step           = step;
+    p.bits           = bitfield;
+    p.numsteps       = numsteps;
+    p.block_totals   = block_totals;
+    p.coords         = coords;
+    p.sample_limit   = sample_limit;
+    p.sample_counter = sample_counter;
+    return launch_march(p, as_stream(stream));
+}
+
+extern "C" int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,
+                                  float principal_x, float principal_y, uint32_t pixel_offset, uint32_t n, float* rays, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (!camera_ok(camera, image + 1u, width, height, focal_x, focal_y, principal_x, principal_y) || rays == nullptr)
+        return fail(NGP_ERR_INVALID, "eval rays: invalid input");
+    eval_rays_kernel<<<(n + 127) / 128, 128, 0, as_stream(stream)>>>(camera_set(camera, image + 1u, width, height, focal_x, focal_y, principal_x, principal_y),
+                                                                    image, pixel_offset, n, rays);
+    return check_launch("eval_rays_kernel");
+}

@@ -1,0 +1,213 @@
+// Device helpers shared by the occupancy grid, ray marching and compositing kernels.
+//
+// The geometric helpers restate the reference's (ngp.train.cu:195-308).  Their floating-point
+// expressions keep the reference's evaluation order; where the reference source has an a*b+c
+// form that the compiler contracts into one fused multiply-add, the fused form is written out
+// explicitly (__fmaf_rn), so sample positions are identical bit for bit.
+#pragma once
+
+#include "common.cuh"
+
+namespace ngp {
+
+constexpr uint32_t kGridSize      = 128u;
+constexpr uint32_t kGridCells     = kGridSize * kGridSize * kGridSize;
+constexpr uint32_t kMarchSteps    = 1024u;
+constexpr float kConeStep         = 1.73205080757f / 1024.0f;  // sqrt(3) / NERF_STEPS
+constexpr uint32_t kRandPerRay    = 16u;                       // MAX_RANDOM_SAMPLES_PER_RAY
+constexpr float kMinOpticalThick  = 0.01f;
+constexpr float kTransmittanceEps = 1e-4f;
+constexpr uint32_t kNetworkBatch  = 1u << 18;                  // NETWORK_BATCH_SIZE
+constexpr uint32_t kMaxSamples    = kNetworkBatch * 16u;       // MAX_SAMPLES
+constexpr uint32_t kBatchGranule  = 128u;
+constexpr float kLossScale        = 128.0f;
+
+// 3-bit interleave of a 7-bit coordinate (Morton order of the 128^3 grid).
+__host__ __device__ __forceinline__ uint32_t morton_spread(uint32_t v) {
+    v = (v * 0x00010001u) & 0xFF0000FFu;
+    v = (v * 0x00000101u) & 0x0F00F00Fu;
+    v = (v * 0x00000011u) & 0xC30C30C3u;
+    v = (v * 0x00000005u) & 0x49249249u;
+    return v;
+}
+__host__ __device__ __forceinline__ uint32_t morton_compact(uint32_t v) {
+    v &= 0x49249249u;
+    v = (v | (v >> 2u)) & 0xC30C30C3u;
+    v = (v | (v >> 4u)) & 0x0F00F00Fu;
+    v = (v | (v >> 8u)) & 0xFF0000FFu;
+    v = (v | (v >> 16u)) & 0x0000FFFFu;
+    return v;
+}
+
+__device__ __forceinline__ bool inside_unit_cube(float3 p) {
+    return p.x >= 0.0f && p.x <= 1.0f && p.y >= 0.0f && p.y <= 1.0f && p.z >= 0.0f && p.z <= 1.0f;
+}
+
+// Slab test against [0,1]^3; out_tmin = max(entry, 0).
+__device__ __forceinline__ bool intersect_unit_cube(float3 o, float3 d, float& out_tmin) {
+    const float3 inv = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
+    const float3 t0  = {-o.x * inv.x, -o.y * inv.y, -o.z * inv.z};
+    const float3 t1  = {(1.0f - o.x) * inv.x, (1.0f - o.y) * inv.y, (1.0f - o.z) * inv.z};
+    const float tmin = fmaxf(fmaxf(fminf(t0.x, t1.x), fminf(t0.y, t1.y)), fminf(t0.z, t1.z));
+    const float tmax = fminf(fminf(fmaxf(t0.x, t1.x), fmaxf(t0.y, t1.y)), fmaxf(t0.z, t1.z));
+    out_tmin         = fmaxf(tmin, 0.0f);
+    return tmax >= out_tmin;
+}
+
+__device__ __forceinline__ bool occupied(float3 p, const uint8_t* __restrict__ bits) {
+    const int x = static_cast<int>(p.x * 128.0f), y = static_cast<int>(p.y * 128.0f), z = static_cast<int>(p.z * 128.0f);
+    if (x < 0 || x >= 128 || y < 0 || y >= 128 || z < 0 || z >= 128) return false;
+    const uint32_t idx = morton_spread(static_cast<uint32_t>(x)) | (morton_spread(static_cast<uint32_t>(y)) << 1u) |
+                         (morton_spread(static_cast<uint32_t>(z)) << 2u);
+    return (__ldg(bits + idx / 8u) >> (idx % 8u)) & 1u;
+}
+
+// Jump to the next occupancy-voxel boundary, quantised to whole cone steps.
+__device__ __forceinline__ float skip_empty_voxel(float t, float3 pos, float3 dir, float3 inv_dir) {
+    const float3 p = {(pos.x - 0.5f) * 128.0f, (pos.y - 0.5f) * 128.0f, (pos.z - 0.5f) * 128.0f};
+    const float tx = (floorf(__fmaf_rn(0.5f, copysignf(1.0f, dir.x), p.x + 0.5f)) - p.x) * inv_dir.x;
+    const float ty = (floorf(__fmaf_rn(0.5f, copysignf(1.0f, dir.y), p.y + 0.5f)) - p.y) * inv_dir.y;
+    const float tz = (floorf(__fmaf_rn(0.5f, copysignf(1.0f, dir.z), p.z + 0.5f)) - p.z) * inv_dir.z;
+    const float t_target = t + fmaxf(fminf(fminf(tx, ty), tz) / 128.0f, 0.0f);
+    return __fmaf_rn(ceilf(fmaxf((t_target - t) / kConeStep, 0.5f)), kConeStep, t);
+}
+
+__device__ __forceinline__ float3 ray_point(float3 o, float3 d, float t) {
+    return {__fmaf_rn(d.x, t, o.x), __fmaf_rn(d.y, t, o.y), __fmaf_rn(d.z, t, o.z)};
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float srgb_to_linear_c(float v) { return v <= 0.04045f ? v / 12.92f : powf((v + 0.055f) / 1.055f, 2.4f); }
+__device__ __forceinline__ float linear_to_srgb_c(float v) { return v < 0.0031308f ? 12.92f * v : __fmaf_rn(1.055f, powf(v, 0.41666f), -0.055f); }
+
+// Premultiplied linear RGBA of an RGBA8 sRGB texel (ngp.train.cu:280-293).
+__device__ __forceinline__ float4 read_texel(uint32_t px, uint32_t py, uint32_t image, uint32_t width, uint32_t height,
+                                             const uint8_t* __restrict__ pixels) {
+    const uint32_t rgba = __ldg(reinterpret_cast<const uint32_t*>(pixels) + (px + static_cast<uint64_t>(py) * width +
+                                                                            static_cast<uint64_t>(image) * width * height));
+    float4 r = {static_cast<float>(rgba & 0xFFu) * (1.0f / 255.0f), static_cast<float>((rgba >> 8) & 0xFFu) * (1.0f / 255.0f),
+                static_cast<float>((rgba >> 16) & 0xFFu) * (1.0f / 255.0f), static_cast<float>(rgba >> 24) * (1.0f / 255.0f)};
+    r.x = srgb_to_linear_c(r.x) * r.w;
+    r.y = srgb_to_linear_c(r.y) * r.w;
+    r.z = srgb_to_linear_c(r.z) * r.w;
+    return r;
+}
+
+// Camera frames: 12 floats per frame = three axis columns and the origin (ngp.dataset.cpp:63).
+struct CameraSet {
+    const float* camera;
+    uint32_t frame_count, width, height;
+    float focal_x, focal_y, principal_x, principal_y;
+};
+
+// Training ray i of a batch (ngp.train.cu:480-517): image by stratified index, pixel from the
+// step's PCG32 stream (snapped to the pixel centre), direction through the pinhole camera.
+// Returns false when the ray misses the unit cube.
+struct TrainRay {
+    float3 origin, dir_raw, dir;
+    float start_t;
+};
+
+__device__ __forceinline__ bool make_train_ray(uint32_t i, uint32_t rays_per_batch, uint32_t step, const CameraSet& cam, TrainRay& r) {
+    const uint32_t image = static_cast<uint32_t>((static_cast<uint64_t>(i) * cam.frame_count) / rays_per_batch) % cam.frame_count;
+    const float* f       = cam.camera + static_cast<uint64_t>(image) * 12u;
+    Pcg32 rng{kTrainSeed};
+    rng.advance(static_cast<uint64_t>(step) << 32u);
+    rng.advance(static_cast<uint64_t>(i) * kRandPerRay);
+    float u = rng.next_float();
+    float v = rng.next_float();
+    const uint32_t px = min(static_cast<uint32_t>(u * static_cast<float>(cam.width)), cam.width - 1u);
+    const uint32_t py = min(static_cast<uint32_t>(v * static_cast<float>(cam.height)), cam.height - 1u);
+    u                 = (static_cast<float>(px) + 0.5f) / static_cast<float>(cam.width);
+    v                 = (static_cast<float>(py) + 0.5f) / static_cast<float>(cam.height);
+    const float ray_x = __fmaf_rn(u, static_cast<float>(cam.width), -cam.principal_x) / cam.focal_x;
+    const float ray_y = __fmaf_rn(v, static_cast<float>(cam.height), -cam.principal_y) / cam.focal_y;
+    r.origin          = {f[9], f[10], f[11]};
+    r.dir_raw = {__fmaf_rn(f[0], ray_x, f[3] * ray_y) + f[6], __fmaf_rn(f[1], ray_x, f[4] * ray_y) + f[7],
+                 __fmaf_rn(f[2], ray_x, f[5] * ray_y) + f[8]};
+    if (r.dir_raw.x == 0.0f && r.dir_raw.y == 0.0f && r.dir_raw.z == 0.0f) r.dir_raw = {f[6], f[7], f[8]};
+    const float len = norm3df(r.dir_raw.x, r.dir_raw.y, r.dir_raw.z);
+    if (len == 0.0f) return false;
+    r.dir = {r.dir_raw.x / len, r.dir_raw.y / len, r.dir_raw.z / len};
+    float tmin;
+    if (!intersect_unit_cube(r.origin, r.dir, tmin)) return false;
+    r.start_t = __fmaf_rn(rng.next_float(), kConeStep, tmin);
+    return true;
+}
+
+// Count the occupied cone steps along a ray (at most kMarchSteps).
+__device__ __forceinline__ uint32_t march_count(float3 o, float3 d, float start_t, const uint8_t* __restrict__ bits) {
+    const float3 inv = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
+    uint32_t n       = 0;
+    float t          = start_t;
+    while (n < kMarchSteps) {
+        const float3 pos = ray_point(o, d, t);
+        if (!inside_unit_cube(pos)) break;
+        if (occupied(pos, bits)) {
+            ++n;
+            t += kConeStep;
+        } else {
+            t = skip_empty_voxel(t, pos, d, inv);
+        }
+    }
+    return n;
+}
+
+// Re-march and write `n` 7-float sample records {pos, dt, (dir + 1) / 2} starting at `out`.
+__device__ __forceinline__ void march_write(float3 o, float3 d, float start_t, uint32_t n, const uint8_t* __restrict__ bits,
+                                            float* __restrict__ out) {
+    const float3 inv  = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
+    const float3 warp = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
+    float t           = start_t;
+    uint32_t j        = 0;
+    while (j < n) {
+        const float3 pos = ray_point(o, d, t);
+        if (!inside_unit_cube(pos)) break;
+        if (occupied(pos, bits)) {
+            float* c = out + static_cast<uint64_t>(j) * 7u;
+            c[0]     = pos.x;
+            c[1]     = pos.y;
+            c[2]     = pos.z;
+            c[3]     = kConeStep;
+            c[4]     = warp.x;
+            c[5]     = warp.y;
+            c[6]     = warp.z;
+            ++j;
+            t += kConeStep;
+        } else {
+            t = skip_empty_voxel(t, pos, d, inv);
+        }
+    }
+}
+
+// ---- block-wide exclusive scan of one uint32 per thread (blockDim.x multiple of 32, <= 1024) ----
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t& total) {
+    __shared__ uint32_t warp_sums[32];
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (uint32_t o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31u) warp_sums[warp] = x;
+    __syncthreads();
+    const uint32_t n_warps = blockDim.x >> 5;
+    if (warp == 0) {
+        uint32_t w = lane < n_warps ? warp_sums[lane] : 0u;
+#pragma unroll
+        for (uint32_t o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < n_warps) warp_sums[lane] = w;
+    }
+    __syncthreads();
+    total                 = warp_sums[n_warps - 1];
+    const uint32_t before = warp == 0 ? 0u : warp_sums[warp - 1];
+    __syncthreads();
+    return before + x - v;
+}
+
+}  // namespace ngp

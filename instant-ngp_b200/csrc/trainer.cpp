@@ -1,0 +1,476 @@
+// Trainer: owns every device buffer and runs the NeRF training step, validation and test
+// rendering on one stream.  Mirrors the reference's ngp::train::InstantNGP
+// (ngp.train.ixx:40-150, ngp.train.cpp:12-229): same step order, same adaptive batch rule,
+// same statistics; the device work is the library's own kernels.
+//
+// Differences from the reference, all B200-motivated:
+// * every buffer is sized once for the largest batch (no per-call attribute setting, no 2^18
+//   chunking of the inference pass: one launch covers up to 2^22 samples);
+// * the network forward of the compacted batch is not run: the backward recomputes its
+//   activations on chip from the encoded inputs;
+// * gradients are fp32 and Adam clears the grid gradient in the same pass;
+// * evaluation renders whole 2^18-pixel tiles instead of 4096-pixel tiles.
+#include <algorithm>
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "sampler.cuh"
+
+using namespace ngp;
+
+namespace {
+
+constexpr uint32_t kMlpParams = 10240;
+
+template <typename T>
+int dalloc(T*& p, size_t count, const char* what) {
+    p = nullptr;
+    if (count == 0) return NGP_OK;
+    void* raw           = nullptr;
+    const cudaError_t e = cudaMalloc(&raw, count * sizeof(T));
+    if (e != cudaSuccess) return fail(NGP_ERR_CUDA, std::string("cudaMalloc ") + what + ": " + cudaGetErrorString(e));
+    p = static_cast<T*>(raw);
+    return NGP_OK;
+}
+
+struct Split {
+    uint8_t* pixels = nullptr;
+    float* camera   = nullptr;
+    uint32_t frames = 0, width = 0, height = 0;
+    float fx = 0, fy = 0, cx = 0, cy = 0;
+};
+
+}  // namespace
+
+struct ngp_trainer {
+    ngp_trainer_config cfg{};
+    ngp_grid_layout layout{};
+    cudaStream_t stream = nullptr;
+    Split train, val, test;
+
+    // parameters and optimizer
+    uint32_t n_params = 0;
+    float* master      = nullptr;
+    uint16_t* params   = nullptr;
+    float* grads       = nullptr;
+    float *adam_m = nullptr, *adam_v = nullptr;
+    uint32_t* adam_steps = nullptr;
+
+    // density grid
+    float *grid_values = nullptr, *grid_scratch = nullptr, *grid_partial = nullptr, *grid_mean = nullptr;
+    uint32_t* grid_indices = nullptr;
+    uint8_t* bitfield      = nullptr;
+    uint32_t* occupied     = nullptr;
+
+    // sampler and network buffers
+    float* coords = nullptr;  // [MAX_SAMPLES][7]
+    float* rays   = nullptr;  // [BATCH][6]
+    uint32_t *ray_indices = nullptr, *numsteps = nullptr, *block_totals = nullptr;
+    uint32_t* counters     = nullptr;  // 0 rays, 1 samples, 2 compacted
+    uint16_t* enc          = nullptr;  // [32][MAX_SAMPLES] encoded positions
+    uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output
+    uint16_t* grid_density = nullptr;  // [2^21] raw density of the grid samples
+    float* ccoords         = nullptr;  // [BATCH][7] compacted
+    uint16_t* dloss        = nullptr;  // [BATCH][16]
+    float* loss_values     = nullptr;  // [BATCH]
+    unsigned char* loss_scratch = nullptr;
+    size_t loss_scratch_bytes   = 0;
+    uint16_t* cenc   = nullptr;  // [32][BATCH] encoded compacted batch
+    uint16_t* denc   = nullptr;  // [32][BATCH] dL/d(encoding)
+    float* mlp_scratch        = nullptr;
+    size_t mlp_scratch_floats = 0;
+    double* eval_sse          = nullptr;
+    uint8_t* comparison       = nullptr;
+
+    // host state (ngp.train.ixx:79-89)
+    uint32_t step              = 0;
+    uint32_t rays_per_batch    = 1u << 12;
+    uint32_t inference_samples = kMaxSamples;
+    uint32_t measured_before = 0, measured = 0;
+    uint32_t ema_step       = 0;
+    uint32_t occupied_cells = 0;
+    float grid_update_ms    = 0.0f;
+};
+
+namespace {
+
+void free_split(Split& s) {
+    cudaFree(s.pixels);
+    cudaFree(s.camera);
+    s = Split{};
+}
+
+void destroy(ngp_trainer* t) {
+    if (t == nullptr) return;
+    if (t->stream) cudaStreamSynchronize(t->stream);
+    free_split(t->train);
+    free_split(t->val);
+    free_split(t->test);
+    void* ptrs[] = {t->master, t->params, t->grads, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
+                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->coords, t->rays, t->ray_indices, t->numsteps, t->block_totals,
+                    t->counters, t->enc, t->out, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
+                    t->mlp_scratch, t->eval_sse, t->comparison};
+    for (void* p : ptrs) cudaFree(p);
+    if (t->stream) cudaStreamDestroy(t->stream);
+    delete t;
+}
+
+int upload_split(Split& s, const ngp_split* in, const char* what) {
+    s = Split{};
+    if (in == nullptr || in->frame_count == 0) return NGP_OK;
+    if (in->pixels == nullptr || in->camera == nullptr || in->width == 0 || in->height == 0 || !(in->focal_x > 0) || !(in->focal_y > 0))
+        return fail(NGP_ERR_INVALID, std::string("invalid dataset split: ") + what);
+    const size_t pix = static_cast<size_t>(in->frame_count) * in->width * in->height * 4u;
+    NGP_TRY(dalloc(s.pixels, pix, "dataset pixels"));
+    NGP_TRY(dalloc(s.camera, static_cast<size_t>(in->frame_count) * 12u, "dataset cameras"));
+    NGP_TRY(check_cuda(cudaMemcpy(s.pixels, in->pixels, pix, cudaMemcpyHostToDevice), "upload pixels"));
+    NGP_TRY(check_cuda(cudaMemcpy(s.camera, in->camera, sizeof(float) * in->frame_count * 12u, cudaMemcpyHostToDevice), "upload cameras"));
+    s.frames = in->frame_count, s.width = in->width, s.height = in->height;
+    s.fx = in->focal_x, s.fy = in->focal_y, s.cx = in->principal_x, s.cy = in->principal_y;
+    return NGP_OK;
+}
+
+// U(-1e-4, 1e-4) grid entries from PCG32(1337) advanced past the MLP weights, four values per
+// thread slot, as the reference's initialize_grid_params_kernel draws them (ngp.train.cu:1002-1017).
+__global__ void init_grid_kernel(float* master, __half* params, uint32_t n_grid, uint32_t mlp_count) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x, n_threads = blockDim.x * gridDim.x;
+    Pcg32 rng{kTrainSeed};
+    rng.advance(static_cast<uint64_t>(mlp_count) + static_cast<uint64_t>(i) * 4u);
+    for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t idx = i + n_threads * j;
+        if (idx >= n_grid) return;
+        const float v = __fmaf_rn(rng.next_float(), 2e-4f, -1e-4f);
+        master[idx]   = v;
+        params[idx]   = __float2half_rn(v);
+    }
+}
+
+__global__ void cast_half_kernel(const float* in, __half* out, uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __float2half_rn(in[i]);
+}
+
+// Xavier-uniform MLP weights drawn on the host from PCG32(1337), in the reference's order
+// (ngp.train.cu:1423-1461).
+int init_params(ngp_trainer* t) {
+    std::vector<float> h(kMlpParams);
+    Pcg32 rng{kTrainSeed};
+    const uint32_t shapes[5][2] = {{64, 32}, {16, 64}, {64, 32}, {64, 64}, {16, 64}};
+    uint32_t off                = 0;
+    for (auto& sh : shapes) {
+        const float scale = std::sqrt(6.0f / static_cast<float>(sh[0] + sh[1]));
+        for (uint32_t i = 0; i < sh[0] * sh[1]; ++i) h[off + i] = rng.next_float() * 2.0f * scale - scale;
+        off += sh[0] * sh[1];
+    }
+    NGP_TRY(check_cuda(cudaMemcpy(t->master, h.data(), sizeof(float) * kMlpParams, cudaMemcpyHostToDevice), "upload mlp params"));
+    cast_half_kernel<<<(kMlpParams + 255) / 256, 256, 0, t->stream>>>(t->master, reinterpret_cast<__half*>(t->params), kMlpParams);
+    NGP_TRY(check_launch("cast_half_kernel"));
+    const uint32_t n_grid    = t->layout.n_params;
+    const uint32_t n_threads = (n_grid + 3u) / 4u;
+    init_grid_kernel<<<(n_threads + 127u) / 128u, 128, 0, t->stream>>>(t->master + kMlpParams, reinterpret_cast<__half*>(t->params) + kMlpParams,
+                                                                     n_grid, kMlpParams);
+    return check_launch("init_grid_kernel");
+}
+
+int encode(ngp_trainer* t, uint32_t n, const float* c, uint16_t* dst, uint32_t stride) {
+    return ngp_encode_grid_forward(&t->layout, n, c, 7, t->params + kMlpParams, dst, stride, t->stream);
+}
+
+// update_density_grid (ngp.train.cu:1526-1595).
+int update_grid(ngp_trainer* t) {
+    uint32_t skip = t->step / 16u;
+    skip          = skip < 1u ? 1u : (skip > 16u ? 16u : skip);
+    if (t->step % skip != 0u) return NGP_OK;
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, t->stream);
+    const Split& s = t->train;
+    if (t->step == 0) {
+        t->ema_step = 0;
+        NGP_TRY(ngp_density_grid_mark_untrained(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, t->grid_values, t->stream));
+    }
+    const uint32_t n_uniform = t->step < 256u ? kGridCells : kGridCells / 4u;
+    const uint32_t n_nonuni  = t->step < 256u ? 0u : kGridCells / 4u;
+    const uint32_t n         = n_uniform + n_nonuni;
+    NGP_TRY(ngp_density_grid_samples(n_uniform, n_nonuni, t->ema_step, t->grid_values, t->coords, t->grid_indices, t->stream));
+    NGP_TRY(encode(t, n, t->coords, t->enc, n));
+    NGP_TRY(ngp_density_forward(n, t->params, t->enc, n, t->grid_density, t->stream));
+    NGP_TRY(ngp_density_grid_splat(n, t->grid_indices, t->grid_density, t->grid_scratch, t->stream));
+    NGP_TRY(ngp_density_grid_update(t->grid_values, t->grid_scratch, 0.95f, t->grid_partial, t->grid_mean, t->bitfield, t->occupied, t->stream));
+    ++t->ema_step;
+    cudaEventRecord(e1, t->stream);
+    cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    t->grid_update_ms += ms;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return NGP_OK;
+}
+
+int train_step(ngp_trainer* t) {
+    const Split& s = t->train;
+    NGP_TRY(update_grid(t));
+    // sample_training_batch (ngp.train.cu:1919-1930)
+    NGP_TRY(ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, t->step, t->rays_per_batch, nullptr,
+                                    t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->block_totals,
+                                    t->counters + 0, t->counters + 1, t->stream));
+    // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524)
+    NGP_TRY(encode(t, t->inference_samples, t->coords, t->enc, t->inference_samples));
+    NGP_TRY(ngp_mlp_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->coords, 7, t->out, nullptr, t->stream));
+    // compositing, loss, compaction, padding (ngp.train.cu:1932-1956)
+    NGP_TRY(ngp_training_loss_and_compact(t->rays_per_batch, t->step, t->counters + 0, s.pixels, s.frames, s.width, s.height, t->out,
+                                          t->counters + 2, t->ray_indices, t->rays, t->numsteps, t->coords, t->ccoords, t->dloss,
+                                          t->loss_values, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    NGP_TRY(ngp_pad_training_batch(t->counters + 2, t->ccoords, t->dloss, t->stream));
+    // encoding of the batch, fused MLP backward (recompute), encoding backward
+    NGP_TRY(encode(t, kNetworkBatch, t->ccoords, t->cenc, kNetworkBatch));
+    NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kNetworkBatch, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
+                             t->mlp_scratch_floats, t->grads, nullptr, 1.0f, t->stream));
+    NGP_TRY(ngp_encode_grid_backward(&t->layout, kNetworkBatch, t->ccoords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams, t->stream));
+    // step_optimizer (ngp.train.cu:1973-1980)
+    NGP_TRY(ngp_adam_step(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale, t->master, t->params, t->grads,
+                          t->adam_m, t->adam_v, t->adam_steps, 1, t->stream));
+    // adaptive batch (ngp.train.cpp:125-133)
+    uint32_t c[3];
+    NGP_TRY(check_cuda(cudaMemcpyAsync(c, t->counters, sizeof(c), cudaMemcpyDeviceToHost, t->stream), "read counters"));
+    NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train step"));
+    t->measured_before = c[1];
+    t->measured        = c[2];
+    if (t->measured == 0u) {
+        cudaMemcpy(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+        return fail(NGP_ERR_STATE, "Training stopped unexpectedly. density_grid_occupied_cells=" + std::to_string(t->occupied_cells));
+    }
+    const uint32_t g     = kBatchGranule;
+    t->inference_samples = ((std::min(t->measured_before, kMaxSamples) + g - 1u) / g) * g;
+    const uint64_t want  = std::min<uint64_t>((static_cast<uint64_t>(t->rays_per_batch) * kNetworkBatch) / t->measured, kNetworkBatch);
+    t->rays_per_batch    = std::min(std::max(static_cast<uint32_t>((want + g - 1u) / g * g), g), kNetworkBatch);
+    ++t->step;
+    return NGP_OK;
+}
+
+// One image (run_evaluation, ngp.train.cu:1597-1658): pixel rays in tiles of 2^18, each tile
+// marched, evaluated and composited with one host read of its sample count.
+int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparison_dev, float* rendered) {
+    const uint32_t total = s.width * s.height;
+    for (uint32_t off = 0; off < total; off += kNetworkBatch) {
+        const uint32_t n = std::min(kNetworkBatch, total - off);
+        NGP_TRY(ngp_make_eval_rays(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, off, n, t->rays, t->stream));
+        NGP_TRY(ngp_march_rays(n, t->rays, 0, 0, t->bitfield, kMaxSamples, t->coords, t->numsteps, t->block_totals, t->counters + 1, t->stream));
+        uint32_t used = 0;
+        NGP_TRY(check_cuda(cudaMemcpyAsync(&used, t->counters + 1, sizeof(used), cudaMemcpyDeviceToHost, t->stream), "eval counter"));
+        NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "eval march"));
+        if (used > kMaxSamples) return fail(NGP_ERR_OVERFLOW, "Evaluation sample budget overflowed (" + std::to_string(used) + " samples).");
+        if (used > 0) {
+            NGP_TRY(encode(t, used, t->coords, t->enc, used));
+            NGP_TRY(ngp_mlp_forward(used, t->params, t->enc, used, t->coords, 7, t->out, nullptr, t->stream));
+        }
+        NGP_TRY(ngp_eval_composite(n, off, image, s.width, s.height, s.pixels, t->numsteps, t->coords, t->out, t->eval_sse, comparison_dev,
+                                   rendered, t->stream));
+    }
+    return NGP_OK;
+}
+
+int run_eval(ngp_trainer* t, const Split& s, uint32_t begin, uint32_t count, uint8_t* comparison_host, double* out_sse) {
+    if (s.frames == 0) return fail(NGP_ERR_STATE, "no images in this split");
+    if (begin >= s.frames || count > s.frames - begin) return fail(NGP_ERR_INVALID, "evaluation image range is out of bounds");
+    if (comparison_host != nullptr) {
+        if (count != 1) return fail(NGP_ERR_INVALID, "test comparison output requires exactly one image");
+        cudaFree(t->comparison);
+        NGP_TRY(dalloc(t->comparison, static_cast<size_t>(s.width) * s.height * 6u, "comparison image"));
+    }
+    NGP_TRY(check_cuda(cudaMemsetAsync(t->eval_sse, 0, sizeof(double), t->stream), "eval clear"));
+    for (uint32_t k = 0; k < count; ++k) NGP_TRY(eval_image(t, s, begin + k, comparison_host != nullptr ? t->comparison : nullptr, nullptr));
+    NGP_TRY(check_cuda(cudaMemcpyAsync(out_sse, t->eval_sse, sizeof(double), cudaMemcpyDeviceToHost, t->stream), "eval sse"));
+    if (comparison_host != nullptr)
+        NGP_TRY(check_cuda(cudaMemcpyAsync(comparison_host, t->comparison, static_cast<size_t>(s.width) * s.height * 6u, cudaMemcpyDeviceToHost,
+                                           t->stream),
+                           "comparison image"));
+    return check_cuda(cudaStreamSynchronize(t->stream), "evaluation");
+}
+
+}  // namespace
+
+extern "C" void ngp_trainer_default_config(ngp_trainer_config* cfg) {
+    if (cfg == nullptr) return;
+    *cfg                      = ngp_trainer_config{};
+    cfg->n_levels             = 8;
+    cfg->features_per_level   = 4;
+    cfg->log2_hashmap_size    = 19;
+    cfg->base_resolution      = 16;
+    cfg->log2_per_level_scale = 1.0;
+    cfg->learning_rate        = 1e-2f;
+}
+
+extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split* train, const ngp_split* validation, const ngp_split* test,
+                                  ngp_trainer** out) {
+    clear_error();
+    if (out == nullptr || cfg == nullptr) return fail(NGP_ERR_INVALID, "trainer: null argument");
+    *out = nullptr;
+    if (train == nullptr || train->frame_count == 0) return fail(NGP_ERR_INVALID, "trainer: the training split is empty");
+    if (cfg->n_levels * cfg->features_per_level != 32) return fail(NGP_ERR_INVALID, "trainer: the encoding must produce 32 features (levels x F)");
+    auto* t      = new ngp_trainer{};
+    t->cfg       = *cfg;
+    const int st = [&]() -> int {
+        NGP_TRY(ngp_grid_layout_make(cfg->n_levels, cfg->features_per_level, cfg->log2_hashmap_size, cfg->base_resolution,
+                                     cfg->log2_per_level_scale, &t->layout));
+        NGP_TRY(check_cuda(cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking), "stream"));
+        NGP_TRY(upload_split(t->train, train, "train"));
+        NGP_TRY(upload_split(t->val, validation, "validation"));
+        NGP_TRY(upload_split(t->test, test, "test"));
+        t->n_params = kMlpParams + t->layout.n_params;
+        NGP_TRY(dalloc(t->master, t->n_params, "params"));
+        NGP_TRY(dalloc(t->params, t->n_params, "params fp16"));
+        NGP_TRY(dalloc(t->grads, t->n_params, "gradients"));
+        NGP_TRY(dalloc(t->adam_m, t->n_params, "adam m"));
+        NGP_TRY(dalloc(t->adam_v, t->n_params, "adam v"));
+        NGP_TRY(dalloc(t->adam_steps, t->n_params, "adam steps"));
+        NGP_TRY(dalloc(t->grid_values, kGridCells, "grid values"));
+        NGP_TRY(dalloc(t->grid_scratch, kGridCells, "grid scratch"));
+        NGP_TRY(dalloc(t->grid_partial, kGridCells / 1024u, "grid partial"));
+        NGP_TRY(dalloc(t->grid_mean, 1, "grid mean"));
+        NGP_TRY(dalloc(t->grid_indices, kGridCells, "grid indices"));
+        NGP_TRY(dalloc(t->bitfield, kGridCells / 8u, "bitfield"));
+        NGP_TRY(dalloc(t->occupied, 1, "occupied count"));
+        NGP_TRY(dalloc(t->coords, static_cast<size_t>(kMaxSamples) * 7u, "sample coords"));
+        NGP_TRY(dalloc(t->rays, static_cast<size_t>(kNetworkBatch) * 6u, "rays"));
+        NGP_TRY(dalloc(t->ray_indices, kNetworkBatch, "ray indices"));
+        NGP_TRY(dalloc(t->numsteps, static_cast<size_t>(kNetworkBatch) * 2u, "numsteps"));
+        NGP_TRY(dalloc(t->block_totals, kNetworkBatch / 128u + 1u, "block totals"));
+        NGP_TRY(dalloc(t->counters, 8, "counters"));
+        NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
+        NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));
+        NGP_TRY(dalloc(t->grid_density, kGridCells, "grid density"));
+        NGP_TRY(dalloc(t->ccoords, static_cast<size_t>(kNetworkBatch) * 7u, "compacted coords"));
+        NGP_TRY(dalloc(t->dloss, static_cast<size_t>(kNetworkBatch) * 16u, "output gradients"));
+        NGP_TRY(dalloc(t->loss_values, kNetworkBatch, "loss values"));
+        t->loss_scratch_bytes = ngp_loss_scratch_bytes(kNetworkBatch);
+        NGP_TRY(dalloc(t->loss_scratch, t->loss_scratch_bytes, "loss scratch"));
+        NGP_TRY(dalloc(t->cenc, static_cast<size_t>(kNetworkBatch) * 32u, "batch encoding"));
+        NGP_TRY(dalloc(t->denc, static_cast<size_t>(kNetworkBatch) * 32u, "encoding gradient"));
+        t->mlp_scratch_floats = ngp_mlp_backward_scratch_floats();
+        NGP_TRY(dalloc(t->mlp_scratch, t->mlp_scratch_floats, "mlp scratch"));
+        NGP_TRY(dalloc(t->eval_sse, 1, "eval sse"));
+        const cudaStream_t s = t->stream;
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->grads, 0, sizeof(float) * t->n_params, s), "clear grads"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->adam_m, 0, sizeof(float) * t->n_params, s), "clear m"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->adam_v, 0, sizeof(float) * t->n_params, s), "clear v"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->adam_steps, 0, sizeof(uint32_t) * t->n_params, s), "clear steps"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->grid_values, 0, sizeof(float) * kGridCells, s), "clear grid"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->grid_scratch, 0, sizeof(float) * kGridCells, s), "clear scratch"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->bitfield, 0xFF, kGridCells / 8u, s), "fill bitfield"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->counters, 0, 8 * sizeof(uint32_t), s), "clear counters"));
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->coords, 0, sizeof(float) * kMaxSamples * 7u, s), "clear coords"));
+        NGP_TRY(init_params(t));
+        return check_cuda(cudaStreamSynchronize(s), "trainer init");
+    }();
+    if (st != NGP_OK) {
+        destroy(t);
+        return st;
+    }
+    *out = t;
+    return NGP_OK;
+}
+
+extern "C" void ngp_trainer_destroy(ngp_trainer* t) { destroy(t); }
+
+extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats* stats) {
+    clear_error();
+    if (t == nullptr) return fail(NGP_ERR_INVALID, "trainer is null");
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, t->stream);
+    t->grid_update_ms  = 0.0f;
+    uint32_t loss_rays = t->rays_per_batch;
+    for (int32_t i = 0; i < iters; ++i) {
+        loss_rays    = t->rays_per_batch;
+        const int st = train_step(t);
+        if (st != NGP_OK) {
+            cudaEventDestroy(e0);
+            cudaEventDestroy(e1);
+            return st;
+        }
+    }
+    cudaEventRecord(e1, t->stream);
+    std::vector<float> losses(loss_rays);
+    NGP_TRY(check_cuda(cudaMemcpyAsync(losses.data(), t->loss_values, sizeof(float) * loss_rays, cudaMemcpyDeviceToHost, t->stream), "read loss"));
+    NGP_TRY(check_cuda(cudaMemcpyAsync(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read occupied"));
+    NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train"));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    float loss_sum = 0.0f;
+    for (float l : losses) loss_sum += l;
+    if (stats != nullptr) {
+        stats->step                                    = t->step;
+        stats->rays_per_batch                          = t->rays_per_batch;
+        stats->measured_sample_count_before_compaction = t->measured_before;
+        stats->measured_sample_count                   = t->measured;
+        stats->density_grid_occupied_cells             = t->occupied_cells;
+        stats->loss                                    = loss_sum * static_cast<float>(t->measured) / static_cast<float>(kNetworkBatch);
+        stats->elapsed_ms                              = ms;
+        stats->density_grid_update_ms                  = t->grid_update_ms;
+        stats->density_grid_occupancy_ratio            = static_cast<float>(t->occupied_cells) / static_cast<float>(kGridCells);
+    }
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_evaluate(ngp_trainer* t, int split, uint32_t image_begin, uint32_t image_count, uint8_t* comparison_host,
+                                    double* out_sse, uint64_t* out_pixels) {
+    clear_error();
+    if (t == nullptr || out_sse == nullptr) return fail(NGP_ERR_INVALID, "evaluate: null argument");
+    const Split& s = split == 1 ? t->val : t->test;
+    NGP_TRY(run_eval(t, s, image_begin, image_count, comparison_host, out_sse));
+    if (out_pixels != nullptr) *out_pixels = static_cast<uint64_t>(s.width) * s.height * image_count;
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint32_t width, uint32_t height, float fx, float fy, float cx,
+                                  float cy, float* rgb_device) {
+    clear_error();
+    if (t == nullptr || camera_host == nullptr || rgb_device == nullptr || width == 0 || height == 0 || !(fx > 0) || !(fy > 0))
+        return fail(NGP_ERR_INVALID, "render: bad input");
+    Split s{};
+    s.frames = 1, s.width = width, s.height = height, s.fx = fx, s.fy = fy, s.cx = cx, s.cy = cy;
+    NGP_TRY(dalloc(s.camera, 12, "render camera"));
+    int st = check_cuda(cudaMemcpyAsync(s.camera, camera_host, sizeof(float) * 12u, cudaMemcpyHostToDevice, t->stream), "render camera");
+    if (st == NGP_OK) st = eval_image(t, s, 0, nullptr, rgb_device);
+    if (st == NGP_OK) st = check_cuda(cudaStreamSynchronize(t->stream), "render");
+    free_split(s);
+    return st;
+}
+
+extern "C" uint32_t ngp_trainer_param_count(const ngp_trainer* t) { return t == nullptr ? 0u : t->n_params; }
+
+extern "C" int ngp_trainer_get_params(const ngp_trainer* t, float* host_out, uint32_t count) {
+    clear_error();
+    if (t == nullptr || host_out == nullptr || count != t->n_params) return fail(NGP_ERR_INVALID, "get params: bad arguments");
+    return check_cuda(cudaMemcpy(host_out, t->master, sizeof(float) * count, cudaMemcpyDeviceToHost), "download params");
+}
+
+extern "C" int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_t count) {
+    clear_error();
+    if (t == nullptr || host_in == nullptr || count != t->n_params) return fail(NGP_ERR_INVALID, "set params: bad arguments");
+    if (t->step != 0) return fail(NGP_ERR_STATE, "weights can only be loaded before training");
+    NGP_TRY(check_cuda(cudaMemcpy(t->master, host_in, sizeof(float) * count, cudaMemcpyHostToDevice), "upload params"));
+    NGP_TRY(check_cuda(cudaMemset(t->grads, 0, sizeof(float) * count), "clear grads"));
+    NGP_TRY(check_cuda(cudaMemset(t->adam_m, 0, sizeof(float) * count), "clear m"));
+    NGP_TRY(check_cuda(cudaMemset(t->adam_v, 0, sizeof(float) * count), "clear v"));
+    NGP_TRY(check_cuda(cudaMemset(t->adam_steps, 0, sizeof(uint32_t) * count), "clear steps"));
+    cast_half_kernel<<<(count + 255) / 256, 256, 0, t->stream>>>(t->master, reinterpret_cast<__half*>(t->params), count);
+    NGP_TRY(check_launch("cast_half_kernel"));
+    return check_cuda(cudaStreamSynchronize(t->stream), "set params");
+}
+
+extern "C" int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host, float* values_host) {
+    clear_error();
+    if (t == nullptr) return fail(NGP_ERR_INVALID, "get grid: null trainer");
+    if (bitfield_host != nullptr) NGP_TRY(check_cuda(cudaMemcpy(bitfield_host, t->bitfield, kGridCells / 8u, cudaMemcpyDeviceToHost), "bitfield"));
+    if (values_host != nullptr) NGP_TRY(check_cuda(cudaMemcpy(values_host, t->grid_values, sizeof(float) * kGridCells, cudaMemcpyDeviceToHost), "values"));
+    return NGP_OK;
+}
