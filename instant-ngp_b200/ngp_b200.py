@@ -187,3 +187,255 @@ def mlp_status(reset: bool = False) -> int:
     v = ctypes.c_uint32(0)
     _check(lib().ngp_mlp_status(ctypes.byref(v), ctypes.c_int(1 if reset else 0)), "ngp_mlp_status")
     return int(v.value)
+
+
+# ---------------------------------------------------------------------------------------------
+# Occupancy grid, marching, compositing / loss, Adam (ngp.train.cu:310-874, 1261-1280)
+# ---------------------------------------------------------------------------------------------
+GRID_CELLS = 128 ** 3
+NETWORK_BATCH = 1 << 18
+MAX_SAMPLES = NETWORK_BATCH * 16
+
+
+def _u32(v):
+    return ctypes.c_uint32(int(v))
+
+
+def _f32(v):
+    return ctypes.c_float(float(v))
+
+
+def density_grid_mark_untrained(camera, frame_count, width, height, fx, fy, cx, cy, values, stream=None) -> None:
+    _check(lib().ngp_density_grid_mark_untrained(_ptr(camera), _u32(frame_count), _u32(width), _u32(height), _f32(fx), _f32(fy), _f32(cx),
+                                                 _f32(cy), _ptr(values), _stream(stream)), "ngp_density_grid_mark_untrained")
+
+
+def density_grid_samples(n_uniform, n_nonuniform, ema_step, values, coords, indices, stream=None) -> None:
+    _check(lib().ngp_density_grid_samples(_u32(n_uniform), _u32(n_nonuniform), _u32(ema_step), _ptr(values), _ptr(coords), _ptr(indices),
+                                          _stream(stream)), "ngp_density_grid_samples")
+
+
+def density_grid_splat(n, indices, density, scratch, stream=None) -> None:
+    _check(lib().ngp_density_grid_splat(_u32(n), _ptr(indices), _ptr(density), _ptr(scratch), _stream(stream)), "ngp_density_grid_splat")
+
+
+def density_grid_update(values, scratch, partial, mean, bitfield, occupied, decay=0.95, stream=None) -> None:
+    _check(lib().ngp_density_grid_update(_ptr(values), _ptr(scratch), _f32(decay), _ptr(partial), _ptr(mean), _ptr(bitfield), _ptr(occupied),
+                                         _stream(stream)), "ngp_density_grid_update")
+
+
+def density_grid_partials() -> int:
+    lib().ngp_density_grid_partials.restype = ctypes.c_uint32
+    return int(lib().ngp_density_grid_partials())
+
+
+def march_block_totals(max_rays: int) -> int:
+    lib().ngp_march_block_totals.restype = ctypes.c_uint32
+    return int(lib().ngp_march_block_totals(_u32(max_rays)))
+
+
+def march_training_rays(camera, frame_count, width, height, fx, fy, cx, cy, step, rays_per_batch, sample_limit, bitfield, coords, rays,
+                        ray_indices, numsteps, block_totals, ray_counter, sample_counter, rays_per_batch_dev=None, stream=None) -> None:
+    _check(lib().ngp_march_training_rays(_ptr(camera), _u32(frame_count), _u32(width), _u32(height), _f32(fx), _f32(fy), _f32(cx), _f32(cy),
+                                         _u32(step), _u32(rays_per_batch), _ptr(rays_per_batch_dev), _u32(sample_limit), _ptr(bitfield),
+                                         _ptr(coords), _ptr(rays), _ptr(ray_indices), _ptr(numsteps), _ptr(block_totals), _ptr(ray_counter),
+                                         _ptr(sample_counter), _stream(stream)), "ngp_march_training_rays")
+
+
+def march_rays(rays, bitfield, coords, numsteps, block_totals, sample_counter, sample_limit=MAX_SAMPLES, jitter=False, step=0, n=None,
+               stream=None) -> None:
+    n = rays.shape[0] if n is None else n
+    _check(lib().ngp_march_rays(_u32(n), _ptr(rays), ctypes.c_int(1 if jitter else 0), _u32(step), _ptr(bitfield), _u32(sample_limit), _ptr(coords),
+                                _ptr(numsteps), _ptr(block_totals), _ptr(sample_counter), _stream(stream)), "ngp_march_rays")
+
+
+def make_eval_rays(camera, image, width, height, fx, fy, cx, cy, pixel_offset, n, rays, stream=None) -> None:
+    _check(lib().ngp_make_eval_rays(_ptr(camera), _u32(image), _u32(width), _u32(height), _f32(fx), _f32(fy), _f32(cx), _f32(cy),
+                                    _u32(pixel_offset), _u32(n), _ptr(rays), _stream(stream)), "ngp_make_eval_rays")
+
+
+def loss_scratch_bytes(max_rays: int) -> int:
+    lib().ngp_loss_scratch_bytes.restype = ctypes.c_uint32
+    return int(lib().ngp_loss_scratch_bytes(_u32(max_rays)))
+
+
+def training_loss_and_compact(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, compacted_counter,
+                              ray_indices, rays, numsteps, coords, compacted_coords, dloss_doutput, loss_values, scratch, stream=None) -> None:
+    _check(lib().ngp_training_loss_and_compact(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),
+                                               _u32(height), _ptr(network_output), _ptr(compacted_counter), _ptr(ray_indices), _ptr(rays),
+                                               _ptr(numsteps), _ptr(coords), _ptr(compacted_coords), _ptr(dloss_doutput), _ptr(loss_values),
+                                               _ptr(scratch), ctypes.c_size_t(scratch.numel() * scratch.element_size()), _stream(stream)),
+           "ngp_training_loss_and_compact")
+
+
+def pad_training_batch(compacted_counter, compacted_coords, dloss_doutput, stream=None) -> None:
+    _check(lib().ngp_pad_training_batch(_ptr(compacted_counter), _ptr(compacted_coords), _ptr(dloss_doutput), _stream(stream)),
+           "ngp_pad_training_batch")
+
+
+def eval_composite(n_pixels, pixel_offset, image, width, height, pixels, numsteps, coords, network_output, sse=None, comparison=None,
+                   rendered=None, stream=None) -> None:
+    _check(lib().ngp_eval_composite(_u32(n_pixels), _u32(pixel_offset), _u32(image), _u32(width), _u32(height), _ptr(pixels), _ptr(numsteps),
+                                    _ptr(coords), _ptr(network_output), _ptr(sse), _ptr(comparison), _ptr(rendered), _stream(stream)),
+           "ngp_eval_composite")
+
+
+def adam_step(n_mlp, master, params, grads, m, v, steps, lr=1e-2, beta1=0.9, beta2=0.99, eps=1e-15, l2_reg=1e-6, loss_scale=128.0,
+              clear_grid_gradients=True, stream=None) -> None:
+    _check(lib().ngp_adam_step(_u32(master.numel()), _u32(n_mlp), _f32(lr), _f32(beta1), _f32(beta2), _f32(eps), _f32(l2_reg), _f32(loss_scale),
+                               _ptr(master), _ptr(params), _ptr(grads), _ptr(m), _ptr(v), _ptr(steps), ctypes.c_int(1 if clear_grid_gradients else 0),
+                               _stream(stream)), "ngp_adam_step")
+
+
+# ---------------------------------------------------------------------------------------------
+# Trainer (the reference's ngp::train::InstantNGP, ngp.train.ixx:40-53)
+# ---------------------------------------------------------------------------------------------
+class TrainerConfig(ctypes.Structure):
+    _fields_ = [("n_levels", ctypes.c_uint32), ("features_per_level", ctypes.c_uint32), ("log2_hashmap_size", ctypes.c_uint32),
+                ("base_resolution", ctypes.c_uint32), ("log2_per_level_scale", ctypes.c_double), ("learning_rate", ctypes.c_float)]
+
+
+class Split(ctypes.Structure):
+    _fields_ = [("pixels", ctypes.c_void_p), ("camera", ctypes.c_void_p), ("frame_count", ctypes.c_uint32), ("width", ctypes.c_uint32),
+                ("height", ctypes.c_uint32), ("focal_x", ctypes.c_float), ("focal_y", ctypes.c_float), ("principal_x", ctypes.c_float),
+                ("principal_y", ctypes.c_float)]
+
+
+class TrainStats(ctypes.Structure):
+    _fields_ = [("step", ctypes.c_uint32), ("rays_per_batch", ctypes.c_uint32), ("measured_sample_count_before_compaction", ctypes.c_uint32),
+                ("measured_sample_count", ctypes.c_uint32), ("density_grid_occupied_cells", ctypes.c_uint32), ("loss", ctypes.c_float),
+                ("elapsed_ms", ctypes.c_float), ("density_grid_update_ms", ctypes.c_float), ("density_grid_occupancy_ratio", ctypes.c_float)]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+def trainer_config(n_levels=8, features_per_level=4, log2_hashmap_size=19, base_resolution=16, log2_per_level_scale=1.0,
+                   learning_rate=1e-2) -> TrainerConfig:
+    return TrainerConfig(n_levels, features_per_level, log2_hashmap_size, base_resolution, log2_per_level_scale, learning_rate)
+
+
+def config0_trainer_config() -> TrainerConfig:
+    return trainer_config(16, 2, 19, 16, math.log2(2048.0 / 16.0) / 15.0)
+
+
+class InstantNGP:
+    """Training / evaluation of one scene (ngp.train.ixx:40-53).  `dataset` is a dict with splits
+    "train", "validation", "test", each a dict(pixels=uint8 [F][H][W][4], camera=float32 [F][12],
+    focal=(fx, fy), principal=(cx, cy)) of host numpy arrays."""
+
+    def __init__(self, dataset: dict, config: TrainerConfig | None = None) -> None:
+        import numpy as np
+
+        self._keep = []
+        splits = []
+        for name in ("train", "validation", "test"):
+            d = dataset.get(name)
+            if d is None or len(d["pixels"]) == 0:
+                splits.append(None)
+                continue
+            px = np.ascontiguousarray(d["pixels"], np.uint8)
+            cam = np.ascontiguousarray(d["camera"], np.float32)
+            self._keep += [px, cam]
+            f, h, w = px.shape[0], px.shape[1], px.shape[2]
+            splits.append(Split(px.ctypes.data, cam.ctypes.data, f, w, h, d["focal"][0], d["focal"][1], d["principal"][0], d["principal"][1]))
+        self.config = config if config is not None else trainer_config()
+        self.handle = ctypes.c_void_p(0)
+        ptrs = [ctypes.byref(s) if s is not None else None for s in splits]
+        _check(lib().ngp_trainer_create(ctypes.byref(self.config), *ptrs, ctypes.byref(self.handle)), "ngp_trainer_create")
+        self._keep = []
+        self.test_size = None if splits[2] is None else (splits[2].width, splits[2].height)
+        self.split_frames = {i: (0 if s is None else int(s.frame_count)) for i, s in enumerate(splits)}
+
+    def close(self) -> None:
+        if self.handle:
+            lib().ngp_trainer_destroy(self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def train(self, iters: int) -> dict:
+        st = TrainStats()
+        _check(lib().ngp_trainer_train(self.handle, ctypes.c_int32(iters), ctypes.byref(st)), "ngp_trainer_train")
+        return st.as_dict()
+
+    def _evaluate(self, split: int, begin: int, count: int, comparison=None):
+        sse = ctypes.c_double(0.0)
+        pixels = ctypes.c_uint64(0)
+        cmp_ptr = None if comparison is None else ctypes.c_void_p(comparison.ctypes.data)
+        _check(lib().ngp_trainer_evaluate(self.handle, ctypes.c_int(split), _u32(begin), _u32(count), cmp_ptr, ctypes.byref(sse),
+                                          ctypes.byref(pixels)), "ngp_trainer_evaluate")
+        return sse.value, pixels.value
+
+    @staticmethod
+    def _psnr(sse: float, pixels: int) -> tuple[float, float]:
+        mse = sse / (pixels * 3.0)
+        return mse, (float("inf") if mse <= 0 else -10.0 * math.log10(mse))
+
+    def validate(self, count: int | None = None) -> dict:
+        """Mean PSNR over the validation images (ngp.train.cpp:157-181)."""
+        n = count if count is not None else self._count(1)
+        sse, px = self._evaluate(1, 0, n)
+        mse, psnr = self._psnr(sse, px)
+        return {"image_count": n, "pixel_count": px, "mse": mse, "psnr": psnr}
+
+    def test(self, count: int | None = None, with_images: bool = False) -> dict:
+        """Test PSNR (ngp.train.cpp:183-229); optionally the side-by-side comparison images."""
+        import numpy as np
+
+        n = count if count is not None else self._count(2)
+        sse_total, px_total, images = 0.0, 0, []
+        for i in range(n):
+            cmp = None
+            if with_images:
+                w, h = self.test_size
+                cmp = np.zeros((h, 2 * w, 3), np.uint8)
+            sse, px = self._evaluate(2, i, 1, cmp)
+            sse_total += sse
+            px_total += px
+            if with_images:
+                images.append(cmp)
+        mse, psnr = self._psnr(sse_total, px_total)
+        return {"image_count": n, "pixel_count": px_total, "mse": mse, "psnr": psnr, "images": images}
+
+    def _count(self, split: int) -> int:
+        return self.split_frames[split]
+
+    def render(self, camera, width: int, height: int, focal, principal, out=None):
+        import numpy as np
+        import torch
+
+        cam = np.ascontiguousarray(camera, np.float32)
+        out = torch.empty((height * width, 3), dtype=torch.float32, device="cuda") if out is None else out
+        _check(lib().ngp_trainer_render(self.handle, ctypes.c_void_p(cam.ctypes.data), _u32(width), _u32(height), _f32(focal[0]), _f32(focal[1]),
+                                        _f32(principal[0]), _f32(principal[1]), _ptr(out)), "ngp_trainer_render")
+        return out
+
+    def param_count(self) -> int:
+        lib().ngp_trainer_param_count.restype = ctypes.c_uint32
+        return int(lib().ngp_trainer_param_count(self.handle))
+
+    def get_params(self):
+        import numpy as np
+
+        out = np.zeros(self.param_count(), np.float32)
+        _check(lib().ngp_trainer_get_params(self.handle, ctypes.c_void_p(out.ctypes.data), _u32(out.size)), "ngp_trainer_get_params")
+        return out
+
+    def set_params(self, params) -> None:
+        import numpy as np
+
+        p = np.ascontiguousarray(params, np.float32)
+        _check(lib().ngp_trainer_set_params(self.handle, ctypes.c_void_p(p.ctypes.data), _u32(p.size)), "ngp_trainer_set_params")
+
+    def get_grid(self):
+        import numpy as np
+
+        bits = np.zeros(GRID_CELLS // 8, np.uint8)
+        vals = np.zeros(GRID_CELLS, np.float32)
+        _check(lib().ngp_trainer_get_grid(self.handle, ctypes.c_void_p(bits.ctypes.data), ctypes.c_void_p(vals.ctypes.data)), "ngp_trainer_get_grid")
+        return bits, vals

@@ -411,3 +411,188 @@ void oracle_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, 
 }
 
 }  // extern "C"
+
+// ======================================================================================
+// Occupancy grid and ray marching (ngp.train.cu:195-249, 383-474, 476-578, 580-667).
+// The a*b+c forms that the reference's compiler contracts are written as std::fmaf, as in the
+// CUDA library, so counts and positions can be compared bit for bit.
+// ======================================================================================
+namespace {
+
+constexpr float kDt = 1.73205080757f / 1024.0f;
+
+inline uint32_t spread3(uint32_t v) {
+    v = (v * 0x00010001u) & 0xFF0000FFu;
+    v = (v * 0x00000101u) & 0x0F00F00Fu;
+    v = (v * 0x00000011u) & 0xC30C30C3u;
+    v = (v * 0x00000005u) & 0x49249249u;
+    return v;
+}
+inline uint32_t compact3(uint32_t v) {
+    v &= 0x49249249u;
+    v = (v | (v >> 2u)) & 0xC30C30C3u;
+    v = (v | (v >> 4u)) & 0x0F00F00Fu;
+    v = (v | (v >> 8u)) & 0xFF0000FFu;
+    v = (v | (v >> 16u)) & 0x0000FFFFu;
+    return v;
+}
+
+struct V3 {
+    float x, y, z;
+};
+
+inline bool inside(V3 p) { return p.x >= 0.0f && p.x <= 1.0f && p.y >= 0.0f && p.y <= 1.0f && p.z >= 0.0f && p.z <= 1.0f; }
+
+inline bool hit_cube(V3 o, V3 d, float& tmin_out) {
+    const V3 inv = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
+    const V3 t0  = {-o.x * inv.x, -o.y * inv.y, -o.z * inv.z};
+    const V3 t1  = {(1.0f - o.x) * inv.x, (1.0f - o.y) * inv.y, (1.0f - o.z) * inv.z};
+    const float tmin = std::fmax(std::fmax(std::fmin(t0.x, t1.x), std::fmin(t0.y, t1.y)), std::fmin(t0.z, t1.z));
+    const float tmax = std::fmin(std::fmin(std::fmax(t0.x, t1.x), std::fmax(t0.y, t1.y)), std::fmax(t0.z, t1.z));
+    tmin_out         = std::fmax(tmin, 0.0f);
+    return tmax >= tmin_out;
+}
+
+inline bool occ(V3 p, const uint8_t* bits) {
+    const int x = static_cast<int>(p.x * 128.0f), y = static_cast<int>(p.y * 128.0f), z = static_cast<int>(p.z * 128.0f);
+    if (x < 0 || x >= 128 || y < 0 || y >= 128 || z < 0 || z >= 128) return false;
+    const uint32_t idx = spread3(x) | (spread3(y) << 1) | (spread3(z) << 2);
+    return (bits[idx / 8] >> (idx % 8)) & 1u;
+}
+
+inline float skip_voxel(float t, V3 pos, V3 d, V3 inv) {
+    const V3 p     = {(pos.x - 0.5f) * 128.0f, (pos.y - 0.5f) * 128.0f, (pos.z - 0.5f) * 128.0f};
+    const float tx = (std::floor(std::fmaf(0.5f, std::copysign(1.0f, d.x), p.x + 0.5f)) - p.x) * inv.x;
+    const float ty = (std::floor(std::fmaf(0.5f, std::copysign(1.0f, d.y), p.y + 0.5f)) - p.y) * inv.y;
+    const float tz = (std::floor(std::fmaf(0.5f, std::copysign(1.0f, d.z), p.z + 0.5f)) - p.z) * inv.z;
+    const float tt = t + std::fmax(std::fmin(std::fmin(tx, ty), tz) / 128.0f, 0.0f);
+    return std::fmaf(std::ceil(std::fmax((tt - t) / kDt, 0.5f)), kDt, t);
+}
+
+inline V3 at(V3 o, V3 d, float t) { return {std::fmaf(d.x, t, o.x), std::fmaf(d.y, t, o.y), std::fmaf(d.z, t, o.z)}; }
+
+// March one ray; write up to `limit` records into out (may be null to count only).
+uint32_t march(V3 o, V3 d, float start, const uint8_t* bits, float* out, uint32_t limit) {
+    const V3 inv  = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
+    const V3 warp = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
+    uint32_t n    = 0;
+    float t       = start;
+    while (n < limit) {
+        const V3 p = at(o, d, t);
+        if (!inside(p)) break;
+        if (occ(p, bits)) {
+            if (out != nullptr) {
+                float* c = out + static_cast<uint64_t>(n) * 7u;
+                c[0] = p.x, c[1] = p.y, c[2] = p.z, c[3] = kDt, c[4] = warp.x, c[5] = warp.y, c[6] = warp.z;
+            }
+            ++n;
+            t += kDt;
+        } else {
+            t = skip_voxel(t, p, d, inv);
+        }
+    }
+    return n;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Explicit rays [n][6] (origin, unit dir); start = tmin + U*dt with U the third draw of the
+// training PCG32 stream of ray i at `step` (jitter) or tmin + dt/2.  Samples in ray order.
+// Returns the total number of samples before the limit.
+uint32_t oracle_march_rays(uint32_t n, const float* rays, int jitter, uint32_t step, const uint8_t* bits, uint32_t sample_limit, uint32_t* numsteps,
+                           float* coords) {
+    uint32_t base = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const float* q = rays + static_cast<uint64_t>(i) * 6u;
+        const V3 o = {q[0], q[1], q[2]}, d = {q[3], q[4], q[5]};
+        float tmin      = 0.0f;
+        uint32_t steps  = 0;
+        float start     = 0.0f;
+        if (hit_cube(o, d, tmin)) {
+            if (jitter) {
+                Pcg rng(1337u);
+                rng.advance(static_cast<uint64_t>(step) << 32u);
+                rng.advance(static_cast<uint64_t>(i) * 16u);
+                rng.next_float();
+                rng.next_float();
+                start = std::fmaf(rng.next_float(), kDt, tmin);
+            } else {
+                start = tmin + 0.5f * kDt;
+            }
+            steps = march(o, d, start, bits, nullptr, 1024u);
+        }
+        const bool keep     = steps > 0 && base + steps <= sample_limit;
+        numsteps[2 * i]     = keep ? steps : 0u;
+        numsteps[2 * i + 1] = keep ? base : 0u;
+        if (keep) march(o, d, start, bits, coords + static_cast<uint64_t>(base) * 7u, steps);
+        base += steps;
+    }
+    return base;
+}
+
+// Density-grid samples (ngp.train.cu:383-424): uniform then non-uniform.
+void oracle_grid_samples(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords, uint32_t* indices) {
+    for (uint32_t g = 0; g < n_uniform + n_nonuniform; ++g) {
+        const bool uni   = g < n_uniform;
+        const uint32_t i = uni ? g : g - n_uniform, count = uni ? n_uniform : n_nonuniform;
+        const float thr  = uni ? -0.01f : 0.01f;
+        Pcg rng(1337u);
+        rng.advance(((static_cast<uint64_t>(ema_step) * 2ull + (uni ? 0ull : 1ull) + 1ull) << 32u) + static_cast<uint64_t>(i) * 4ull);
+        uint32_t idx = 0;
+        for (uint32_t j = 0; j < 10; ++j) {
+            idx = static_cast<uint32_t>(((static_cast<uint64_t>(i) + static_cast<uint64_t>(ema_step) * count) * 56924617ull + j * 19349663ull + 96925573ull) %
+                                        (128u * 128u * 128u));
+            if (values[idx] > thr) break;
+        }
+        float* c   = coords + static_cast<uint64_t>(g) * 7u;
+        c[0]       = (static_cast<float>(compact3(idx)) + rng.next_float()) / 128.0f;
+        c[1]       = (static_cast<float>(compact3(idx >> 1)) + rng.next_float()) / 128.0f;
+        c[2]       = (static_cast<float>(compact3(idx >> 2)) + rng.next_float()) / 128.0f;
+        c[3]       = kDt;
+        c[4] = c[5] = c[6] = 0.5f;
+        indices[g] = idx;
+    }
+}
+
+// EMA, mean (fp64) and bitfield (ngp.train.cu:434-474).  Returns the occupied count.
+uint32_t oracle_grid_update(float* values, const float* scratch, float decay, float* mean_out, uint8_t* bits) {
+    const uint32_t N = 128u * 128u * 128u;
+    double sum       = 0.0;
+    for (uint32_t i = 0; i < N; ++i) {
+        const float v = values[i];
+        values[i]     = v < 0.0f ? v : std::fmax(v * decay, scratch[i]);
+        sum += std::fmax(values[i], 0.0f);
+    }
+    const float mean = static_cast<float>(sum / N);
+    *mean_out        = mean;
+    const float thr  = std::fmin(0.01f, mean);
+    uint32_t count   = 0;
+    for (uint32_t b = 0; b < N / 8; ++b) {
+        uint32_t byte = 0;
+        for (uint32_t j = 0; j < 8; ++j) byte |= values[8 * b + j] > thr ? (1u << j) : 0u;
+        bits[b] = static_cast<uint8_t>(byte);
+        count += __builtin_popcount(byte);
+    }
+    return count;
+}
+
+// Adam on fp32 gradients (ngp.train.cu:1261-1280), fp64-free restatement in fp32 with libm.
+void oracle_adam(uint32_t n, uint32_t n_mlp, float lr, float b1, float b2, float eps, float l2, float loss_scale, float* master, uint16_t* params,
+                 const float* grads, float* m, float* v, uint32_t* steps) {
+    for (uint32_t i = 0; i < n; ++i) {
+        float g = grads[i] / loss_scale;
+        if (i >= n_mlp && g == 0.0f) continue;
+        const float w = master[i];
+        if (i < n_mlp) g = std::fmaf(l2, w, g);
+        m[i]             = std::fmaf(b1, m[i], (1.0f - b1) * g);
+        v[i]             = std::fmaf(b2, v[i], (1.0f - b2) * (g * g));
+        const uint32_t s = ++steps[i];
+        const float lrt  = lr * std::sqrt(1.0f - std::pow(b2, static_cast<float>(s))) / (1.0f - std::pow(b1, static_cast<float>(s)));
+        master[i]        = w - lrt * m[i] / (std::sqrt(v[i]) + eps);
+        params[i]        = f2h(master[i]);
+    }
+}
+
+}  // extern "C"

@@ -165,3 +165,47 @@ def _oracle_mlp_methods():
 
 
 _oracle_mlp_methods()
+
+
+def _oracle_sampler_methods():
+    def march_rays(self, rays, bitfield, jitter=False, step=0, sample_limit=1 << 22):
+        rays = np.ascontiguousarray(rays, np.float32)
+        bits = np.ascontiguousarray(bitfield, np.uint8)
+        n = rays.shape[0]
+        numsteps = np.zeros((n, 2), np.uint32)
+        coords = np.zeros((min(sample_limit, n * 1024), 7), np.float32)
+        self.lib.oracle_march_rays.restype = ctypes.c_uint32
+        total = self.lib.oracle_march_rays(ctypes.c_uint32(n), _p(rays), ctypes.c_int(int(jitter)), ctypes.c_uint32(step), _p(bits),
+                                           ctypes.c_uint32(sample_limit), _p(numsteps), _p(coords))
+        return numsteps, coords, int(total)
+
+    def grid_samples(self, n_uniform, n_nonuniform, ema_step, values):
+        values = np.ascontiguousarray(values, np.float32)
+        n = n_uniform + n_nonuniform
+        coords = np.zeros((n, 7), np.float32)
+        idx = np.zeros(n, np.uint32)
+        self.lib.oracle_grid_samples(ctypes.c_uint32(n_uniform), ctypes.c_uint32(n_nonuniform), ctypes.c_uint32(ema_step), _p(values), _p(coords),
+                                     _p(idx))
+        return coords, idx
+
+    def grid_update(self, values, scratch, decay=0.95):
+        values = np.array(values, np.float32)
+        scratch = np.ascontiguousarray(scratch, np.float32)
+        mean = np.zeros(1, np.float32)
+        bits = np.zeros(values.size // 8, np.uint8)
+        self.lib.oracle_grid_update.restype = ctypes.c_uint32
+        cnt = self.lib.oracle_grid_update(_p(values), _p(scratch), ctypes.c_float(decay), _p(mean), _p(bits))
+        return values, float(mean[0]), bits, int(cnt)
+
+    def adam(self, n_mlp, master, params, grads, m, v, steps, lr=1e-2, b1=0.9, b2=0.99, eps=1e-15, l2=1e-6, loss_scale=128.0):
+        arrs = [np.array(a) for a in (master, params.view(np.uint16), grads, m, v, steps)]
+        self.lib.oracle_adam(ctypes.c_uint32(arrs[0].size), ctypes.c_uint32(n_mlp), ctypes.c_float(lr), ctypes.c_float(b1), ctypes.c_float(b2),
+                             ctypes.c_float(eps), ctypes.c_float(l2), ctypes.c_float(loss_scale), *[_p(a) for a in arrs])
+        arrs[1] = arrs[1].view(np.float16)
+        return [arrs[i] for i in (0, 1, 3, 4, 5)]
+
+    for f in (march_rays, grid_samples, grid_update, adam):
+        setattr(Oracle, f.__name__, f)
+
+
+_oracle_sampler_methods()

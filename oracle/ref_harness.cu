@@ -78,6 +78,80 @@ int ref_mlp_forward(uint32_t n, const uint16_t* mlp_params, const uint16_t* x, u
     return status_of(cudaGetLastError());
 }
 
+// generate_training_samples_kernel (ngp.train.cu:476-578), counters cleared first.
+int ref_generate_training_samples(uint32_t rays_per_batch, uint32_t sample_limit, uint32_t step, uint32_t frame_count, uint32_t width,
+                                  uint32_t height, float fx, float fy, float cx, float cy, const float* camera, const uint8_t* occupancy,
+                                  uint32_t* ray_counter, uint32_t* sample_counter, uint32_t* ray_indices, float* rays, uint32_t* numsteps,
+                                  float* coords) {
+    cudaMemset(ray_counter, 0, 4);
+    cudaMemset(sample_counter, 0, 4);
+    ref::generate_training_samples_kernel<<<(rays_per_batch + 127u) / 128u, 128u>>>(rays_per_batch, sample_limit, step, frame_count, width, height, fx,
+                                                                                     fy, cx, cy, camera, occupancy, ray_counter, sample_counter,
+                                                                                     ray_indices, rays, numsteps, coords);
+    return status_of(cudaDeviceSynchronize());
+}
+
+// generate_evaluation_samples_kernel (ngp.train.cu:580-667) for one tile of pixels.
+int ref_generate_evaluation_samples(uint32_t tile_pixels, uint32_t pixel_offset, uint32_t max_samples, uint32_t width, uint32_t height, float fx,
+                                    float fy, float cx, float cy, const float* camera, uint32_t image, const uint8_t* occupancy,
+                                    uint32_t* sample_counter, uint32_t* overflow_counter, uint32_t* numsteps, float* coords) {
+    cudaMemset(sample_counter, 0, 4);
+    cudaMemset(overflow_counter, 0, 4);
+    ref::generate_evaluation_samples_kernel<<<(tile_pixels + 127u) / 128u, 128u>>>(tile_pixels, pixel_offset, max_samples, width, height, fx, fy, cx,
+                                                                                   cy, camera, image, occupancy, sample_counter, overflow_counter,
+                                                                                   numsteps, coords);
+    return status_of(cudaDeviceSynchronize());
+}
+
+// mark_untrained_density_grid_kernel (ngp.train.cu:310-381).
+int ref_mark_untrained(float* values, uint32_t frame_count, uint32_t width, uint32_t height, float fx, float fy, float cx, float cy,
+                       const float* camera) {
+    ref::mark_untrained_density_grid_kernel<<<ref::NERF_GRID_CELLS / 128u, 128u>>>(values, frame_count, width, height, fx, fy, cx, cy, camera);
+    return status_of(cudaDeviceSynchronize());
+}
+
+// generate_density_grid_samples_kernel (ngp.train.cu:383-424), uniform (phase 0) then nonuniform.
+int ref_grid_samples(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords, uint32_t* indices) {
+    if (n_uniform)
+        ref::generate_density_grid_samples_kernel<<<(n_uniform + 127u) / 128u, 128u>>>(n_uniform, ema_step, 0u, -0.01f, values, coords, indices);
+    if (n_nonuniform)
+        ref::generate_density_grid_samples_kernel<<<(n_nonuniform + 127u) / 128u, 128u>>>(n_nonuniform, ema_step, 1u, ref::NERF_MIN_OPTICAL_THICKNESS,
+                                                                                          values, coords + static_cast<uint64_t>(n_uniform) * 7u,
+                                                                                          indices + n_uniform);
+    return status_of(cudaDeviceSynchronize());
+}
+
+// K3-K6 (ngp.train.cu:426-474): splat, EMA, mean, bitfield, in the reference's launch order.
+int ref_grid_update(uint32_t n, const uint32_t* indices, const uint16_t* density, float* scratch, float* values, float* mean, uint8_t* occupancy,
+                    uint32_t* occupied) {
+    ref::splat_density_grid_samples_kernel<<<(n + 127u) / 128u, 128u>>>(n, indices, reinterpret_cast<const __half*>(density), scratch);
+    ref::update_density_grid_ema_kernel<<<ref::NERF_GRID_CELLS / 128u, 128u>>>(scratch, values);
+    cudaMemset(mean, 0, 4);
+    cudaMemset(occupied, 0, 4);
+    ref::reduce_density_grid_mean_kernel<<<(ref::NERF_GRID_CELLS / 4u + 1023u) / 1024u, 1024u>>>(values, mean);
+    ref::build_density_grid_bitfield_kernel<<<(ref::NERF_GRID_CELLS / 8u + 127u) / 128u, 128u>>>(values, mean, occupancy, occupied);
+    return status_of(cudaDeviceSynchronize());
+}
+
+// compute_training_loss_and_compact_kernel (ngp.train.cu:747-860), counters and loss cleared.
+int ref_training_loss(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels, uint32_t frame_count,
+                      uint32_t width, uint32_t height, const uint16_t* network_output, uint32_t* compacted_counter, const uint32_t* ray_indices,
+                      const float* rays, uint32_t* numsteps, const float* coords, float* coords_out, uint16_t* dloss, float* loss) {
+    cudaMemset(compacted_counter, 0, 4);
+    cudaMemset(loss, 0, sizeof(float) * rays_per_batch);
+    ref::compute_training_loss_and_compact_kernel<<<(rays_per_batch + 127u) / 128u, 128u>>>(
+        rays_per_batch, step, ray_counter, pixels, frame_count, width, height, reinterpret_cast<const __half*>(network_output), compacted_counter,
+        ray_indices, rays, numsteps, coords, coords_out, reinterpret_cast<__half*>(dloss), loss);
+    return status_of(cudaDeviceSynchronize());
+}
+
+// adam_step_kernel (ngp.train.cu:1261-1280) over the reference's full parameter vector.
+int ref_adam(float* master, uint16_t* params, const uint16_t* grads, float* m, float* v, uint32_t* steps) {
+    const uint32_t n = cfg::NETWORK_PARAMETER_LAYOUT.total_param_count;
+    ref::adam_step_kernel<<<(n + 127u) / 128u, 128u>>>(master, reinterpret_cast<__half*>(params), reinterpret_cast<const __half*>(grads), m, v, steps);
+    return status_of(cudaDeviceSynchronize());
+}
+
 // PCG32 as the reference's device code runs it (ngp.train.cu:89-143), for pinning.
 int ref_pcg32(uint64_t initstate, uint64_t initseq, uint64_t advance, uint32_t count, uint32_t* out_uint, float* out_float) {
     ref::Pcg32 a{initstate, initseq};

@@ -1,0 +1,372 @@
+"""Occupancy grid, ray marching, compositing/loss and Adam: CUDA library vs the CPU oracle and the
+reference's own kernels (oracle/_ref).
+
+Bars (north_star: occupancy bitfield, per-ray sample counts and positions bit-exact):
+* marching, library vs oracle and vs the reference kernels: per-ray counts and sample records
+  bit-exact (the reference places rays in atomic order; rays are matched by their index);
+* grid samples and EMA: bit-exact; bitfield: bit-exact except cells within 1e-6 relative of the
+  threshold (the reference's mean is an order-dependent float atomic sum);
+* loss / gradients (fp32 with libm transcendental functions): per-ray loss within 1e-5 relative,
+  compacted counts exact, fp16 gradients within 2 ulp;
+* Adam: within 1e-6 relative of the oracle.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import pytest
+
+import workloads
+
+pytestmark = pytest.mark.gpu
+
+V = ctypes.c_void_p
+
+
+def T(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def P(t):
+    return V(t.data_ptr())
+
+
+@pytest.fixture(scope="module")
+def blob_bitfield():
+    vals = workloads.blob_grid_values(workloads.gaussian_blob_density())
+    bits = np.packbits((vals > 0.01).reshape(-1, 8), axis=1, bitorder="little").reshape(-1)
+    return bits
+
+
+@pytest.fixture(scope="module")
+def small_scene():
+    return workloads.procedural_dataset(n_train=6, n_test=2, width=96, height=80, seed=5)
+
+
+def run_march(ngp, rays, bits, jitter, step=0, limit=1 << 22):
+    import torch
+
+    n = rays.shape[0]
+    coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    numsteps = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    totals = torch.zeros(ngp.march_block_totals(n), dtype=torch.int32, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_rays(T(rays), T(bits), coords, numsteps, totals, counter, sample_limit=limit, jitter=jitter, step=step)
+    torch.cuda.synchronize()
+    return numsteps.cpu().numpy().view(np.uint32), coords.cpu().numpy(), int(counter.item())
+
+
+@pytest.mark.parametrize("n", [1, 127, 4096])
+@pytest.mark.parametrize("jitter", [False, True])
+def test_march_bit_exact_vs_oracle(ngp, oracle, blob_bitfield, n, jitter):
+    rays = workloads.march_rays_config2(n, seed=n)
+    ns, coords, total = run_march(ngp, rays, blob_bitfield, jitter, step=7)
+    ons, ocoords, ototal = oracle.march_rays(rays, blob_bitfield, jitter=jitter, step=7)
+    assert total == ototal
+    assert (ns == ons).all()
+    used = int(ns[:, 0].sum())
+    assert coords[:used].tobytes() == ocoords[:used].tobytes()
+
+
+def test_march_full_config2(ngp, oracle, blob_bitfield):
+    """Config 2 at full size: 2^18 rays, bit-exact against the oracle."""
+    rays = workloads.march_rays_config2(1 << 18, seed=2)
+    ns, coords, total = run_march(ngp, rays, blob_bitfield, False)
+    ons, ocoords, ototal = oracle.march_rays(rays, blob_bitfield)
+    assert total == ototal and (ns == ons).all()
+    used = int(ns[:, 0].sum())
+    assert used > 100000
+    assert coords[:used].tobytes() == ocoords[:used].tobytes()
+
+
+def test_march_sample_limit_drops_whole_rays(ngp, oracle, blob_bitfield):
+    rays = workloads.march_rays_config2(2048, seed=9)
+    ns, _, total = run_march(ngp, rays, blob_bitfield, False, limit=20000)
+    ons, _, _ = oracle.march_rays(rays, blob_bitfield, sample_limit=20000)
+    assert (ns == ons).all() and total > 20000
+    assert ns[:, 0].sum() <= 20000
+
+
+def test_march_empty_grid(ngp, blob_bitfield):
+    rays = workloads.march_rays_config2(300, seed=1)
+    ns, _, total = run_march(ngp, rays, np.zeros_like(blob_bitfield), True)
+    assert total == 0 and (ns == 0).all()
+
+
+def _scene_tensors(scene):
+    tr = scene["train"]
+    return T(tr["pixels"]), T(tr["camera"]), tr
+
+
+def test_training_rays_vs_reference_kernel(ngp, reflib, small_scene, blob_bitfield):
+    """generate_training_samples_kernel vs ours: per ray, the same sample count and records."""
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    bits = T(blob_bitfield)
+    n, limit, step = 8192, 1 << 22, 3
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    # reference
+    rc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    r_idx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    r_rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    r_ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    r_coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    reflib.call("ref_generate_training_samples", ctypes.c_uint32(n), ctypes.c_uint32(limit), ctypes.c_uint32(step), ctypes.c_uint32(F),
+                ctypes.c_uint32(W), ctypes.c_uint32(H), ctypes.c_float(fx), ctypes.c_float(fy), ctypes.c_float(cx), ctypes.c_float(cy), P(cam),
+                P(bits), P(rc), P(sc), P(r_idx), P(r_rays), P(r_ns), P(r_coords))
+    # ours
+    o_ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    o_rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    o_idx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    o_coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    totals = torch.zeros(ngp.march_block_totals(n), dtype=torch.int32, device="cuda")
+    orc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    osc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, o_coords, o_rays, o_idx, o_ns, totals, orc, osc)
+    torch.cuda.synchronize()
+    assert int(sc.item()) == int(osc.item())
+    k = int(rc.item())
+    ridx = r_idx[:k].cpu().numpy()
+    rns = r_ns[:k].cpu().numpy()
+    rco = r_coords.cpu().numpy()
+    ons = o_ns.cpu().numpy()
+    oco = o_coords.cpu().numpy()
+    orays = o_rays.cpu().numpy()
+    rrays = r_rays[:k].cpu().numpy()
+    assert k == int((ons[:, 0] > 0).sum())
+    assert (ons[ridx, 0] == rns[:, 0]).all()
+    assert orays[ridx].tobytes() == rrays.tobytes()
+    for j in range(k):
+        a = rco[rns[j, 1]: rns[j, 1] + rns[j, 0]]
+        b = oco[ons[ridx[j], 1]: ons[ridx[j], 1] + rns[j, 0]]
+        assert a.tobytes() == b.tobytes(), j
+
+
+def test_eval_rays_vs_reference_kernel(ngp, reflib, small_scene, blob_bitfield):
+    """generate_evaluation_samples_kernel vs ours on one 4096-pixel tile: per pixel, the same samples."""
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    bits = T(blob_bitfield)
+    n, off, image = 4096, 1000, 1
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ov = torch.zeros(1, dtype=torch.int32, device="cuda")
+    r_ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    r_coords = torch.zeros((n * 1024, 7), dtype=torch.float32, device="cuda")
+    reflib.call("ref_generate_evaluation_samples", ctypes.c_uint32(n), ctypes.c_uint32(off), ctypes.c_uint32(n * 1024), ctypes.c_uint32(W),
+                ctypes.c_uint32(H), ctypes.c_float(fx), ctypes.c_float(fy), ctypes.c_float(cx), ctypes.c_float(cy), P(cam), ctypes.c_uint32(image),
+                P(bits), P(sc), P(ov), P(r_ns), P(r_coords))
+    rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    ngp.make_eval_rays(cam, image, W, H, fx, fy, cx, cy, off, n, rays)
+    torch.cuda.synchronize()
+    ns, coords, total = run_march(ngp, rays.cpu().numpy(), blob_bitfield, False)
+    rns = r_ns.cpu().numpy()
+    rco = r_coords.cpu().numpy()
+    assert total == int(sc.item()) and int(ov.item()) == 0
+    assert (ns[:, 0] == rns[:, 0]).all()
+    for i in np.nonzero(rns[:, 0])[0]:
+        assert rco[rns[i, 1]: rns[i, 1] + rns[i, 0]].tobytes() == coords[ns[i, 1]: ns[i, 1] + ns[i, 0]].tobytes(), i
+
+
+def test_grid_samples_and_update_vs_reference(ngp, oracle, reflib):
+    import torch
+
+    vals0 = workloads.blob_grid_values(workloads.gaussian_blob_density())
+    vals0[::97] = -1.0  # some untrained cells
+    nu, nn = 1 << 16, 1 << 16
+    values = T(vals0)
+    coords = torch.zeros((nu + nn, 7), dtype=torch.float32, device="cuda")
+    idx = torch.zeros(nu + nn, dtype=torch.int32, device="cuda")
+    ngp.density_grid_samples(nu, nn, 5, values, coords, idx)
+    rcoords = torch.zeros_like(coords)
+    ridx = torch.zeros_like(idx)
+    reflib.call("ref_grid_samples", ctypes.c_uint32(nu), ctypes.c_uint32(nn), ctypes.c_uint32(5), P(values), P(rcoords), P(ridx))
+    torch.cuda.synchronize()
+    oc, oi = oracle.grid_samples(nu, nn, 5, vals0)
+    assert coords.cpu().numpy().tobytes() == rcoords.cpu().numpy().tobytes() == oc.tobytes()
+    assert (idx.cpu().numpy().view(np.uint32) == oi).all() and (ridx.cpu().numpy().view(np.uint32) == oi).all()
+
+    # splat + EMA + mean + bitfield on the same densities
+    rng = np.random.default_rng(4)
+    dens = rng.normal(-1.0, 2.0, nu + nn).astype(np.float16)
+    D = T(dens)
+    scratch = torch.zeros(128 ** 3, dtype=torch.float32, device="cuda")
+    ngp.density_grid_splat(nu + nn, idx, D, scratch)
+    torch.cuda.synchronize()
+    splatted = scratch.cpu().numpy()
+    v_ours = values.clone()
+    partial = torch.zeros(ngp.density_grid_partials(), dtype=torch.float32, device="cuda")
+    mean = torch.zeros(1, dtype=torch.float32, device="cuda")
+    bits = torch.zeros(128 ** 3 // 8, dtype=torch.uint8, device="cuda")
+    occ = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.density_grid_update(v_ours, scratch, partial, mean, bits, occ)
+    v_ref = values.clone()
+    rs = torch.zeros_like(scratch)
+    rmean = torch.zeros(1, dtype=torch.float32, device="cuda")
+    rbits = torch.zeros_like(bits)
+    rocc = torch.zeros_like(occ)
+    reflib.call("ref_grid_update", ctypes.c_uint32(nu + nn), P(idx), P(D), P(rs), P(v_ref), P(rmean), P(rbits), P(rocc))
+    torch.cuda.synchronize()
+    assert (scratch == 0).all()  # cleared for the next update
+    assert v_ours.cpu().numpy().tobytes() == v_ref.cpu().numpy().tobytes()
+    ov, omean, obits, ocnt = oracle.grid_update(vals0, splatted)
+    assert v_ours.cpu().numpy().tobytes() == ov.tobytes()
+    m = float(mean.item())
+    assert abs(m - omean) <= 1e-5 * omean and abs(m - float(rmean.item())) <= 1e-5 * omean
+    thr = min(0.01, m)
+    near = np.abs(ov - thr) <= 1e-6 * thr
+    ours_bits = np.unpackbits(bits.cpu().numpy(), bitorder="little").astype(bool)
+    ref_bits = np.unpackbits(rbits.cpu().numpy(), bitorder="little").astype(bool)
+    ora_bits = np.unpackbits(obits, bitorder="little").astype(bool)
+    assert (ours_bits[~near] == ref_bits[~near]).all() and (ours_bits[~near] == ora_bits[~near]).all()
+    assert int(occ.item()) == int(ours_bits.sum())
+
+
+def test_mark_untrained_vs_reference(ngp, reflib, small_scene):
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    ours = torch.zeros(128 ** 3, dtype=torch.float32, device="cuda")
+    ref = torch.zeros_like(ours)
+    ngp.density_grid_mark_untrained(cam, F, W, H, fx, fy, cx, cy, ours)
+    reflib.call("ref_mark_untrained", P(ref), ctypes.c_uint32(F), ctypes.c_uint32(W), ctypes.c_uint32(H), ctypes.c_float(fx), ctypes.c_float(fy),
+                ctypes.c_float(cx), ctypes.c_float(cy), P(cam))
+    torch.cuda.synchronize()
+    a, b = ours.cpu().numpy(), ref.cpu().numpy()
+    assert 0.0 < (a == 0).mean() < 1.0
+    assert (a != b).mean() < 1e-4  # cells decided by a last-ulp comparison may differ
+
+
+def test_adam_vs_oracle(ngp, oracle):
+    import torch
+
+    rng = np.random.default_rng(0)
+    n, n_mlp = 40000, 10240
+    master = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    grads = rng.normal(0, 10, n).astype(np.float32)
+    grads[n_mlp::3] = 0.0  # sparse grid entries are skipped
+    m = rng.normal(0, 0.01, n).astype(np.float32)
+    v = rng.uniform(0, 0.01, n).astype(np.float32)
+    steps = rng.integers(0, 5, n).astype(np.uint32)
+    params = master.astype(np.float16)
+    tm, tp, tg, tmm, tv, ts = (T(a) for a in (master, params.view(np.int16), grads, m, v, steps.view(np.int32)))
+    ngp.adam_step(n_mlp, tm, tp, tg, tmm, tv, ts)
+    torch.cuda.synchronize()
+    om, op, omm, ov, os_ = oracle.adam(n_mlp, master, params, grads, m, v, steps)
+    np.testing.assert_allclose(tm.cpu().numpy(), om, rtol=1e-6, atol=1e-9)
+    np.testing.assert_allclose(tmm.cpu().numpy(), omm, rtol=1e-6, atol=1e-12)
+    np.testing.assert_allclose(tv.cpu().numpy(), ov, rtol=1e-6, atol=1e-12)
+    assert (ts.cpu().numpy().view(np.uint32) == os_).all()
+    g = tg.cpu().numpy()
+    assert (g[n_mlp:] == 0).all() and (g[:n_mlp] == grads[:n_mlp]).all()  # grid gradient cleared, MLP kept
+
+
+def test_adam_vs_reference_kernel(ngp, reflib):
+    """The reference's adam_step_kernel on fp16 gradients vs ours on the same values in fp32."""
+    import torch
+
+    total = int(reflib.lib.ref_total_param_count())
+    n_mlp = int(reflib.lib.ref_mlp_param_count())
+    rng = np.random.default_rng(1)
+    master = rng.uniform(-0.1, 0.1, total).astype(np.float32)
+    g16 = rng.normal(0, 5, total).astype(np.float16)
+    g16[n_mlp::2] = 0
+    params = master.astype(np.float16)
+    zeros = np.zeros(total, np.float32)
+    r = [T(a) for a in (master, params.view(np.int16), g16.view(np.int16), zeros, zeros, np.zeros(total, np.int32))]
+    o = [T(a) for a in (master, params.view(np.int16), g16.astype(np.float32), zeros, zeros, np.zeros(total, np.int32))]
+    for _ in range(3):
+        reflib.call("ref_adam", P(r[0]), P(r[1]), P(r[2]), P(r[3]), P(r[4]), P(r[5]))
+        ngp.adam_step(n_mlp, o[0], o[1], o[2], o[3], o[4], o[5], clear_grid_gradients=False)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(o[0].cpu().numpy(), r[0].cpu().numpy(), rtol=2e-6, atol=1e-8)
+    assert (o[5].cpu().numpy() == r[5].cpu().numpy()).all()
+
+
+def _synthetic_output(coords: np.ndarray) -> np.ndarray:
+    """A smooth deterministic 'network output' per sample record (raw rgb, raw density)."""
+    out = np.zeros((coords.shape[0], 16), np.float16)
+    x, y, z = coords[:, 0], coords[:, 1], coords[:, 2]
+    out[:, 0] = np.sin(7 * x) * 2
+    out[:, 1] = np.cos(5 * y) * 2
+    out[:, 2] = (z - 0.5) * 4
+    out[:, 3] = np.sin(3 * x + 2 * y) * 4 + 1.5
+    return out
+
+
+def test_training_loss_vs_reference_kernel(ngp, reflib, small_scene, blob_bitfield):
+    """compute_training_loss_and_compact_kernel vs ours on the same rays and network outputs:
+    per-ray loss, compacted count and per-sample gradients (rays matched by index)."""
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    bits = T(blob_bitfield)
+    n, limit, step = 4096, 1 << 20, 11
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    # ours: march, outputs, loss
+    ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    ridx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    totals = torch.zeros(ngp.march_block_totals(n), dtype=torch.int32, device="cuda")
+    rc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, coords, rays, ridx, ns, totals, rc, sc)
+    torch.cuda.synchronize()
+    total = int(sc.item())
+    out = T(np.concatenate([_synthetic_output(coords[:total].cpu().numpy()), np.zeros((limit - total, 16), np.float16)]))
+    ccoords = torch.zeros((1 << 18, 7), dtype=torch.float32, device="cuda")
+    dloss = torch.zeros((1 << 18, 16), dtype=torch.float16, device="cuda")
+    loss = torch.zeros(n, dtype=torch.float32, device="cuda")
+    cc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(ngp.loss_scratch_bytes(n), dtype=torch.uint8, device="cuda")
+    ngp.training_loss_and_compact(n, step, rc, pix, F, W, H, out, cc, ridx, rays, ns, coords, ccoords, dloss, loss, scratch)
+    # reference: its own march, same output function, its loss kernel
+    r_rc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    r_sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    r_idx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    r_rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    r_ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    r_coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    reflib.call("ref_generate_training_samples", ctypes.c_uint32(n), ctypes.c_uint32(limit), ctypes.c_uint32(step), ctypes.c_uint32(F),
+                ctypes.c_uint32(W), ctypes.c_uint32(H), ctypes.c_float(fx), ctypes.c_float(fy), ctypes.c_float(cx), ctypes.c_float(cy), P(cam),
+                P(bits), P(r_rc), P(r_sc), P(r_idx), P(r_rays), P(r_ns), P(r_coords))
+    r_out = T(np.concatenate([_synthetic_output(r_coords[:total].cpu().numpy()), np.zeros((limit - total, 16), np.float16)]))
+    r_cc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    r_ccoords = torch.zeros_like(ccoords)
+    r_dloss = torch.zeros_like(dloss)
+    r_loss = torch.zeros(n, dtype=torch.float32, device="cuda")
+    reflib.call("ref_training_loss", ctypes.c_uint32(n), ctypes.c_uint32(step), P(r_rc), P(pix), ctypes.c_uint32(F), ctypes.c_uint32(W),
+                ctypes.c_uint32(H), P(r_out), P(r_cc), P(r_idx), P(r_rays), P(r_ns), P(r_coords), P(r_ccoords), P(r_dloss), P(r_loss))
+    torch.cuda.synchronize()
+    assert int(cc.item()) == int(r_cc.item())
+    k = int(r_rc.item())
+    ri = r_idx[:k].cpu().numpy()
+    rns = r_ns[:k].cpu().numpy()
+    ons = ns.cpu().numpy()
+    assert (ons[ri, 0] == rns[:, 0]).all()  # compacted counts per ray
+    ol = loss.cpu().numpy()
+    rl = r_loss[:k].cpu().numpy()
+    np.testing.assert_allclose(ol[ri], rl, rtol=1e-5, atol=1e-9)
+    od = dloss.float().cpu().numpy()
+    rd = r_dloss.float().cpu().numpy()
+    oc = ccoords.cpu().numpy()
+    rcc = r_ccoords.cpu().numpy()
+    for j in range(k):
+        c = rns[j, 0]
+        a, b = rns[j, 1], ons[ri[j], 1]
+        assert rcc[a: a + c].tobytes() == oc[b: b + c].tobytes()
+        x, y = od[b: b + c, :4], rd[a: a + c, :4]
+        assert (np.abs(x - y) <= 2e-3 * np.abs(y) + 1e-7).all(), j
