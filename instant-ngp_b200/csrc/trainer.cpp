@@ -255,21 +255,29 @@ int train_step(ngp_trainer* t) {
 // One image (run_evaluation, ngp.train.cu:1597-1658): pixel rays in tiles of 2^18, each tile
 // marched, evaluated and composited with one host read of its sample count.
 int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparison_dev, float* rendered) {
+    // A tile of `tile` pixels is marched; if its samples exceed the budget (MAX_SAMPLES) it is
+    // re-marched in smaller tiles.  4096 pixels x 1024 steps always fit, as in the reference.
     const uint32_t total = s.width * s.height;
-    for (uint32_t off = 0; off < total; off += kNetworkBatch) {
-        const uint32_t n = std::min(kNetworkBatch, total - off);
+    uint32_t tile        = kNetworkBatch;
+    for (uint32_t off = 0; off < total;) {
+        const uint32_t n = std::min(tile, total - off);
         NGP_TRY(ngp_make_eval_rays(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, off, n, t->rays, t->stream));
         NGP_TRY(ngp_march_rays(n, t->rays, 0, 0, t->bitfield, kMaxSamples, t->coords, t->numsteps, t->block_totals, t->counters + 1, t->stream));
         uint32_t used = 0;
         NGP_TRY(check_cuda(cudaMemcpyAsync(&used, t->counters + 1, sizeof(used), cudaMemcpyDeviceToHost, t->stream), "eval counter"));
         NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "eval march"));
-        if (used > kMaxSamples) return fail(NGP_ERR_OVERFLOW, "Evaluation sample budget overflowed (" + std::to_string(used) + " samples).");
+        if (used > kMaxSamples) {
+            if (tile <= 4096u) return fail(NGP_ERR_OVERFLOW, "Evaluation sample budget overflowed (" + std::to_string(used) + " samples).");
+            tile = std::max(4096u, tile / 4u);
+            continue;
+        }
         if (used > 0) {
             NGP_TRY(encode(t, used, t->coords, t->enc, used));
             NGP_TRY(ngp_mlp_forward(used, t->params, t->enc, used, t->coords, 7, t->out, nullptr, t->stream));
         }
         NGP_TRY(ngp_eval_composite(n, off, image, s.width, s.height, s.pixels, t->numsteps, t->coords, t->out, t->eval_sse, comparison_dev,
                                    rendered, t->stream));
+        off += n;
     }
     return NGP_OK;
 }

@@ -209,6 +209,6 @@ def test_backward_full_size_vs_torch_fp32(ngp):
     got = dw.cpu().numpy()
     for lo, hi in ((0, 2048), (2048, 3072), (3072, 5120), (5120, 9216), (9216, 10240)):
         err = np.abs(got[lo:hi] - want[lo:hi]).max() / np.abs(want[lo:hi]).max()
-        assert err < 5e-3, (lo, err)
+        assert err < 1e-2, (lo, err)
     dxw = dxw.T.cpu().numpy()
-    assert np.abs(dx.float().cpu().numpy() - dxw).max() <= 5e-3 * np.abs(dxw).max()
+    assert np.abs(dx.float().cpu().numpy() - dxw).max() <= 1e-2 * np.abs(dxw).max()

@@ -30,7 +30,7 @@ def test_training_converges(ngp, scene, cfg):
     assert 128 <= s2["rays_per_batch"] <= 1 << 18 and s2["rays_per_batch"] % 128 == 0
     assert 0.0 < s2["density_grid_occupancy_ratio"] < 1.0
     assert np.isfinite(s2["loss"]) and s2["loss"] < s1["loss"]
-    assert after["psnr"] > before["psnr"] + 3.0, (before, after["psnr"])
+    assert after["psnr"] > before + 3.0, (before, after["psnr"])
     v = model.validate()
     assert v["image_count"] == 1 and np.isfinite(v["psnr"])
     model.close()
@@ -44,8 +44,10 @@ def test_weights_roundtrip_and_load_rules(ngp, scene):
     b = ngp.InstantNGP(scene)
     b.set_params(w)
     assert (b.get_params() == w).all()
-    pa, pb = a.test(1)["psnr"], b.test(1)["psnr"]
-    assert abs(pa - pb) < 1e-6 or (np.isinf(pa) and np.isinf(pb))
+    # weights only (as the reference's load_weights): b keeps its own, untrained occupancy grid
+    fresh = ngp.InstantNGP(scene)
+    assert b.test(1)["psnr"] > fresh.test(1)["psnr"]
+    fresh.close()
     with pytest.raises(RuntimeError, match="before training"):
         a.set_params(w)
     a.close()
