@@ -278,6 +278,13 @@ NGP_API uint32_t ngp_trainer_param_count(const ngp_trainer* t);
  * loading resets the optimizer and is allowed only before training, ngp.train.cpp:312). */
 NGP_API int ngp_trainer_get_params(const ngp_trainer* t, float* host_out, uint32_t count);
 NGP_API int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_t count);
+/* Data parallelism over NVLink (no counterpart in the single-GPU reference; hooks between
+ * backward_network and step_optimizer, ngp.train.cpp:123-124).  Rank 0 creates an NCCL unique id
+ * (ngp_nccl_unique_id, 128 bytes), the caller shares it with every rank, and each rank's trainer
+ * joins before its first step.  Each rank then marches its own rays (PCG32 stream step*world +
+ * rank) and the fp32 gradient is averaged with one all-reduce per step. */
+NGP_API int ngp_nccl_unique_id(uint8_t* out, size_t bytes);
+NGP_API int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank);
 /* Occupancy bitfield (2^18 bytes) and density-grid values (2^21 floats) to the host. */
 NGP_API int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host, float* values_host);
 

@@ -12,11 +12,14 @@
 // * evaluation renders whole 2^18-pixel tiles instead of 4096-pixel tiles.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <string>
 #include <vector>
 
 #include "common.cuh"
 #include "sampler.cuh"
+
+#include <nccl.h>
 
 using namespace ngp;
 
@@ -86,6 +89,9 @@ struct ngp_trainer {
 
     // host state (ngp.train.ixx:79-89)
     uint32_t step              = 0;
+    // data parallelism: one trainer per GPU, rays split by rank, gradients all-reduced
+    ncclComm_t comm = nullptr;
+    int world = 1, rank = 0;
     uint32_t rays_per_batch    = 1u << 12;
     uint32_t inference_samples = kMaxSamples;
     uint32_t measured_before = 0, measured = 0;
@@ -113,6 +119,7 @@ void destroy(ngp_trainer* t) {
                     t->counters, t->enc, t->out, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison};
     for (void* p : ptrs) cudaFree(p);
+    if (t->comm) ncclCommDestroy(t->comm);
     if (t->stream) cudaStreamDestroy(t->stream);
     delete t;
 }
@@ -215,14 +222,17 @@ int train_step(ngp_trainer* t) {
     const Split& s = t->train;
     NGP_TRY(update_grid(t));
     // sample_training_batch (ngp.train.cu:1919-1930)
-    NGP_TRY(ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, t->step, t->rays_per_batch, nullptr,
+    // each rank draws its rays from its own PCG32 stream; rank 0 of a single-GPU run uses the
+    // reference's stream (step << 32)
+    const uint32_t rng_step = t->step * static_cast<uint32_t>(t->world) + static_cast<uint32_t>(t->rank);
+    NGP_TRY(ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, rng_step, t->rays_per_batch, nullptr,
                                     t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->block_totals,
                                     t->counters + 0, t->counters + 1, t->stream));
     // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524)
     NGP_TRY(encode(t, t->inference_samples, t->coords, t->enc, t->inference_samples));
     NGP_TRY(ngp_mlp_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->coords, 7, t->out, nullptr, t->stream));
     // compositing, loss, compaction, padding (ngp.train.cu:1932-1956)
-    NGP_TRY(ngp_training_loss_and_compact(t->rays_per_batch, t->step, t->counters + 0, s.pixels, s.frames, s.width, s.height, t->out,
+    NGP_TRY(ngp_training_loss_and_compact(t->rays_per_batch, rng_step, t->counters + 0, s.pixels, s.frames, s.width, s.height, t->out,
                                           t->counters + 2, t->ray_indices, t->rays, t->numsteps, t->coords, t->ccoords, t->dloss,
                                           t->loss_values, t->loss_scratch, t->loss_scratch_bytes, t->stream));
     NGP_TRY(ngp_pad_training_batch(t->counters + 2, t->ccoords, t->dloss, t->stream));
@@ -231,8 +241,14 @@ int train_step(ngp_trainer* t) {
     NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kNetworkBatch, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
                              t->mlp_scratch_floats, t->grads, nullptr, 1.0f, t->stream));
     NGP_TRY(ngp_encode_grid_backward(&t->layout, kNetworkBatch, t->ccoords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams, t->stream));
+    // data parallel: average the fp32 gradient over ranks (one all-reduce per step); every rank
+    // then takes the identical Adam step, so the replicas (and their density grids) stay equal
+    if (t->comm != nullptr) {
+        const ncclResult_t r = ncclAllReduce(t->grads, t->grads, t->n_params, ncclFloat, ncclSum, t->comm, t->stream);
+        if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+    }
     // step_optimizer (ngp.train.cu:1973-1980)
-    NGP_TRY(ngp_adam_step(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale, t->master, t->params, t->grads,
+    NGP_TRY(ngp_adam_step(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world), t->master, t->params, t->grads,
                           t->adam_m, t->adam_v, t->adam_steps, 1, t->stream));
     // adaptive batch (ngp.train.cpp:125-133)
     uint32_t c[3];
@@ -384,6 +400,30 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
 }
 
 extern "C" void ngp_trainer_destroy(ngp_trainer* t) { destroy(t); }
+
+extern "C" int ngp_nccl_unique_id(uint8_t* out, size_t bytes) {
+    clear_error();
+    if (out == nullptr || bytes < sizeof(ncclUniqueId)) return fail(NGP_ERR_INVALID, "nccl id: buffer too small");
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    std::memcpy(out, &id, sizeof(id));
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank) {
+    clear_error();
+    if (t == nullptr || unique_id == nullptr || world < 1 || rank < 0 || rank >= world) return fail(NGP_ERR_INVALID, "trainer join: bad arguments");
+    if (t->step != 0) return fail(NGP_ERR_STATE, "trainer join: only before training");
+    if (world == 1) return NGP_OK;
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    const ncclResult_t r = ncclCommInitRank(&t->comm, world, id, rank);
+    if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    t->world = world;
+    t->rank  = rank;
+    return NGP_OK;
+}
 
 extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats* stats) {
     clear_error();

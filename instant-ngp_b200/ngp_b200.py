@@ -432,6 +432,24 @@ class InstantNGP:
         p = np.ascontiguousarray(params, np.float32)
         _check(lib().ngp_trainer_set_params(self.handle, ctypes.c_void_p(p.ctypes.data), _u32(p.size)), "ngp_trainer_set_params")
 
+    def join(self, unique_id: bytes, world: int, rank: int) -> None:
+        """Join a data-parallel group of `world` trainers (one per GPU) before the first step."""
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id[:128].ljust(128, b"\0"))
+        _check(lib().ngp_trainer_join(self.handle, buf, ctypes.c_int(world), ctypes.c_int(rank)), "ngp_trainer_join")
+
+    def join_process_group(self) -> None:
+        """Join using the current torch.distributed process group to share the NCCL id."""
+        import torch
+        import torch.distributed as dist
+
+        world, rank = dist.get_world_size(), dist.get_rank()
+        if world == 1:
+            return
+        uid = nccl_unique_id() if rank == 0 else bytes(128)
+        t = torch.tensor(list(uid), dtype=torch.uint8, device="cuda")
+        dist.broadcast(t, src=0)
+        self.join(bytes(t.cpu().tolist()), world, rank)
+
     def get_grid(self):
         import numpy as np
 
@@ -439,3 +457,9 @@ class InstantNGP:
         vals = np.zeros(GRID_CELLS, np.float32)
         _check(lib().ngp_trainer_get_grid(self.handle, ctypes.c_void_p(bits.ctypes.data), ctypes.c_void_p(vals.ctypes.data)), "ngp_trainer_get_grid")
         return bits, vals
+
+
+def nccl_unique_id() -> bytes:
+    buf = (ctypes.c_uint8 * 128)()
+    _check(lib().ngp_nccl_unique_id(buf, ctypes.c_size_t(128)), "ngp_nccl_unique_id")
+    return bytes(buf)
