@@ -1,23 +1,25 @@
 """Benchmark of the B200-native NeRF hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload encode]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload train|encode]
 
-Workloads (BASELINE configurations, seeded synthetic inputs -- the reference's datasets are not
-available here):
-  encode  config 0: hash-grid encoding forward + backward, 2^18 points per GPU, L=16, F=2,
-          log2 T=19, base 16, b=exp(ln(2048/16)/15).  One step = forward, zero the fp32 gradient
-          table, backward (and, for N > 1, an NCCL all-reduce of the gradient table).
+Workloads (BASELINE configurations; seeded synthetic inputs stand in for the reference's
+NeRF-synthetic datasets, which are not available here):
+  train   config 3 (default): end-to-end NeRF training on the procedural 64-sphere scene, 100
+          train / 20 test views of 800x800, config-0 hash grid + config-1 MLPs, batch 2^18
+          samples per step per GPU with the adaptive ray count.  One step = the reference's
+          step (density-grid update on its schedule, marching, inference pass, loss and
+          compaction, backward, Adam); data parallel over N GPUs with one NCCL gradient
+          all-reduce per step (weak scaling: 2^18 samples per GPU).
+  encode  config 0: hash-grid encoding forward + backward, 2^18 points per GPU.
 
-Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events on the launching
-stream; L2 is flushed (a 256 MB write) before every timed step, outside the events.  The whole
-timed loop is bracketed by a barrier and a device synchronize; the max over ranks is reported.
-`value` is the whole-job throughput (all ranks' points / max per-rank time).  `e2e` repeats the
-step through the public API with host-resident (pinned) inputs copied in and the result copied
-out inside the timed region.
+Timing: W untimed warm-up steps, then K steps timed on the device with CUDA events on the
+stream that runs them, bracketed by a barrier and a device synchronize; the max over ranks is
+reported.  Training's working set (117 MB of samples, 268 MB of encodings, 256 MB dataset)
+exceeds the 126 MB L2; the encode workload flushes L2 before every timed step.
 
 --impl reference runs the reference's own CUDA build (oracle/_ref, compiled from the reference's
-sources for sm_100a) on the same workload at the reference's layout (8 levels x 4 features, the
-only one its kernels support), on rank 0 only.
+sources for sm_100a) on the same workload, on rank 0 only, at the reference's compiled grid
+layout (8 levels x 4 features; its kernels support no other).
 """
 from __future__ import annotations
 
@@ -39,6 +41,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "instant-ngp_b200"))
 
 L2_FLUSH_BYTES = 256 << 20
+BATCH = 1 << 18
 
 
 def load_peaks() -> dict:
@@ -65,8 +68,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            threading.Thread(target=self._read, daemon=True).start()
         except OSError:
             self.proc = None
         return self
@@ -76,7 +78,6 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def wait_first(self, timeout: float = 5.0) -> None:
-        """Block until nvidia-smi has produced its first sample, so the timed region is covered."""
         t0 = time.time()
         while self.proc is not None and not self.lines and time.time() - t0 < timeout:
             time.sleep(0.05)
@@ -142,15 +143,214 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def clocks_ok(c: dict) -> bool:
+    return not any(r in c.get("reasons", []) for r in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"))
+
+
+# ------------------------------------------------------------------------------------------------
+# train workload (config 3)
+# ------------------------------------------------------------------------------------------------
+def make_dataset(args):
+    import workloads
+
+    return workloads.procedural_dataset(n_train=args.views, n_test=args.test_views, width=args.res, height=args.res, seed=3, device="cuda")
+
+
+# FLOPs per row of the fused MLPs: forward 2*(32*64 + 64*16) + 2*(32*64 + 64*64 + 64*16) = 20,480;
+# forward + backward (input gradients + weight gradients) = 61,440.
+MLP_FWD_FLOP = 20480
+MLP_FWDBWD_FLOP = 61440
+
+
+def phase_roofline(phases: dict, peaks: dict) -> dict:
+    """Roofline of the dominant phase of the training step (per-launch averages from the
+    trainer's in-step CUDA events)."""
+    steps = max(phases["steps"], 1)
+    ms = {k: v / steps for k, v in phases["ms"].items()}
+    n_inf = phases["mean_inference_samples"]
+    total = sum(ms.values())
+    dom = max(ms, key=ms.get)
+    t = ms[dom] * 1e-3
+    if dom in ("mlp_fwd_inference", "mlp_bwd"):
+        flops = (MLP_FWD_FLOP * n_inf) if dom == "mlp_fwd_inference" else (MLP_FWDBWD_FLOP * BATCH)
+        achieved = flops / t / 1e12
+        return {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": None, "share": round(ms[dom] / total, 3),
+                "peak_source": peaks["source"] + " (sustained dense bf16; fp16 has the same tensor rate)"}
+    # memory-bound phases: algorithmic bytes per unit
+    per = {"encode_fwd_inference": (28 + 64 + 16 * 8 * 2 * 2, n_inf), "encode_fwd_batch": (28 + 64 + 16 * 8 * 2 * 2, BATCH),
+           "encode_bwd": (28 + 64 + 16 * 8 * 2 * 4, BATCH), "march": (28 * 1.0, n_inf), "loss_compact_pad": (28 + 32 + 28 + 32, BATCH),
+           "adam": (38, 12_206_480), "grid_update": (16, 128 ** 3 * 2), "allreduce": (8, 12_206_480)}
+    b, n = per.get(dom, (0, 0))
+    achieved = b * n / t / 1e9
+    return {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "share": round(ms[dom] / total, 3), "peak_source": peaks["source"],
+            "note": "achieved counts the phase's HBM streams plus table bytes gathered/scattered per unit (L2-served)"}
+
+
+def bench_train_ours(args, rank, world, local):
+    import torch
+    import ngp_b200 as ngp
+
+    peaks = load_peaks()
+    ds = make_dataset(args)
+    model = ngp.InstantNGP(ds, ngp.config0_trainer_config())
+    if world > 1:
+        model.join_process_group()
+    model.train(args.warmup)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        clocks.wait_first()
+        stats = model.train(args.steps)
+        time.sleep(0.25)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(stats["elapsed_ms"], world)
+    # per-phase breakdown (separate, profiled steps; not part of the timed number)
+    model.set_profiling(True)
+    model.train(min(args.steps, 50))
+    phases = model.phase_times()
+    model.set_profiling(False)
+    # e2e through the public API: one train(1) call per step (host round trip, counters and loss
+    # read back every step), timed with events around the whole loop
+    n_e2e = max(3, args.steps // 4)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    rays = 0
+    for _ in range(n_e2e):
+        st = model.train(1)
+        rays = st["rays_per_batch"]
+    e.record()
+    e.synchronize()
+    e2e_ms = max_over_ranks(s.elapsed_time(e) / n_e2e, world)
+    psnr = model.test(count=min(4, args.test_views))["psnr"] if rank == 0 else None
+    model.close()
+    value = world * BATCH * args.steps / (ms * 1e-3)
+    res = {
+        "metric": "NeRF train samples/s (config 3)",
+        "value": round(value, 1),
+        "unit": "samples/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 params/activations, fp32 accumulation, gradients and Adam",
+        "data": "synthetic procedural scene (64 Lambert spheres, seeded), rendered on the device",
+        "config": {"workload": "config3 end-to-end training", "views": args.views, "resolution": args.res, "batch_samples_per_gpu": BATCH,
+                   "grid": "L=16 F=2 log2T=19 base 16 b=1.3819", "mlp": "density 32-64-16, colour 32-64-64-16",
+                   "parallelism": f"dp{world} (NCCL all-reduce of the fp32 gradient per step)",
+                   "l2": "working set > L2 (samples 117 MB, encodings 268 MB, dataset 256 MB); no flush",
+                   "pre_compaction_samples_per_step": stats["measured_sample_count_before_compaction"],
+                   "rays_per_batch": stats["rays_per_batch"], "test_psnr_after_run": psnr,
+                   "steps_trained": args.warmup + args.steps},
+        "phase_ms_per_step": {k: round(v / max(phases["steps"], 1), 4) for k, v in phases["ms"].items()},
+        "roofline": phase_roofline(phases, peaks),
+        "e2e": {"value": round(world * BATCH / (e2e_ms * 1e-3), 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 12 + 4 * rays,
+                "note": "InstantNGP.train(1) per step; the dataset is uploaded once at construction (as the reference does), each step "
+                        "reads back its 3 counters and the per-ray loss"},
+        "gpu_launches": None,
+        "clocks": clocks.summary(),
+    }
+    res["gpu_launches"] = res_launch_count(phases, args.steps)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_train(args)
+    return res
+
+
+def res_launch_count(phases, steps):
+    # kernels of one steady-state step: march 3, encode 1, mlp fwd 1, loss 3 (+memset), pad 1,
+    # encode 1, mlp bwd 2, encode bwd 1, adam 1; grid update (every 16 steps) 6
+    return int(steps * 14 + steps // 16 * 6)
+
+
+def cpu_baseline_train(args, budget_s: float = 15.0) -> dict:
+    """The scalar C++ oracle of the encoding + MLP forward (the inference pass, the dominant work
+    per training sample) on the host cores, bounded sample; reported per sample."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import ngp_b200 as ngp
+    import workloads
+    from oracle import Oracle
+
+    ora = Oracle()
+    cores = os.cpu_count() or 1
+    lay = ngp.config0_layout()
+    layt = (np.array(lay.level_offsets(), np.uint32), np.array(lay.level_resolutions(), np.uint32), np.array(lay.level_scales(), np.float32))
+    n = 1 << 13
+    coords, table, _ = workloads.encode_inputs(n, lay.n_params, 16, 2, seed=7, coord_stride=7)
+    _, c2, _ = workloads.mlp_inputs(n, seed=8)
+    coords[:, 4:7] = c2[:, 4:7]
+    params = workloads.xavier_mlp_params(1)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        x = ora.encode_forward(layt, coords, table, 2, mode=0, threads=cores)
+        ora.mlp_forward(params, x, coords, threads=cores)
+        done += n
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt, 1), "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{done} samples through the scalar encoding + MLP forward ({n}-sample batches, {dt:.1f} s); backward, marching "
+                      f"and Adam not included, so this bounds the CPU rate from above"}
+
+
+def bench_train_reference(args, rank, world, local):
+    import torch
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from oracle import RefLib
+
+    ref = RefLib()
+    ds = make_dataset(args)
+    tr, te = ds["train"], ds["test"]
+    px, cam = np.ascontiguousarray(tr["pixels"]), np.ascontiguousarray(tr["camera"])
+    tpx, tcam = np.ascontiguousarray(te["pixels"]), np.ascontiguousarray(te["camera"])
+    f = ref.lib
+    f.ref_train_create.restype = ctypes.c_void_p
+    h = f.ref_train_create(ctypes.c_void_p(px.ctypes.data), ctypes.c_size_t(px.nbytes), ctypes.c_void_p(cam.ctypes.data), ctypes.c_uint32(px.shape[0]),
+                           ctypes.c_uint32(args.res), ctypes.c_uint32(args.res), ctypes.c_float(tr["focal"][0]), ctypes.c_float(tr["focal"][1]),
+                           ctypes.c_float(tr["principal"][0]), ctypes.c_float(tr["principal"][1]), ctypes.c_void_p(tpx.ctypes.data),
+                           ctypes.c_size_t(tpx.nbytes), ctypes.c_void_p(tcam.ctypes.data), ctypes.c_uint32(tpx.shape[0]))
+    if not h:
+        return {"impl": "reference", "unavailable": "reference trainer construction failed"}
+    h = ctypes.c_void_p(h)
+    out = (ctypes.c_float * 4)()
+    if f.ref_train_steps(h, ctypes.c_int32(args.warmup), out) != 0:
+        return {"impl": "reference", "unavailable": "reference training stopped during warm-up"}
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        clocks.wait_first()
+        rc = f.ref_train_steps(h, ctypes.c_int32(args.steps), out)
+        time.sleep(0.25)
+    ms = float(out[0])
+    sse = ctypes.c_double(0)
+    f.ref_train_test_sse(h, ctypes.byref(sse))
+    mse = sse.value / (args.test_views * args.res * args.res * 3.0)
+    f.ref_train_destroy(h)
+    value = BATCH * args.steps / (ms * 1e-3)
+    return {
+        "impl": "reference", "metric": "NeRF train samples/s (config 3)", "value": round(value, 1), "unit": "samples/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 params/activations and accumulation (reference)", "data": "synthetic procedural scene (seeded)",
+        "config": {"workload": "config3 end-to-end training", "views": args.views, "resolution": args.res, "batch_samples_per_gpu": BATCH,
+                   "grid": "reference compiled layout L=8 F=4 log2T=19 (its kernels support no other)", "parallelism": "dp1",
+                   "pre_compaction_samples_per_step": int(out[2]), "rays_per_batch": int(out[3]),
+                   "test_psnr_after_run": (-10 * math.log10(mse)) if mse > 0 else None, "steps_trained": args.warmup + args.steps,
+                   "ok": rc == 0},
+        "cpu_baseline": {"value": round(value, 1), "unit": "samples/s", "cores": 0, "kind": "reference",
+                         "sample": "reference CUDA build (oracle/_ref: its own ngp::cuda step sequence) on one B200; the reference has "
+                                   "no CPU implementation of this path"},
+        "e2e": {"value": round(value, 1), "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 8},
+        "clocks": clocks.summary(),
+    }
+
+
 # ------------------------------------------------------------------------------------------------
 # encode workload (config 0)
 # ------------------------------------------------------------------------------------------------
-ENCODE_N = 1 << 18
-
-
-def time_steps(step_fn, steps: int, warmup: int, flush, stream, world: int, events_per_kernel=None):
-    """Warm up, then time `steps` calls of step_fn, each between CUDA events on `stream` with an
-    L2 flush before it (outside the events).  Returns per-step ms list (this rank)."""
+def time_steps(step_fn, steps: int, warmup: int, flush, stream, world: int):
     import torch
 
     for _ in range(warmup):
@@ -179,7 +379,7 @@ def bench_encode_ours(args, rank, world, local):
     import workloads
 
     layout = ngp.config0_layout()
-    L, F, n = 16, 2, ENCODE_N
+    L, F, n = 16, 2, BATCH
     coords_h, table_h, dy_h = workloads.encode_inputs(n, layout.n_params, L, F, seed=1000 + rank)
     stream = torch.cuda.current_stream()
     coords = torch.from_numpy(coords_h).cuda()
@@ -201,35 +401,27 @@ def bench_encode_ours(args, rank, world, local):
 
             dist.all_reduce(grad)
 
-    # per-kernel timing (for the roofline) on the same stream, L2 flushed before each launch
-    def kernel_times(reps=20):
-        fw, bw = [], []
-        for _ in range(reps):
-            for which, acc in (("f", fw), ("b", bw)):
-                flush()
-                if which == "b":
-                    grad.zero_()
-                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s.record(stream)
-                if which == "f":
-                    ngp.encode_grid_forward(layout, coords, table, feats, stream=stream)
-                else:
-                    ngp.encode_grid_backward(layout, coords, dy, grad, stream=stream)
-                e.record(stream)
-                e.synchronize()
-                acc.append(s.elapsed_time(e))
-        return statistics.median(fw), statistics.median(bw)
-
     with ClockSampler(local) as clocks:
         clocks.wait_first()
         times = time_steps(step, args.steps, args.warmup, flush, stream, world)
         time.sleep(0.25)
     ms = max_over_ranks(sum(times) / len(times), world)
-    fwd_ms, bwd_ms = kernel_times() if not args.quick else (float("nan"), float("nan"))
-    if args.quick:
-        return {"metric": "hash-encode fwd+bwd Gpts/s (config 0)", "value": world * n / (ms * 1e-3) / 1e9, "quick": True}
-
-    # e2e through the public API: pinned host inputs in, encoded features out, every step.
+    fw, bw = [], []
+    for _ in range(20):
+        for which, acc in (("f", fw), ("b", bw)):
+            flush()
+            if which == "b":
+                grad.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            if which == "f":
+                ngp.encode_grid_forward(layout, coords, table, feats, stream=stream)
+            else:
+                ngp.encode_grid_backward(layout, coords, dy, grad, stream=stream)
+            e.record(stream)
+            e.synchronize()
+            acc.append(s.elapsed_time(e))
+    fwd_ms, bwd_ms = statistics.median(fw), statistics.median(bw)
     coords_pin = torch.from_numpy(coords_h).pin_memory()
     dy_pin = torch.from_numpy(dy_h).pin_memory()
     feats_pin = torch.empty((L * F, n), dtype=torch.float16).pin_memory()
@@ -242,73 +434,31 @@ def bench_encode_ours(args, rank, world, local):
 
     e2e_times = time_steps(e2e_step, max(3, args.steps // 2), 2, flush, stream, world)
     e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
-    h2d = coords_h.nbytes + dy_h.nbytes
-    d2h = feats.numel() * 2
-
     peaks = load_peaks()
-    # algorithmic bytes per point (forward): 12 B coords + 64 B features out (HBM) + 8 corners x
-    # 16 levels x 2 features x 2 B gathered from the table (served by L2 / L1).
     fwd_bytes_pt = 12 + L * F * 2 + L * 8 * F * 2
     bwd_bytes_pt = 12 + L * F * 2 + L * 8 * F * 4
     dom = "forward" if fwd_ms >= bwd_ms else "backward"
-    dom_ms = max(fwd_ms, bwd_ms)
     dom_bytes = (fwd_bytes_pt if dom == "forward" else bwd_bytes_pt) * n
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-    res = {
-        "metric": "hash-encode fwd+bwd Gpts/s (config 0)",
-        "value": round(world * n / (ms * 1e-3) / 1e9, 4),
-        "unit": "Gpts/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(ms, 5),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "fp16 table/features, fp32 accumulation and gradients",
+    achieved = dom_bytes / (max(fwd_ms, bwd_ms) * 1e-3) / 1e9
+    return {
+        "metric": "hash-encode fwd+bwd Gpts/s (config 0)", "value": round(world * n / (ms * 1e-3) / 1e9, 4), "unit": "Gpts/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 table/features, fp32 accumulation and gradients",
         "data": "synthetic (seeded uniform points, U(+-1e-4) fp16 table, N(0,1) fp16 dL/dy)",
-        "config": {"workload": "config0 hash-grid encode fwd+bwd", "points_per_gpu": n, "levels": L, "features": F,
-                   "log2_hashmap_size": 19, "base_resolution": 16, "per_level_scale": round(2 ** (7 / 15), 6),
-                   "parallelism": f"dp{world}", "l2": "flushed (256 MB write) before every timed step"},
+        "config": {"workload": "config0 hash-grid encode fwd+bwd", "points_per_gpu": n, "levels": L, "features": F, "log2_hashmap_size": 19,
+                   "base_resolution": 16, "per_level_scale": round(2 ** (7 / 15), 6), "parallelism": f"dp{world}",
+                   "l2": "flushed (256 MB write) before every timed step"},
         "kernels_ms": {"encode_forward": round(fwd_ms, 5), "encode_backward": round(bwd_ms, 5)},
-        "roofline": {"kernel": f"encode_{dom}", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
-                     "peak_source": peaks["source"],
+        "roofline": {"kernel": f"encode_{dom}", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"],
                      "note": "achieved counts HBM streams plus table bytes gathered (L2-served) per point"},
-        "e2e": {"value": round(world * n / (e2e_ms * 1e-3) / 1e9, 4), "unit": "Gpts/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": 2 * args.steps,
-        "clocks": clocks.summary(),
+        "e2e": {"value": round(world * n / (e2e_ms * 1e-3) / 1e9, 4), "unit": "Gpts/s", "h2d_bytes_per_step": coords_h.nbytes + dy_h.nbytes,
+                "d2h_bytes_per_step": feats.numel() * 2},
+        "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline_encode(layout)
-    return res
-
-
-def cpu_baseline_encode(layout, budget_s: float = 12.0) -> dict:
-    """The oracle (scalar C++ port of the reference math) on the host cores, bounded sample."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import workloads
-    from oracle import Oracle
-
-    ora = Oracle()
-    cores = os.cpu_count() or 1
-    lay = (np.array(layout.level_offsets(), np.uint32), np.array(layout.level_resolutions(), np.uint32),
-           np.array(layout.level_scales(), np.float32))
-    n = 1 << 15
-    coords, table, dy = workloads.encode_inputs(n, layout.n_params, 16, 2, seed=7)
-    done, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < budget_s:
-        ora.encode_forward(lay, coords, table, 2, mode=0, threads=cores)
-        ora.encode_backward(lay, coords, dy, 2, threads=cores)
-        done += n
-    dt = time.perf_counter() - t0
-    return {"value": round(done / dt / 1e9, 6), "unit": "Gpts/s", "cores": cores, "kind": "port",
-            "sample": f"{done} points of config 0 (fwd+bwd, {n}-point batches) in {dt:.1f} s"}
 
 
 def bench_encode_reference(args, rank, world, local):
-    """The reference's own encode_grid_forward/backward kernels (its 8x4 layout) on one B200."""
     import torch
 
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -316,15 +466,11 @@ def bench_encode_reference(args, rank, world, local):
     from oracle import RefLib
 
     ref = RefLib()
-    total = int(ref.lib.ref_total_param_count())
-    mlp = int(ref.lib.ref_mlp_param_count())
-    n_grid = total - mlp
-    n = ENCODE_N
+    n_grid = int(ref.lib.ref_total_param_count()) - int(ref.lib.ref_mlp_param_count())
+    n = BATCH
     coords_h, table_h, dy_h = workloads.encode_inputs(n, n_grid, 8, 4, seed=1000, coord_stride=7)
     stream = torch.cuda.current_stream()
-    coords = torch.from_numpy(coords_h).cuda()
-    table = torch.from_numpy(table_h.view(np.int16)).cuda()
-    dy = torch.from_numpy(dy_h).cuda()
+    coords, table, dy = (torch.from_numpy(a).cuda() for a in (coords_h, table_h.view(np.int16), dy_h))
     feats = torch.empty((32, n), dtype=torch.float16, device="cuda")
     grad = torch.empty(n_grid, dtype=torch.float16, device="cuda")
     flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
@@ -344,16 +490,11 @@ def bench_encode_reference(args, rank, world, local):
     ms = sum(times) / len(times)
     value = n / (ms * 1e-3) / 1e9
     return {
-        "impl": "reference",
-        "metric": "hash-encode fwd+bwd Gpts/s (config 0)",
-        "value": round(value, 4), "unit": "Gpts/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp16 table/features, fp16 accumulation and gradients (reference)",
-        "data": "synthetic (seeded)",
+        "impl": "reference", "metric": "hash-encode fwd+bwd Gpts/s (config 0)", "value": round(value, 4), "unit": "Gpts/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 table/features, fp16 accumulation and gradients (reference)", "data": "synthetic (seeded)",
         "config": {"workload": "config0 hash-grid encode fwd+bwd", "points_per_gpu": n, "levels": 8, "features": 4,
-                   "note": "reference kernels support only their compiled 8x4 layout (static_assert ngp.train.cu:58); "
-                           "same 32 features and 512 gathered table bytes per point as config 0",
-                   "parallelism": "dp1", "l2": "flushed (256 MB write) before every timed step"},
+                   "note": "reference kernels support only their compiled 8x4 layout (static_assert ngp.train.cu:58)", "parallelism": "dp1"},
         "cpu_baseline": {"value": round(value, 4), "unit": "Gpts/s", "cores": 0, "kind": "reference",
                          "sample": "reference CUDA build (oracle/_ref) on one B200; the reference has no CPU implementation"},
         "e2e": {"value": round(value, 4), "unit": "Gpts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -364,21 +505,29 @@ def bench_encode_reference(args, rank, world, local):
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["encode"], default="encode")
+    ap.add_argument("--workload", choices=["train", "encode"], default="train")
+    ap.add_argument("--views", type=int, default=100)
+    ap.add_argument("--test-views", type=int, default=20)
+    ap.add_argument("--res", type=int, default=800)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--quick", action="store_true", help="timed steps only (for profiler runs)")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 300 if args.workload == "train" else 500
+    if args.warmup is None:
+        args.warmup = 300 if args.workload == "train" else 5
     args.warmup = max(args.warmup, 3)
 
     rank, world, local = dist_setup()
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(bench_encode_reference(args, rank, world, local)), flush=True)
+            fn = bench_train_reference if args.workload == "train" else bench_encode_reference
+            print(json.dumps(fn(args, rank, world, local)), flush=True)
         return 0
-    res = bench_encode_ours(args, rank, world, local)
+    fn = bench_train_ours if args.workload == "train" else bench_encode_ours
+    res = fn(args, rank, world, local)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

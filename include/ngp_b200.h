@@ -285,6 +285,13 @@ NGP_API int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_
  * rank) and the fp32 gradient is averaged with one all-reduce per step. */
 NGP_API int ngp_nccl_unique_id(uint8_t* out, size_t bytes);
 NGP_API int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank);
+/* Per-phase device time of the training step, summed over the steps since profiling was
+ * enabled (cudaEvents between phases): 0 grid update, 1 ray marching, 2 encoding of the
+ * inference samples, 3 network forward of the inference samples, 4 loss + compaction + padding,
+ * 5 encoding of the batch, 6 network backward, 7 encoding backward, 8 gradient all-reduce,
+ * 9 Adam.  out_ms needs 10 floats; out_mean_inference_samples = mean samples evaluated per step. */
+NGP_API int ngp_trainer_set_profiling(ngp_trainer* t, int enable);
+NGP_API int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_steps, float* out_mean_inference_samples);
 /* Occupancy bitfield (2^18 bytes) and density-grid values (2^21 floats) to the host. */
 NGP_API int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host, float* values_host);
 

@@ -25,7 +25,8 @@ using namespace ngp;
 
 namespace {
 
-constexpr uint32_t kMlpParams = 10240;
+constexpr uint32_t kMlpParams  = 10240;
+constexpr int kTrainPhases     = 10;  // see ngp_trainer_phase_times
 
 template <typename T>
 int dalloc(T*& p, size_t count, const char* what) {
@@ -92,6 +93,12 @@ struct ngp_trainer {
     // data parallelism: one trainer per GPU, rays split by rank, gradients all-reduced
     ncclComm_t comm = nullptr;
     int world = 1, rank = 0;
+    // optional per-phase timing (cudaEvents between the phases of a step)
+    bool profiling = false;
+    cudaEvent_t marks[kTrainPhases + 1] = {};
+    double phase_ms[kTrainPhases]       = {};
+    double inference_samples_sum        = 0.0;
+    uint32_t profiled_steps             = 0;
     uint32_t rays_per_batch    = 1u << 12;
     uint32_t inference_samples = kMaxSamples;
     uint32_t measured_before = 0, measured = 0;
@@ -120,6 +127,8 @@ void destroy(ngp_trainer* t) {
                     t->mlp_scratch, t->eval_sse, t->comparison};
     for (void* p : ptrs) cudaFree(p);
     if (t->comm) ncclCommDestroy(t->comm);
+    for (cudaEvent_t e : t->marks)
+        if (e) cudaEventDestroy(e);
     if (t->stream) cudaStreamDestroy(t->stream);
     delete t;
 }
@@ -218,9 +227,15 @@ int update_grid(ngp_trainer* t) {
     return NGP_OK;
 }
 
+void mark(ngp_trainer* t, int k) {
+    if (t->profiling) cudaEventRecord(t->marks[k], t->stream);
+}
+
 int train_step(ngp_trainer* t) {
     const Split& s = t->train;
+    mark(t, 0);
     NGP_TRY(update_grid(t));
+    mark(t, 1);
     // sample_training_batch (ngp.train.cu:1919-1930)
     // each rank draws its rays from its own PCG32 stream; rank 0 of a single-GPU run uses the
     // reference's stream (step << 32)
@@ -228,32 +243,50 @@ int train_step(ngp_trainer* t) {
     NGP_TRY(ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, rng_step, t->rays_per_batch, nullptr,
                                     t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->block_totals,
                                     t->counters + 0, t->counters + 1, t->stream));
+    mark(t, 2);
     // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524)
     NGP_TRY(encode(t, t->inference_samples, t->coords, t->enc, t->inference_samples));
+    mark(t, 3);
     NGP_TRY(ngp_mlp_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->coords, 7, t->out, nullptr, t->stream));
+    mark(t, 4);
     // compositing, loss, compaction, padding (ngp.train.cu:1932-1956)
     NGP_TRY(ngp_training_loss_and_compact(t->rays_per_batch, rng_step, t->counters + 0, s.pixels, s.frames, s.width, s.height, t->out,
                                           t->counters + 2, t->ray_indices, t->rays, t->numsteps, t->coords, t->ccoords, t->dloss,
                                           t->loss_values, t->loss_scratch, t->loss_scratch_bytes, t->stream));
     NGP_TRY(ngp_pad_training_batch(t->counters + 2, t->ccoords, t->dloss, t->stream));
+    mark(t, 5);
     // encoding of the batch, fused MLP backward (recompute), encoding backward
     NGP_TRY(encode(t, kNetworkBatch, t->ccoords, t->cenc, kNetworkBatch));
+    mark(t, 6);
     NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kNetworkBatch, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
                              t->mlp_scratch_floats, t->grads, nullptr, 1.0f, t->stream));
+    mark(t, 7);
     NGP_TRY(ngp_encode_grid_backward(&t->layout, kNetworkBatch, t->ccoords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams, t->stream));
+    mark(t, 8);
     // data parallel: average the fp32 gradient over ranks (one all-reduce per step); every rank
     // then takes the identical Adam step, so the replicas (and their density grids) stay equal
     if (t->comm != nullptr) {
         const ncclResult_t r = ncclAllReduce(t->grads, t->grads, t->n_params, ncclFloat, ncclSum, t->comm, t->stream);
         if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
     }
+    mark(t, 9);
     // step_optimizer (ngp.train.cu:1973-1980)
     NGP_TRY(ngp_adam_step(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world), t->master, t->params, t->grads,
                           t->adam_m, t->adam_v, t->adam_steps, 1, t->stream));
+    mark(t, 10);
     // adaptive batch (ngp.train.cpp:125-133)
     uint32_t c[3];
     NGP_TRY(check_cuda(cudaMemcpyAsync(c, t->counters, sizeof(c), cudaMemcpyDeviceToHost, t->stream), "read counters"));
     NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train step"));
+    if (t->profiling) {
+        for (int k = 0; k < kTrainPhases; ++k) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, t->marks[k], t->marks[k + 1]);
+            t->phase_ms[k] += ms;
+        }
+        t->inference_samples_sum += t->inference_samples;
+        ++t->profiled_steps;
+    }
     t->measured_before = c[1];
     t->measured        = c[2];
     if (t->measured == 0u) {
@@ -520,5 +553,27 @@ extern "C" int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host
     if (t == nullptr) return fail(NGP_ERR_INVALID, "get grid: null trainer");
     if (bitfield_host != nullptr) NGP_TRY(check_cuda(cudaMemcpy(bitfield_host, t->bitfield, kGridCells / 8u, cudaMemcpyDeviceToHost), "bitfield"));
     if (values_host != nullptr) NGP_TRY(check_cuda(cudaMemcpy(values_host, t->grid_values, sizeof(float) * kGridCells, cudaMemcpyDeviceToHost), "values"));
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_set_profiling(ngp_trainer* t, int enable) {
+    clear_error();
+    if (t == nullptr) return fail(NGP_ERR_INVALID, "profiling: null trainer");
+    if (enable && t->marks[0] == nullptr)
+        for (cudaEvent_t& e : t->marks) NGP_TRY(check_cuda(cudaEventCreate(&e), "profiling events"));
+    t->profiling = enable != 0;
+    for (double& v : t->phase_ms) v = 0.0;
+    t->inference_samples_sum = 0.0;
+    t->profiled_steps        = 0;
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_steps, float* out_mean_inference_samples) {
+    clear_error();
+    if (t == nullptr || out_ms == nullptr || n < static_cast<uint32_t>(kTrainPhases)) return fail(NGP_ERR_INVALID, "phase times: bad arguments");
+    for (int k = 0; k < kTrainPhases; ++k) out_ms[k] = static_cast<float>(t->phase_ms[k]);
+    if (out_steps != nullptr) *out_steps = t->profiled_steps;
+    if (out_mean_inference_samples != nullptr)
+        *out_mean_inference_samples = t->profiled_steps ? static_cast<float>(t->inference_samples_sum / t->profiled_steps) : 0.0f;
     return NGP_OK;
 }

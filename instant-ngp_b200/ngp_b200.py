@@ -432,6 +432,19 @@ class InstantNGP:
         p = np.ascontiguousarray(params, np.float32)
         _check(lib().ngp_trainer_set_params(self.handle, ctypes.c_void_p(p.ctypes.data), _u32(p.size)), "ngp_trainer_set_params")
 
+    PHASES = ("grid_update", "march", "encode_fwd_inference", "mlp_fwd_inference", "loss_compact_pad", "encode_fwd_batch", "mlp_bwd",
+              "encode_bwd", "allreduce", "adam")
+
+    def set_profiling(self, enable: bool = True) -> None:
+        _check(lib().ngp_trainer_set_profiling(self.handle, ctypes.c_int(1 if enable else 0)), "ngp_trainer_set_profiling")
+
+    def phase_times(self) -> dict:
+        out = (ctypes.c_float * 10)()
+        steps = ctypes.c_uint32(0)
+        mean_n = ctypes.c_float(0)
+        _check(lib().ngp_trainer_phase_times(self.handle, out, _u32(10), ctypes.byref(steps), ctypes.byref(mean_n)), "ngp_trainer_phase_times")
+        return {"steps": steps.value, "mean_inference_samples": mean_n.value, "ms": dict(zip(self.PHASES, list(out)))}
+
     def join(self, unique_id: bytes, world: int, rank: int) -> None:
         """Join a data-parallel group of `world` trainers (one per GPU) before the first step."""
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id[:128].ljust(128, b"\0"))
