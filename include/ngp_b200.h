@@ -212,6 +212,23 @@ NGP_API int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t step
                                           const float* coords, float* compacted_coords, uint16_t* dloss_doutput, float* loss_values,
                                           void* scratch, size_t scratch_bytes, void* stream);
 
+/* ngp_training_loss_and_compact without any device allocation by the caller or the library.
+ * No counterpart in the reference.  For callers that cannot allocate device memory when the loss
+ * runs (host callbacks and driver-managed regions where cudaMalloc is not allowed, plugin hosts
+ * that give a fixed memory budget): the scratch comes from one static device array of about
+ * 5 MiB that each GPU loading the library keeps until the process exits.  Limit: rays_per_batch
+ * <= ngp_training_loss_and_compact_noalloc_max_rays() (2^18); larger requests fail with
+ * NGP_ERR_INVALID.  The first call on a device looks up the array's device address (with that
+ * device current) and should come before any stream capture.  All calls on a device share the
+ * array: calls whose work overlaps on the GPU race with each other.  The scratch needs no
+ * clearing between calls (every byte read is written earlier in the same call). */
+NGP_API uint32_t ngp_training_loss_and_compact_noalloc_max_rays(void);
+NGP_API int ngp_training_loss_and_compact_noalloc(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                                  uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                                  uint32_t* compacted_counter, const uint32_t* ray_indices, const float* rays, uint32_t* numsteps,
+                                                  const float* coords, float* compacted_coords, uint16_t* dloss_doutput, float* loss_values,
+                                                  void* stream);
+
 /* Wrap-around padding of the compacted batch to 2^18 samples, copied gradients scaled by
  * count / 2^18.  Replaces K12/K13 (ngp.train.cu:862-874, 1946-1956). */
 NGP_API int ngp_pad_training_batch(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, void* stream);

@@ -331,3 +331,63 @@ extern "C" int ngp_eval_composite(uint32_t n_pixels, uint32_t pixel_offset, uint
         rendered);
     return check_launch("eval_composite_kernel");
 }
+
+// ---------------------------------------------------------------------------------------------
+// Variant without any allocation.
+//
+// Some callers cannot allocate device memory at the point where they run the loss: code that
+// runs inside a host callback or a driver-managed region where cudaMalloc is not allowed,
+// runtimes that hand a plugin only fixed buffers and forbid it from growing its footprint, and
+// integrations whose memory budget is fixed at start-up.  For them this entry point takes its
+// scratch from one statically sized device array that every GPU loading the library holds until
+// the process exits (kNoAllocScratchBytes, about 5 MiB: room for 2^18 rays).
+// ---------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr uint32_t kNoAllocMaxRays      = 1u << 18;
+constexpr size_t kNoAllocScratchBytes   = static_cast<size_t>(kNoAllocMaxRays) * 20u + (kNoAllocMaxRays / 128u) * 4u + 256u;
+static __device__ __align__(256) unsigned char g_noalloc_loss_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of this GPU's copy of the array, looked up once per device with that device
+// current.  The host-side name of the array is not a device address and must never be passed to
+// a kernel.
+int noalloc_scratch(void** out) {
+    int device = 0;
+    NGP_TRY(check_cuda(cudaGetDevice(&device), "no-alloc loss: cudaGetDevice"));
+    if (device < 0 || device >= kMaxDevices) return fail(NGP_ERR_INVALID, "no-alloc loss: device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[device] == nullptr) {
+        void* p = nullptr;
+        NGP_TRY(check_cuda(cudaGetSymbolAddress(&p, g_noalloc_loss_scratch), "no-alloc loss: cudaGetSymbolAddress"));
+        g_noalloc_ptr[device] = p;
+    }
+    *out = g_noalloc_ptr[device];
+    return NGP_OK;
+}
+
+}  // namespace
+
+extern "C" uint32_t ngp_training_loss_and_compact_noalloc_max_rays(void) { return kNoAllocMaxRays; }
+
+extern "C" int ngp_training_loss_and_compact_noalloc(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                                     uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                                     uint32_t* compacted_counter, const uint32_t* ray_indices, const float* rays,
+                                                     uint32_t* numsteps, const float* coords, float* compacted_coords, uint16_t* dloss_doutput,
+                                                     float* loss_values, void* stream) {
+    clear_error();
+    if (rays_per_batch > kNoAllocMaxRays)
+        return fail(NGP_ERR_INVALID, "training loss (no-alloc): rays_per_batch " + std::to_string(rays_per_batch) + " exceeds the static scratch limit of " +
+                                         std::to_string(kNoAllocMaxRays) + " rays");
+    if (rays_per_batch == 0) return NGP_OK;
+    void* scratch = nullptr;
+    NGP_TRY(noalloc_scratch(&scratch));
+    return ngp_training_loss_and_compact(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, compacted_counter,
+                                         ray_indices, rays, numsteps, coords, compacted_coords, dloss_doutput, loss_values, scratch,
+                                         kNoAllocScratchBytes, stream);
+}
