@@ -322,3 +322,52 @@ void ref_train_destroy(void* handle) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Marching of given rays with the reference's own device helpers (intersect_unit_aabb,
+// is_density_grid_occupied, advance_to_next_density_voxel; ngp.train.cu:199-249), in the loop of
+// generate_evaluation_samples_kernel (ngp.train.cu:609-666) written the same way, so golden
+// marching fixtures can be made for rays given on the host.  One thread per ray, slots by ray
+// order: the caller passes per-ray output offsets (max 1024 samples per ray).
+// ---------------------------------------------------------------------------------------------
+namespace {
+__global__ void ref_march_given_rays_kernel(uint32_t n, const float* __restrict__ rays, const uint8_t* __restrict__ occupancy,
+                                            uint32_t* __restrict__ numsteps_out, float* __restrict__ coords_out) {
+    const uint32_t i = threadIdx.x + blockIdx.x * blockDim.x;
+    if (i >= n) return;
+    numsteps_out[i] = 0u;
+    const float* r                        = rays + static_cast<uint64_t>(i) * 6u;
+    const float3 ray_origin               = {r[0], r[1], r[2]};
+    const float3 ray_direction_normalized = {r[3], r[4], r[5]};
+    float tmin                            = 0.0f;
+    if (!ref::intersect_unit_aabb(ray_origin, ray_direction_normalized, tmin)) return;
+    constexpr float dt         = ref::MIN_CONE_STEPSIZE;
+    const float start_t        = tmin + 0.5f * dt;
+    const float3 inv_direction = {1.0f / ray_direction_normalized.x, 1.0f / ray_direction_normalized.y, 1.0f / ray_direction_normalized.z};
+    std::uint32_t numsteps     = 0u;
+    float t                    = start_t;
+    float3 pos                 = {};
+    float* out                 = coords_out + static_cast<uint64_t>(i) * ref::NERF_STEPS * 7u;
+    const float3 warped_direction = {(ray_direction_normalized.x + 1.0f) * 0.5f, (ray_direction_normalized.y + 1.0f) * 0.5f,
+                                     (ray_direction_normalized.z + 1.0f) * 0.5f};
+    while (numsteps < ref::NERF_STEPS) {
+        pos = {ray_origin.x + ray_direction_normalized.x * t, ray_origin.y + ray_direction_normalized.y * t, ray_origin.z + ray_direction_normalized.z * t};
+        if (!ref::unit_aabb_contains(pos)) break;
+        if (ref::is_density_grid_occupied(pos, occupancy)) {
+            float* coord = out + static_cast<uint64_t>(numsteps) * 7u;
+            coord[0] = pos.x, coord[1] = pos.y, coord[2] = pos.z, coord[3] = dt;
+            coord[4] = warped_direction.x, coord[5] = warped_direction.y, coord[6] = warped_direction.z;
+            ++numsteps;
+            t += dt;
+        } else {
+            t = ref::advance_to_next_density_voxel(t, pos, ray_direction_normalized, inv_direction);
+        }
+    }
+    numsteps_out[i] = numsteps;
+}
+}  // namespace
+
+extern "C" int ref_march_given_rays(uint32_t n, const float* rays, const uint8_t* occupancy, uint32_t* numsteps, float* coords) {
+    ref_march_given_rays_kernel<<<(n + 127u) / 128u, 128u>>>(n, rays, occupancy, numsteps, coords);
+    return status_of(cudaDeviceSynchronize());
+}

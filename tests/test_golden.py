@@ -1,0 +1,55 @@
+"""CPU tier: the oracle against golden fixtures produced by the reference's own kernels on a B200
+(tests/golden/make_golden.py).  No GPU needed."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import workloads
+from conftest import GOLDEN
+
+
+def load(name):
+    p = GOLDEN / name
+    if not p.exists():
+        pytest.skip(f"{name} not generated yet")
+    return np.load(p)
+
+
+def test_pcg32_matches_reference(oracle):
+    g = load("pcg32_ref.npz")
+    u, f = oracle.pcg32(int(g["seed"]), int(g["seq"]), int(g["advance"]), len(g["uint"]))
+    assert (u == g["uint"]).all() and (f == g["float"]).all()
+
+
+def test_encode_forward_reference_mode_bit_exact(oracle):
+    g = load("encode_forward_ref.npz")
+    coords, table, _ = workloads.encode_inputs(int(g["n"]), int(g["n_grid"]), 8, 4, seed=int(g["seed"]), coord_stride=7)
+    out = oracle.encode_forward(oracle.grid_layout(8, 4, 19, 16, 1.0), coords, table, 4, mode=1)
+    assert (out.view(np.uint16) == g["out"]).all()
+
+
+def test_sh_within_one_ulp_of_reference(oracle):
+    g = load("sh_ref.npz")
+    _, coords, _ = workloads.mlp_inputs(int(g["n"]), seed=int(g["seed"]))
+    a = oracle.sh_encode(coords).view(np.int16).astype(np.int32)
+    b = g["out"].view(np.int16).astype(np.int32)
+    assert np.abs(a - b).max() <= 1
+
+
+def test_march_bit_exact_vs_reference(oracle):
+    g = load("march_ref.npz")
+    vals = workloads.blob_grid_values(workloads.gaussian_blob_density())
+    bits = np.packbits((vals > 0.01).reshape(-1, 8), axis=1, bitorder="little").reshape(-1)
+    rays = workloads.march_rays_config2(int(g["n"]), seed=int(g["seed"]))
+    ns, coords, total = oracle.march_rays(rays, bits)
+    assert (ns[:, 0] == g["numsteps"]).all()
+    assert total == int(g["numsteps"].sum())
+    assert coords[:total].tobytes() == g["coords"].tobytes()
+
+
+def test_grid_samples_bit_exact_vs_reference(oracle):
+    g = load("grid_samples_ref.npz")
+    vals = workloads.blob_grid_values(workloads.gaussian_blob_density())
+    c, i = oracle.grid_samples(int(g["n_uniform"]), int(g["n_nonuniform"]), int(g["ema_step"]), vals)
+    assert c.tobytes() == g["coords"].tobytes() and (i == g["indices"]).all()
