@@ -4,16 +4,24 @@
 // Replaces K10-K13 (ngp.train.cu:669-874) and the host wrappers
 // compute_training_loss_and_compact_samples / pad_compacted_training_batch (1932-1956).
 //
-// The reference reserves compacted slots with a global atomic (ray order nondeterministic).
-// Here pass 1 composites each ray and counts the samples it keeps (front-to-back until the
-// transmittance drops below 1e-4), one CTA scans the per-CTA totals, and pass 2 writes each
-// ray's compacted samples, network-output gradients and loss at its prefix offset.
+// The reference reserves compacted slots with a global atomic (ray order nondeterministic) and
+// composites each ray in one thread.  Here one warp composites one ray, 32 samples at a time:
+// each lane recomputes its transmittance and colour prefix by a sequential loop over the
+// earlier lanes' values (shuffled), in the same order as a one-thread loop, so results are
+// identical to the sequential compositing while a ray's samples are processed in parallel.
+// Pass 1 counts the samples each ray keeps (front-to-back until the transmittance drops below
+// 1e-4), one CTA scans the per-CTA totals, and pass 2 writes each ray's compacted samples,
+// network-output gradients and loss at its prefix offset.
+#include <mutex>
+
 #include "sampler.cuh"
 
 namespace ngp {
 namespace {
 
-constexpr uint32_t kThreads = 128u;
+constexpr uint32_t kRaysPerCta = 8u;
+constexpr uint32_t kCtaThreads = kRaysPerCta * 32u;
+constexpr uint32_t kThreads    = 128u;  // evaluation compositing (one thread per pixel)
 
 struct LossParams {
     uint32_t rays_per_batch;        // rays of the step (scales the loss and its gradient)
@@ -67,27 +75,55 @@ __device__ __forceinline__ void load_output(const __half* o, float& r, float& g,
     r = rg.x, g = rg.y, b = bd.x, d = bd.y;
 }
 
+// Transmittance before this lane's sample: T * q_0 * q_1 * ... * q_{lane-1}, multiplied in lane
+// order exactly as the sequential loop does.
+__device__ __forceinline__ float prefix_transmittance(float T, float q) {
+    const uint32_t lane = threadIdx.x & 31u;
+    float Tb            = T;
+#pragma unroll
+    for (uint32_t k = 0; k < 31; ++k) {
+        const float qk = __shfl_sync(0xFFFFFFFFu, q, k);
+        if (k < lane) Tb *= qk;
+    }
+    return Tb;
+}
+
 // Pass 1 (first loop of K11, ngp.train.cu:751-802): composite, count the kept samples.
-__global__ void __launch_bounds__(kThreads) loss_pass1_kernel(const __grid_constant__ LossParams p) {
-    const uint32_t n = loss_rays(p);
-    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
-    uint32_t kept    = 0;
+__global__ void __launch_bounds__(kCtaThreads) loss_pass1_kernel(const __grid_constant__ LossParams p) {
+    __shared__ uint32_t s_kept[kRaysPerCta];
+    const uint32_t n    = loss_rays(p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    uint32_t kept       = 0;
     if (i < n) {
         const uint32_t steps = p.numsteps[2u * i], base = p.numsteps[2u * i + 1u];
         const __half* out    = p.network_output + static_cast<uint64_t>(base) * 16u;
         const float* c       = p.coords + static_cast<uint64_t>(base) * 7u;
         float T              = 1.0f;
         float3 rgb           = {0.0f, 0.0f, 0.0f};
-        for (; kept < steps; ++kept) {
-            if (T < kTransmittanceEps) break;
-            float r, g, b, d;
-            load_output(out + static_cast<uint64_t>(kept) * 16u, r, g, b, d);
-            const float alpha  = 1.0f - __expf(-expf(d) * c[static_cast<uint64_t>(kept) * 7u + 3u]);
-            const float weight = alpha * T;
-            rgb.x              = __fmaf_rn(weight, sigmoidf_(r), rgb.x);
-            rgb.y              = __fmaf_rn(weight, sigmoidf_(g), rgb.y);
-            rgb.z              = __fmaf_rn(weight, sigmoidf_(b), rgb.z);
-            T *= 1.0f - alpha;
+        for (uint32_t c0 = 0; c0 < steps; c0 += 32u) {
+            const uint32_t j = c0 + lane;
+            const bool valid = j < steps;
+            float r = 0.f, g = 0.f, b = 0.f, d = 0.f, dt = 0.f;
+            if (valid) {
+                load_output(out + static_cast<uint64_t>(j) * 16u, r, g, b, d);
+                dt = c[static_cast<uint64_t>(j) * 7u + 3u];
+            }
+            const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
+            const float3 col  = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
+            const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+            const bool keep   = valid && !(Tb < kTransmittanceEps);
+            const uint32_t nk = __popc(__ballot_sync(0xFFFFFFFFu, keep));
+            const float w     = alpha * Tb;
+            for (uint32_t k = 0; k < nk; ++k) {
+                const float wk = __shfl_sync(0xFFFFFFFFu, w, k);
+                rgb.x          = __fmaf_rn(wk, __shfl_sync(0xFFFFFFFFu, col.x, k), rgb.x);
+                rgb.y          = __fmaf_rn(wk, __shfl_sync(0xFFFFFFFFu, col.y, k), rgb.y);
+                rgb.z          = __fmaf_rn(wk, __shfl_sync(0xFFFFFFFFu, col.z, k), rgb.z);
+            }
+            if (nk > 0) T = __shfl_sync(0xFFFFFFFFu, Tb * (1.0f - alpha), nk - 1u);
+            kept += nk;
+            if (nk < min(32u, steps - c0)) break;
         }
         if (kept == steps) {
             float3 bg, target;
@@ -96,28 +132,41 @@ __global__ void __launch_bounds__(kThreads) loss_pass1_kernel(const __grid_const
             rgb.y = __fmaf_rn(T, bg.y, rgb.y);
             rgb.z = __fmaf_rn(T, bg.z, rgb.z);
         }
-        p.ray_rgb[i] = make_float4(rgb.x, rgb.y, rgb.z, 0.0f);
-        p.kept[i]    = kept;
+        if (lane == 0) {
+            p.ray_rgb[i] = make_float4(rgb.x, rgb.y, rgb.z, 0.0f);
+            p.kept[i]    = kept;
+        }
     }
-    uint32_t total;
-    block_exclusive_scan(kept, total);
-    if (threadIdx.x == 0) p.block_totals[blockIdx.x] = total;
+    if (lane == 0) s_kept[warp] = kept;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t total = 0;
+        for (uint32_t w = 0; w < kRaysPerCta; ++w) total += s_kept[w];
+        p.block_totals[blockIdx.x] = total;
+    }
 }
 
 // Pass 2 (rest of K11, ngp.train.cu:804-859): clamp to the batch, copy the kept samples, write
 // dL/d(raw rgb) and dL/d(raw density) per sample, scaled by 128 / rays_per_batch.
-__global__ void __launch_bounds__(kThreads) loss_pass2_kernel(const __grid_constant__ LossParams p) {
-    const uint32_t n = loss_rays(p);
-    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
-    const uint32_t k = i < n ? p.kept[i] : 0u;
-    uint32_t total;
-    const uint32_t cbase = p.block_totals[blockIdx.x] + block_exclusive_scan(k, total);
+__global__ void __launch_bounds__(kCtaThreads) loss_pass2_kernel(const __grid_constant__ LossParams p) {
+    const uint32_t n    = loss_rays(p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    uint32_t cbase      = p.block_totals[blockIdx.x];
+    for (uint32_t w = 0; w < warp; ++w) {
+        const uint32_t q = blockIdx.x * kRaysPerCta + w;
+        cbase += q < n ? p.kept[q] : 0u;
+    }
     if (i >= n) return;
+    const uint32_t k         = p.kept[i];
     const uint32_t remaining = cbase < p.batch ? p.batch - cbase : 0u;
     const uint32_t cn        = k < remaining ? k : remaining;
     const uint32_t base      = p.numsteps[2u * i + 1u];
-    p.numsteps[2u * i]       = cn;
-    p.numsteps[2u * i + 1u]  = cbase;
+    __syncwarp();
+    if (lane == 0) {
+        p.numsteps[2u * i]      = cn;
+        p.numsteps[2u * i + 1u] = cbase;
+    }
     if (cn == 0) return;
 
     float3 bg, target;
@@ -126,7 +175,7 @@ __global__ void __launch_bounds__(kThreads) loss_pass2_kernel(const __grid_const
     const float3 rgb  = {rr.x, rr.y, rr.z};
     const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
     const float3 grad = {2.0f * diff.x, 2.0f * diff.y, 2.0f * diff.z};
-    if (p.loss_output != nullptr)
+    if (p.loss_output != nullptr && lane == 0)
         p.loss_output[i] = __fmaf_rn(diff.z, diff.z, __fmaf_rn(diff.x, diff.x, diff.y * diff.y)) / (3.0f * static_cast<float>(p.rays_per_batch));
     const float scale   = kLossScale / static_cast<float>(p.rays_per_batch);
     const float* ray    = p.rays + static_cast<uint64_t>(i) * 6u;
@@ -137,34 +186,55 @@ __global__ void __launch_bounds__(kThreads) loss_pass2_kernel(const __grid_const
     __half* dout        = p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u;
     float T             = 1.0f;
     float3 acc          = {0.0f, 0.0f, 0.0f};
-    for (uint32_t j = 0; j < cn; ++j) {
-        const float* c = cin + static_cast<uint64_t>(j) * 7u;
-        float* co      = cout + static_cast<uint64_t>(j) * 7u;
+    for (uint32_t c0 = 0; c0 < cn; c0 += 32u) {
+        const uint32_t j = c0 + lane;
+        const bool valid = j < cn;
+        float cv[7]      = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float mr = 0.f, mg = 0.f, mb = 0.f, md = 0.f;
+        if (valid) {
+            const float* c = cin + static_cast<uint64_t>(j) * 7u;
+            float* co      = cout + static_cast<uint64_t>(j) * 7u;
 #pragma unroll
-        for (int q = 0; q < 7; ++q) co[q] = c[q];
-        const float depth = norm3df(c[0] - origin.x, c[1] - origin.y, c[2] - origin.z);
-        const float dt    = c[3];
-        float mr, mg, mb, md;
-        load_output(out + static_cast<uint64_t>(j) * 16u, mr, mg, mb, md);
+            for (int q = 0; q < 7; ++q) co[q] = cv[q] = c[q];
+            load_output(out + static_cast<uint64_t>(j) * 16u, mr, mg, mb, md);
+        }
+        const float dt     = cv[3];
         const float3 col   = {sigmoidf_(mr), sigmoidf_(mg), sigmoidf_(mb)};
-        const float alpha  = 1.0f - __expf(-expf(md) * dt);
-        const float weight = alpha * T;
-        acc.x              = __fmaf_rn(weight, col.x, acc.x);
-        acc.y              = __fmaf_rn(weight, col.y, acc.y);
-        acc.z              = __fmaf_rn(weight, col.z, acc.z);
-        T *= 1.0f - alpha;
-        const float3 suffix = {rgb.x - acc.x, rgb.y - acc.y, rgb.z - acc.z};
-        const float g0      = scale * (weight * grad.x * (col.x * (1.0f - col.x)));
-        const float g1      = scale * (weight * grad.y * (col.y * (1.0f - col.y)));
-        const float g2      = scale * (weight * grad.z * (col.z * (1.0f - col.z)));
-        const float dd      = expf(fminf(fmaxf(md, -15.0f), 15.0f));
-        const float sum = __fmaf_rn(grad.z, __fmaf_rn(T, col.z, -suffix.z),
-                                    __fmaf_rn(grad.x, __fmaf_rn(T, col.x, -suffix.x), grad.y * __fmaf_rn(T, col.y, -suffix.y)));
-        const float g3  = __fmaf_rn(scale, dd * (dt * sum), (md > -10.0f && depth < 0.1f) ? 1e-4f : 0.0f);
-        uint4* d        = reinterpret_cast<uint4*>(dout + static_cast<uint64_t>(j) * 16u);
-        __half2 h01 = __floats2half2_rn(g0, g1), h23 = __floats2half2_rn(g2, g3);
-        d[0]        = make_uint4(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23), 0u, 0u);
-        d[1]        = make_uint4(0u, 0u, 0u, 0u);
+        const float alpha  = valid ? 1.0f - __expf(-expf(md) * dt) : 0.0f;
+        const float Tb     = prefix_transmittance(T, 1.0f - alpha);
+        const float weight = alpha * Tb;
+        // colour prefix including this sample, accumulated in sample order
+        float3 a = acc;
+        for (uint32_t q = 0; q < 32u; ++q) {
+            const float wq = __shfl_sync(0xFFFFFFFFu, weight, q);
+            const float cx = __shfl_sync(0xFFFFFFFFu, col.x, q), cy = __shfl_sync(0xFFFFFFFFu, col.y, q), cz = __shfl_sync(0xFFFFFFFFu, col.z, q);
+            if (q <= lane) {
+                a.x = __fmaf_rn(wq, cx, a.x);
+                a.y = __fmaf_rn(wq, cy, a.y);
+                a.z = __fmaf_rn(wq, cz, a.z);
+            }
+        }
+        const float Ta = Tb * (1.0f - alpha);
+        if (valid) {
+            const float depth   = norm3df(cv[0] - origin.x, cv[1] - origin.y, cv[2] - origin.z);
+            const float3 suffix = {rgb.x - a.x, rgb.y - a.y, rgb.z - a.z};
+            const float g0      = scale * (weight * grad.x * (col.x * (1.0f - col.x)));
+            const float g1      = scale * (weight * grad.y * (col.y * (1.0f - col.y)));
+            const float g2      = scale * (weight * grad.z * (col.z * (1.0f - col.z)));
+            const float dd      = expf(fminf(fmaxf(md, -15.0f), 15.0f));
+            const float sum = __fmaf_rn(grad.z, __fmaf_rn(Ta, col.z, -suffix.z),
+                                        __fmaf_rn(grad.x, __fmaf_rn(Ta, col.x, -suffix.x), grad.y * __fmaf_rn(Ta, col.y, -suffix.y)));
+            const float g3 = __fmaf_rn(scale, dd * (dt * sum), (md > -10.0f && depth < 0.1f) ? 1e-4f : 0.0f);
+            uint4* d       = reinterpret_cast<uint4*>(dout + static_cast<uint64_t>(j) * 16u);
+            __half2 h01 = __floats2half2_rn(g0, g1), h23 = __floats2half2_rn(g2, g3);
+            d[0]        = make_uint4(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23), 0u, 0u);
+            d[1]        = make_uint4(0u, 0u, 0u, 0u);
+        }
+        const uint32_t last = min(31u, cn - 1u - c0);
+        T                   = __shfl_sync(0xFFFFFFFFu, Ta, last);
+        acc.x               = __shfl_sync(0xFFFFFFFFu, a.x, last);
+        acc.y               = __shfl_sync(0xFFFFFFFFu, a.y, last);
+        acc.z               = __shfl_sync(0xFFFFFFFFu, a.z, last);
     }
 }
 
@@ -257,15 +327,16 @@ __global__ void __launch_bounds__(kThreads) eval_composite_kernel(uint32_t n_pix
     }
 }
 
+constexpr size_t loss_scratch_size(uint32_t max_rays) {
+    return static_cast<size_t>(max_rays) * 20u + ((max_rays + kRaysPerCta - 1u) / kRaysPerCta) * 4u + 256u;
+}
+
 }  // namespace
 }  // namespace ngp
 
 using namespace ngp;
 
-extern "C" uint32_t ngp_loss_scratch_bytes(uint32_t max_rays) {
-    const uint32_t blocks = (max_rays + kThreads - 1) / kThreads;
-    return max_rays * (16u + 4u) + blocks * 4u + 256u;
-}
+extern "C" uint32_t ngp_loss_scratch_bytes(uint32_t max_rays) { return static_cast<uint32_t>(loss_scratch_size(max_rays)); }
 
 extern "C" int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
                                              uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
@@ -278,10 +349,10 @@ extern "C" int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t s
         coords == nullptr || compacted_coords == nullptr || dloss_doutput == nullptr || scratch == nullptr || frame_count == 0 || width == 0 ||
         height == 0)
         return fail(NGP_ERR_INVALID, "training loss: invalid input");
-    if (scratch_bytes < ngp_loss_scratch_bytes(rays_per_batch)) return fail(NGP_ERR_INVALID, "training loss: scratch too small");
+    if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "training loss: scratch too small");
     if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "training loss: scratch must be 16-byte aligned");
     const cudaStream_t s  = as_stream(stream);
-    const uint32_t blocks = (rays_per_batch + kThreads - 1) / kThreads;
+    const uint32_t blocks = (rays_per_batch + kRaysPerCta - 1) / kRaysPerCta;
     unsigned char* sc     = static_cast<unsigned char*>(scratch);
     LossParams p{};
     p.rays_per_batch = rays_per_batch;
@@ -304,11 +375,11 @@ extern "C" int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t s
     p.block_totals   = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(rays_per_batch) * 20u);
     p.batch          = kNetworkBatch;
     if (loss_values != nullptr) NGP_TRY(check_cuda(cudaMemsetAsync(loss_values, 0, sizeof(float) * rays_per_batch, s), "training loss: clear"));
-    loss_pass1_kernel<<<blocks, kThreads, 0, s>>>(p);
+    loss_pass1_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
     NGP_TRY(check_launch("loss_pass1_kernel"));
     scan_kept_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, compacted_counter, kNetworkBatch);
     NGP_TRY(check_launch("scan_kept_kernel"));
-    loss_pass2_kernel<<<blocks, kThreads, 0, s>>>(p);
+    loss_pass2_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
     return check_launch("loss_pass2_kernel");
 }
 
@@ -342,12 +413,10 @@ extern "C" int ngp_eval_composite(uint32_t n_pixels, uint32_t pixel_offset, uint
 // scratch from one statically sized device array that every GPU loading the library holds until
 // the process exits (kNoAllocScratchBytes, about 5 MiB: room for 2^18 rays).
 // ---------------------------------------------------------------------------------------------
-#include <mutex>
-
 namespace {
 
-constexpr uint32_t kNoAllocMaxRays      = 1u << 18;
-constexpr size_t kNoAllocScratchBytes   = static_cast<size_t>(kNoAllocMaxRays) * 20u + (kNoAllocMaxRays / 128u) * 4u + 256u;
+constexpr uint32_t kNoAllocMaxRays    = 1u << 18;
+constexpr size_t kNoAllocScratchBytes = loss_scratch_size(kNoAllocMaxRays);
 static __device__ __align__(256) unsigned char g_noalloc_loss_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;

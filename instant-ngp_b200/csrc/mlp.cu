@@ -564,8 +564,22 @@ __global__ void sh_encode_kernel(uint32_t n, const float* __restrict__ coords, u
 }
 
 int mlp_grid(int smem_bytes, const void* kernel, uint32_t n_tiles, uint32_t tmem_cols) {
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem_bytes) != cudaSuccess || per_sm < 1) per_sm = 1;
+    // CTAs per SM from shared memory (1 KB per CTA is reserved by the hardware), registers and
+    // TMEM columns (512 per SM).
+    static int smem_per_sm = [] {
+        int device = 0, v = 0;
+        cudaGetDevice(&device);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
+        return v > 0 ? v : 233472;
+    }();
+    cudaFuncAttributes attr{};
+    cudaFuncGetAttributes(&attr, kernel);
+    const int per_cta_smem = smem_bytes + static_cast<int>(attr.sharedSizeBytes) + 1024;
+    int per_sm            = smem_per_sm / per_cta_smem;
+    const int regs        = attr.numRegs > 0 ? attr.numRegs : 64;
+    const int by_regs     = 65536 / (regs * static_cast<int>(kThreads));
+    per_sm                = per_sm < by_regs ? per_sm : by_regs;
+    if (per_sm < 1) per_sm = 1;
     const int by_tmem = static_cast<int>(512u / tmem_cols);
     per_sm            = per_sm < by_tmem ? per_sm : by_tmem;
     const uint32_t g  = static_cast<uint32_t>(per_sm * sm_count());
@@ -575,11 +589,8 @@ int mlp_grid(int smem_bytes, const void* kernel, uint32_t n_tiles, uint32_t tmem
 }  // namespace
 
 uint32_t mlp_backward_max_ctas() {
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mlp_backward_kernel, kThreads, kBwdSmem);
-    if (per_sm < 1) per_sm = 1;
-    const int by_tmem = static_cast<int>(512u / kBwdTmemCols);
-    return static_cast<uint32_t>((per_sm < by_tmem ? per_sm : by_tmem) * sm_count());
+    // upper bound of the backward grid: TMEM allows 512 / 256 = 2 CTAs per SM
+    return static_cast<uint32_t>((512u / kBwdTmemCols) * static_cast<uint32_t>(sm_count()));
 }
 
 }  // namespace ngp

@@ -211,13 +211,20 @@ __device__ __forceinline__ bool setup_ray(const MarchParams& p, uint32_t i, uint
     return true;
 }
 
-__global__ void __launch_bounds__(kThreads) march_count_kernel(const __grid_constant__ MarchParams p) {
-    const uint32_t n = march_ray_count(p);
-    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
-    uint32_t steps   = 0;
-    if (i < n) {
-        TrainRay r{};
-        if (setup_ray(p, i, n, r)) steps = march_count(r.origin, r.dir, r.start_t, p.bits);
+// A group of kMarchGroup lanes per ray, kRaysPerCta rays per CTA.  Count pass: per-ray step
+// counts and per-CTA totals.
+constexpr uint32_t kCtaThreads = 256u;
+constexpr uint32_t kRaysPerCta = kCtaThreads / kMarchGroup;
+
+__global__ void __launch_bounds__(kCtaThreads) march_count_kernel(const __grid_constant__ MarchParams p) {
+    __shared__ uint32_t s_steps[kRaysPerCta];
+    const uint32_t n    = march_ray_count(p);
+    const uint32_t slot = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
+    TrainRay r{};
+    const bool active    = i < n && setup_ray(p, i, n, r);
+    const uint32_t steps = group_march_count(r.origin, r.dir, r.start_t, active, p.bits);
+    if (i < n && g == 0) {
         p.numsteps[2u * i] = steps;
         if (p.rays_out != nullptr) {
             float* o = p.rays_out + static_cast<uint64_t>(i) * 6u;
@@ -225,9 +232,15 @@ __global__ void __launch_bounds__(kThreads) march_count_kernel(const __grid_cons
         }
         if (p.ray_indices != nullptr) p.ray_indices[i] = i;
     }
-    uint32_t total;
-    block_exclusive_scan(steps, total);
-    if (threadIdx.x == 0) p.block_totals[blockIdx.x] = total;
+    if (g == 0) s_steps[slot] = steps;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        uint32_t total = 0;
+        for (uint32_t w = threadIdx.x; w < kRaysPerCta; w += 32) total += s_steps[w];
+#pragma unroll
+        for (uint32_t o = 16; o > 0; o >>= 1) total += __shfl_down_sync(0xFFFFFFFFu, total, o);
+        if (threadIdx.x == 0) p.block_totals[blockIdx.x] = total;
+    }
 }
 
 // One CTA: exclusive scan of the per-CTA totals in place; writes the grand total.
@@ -248,21 +261,27 @@ __global__ void __launch_bounds__(1024) scan_totals_kernel(uint32_t* __restrict_
     }
 }
 
-__global__ void __launch_bounds__(kThreads) march_write_kernel(const __grid_constant__ MarchParams p) {
-    const uint32_t n     = march_ray_count(p);
-    const uint32_t i     = blockIdx.x * kThreads + threadIdx.x;
+__global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_constant__ MarchParams p) {
+    __shared__ uint32_t s_base[kRaysPerCta];
+    const uint32_t n    = march_ray_count(p);
+    const uint32_t slot = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
+    // this ray's first sample: CTA base + counts of the CTA's earlier rays (exclusive scan)
     const uint32_t steps = i < n ? p.numsteps[2u * i] : 0u;
     uint32_t total;
-    const uint32_t base = p.block_totals[blockIdx.x] + block_exclusive_scan(steps, total);
-    if (i >= n) return;
+    const uint32_t ex = block_exclusive_scan(g == 0 ? steps : 0u, total);
+    if (g == 0) s_base[slot] = ex;
+    __syncthreads();
+    const uint32_t base = p.block_totals[blockIdx.x] + s_base[slot];
     // rays whose samples would cross the sample limit are dropped (ngp.train.cu:537-538)
-    const uint32_t kept     = base + steps <= p.sample_limit ? steps : 0u;
-    p.numsteps[2u * i]      = kept;
-    p.numsteps[2u * i + 1u] = kept ? base : 0u;
-    if (kept == 0) return;
+    const uint32_t kept = (i < n && base + steps <= p.sample_limit) ? steps : 0u;
+    if (i < n && g == 0) {
+        p.numsteps[2u * i]      = kept;
+        p.numsteps[2u * i + 1u] = kept ? base : 0u;
+    }
     TrainRay r{};
-    setup_ray(p, i, n, r);
-    march_write(r.origin, r.dir, r.start_t, kept, p.bits, p.coords + static_cast<uint64_t>(base) * 7u);
+    if (kept > 0) setup_ray(p, i, n, r);
+    group_march_write(r.origin, r.dir, r.start_t, kept, p.bits, p.coords + static_cast<uint64_t>(base) * 7u);
 }
 
 // Evaluation pixel rays (ngp.train.cu:587-614): pixel centre through the pinhole camera,
@@ -288,12 +307,12 @@ __global__ void eval_rays_kernel(const CameraSet cam, uint32_t image, uint32_t p
 }
 
 int launch_march(const MarchParams& p, cudaStream_t s) {
-    const uint32_t blocks = (p.n_rays + kThreads - 1) / kThreads;
-    march_count_kernel<<<blocks, kThreads, 0, s>>>(p);
+    const uint32_t blocks = (p.n_rays + kRaysPerCta - 1) / kRaysPerCta;
+    march_count_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
     NGP_TRY(check_launch("march_count_kernel"));
     scan_totals_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, p.n_rays_dev, p.n_rays, p.sample_counter, p.ray_counter);
     NGP_TRY(check_launch("scan_totals_kernel"));
-    march_write_kernel<<<blocks, kThreads, 0, s>>>(p);
+    march_write_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
     return check_launch("march_write_kernel");
 }
 
@@ -309,7 +328,7 @@ bool camera_ok(const float* camera, uint32_t frame_count, uint32_t width, uint32
 
 using namespace ngp;
 
-extern "C" uint32_t ngp_march_block_totals(uint32_t max_rays) { return (max_rays + kThreads - 1) / kThreads; }
+extern "C" uint32_t ngp_march_block_totals(uint32_t max_rays) { return (max_rays + kRaysPerCta - 1) / kRaysPerCta; }
 
 extern "C" int ngp_density_grid_mark_untrained(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x,
                                                float focal_y, float principal_x, float principal_y, float* values, void* stream) {

@@ -211,3 +211,178 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t& t
 }
 
 }  // namespace ngp
+
+namespace ngp {
+
+// ---- group-cooperative marching --------------------------------------------------------------
+// A group of G adjacent lanes marches one ray (32 / G rays per warp).  From the current t, lane g
+// of the group takes the g-th next cone step t_g = ((t + dt) + dt) ... (g sequential additions,
+// so t_g equals the sequential march's value bit for bit) and tests it; the lanes before the
+// first unoccupied or outside position are exactly the samples the sequential loop would emit,
+// after which lane f's position decides the skip (or the end).  Results are identical to
+// march_count / march_write, with up to G samples resolved per round; skips through empty space
+// stay sequential, so G trades parallelism per ray against total work.
+#ifndef NGP_MARCH_GROUP
+#define NGP_MARCH_GROUP 4
+#endif
+constexpr uint32_t kMarchGroup = NGP_MARCH_GROUP;
+
+struct GroupMarch {
+    float3 o, d, inv;
+    float t;
+    uint32_t n;
+    bool done;
+};
+
+__device__ __forceinline__ void group_march_begin(GroupMarch& m, float3 o, float3 d, float start_t, bool active) {
+    m.o = o, m.d = d, m.inv = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z}, m.t = start_t, m.n = 0, m.done = !active;
+}
+
+// One round for every group of the warp (all 32 lanes call it together).  Returns the samples
+// this group emitted (uniform within the group); `emit` marks this lane's position as one.
+__device__ __forceinline__ uint32_t group_march_round(GroupMarch& m, const uint8_t* __restrict__ bits, uint32_t limit, float3& my_pos, bool& emit) {
+    constexpr uint32_t G    = kMarchGroup;
+    const uint32_t lane     = threadIdx.x & 31u;
+    const uint32_t g        = lane % G;
+    const uint32_t group_lo = lane - g;
+    float tk                = m.t;
+    for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
+    my_pos              = ray_point(m.o, m.d, tk);
+    const bool ins      = !m.done && inside_unit_cube(my_pos);
+    const bool oc       = ins && occupied(my_pos, bits);
+    const uint32_t stop = (__ballot_sync(0xFFFFFFFFu, !oc) >> group_lo) & ((1u << G) - 1u);
+    const uint32_t f    = stop ? static_cast<uint32_t>(__ffs(stop)) - 1u : G;
+    const uint32_t room = limit - m.n;
+    const uint32_t k    = m.done ? 0u : (f < room ? f : room);
+    emit                = g < k;
+    const float t_last  = __shfl_sync(0xFFFFFFFFu, tk, group_lo + G - 1u);
+    const bool f_inside = __shfl_sync(0xFFFFFFFFu, ins, group_lo + (f < G ? f : 0u));
+    const float next    = skip_empty_voxel(tk, my_pos, m.d, m.inv);
+    const float f_next  = __shfl_sync(0xFFFFFFFFu, next, group_lo + (f < G ? f : 0u));
+    if (m.done) return 0u;
+    m.n += k;
+    if (m.n >= limit) {
+        m.done = true;
+    } else if (f == G) {
+        m.t = t_last + kConeStep;
+    } else if (!f_inside) {
+        m.done = true;
+    } else {
+        m.t = f_next;
+    }
+    return k;
+}
+
+// Sample count of this group's ray (all lanes of the warp call it; inactive groups pass active=false).
+__device__ __forceinline__ uint32_t group_march_count(float3 o, float3 d, float start_t, bool active, const uint8_t* __restrict__ bits) {
+    GroupMarch m;
+    group_march_begin(m, o, d, start_t, active);
+    while (__any_sync(0xFFFFFFFFu, !m.done)) {
+        float3 p;
+        bool e;
+        group_march_round(m, bits, kMarchSteps, p, e);
+    }
+    return m.n;
+}
+
+// Writes exactly `n` records (n = this ray's count) starting at `out`; n = 0 for inactive groups.
+__device__ __forceinline__ void group_march_write(float3 o, float3 d, float start_t, uint32_t n, const uint8_t* __restrict__ bits,
+                                                  float* __restrict__ out) {
+    const float3 w3     = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
+    const uint32_t g    = (threadIdx.x & 31u) % kMarchGroup;
+    GroupMarch m;
+    group_march_begin(m, o, d, start_t, n > 0);
+    while (__any_sync(0xFFFFFFFFu, !m.done)) {
+        float3 p;
+        bool e;
+        const uint32_t before = m.n;
+        group_march_round(m, bits, n, p, e);
+        if (e) {
+            float* c = out + static_cast<uint64_t>(before + g) * 7u;
+            c[0] = p.x, c[1] = p.y, c[2] = p.z, c[3] = kConeStep, c[4] = w3.x, c[5] = w3.y, c[6] = w3.z;
+        }
+    }
+}
+
+// ---- occupied runs ----------------------------------------------------------------------------
+// The count pass records each ray's runs of consecutive occupied cone steps (the t of the run's
+// first sample and its length).  The write pass then expands the runs with the same sequential
+// t additions instead of marching through empty space a second time; a ray with more than
+// kMaxRuns runs is marched again instead.
+constexpr uint32_t kMaxRuns      = 48u;
+constexpr uint32_t kRunsOverflow = 0xFFFFFFFFu;
+
+__device__ __forceinline__ uint32_t group_march_count_runs(float3 o, float3 d, float start_t, bool active, const uint8_t* __restrict__ bits,
+                                                           uint2* __restrict__ runs, uint32_t& n_runs) {
+    const uint32_t g = (threadIdx.x & 31u) % kMarchGroup;
+    GroupMarch m;
+    group_march_begin(m, o, d, start_t, active);
+    float run_t0   = 0.0f;
+    uint32_t run_n = 0;
+    n_runs         = 0;
+    while (__any_sync(0xFFFFFFFFu, !m.done)) {
+        const bool was_done = m.done;
+        const float t_round = m.t;
+        float3 p;
+        bool e;
+        const uint32_t k = group_march_round(m, bits, kMarchSteps, p, e);
+        if (was_done) continue;
+        if (k > 0) {
+            if (run_n == 0) run_t0 = t_round;
+            run_n += k;
+        }
+        const bool continues = k == kMarchGroup && !m.done;
+        if (!continues && run_n > 0) {
+            if (n_runs < kMaxRuns && g == 0) runs[n_runs] = make_uint2(__float_as_uint(run_t0), run_n);
+            ++n_runs;
+            run_n = 0;
+        }
+    }
+    if (n_runs > kMaxRuns) n_runs = kRunsOverflow;
+    return m.n;
+}
+
+// Expand this group's runs into `n` sample records at `out` (active = the ray's runs are valid).
+__device__ __forceinline__ void group_expand_runs(float3 d_unit, float3 o, const uint2* __restrict__ runs, uint32_t n_runs, uint32_t n,
+                                                  bool active, float* __restrict__ out) {
+    const float3 w3         = {(d_unit.x + 1.0f) * 0.5f, (d_unit.y + 1.0f) * 0.5f, (d_unit.z + 1.0f) * 0.5f};
+    const uint32_t lane     = threadIdx.x & 31u;
+    const uint32_t g        = lane % kMarchGroup;
+    const uint32_t group_lo = lane - g;
+    uint32_t r = 0, in_run = 0, written = 0, cnt = 0;
+    float t = 0.0f;
+    active  = active && n_runs > 0 && n > 0;
+    if (active) {
+        const uint2 run = runs[0];
+        t               = __uint_as_float(run.x);
+        cnt             = run.y;
+    }
+    while (__any_sync(0xFFFFFFFFu, active)) {
+        float tk = t;
+        for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
+        const float t_last = __shfl_sync(0xFFFFFFFFu, tk, group_lo + kMarchGroup - 1u);
+        if (!active) continue;
+        const uint32_t adv = min(min(kMarchGroup, cnt - in_run), n - written);
+        if (g < adv) {
+            const float3 p = ray_point(o, d_unit, tk);
+            float* c       = out + static_cast<uint64_t>(written + g) * 7u;
+            c[0] = p.x, c[1] = p.y, c[2] = p.z, c[3] = kConeStep, c[4] = w3.x, c[5] = w3.y, c[6] = w3.z;
+        }
+        written += adv;
+        in_run += adv;
+        t = t_last + kConeStep;
+        if (in_run == cnt) {
+            ++r;
+            in_run = 0;
+            if (r == n_runs || written >= n) {
+                active = false;
+            } else {
+                const uint2 run = runs[r];
+                t               = __uint_as_float(run.x);
+                cnt             = run.y;
+            }
+        }
+    }
+}
+
+}  // namespace ngp

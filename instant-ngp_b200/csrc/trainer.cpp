@@ -396,7 +396,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->rays, static_cast<size_t>(kNetworkBatch) * 6u, "rays"));
         NGP_TRY(dalloc(t->ray_indices, kNetworkBatch, "ray indices"));
         NGP_TRY(dalloc(t->numsteps, static_cast<size_t>(kNetworkBatch) * 2u, "numsteps"));
-        NGP_TRY(dalloc(t->block_totals, kNetworkBatch / 128u + 1u, "block totals"));
+        NGP_TRY(dalloc(t->block_totals, ngp_march_block_totals(kNetworkBatch) + 1u, "block totals"));
         NGP_TRY(dalloc(t->counters, 8, "counters"));
         NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
         NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));
