@@ -168,9 +168,11 @@ NGP_API int ngp_density_grid_update(float* values, float* scratch, float decay, 
 /* ------------------------------------------------------------------------------------------
  * Ray marching (dt = sqrt(3)/1024, <= 1024 occupied steps, empty-space skipping).  Samples are
  * placed in ray order: numsteps[2i] = samples of ray i, numsteps[2i+1] = its first sample.
- * block_totals: ngp_march_block_totals(n_rays) uint32 of scratch.
+ * scratch: ngp_march_scratch_words(n_rays) uint32 of device memory, 8-byte aligned (per-CTA
+ * sample totals and each ray's runs of occupied steps, so that samples are written without
+ * marching the ray a second time).
  * ------------------------------------------------------------------------------------------ */
-NGP_API uint32_t ngp_march_block_totals(uint32_t max_rays);
+NGP_API uint64_t ngp_march_scratch_words(uint32_t max_rays);
 
 /* Training rays of `step` from the cameras (PCG32 pixels, start jitter) -> 7-float sample
  * records, rays [i][6] (origin, unnormalised direction), ray_indices (identity), numsteps,
@@ -181,14 +183,14 @@ NGP_API uint32_t ngp_march_block_totals(uint32_t max_rays);
 NGP_API int ngp_march_training_rays(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x,
                                     float focal_y, float principal_x, float principal_y, uint32_t step, uint32_t rays_per_batch,
                                     const uint32_t* rays_per_batch_dev, uint32_t sample_limit, const uint8_t* bitfield, float* coords,
-                                    float* rays, uint32_t* ray_indices, uint32_t* numsteps, uint32_t* block_totals, uint32_t* ray_counter,
+                                    float* rays, uint32_t* ray_indices, uint32_t* numsteps, uint32_t* scratch, uint32_t* ray_counter,
                                     uint32_t* sample_counter, void* stream);
 
 /* Explicit rays [n][6] (origin, unit direction) in the unit-cube frame; jitter != 0 starts at
  * tmin + U*dt with U the third draw of the training PCG32 stream of ray i at `step` (as
  * training rays do), else at tmin + dt/2 (the evaluation rule, ngp.train.cu:613). */
 NGP_API int ngp_march_rays(uint32_t n_rays, const float* rays, int jitter, uint32_t step, const uint8_t* bitfield, uint32_t sample_limit,
-                           float* coords, uint32_t* numsteps, uint32_t* block_totals, uint32_t* sample_counter, void* stream);
+                           float* coords, uint32_t* numsteps, uint32_t* scratch, uint32_t* sample_counter, void* stream);
 
 /* Pixel rays [n][6] (origin, unit direction) of pixels [pixel_offset, pixel_offset + n) of image
  * `image`.  Replaces the ray set-up of generate_evaluation_samples_kernel (ngp.train.cu:587-614). */

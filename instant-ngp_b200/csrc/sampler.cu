@@ -18,7 +18,6 @@
 namespace ngp {
 namespace {
 
-constexpr uint32_t kThreads = 128u;
 
 // ------------------------------------------------------------------------------------------
 // density grid
@@ -179,7 +178,8 @@ struct MarchParams {
     uint32_t n_rays;
     const uint8_t* bits;
     uint32_t* numsteps;           // [n][2] (count, base) per ray
-    uint32_t* block_totals;       // per-CTA sample totals
+    uint32_t* block_totals;       // per-CTA sample totals (scratch head)
+    uint2* runs;                  // [n][kMaxRuns] occupied runs per ray (scratch tail)
     float* rays_out;              // training: [n][6] origin + unnormalised direction
     uint32_t* ray_indices;        // training: identity
     float* coords;                // sample records
@@ -223,9 +223,11 @@ __global__ void __launch_bounds__(kCtaThreads) march_count_kernel(const __grid_c
     const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
     TrainRay r{};
     const bool active    = i < n && setup_ray(p, i, n, r);
-    const uint32_t steps = group_march_count(r.origin, r.dir, r.start_t, active, p.bits);
+    uint32_t n_runs;
+    const uint32_t steps = group_march_count_runs(r.origin, r.dir, r.start_t, active, p.bits, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs);
     if (i < n && g == 0) {
-        p.numsteps[2u * i] = steps;
+        p.numsteps[2u * i]      = steps;
+        p.numsteps[2u * i + 1u] = n_runs;  // read back by the write pass, then replaced by the base
         if (p.rays_out != nullptr) {
             float* o = p.rays_out + static_cast<uint64_t>(i) * 6u;
             o[0] = r.origin.x, o[1] = r.origin.y, o[2] = r.origin.z, o[3] = r.dir_raw.x, o[4] = r.dir_raw.y, o[5] = r.dir_raw.z;
@@ -267,7 +269,8 @@ __global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_c
     const uint32_t slot = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
     const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
     // this ray's first sample: CTA base + counts of the CTA's earlier rays (exclusive scan)
-    const uint32_t steps = i < n ? p.numsteps[2u * i] : 0u;
+    const uint32_t steps  = i < n ? p.numsteps[2u * i] : 0u;
+    const uint32_t n_runs = i < n ? p.numsteps[2u * i + 1u] : 0u;
     uint32_t total;
     const uint32_t ex = block_exclusive_scan(g == 0 ? steps : 0u, total);
     if (g == 0) s_base[slot] = ex;
@@ -281,7 +284,11 @@ __global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_c
     }
     TrainRay r{};
     if (kept > 0) setup_ray(p, i, n, r);
-    group_march_write(r.origin, r.dir, r.start_t, kept, p.bits, p.coords + static_cast<uint64_t>(base) * 7u);
+    float* out          = p.coords + static_cast<uint64_t>(base) * 7u;
+    const bool overflow = n_runs == kRunsOverflow;
+    // rays with few runs expand them; the rare ray with more runs than recorded marches again
+    group_expand_runs(r.dir, r.origin, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs, kept, !overflow, out);
+    group_march_write(r.origin, r.dir, r.start_t, overflow ? kept : 0u, p.bits, out);
 }
 
 // Evaluation pixel rays (ngp.train.cu:587-614): pixel centre through the pinhole camera,
@@ -306,8 +313,15 @@ __global__ void eval_rays_kernel(const CameraSet cam, uint32_t image, uint32_t p
     o[3] = d.x / len, o[4] = d.y / len, o[5] = d.z / len;
 }
 
-int launch_march(const MarchParams& p, cudaStream_t s) {
-    const uint32_t blocks = (p.n_rays + kRaysPerCta - 1) / kRaysPerCta;
+uint32_t march_blocks(uint32_t n_rays) { return (n_rays + kRaysPerCta - 1) / kRaysPerCta; }
+
+// Scratch: per-CTA totals, then (8-byte aligned) kMaxRuns run records per ray.
+uint64_t march_scratch_words(uint32_t n_rays) { return ((march_blocks(n_rays) + 1ull) & ~1ull) + 2ull * kMaxRuns * n_rays; }
+
+int launch_march(MarchParams p, uint32_t* scratch, cudaStream_t s) {
+    const uint32_t blocks = march_blocks(p.n_rays);
+    p.block_totals        = scratch;
+    p.runs                = reinterpret_cast<uint2*>(scratch + ((blocks + 1u) & ~1u));
     march_count_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
     NGP_TRY(check_launch("march_count_kernel"));
     scan_totals_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, p.n_rays_dev, p.n_rays, p.sample_counter, p.ray_counter);
@@ -328,7 +342,7 @@ bool camera_ok(const float* camera, uint32_t frame_count, uint32_t width, uint32
 
 using namespace ngp;
 
-extern "C" uint32_t ngp_march_block_totals(uint32_t max_rays) { return (max_rays + kRaysPerCta - 1) / kRaysPerCta; }
+extern "C" uint64_t ngp_march_scratch_words(uint32_t max_rays) { return march_scratch_words(max_rays); }
 
 extern "C" int ngp_density_grid_mark_untrained(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x,
                                                float focal_y, float principal_x, float principal_y, float* values, void* stream) {
@@ -376,12 +390,12 @@ extern "C" int ngp_density_grid_update(float* values, float* scratch, float deca
 extern "C" int ngp_march_training_rays(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float focal_x, float focal_y,
                                        float principal_x, float principal_y, uint32_t step, uint32_t rays_per_batch,
                                        const uint32_t* rays_per_batch_dev, uint32_t sample_limit, const uint8_t* bitfield, float* coords,
-                                       float* rays, uint32_t* ray_indices, uint32_t* numsteps, uint32_t* block_totals, uint32_t* ray_counter,
+                                       float* rays, uint32_t* ray_indices, uint32_t* numsteps, uint32_t* scratch, uint32_t* ray_counter,
                                        uint32_t* sample_counter, void* stream) {
     clear_error();
     if (rays_per_batch == 0) return NGP_OK;
     if (!camera_ok(camera, frame_count, width, height, focal_x, focal_y, principal_x, principal_y) || bitfield == nullptr || coords == nullptr ||
-        numsteps == nullptr || block_totals == nullptr || sample_limit == 0)
+        numsteps == nullptr || scratch == nullptr || sample_limit == 0)
         return fail(NGP_ERR_INVALID, "march training rays: invalid input");
     MarchParams p{};
     p.cam            = camera_set(camera, frame_count, width, height, focal_x, focal_y, principal_x, principal_y);
@@ -390,21 +404,20 @@ extern "C" int ngp_march_training_rays(const float* camera, uint32_t frame_count
     p.n_rays         = rays_per_batch;
     p.bits           = bitfield;
     p.numsteps       = numsteps;
-    p.block_totals   = block_totals;
     p.rays_out       = rays;
     p.ray_indices    = ray_indices;
     p.coords         = coords;
     p.sample_limit   = sample_limit;
     p.ray_counter    = ray_counter;
     p.sample_counter = sample_counter;
-    return launch_march(p, as_stream(stream));
+    return launch_march(p, scratch, as_stream(stream));
 }
 
 extern "C" int ngp_march_rays(uint32_t n_rays, const float* rays, int jitter, uint32_t step, const uint8_t* bitfield, uint32_t sample_limit,
-                              float* coords, uint32_t* numsteps, uint32_t* block_totals, uint32_t* sample_counter, void* stream) {
+                              float* coords, uint32_t* numsteps, uint32_t* scratch, uint32_t* sample_counter, void* stream) {
     clear_error();
     if (n_rays == 0) return NGP_OK;
-    if (rays == nullptr || bitfield == nullptr || coords == nullptr || numsteps == nullptr || block_totals == nullptr || sample_limit == 0)
+    if (rays == nullptr || bitfield == nullptr || coords == nullptr || numsteps == nullptr || scratch == nullptr || sample_limit == 0)
         return fail(NGP_ERR_INVALID, "march rays: invalid input");
     MarchParams p{};
     p.n_rays         = n_rays;
@@ -413,11 +426,10 @@ extern "C" int ngp_march_rays(uint32_t n_rays, const float* rays, int jitter, ui
     p.step           = step;
     p.bits           = bitfield;
     p.numsteps       = numsteps;
-    p.block_totals   = block_totals;
     p.coords         = coords;
     p.sample_limit   = sample_limit;
     p.sample_counter = sample_counter;
-    return launch_march(p, as_stream(stream));
+    return launch_march(p, scratch, as_stream(stream));
 }
 
 extern "C" int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,

@@ -71,7 +71,7 @@ struct ngp_trainer {
     // sampler and network buffers
     float* coords = nullptr;  // [MAX_SAMPLES][7]
     float* rays   = nullptr;  // [BATCH][6]
-    uint32_t *ray_indices = nullptr, *numsteps = nullptr, *block_totals = nullptr;
+    uint32_t *ray_indices = nullptr, *numsteps = nullptr, *march_scratch = nullptr;
     uint32_t* counters     = nullptr;  // 0 rays, 1 samples, 2 compacted
     uint16_t* enc          = nullptr;  // [32][MAX_SAMPLES] encoded positions
     uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output
@@ -122,7 +122,7 @@ void destroy(ngp_trainer* t) {
     free_split(t->val);
     free_split(t->test);
     void* ptrs[] = {t->master, t->params, t->grads, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
-                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->coords, t->rays, t->ray_indices, t->numsteps, t->block_totals,
+                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
                     t->counters, t->enc, t->out, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison};
     for (void* p : ptrs) cudaFree(p);
@@ -241,7 +241,7 @@ int train_step(ngp_trainer* t) {
     // reference's stream (step << 32)
     const uint32_t rng_step = t->step * static_cast<uint32_t>(t->world) + static_cast<uint32_t>(t->rank);
     NGP_TRY(ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, rng_step, t->rays_per_batch, nullptr,
-                                    t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->block_totals,
+                                    t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
                                     t->counters + 0, t->counters + 1, t->stream));
     mark(t, 2);
     // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524)
@@ -311,7 +311,7 @@ int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparis
     for (uint32_t off = 0; off < total;) {
         const uint32_t n = std::min(tile, total - off);
         NGP_TRY(ngp_make_eval_rays(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, off, n, t->rays, t->stream));
-        NGP_TRY(ngp_march_rays(n, t->rays, 0, 0, t->bitfield, kMaxSamples, t->coords, t->numsteps, t->block_totals, t->counters + 1, t->stream));
+        NGP_TRY(ngp_march_rays(n, t->rays, 0, 0, t->bitfield, kMaxSamples, t->coords, t->numsteps, t->march_scratch, t->counters + 1, t->stream));
         uint32_t used = 0;
         NGP_TRY(check_cuda(cudaMemcpyAsync(&used, t->counters + 1, sizeof(used), cudaMemcpyDeviceToHost, t->stream), "eval counter"));
         NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "eval march"));
@@ -396,7 +396,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->rays, static_cast<size_t>(kNetworkBatch) * 6u, "rays"));
         NGP_TRY(dalloc(t->ray_indices, kNetworkBatch, "ray indices"));
         NGP_TRY(dalloc(t->numsteps, static_cast<size_t>(kNetworkBatch) * 2u, "numsteps"));
-        NGP_TRY(dalloc(t->block_totals, ngp_march_block_totals(kNetworkBatch) + 1u, "block totals"));
+        NGP_TRY(dalloc(t->march_scratch, ngp_march_scratch_words(kNetworkBatch), "march scratch"));
         NGP_TRY(dalloc(t->counters, 8, "counters"));
         NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
         NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));

@@ -229,24 +229,24 @@ def density_grid_partials() -> int:
     return int(lib().ngp_density_grid_partials())
 
 
-def march_block_totals(max_rays: int) -> int:
-    lib().ngp_march_block_totals.restype = ctypes.c_uint32
-    return int(lib().ngp_march_block_totals(_u32(max_rays)))
+def march_scratch_words(max_rays: int) -> int:
+    lib().ngp_march_scratch_words.restype = ctypes.c_uint64
+    return int(lib().ngp_march_scratch_words(_u32(max_rays)))
 
 
 def march_training_rays(camera, frame_count, width, height, fx, fy, cx, cy, step, rays_per_batch, sample_limit, bitfield, coords, rays,
-                        ray_indices, numsteps, block_totals, ray_counter, sample_counter, rays_per_batch_dev=None, stream=None) -> None:
+                        ray_indices, numsteps, scratch, ray_counter, sample_counter, rays_per_batch_dev=None, stream=None) -> None:
     _check(lib().ngp_march_training_rays(_ptr(camera), _u32(frame_count), _u32(width), _u32(height), _f32(fx), _f32(fy), _f32(cx), _f32(cy),
                                          _u32(step), _u32(rays_per_batch), _ptr(rays_per_batch_dev), _u32(sample_limit), _ptr(bitfield),
-                                         _ptr(coords), _ptr(rays), _ptr(ray_indices), _ptr(numsteps), _ptr(block_totals), _ptr(ray_counter),
+                                         _ptr(coords), _ptr(rays), _ptr(ray_indices), _ptr(numsteps), _ptr(scratch), _ptr(ray_counter),
                                          _ptr(sample_counter), _stream(stream)), "ngp_march_training_rays")
 
 
-def march_rays(rays, bitfield, coords, numsteps, block_totals, sample_counter, sample_limit=MAX_SAMPLES, jitter=False, step=0, n=None,
+def march_rays(rays, bitfield, coords, numsteps, scratch, sample_counter, sample_limit=MAX_SAMPLES, jitter=False, step=0, n=None,
                stream=None) -> None:
     n = rays.shape[0] if n is None else n
     _check(lib().ngp_march_rays(_u32(n), _ptr(rays), ctypes.c_int(1 if jitter else 0), _u32(step), _ptr(bitfield), _u32(sample_limit), _ptr(coords),
-                                _ptr(numsteps), _ptr(block_totals), _ptr(sample_counter), _stream(stream)), "ngp_march_rays")
+                                _ptr(numsteps), _ptr(scratch), _ptr(sample_counter), _stream(stream)), "ngp_march_rays")
 
 
 def make_eval_rays(camera, image, width, height, fx, fy, cx, cy, pixel_offset, n, rays, stream=None) -> None:

@@ -53,7 +53,7 @@ def run_march(ngp, rays, bits, jitter, step=0, limit=1 << 22):
     n = rays.shape[0]
     coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
     numsteps = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
-    totals = torch.zeros(ngp.march_block_totals(n), dtype=torch.int32, device="cuda")
+    totals = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
     counter = torch.zeros(1, dtype=torch.int32, device="cuda")
     ngp.march_rays(T(rays), T(bits), coords, numsteps, totals, counter, sample_limit=limit, jitter=jitter, step=step)
     torch.cuda.synchronize()
@@ -69,6 +69,22 @@ def test_march_bit_exact_vs_oracle(ngp, oracle, blob_bitfield, n, jitter):
     assert total == ototal
     assert (ns == ons).all()
     used = int(ns[:, 0].sum())
+    assert coords[:used].tobytes() == ocoords[:used].tobytes()
+
+
+@pytest.mark.parametrize("density", [0.02, 0.3, 0.9])
+def test_march_random_bitfield_runs(ngp, oracle, density):
+    """Scattered occupancy: rays cross many separate occupied runs (beyond the per-ray run
+    record, which makes those rays march a second time) -- still bit-exact."""
+    rng = np.random.default_rng(int(density * 100))
+    occ = rng.random(128 ** 3) < density
+    bits = np.packbits(occ.reshape(-1, 8), axis=1, bitorder="little").reshape(-1)
+    rays = workloads.march_rays_config2(4096, seed=11)
+    ns, coords, total = run_march(ngp, rays, bits, True, step=3)
+    ons, ocoords, ototal = oracle.march_rays(rays, bits, jitter=True, step=3)
+    assert total == ototal and (ns == ons).all()
+    used = int(ns[:, 0].sum())
+    assert used > 0
     assert coords[:used].tobytes() == ocoords[:used].tobytes()
 
 
@@ -126,7 +142,7 @@ def test_training_rays_vs_reference_kernel(ngp, reflib, small_scene, blob_bitfie
     o_rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
     o_idx = torch.zeros(n, dtype=torch.int32, device="cuda")
     o_coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
-    totals = torch.zeros(ngp.march_block_totals(n), dtype=torch.int32, device="cuda")
+    totals = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
     orc = torch.zeros(1, dtype=torch.int32, device="cuda")
     osc = torch.zeros(1, dtype=torch.int32, device="cuda")
     ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, o_coords, o_rays, o_idx, o_ns, totals, orc, osc)
@@ -320,7 +336,7 @@ def test_training_loss_vs_reference_kernel(ngp, reflib, small_scene, blob_bitfie
     rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
     ridx = torch.zeros(n, dtype=torch.int32, device="cuda")
     coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
-    totals = torch.zeros(ngp.march_block_totals(n), dtype=torch.int32, device="cuda")
+    totals = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
     rc = torch.zeros(1, dtype=torch.int32, device="cuda")
     sc = torch.zeros(1, dtype=torch.int32, device="cuda")
     ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, coords, rays, ridx, ns, totals, rc, sc)

@@ -32,7 +32,7 @@ def _setup(ngp, n):
     ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
     rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
     ridx = torch.zeros(n, dtype=torch.int32, device="cuda")
-    totals = torch.zeros(ngp.march_block_totals(n), dtype=torch.int32, device="cuda")
+    totals = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
     rc = torch.zeros(1, dtype=torch.int32, device="cuda")
     sc = torch.zeros(1, dtype=torch.int32, device="cuda")
     ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, 2, n, limit, bits, coords, rays, ridx, ns, totals, rc, sc)
