@@ -22,6 +22,15 @@
 #ifndef NGP_ENC_FWD_INTERLEAVE
 #define NGP_ENC_FWD_INTERLEAVE 0  // 1: consecutive CTAs take consecutive levels; 0: level = blockIdx.y
 #endif
+#ifndef NGP_ENC_FWD_LEVELS
+#define NGP_ENC_FWD_LEVELS 2  // > 0: point-major forward, each thread runs all levels of its point, this many at a time
+#endif
+#ifndef NGP_ENC_BWD_POINTS
+#define NGP_ENC_BWD_POINTS 0  // 1: point-major backward (a thread scatters all levels of its point)
+#endif
+#ifndef NGP_ENC_BWD_AGG_RES
+#define NGP_ENC_BWD_AGG_RES 256  // levels up to this resolution pre-sum the lanes of a warp that share a cell
+#endif
 #ifndef NGP_ENC_BWD_INTERLEAVE
 #define NGP_ENC_BWD_INTERLEAVE 1
 #endif
@@ -177,6 +186,62 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_kernel(const ui
     }
 }
 
+// Point-major forward: a thread reads its point once and walks the levels LPI at a time (8 * LPI
+// gathers in flight).  Same per-(point, level) arithmetic as encode_forward_kernel.
+template <uint32_t F, uint32_t LPI>
+__global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(const uint32_t n, const float* __restrict__ coords,
+                                                                               const uint32_t coord_stride, const __half* __restrict__ table,
+                                                                               __half* __restrict__ out, const uint32_t out_stride,
+                                                                               const __grid_constant__ GridParams grid) {
+    using Vec        = typename FeatureVec<F>::type;
+    const uint32_t i = blockIdx.x * kEncodeThreads + threadIdx.x;
+    if (i >= n) return;
+    const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
+    const float x[3] = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
+    const Vec* tab   = reinterpret_cast<const Vec*>(table);
+    for (uint32_t l0 = 0; l0 < grid.n_levels; l0 += LPI) {
+        float frac[LPI][3];
+        Vec v[LPI][8];
+#pragma unroll
+        for (uint32_t j = 0; j < LPI; ++j) {
+            const uint32_t level = min(l0 + j, grid.n_levels - 1u);
+            const uint32_t off = grid.offsets[level], size = grid.offsets[level + 1] - off, res = grid.resolution[level];
+            const float scale = grid.scale[level];
+            uint32_t cell[3];
+#pragma unroll
+            for (uint32_t d = 0; d < 3; ++d) position_fraction(x[d], scale, frac[j][d], cell[d]);
+            const Vec* lvl = tab + off;
+#pragma unroll
+            for (uint32_t yz = 0; yz < 4; ++yz) {
+                const uint32_t cy = cell[1] + (yz & 1u), cz = cell[2] + (yz >> 1);
+                v[j][2 * yz]      = __ldg(lvl + grid_index(size, res, cell[0], cy, cz));
+                v[j][2 * yz + 1]  = __ldg(lvl + grid_index(size, res, cell[0] + 1u, cy, cz));
+            }
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < LPI; ++j) {
+            const uint32_t level = l0 + j;
+            if (level >= grid.n_levels) break;
+            float acc[F];
+#pragma unroll
+            for (uint32_t f = 0; f < F; ++f) acc[f] = 0.0f;
+#pragma unroll
+            for (uint32_t corner = 0; corner < 8; ++corner) {
+                const float wx = (corner & 1u) ? frac[j][0] : __fsub_rn(1.0f, frac[j][0]);
+                const float wy = (corner & 2u) ? frac[j][1] : __fsub_rn(1.0f, frac[j][1]);
+                const float wz = (corner & 4u) ? frac[j][2] : __fsub_rn(1.0f, frac[j][2]);
+                const float w  = __fmul_rn(__fmul_rn(wx, wy), wz);
+                float val[F];
+                unpack<F>(v[j][corner], val);
+#pragma unroll
+                for (uint32_t f = 0; f < F; ++f) acc[f] = __fmaf_rn(w, val[f], acc[f]);
+            }
+#pragma unroll
+            for (uint32_t f = 0; f < F; ++f) out[static_cast<uint64_t>(level * F + f) * out_stride + i] = __float2half_rn(acc[f]);
+        }
+    }
+}
+
 template <uint32_t F>
 __device__ __forceinline__ void scatter_add(float* dst, const float (&g)[F]) {
     if constexpr (F == 1) {
@@ -191,37 +256,25 @@ __device__ __forceinline__ void scatter_add(float* dst, const float (&g)[F]) {
     }
 }
 
+// Scatter one (point, level) gradient: the 8 corner contributions (corner weights in the forward
+// kernel's order, (wx * wy) * wz, times dy).
 template <uint32_t F>
-__global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const uint32_t n, const float* __restrict__ coords,
-                                                                         const uint32_t coord_stride,
-                                                                         const __half* __restrict__ dy, const uint32_t dy_stride,
-                                                                         float* __restrict__ table_grad,
-                                                                         const __grid_constant__ GridParams grid) {
-    uint32_t level, chunk;
-    cta_level_chunk<NGP_ENC_BWD_INTERLEAVE>(grid.n_levels, level, chunk);
-    const uint32_t i = chunk * kEncodeThreads + threadIdx.x;
-    if (i >= n) return;
+__device__ __forceinline__ void scatter_level(const float (&x)[3], const float (&g)[F], float* __restrict__ table_grad, const GridParams& grid,
+                                              uint32_t level) {
     const uint32_t level_offset = grid.offsets[level];
     const uint32_t hashmap_size = grid.offsets[level + 1] - level_offset;
     const uint32_t resolution   = grid.resolution[level];
     const float scale           = grid.scale[level];
     float* __restrict__ lvl     = table_grad + static_cast<uint64_t>(level_offset) * F;
-
-    float g[F];
-#pragma unroll
-    for (uint32_t f = 0; f < F; ++f) g[f] = __half2float(dy[static_cast<uint64_t>(level * F + f) * dy_stride + i]);
-
     float frac[3];
     uint32_t cell[3];
-    const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
 #pragma unroll
-    for (uint32_t d = 0; d < 3; ++d) position_fraction(__ldg(c + d), scale, frac[d], cell[d]);
+    for (uint32_t d = 0; d < 3; ++d) position_fraction(x[d], scale, frac[d], cell[d]);
 
     const float wx0 = __fsub_rn(1.0f, frac[0]), wx1 = frac[0];
 #pragma unroll
     for (uint32_t yz = 0; yz < 4; ++yz) {
         const uint32_t cy  = cell[1] + (yz & 1u), cz = cell[2] + (yz >> 1);
-        // corner weights in the forward kernel's order: (wx * wy) * wz
         const float wy     = (yz & 1u) ? frac[1] : __fsub_rn(1.0f, frac[1]);
         const float wz     = (yz & 2u) ? frac[2] : __fsub_rn(1.0f, frac[2]);
         const float w0     = __fmul_rn(__fmul_rn(wx0, wy), wz);
@@ -255,6 +308,131 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const u
     }
 }
 
+template <uint32_t F>
+__device__ __forceinline__ void load_dy(const __half* __restrict__ dy, uint32_t dy_stride, uint32_t level, uint32_t i, float (&g)[F]) {
+#pragma unroll
+    for (uint32_t f = 0; f < F; ++f) g[f] = __half2float(dy[static_cast<uint64_t>(level * F + f) * dy_stride + i]);
+}
+
+// Warp-aggregated scatter for coarse levels: consecutive points (samples along one ray) often
+// fall into the same cell and so update the same 8 corners.  The lanes of a warp that share a
+// cell add their 8 corner contributions in lane order, and only the lowest of them issues the
+// atomics.  `stage` is this warp's [32][8 * F] shared-memory slot; `active` the lanes present.
+template <uint32_t F>
+__device__ __forceinline__ void scatter_level_warp(const float (&x)[3], const float (&g)[F], float* __restrict__ table_grad, const GridParams& grid,
+                                                   uint32_t level, uint32_t active, float* __restrict__ stage) {
+    const uint32_t level_offset = grid.offsets[level];
+    const uint32_t hashmap_size = grid.offsets[level + 1] - level_offset;
+    const uint32_t resolution   = grid.resolution[level];
+    const float scale           = grid.scale[level];
+    float* __restrict__ lvl     = table_grad + static_cast<uint64_t>(level_offset) * F;
+    float frac[3];
+    uint32_t cell[3];
+#pragma unroll
+    for (uint32_t d = 0; d < 3; ++d) position_fraction(x[d], scale, frac[d], cell[d]);
+    const uint32_t lane  = threadIdx.x & 31u;
+    const uint64_t key   = cell[0] | (static_cast<uint64_t>(cell[1]) << 21) | (static_cast<uint64_t>(cell[2]) << 42);
+    const uint32_t peers = __match_any_sync(active, key);
+    const bool lone      = __popc(peers) == 1;
+
+    float c[8][F];
+    const float wx0 = __fsub_rn(1.0f, frac[0]), wx1 = frac[0];
+#pragma unroll
+    for (uint32_t yz = 0; yz < 4; ++yz) {
+        const float wy = (yz & 1u) ? frac[1] : __fsub_rn(1.0f, frac[1]);
+        const float wz = (yz & 2u) ? frac[2] : __fsub_rn(1.0f, frac[2]);
+        const float w0 = __fmul_rn(__fmul_rn(wx0, wy), wz);
+        const float w1 = __fmul_rn(__fmul_rn(wx1, wy), wz);
+#pragma unroll
+        for (uint32_t f = 0; f < F; ++f) {
+            c[2 * yz][f]     = __fmul_rn(w0, g[f]);
+            c[2 * yz + 1][f] = __fmul_rn(w1, g[f]);
+        }
+    }
+    if (!lone) {
+        float* mine = stage + lane * (8u * F);
+#pragma unroll
+        for (uint32_t k = 0; k < 8; ++k)
+#pragma unroll
+            for (uint32_t f = 0; f < F; ++f) mine[k * F + f] = c[k][f];
+    }
+    __syncwarp(active);
+    const bool leader = lone || (static_cast<uint32_t>(__ffs(peers)) - 1u) == lane;
+    if (!lone && leader) {
+        for (uint32_t rest = peers & (peers - 1u); rest; rest &= rest - 1u) {
+            const float* other = stage + (static_cast<uint32_t>(__ffs(rest)) - 1u) * (8u * F);
+#pragma unroll
+            for (uint32_t k = 0; k < 8; ++k)
+#pragma unroll
+                for (uint32_t f = 0; f < F; ++f) c[k][f] += other[k * F + f];
+        }
+    }
+    __syncwarp(active);
+    if (!leader) return;
+#pragma unroll
+    for (uint32_t yz = 0; yz < 4; ++yz) {
+        const uint32_t cy = cell[1] + (yz & 1u), cz = cell[2] + (yz >> 1);
+        const uint32_t i0 = grid_index(hashmap_size, resolution, cell[0], cy, cz);
+        const uint32_t i1 = grid_index(hashmap_size, resolution, cell[0] + 1u, cy, cz);
+        if ((i0 ^ i1) == 1u) {
+            const uint32_t lo = i0 < i1 ? i0 : i1;
+            float pair[2 * F];
+#pragma unroll
+            for (uint32_t f = 0; f < F; ++f) {
+                pair[f]     = i0 < i1 ? c[2 * yz][f] : c[2 * yz + 1][f];
+                pair[F + f] = i0 < i1 ? c[2 * yz + 1][f] : c[2 * yz][f];
+            }
+            scatter_add<2 * F>(lvl + static_cast<uint64_t>(lo) * F, pair);
+        } else {
+            scatter_add<F>(lvl + static_cast<uint64_t>(i0) * F, c[2 * yz]);
+            scatter_add<F>(lvl + static_cast<uint64_t>(i1) * F, c[2 * yz + 1]);
+        }
+    }
+}
+
+// Level-major backward: each CTA scatters one level for a chunk of points.
+template <uint32_t F>
+__global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const uint32_t n, const float* __restrict__ coords,
+                                                                         const uint32_t coord_stride,
+                                                                         const __half* __restrict__ dy, const uint32_t dy_stride,
+                                                                         float* __restrict__ table_grad,
+                                                                         const __grid_constant__ GridParams grid) {
+    uint32_t level, chunk;
+    cta_level_chunk<NGP_ENC_BWD_INTERLEAVE>(grid.n_levels, level, chunk);
+    const uint32_t i = chunk * kEncodeThreads + threadIdx.x;
+    if (i >= n) return;
+    float g[F];
+    load_dy<F>(dy, dy_stride, level, i, g);
+    const float* c    = coords + static_cast<uint64_t>(i) * coord_stride;
+    const float x[3]  = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
+    if constexpr (F <= 2 && NGP_ENC_BWD_AGG_RES > 0) {
+        if (grid.resolution[level] <= NGP_ENC_BWD_AGG_RES) {
+            __shared__ float stage[kEncodeThreads / 32u][32u * 8u * F];
+            scatter_level_warp<F>(x, g, table_grad, grid, level, __activemask(), stage[threadIdx.x >> 5]);
+            return;
+        }
+    }
+    scatter_level<F>(x, g, table_grad, grid, level);
+}
+
+// Point-major backward: a thread reads its point once and scatters every level.
+template <uint32_t F>
+__global__ void __launch_bounds__(kEncodeThreads) encode_backward_points_kernel(const uint32_t n, const float* __restrict__ coords,
+                                                                                const uint32_t coord_stride,
+                                                                                const __half* __restrict__ dy, const uint32_t dy_stride,
+                                                                                float* __restrict__ table_grad,
+                                                                                const __grid_constant__ GridParams grid) {
+    const uint32_t i = blockIdx.x * kEncodeThreads + threadIdx.x;
+    if (i >= n) return;
+    const float* c   = coords + static_cast<uint64_t>(i) * coord_stride;
+    const float x[3] = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
+    for (uint32_t level = 0; level < grid.n_levels; ++level) {
+        float g[F];
+        load_dy<F>(dy, dy_stride, level, i, g);
+        scatter_level<F>(x, g, table_grad, grid, level);
+    }
+}
+
 int validate_layout(const ngp_grid_layout* layout) {
     if (layout == nullptr) return fail(NGP_ERR_INVALID, "grid layout is null");
     if (layout->n_levels == 0 || layout->n_levels > NGP_MAX_LEVELS) return fail(NGP_ERR_INVALID, "grid layout: bad level count");
@@ -277,6 +455,22 @@ extern "C" int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n
     if (coords == nullptr || table == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "encode forward: null pointer");
     if (coord_stride < 3 || out_stride < n) return fail(NGP_ERR_INVALID, "encode forward: bad stride");
     const GridParams grid = make_grid_params(*layout);
+#if NGP_ENC_FWD_LEVELS > 0
+    {
+        constexpr uint32_t lpi = NGP_ENC_FWD_LEVELS;
+        const uint32_t blocks  = (n + kEncodeThreads - 1) / kEncodeThreads;
+        const auto* t          = reinterpret_cast<const __half*>(table);
+        auto* o                = reinterpret_cast<__half*>(out);
+        const cudaStream_t s   = as_stream(stream);
+        switch (layout->features_per_level) {
+            case 1: encode_forward_points_kernel<1, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+            case 2: encode_forward_points_kernel<2, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+            case 4: encode_forward_points_kernel<4, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+            default: encode_forward_points_kernel<8, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
+        }
+        return check_launch("encode_forward_points_kernel");
+    }
+#endif
     constexpr uint32_t ppt = NGP_ENC_FWD_PPT;
     const dim3 blocks = encode_grid(NGP_ENC_FWD_INTERLEAVE, (n + kEncodeThreads * ppt - 1) / (kEncodeThreads * ppt), layout->n_levels);
     const auto* t = reinterpret_cast<const __half*>(table);
@@ -298,8 +492,21 @@ extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t 
     if (coords == nullptr || dy == nullptr || table_grad == nullptr) return fail(NGP_ERR_INVALID, "encode backward: null pointer");
     if (coord_stride < 3 || dy_stride < n) return fail(NGP_ERR_INVALID, "encode backward: bad stride");
     const GridParams grid = make_grid_params(*layout);
-    const dim3 blocks = encode_grid(NGP_ENC_BWD_INTERLEAVE, (n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
     const auto* g = reinterpret_cast<const __half*>(dy);
+#if NGP_ENC_BWD_POINTS
+    {
+        const uint32_t blocks = (n + kEncodeThreads - 1) / kEncodeThreads;
+        const cudaStream_t s  = as_stream(stream);
+        switch (layout->features_per_level) {
+            case 1: encode_backward_points_kernel<1><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+            case 2: encode_backward_points_kernel<2><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+            case 4: encode_backward_points_kernel<4><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+            default: encode_backward_points_kernel<8><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+        }
+        return check_launch("encode_backward_points_kernel");
+    }
+#endif
+    const dim3 blocks = encode_grid(NGP_ENC_BWD_INTERLEAVE, (n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
     switch (layout->features_per_level) {
         case 1: encode_backward_kernel<1><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
         case 2: encode_backward_kernel<2><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;

@@ -96,6 +96,26 @@ def test_backward_vs_oracle(ngp, oracle, cfg, n):
     assert ((got != 0) == (want != 0)).mean() > 0.999
 
 
+@pytest.mark.parametrize("n", [37, 4000])
+def test_backward_ray_ordered_points_vs_oracle(ngp, oracle, n):
+    """Points along rays at the marching step (as training batches are laid out): neighbouring
+    lanes share cells on the coarse levels, whose updates are summed inside the warp first."""
+    layout = ngp.grid_layout(*CFG0)
+    rng = np.random.default_rng(n)
+    n_rays = max(1, n // 40)
+    o = rng.uniform(0.2, 0.8, (n_rays, 3))
+    d = rng.normal(size=(n_rays, 3))
+    d /= np.linalg.norm(d, axis=1, keepdims=True)
+    t = np.arange(40) * (math.sqrt(3.0) / 1024.0)
+    pts = np.clip(o[:, None, :] + t[None, :, None] * d[:, None, :], 0.0, 1.0).reshape(-1, 3)[:n]
+    coords = np.ascontiguousarray(pts, np.float32)
+    dy = rng.normal(0, 1, (32, n)).astype(np.float16)
+    got = run_backward(ngp, layout, coords, dy, 2)
+    want = oracle.encode_backward(oracle.grid_layout(*CFG0), coords, dy, 2)
+    tol = 1e-3 * np.abs(want) + 1e-6 * np.abs(want).max()
+    assert (np.abs(got - want) <= tol).all()
+
+
 def test_backward_full_size_level_sums(ngp):
     """2^18 points: the corner weights sum to one, so each level/feature's gradient sums to sum(dy)."""
     layout = ngp.grid_layout(*CFG0)
