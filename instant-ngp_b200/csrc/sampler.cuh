@@ -215,15 +215,23 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t& t
 namespace ngp {
 
 // ---- group-cooperative marching --------------------------------------------------------------
-// A group of G adjacent lanes marches one ray (32 / G rays per warp).  From the current t, lane g
-// of the group takes the g-th next cone step t_g = ((t + dt) + dt) ... (g sequential additions,
-// so t_g equals the sequential march's value bit for bit) and tests it; the lanes before the
-// first unoccupied or outside position are exactly the samples the sequential loop would emit,
-// after which lane f's position decides the skip (or the end).  Results are identical to
-// march_count / march_write, with up to G samples resolved per round; skips through empty space
-// stay sequential, so G trades parallelism per ray against total work.
+// A group of G adjacent lanes marches one ray (32 / G rays per warp).  Each round the group
+// speculates on the occupancy of the next G positions of the sequential march and keeps the
+// prefix whose speculation held, so every accepted position is computed by exactly the
+// sequential march's float operations (results are bit-identical to march_count / march_write):
+//  * run mode (the last position seen was occupied): lane g takes t_g = ((t + dt) + dt) ...
+//    (g sequential additions), i.e. it assumes the lanes before it were occupied.  Lanes before
+//    the first unoccupied lane f are samples; lane f's position decides the skip (or the end).
+//  * skip mode (the last position seen was empty): lane g applies g successive empty-voxel skips
+//    to t, i.e. it assumes the lanes before it were inside the grid and empty.  The first lane f
+//    that is occupied is a sample (then run mode continues at t_f + dt); an outside lane ends the
+//    ray; with all G empty the march continues from the skip after lane G-1.
+// Up to G occupied steps or G empty voxels are resolved per round.
 #ifndef NGP_MARCH_GROUP
 #define NGP_MARCH_GROUP 4
+#endif
+#ifndef NGP_MARCH_SKIP_SPEC
+#define NGP_MARCH_SKIP_SPEC 1  // 0: empty voxels are skipped one per round
 #endif
 constexpr uint32_t kMarchGroup = NGP_MARCH_GROUP;
 
@@ -232,74 +240,95 @@ struct GroupMarch {
     float t;
     uint32_t n;
     bool done;
+    bool skip;  // next round speculates empty voxels
 };
 
 __device__ __forceinline__ void group_march_begin(GroupMarch& m, float3 o, float3 d, float start_t, bool active) {
-    m.o = o, m.d = d, m.inv = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z}, m.t = start_t, m.n = 0, m.done = !active;
+    m.o = o, m.d = d, m.inv = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z}, m.t = start_t, m.n = 0, m.done = !active, m.skip = false;
 }
 
-// One round for every group of the warp (all 32 lanes call it together).  Returns the samples
-// this group emitted (uniform within the group); `emit` marks this lane's position as one.
-__device__ __forceinline__ uint32_t group_march_round(GroupMarch& m, const uint8_t* __restrict__ bits, uint32_t limit, float3& my_pos, bool& emit) {
+// Result of one round for the calling lane's group.
+struct MarchRound {
+    uint32_t k;      // samples emitted (uniform in the group)
+    float first_t;   // t of the first emitted sample
+    bool emit;       // this lane's position is an emitted sample ...
+    uint32_t slot;   // ... the slot-th of this round
+    float3 pos;      // this lane's position
+    bool cont;       // the next round's first position directly follows the last emitted sample
+};
+
+// One round for every group of the warp (all 32 lanes call it together).
+__device__ __forceinline__ MarchRound group_march_round(GroupMarch& m, const uint8_t* __restrict__ bits, uint32_t limit) {
     constexpr uint32_t G    = kMarchGroup;
     const uint32_t lane     = threadIdx.x & 31u;
     const uint32_t g        = lane % G;
     const uint32_t group_lo = lane - g;
+    const bool skip_mode    = NGP_MARCH_SKIP_SPEC && m.skip;
     float tk                = m.t;
-    for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
-    my_pos              = ray_point(m.o, m.d, tk);
-    const bool ins      = !m.done && inside_unit_cube(my_pos);
-    const bool oc       = ins && occupied(my_pos, bits);
-    const uint32_t stop = (__ballot_sync(0xFFFFFFFFu, !oc) >> group_lo) & ((1u << G) - 1u);
-    const uint32_t f    = stop ? static_cast<uint32_t>(__ffs(stop)) - 1u : G;
-    const uint32_t room = limit - m.n;
-    const uint32_t k    = m.done ? 0u : (f < room ? f : room);
-    emit                = g < k;
-    const float t_last  = __shfl_sync(0xFFFFFFFFu, tk, group_lo + G - 1u);
-    const bool f_inside = __shfl_sync(0xFFFFFFFFu, ins, group_lo + (f < G ? f : 0u));
-    const float next    = skip_empty_voxel(tk, my_pos, m.d, m.inv);
-    const float f_next  = __shfl_sync(0xFFFFFFFFu, next, group_lo + (f < G ? f : 0u));
-    if (m.done) return 0u;
-    m.n += k;
-    if (m.n >= limit) {
-        m.done = true;
-    } else if (f == G) {
-        m.t = t_last + kConeStep;
-    } else if (!f_inside) {
-        m.done = true;
+    if (skip_mode) {
+        for (uint32_t j = 0; j < g; ++j) tk = skip_empty_voxel(tk, ray_point(m.o, m.d, tk), m.d, m.inv);
     } else {
-        m.t = f_next;
+        for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
     }
-    return k;
-}
-
-// Sample count of this group's ray (all lanes of the warp call it; inactive groups pass active=false).
-__device__ __forceinline__ uint32_t group_march_count(float3 o, float3 d, float start_t, bool active, const uint8_t* __restrict__ bits) {
-    GroupMarch m;
-    group_march_begin(m, o, d, start_t, active);
-    while (__any_sync(0xFFFFFFFFu, !m.done)) {
-        float3 p;
-        bool e;
-        group_march_round(m, bits, kMarchSteps, p, e);
+    MarchRound r;
+    r.pos                = ray_point(m.o, m.d, tk);
+    const bool ins       = !m.done && inside_unit_cube(r.pos);
+    const bool oc        = ins && occupied(r.pos, bits);
+    const bool stop_here = skip_mode ? (!ins || oc) : !oc;
+    const uint32_t stop  = (__ballot_sync(0xFFFFFFFFu, stop_here) >> group_lo) & ((1u << G) - 1u);
+    const uint32_t f     = stop ? static_cast<uint32_t>(__ffs(stop)) - 1u : G;
+    const uint32_t fl    = group_lo + (f < G ? f : G - 1u);
+    const float next     = skip_empty_voxel(tk, r.pos, m.d, m.inv);
+    const float f_t      = __shfl_sync(0xFFFFFFFFu, tk, fl);
+    const bool f_inside  = __shfl_sync(0xFFFFFFFFu, ins, fl);
+    const float f_next   = __shfl_sync(0xFFFFFFFFu, next, fl);
+    const float t_last   = __shfl_sync(0xFFFFFFFFu, tk, group_lo + G - 1u);
+    r.k = 0, r.first_t = 0.0f, r.emit = false, r.slot = 0, r.cont = false;
+    if (m.done) return r;
+    const uint32_t room = limit - m.n;
+    if (skip_mode) {
+        if (f == G) {
+            m.t = f_next;  // G empty voxels: lane G-1's skip
+        } else if (!f_inside) {
+            m.done = true;
+        } else {
+            r.k = 1, r.first_t = f_t, r.emit = g == f, r.slot = 0;
+            m.n += 1;
+            m.t    = f_t + kConeStep;
+            m.skip = false;
+            if (m.n >= limit) m.done = true;
+        }
+    } else {
+        r.k = f < room ? f : room;
+        r.first_t = m.t, r.emit = g < r.k, r.slot = g;
+        m.n += r.k;
+        if (m.n >= limit) {
+            m.done = true;
+        } else if (f == G) {
+            m.t = t_last + kConeStep;
+        } else if (!f_inside) {
+            m.done = true;
+        } else {
+            m.t    = f_next;
+            m.skip = NGP_MARCH_SKIP_SPEC;
+        }
     }
-    return m.n;
+    r.cont = r.k > 0 && !m.done && !m.skip;
+    return r;
 }
 
 // Writes exactly `n` records (n = this ray's count) starting at `out`; n = 0 for inactive groups.
 __device__ __forceinline__ void group_march_write(float3 o, float3 d, float start_t, uint32_t n, const uint8_t* __restrict__ bits,
                                                   float* __restrict__ out) {
-    const float3 w3     = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
-    const uint32_t g    = (threadIdx.x & 31u) % kMarchGroup;
+    const float3 w3 = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
     GroupMarch m;
     group_march_begin(m, o, d, start_t, n > 0);
     while (__any_sync(0xFFFFFFFFu, !m.done)) {
-        float3 p;
-        bool e;
         const uint32_t before = m.n;
-        group_march_round(m, bits, n, p, e);
-        if (e) {
-            float* c = out + static_cast<uint64_t>(before + g) * 7u;
-            c[0] = p.x, c[1] = p.y, c[2] = p.z, c[3] = kConeStep, c[4] = w3.x, c[5] = w3.y, c[6] = w3.z;
+        const MarchRound r    = group_march_round(m, bits, n);
+        if (r.emit) {
+            float* c = out + static_cast<uint64_t>(before + r.slot) * 7u;
+            c[0] = r.pos.x, c[1] = r.pos.y, c[2] = r.pos.z, c[3] = kConeStep, c[4] = w3.x, c[5] = w3.y, c[6] = w3.z;
         }
     }
 }
@@ -312,6 +341,8 @@ __device__ __forceinline__ void group_march_write(float3 o, float3 d, float star
 constexpr uint32_t kMaxRuns      = 48u;
 constexpr uint32_t kRunsOverflow = 0xFFFFFFFFu;
 
+// Sample count of this group's ray (all lanes of the warp call it; inactive groups pass
+// active=false); its runs go to `runs`, their number (or kRunsOverflow) to n_runs.
 __device__ __forceinline__ uint32_t group_march_count_runs(float3 o, float3 d, float start_t, bool active, const uint8_t* __restrict__ bits,
                                                            uint2* __restrict__ runs, uint32_t& n_runs) {
     const uint32_t g = (threadIdx.x & 31u) % kMarchGroup;
@@ -321,18 +352,12 @@ __device__ __forceinline__ uint32_t group_march_count_runs(float3 o, float3 d, f
     uint32_t run_n = 0;
     n_runs         = 0;
     while (__any_sync(0xFFFFFFFFu, !m.done)) {
-        const bool was_done = m.done;
-        const float t_round = m.t;
-        float3 p;
-        bool e;
-        const uint32_t k = group_march_round(m, bits, kMarchSteps, p, e);
-        if (was_done) continue;
-        if (k > 0) {
-            if (run_n == 0) run_t0 = t_round;
-            run_n += k;
+        const MarchRound r = group_march_round(m, bits, kMarchSteps);
+        if (r.k > 0) {
+            if (run_n == 0) run_t0 = r.first_t;
+            run_n += r.k;
         }
-        const bool continues = k == kMarchGroup && !m.done;
-        if (!continues && run_n > 0) {
+        if (!r.cont && run_n > 0) {
             if (n_runs < kMaxRuns && g == 0) runs[n_runs] = make_uint2(__float_as_uint(run_t0), run_n);
             ++n_runs;
             run_n = 0;

@@ -105,6 +105,14 @@ struct ngp_trainer {
     uint32_t ema_step       = 0;
     uint32_t occupied_cells = 0;
     float grid_update_ms    = 0.0f;
+    // Cross-step pipelining inside one train call: once a step's loss pass has produced its
+    // counters, the next step's rays are marched on march_stream while this step's backward and
+    // optimizer run (marching reads only the bitfield, which changes only on grid-update steps).
+    cudaStream_t march_stream = nullptr;
+    cudaEvent_t ev_counts = nullptr, ev_march = nullptr;
+    uint32_t* host_counters = nullptr;  // pinned copy of counters 0..2
+    bool premarched         = false;    // step `step` was marched on march_stream
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> grid_events;  // pending grid-update timings
 };
 
 namespace {
@@ -127,8 +135,14 @@ void destroy(ngp_trainer* t) {
                     t->mlp_scratch, t->eval_sse, t->comparison};
     for (void* p : ptrs) cudaFree(p);
     if (t->comm) ncclCommDestroy(t->comm);
+    if (t->march_stream) cudaStreamSynchronize(t->march_stream);
     for (cudaEvent_t e : t->marks)
         if (e) cudaEventDestroy(e);
+    for (auto& pr : t->grid_events) cudaEventDestroy(pr.first), cudaEventDestroy(pr.second);
+    if (t->ev_counts) cudaEventDestroy(t->ev_counts);
+    if (t->ev_march) cudaEventDestroy(t->ev_march);
+    if (t->host_counters) cudaFreeHost(t->host_counters);
+    if (t->march_stream) cudaStreamDestroy(t->march_stream);
     if (t->stream) cudaStreamDestroy(t->stream);
     delete t;
 }
@@ -194,14 +208,20 @@ int encode(ngp_trainer* t, uint32_t n, const float* c, uint16_t* dst, uint32_t s
     return ngp_encode_grid_forward(&t->layout, n, c, 7, t->params + kMlpParams, dst, stride, t->stream);
 }
 
+// Grid-update schedule of update_density_grid (ngp.train.cu:1526-1531).
+bool grid_update_due(uint32_t step) {
+    uint32_t skip = step / 16u;
+    skip          = skip < 1u ? 1u : (skip > 16u ? 16u : skip);
+    return step % skip == 0u;
+}
+
 // update_density_grid (ngp.train.cu:1526-1595).
 int update_grid(ngp_trainer* t) {
-    uint32_t skip = t->step / 16u;
-    skip          = skip < 1u ? 1u : (skip > 16u ? 16u : skip);
-    if (t->step % skip != 0u) return NGP_OK;
+    if (!grid_update_due(t->step)) return NGP_OK;
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
+    t->grid_events.emplace_back(e0, e1);
     cudaEventRecord(e0, t->stream);
     const Split& s = t->train;
     if (t->step == 0) {
@@ -218,31 +238,51 @@ int update_grid(ngp_trainer* t) {
     NGP_TRY(ngp_density_grid_update(t->grid_values, t->grid_scratch, 0.95f, t->grid_partial, t->grid_mean, t->bitfield, t->occupied, t->stream));
     ++t->ema_step;
     cudaEventRecord(e1, t->stream);
-    cudaEventSynchronize(e1);
-    float ms = 0.0f;
-    cudaEventElapsedTime(&ms, e0, e1);
-    t->grid_update_ms += ms;
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
     return NGP_OK;
+}
+
+// Adds the finished grid updates' durations to grid_update_ms.
+void collect_grid_times(ngp_trainer* t) {
+    for (auto& pr : t->grid_events) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(pr.second) == cudaSuccess && cudaEventElapsedTime(&ms, pr.first, pr.second) == cudaSuccess) t->grid_update_ms += ms;
+        cudaEventDestroy(pr.first);
+        cudaEventDestroy(pr.second);
+    }
+    t->grid_events.clear();
+}
+
+int march_step(ngp_trainer* t, uint32_t step, cudaStream_t stream) {
+    const Split& s          = t->train;
+    const uint32_t rng_step = step * static_cast<uint32_t>(t->world) + static_cast<uint32_t>(t->rank);
+    return ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, rng_step, t->rays_per_batch, nullptr,
+                                   t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
+                                   t->counters + 0, t->counters + 1, stream);
 }
 
 void mark(ngp_trainer* t, int k) {
     if (t->profiling) cudaEventRecord(t->marks[k], t->stream);
 }
 
-int train_step(ngp_trainer* t) {
+// One training step.  `premarch_next`: march step + 1 on march_stream once this step's counters
+// are known (the caller guarantees that step + 1 follows in the same call).
+int train_step(ngp_trainer* t, bool premarch_next) {
     const Split& s = t->train;
     mark(t, 0);
-    NGP_TRY(update_grid(t));
-    mark(t, 1);
-    // sample_training_batch (ngp.train.cu:1919-1930)
-    // each rank draws its rays from its own PCG32 stream; rank 0 of a single-GPU run uses the
-    // reference's stream (step << 32)
+    if (t->premarched) {
+        // marched during the previous step's backward pass (no grid update is due at this step)
+        NGP_TRY(check_cuda(cudaStreamWaitEvent(t->stream, t->ev_march, 0), "wait march"));
+        t->premarched = false;
+        mark(t, 1);
+    } else {
+        NGP_TRY(update_grid(t));
+        mark(t, 1);
+        // sample_training_batch (ngp.train.cu:1919-1930)
+        // each rank draws its rays from its own PCG32 stream; rank 0 of a single-GPU run uses the
+        // reference's stream (step << 32)
+        NGP_TRY(march_step(t, t->step, t->stream));
+    }
     const uint32_t rng_step = t->step * static_cast<uint32_t>(t->world) + static_cast<uint32_t>(t->rank);
-    NGP_TRY(ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, rng_step, t->rays_per_batch, nullptr,
-                                    t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
-                                    t->counters + 0, t->counters + 1, t->stream));
     mark(t, 2);
     // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524)
     NGP_TRY(encode(t, t->inference_samples, t->coords, t->enc, t->inference_samples));
@@ -254,6 +294,8 @@ int train_step(ngp_trainer* t) {
                                           t->counters + 2, t->ray_indices, t->rays, t->numsteps, t->coords, t->ccoords, t->dloss,
                                           t->loss_values, t->loss_scratch, t->loss_scratch_bytes, t->stream));
     NGP_TRY(ngp_pad_training_batch(t->counters + 2, t->ccoords, t->dloss, t->stream));
+    NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, t->counters, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
+    NGP_TRY(check_cuda(cudaEventRecord(t->ev_counts, t->stream), "record counters"));
     mark(t, 5);
     // encoding of the batch, fused MLP backward (recompute), encoding backward
     NGP_TRY(encode(t, kNetworkBatch, t->ccoords, t->cenc, kNetworkBatch));
@@ -274,11 +316,12 @@ int train_step(ngp_trainer* t) {
     NGP_TRY(ngp_adam_step(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world), t->master, t->params, t->grads,
                           t->adam_m, t->adam_v, t->adam_steps, 1, t->stream));
     mark(t, 10);
-    // adaptive batch (ngp.train.cpp:125-133)
-    uint32_t c[3];
-    NGP_TRY(check_cuda(cudaMemcpyAsync(c, t->counters, sizeof(c), cudaMemcpyDeviceToHost, t->stream), "read counters"));
-    NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train step"));
+    // adaptive batch (ngp.train.cpp:125-133): this step's counters were copied after the loss
+    // pass; the host waits for them while the backward pass and Adam run
+    NGP_TRY(check_cuda(cudaEventSynchronize(t->ev_counts), "train step counters"));
+    const uint32_t c[3] = {t->host_counters[0], t->host_counters[1], t->host_counters[2]};
     if (t->profiling) {
+        NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train step"));
         for (int k = 0; k < kTrainPhases; ++k) {
             float ms = 0.0f;
             cudaEventElapsedTime(&ms, t->marks[k], t->marks[k + 1]);
@@ -298,6 +341,14 @@ int train_step(ngp_trainer* t) {
     const uint64_t want  = std::min<uint64_t>((static_cast<uint64_t>(t->rays_per_batch) * kNetworkBatch) / t->measured, kNetworkBatch);
     t->rays_per_batch    = std::min(std::max(static_cast<uint32_t>((want + g - 1u) / g * g), g), kNetworkBatch);
     ++t->step;
+    if (premarch_next && !t->profiling && !grid_update_due(t->step)) {
+        // the march overwrites coords/rays/numsteps/counters 0-1, which this step last read in
+        // its loss pass (ev_counts follows it)
+        NGP_TRY(check_cuda(cudaStreamWaitEvent(t->march_stream, t->ev_counts, 0), "march after loss"));
+        NGP_TRY(march_step(t, t->step, t->march_stream));
+        NGP_TRY(check_cuda(cudaEventRecord(t->ev_march, t->march_stream), "record march"));
+        t->premarched = true;
+    }
     return NGP_OK;
 }
 
@@ -375,6 +426,10 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(ngp_grid_layout_make(cfg->n_levels, cfg->features_per_level, cfg->log2_hashmap_size, cfg->base_resolution,
                                      cfg->log2_per_level_scale, &t->layout));
         NGP_TRY(check_cuda(cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking), "stream"));
+        NGP_TRY(check_cuda(cudaStreamCreateWithFlags(&t->march_stream, cudaStreamNonBlocking), "march stream"));
+        NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_counts, cudaEventDisableTiming), "event"));
+        NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_march, cudaEventDisableTiming), "event"));
+        NGP_TRY(check_cuda(cudaMallocHost(&t->host_counters, 4 * sizeof(uint32_t)), "pinned counters"));
         NGP_TRY(upload_split(t->train, train, "train"));
         NGP_TRY(upload_split(t->val, validation, "validation"));
         NGP_TRY(upload_split(t->test, test, "test"));
@@ -469,8 +524,10 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
     uint32_t loss_rays = t->rays_per_batch;
     for (int32_t i = 0; i < iters; ++i) {
         loss_rays    = t->rays_per_batch;
-        const int st = train_step(t);
+        const int st = train_step(t, i + 1 < iters);
         if (st != NGP_OK) {
+            cudaStreamSynchronize(t->march_stream);
+            t->premarched = false;
             cudaEventDestroy(e0);
             cudaEventDestroy(e1);
             return st;
@@ -481,6 +538,7 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
     NGP_TRY(check_cuda(cudaMemcpyAsync(losses.data(), t->loss_values, sizeof(float) * loss_rays, cudaMemcpyDeviceToHost, t->stream), "read loss"));
     NGP_TRY(check_cuda(cudaMemcpyAsync(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read occupied"));
     NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train"));
+    collect_grid_times(t);
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, e0, e1);
     cudaEventDestroy(e0);
