@@ -160,6 +160,8 @@ def make_dataset(args):
 # forward + backward (input gradients + weight gradients) = 61,440.
 MLP_FWD_FLOP = 20480
 MLP_FWDBWD_FLOP = 61440
+DENSITY_FWD_FLOP = 6144
+COMPACTED_ROWS = BATCH + 1024
 
 
 def phase_roofline(phases: dict, peaks: dict) -> dict:
@@ -171,15 +173,16 @@ def phase_roofline(phases: dict, peaks: dict) -> dict:
     total = sum(ms.values())
     dom = max(ms, key=ms.get)
     t = ms[dom] * 1e-3
-    if dom in ("mlp_fwd_inference", "mlp_bwd"):
-        flops = (MLP_FWD_FLOP * n_inf) if dom == "mlp_fwd_inference" else (MLP_FWDBWD_FLOP * BATCH)
+    if dom in ("density_fwd_inference", "mlp_bwd"):
+        flops = (DENSITY_FWD_FLOP * n_inf) if dom == "density_fwd_inference" else (MLP_FWDBWD_FLOP * BATCH)
         achieved = flops / t / 1e12
         return {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": None, "share": round(ms[dom] / total, 3),
                 "peak_source": peaks["source"] + " (sustained dense bf16; fp16 has the same tensor rate)"}
     # memory-bound phases: algorithmic bytes per unit
-    per = {"encode_fwd_inference": (28 + 64 + 16 * 8 * 2 * 2, n_inf), "encode_fwd_batch": (28 + 64 + 16 * 8 * 2 * 2, BATCH),
-           "encode_bwd": (28 + 64 + 16 * 8 * 2 * 4, BATCH), "march": (28 * 1.0, n_inf), "loss_compact_pad": (28 + 32 + 28 + 32, BATCH),
+    per = {"encode_fwd_inference": (28 + 64 + 16 * 8 * 2 * 2, n_inf), "compact": (2 + 4 + (28 + 64) * 2 * BATCH / max(n_inf, 1), n_inf),
+           "mlp_fwd_loss_pad": (28 + 64 + 32 + 28 + 32 + 32, COMPACTED_ROWS),
+           "encode_bwd": (28 + 64 + 16 * 8 * 2 * 4, BATCH), "march": (28 * 1.0, n_inf),
            "adam": (38, 12_206_480), "grid_update": (16, 128 ** 3 * 2), "allreduce": (8, 12_206_480)}
     b, n = per.get(dom, (0, 0))
     achieved = b * n / t / 1e9

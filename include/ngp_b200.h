@@ -231,6 +231,38 @@ NGP_API int ngp_training_loss_and_compact_noalloc(uint32_t rays_per_batch, uint3
                                                   const float* coords, float* compacted_coords, uint16_t* dloss_doutput, float* loss_values,
                                                   void* stream);
 
+/* Density-first variant of ngp_training_loss_and_compact, used by the trainer: which samples a
+ * ray keeps depends only on the densities, so the pre-compaction pass needs only the density
+ * network and the colour network runs on the kept samples alone.  Same kept set, order, losses
+ * and gradients as ngp_training_loss_and_compact (bit for bit).
+ *
+ * Rows of the compacted buffers: ngp_compacted_rows() = 2^18 + 1024 (the ray that straddles the
+ * batch end is compacted whole, so that its colour can be composited).
+ *
+ * Step 1: density fp16 [samples] (raw, e.g. from ngp_density_forward) -> compacted records
+ * [rows][7], optionally the encoded positions of the kept samples (enc [32][enc_stride] ->
+ * compacted_enc [32][rows]), numsteps rewritten to (kept, compacted base), *compacted_counter
+ * = min(kept total, 2^18).  scratch: ngp_loss_scratch_bytes(rays_per_batch), 16-byte aligned,
+ * passed unchanged to step 2. */
+NGP_API uint32_t ngp_compacted_rows(void);
+NGP_API int ngp_training_compact_by_density(uint32_t rays_per_batch, const uint32_t* ray_counter, const uint16_t* density, const float* coords,
+                                            const uint16_t* enc, uint32_t enc_stride, uint32_t* numsteps, float* compacted_coords,
+                                            uint16_t* compacted_enc, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
+                                            void* stream);
+
+/* Step 2, after the full network ran on the compacted rows (compacted_output fp16 [rows][16]):
+ * compositing, loss and gradients as ngp_training_loss_and_compact; numsteps ends as
+ * (samples in the batch, compacted base). */
+NGP_API int ngp_training_loss_compacted(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                        uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* compacted_output,
+                                        const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* compacted_coords,
+                                        uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, void* stream);
+
+/* ngp_pad_training_batch that also pads the compacted encoded positions (enc [32][enc_stride]),
+ * so that they equal the encoding of the padded records. */
+NGP_API int ngp_pad_training_batch_enc(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, uint16_t* enc,
+                                       uint32_t enc_stride, void* stream);
+
 /* Wrap-around padding of the compacted batch to 2^18 samples, copied gradients scaled by
  * count / 2^18.  Replaces K12/K13 (ngp.train.cu:862-874, 1946-1956). */
 NGP_API int ngp_pad_training_batch(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, void* stream);

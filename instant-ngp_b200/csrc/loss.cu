@@ -49,23 +49,28 @@ __device__ __forceinline__ uint32_t loss_rays(const LossParams& p) {
 }
 
 // Target pixel and random background of ray `ray_index` in this step (ngp.train.cu:781-796).
-__device__ __forceinline__ void ray_target(const LossParams& p, uint32_t ray_index, float3& bg, float3& target) {
+__device__ __forceinline__ void ray_target(uint32_t step, uint32_t rays_per_batch, const uint8_t* __restrict__ pixels, uint32_t frame_count,
+                                           uint32_t width, uint32_t height, uint32_t ray_index, float3& bg, float3& target) {
     Pcg32 rng{kTrainSeed};
-    rng.advance(static_cast<uint64_t>(p.step) << 32u);
+    rng.advance(static_cast<uint64_t>(step) << 32u);
     rng.advance(static_cast<uint64_t>(ray_index) * kRandPerRay);
-    const uint32_t image = static_cast<uint32_t>((static_cast<uint64_t>(ray_index) * p.frame_count) / p.rays_per_batch) % p.frame_count;
+    const uint32_t image = static_cast<uint32_t>((static_cast<uint64_t>(ray_index) * frame_count) / rays_per_batch) % frame_count;
     float u = rng.next_float(), v = rng.next_float();
-    uint32_t px = min(static_cast<uint32_t>(u * static_cast<float>(p.width)), p.width - 1u);
-    uint32_t py = min(static_cast<uint32_t>(v * static_cast<float>(p.height)), p.height - 1u);
-    u           = (static_cast<float>(px) + 0.5f) / static_cast<float>(p.width);
-    v           = (static_cast<float>(py) + 0.5f) / static_cast<float>(p.height);
+    uint32_t px = min(static_cast<uint32_t>(u * static_cast<float>(width)), width - 1u);
+    uint32_t py = min(static_cast<uint32_t>(v * static_cast<float>(height)), height - 1u);
+    u           = (static_cast<float>(px) + 0.5f) / static_cast<float>(width);
+    v           = (static_cast<float>(py) + 0.5f) / static_cast<float>(height);
     bg          = {rng.next_float(), rng.next_float(), rng.next_float()};
-    px          = min(static_cast<uint32_t>(u * static_cast<float>(p.width)), p.width - 1u);
-    py          = min(static_cast<uint32_t>(v * static_cast<float>(p.height)), p.height - 1u);
-    const float4 texel = read_texel(px, py, image, p.width, p.height, p.pixels);
+    px          = min(static_cast<uint32_t>(u * static_cast<float>(width)), width - 1u);
+    py          = min(static_cast<uint32_t>(v * static_cast<float>(height)), height - 1u);
+    const float4 texel = read_texel(px, py, image, width, height, pixels);
     const float3 bgl   = {srgb_to_linear_c(bg.x), srgb_to_linear_c(bg.y), srgb_to_linear_c(bg.z)};
     target = {linear_to_srgb_c(__fmaf_rn(1.0f - texel.w, bgl.x, texel.x)), linear_to_srgb_c(__fmaf_rn(1.0f - texel.w, bgl.y, texel.y)),
               linear_to_srgb_c(__fmaf_rn(1.0f - texel.w, bgl.z, texel.z))};
+}
+
+__device__ __forceinline__ void ray_target(const LossParams& p, uint32_t ray_index, float3& bg, float3& target) {
+    ray_target(p.step, p.rays_per_batch, p.pixels, p.frame_count, p.width, p.height, ray_index, bg, target);
 }
 
 __device__ __forceinline__ void load_output(const __half* o, float& r, float& g, float& b, float& d) {
@@ -87,6 +92,88 @@ __device__ __forceinline__ float prefix_transmittance(float T, float q) {
     }
     return Tb;
 }
+
+// Gradients of one ray's first cn samples (rest of K11, ngp.train.cu:804-859): dL/d(raw rgb) and
+// dL/d(raw density) per sample, times `scale`; the sample records are also copied to cout when
+// it is not null.  The whole warp calls it for one ray.
+__device__ __forceinline__ void ray_gradients(float3 rgb, float3 target, float scale, const float* __restrict__ ray, const float* __restrict__ cin,
+                                              const __half* __restrict__ out, float* __restrict__ cout, __half* __restrict__ dout, uint32_t cn) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const float3 diff   = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
+    const float3 grad   = {2.0f * diff.x, 2.0f * diff.y, 2.0f * diff.z};
+    const float3 origin = {ray[0], ray[1], ray[2]};
+    float T             = 1.0f;
+    float3 acc          = {0.0f, 0.0f, 0.0f};
+    for (uint32_t c0 = 0; c0 < cn; c0 += 32u) {
+        const uint32_t j = c0 + lane;
+        const bool valid = j < cn;
+        float cv[7]      = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float mr = 0.f, mg = 0.f, mb = 0.f, md = 0.f;
+        if (valid) {
+            const float* c = cin + static_cast<uint64_t>(j) * 7u;
+#pragma unroll
+            for (int q = 0; q < 7; ++q) cv[q] = c[q];
+            if (cout != nullptr) {
+                float* co = cout + static_cast<uint64_t>(j) * 7u;
+#pragma unroll
+                for (int q = 0; q < 7; ++q) co[q] = cv[q];
+            }
+            load_output(out + static_cast<uint64_t>(j) * 16u, mr, mg, mb, md);
+        }
+        const float dt     = cv[3];
+        const float3 col   = {sigmoidf_(mr), sigmoidf_(mg), sigmoidf_(mb)};
+        const float alpha  = valid ? 1.0f - __expf(-expf(md) * dt) : 0.0f;
+        const float Tb     = prefix_transmittance(T, 1.0f - alpha);
+        const float weight = alpha * Tb;
+        // colour prefix including this sample, accumulated in sample order
+        float3 a = acc;
+        for (uint32_t q = 0; q < 32u; ++q) {
+            const float wq = __shfl_sync(0xFFFFFFFFu, weight, q);
+            const float cx = __shfl_sync(0xFFFFFFFFu, col.x, q), cy = __shfl_sync(0xFFFFFFFFu, col.y, q), cz = __shfl_sync(0xFFFFFFFFu, col.z, q);
+            if (q <= lane) {
+                a.x = __fmaf_rn(wq, cx, a.x);
+                a.y = __fmaf_rn(wq, cy, a.y);
+                a.z = __fmaf_rn(wq, cz, a.z);
+            }
+        }
+        const float Ta = Tb * (1.0f - alpha);
+        if (valid) {
+            const float depth   = norm3df(cv[0] - origin.x, cv[1] - origin.y, cv[2] - origin.z);
+            const float3 suffix = {rgb.x - a.x, rgb.y - a.y, rgb.z - a.z};
+            const float g0      = scale * (weight * grad.x * (col.x * (1.0f - col.x)));
+            const float g1      = scale * (weight * grad.y * (col.y * (1.0f - col.y)));
+            const float g2      = scale * (weight * grad.z * (col.z * (1.0f - col.z)));
+            const float dd      = expf(fminf(fmaxf(md, -15.0f), 15.0f));
+            const float sum = __fmaf_rn(grad.z, __fmaf_rn(Ta, col.z, -suffix.z),
+                                        __fmaf_rn(grad.x, __fmaf_rn(Ta, col.x, -suffix.x), grad.y * __fmaf_rn(Ta, col.y, -suffix.y)));
+            const float g3 = __fmaf_rn(scale, dd * (dt * sum), (md > -10.0f && depth < 0.1f) ? 1e-4f : 0.0f);
+            uint4* d       = reinterpret_cast<uint4*>(dout + static_cast<uint64_t>(j) * 16u);
+            __half2 h01 = __floats2half2_rn(g0, g1), h23 = __floats2half2_rn(g2, g3);
+            d[0]        = make_uint4(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23), 0u, 0u);
+            d[1]        = make_uint4(0u, 0u, 0u, 0u);
+        }
+        const uint32_t last = min(31u, cn - 1u - c0);
+        T                   = __shfl_sync(0xFFFFFFFFu, Ta, last);
+        acc.x               = __shfl_sync(0xFFFFFFFFu, a.x, last);
+        acc.y               = __shfl_sync(0xFFFFFFFFu, a.y, last);
+        acc.z               = __shfl_sync(0xFFFFFFFFu, a.z, last);
+    }
+}
+
+__global__ void __launch_bounds__(1024) scan_kept_kernel(uint32_t* __restrict__ totals, uint32_t n_blocks, uint32_t* __restrict__ compacted_counter,
+                                                         uint32_t batch) {
+    uint32_t carry = 0;
+    for (uint32_t b = 0; b < n_blocks; b += 1024u) {
+        const uint32_t k = b + threadIdx.x;
+        const uint32_t v = k < n_blocks ? totals[k] : 0u;
+        uint32_t sum;
+        const uint32_t ex = block_exclusive_scan(v, sum);
+        if (k < n_blocks) totals[k] = carry + ex;
+        carry += sum;
+    }
+    if (threadIdx.x == 0) *compacted_counter = carry < batch ? carry : batch;
+}
+
 
 // Pass 1 (first loop of K11, ngp.train.cu:751-802): composite, count the kept samples.
 __global__ void __launch_bounds__(kCtaThreads) loss_pass1_kernel(const __grid_constant__ LossParams p) {
@@ -174,91 +261,198 @@ __global__ void __launch_bounds__(kCtaThreads) loss_pass2_kernel(const __grid_co
     const float4 rr   = p.ray_rgb[i];
     const float3 rgb  = {rr.x, rr.y, rr.z};
     const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
-    const float3 grad = {2.0f * diff.x, 2.0f * diff.y, 2.0f * diff.z};
     if (p.loss_output != nullptr && lane == 0)
         p.loss_output[i] = __fmaf_rn(diff.z, diff.z, __fmaf_rn(diff.x, diff.x, diff.y * diff.y)) / (3.0f * static_cast<float>(p.rays_per_batch));
-    const float scale   = kLossScale / static_cast<float>(p.rays_per_batch);
-    const float* ray    = p.rays + static_cast<uint64_t>(i) * 6u;
-    const float3 origin = {ray[0], ray[1], ray[2]};
-    const float* cin    = p.coords + static_cast<uint64_t>(base) * 7u;
-    const __half* out   = p.network_output + static_cast<uint64_t>(base) * 16u;
-    float* cout         = p.coords_out + static_cast<uint64_t>(cbase) * 7u;
-    __half* dout        = p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u;
-    float T             = 1.0f;
-    float3 acc          = {0.0f, 0.0f, 0.0f};
-    for (uint32_t c0 = 0; c0 < cn; c0 += 32u) {
-        const uint32_t j = c0 + lane;
-        const bool valid = j < cn;
-        float cv[7]      = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        float mr = 0.f, mg = 0.f, mb = 0.f, md = 0.f;
-        if (valid) {
-            const float* c = cin + static_cast<uint64_t>(j) * 7u;
-            float* co      = cout + static_cast<uint64_t>(j) * 7u;
-#pragma unroll
-            for (int q = 0; q < 7; ++q) co[q] = cv[q] = c[q];
-            load_output(out + static_cast<uint64_t>(j) * 16u, mr, mg, mb, md);
+    ray_gradients(rgb, target, kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u,
+                  p.coords + static_cast<uint64_t>(base) * 7u, p.network_output + static_cast<uint64_t>(base) * 16u,
+                  p.coords_out + static_cast<uint64_t>(cbase) * 7u, p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u, cn);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Density-first flow.  Which samples a ray keeps depends only on the densities (the
+// transmittance), so the pre-compaction pass needs only the density network; the colour
+// network then runs on the kept samples alone.  The results are identical to the flow above:
+// the kept set, its order and every network output are the same (each output row is a function
+// of its own input row), so the composited colours, losses and gradients match bit for bit.
+//   1. keep pass: per ray, the kept count from the raw densities (same transmittance loop);
+//   2. one CTA scans the per-CTA totals;
+//   3. copy pass: each ray whose compacted base lies inside the batch copies all its kept
+//      samples (records and encoded positions) to the compacted buffers, which hold
+//      kCompactedRows = batch + kMarchSteps rows, so the ray straddling the batch end is whole;
+//   4. (the caller runs the full network on the compacted rows)
+//   5. loss pass: composite each ray from its compacted outputs, then the gradients of its
+//      samples inside the batch (as pass 2 above).
+// ---------------------------------------------------------------------------------------------
+static_assert(kCompactedRows == kNetworkBatch + kMarchSteps, "compacted rows");
+
+struct KeepParams {
+    uint32_t rays_per_batch;
+    const uint32_t* ray_counter;
+    const __half* density;      // [samples] raw density
+    const float* coords;        // pre-compaction records
+    const __half* enc;          // optional: [32][enc_stride] encoded positions
+    uint32_t enc_stride;
+    uint32_t* numsteps;         // [ray][2] (steps, base) in; (kept, compacted base) out
+    float* coords_out;          // [kCompactedRows][7]
+    __half* enc_out;            // optional: [32][kCompactedRows]
+    uint32_t* kept;             // scratch [ray]
+    uint32_t* steps;            // scratch [ray]: marched samples
+    uint32_t* block_totals;     // scratch [ray blocks]
+};
+
+__device__ __forceinline__ uint32_t keep_rays(const KeepParams& p) {
+    const uint32_t n = p.ray_counter != nullptr ? *p.ray_counter : p.rays_per_batch;
+    return min(n, p.rays_per_batch);
+}
+
+// Step 1 (the transmittance part of pass 1).
+__global__ void __launch_bounds__(kCtaThreads) keep_pass_kernel(const __grid_constant__ KeepParams p) {
+    __shared__ uint32_t s_kept[kRaysPerCta];
+    const uint32_t n    = keep_rays(p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    uint32_t kept       = 0;
+    if (i < n) {
+        const uint32_t steps = p.numsteps[2u * i], base = p.numsteps[2u * i + 1u];
+        const __half* dens   = p.density + base;
+        const float* c       = p.coords + static_cast<uint64_t>(base) * 7u;
+        float T              = 1.0f;
+        for (uint32_t c0 = 0; c0 < steps; c0 += 32u) {
+            const uint32_t j  = c0 + lane;
+            const bool valid  = j < steps;
+            const float d     = valid ? __half2float(dens[j]) : 0.0f;
+            const float dt    = valid ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
+            const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
+            const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+            const bool keep   = valid && !(Tb < kTransmittanceEps);
+            const uint32_t nk = __popc(__ballot_sync(0xFFFFFFFFu, keep));
+            if (nk > 0) T = __shfl_sync(0xFFFFFFFFu, Tb * (1.0f - alpha), nk - 1u);
+            kept += nk;
+            if (nk < min(32u, steps - c0)) break;
         }
-        const float dt     = cv[3];
-        const float3 col   = {sigmoidf_(mr), sigmoidf_(mg), sigmoidf_(mb)};
-        const float alpha  = valid ? 1.0f - __expf(-expf(md) * dt) : 0.0f;
-        const float Tb     = prefix_transmittance(T, 1.0f - alpha);
-        const float weight = alpha * Tb;
-        // colour prefix including this sample, accumulated in sample order
-        float3 a = acc;
-        for (uint32_t q = 0; q < 32u; ++q) {
-            const float wq = __shfl_sync(0xFFFFFFFFu, weight, q);
-            const float cx = __shfl_sync(0xFFFFFFFFu, col.x, q), cy = __shfl_sync(0xFFFFFFFFu, col.y, q), cz = __shfl_sync(0xFFFFFFFFu, col.z, q);
-            if (q <= lane) {
-                a.x = __fmaf_rn(wq, cx, a.x);
-                a.y = __fmaf_rn(wq, cy, a.y);
-                a.z = __fmaf_rn(wq, cz, a.z);
-            }
+        if (lane == 0) {
+            p.kept[i]  = kept;
+            p.steps[i] = steps;
         }
-        const float Ta = Tb * (1.0f - alpha);
-        if (valid) {
-            const float depth   = norm3df(cv[0] - origin.x, cv[1] - origin.y, cv[2] - origin.z);
-            const float3 suffix = {rgb.x - a.x, rgb.y - a.y, rgb.z - a.z};
-            const float g0      = scale * (weight * grad.x * (col.x * (1.0f - col.x)));
-            const float g1      = scale * (weight * grad.y * (col.y * (1.0f - col.y)));
-            const float g2      = scale * (weight * grad.z * (col.z * (1.0f - col.z)));
-            const float dd      = expf(fminf(fmaxf(md, -15.0f), 15.0f));
-            const float sum = __fmaf_rn(grad.z, __fmaf_rn(Ta, col.z, -suffix.z),
-                                        __fmaf_rn(grad.x, __fmaf_rn(Ta, col.x, -suffix.x), grad.y * __fmaf_rn(Ta, col.y, -suffix.y)));
-            const float g3 = __fmaf_rn(scale, dd * (dt * sum), (md > -10.0f && depth < 0.1f) ? 1e-4f : 0.0f);
-            uint4* d       = reinterpret_cast<uint4*>(dout + static_cast<uint64_t>(j) * 16u);
-            __half2 h01 = __floats2half2_rn(g0, g1), h23 = __floats2half2_rn(g2, g3);
-            d[0]        = make_uint4(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23), 0u, 0u);
-            d[1]        = make_uint4(0u, 0u, 0u, 0u);
-        }
-        const uint32_t last = min(31u, cn - 1u - c0);
-        T                   = __shfl_sync(0xFFFFFFFFu, Ta, last);
-        acc.x               = __shfl_sync(0xFFFFFFFFu, a.x, last);
-        acc.y               = __shfl_sync(0xFFFFFFFFu, a.y, last);
-        acc.z               = __shfl_sync(0xFFFFFFFFu, a.z, last);
+    }
+    if (lane == 0) s_kept[warp] = kept;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t total = 0;
+        for (uint32_t w = 0; w < kRaysPerCta; ++w) total += s_kept[w];
+        p.block_totals[blockIdx.x] = total;
     }
 }
 
-__global__ void __launch_bounds__(1024) scan_kept_kernel(uint32_t* __restrict__ totals, uint32_t n_blocks, uint32_t* __restrict__ compacted_counter,
-                                                         uint32_t batch) {
-    uint32_t carry = 0;
-    for (uint32_t b = 0; b < n_blocks; b += 1024u) {
-        const uint32_t k = b + threadIdx.x;
-        const uint32_t v = k < n_blocks ? totals[k] : 0u;
-        uint32_t sum;
-        const uint32_t ex = block_exclusive_scan(v, sum);
-        if (k < n_blocks) totals[k] = carry + ex;
-        carry += sum;
+// Step 3.
+__global__ void __launch_bounds__(kCtaThreads) compact_copy_kernel(const __grid_constant__ KeepParams p) {
+    const uint32_t n    = keep_rays(p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    uint32_t cbase      = p.block_totals[blockIdx.x];
+    for (uint32_t w = 0; w < warp; ++w) {
+        const uint32_t q = blockIdx.x * kRaysPerCta + w;
+        cbase += q < n ? p.kept[q] : 0u;
     }
-    if (threadIdx.x == 0) *compacted_counter = carry < batch ? carry : batch;
+    if (i >= n) return;
+    const uint32_t k    = cbase < kNetworkBatch ? p.kept[i] : 0u;
+    const uint32_t base = p.numsteps[2u * i + 1u];
+    __syncwarp();
+    if (lane == 0) {
+        p.numsteps[2u * i]      = k;
+        p.numsteps[2u * i + 1u] = cbase;
+    }
+    const float* cin = p.coords + static_cast<uint64_t>(base) * 7u;
+    float* cout      = p.coords_out + static_cast<uint64_t>(cbase) * 7u;
+    for (uint32_t j = lane; j < k * 7u; j += 32u) cout[j] = cin[j];
+    if (p.enc_out != nullptr) {
+        for (uint32_t j = lane; j < k; j += 32u)
+#pragma unroll 8
+            for (uint32_t f = 0; f < 32u; ++f)
+                p.enc_out[static_cast<uint64_t>(f) * kCompactedRows + cbase + j] = p.enc[static_cast<uint64_t>(f) * p.enc_stride + base + j];
+    }
+}
+
+struct CompactedLossParams {
+    uint32_t rays_per_batch;
+    uint32_t step;
+    const uint32_t* ray_counter;
+    const uint8_t* pixels;
+    uint32_t frame_count, width, height;
+    const __half* output;          // [kCompactedRows][16] network output of the compacted rows
+    const uint32_t* ray_indices;
+    const float* rays;
+    uint32_t* numsteps;            // (kept, compacted base) in; (samples in the batch, base) out
+    const float* coords;           // compacted records
+    __half* dloss_doutput;         // [batch][16]
+    float* loss_output;
+    const uint32_t* steps;         // scratch from the keep pass
+};
+
+// Step 5: pass 1's compositing over the compacted outputs, then pass 2.
+__global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __grid_constant__ CompactedLossParams p) {
+    const uint32_t n    = min(p.ray_counter != nullptr ? *p.ray_counter : p.rays_per_batch, p.rays_per_batch);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    if (i >= n) return;
+    const uint32_t k     = p.numsteps[2u * i];
+    const uint32_t cbase = p.numsteps[2u * i + 1u];
+    const uint32_t cn    = cbase < kNetworkBatch ? min(k, kNetworkBatch - cbase) : 0u;
+    __syncwarp();
+    if (lane == 0) p.numsteps[2u * i] = cn;
+    if (cn == 0) return;
+    const __half* out = p.output + static_cast<uint64_t>(cbase) * 16u;
+    const float* cin  = p.coords + static_cast<uint64_t>(cbase) * 7u;
+
+    // composite the k kept samples (pass 1)
+    float T    = 1.0f;
+    float3 rgb = {0.0f, 0.0f, 0.0f};
+    for (uint32_t c0 = 0; c0 < k; c0 += 32u) {
+        const uint32_t j = c0 + lane;
+        const bool valid = j < k;
+        float r = 0.f, g = 0.f, b = 0.f, d = 0.f, dt = 0.f;
+        if (valid) {
+            load_output(out + static_cast<uint64_t>(j) * 16u, r, g, b, d);
+            dt = cin[static_cast<uint64_t>(j) * 7u + 3u];
+        }
+        const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
+        const float3 col  = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
+        const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+        const uint32_t nk = min(32u, k - c0);
+        const float w     = alpha * Tb;
+        for (uint32_t q = 0; q < nk; ++q) {
+            const float wq = __shfl_sync(0xFFFFFFFFu, w, q);
+            rgb.x          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.x, q), rgb.x);
+            rgb.y          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.y, q), rgb.y);
+            rgb.z          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.z, q), rgb.z);
+        }
+        T = __shfl_sync(0xFFFFFFFFu, Tb * (1.0f - alpha), nk - 1u);
+    }
+    float3 bg, target;
+    ray_target(p.step, p.rays_per_batch, p.pixels, p.frame_count, p.width, p.height, p.ray_indices != nullptr ? p.ray_indices[i] : i, bg, target);
+    if (k == p.steps[i]) {
+        rgb.x = __fmaf_rn(T, bg.x, rgb.x);
+        rgb.y = __fmaf_rn(T, bg.y, rgb.y);
+        rgb.z = __fmaf_rn(T, bg.z, rgb.z);
+    }
+    const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
+    if (p.loss_output != nullptr && lane == 0)
+        p.loss_output[i] = __fmaf_rn(diff.z, diff.z, __fmaf_rn(diff.x, diff.x, diff.y * diff.y)) / (3.0f * static_cast<float>(p.rays_per_batch));
+    ray_gradients(rgb, target, kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u, cin, out, nullptr,
+                  p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u, cn);
 }
 
 // K12 + K13 (ngp.train.cu:862-874): fill the batch tail [n, batch) by wrap-around copies of the
 // first n samples; the copied gradients are scaled by n / batch.
-__global__ void pad_batch_kernel(const uint32_t* __restrict__ count, float* __restrict__ coords, __half* __restrict__ dloss, uint32_t batch) {
+__global__ void pad_batch_kernel(const uint32_t* __restrict__ count, float* __restrict__ coords, __half* __restrict__ dloss, uint32_t batch,
+                                 __half* __restrict__ enc, uint32_t enc_stride) {
     const uint32_t n = *count;
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;  // row of the batch
     if (n == 0 || r < n || r >= batch) return;
     const uint32_t src = r % n;
+    if (enc != nullptr)
+#pragma unroll 8
+        for (uint32_t f = 0; f < 32u; ++f) enc[static_cast<uint64_t>(f) * enc_stride + r] = enc[static_cast<uint64_t>(f) * enc_stride + src];
 #pragma unroll
     for (int q = 0; q < 7; ++q) coords[static_cast<uint64_t>(r) * 7u + q] = coords[static_cast<uint64_t>(src) * 7u + q];
     const float s = static_cast<float>(n) / static_cast<float>(batch);
@@ -383,11 +577,90 @@ extern "C" int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t s
     return check_launch("loss_pass2_kernel");
 }
 
+extern "C" uint32_t ngp_compacted_rows(void) { return kCompactedRows; }
+
+extern "C" int ngp_training_compact_by_density(uint32_t rays_per_batch, const uint32_t* ray_counter, const uint16_t* density, const float* coords,
+                                               const uint16_t* enc, uint32_t enc_stride, uint32_t* numsteps, float* compacted_coords,
+                                               uint16_t* compacted_enc, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
+                                               void* stream) {
+    clear_error();
+    if (rays_per_batch == 0) return NGP_OK;
+    if (density == nullptr || coords == nullptr || numsteps == nullptr || compacted_coords == nullptr || compacted_counter == nullptr ||
+        scratch == nullptr || (compacted_enc != nullptr && enc == nullptr))
+        return fail(NGP_ERR_INVALID, "compact by density: invalid input");
+    if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "compact by density: scratch too small");
+    if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "compact by density: scratch must be 16-byte aligned");
+    const cudaStream_t s  = as_stream(stream);
+    const uint32_t blocks = (rays_per_batch + kRaysPerCta - 1) / kRaysPerCta;
+    unsigned char* sc     = static_cast<unsigned char*>(scratch);
+    KeepParams p{};
+    p.rays_per_batch = rays_per_batch;
+    p.ray_counter    = ray_counter;
+    p.density        = reinterpret_cast<const __half*>(density);
+    p.coords         = coords;
+    p.enc            = reinterpret_cast<const __half*>(enc);
+    p.enc_stride     = enc_stride;
+    p.numsteps       = numsteps;
+    p.coords_out     = compacted_coords;
+    p.enc_out        = reinterpret_cast<__half*>(compacted_enc);
+    p.steps          = reinterpret_cast<uint32_t*>(sc);
+    p.kept           = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(rays_per_batch) * 4u);
+    p.block_totals   = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(rays_per_batch) * 20u);
+    keep_pass_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
+    NGP_TRY(check_launch("keep_pass_kernel"));
+    scan_kept_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, compacted_counter, kNetworkBatch);
+    NGP_TRY(check_launch("scan_kept_kernel"));
+    compact_copy_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
+    return check_launch("compact_copy_kernel");
+}
+
+extern "C" int ngp_training_loss_compacted(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                           uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* compacted_output,
+                                           const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* compacted_coords,
+                                           uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, void* stream) {
+    clear_error();
+    if (rays_per_batch == 0) return NGP_OK;
+    if (pixels == nullptr || compacted_output == nullptr || rays == nullptr || numsteps == nullptr || compacted_coords == nullptr ||
+        dloss_doutput == nullptr || scratch == nullptr || frame_count == 0 || width == 0 || height == 0)
+        return fail(NGP_ERR_INVALID, "compacted loss: invalid input");
+    if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "compacted loss: scratch too small");
+    const cudaStream_t s = as_stream(stream);
+    CompactedLossParams p{};
+    p.rays_per_batch = rays_per_batch;
+    p.step           = step;
+    p.ray_counter    = ray_counter;
+    p.pixels         = pixels;
+    p.frame_count    = frame_count;
+    p.width          = width;
+    p.height         = height;
+    p.output         = reinterpret_cast<const __half*>(compacted_output);
+    p.ray_indices    = ray_indices;
+    p.rays           = rays;
+    p.numsteps       = numsteps;
+    p.coords         = compacted_coords;
+    p.dloss_doutput  = reinterpret_cast<__half*>(dloss_doutput);
+    p.loss_output    = loss_values;
+    p.steps          = static_cast<const uint32_t*>(scratch);
+    if (loss_values != nullptr) NGP_TRY(check_cuda(cudaMemsetAsync(loss_values, 0, sizeof(float) * rays_per_batch, s), "compacted loss: clear"));
+    loss_compacted_kernel<<<(rays_per_batch + kRaysPerCta - 1) / kRaysPerCta, kCtaThreads, 0, s>>>(p);
+    return check_launch("loss_compacted_kernel");
+}
+
 extern "C" int ngp_pad_training_batch(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, void* stream) {
     clear_error();
     if (compacted_counter == nullptr || compacted_coords == nullptr || dloss_doutput == nullptr) return fail(NGP_ERR_INVALID, "pad batch: null pointer");
     pad_batch_kernel<<<kNetworkBatch / 256u, 256, 0, as_stream(stream)>>>(compacted_counter, compacted_coords, reinterpret_cast<__half*>(dloss_doutput),
-                                                                            kNetworkBatch);
+                                                                            kNetworkBatch, nullptr, 0u);
+    return check_launch("pad_batch_kernel");
+}
+
+extern "C" int ngp_pad_training_batch_enc(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, uint16_t* enc,
+                                          uint32_t enc_stride, void* stream) {
+    clear_error();
+    if (compacted_counter == nullptr || compacted_coords == nullptr || dloss_doutput == nullptr || enc == nullptr || enc_stride < kNetworkBatch)
+        return fail(NGP_ERR_INVALID, "pad batch: invalid input");
+    pad_batch_kernel<<<kNetworkBatch / 256u, 256, 0, as_stream(stream)>>>(compacted_counter, compacted_coords, reinterpret_cast<__half*>(dloss_doutput),
+                                                                            kNetworkBatch, reinterpret_cast<__half*>(enc), enc_stride);
     return check_launch("pad_batch_kernel");
 }
 

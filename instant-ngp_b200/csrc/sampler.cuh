@@ -13,6 +13,8 @@ namespace ngp {
 constexpr uint32_t kGridSize      = 128u;
 constexpr uint32_t kGridCells     = kGridSize * kGridSize * kGridSize;
 constexpr uint32_t kMarchSteps    = 1024u;
+// rows of the compacted training buffers: the batch plus one whole ray straddling its end
+constexpr uint32_t kCompactedRows = (1u << 18) + kMarchSteps;
 constexpr float kConeStep         = 1.73205080757f / 1024.0f;  // sqrt(3) / NERF_STEPS
 constexpr uint32_t kRandPerRay    = 16u;                       // MAX_RANDOM_SAMPLES_PER_RAY
 constexpr float kMinOpticalThick  = 0.01f;

@@ -74,14 +74,15 @@ struct ngp_trainer {
     uint32_t *ray_indices = nullptr, *numsteps = nullptr, *march_scratch = nullptr;
     uint32_t* counters     = nullptr;  // 0 rays, 1 samples, 2 compacted
     uint16_t* enc          = nullptr;  // [32][MAX_SAMPLES] encoded positions
-    uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output
+    uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output (training: raw densities)
+    uint16_t* cout         = nullptr;  // [COMPACTED_ROWS][16] network output of the compacted samples
     uint16_t* grid_density = nullptr;  // [2^21] raw density of the grid samples
-    float* ccoords         = nullptr;  // [BATCH][7] compacted
+    float* ccoords         = nullptr;  // [COMPACTED_ROWS][7] compacted
     uint16_t* dloss        = nullptr;  // [BATCH][16]
     float* loss_values     = nullptr;  // [BATCH]
     unsigned char* loss_scratch = nullptr;
     size_t loss_scratch_bytes   = 0;
-    uint16_t* cenc   = nullptr;  // [32][BATCH] encoded compacted batch
+    uint16_t* cenc   = nullptr;  // [32][COMPACTED_ROWS] encoded compacted samples
     uint16_t* denc   = nullptr;  // [32][BATCH] dL/d(encoding)
     float* mlp_scratch        = nullptr;
     size_t mlp_scratch_floats = 0;
@@ -131,7 +132,7 @@ void destroy(ngp_trainer* t) {
     free_split(t->test);
     void* ptrs[] = {t->master, t->params, t->grads, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
                     t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
-                    t->counters, t->enc, t->out, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
+                    t->counters, t->enc, t->out, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison};
     for (void* p : ptrs) cudaFree(p);
     if (t->comm) ncclCommDestroy(t->comm);
@@ -284,23 +285,27 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     }
     const uint32_t rng_step = t->step * static_cast<uint32_t>(t->world) + static_cast<uint32_t>(t->rank);
     mark(t, 2);
-    // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524)
+    // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524): only the density
+    // network is needed to decide which samples each ray keeps
     NGP_TRY(encode(t, t->inference_samples, t->coords, t->enc, t->inference_samples));
     mark(t, 3);
-    NGP_TRY(ngp_mlp_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->coords, 7, t->out, nullptr, t->stream));
+    NGP_TRY(ngp_density_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->out, t->stream));
     mark(t, 4);
-    // compositing, loss, compaction, padding (ngp.train.cu:1932-1956)
-    NGP_TRY(ngp_training_loss_and_compact(t->rays_per_batch, rng_step, t->counters + 0, s.pixels, s.frames, s.width, s.height, t->out,
-                                          t->counters + 2, t->ray_indices, t->rays, t->numsteps, t->coords, t->ccoords, t->dloss,
-                                          t->loss_values, t->loss_scratch, t->loss_scratch_bytes, t->stream));
-    NGP_TRY(ngp_pad_training_batch(t->counters + 2, t->ccoords, t->dloss, t->stream));
+    // compaction (ngp.train.cu:1932-1944): the kept samples' records and encodings
+    NGP_TRY(ngp_training_compact_by_density(t->rays_per_batch, t->counters + 0, t->out, t->coords, t->enc, t->inference_samples, t->numsteps,
+                                            t->ccoords, t->cenc, t->counters + 2, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    mark(t, 5);
+    // the full network on the compacted rows, then compositing, loss and padding (1944-1956)
+    NGP_TRY(ngp_mlp_forward(kCompactedRows, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->cout, nullptr, t->stream));
+    NGP_TRY(ngp_training_loss_compacted(t->rays_per_batch, rng_step, t->counters + 0, s.pixels, s.frames, s.width, s.height, t->cout, t->ray_indices,
+                                        t->rays, t->numsteps, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->loss_scratch_bytes,
+                                        t->stream));
+    NGP_TRY(ngp_pad_training_batch_enc(t->counters + 2, t->ccoords, t->dloss, t->cenc, kCompactedRows, t->stream));
     NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, t->counters, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
     NGP_TRY(check_cuda(cudaEventRecord(t->ev_counts, t->stream), "record counters"));
-    mark(t, 5);
-    // encoding of the batch, fused MLP backward (recompute), encoding backward
-    NGP_TRY(encode(t, kNetworkBatch, t->ccoords, t->cenc, kNetworkBatch));
     mark(t, 6);
-    NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kNetworkBatch, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
+    // fused MLP backward (recompute) and encoding backward on the batch
+    NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
                              t->mlp_scratch_floats, t->grads, nullptr, 1.0f, t->stream));
     mark(t, 7);
     NGP_TRY(ngp_encode_grid_backward(&t->layout, kNetworkBatch, t->ccoords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams, t->stream));
@@ -456,12 +461,13 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
         NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));
         NGP_TRY(dalloc(t->grid_density, kGridCells, "grid density"));
-        NGP_TRY(dalloc(t->ccoords, static_cast<size_t>(kNetworkBatch) * 7u, "compacted coords"));
+        NGP_TRY(dalloc(t->ccoords, static_cast<size_t>(kCompactedRows) * 7u, "compacted coords"));
+        NGP_TRY(dalloc(t->cout, static_cast<size_t>(kCompactedRows) * 16u, "compacted network output"));
         NGP_TRY(dalloc(t->dloss, static_cast<size_t>(kNetworkBatch) * 16u, "output gradients"));
         NGP_TRY(dalloc(t->loss_values, kNetworkBatch, "loss values"));
         t->loss_scratch_bytes = ngp_loss_scratch_bytes(kNetworkBatch);
         NGP_TRY(dalloc(t->loss_scratch, t->loss_scratch_bytes, "loss scratch"));
-        NGP_TRY(dalloc(t->cenc, static_cast<size_t>(kNetworkBatch) * 32u, "batch encoding"));
+        NGP_TRY(dalloc(t->cenc, static_cast<size_t>(kCompactedRows) * 32u, "batch encoding"));
         NGP_TRY(dalloc(t->denc, static_cast<size_t>(kNetworkBatch) * 32u, "encoding gradient"));
         t->mlp_scratch_floats = ngp_mlp_backward_scratch_floats();
         NGP_TRY(dalloc(t->mlp_scratch, t->mlp_scratch_floats, "mlp scratch"));

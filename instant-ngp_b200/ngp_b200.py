@@ -273,6 +273,33 @@ def pad_training_batch(compacted_counter, compacted_coords, dloss_doutput, strea
            "ngp_pad_training_batch")
 
 
+def compacted_rows() -> int:
+    lib().ngp_compacted_rows.restype = ctypes.c_uint32
+    return int(lib().ngp_compacted_rows())
+
+
+def training_compact_by_density(rays_per_batch, ray_counter, density, coords, numsteps, compacted_coords, compacted_counter, scratch,
+                                enc=None, enc_stride=0, compacted_enc=None, stream=None) -> None:
+    _check(lib().ngp_training_compact_by_density(_u32(rays_per_batch), _ptr(ray_counter), _ptr(density), _ptr(coords), _ptr(enc), _u32(enc_stride),
+                                                 _ptr(numsteps), _ptr(compacted_coords), _ptr(compacted_enc), _ptr(compacted_counter),
+                                                 _ptr(scratch), ctypes.c_size_t(scratch.numel() * scratch.element_size()), _stream(stream)),
+           "ngp_training_compact_by_density")
+
+
+def training_loss_compacted(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, compacted_output, ray_indices, rays,
+                            numsteps, compacted_coords, dloss_doutput, loss_values, scratch, stream=None) -> None:
+    _check(lib().ngp_training_loss_compacted(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),
+                                             _u32(height), _ptr(compacted_output), _ptr(ray_indices), _ptr(rays), _ptr(numsteps),
+                                             _ptr(compacted_coords), _ptr(dloss_doutput), _ptr(loss_values), _ptr(scratch),
+                                             ctypes.c_size_t(scratch.numel() * scratch.element_size()), _stream(stream)),
+           "ngp_training_loss_compacted")
+
+
+def pad_training_batch_enc(compacted_counter, compacted_coords, dloss_doutput, enc, enc_stride, stream=None) -> None:
+    _check(lib().ngp_pad_training_batch_enc(_ptr(compacted_counter), _ptr(compacted_coords), _ptr(dloss_doutput), _ptr(enc), _u32(enc_stride),
+                                            _stream(stream)), "ngp_pad_training_batch_enc")
+
+
 def eval_composite(n_pixels, pixel_offset, image, width, height, pixels, numsteps, coords, network_output, sse=None, comparison=None,
                    rendered=None, stream=None) -> None:
     _check(lib().ngp_eval_composite(_u32(n_pixels), _u32(pixel_offset), _u32(image), _u32(width), _u32(height), _ptr(pixels), _ptr(numsteps),
@@ -432,7 +459,7 @@ class InstantNGP:
         p = np.ascontiguousarray(params, np.float32)
         _check(lib().ngp_trainer_set_params(self.handle, ctypes.c_void_p(p.ctypes.data), _u32(p.size)), "ngp_trainer_set_params")
 
-    PHASES = ("grid_update", "march", "encode_fwd_inference", "mlp_fwd_inference", "loss_compact_pad", "encode_fwd_batch", "mlp_bwd",
+    PHASES = ("grid_update", "march", "encode_fwd_inference", "density_fwd_inference", "compact", "mlp_fwd_loss_pad", "mlp_bwd",
               "encode_bwd", "allreduce", "adam")
 
     def set_profiling(self, enable: bool = True) -> None:

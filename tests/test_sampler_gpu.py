@@ -386,3 +386,77 @@ def test_training_loss_vs_reference_kernel(ngp, reflib, small_scene, blob_bitfie
         assert rcc[a: a + c].tobytes() == oc[b: b + c].tobytes()
         x, y = od[b: b + c, :4], rd[a: a + c, :4]
         assert (np.abs(x - y) <= 2e-3 * np.abs(y) + 1e-7).all(), j
+
+
+def test_density_first_flow_matches_loss_and_compact(ngp, small_scene, blob_bitfield):
+    """The trainer's density-first flow (density network on every sample, compaction, full network
+    on the compacted rows, loss) against the one-pass entry point given the full network's
+    outputs: counts, compacted records, encodings (after padding), gradients and losses
+    bit-identical, including the ray that straddles the end of the 2^18 batch."""
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    bits = T(blob_bitfield)
+    n, limit, step, batch = 12288, 1 << 21, 5, 1 << 18
+    rows = ngp.compacted_rows()
+    assert rows == batch + 1024
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    layout = ngp.grid_layout(16, 2, 19, 16, math.log2(128.0) / 15.0)
+    _, table, _ = workloads.encode_inputs(1, layout.n_params, 16, 2, seed=4)
+    table = (table.astype(np.float32) * 2e4).astype(np.float16)  # densities that end rays early
+    table_t = T(table.view(np.int16))
+    params = T(workloads.xavier_mlp_params(9).view(np.int16))
+    ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    ridx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    msc = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
+    rc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, coords, rays, ridx, ns, msc, rc, sc)
+    torch.cuda.synchronize()
+    total = int(sc.item())
+    m = (total + 127) // 128 * 128
+    assert total > 2 * batch
+    enc = torch.zeros((32, m), dtype=torch.float16, device="cuda")
+    ngp.encode_grid_forward(layout, coords, table_t, enc, n=m, coord_stride=7, out_stride=m)
+    scratch = torch.zeros(ngp.loss_scratch_bytes(n), dtype=torch.uint8, device="cuda")
+    # one-pass flow
+    out = torch.zeros((m, 16), dtype=torch.float16, device="cuda")
+    ngp.mlp_forward(params, enc, coords, out, n=m, x_stride=m)
+    ns_a = ns.clone()
+    cc_a = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ccoords_a = torch.zeros((batch, 7), dtype=torch.float32, device="cuda")
+    dloss_a = torch.zeros((batch, 16), dtype=torch.float16, device="cuda")
+    loss_a = torch.zeros(n, dtype=torch.float32, device="cuda")
+    ngp.training_loss_and_compact(n, step, rc, pix, F, W, H, out, cc_a, ridx, rays, ns_a, coords, ccoords_a, dloss_a, loss_a, scratch)
+    ngp.pad_training_batch(cc_a, ccoords_a, dloss_a)
+    cenc_a = torch.zeros((32, batch), dtype=torch.float16, device="cuda")
+    ngp.encode_grid_forward(layout, ccoords_a, table_t, cenc_a, n=batch, coord_stride=7, out_stride=batch)
+    # density-first flow
+    dens = torch.zeros(m, dtype=torch.float16, device="cuda")
+    ngp.density_forward(params, enc, dens, n=m, x_stride=m)
+    ns_b = ns.clone()
+    cc_b = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ccoords_b = torch.zeros((rows, 7), dtype=torch.float32, device="cuda")
+    cenc_b = torch.zeros((32, rows), dtype=torch.float16, device="cuda")
+    ngp.training_compact_by_density(n, rc, dens, coords, ns_b, ccoords_b, cc_b, scratch, enc=enc, enc_stride=m, compacted_enc=cenc_b)
+    cout = torch.zeros((rows, 16), dtype=torch.float16, device="cuda")
+    ngp.mlp_forward(params, cenc_b, ccoords_b, cout, n=rows, x_stride=rows)
+    dloss_b = torch.zeros((batch, 16), dtype=torch.float16, device="cuda")
+    loss_b = torch.zeros(n, dtype=torch.float32, device="cuda")
+    ngp.training_loss_compacted(n, step, rc, pix, F, W, H, cout, ridx, rays, ns_b, ccoords_b, dloss_b, loss_b, scratch)
+    ngp.pad_training_batch_enc(cc_b, ccoords_b, dloss_b, cenc_b, rows)
+    torch.cuda.synchronize()
+    assert int(cc_a.item()) == int(cc_b.item()) == batch
+    assert (ns_a.cpu().numpy() == ns_b.cpu().numpy()).all()
+    kept = ns_a.cpu().numpy()[:, 0]
+    assert 0 < (kept > 0).sum() < n  # rays beyond the batch end were dropped
+    assert ccoords_a.cpu().numpy().tobytes() == ccoords_b[:batch].cpu().numpy().tobytes()
+    assert dloss_a.cpu().numpy().view(np.uint16).tobytes() == dloss_b.cpu().numpy().view(np.uint16).tobytes()
+    assert loss_a.cpu().numpy().tobytes() == loss_b.cpu().numpy().tobytes()
+    assert cenc_a.cpu().numpy().view(np.uint16).tobytes() == cenc_b[:, :batch].cpu().numpy().view(np.uint16).tobytes()
+    # some rays stopped early (transmittance), so the flow's keep decision was exercised
+    steps = ns.cpu().numpy()[:, 0]
+    assert (kept[kept > 0] < steps[kept > 0]).any()
