@@ -362,14 +362,20 @@ __global__ void __launch_bounds__(kCtaThreads) compact_copy_kernel(const __grid_
         p.numsteps[2u * i]      = k;
         p.numsteps[2u * i + 1u] = cbase;
     }
-    const float* cin = p.coords + static_cast<uint64_t>(base) * 7u;
-    float* cout      = p.coords_out + static_cast<uint64_t>(cbase) * 7u;
-    for (uint32_t j = lane; j < k * 7u; j += 32u) cout[j] = cin[j];
+    const float* __restrict__ cin = p.coords + static_cast<uint64_t>(base) * 7u;
+    float* __restrict__ cout      = p.coords_out + static_cast<uint64_t>(cbase) * 7u;
+    for (uint32_t j = lane; j < k * 7u; j += 32u) cout[j] = __ldg(cin + j);
     if (p.enc_out != nullptr) {
-        for (uint32_t j = lane; j < k; j += 32u)
-#pragma unroll 8
-            for (uint32_t f = 0; f < 32u; ++f)
-                p.enc_out[static_cast<uint64_t>(f) * kCompactedRows + cbase + j] = p.enc[static_cast<uint64_t>(f) * p.enc_stride + base + j];
+        // all 32 features of a sample are loaded before any is stored (independent loads in flight)
+        const unsigned short* __restrict__ src = reinterpret_cast<const unsigned short*>(p.enc) + base;
+        unsigned short* __restrict__ dst       = reinterpret_cast<unsigned short*>(p.enc_out) + cbase;
+        for (uint32_t j = lane; j < k; j += 32u) {
+            unsigned short v[32];
+#pragma unroll
+            for (uint32_t f = 0; f < 32u; ++f) v[f] = __ldg(src + static_cast<uint64_t>(f) * p.enc_stride + j);
+#pragma unroll
+            for (uint32_t f = 0; f < 32u; ++f) dst[static_cast<uint64_t>(f) * kCompactedRows + j] = v[f];
+        }
     }
 }
 
