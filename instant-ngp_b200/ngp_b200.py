@@ -12,10 +12,11 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
-LIB_PATH = PKG_DIR / "libngp_b200.so"
+LIB_PATH = Path(os.environ["NGP_B200_LIB"]) if os.environ.get("NGP_B200_LIB") else PKG_DIR / "libngp_b200.so"
 
 MAX_LEVELS = 32
 SAMPLE_FLOATS = 7
