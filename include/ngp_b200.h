@@ -284,6 +284,18 @@ NGP_API int ngp_adam_step(uint32_t n_params, uint32_t n_mlp, float lr, float bet
                           float* params_full_precision, uint16_t* params, float* gradients, float* first_moments, float* second_moments,
                           uint32_t* param_steps, int clear_grid_gradients, void* stream);
 
+/* The bias-corrected rate lr * sqrt(1 - beta2^t) / (1 - beta1^t) for t in [first, first + count)
+ * -> table[t].  With such a table, ngp_adam_step_table reads the rate of each parameter's step
+ * count instead of evaluating two powf per parameter (same values: the same function of t). */
+NGP_API int ngp_adam_lr_table(float* table, uint32_t first, uint32_t count, float lr, float beta1, float beta2, void* stream);
+
+/* ngp_adam_step using lr_table[1 .. table_len] (filled by ngp_adam_lr_table with the same lr and
+ * betas); step counts beyond table_len fall back to computing the rate. */
+NGP_API int ngp_adam_step_table(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg,
+                                float loss_scale, float* params_full_precision, uint16_t* params, float* gradients, float* first_moments,
+                                float* second_moments, uint32_t* param_steps, int clear_grid_gradients, const float* lr_table,
+                                uint32_t table_len, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Trainer: the reference's ngp::train::InstantNGP (ngp.train.ixx:40-53) as an opaque handle.
  * ------------------------------------------------------------------------------------------ */

@@ -25,7 +25,14 @@ struct AdamParams {
     float* v;
     uint32_t* steps;
     int clear_grid_grad;
+    const float* lr_table;  // optional: lr_table[t] = bias-corrected rate after t steps, t <= table_len
+    uint32_t table_len;
 };
+
+// Bias-corrected learning rate after `step` steps (ngp.train.cu:1275).
+__device__ __forceinline__ float corrected_lr(float lr, float beta1, float beta2, uint32_t step) {
+    return lr * sqrtf(1.0f - powf(beta2, static_cast<float>(step))) / (1.0f - powf(beta1, static_cast<float>(step)));
+}
 
 __device__ __forceinline__ void adam_one(const AdamParams& p, uint32_t i, float& master, float graw, float& m, float& v, uint32_t& step,
                                          __half& out) {
@@ -36,7 +43,9 @@ __device__ __forceinline__ void adam_one(const AdamParams& p, uint32_t i, float&
     m = __fmaf_rn(p.beta1, m, (1.0f - p.beta1) * g);
     v = __fmaf_rn(p.beta2, v, (1.0f - p.beta2) * (g * g));
     step += 1u;
-    const float lr_t = p.lr * sqrtf(1.0f - powf(p.beta2, static_cast<float>(step))) / (1.0f - powf(p.beta1, static_cast<float>(step)));
+    // the rate depends only on the step count: read it from the table (the same function
+    // evaluated once per step count) instead of two powf per parameter
+    const float lr_t = step <= p.table_len ? __ldg(p.lr_table + step) : corrected_lr(p.lr, p.beta1, p.beta2, step);
     master           = w - lr_t * m / (sqrtf(v) + p.eps);
     out              = __float2half_rn(master);
 }
@@ -73,6 +82,29 @@ __global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamP
     }
 }
 
+__global__ void lr_table_kernel(float* __restrict__ table, uint32_t first, uint32_t count, float lr, float beta1, float beta2) {
+    const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k < count) table[first + k] = corrected_lr(lr, beta1, beta2, first + k);
+}
+
+int adam_launch(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg, float loss_scale,
+                float* params_full_precision, uint16_t* params, float* gradients, float* first_moments, float* second_moments,
+                uint32_t* param_steps, int clear_grid_gradients, const float* lr_table, uint32_t table_len, void* stream) {
+    if (n_params == 0) return NGP_OK;
+    if (params_full_precision == nullptr || params == nullptr || gradients == nullptr || first_moments == nullptr || second_moments == nullptr ||
+        param_steps == nullptr || n_mlp > n_params || n_mlp % 4u != 0 || loss_scale == 0.0f || (table_len > 0 && lr_table == nullptr))
+        return fail(NGP_ERR_INVALID, "adam: invalid input");
+    if ((reinterpret_cast<uintptr_t>(params_full_precision) | reinterpret_cast<uintptr_t>(gradients) | reinterpret_cast<uintptr_t>(first_moments) |
+         reinterpret_cast<uintptr_t>(second_moments) | reinterpret_cast<uintptr_t>(param_steps)) % 16u != 0 ||
+        reinterpret_cast<uintptr_t>(params) % 8u != 0)
+        return fail(NGP_ERR_INVALID, "adam: buffers must be 16-byte aligned (fp16 copy 8-byte)");
+    AdamParams p{n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, 1.0f / loss_scale, params_full_precision, reinterpret_cast<__half*>(params),
+                 gradients, first_moments, second_moments, param_steps, clear_grid_gradients, lr_table, table_len};
+    const uint32_t groups = (n_params + 3u) / 4u;
+    adam_kernel<<<(groups + 255u) / 256u, 256, 0, as_stream(stream)>>>(p);
+    return check_launch("adam_kernel");
+}
+
 }  // namespace
 }  // namespace ngp
 
@@ -82,17 +114,23 @@ extern "C" int ngp_adam_step(uint32_t n_params, uint32_t n_mlp, float lr, float 
                              float* params_full_precision, uint16_t* params, float* gradients, float* first_moments, float* second_moments,
                              uint32_t* param_steps, int clear_grid_gradients, void* stream) {
     clear_error();
-    if (n_params == 0) return NGP_OK;
-    if (params_full_precision == nullptr || params == nullptr || gradients == nullptr || first_moments == nullptr || second_moments == nullptr ||
-        param_steps == nullptr || n_mlp > n_params || n_mlp % 4u != 0 || loss_scale == 0.0f)
-        return fail(NGP_ERR_INVALID, "adam: invalid input");
-    if ((reinterpret_cast<uintptr_t>(params_full_precision) | reinterpret_cast<uintptr_t>(gradients) | reinterpret_cast<uintptr_t>(first_moments) |
-         reinterpret_cast<uintptr_t>(second_moments) | reinterpret_cast<uintptr_t>(param_steps)) % 16u != 0 ||
-        reinterpret_cast<uintptr_t>(params) % 8u != 0)
-        return fail(NGP_ERR_INVALID, "adam: buffers must be 16-byte aligned (fp16 copy 8-byte)");
-    AdamParams p{n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, 1.0f / loss_scale, params_full_precision, reinterpret_cast<__half*>(params),
-                 gradients, first_moments, second_moments, param_steps, clear_grid_gradients};
-    const uint32_t groups = (n_params + 3u) / 4u;
-    adam_kernel<<<(groups + 255u) / 256u, 256, 0, as_stream(stream)>>>(p);
-    return check_launch("adam_kernel");
+    return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, gradients, first_moments,
+                       second_moments, param_steps, clear_grid_gradients, nullptr, 0u, stream);
+}
+
+extern "C" int ngp_adam_lr_table(float* table, uint32_t first, uint32_t count, float lr, float beta1, float beta2, void* stream) {
+    clear_error();
+    if (count == 0) return NGP_OK;
+    if (table == nullptr) return fail(NGP_ERR_INVALID, "adam lr table: null table");
+    lr_table_kernel<<<(count + 255u) / 256u, 256, 0, as_stream(stream)>>>(table, first, count, lr, beta1, beta2);
+    return check_launch("lr_table_kernel");
+}
+
+extern "C" int ngp_adam_step_table(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg,
+                                   float loss_scale, float* params_full_precision, uint16_t* params, float* gradients, float* first_moments,
+                                   float* second_moments, uint32_t* param_steps, int clear_grid_gradients, const float* lr_table,
+                                   uint32_t table_len, void* stream) {
+    clear_error();
+    return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, gradients, first_moments,
+                       second_moments, param_steps, clear_grid_gradients, lr_table, table_len, stream);
 }

@@ -27,6 +27,8 @@ namespace {
 
 constexpr uint32_t kMlpParams  = 10240;
 constexpr int kTrainPhases     = 10;  // see ngp_trainer_phase_times
+constexpr uint32_t kLrTableCapacity = 1u << 20;
+constexpr uint32_t kLrTableBlock    = 4096u;
 
 template <typename T>
 int dalloc(T*& p, size_t count, const char* what) {
@@ -113,6 +115,10 @@ struct ngp_trainer {
     cudaEvent_t ev_counts = nullptr, ev_march = nullptr;
     uint32_t* host_counters = nullptr;  // pinned copy of counters 0..2
     bool premarched         = false;    // step `step` was marched on march_stream
+    // Adam: bias-corrected rate per step count, entries [1, lr_table_len] filled
+    float* lr_table       = nullptr;
+    uint32_t lr_table_len = 0;
+    uint32_t adam_calls   = 0;  // bounds every parameter's step count
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> grid_events;  // pending grid-update timings
 };
 
@@ -133,7 +139,7 @@ void destroy(ngp_trainer* t) {
     void* ptrs[] = {t->master, t->params, t->grads, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
                     t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
                     t->counters, t->enc, t->out, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
-                    t->mlp_scratch, t->eval_sse, t->comparison};
+                    t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table};
     for (void* p : ptrs) cudaFree(p);
     if (t->comm) ncclCommDestroy(t->comm);
     if (t->march_stream) cudaStreamSynchronize(t->march_stream);
@@ -318,8 +324,17 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     }
     mark(t, 9);
     // step_optimizer (ngp.train.cu:1973-1980)
-    NGP_TRY(ngp_adam_step(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world), t->master, t->params, t->grads,
-                          t->adam_m, t->adam_v, t->adam_steps, 1, t->stream));
+    if (t->adam_calls + 1u > t->lr_table_len) {
+        // extend the bias-corrected rate table by a block of step counts
+        const uint32_t first = t->lr_table_len + 1u, count = std::min(kLrTableBlock, kLrTableCapacity - first);
+        if (count > 0) {
+            NGP_TRY(ngp_adam_lr_table(t->lr_table, first, count, t->cfg.learning_rate, 0.9f, 0.99f, t->stream));
+            t->lr_table_len += count;
+        }
+    }
+    ++t->adam_calls;
+    NGP_TRY(ngp_adam_step_table(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world),
+                                t->master, t->params, t->grads, t->adam_m, t->adam_v, t->adam_steps, 1, t->lr_table, t->lr_table_len, t->stream));
     mark(t, 10);
     // adaptive batch (ngp.train.cpp:125-133): this step's counters were copied after the loss
     // pass; the host waits for them while the backward pass and Adam run
@@ -472,6 +487,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         t->mlp_scratch_floats = ngp_mlp_backward_scratch_floats();
         NGP_TRY(dalloc(t->mlp_scratch, t->mlp_scratch_floats, "mlp scratch"));
         NGP_TRY(dalloc(t->eval_sse, 1, "eval sse"));
+        NGP_TRY(dalloc(t->lr_table, kLrTableCapacity, "adam rate table"));
         const cudaStream_t s = t->stream;
         NGP_TRY(check_cuda(cudaMemsetAsync(t->grads, 0, sizeof(float) * t->n_params, s), "clear grads"));
         NGP_TRY(check_cuda(cudaMemsetAsync(t->adam_m, 0, sizeof(float) * t->n_params, s), "clear m"));

@@ -315,6 +315,19 @@ def adam_step(n_mlp, master, params, grads, m, v, steps, lr=1e-2, beta1=0.9, bet
                                _stream(stream)), "ngp_adam_step")
 
 
+def adam_lr_table(table, first, count, lr=1e-2, beta1=0.9, beta2=0.99, stream=None) -> None:
+    _check(lib().ngp_adam_lr_table(_ptr(table), _u32(first), _u32(count), _f32(lr), _f32(beta1), _f32(beta2), _stream(stream)),
+           "ngp_adam_lr_table")
+
+
+def adam_step_table(n_mlp, master, params, grads, m, v, steps, lr_table, table_len, lr=1e-2, beta1=0.9, beta2=0.99, eps=1e-15, l2_reg=1e-6,
+                    loss_scale=128.0, clear_grid_gradients=True, stream=None) -> None:
+    _check(lib().ngp_adam_step_table(_u32(master.numel()), _u32(n_mlp), _f32(lr), _f32(beta1), _f32(beta2), _f32(eps), _f32(l2_reg),
+                                     _f32(loss_scale), _ptr(master), _ptr(params), _ptr(grads), _ptr(m), _ptr(v), _ptr(steps),
+                                     ctypes.c_int(1 if clear_grid_gradients else 0), _ptr(lr_table), _u32(table_len), _stream(stream)),
+           "ngp_adam_step_table")
+
+
 # ---------------------------------------------------------------------------------------------
 # Trainer (the reference's ngp::train::InstantNGP, ngp.train.ixx:40-53)
 # ---------------------------------------------------------------------------------------------

@@ -288,6 +288,32 @@ def test_adam_vs_oracle(ngp, oracle):
     assert (g[n_mlp:] == 0).all() and (g[:n_mlp] == grads[:n_mlp]).all()  # grid gradient cleared, MLP kept
 
 
+def test_adam_rate_table_bit_identical(ngp):
+    """Adam with the per-step-count rate table (partly covering the step counts, the rest
+    computed) gives the same bits as Adam computing every rate."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    n, n_mlp = 50000, 10240
+    master = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    grads = rng.normal(0, 10, n).astype(np.float32)
+    grads[n_mlp::4] = 0.0
+    m = rng.normal(0, 0.01, n).astype(np.float32)
+    v = rng.uniform(0, 0.01, n).astype(np.float32)
+    steps = rng.integers(0, 3000, n).astype(np.uint32)
+    params = master.astype(np.float16)
+    a = [T(x) for x in (master, params.view(np.int16), grads, m, v, steps.view(np.int32))]
+    b = [x.clone() for x in a]
+    table = torch.zeros(4096, dtype=torch.float32, device="cuda")
+    ngp.adam_lr_table(table, 1, 1000)
+    ngp.adam_lr_table(table, 1001, 1000)
+    ngp.adam_step(n_mlp, *a)
+    ngp.adam_step_table(n_mlp, *b, table, 2000)
+    torch.cuda.synchronize()
+    for x, y in zip(a, b):
+        assert x.cpu().numpy().tobytes() == y.cpu().numpy().tobytes()
+
+
 def test_adam_vs_reference_kernel(ngp, reflib):
     """The reference's adam_step_kernel on fp16 gradients vs ours on the same values in fp32."""
     import torch
