@@ -79,7 +79,11 @@ __device__ __forceinline__ uint32_t grid_index(uint32_t hashmap_size, uint32_t r
         stride = 0xFFFFFFFFu;
     }
     if (hashmap_size < stride) index = x ^ (y * 2654435761u) ^ (z * 805459861u);
-    return index % hashmap_size;
+    // index % hashmap_size without the integer division where it is not needed: hashed levels
+    // have a power-of-two size (a mask), and dense indices are below the size except for the
+    // +1 corners on the upper faces
+    if ((hashmap_size & (hashmap_size - 1u)) == 0u) return index & (hashmap_size - 1u);
+    return index < hashmap_size ? index : index % hashmap_size;
 }
 
 // ---- PCG32 ---------------------------------------------------------------------------------
