@@ -164,9 +164,28 @@ DENSITY_FWD_FLOP = 6144
 COMPACTED_ROWS = BATCH + 1024
 
 
+# Algorithmic HBM bytes per unit of each training-step phase (inputs read once, outputs written
+# once; table gathers and atomics are L1/L2-served and counted separately), and the DRAM bytes
+# per unit that one ncu capture of the phase's main kernel measured (the profiles/ summaries of
+# the config-3 step: DRAM read + write of that launch / units it processed).
+PHASE_BYTES = {
+    # coords 12 B read + 32 fp16 features written
+    "encode_fwd_inference": {"unit": "pre-compaction sample", "bytes": 12 + 64, "l2_gather_bytes": 16 * 8 * 4,
+                             "kernel": "encode_forward_points_kernel", "ncu_dram_bytes_per_unit": (63.969280e6 + 56.157440e6) / 1414912},
+    # 12 B rays in + 28 B records out per sample (dominant), 8 B per ray of counts
+    "march": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "march_count_kernel + march_write_kernel"},
+    "encode_bwd": {"unit": "batch sample", "bytes": 12 + 64, "l2_atomic_bytes": 16 * 8 * 2 * 4, "kernel": "encode_backward_kernel"},
+    "adam": {"unit": "parameter", "bytes": 40, "kernel": "adam_kernel"},
+    "compact": {"unit": "batch sample", "bytes": 2 * (28 + 64), "kernel": "keep_pass_kernel + compact_copy_kernel"},
+    "mlp_fwd_loss_pad": {"unit": "batch sample", "bytes": 64 + 32 + 28 + 32, "kernel": "mlp_forward_kernel + loss_compacted_kernel"},
+    "grid_update": {"unit": "grid cell", "bytes": 16, "kernel": "density grid kernels"},
+}
+
+
 def phase_roofline(phases: dict, peaks: dict) -> dict:
-    """Roofline of the dominant phase of the training step (per-launch averages from the
-    trainer's in-step CUDA events)."""
+    """Roofline of the dominant phase of the training step.  Phase durations come from CUDA events
+    recorded on the trainer's stream between the phases of profiled steps (run right after the
+    timed steps, on the same model); units per launch are the step's sample counts."""
     steps = max(phases["steps"], 1)
     ms = {k: v / steps for k, v in phases["ms"].items()}
     n_inf = phases["mean_inference_samples"]
@@ -179,16 +198,21 @@ def phase_roofline(phases: dict, peaks: dict) -> dict:
         return {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": None, "share": round(ms[dom] / total, 3),
                 "peak_source": peaks["source"] + " (sustained dense bf16; fp16 has the same tensor rate)"}
-    # memory-bound phases: algorithmic bytes per unit
-    per = {"encode_fwd_inference": (28 + 64 + 16 * 8 * 2 * 2, n_inf), "compact": (2 + 4 + (28 + 64) * 2 * BATCH / max(n_inf, 1), n_inf),
-           "mlp_fwd_loss_pad": (28 + 64 + 32 + 28 + 32 + 32, COMPACTED_ROWS),
-           "encode_bwd": (28 + 64 + 16 * 8 * 2 * 4, BATCH), "march": (28 * 1.0, n_inf),
-           "adam": (38, 12_206_480), "grid_update": (16, 128 ** 3 * 2), "allreduce": (8, 12_206_480)}
-    b, n = per.get(dom, (0, 0))
-    achieved = b * n / t / 1e9
-    return {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "share": round(ms[dom] / total, 3), "peak_source": peaks["source"],
-            "note": "achieved counts the phase's HBM streams plus table bytes gathered/scattered per unit (L2-served)"}
+    info = PHASE_BYTES.get(dom, {"unit": "?", "bytes": 0, "kernel": dom})
+    units = {"pre-compaction sample": n_inf, "batch sample": BATCH, "parameter": 12_206_480, "grid cell": 128 ** 3 * 2}.get(info["unit"], 0)
+    achieved = info["bytes"] * units / t / 1e9
+    res = {"kernel": info["kernel"], "phase": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+           "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "share": round(ms[dom] / total, 3),
+           "peak_source": peaks["source"] + " (HBM copy bandwidth)",
+           "per_unit": f"{info['bytes']} algorithmic HBM bytes per {info['unit']}, {units:.0f} units per launch, {ms[dom] * 1e3:.1f} us per launch"}
+    if "ncu_dram_bytes_per_unit" in info:
+        res["traffic"] = round(info["ncu_dram_bytes_per_unit"] * units)
+        res["traffic_note"] = "ncu DRAM read+write of one launch of this kernel in the config-3 step, per unit, times this launch's units"
+    if "l2_gather_bytes" in info:
+        res["l2_gather_GBps"] = round(info["l2_gather_bytes"] * units / t / 1e9, 1)
+        res["note"] = ("the table (24 MB) is L2-resident: the kernel is bound by L1/L2 gather issue (16 levels x 8 corner loads per "
+                       "sample), not by HBM; l2_gather_GBps counts the gathered table bytes")
+    return res
 
 
 def bench_train_ours(args, rank, world, local):
