@@ -296,6 +296,27 @@ NGP_API int ngp_adam_step_table(uint32_t n_params, uint32_t n_mlp, float lr, flo
                                 float* second_moments, uint32_t* param_steps, int clear_grid_gradients, const float* lr_table,
                                 uint32_t table_len, void* stream);
 
+/* Adam on fp16 gradients (the reference's format and loss-scaled values), as adam_step_kernel;
+ * lr_table optional (table_len 0).  Replaces step_optimizer (ngp.train.cu:1973-1980) for callers
+ * that keep fp16 gradients. */
+NGP_API int ngp_adam_step_f16(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg, float loss_scale,
+                              float* params_full_precision, uint16_t* params, const uint16_t* gradients, float* first_moments,
+                              float* second_moments, uint32_t* param_steps, const float* lr_table, uint32_t table_len, void* stream);
+
+/* fp32 gradients -> fp16 (round to nearest); clear != 0 zeroes the fp32 source. */
+NGP_API int ngp_gradients_to_half(uint32_t n, float* gradients, uint16_t* out, int clear, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Parameter initialisation (the reference's seeds and order).
+ * ------------------------------------------------------------------------------------------ */
+/* Replaces initialize_mlp_parameters (ngp.train.cu:1423-1461): the 10,240 MLP weights,
+ * Xavier-uniform per matrix from PCG32 seed 1337, fp32 master + fp16 copy (synchronous). */
+NGP_API int ngp_init_mlp_parameters(float* master, uint16_t* params, void* stream);
+/* Replaces initialize_grid_params_kernel (ngp.train.cu:1002-1017): n_grid values U(-1e-4, 1e-4). */
+NGP_API int ngp_init_grid_parameters(uint32_t n_grid, float* master_grid, uint16_t* params_grid, void* stream);
+/* fp32 -> fp16 copy (cast_params_to_half_kernel). */
+NGP_API int ngp_cast_to_half(uint32_t n, const float* in, uint16_t* out, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Trainer: the reference's ngp::train::InstantNGP (ngp.train.ixx:40-53) as an opaque handle.
  * ------------------------------------------------------------------------------------------ */

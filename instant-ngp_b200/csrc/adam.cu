@@ -20,7 +20,8 @@ struct AdamParams {
     float lr, beta1, beta2, eps, l2, inv_loss_scale;
     float* master;
     __half* params;
-    float* grad;
+    float* grad;          // fp32 gradients, or
+    const __half* grad16; // fp16 gradients (the reference's format; never cleared)
     float* m;
     float* v;
     uint32_t* steps;
@@ -50,12 +51,25 @@ __device__ __forceinline__ void adam_one(const AdamParams& p, uint32_t i, float&
     out              = __float2half_rn(master);
 }
 
+template <bool HALF_GRAD>
+__device__ __forceinline__ float4 load_grad4(const AdamParams& p, uint32_t q) {
+    if constexpr (HALF_GRAD) {
+        const uint2 raw  = reinterpret_cast<const uint2*>(p.grad16)[q];
+        const float2 lo  = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 hi  = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        return make_float4(lo.x, lo.y, hi.x, hi.y);
+    } else {
+        return reinterpret_cast<const float4*>(p.grad)[q];
+    }
+}
+
+template <bool HALF_GRAD>
 __global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamParams p) {
     const uint32_t q  = blockIdx.x * blockDim.x + threadIdx.x;  // group of 4
     const uint32_t i0 = q * 4u;
     if (i0 >= p.n_params) return;
     if (i0 + 4u <= p.n_params) {
-        const float4 g  = reinterpret_cast<const float4*>(p.grad)[q];
+        const float4 g  = load_grad4<HALF_GRAD>(p, q);
         const bool grid = i0 >= p.n_mlp;
         if (grid && g.x == 0.0f && g.y == 0.0f && g.z == 0.0f && g.w == 0.0f) return;  // untouched entries: one 16-byte read
         float4 w  = reinterpret_cast<float4*>(p.master)[q];
@@ -73,12 +87,13 @@ __global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamP
         reinterpret_cast<float4*>(p.v)[q]      = v;
         reinterpret_cast<uint4*>(p.steps)[q]   = s;
         reinterpret_cast<uint2*>(p.params)[q]  = hv;
-        if (grid && p.clear_grid_grad) reinterpret_cast<float4*>(p.grad)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!HALF_GRAD && grid && p.clear_grid_grad) reinterpret_cast<float4*>(p.grad)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
         return;
     }
     for (uint32_t i = i0; i < p.n_params; ++i) {
-        adam_one(p, i, p.master[i], p.grad[i], p.m[i], p.v[i], p.steps[i], p.params[i]);
-        if (i >= p.n_mlp && p.clear_grid_grad) p.grad[i] = 0.0f;
+        const float g = HALF_GRAD ? __half2float(p.grad16[i]) : p.grad[i];
+        adam_one(p, i, p.master[i], g, p.m[i], p.v[i], p.steps[i], p.params[i]);
+        if (!HALF_GRAD && i >= p.n_mlp && p.clear_grid_grad) p.grad[i] = 0.0f;
     }
 }
 
@@ -88,21 +103,33 @@ __global__ void lr_table_kernel(float* __restrict__ table, uint32_t first, uint3
 }
 
 int adam_launch(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg, float loss_scale,
-                float* params_full_precision, uint16_t* params, float* gradients, float* first_moments, float* second_moments,
-                uint32_t* param_steps, int clear_grid_gradients, const float* lr_table, uint32_t table_len, void* stream) {
+                float* params_full_precision, uint16_t* params, float* gradients, const uint16_t* gradients16, float* first_moments,
+                float* second_moments, uint32_t* param_steps, int clear_grid_gradients, const float* lr_table, uint32_t table_len, void* stream) {
     if (n_params == 0) return NGP_OK;
-    if (params_full_precision == nullptr || params == nullptr || gradients == nullptr || first_moments == nullptr || second_moments == nullptr ||
-        param_steps == nullptr || n_mlp > n_params || n_mlp % 4u != 0 || loss_scale == 0.0f || (table_len > 0 && lr_table == nullptr))
+    if (params_full_precision == nullptr || params == nullptr || (gradients == nullptr) == (gradients16 == nullptr) || first_moments == nullptr ||
+        second_moments == nullptr || param_steps == nullptr || n_mlp > n_params || n_mlp % 4u != 0 || loss_scale == 0.0f ||
+        (table_len > 0 && lr_table == nullptr))
         return fail(NGP_ERR_INVALID, "adam: invalid input");
     if ((reinterpret_cast<uintptr_t>(params_full_precision) | reinterpret_cast<uintptr_t>(gradients) | reinterpret_cast<uintptr_t>(first_moments) |
          reinterpret_cast<uintptr_t>(second_moments) | reinterpret_cast<uintptr_t>(param_steps)) % 16u != 0 ||
-        reinterpret_cast<uintptr_t>(params) % 8u != 0)
-        return fail(NGP_ERR_INVALID, "adam: buffers must be 16-byte aligned (fp16 copy 8-byte)");
-    AdamParams p{n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, 1.0f / loss_scale, params_full_precision, reinterpret_cast<__half*>(params),
-                 gradients, first_moments, second_moments, param_steps, clear_grid_gradients, lr_table, table_len};
+        (reinterpret_cast<uintptr_t>(params) | reinterpret_cast<uintptr_t>(gradients16)) % 8u != 0)
+        return fail(NGP_ERR_INVALID, "adam: buffers must be 16-byte aligned (fp16 buffers 8-byte)");
+    AdamParams p{n_params,      n_mlp,     lr,       beta1,    beta2,       eps,
+                 l2_reg,        1.0f / loss_scale, params_full_precision, reinterpret_cast<__half*>(params), gradients,
+                 reinterpret_cast<const __half*>(gradients16), first_moments, second_moments, param_steps, clear_grid_gradients, lr_table, table_len};
     const uint32_t groups = (n_params + 3u) / 4u;
-    adam_kernel<<<(groups + 255u) / 256u, 256, 0, as_stream(stream)>>>(p);
+    if (gradients16 != nullptr)
+        adam_kernel<true><<<(groups + 255u) / 256u, 256, 0, as_stream(stream)>>>(p);
+    else
+        adam_kernel<false><<<(groups + 255u) / 256u, 256, 0, as_stream(stream)>>>(p);
     return check_launch("adam_kernel");
+}
+
+__global__ void grad_to_half_kernel(uint32_t n, float* __restrict__ src, __half* __restrict__ dst, int clear) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    dst[i] = __float2half_rn(src[i]);
+    if (clear) src[i] = 0.0f;
 }
 
 }  // namespace
@@ -114,8 +141,8 @@ extern "C" int ngp_adam_step(uint32_t n_params, uint32_t n_mlp, float lr, float 
                              float* params_full_precision, uint16_t* params, float* gradients, float* first_moments, float* second_moments,
                              uint32_t* param_steps, int clear_grid_gradients, void* stream) {
     clear_error();
-    return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, gradients, first_moments,
-                       second_moments, param_steps, clear_grid_gradients, nullptr, 0u, stream);
+    return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, gradients, nullptr,
+                       first_moments, second_moments, param_steps, clear_grid_gradients, nullptr, 0u, stream);
 }
 
 extern "C" int ngp_adam_lr_table(float* table, uint32_t first, uint32_t count, float lr, float beta1, float beta2, void* stream) {
@@ -131,6 +158,23 @@ extern "C" int ngp_adam_step_table(uint32_t n_params, uint32_t n_mlp, float lr, 
                                    float* second_moments, uint32_t* param_steps, int clear_grid_gradients, const float* lr_table,
                                    uint32_t table_len, void* stream) {
     clear_error();
-    return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, gradients, first_moments,
-                       second_moments, param_steps, clear_grid_gradients, lr_table, table_len, stream);
+    return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, gradients, nullptr,
+                       first_moments, second_moments, param_steps, clear_grid_gradients, lr_table, table_len, stream);
+}
+
+extern "C" int ngp_adam_step_f16(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg, float loss_scale,
+                                 float* params_full_precision, uint16_t* params, const uint16_t* gradients, float* first_moments,
+                                 float* second_moments, uint32_t* param_steps, const float* lr_table, uint32_t table_len, void* stream) {
+    clear_error();
+    if (gradients == nullptr) return fail(NGP_ERR_INVALID, "adam: null gradients");
+    return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, nullptr, gradients,
+                       first_moments, second_moments, param_steps, 0, lr_table, table_len, stream);
+}
+
+extern "C" int ngp_gradients_to_half(uint32_t n, float* gradients, uint16_t* out, int clear, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (gradients == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "gradients to half: null pointer");
+    grad_to_half_kernel<<<(n + 255u) / 256u, 256, 0, as_stream(stream)>>>(n, gradients, reinterpret_cast<__half*>(out), clear);
+    return check_launch("grad_to_half_kernel");
 }

@@ -192,23 +192,8 @@ __global__ void cast_half_kernel(const float* in, __half* out, uint32_t n) {
 // Xavier-uniform MLP weights drawn on the host from PCG32(1337), in the reference's order
 // (ngp.train.cu:1423-1461).
 int init_params(ngp_trainer* t) {
-    std::vector<float> h(kMlpParams);
-    Pcg32 rng{kTrainSeed};
-    const uint32_t shapes[5][2] = {{64, 32}, {16, 64}, {64, 32}, {64, 64}, {16, 64}};
-    uint32_t off                = 0;
-    for (auto& sh : shapes) {
-        const float scale = std::sqrt(6.0f / static_cast<float>(sh[0] + sh[1]));
-        for (uint32_t i = 0; i < sh[0] * sh[1]; ++i) h[off + i] = rng.next_float() * 2.0f * scale - scale;
-        off += sh[0] * sh[1];
-    }
-    NGP_TRY(check_cuda(cudaMemcpy(t->master, h.data(), sizeof(float) * kMlpParams, cudaMemcpyHostToDevice), "upload mlp params"));
-    cast_half_kernel<<<(kMlpParams + 255) / 256, 256, 0, t->stream>>>(t->master, reinterpret_cast<__half*>(t->params), kMlpParams);
-    NGP_TRY(check_launch("cast_half_kernel"));
-    const uint32_t n_grid    = t->layout.n_params;
-    const uint32_t n_threads = (n_grid + 3u) / 4u;
-    init_grid_kernel<<<(n_threads + 127u) / 128u, 128, 0, t->stream>>>(t->master + kMlpParams, reinterpret_cast<__half*>(t->params) + kMlpParams,
-                                                                     n_grid, kMlpParams);
-    return check_launch("init_grid_kernel");
+    NGP_TRY(ngp_init_mlp_parameters(t->master, t->params, t->stream));
+    return ngp_init_grid_parameters(t->layout.n_params, t->master + kMlpParams, t->params + kMlpParams, t->stream);
 }
 
 int encode(ngp_trainer* t, uint32_t n, const float* c, uint16_t* dst, uint32_t stride) {
@@ -656,4 +641,44 @@ extern "C" int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint
     if (out_mean_inference_samples != nullptr)
         *out_mean_inference_samples = t->profiled_steps ? static_cast<float>(t->inference_samples_sum / t->profiled_steps) : 0.0f;
     return NGP_OK;
+}
+
+// initialize_mlp_parameters (ngp.train.cu:1423-1461): Xavier-uniform per matrix from one PCG32
+// stream (seed 1337) in the packed order, fp32 master + fp16 copy.
+extern "C" int ngp_init_mlp_parameters(float* master, uint16_t* params, void* stream) {
+    clear_error();
+    if (master == nullptr || params == nullptr) return fail(NGP_ERR_INVALID, "init mlp parameters: null pointer");
+    std::vector<float> h(kMlpParams);
+    Pcg32 rng{kTrainSeed};
+    const uint32_t shapes[5][2] = {{64, 32}, {16, 64}, {64, 32}, {64, 64}, {16, 64}};
+    uint32_t off                = 0;
+    for (auto& sh : shapes) {
+        const float scale = std::sqrt(6.0f / static_cast<float>(sh[0] + sh[1]));
+        for (uint32_t i = 0; i < sh[0] * sh[1]; ++i) h[off + i] = rng.next_float() * 2.0f * scale - scale;
+        off += sh[0] * sh[1];
+    }
+    const cudaStream_t s = as_stream(stream);
+    NGP_TRY(check_cuda(cudaMemcpyAsync(master, h.data(), sizeof(float) * kMlpParams, cudaMemcpyHostToDevice, s), "upload mlp params"));
+    cast_half_kernel<<<(kMlpParams + 255) / 256, 256, 0, s>>>(master, reinterpret_cast<__half*>(params), kMlpParams);
+    NGP_TRY(check_launch("cast_half_kernel"));
+    return check_cuda(cudaStreamSynchronize(s), "init mlp parameters");  // h goes out of scope
+}
+
+// initialize_grid_params_kernel (ngp.train.cu:1002-1017): U(-1e-4, 1e-4) from the PCG32 stream
+// continued after the MLP's draws, four values per thread.
+extern "C" int ngp_init_grid_parameters(uint32_t n_grid, float* master_grid, uint16_t* params_grid, void* stream) {
+    clear_error();
+    if (n_grid == 0) return NGP_OK;
+    if (master_grid == nullptr || params_grid == nullptr) return fail(NGP_ERR_INVALID, "init grid parameters: null pointer");
+    const uint32_t n_threads = (n_grid + 3u) / 4u;
+    init_grid_kernel<<<(n_threads + 127u) / 128u, 128, 0, as_stream(stream)>>>(master_grid, reinterpret_cast<__half*>(params_grid), n_grid, kMlpParams);
+    return check_launch("init_grid_kernel");
+}
+
+extern "C" int ngp_cast_to_half(uint32_t n, const float* in, uint16_t* out, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (in == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "cast to half: null pointer");
+    cast_half_kernel<<<(n + 255u) / 256u, 256, 0, as_stream(stream)>>>(in, reinterpret_cast<__half*>(out), n);
+    return check_launch("cast_half_kernel");
 }

@@ -17,6 +17,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "libngp_oracle.so"
 REF_SO = HERE / "_ref" / "libngp_ref.so"
+SHIM_REPLAY_SO = HERE / "_ref" / "libngp_shim_replay.so"
 
 _u32p = ctypes.POINTER(ctypes.c_uint32)
 
@@ -30,7 +31,7 @@ def build_ref() -> Path | None:
     """Build oracle/_ref from the reference sources when they are present (not on a GPU box)."""
     if not Path("/root/reference/ngp.train.cu").exists():
         return REF_SO if REF_SO.exists() else None
-    subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE), "ref", "shim"], check=True)
     return REF_SO
 
 
@@ -120,6 +121,54 @@ class RefLib:
         status = getattr(self.lib, name)(*args)
         if status != 0:
             raise RuntimeError(f"{name} failed with CUDA status {status}")
+
+
+class ReplayTrainer:
+    """The reference's training loop (InstantNGP::train, ngp.train.cpp:108-155, replayed through
+    the ngp::cuda interface by train_replay.inc) on one implementation of that interface: the
+    reference's own ngp.train.cu (REF_SO) or this library's drop-in layer (SHIM_REPLAY_SO)."""
+
+    def __init__(self, so: Path, split_train: dict, split_test: dict | None = None) -> None:
+        if not so.exists():
+            raise RuntimeError(f"{so} missing: run `make -C oracle ref shim` where the reference sources are present")
+        self.lib = ctypes.CDLL(str(so))
+        self.lib.ref_train_create.restype = ctypes.c_void_p
+        px, cam = np.ascontiguousarray(split_train["pixels"]), np.ascontiguousarray(split_train["camera"], np.float32)
+        self._keep = [px, cam]
+        tpx = tcam = None
+        n_test = 0
+        if split_test is not None:
+            tpx, tcam = np.ascontiguousarray(split_test["pixels"]), np.ascontiguousarray(split_test["camera"], np.float32)
+            n_test = tpx.shape[0]
+            self._keep += [tpx, tcam]
+        self.frames, self.height, self.width = px.shape[0], px.shape[1], px.shape[2]
+        self.n_test = n_test
+        (fx, fy), (cx, cy) = split_train["focal"], split_train["principal"]
+        h = self.lib.ref_train_create(_p(px), ctypes.c_size_t(px.nbytes), _p(cam), ctypes.c_uint32(self.frames), ctypes.c_uint32(self.width),
+                                      ctypes.c_uint32(self.height), ctypes.c_float(fx), ctypes.c_float(fy), ctypes.c_float(cx), ctypes.c_float(cy),
+                                      _p(tpx), ctypes.c_size_t(0 if tpx is None else tpx.nbytes), _p(tcam), ctypes.c_uint32(n_test))
+        if not h:
+            raise RuntimeError("ref_train_create failed")
+        self.handle = ctypes.c_void_p(h)
+
+    def train(self, steps: int) -> dict:
+        out = (ctypes.c_float * 4)()
+        rc = self.lib.ref_train_steps(self.handle, ctypes.c_int32(steps), out)
+        if rc != 0:
+            raise RuntimeError(f"ref_train_steps failed ({rc})")
+        return {"elapsed_ms": float(out[0]), "measured": int(out[1]), "measured_before": int(out[2]), "rays_per_batch": int(out[3])}
+
+    def test_psnr(self) -> float:
+        sse = ctypes.c_double(0)
+        if self.lib.ref_train_test_sse(self.handle, ctypes.byref(sse)) != 0:
+            raise RuntimeError("ref_train_test_sse failed")
+        mse = sse.value / (self.n_test * self.width * self.height * 3.0)
+        return -10.0 * np.log10(mse) if mse > 0 else float("inf")
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.ref_train_destroy(self.handle)
+            self.handle = None
 
 
 def _oracle_mlp_methods():

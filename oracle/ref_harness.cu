@@ -166,162 +166,7 @@ int ref_pcg32(uint64_t initstate, uint64_t initseq, uint64_t advance, uint32_t c
 
 }  // extern "C"
 
-// ---------------------------------------------------------------------------------------------
-// The reference's training loop, replayed through its own device ABI exactly as
-// InstantNGP::train does (ngp.train.cpp:12-100 construction, 108-155 step loop), for the
-// bench's reference arm and for PSNR parity.  The C++23-module trainer itself cannot be built
-// here (it needs `import std`), so this is the same sequence of ngp::cuda calls.
-// ---------------------------------------------------------------------------------------------
-namespace {
-struct RefTrainer {
-    const uint8_t* pixels = nullptr;
-    const float* camera   = nullptr;
-    const uint8_t* test_pixels = nullptr;
-    const float* test_camera   = nullptr;
-    uint32_t frames, width, height, test_frames;
-    float fx, fy, cx, cy;
-    float *sample_coords, *rays, *density_grid_values, *density_grid_scratch, *density_grid_mean, *compacted_sample_coords, *loss_values;
-    uint32_t *ray_indices, *numsteps, *ray_counter, *sample_counter, *density_grid_indices, *density_grid_occupied_count, *compacted_sample_counter;
-    uint32_t *evaluation_numsteps, *evaluation_sample_counter, *evaluation_overflow_counter;
-    double* evaluation_loss_sum;
-    uint8_t* occupancy;
-    uint16_t *density_input, *rgb_input, *network_output, *network_output_gradients, *rgb_output_gradients, *rgb_input_gradients,
-        *density_input_gradients, *density_forward_hidden, *rgb_forward_hidden, *density_backward_hidden, *rgb_backward_hidden, *params,
-        *param_gradients;
-    void* cublaslt = nullptr;
-    uint8_t* cublaslt_workspace;
-    float *params_full_precision, *m, *v;
-    uint32_t* param_steps;
-    uint32_t step = 0, rays_per_batch = cfg::INITIAL_RAYS_PER_BATCH, inference_sample_count = cfg::MAX_SAMPLES, measured_before = 0,
-             measured = 0, ema_step = 0;
-};
-}  // namespace
-
-extern "C" {
-
-void* ref_train_create(const uint8_t* pixels, size_t pixel_bytes, const float* camera, uint32_t frames, uint32_t width, uint32_t height, float fx,
-                       float fy, float cx, float cy, const uint8_t* test_pixels, size_t test_bytes, const float* test_camera, uint32_t test_frames) {
-    try {
-        auto* t = new RefTrainer{};
-        t->frames = frames, t->width = width, t->height = height, t->fx = fx, t->fy = fy, t->cx = cx, t->cy = cy, t->test_frames = test_frames;
-        ref::upload_dataset(pixels, pixel_bytes, camera, frames * 12u, t->pixels, t->camera);
-        if (test_frames) ref::upload_dataset(test_pixels, test_bytes, test_camera, test_frames * 12u, t->test_pixels, t->test_camera);
-        ref::allocate_sampler_buffers(t->sample_coords, t->rays, t->ray_indices, t->numsteps, t->ray_counter, t->sample_counter, t->occupancy);
-        ref::allocate_network_buffers(t->density_input, t->rgb_input, t->network_output, t->network_output_gradients, t->rgb_output_gradients,
-                                      t->rgb_input_gradients, t->density_input_gradients, t->density_forward_hidden, t->rgb_forward_hidden,
-                                      t->density_backward_hidden, t->rgb_backward_hidden, t->cublaslt, t->cublaslt_workspace);
-        ref::allocate_density_grid_buffers(t->density_grid_values, t->density_grid_scratch, t->density_grid_indices, t->density_grid_mean,
-                                           t->density_grid_occupied_count);
-        ref::allocate_training_loss_buffers(t->compacted_sample_counter, t->compacted_sample_coords, t->loss_values);
-        ref::allocate_evaluation_buffers(t->evaluation_numsteps, t->evaluation_sample_counter, t->evaluation_overflow_counter, t->evaluation_loss_sum);
-        ref::allocate_trainable_parameter_buffers(t->params_full_precision, t->params, t->param_gradients);
-        ref::allocate_adam_state(t->m, t->v, t->param_steps);
-        ref::initialize_mlp_parameters(t->params_full_precision, t->params, t->param_gradients);
-        ref::initialize_grid_parameters(t->params_full_precision, t->params, t->param_gradients);
-        cudaDeviceSynchronize();
-        return t;
-    } catch (const std::exception& e) {
-        std::fprintf(stderr, "ref_train_create: %s\n", e.what());
-        return nullptr;
-    }
-}
-
-// Run `iters` steps; out[0..3] = elapsed ms (cudaEvents), last compacted count, last
-// pre-compaction count, rays_per_batch.
-int ref_train_steps(void* handle, int32_t iters, float* out) {
-    auto* t = static_cast<RefTrainer*>(handle);
-    try {
-        cudaEvent_t e0, e1;
-        cudaEventCreate(&e0);
-        cudaEventCreate(&e1);
-        cudaEventRecord(e0);
-        for (int32_t i = 0; i < iters; ++i) {
-            float ms = 0.0f;
-            ref::update_density_grid(t->camera, t->frames, t->width, t->height, t->fx, t->fy, t->cx, t->cy, t->step, t->params, t->sample_coords,
-                                     t->density_input, t->network_output, t->density_grid_values, t->density_grid_scratch, t->density_grid_indices,
-                                     t->density_grid_mean, t->density_grid_occupied_count, t->occupancy, t->ema_step, ms);
-            ref::sample_training_batch(t->camera, t->frames, t->width, t->height, t->fx, t->fy, t->cx, t->cy, t->step, t->rays_per_batch,
-                                       t->inference_sample_count, t->occupancy, t->sample_coords, t->rays, t->ray_indices, t->numsteps,
-                                       t->ray_counter, t->sample_counter);
-            ref::evaluate_network(t->inference_sample_count, t->sample_coords, t->params, t->density_input, t->rgb_input, t->network_output);
-            ref::compute_training_loss_and_compact_samples(t->rays_per_batch, t->step, t->ray_counter, t->pixels, t->frames, t->width, t->height,
-                                                           t->network_output, t->compacted_sample_counter, t->ray_indices, t->rays, t->numsteps,
-                                                           t->sample_coords, t->compacted_sample_coords, t->network_output_gradients,
-                                                           t->loss_values);
-            ref::pad_compacted_training_batch(t->compacted_sample_counter, t->compacted_sample_coords, t->network_output_gradients);
-            ref::forward_network(t->compacted_sample_coords, t->params, t->density_input, t->rgb_input, t->density_forward_hidden,
-                                 t->rgb_forward_hidden, t->network_output);
-            ref::backward_network(t->compacted_sample_coords, t->params, t->param_gradients, t->density_input, t->rgb_input,
-                                  t->density_forward_hidden, t->rgb_forward_hidden, t->network_output, t->network_output_gradients,
-                                  t->rgb_output_gradients, t->rgb_input_gradients, t->density_input_gradients, t->density_backward_hidden,
-                                  t->rgb_backward_hidden, t->cublaslt, t->cublaslt_workspace);
-            ref::step_optimizer(t->params_full_precision, t->params, t->param_gradients, t->m, t->v, t->param_steps);
-            ref::read_counter(t->sample_counter, t->measured_before);
-            ref::read_counter(t->compacted_sample_counter, t->measured);
-            if (t->measured == 0u) return 2;
-            const uint32_t g          = cfg::NETWORK_BATCH_GRANULARITY;
-            t->inference_sample_count = ((std::min(t->measured_before, cfg::MAX_SAMPLES) + g - 1u) / g) * g;
-            t->rays_per_batch = std::min(std::max(((static_cast<uint32_t>(std::min((static_cast<uint64_t>(t->rays_per_batch) * cfg::NETWORK_BATCH_SIZE) /
-                                                                                           t->measured,
-                                                                                       static_cast<uint64_t>(cfg::NETWORK_BATCH_SIZE))) +
-                                                    g - 1u) /
-                                                   g) *
-                                                      g,
-                                                  g),
-                                         cfg::NETWORK_BATCH_SIZE);
-            ++t->step;
-        }
-        cudaEventRecord(e1);
-        cudaEventSynchronize(e1);
-        cudaEventElapsedTime(out, e0, e1);
-        cudaEventDestroy(e0);
-        cudaEventDestroy(e1);
-        out[1] = static_cast<float>(t->measured);
-        out[2] = static_cast<float>(t->measured_before);
-        out[3] = static_cast<float>(t->rays_per_batch);
-        return 0;
-    } catch (const std::exception& e) {
-        std::fprintf(stderr, "ref_train_steps: %s\n", e.what());
-        return 1;
-    }
-}
-
-// Squared error summed over the test images (run_evaluation, as InstantNGP::test does).
-int ref_train_test_sse(void* handle, double* out_sse) {
-    auto* t = static_cast<RefTrainer*>(handle);
-    try {
-        double total = 0.0;
-        for (uint32_t i = 0; i < t->test_frames; ++i) {
-            double sse = 0.0;
-            ref::run_evaluation(t->test_pixels, t->test_camera, t->test_frames, i, 1u, t->width, t->height, t->fx, t->fy, t->cx, t->cy, t->occupancy,
-                                t->params, t->sample_coords, t->density_input, t->rgb_input, t->network_output, t->evaluation_numsteps,
-                                t->evaluation_sample_counter, t->evaluation_overflow_counter, t->evaluation_loss_sum, nullptr, nullptr, sse);
-            total += sse;
-        }
-        *out_sse = total;
-        return 0;
-    } catch (const std::exception& e) {
-        std::fprintf(stderr, "ref_train_test_sse: %s\n", e.what());
-        return 1;
-    }
-}
-
-void ref_train_destroy(void* handle) {
-    auto* t = static_cast<RefTrainer*>(handle);
-    if (t == nullptr) return;
-    ref::destroy_cublaslt(t->cublaslt);
-    ref::free_device_buffers(t->pixels, t->camera, t->test_pixels, t->test_camera, t->sample_coords, t->rays, t->ray_indices, t->numsteps,
-                             t->ray_counter, t->sample_counter, t->occupancy, t->density_grid_values, t->density_grid_scratch,
-                             t->density_grid_indices, t->density_grid_mean, t->density_grid_occupied_count, t->compacted_sample_counter,
-                             t->compacted_sample_coords, t->loss_values, t->evaluation_numsteps, t->evaluation_sample_counter,
-                             t->evaluation_overflow_counter, t->evaluation_loss_sum, t->density_input, t->rgb_input, t->network_output,
-                             t->network_output_gradients, t->rgb_output_gradients, t->rgb_input_gradients, t->density_input_gradients,
-                             t->density_forward_hidden, t->rgb_forward_hidden, t->density_backward_hidden, t->rgb_backward_hidden,
-                             t->cublaslt_workspace, t->params_full_precision, t->params, t->param_gradients, t->m, t->v, t->param_steps);
-    delete t;
-}
-
-}  // extern "C"
+#include "train_replay.inc"
 
 // ---------------------------------------------------------------------------------------------
 // Marching of given rays with the reference's own device helpers (intersect_unit_aabb,

@@ -1,0 +1,45 @@
+"""The drop-in `ngp::cuda` layer (instant-ngp_b200/shim/ngp_train_cuda.cpp): the reference's own
+training loop (InstantNGP::train, ngp.train.cpp:108-155, replayed through ngp.train.h's interface
+by oracle/train_replay.inc) runs once on the reference's ngp.train.cu and once on this library,
+on the same seeded scene.  Sample placement differs (ray order vs atomic order) and gradients are
+summed in fp32 instead of fp16, so the runs are compared statistically: both train, the
+adaptive batch settles to similar ray and sample counts (within 0.6-1.7x), and the test PSNR after
+1000 steps is at least the reference's minus 0.5 dB (on this 12-view 160x160 scene single runs vary
+by about a dB; the drop-in layer measured 20.3 vs 19.0 and 23.5 vs 20.9 dB on two seeds)."""
+from __future__ import annotations
+
+import pytest
+
+import workloads
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def scene():
+    return workloads.procedural_dataset(n_train=12, n_test=2, width=160, height=160, seed=11)
+
+
+def _replay(so, scene, steps):
+    from oracle import ReplayTrainer
+
+    t = ReplayTrainer(so, scene["train"], scene["test"])
+    try:
+        stats = t.train(steps)
+        psnr = t.test_psnr()
+    finally:
+        t.close()
+    return stats, psnr
+
+
+def test_reference_loop_on_drop_in_layer(reflib, scene):
+    from oracle import REF_SO, SHIM_REPLAY_SO
+
+    ref_stats, ref_psnr = _replay(REF_SO, scene, 1000)
+    our_stats, our_psnr = _replay(SHIM_REPLAY_SO, scene, 1000)
+    print(f"reference {ref_psnr:.2f} dB {ref_stats}; drop-in {our_psnr:.2f} dB {our_stats}")
+    assert our_stats["measured"] > 0 and ref_stats["measured"] > 0
+    assert 0.6 < our_stats["rays_per_batch"] / ref_stats["rays_per_batch"] < 1.7
+    assert 0.6 < our_stats["measured_before"] / ref_stats["measured_before"] < 1.7
+    assert our_psnr >= ref_psnr - 0.5
+    assert our_psnr > 15.0
