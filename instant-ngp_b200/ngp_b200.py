@@ -493,16 +493,12 @@ class InstantNGP:
 
     def join_process_group(self) -> None:
         """Join using the current torch.distributed process group to share the NCCL id."""
-        import torch
         import torch.distributed as dist
 
         world, rank = dist.get_world_size(), dist.get_rank()
         if world == 1:
             return
-        uid = nccl_unique_id() if rank == 0 else bytes(128)
-        t = torch.tensor(list(uid), dtype=torch.uint8, device="cuda")
-        dist.broadcast(t, src=0)
-        self.join(bytes(t.cpu().tolist()), world, rank)
+        self.join(share_nccl_id(), world, rank)
 
     def get_grid(self):
         import numpy as np
@@ -511,6 +507,20 @@ class InstantNGP:
         vals = np.zeros(GRID_CELLS, np.float32)
         _check(lib().ngp_trainer_get_grid(self.handle, ctypes.c_void_p(bits.ctypes.data), ctypes.c_void_p(vals.ctypes.data)), "ngp_trainer_get_grid")
         return bits, vals
+
+
+def share_nccl_id() -> bytes:
+    """Rank 0 creates an NCCL unique id and broadcasts it over the current torch.distributed group
+    (any backend: the id travels in a CPU tensor for gloo, a device tensor for nccl)."""
+    import torch
+    import torch.distributed as dist
+
+    rank = dist.get_rank()
+    uid = nccl_unique_id() if rank == 0 else bytes(128)
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor(list(uid), dtype=torch.uint8, device=device)
+    dist.broadcast(t, src=0)
+    return bytes(t.cpu().tolist())
 
 
 def nccl_unique_id() -> bytes:
