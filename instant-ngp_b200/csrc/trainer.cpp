@@ -50,6 +50,14 @@ struct Split {
 
 }  // namespace
 
+struct MarchSet {
+    float* coords         = nullptr;  // [MAX_SAMPLES][7]
+    float* rays           = nullptr;  // [BATCH][6]
+    uint32_t* ray_indices = nullptr;
+    uint32_t* numsteps    = nullptr;
+    uint32_t* counters    = nullptr;  // 0 rays, 1 samples, 2 compacted
+};
+
 struct ngp_trainer {
     ngp_trainer_config cfg{};
     ngp_grid_layout layout{};
@@ -61,6 +69,7 @@ struct ngp_trainer {
     float* master      = nullptr;
     uint16_t* params   = nullptr;
     float* grads       = nullptr;
+    uint16_t* grads16  = nullptr;  // data parallel: fp16 gradient exchanged between ranks
     float *adam_m = nullptr, *adam_v = nullptr;
     uint32_t* adam_steps = nullptr;
 
@@ -71,10 +80,14 @@ struct ngp_trainer {
     uint32_t* occupied     = nullptr;
 
     // sampler and network buffers
-    float* coords = nullptr;  // [MAX_SAMPLES][7]
-    float* rays   = nullptr;  // [BATCH][6]
+    // Two sets of march outputs, used by alternate steps, so that the next step's march can run
+    // while this step's loss pass still reads its rays and sample counts.  Set 0 also serves
+    // evaluation and the density-grid samples.
+    MarchSet sets[2];
+    float* coords = nullptr;  // set 0: [MAX_SAMPLES][7]
+    float* rays   = nullptr;  // set 0: [BATCH][6]
     uint32_t *ray_indices = nullptr, *numsteps = nullptr, *march_scratch = nullptr;
-    uint32_t* counters     = nullptr;  // 0 rays, 1 samples, 2 compacted
+    uint32_t* counters     = nullptr;  // set 0: 0 rays, 1 samples, 2 compacted
     uint16_t* enc          = nullptr;  // [32][MAX_SAMPLES] encoded positions
     uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output (training: raw densities)
     uint16_t* cout         = nullptr;  // [COMPACTED_ROWS][16] network output of the compacted samples
@@ -136,11 +149,11 @@ void destroy(ngp_trainer* t) {
     free_split(t->train);
     free_split(t->val);
     free_split(t->test);
-    void* ptrs[] = {t->master, t->params, t->grads, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
-                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
-                    t->counters, t->enc, t->out, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
+    void* ptrs[] = {t->master, t->params, t->grads, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
+                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->enc, t->out, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table};
     for (void* p : ptrs) cudaFree(p);
+    for (MarchSet& m : t->sets) cudaFree(m.coords), cudaFree(m.rays), cudaFree(m.ray_indices), cudaFree(m.numsteps), cudaFree(m.counters);
     if (t->comm) ncclCommDestroy(t->comm);
     if (t->march_stream) cudaStreamSynchronize(t->march_stream);
     for (cudaEvent_t e : t->marks)
@@ -223,8 +236,9 @@ int update_grid(ngp_trainer* t) {
     const uint32_t n_uniform = t->step < 256u ? kGridCells : kGridCells / 4u;
     const uint32_t n_nonuni  = t->step < 256u ? 0u : kGridCells / 4u;
     const uint32_t n         = n_uniform + n_nonuni;
-    NGP_TRY(ngp_density_grid_samples(n_uniform, n_nonuni, t->ema_step, t->grid_values, t->coords, t->grid_indices, t->stream));
-    NGP_TRY(encode(t, n, t->coords, t->enc, n));
+    float* coords = t->sets[t->step & 1u].coords;
+    NGP_TRY(ngp_density_grid_samples(n_uniform, n_nonuni, t->ema_step, t->grid_values, coords, t->grid_indices, t->stream));
+    NGP_TRY(encode(t, n, coords, t->enc, n));
     NGP_TRY(ngp_density_forward(n, t->params, t->enc, n, t->grid_density, t->stream));
     NGP_TRY(ngp_density_grid_splat(n, t->grid_indices, t->grid_density, t->grid_scratch, t->stream));
     NGP_TRY(ngp_density_grid_update(t->grid_values, t->grid_scratch, 0.95f, t->grid_partial, t->grid_mean, t->bitfield, t->occupied, t->stream));
@@ -247,9 +261,10 @@ void collect_grid_times(ngp_trainer* t) {
 int march_step(ngp_trainer* t, uint32_t step, cudaStream_t stream) {
     const Split& s          = t->train;
     const uint32_t rng_step = step * static_cast<uint32_t>(t->world) + static_cast<uint32_t>(t->rank);
+    const MarchSet& m       = t->sets[step & 1u];
     return ngp_march_training_rays(s.camera, s.frames, s.width, s.height, s.fx, s.fy, s.cx, s.cy, rng_step, t->rays_per_batch, nullptr,
-                                   t->inference_samples, t->bitfield, t->coords, t->rays, t->ray_indices, t->numsteps, t->march_scratch,
-                                   t->counters + 0, t->counters + 1, stream);
+                                   t->inference_samples, t->bitfield, m.coords, m.rays, m.ray_indices, m.numsteps, t->march_scratch,
+                                   m.counters + 0, m.counters + 1, stream);
 }
 
 void mark(ngp_trainer* t, int k) {
@@ -278,22 +293,25 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     mark(t, 2);
     // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524): only the density
     // network is needed to decide which samples each ray keeps
-    NGP_TRY(encode(t, t->inference_samples, t->coords, t->enc, t->inference_samples));
+    const MarchSet& m = t->sets[t->step & 1u];
+    NGP_TRY(encode(t, t->inference_samples, m.coords, t->enc, t->inference_samples));
     mark(t, 3);
     NGP_TRY(ngp_density_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->out, t->stream));
     mark(t, 4);
     // compaction (ngp.train.cu:1932-1944): the kept samples' records and encodings
-    NGP_TRY(ngp_training_compact_by_density(t->rays_per_batch, t->counters + 0, t->out, t->coords, t->enc, t->inference_samples, t->numsteps,
-                                            t->ccoords, t->cenc, t->counters + 2, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    NGP_TRY(ngp_training_compact_by_density(t->rays_per_batch, m.counters + 0, t->out, m.coords, t->enc, t->inference_samples, m.numsteps,
+                                            t->ccoords, t->cenc, m.counters + 2, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    // the step's counters are final here: the host reads them (for the next step's batch size)
+    // while the rest of the step runs
+    NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, m.counters, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
+    NGP_TRY(check_cuda(cudaEventRecord(t->ev_counts, t->stream), "record counters"));
     mark(t, 5);
     // the full network on the compacted rows, then compositing, loss and padding (1944-1956)
     NGP_TRY(ngp_mlp_forward(kCompactedRows, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->cout, nullptr, t->stream));
-    NGP_TRY(ngp_training_loss_compacted(t->rays_per_batch, rng_step, t->counters + 0, s.pixels, s.frames, s.width, s.height, t->cout, t->ray_indices,
-                                        t->rays, t->numsteps, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->loss_scratch_bytes,
+    NGP_TRY(ngp_training_loss_compacted(t->rays_per_batch, rng_step, m.counters + 0, s.pixels, s.frames, s.width, s.height, t->cout, m.ray_indices,
+                                        m.rays, m.numsteps, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->loss_scratch_bytes,
                                         t->stream));
-    NGP_TRY(ngp_pad_training_batch_enc(t->counters + 2, t->ccoords, t->dloss, t->cenc, kCompactedRows, t->stream));
-    NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, t->counters, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
-    NGP_TRY(check_cuda(cudaEventRecord(t->ev_counts, t->stream), "record counters"));
+    NGP_TRY(ngp_pad_training_batch_enc(m.counters + 2, t->ccoords, t->dloss, t->cenc, kCompactedRows, t->stream));
     mark(t, 6);
     // fused MLP backward (recompute) and encoding backward on the batch
     NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
@@ -301,10 +319,42 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     mark(t, 7);
     NGP_TRY(ngp_encode_grid_backward(&t->layout, kNetworkBatch, t->ccoords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams, t->stream));
     mark(t, 8);
+    // adaptive batch (ngp.train.cpp:125-133): this step's counters were copied after the loss
+    // pass; the host waits for them while the backward pass runs, then launches the next step's
+    // march on march_stream
+    NGP_TRY(check_cuda(cudaEventSynchronize(t->ev_counts), "train step counters"));
+    const uint32_t c[3] = {t->host_counters[0], t->host_counters[1], t->host_counters[2]};
+    t->measured_before  = c[1];
+    t->measured         = c[2];
+    if (t->measured == 0u) {
+        cudaMemcpy(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+        return fail(NGP_ERR_STATE, "Training stopped unexpectedly. density_grid_occupied_cells=" + std::to_string(t->occupied_cells));
+    }
+    const uint32_t g           = kBatchGranule;
+    const uint32_t next_step   = t->step + 1u;
+    const uint32_t next_infer  = ((std::min(t->measured_before, kMaxSamples) + g - 1u) / g) * g;
+    const uint64_t want        = std::min<uint64_t>((static_cast<uint64_t>(t->rays_per_batch) * kNetworkBatch) / t->measured, kNetworkBatch);
+    const uint32_t next_rays   = std::min(std::max(static_cast<uint32_t>((want + g - 1u) / g * g), g), kNetworkBatch);
+    const bool premarch        = premarch_next && !t->profiling && !grid_update_due(next_step);
+    if (premarch) {
+        // the march writes the other set of march outputs, last read by the previous step (which
+        // ev_counts follows in stream order)
+        t->rays_per_batch    = next_rays;
+        t->inference_samples = next_infer;
+        NGP_TRY(check_cuda(cudaStreamWaitEvent(t->march_stream, t->ev_counts, 0), "march after loss"));
+        NGP_TRY(march_step(t, next_step, t->march_stream));
+        NGP_TRY(check_cuda(cudaEventRecord(t->ev_march, t->march_stream), "record march"));
+    }
     // data parallel: average the fp32 gradient over ranks (one all-reduce per step); every rank
-    // then takes the identical Adam step, so the replicas (and their density grids) stay equal
+    // then takes the identical Adam step, so the replicas (and their density grids) stay equal.
+    // The collective waits for the next step's march: NCCL's kernels must not share the SMs
+    // with a long-running kernel of another stream (a delayed rank stalls every rank).
+    // The gradient crosses NVLink in fp16 (the reference's gradient format, loss-scaled by 128):
+    // half the bytes of fp32; the fp32 accumulation buffer is cleared by the conversion.
     if (t->comm != nullptr) {
-        const ncclResult_t r = ncclAllReduce(t->grads, t->grads, t->n_params, ncclFloat, ncclSum, t->comm, t->stream);
+        if (premarch) NGP_TRY(check_cuda(cudaStreamWaitEvent(t->stream, t->ev_march, 0), "all-reduce after march"));
+        NGP_TRY(ngp_gradients_to_half(t->n_params, t->grads, t->grads16, 1, t->stream));
+        const ncclResult_t r = ncclAllReduce(t->grads16, t->grads16, t->n_params, ncclHalf, ncclSum, t->comm, t->stream);
         if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
     }
     mark(t, 9);
@@ -318,13 +368,13 @@ int train_step(ngp_trainer* t, bool premarch_next) {
         }
     }
     ++t->adam_calls;
-    NGP_TRY(ngp_adam_step_table(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world),
-                                t->master, t->params, t->grads, t->adam_m, t->adam_v, t->adam_steps, 1, t->lr_table, t->lr_table_len, t->stream));
+    if (t->comm != nullptr)
+        NGP_TRY(ngp_adam_step_f16(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world),
+                                  t->master, t->params, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->lr_table, t->lr_table_len, t->stream));
+    else
+        NGP_TRY(ngp_adam_step_table(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale, t->master, t->params,
+                                    t->grads, t->adam_m, t->adam_v, t->adam_steps, 1, t->lr_table, t->lr_table_len, t->stream));
     mark(t, 10);
-    // adaptive batch (ngp.train.cpp:125-133): this step's counters were copied after the loss
-    // pass; the host waits for them while the backward pass and Adam run
-    NGP_TRY(check_cuda(cudaEventSynchronize(t->ev_counts), "train step counters"));
-    const uint32_t c[3] = {t->host_counters[0], t->host_counters[1], t->host_counters[2]};
     if (t->profiling) {
         NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train step"));
         for (int k = 0; k < kTrainPhases; ++k) {
@@ -335,25 +385,10 @@ int train_step(ngp_trainer* t, bool premarch_next) {
         t->inference_samples_sum += t->inference_samples;
         ++t->profiled_steps;
     }
-    t->measured_before = c[1];
-    t->measured        = c[2];
-    if (t->measured == 0u) {
-        cudaMemcpy(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost);
-        return fail(NGP_ERR_STATE, "Training stopped unexpectedly. density_grid_occupied_cells=" + std::to_string(t->occupied_cells));
-    }
-    const uint32_t g     = kBatchGranule;
-    t->inference_samples = ((std::min(t->measured_before, kMaxSamples) + g - 1u) / g) * g;
-    const uint64_t want  = std::min<uint64_t>((static_cast<uint64_t>(t->rays_per_batch) * kNetworkBatch) / t->measured, kNetworkBatch);
-    t->rays_per_batch    = std::min(std::max(static_cast<uint32_t>((want + g - 1u) / g * g), g), kNetworkBatch);
-    ++t->step;
-    if (premarch_next && !t->profiling && !grid_update_due(t->step)) {
-        // the march overwrites coords/rays/numsteps/counters 0-1, which this step last read in
-        // its loss pass (ev_counts follows it)
-        NGP_TRY(check_cuda(cudaStreamWaitEvent(t->march_stream, t->ev_counts, 0), "march after loss"));
-        NGP_TRY(march_step(t, t->step, t->march_stream));
-        NGP_TRY(check_cuda(cudaEventRecord(t->ev_march, t->march_stream), "record march"));
-        t->premarched = true;
-    }
+    t->rays_per_batch    = next_rays;
+    t->inference_samples = next_infer;
+    t->step              = next_step;
+    t->premarched        = premarch;
     return NGP_OK;
 }
 
@@ -442,6 +477,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->master, t->n_params, "params"));
         NGP_TRY(dalloc(t->params, t->n_params, "params fp16"));
         NGP_TRY(dalloc(t->grads, t->n_params, "gradients"));
+        NGP_TRY(dalloc(t->grads16, t->n_params, "fp16 gradients"));
         NGP_TRY(dalloc(t->adam_m, t->n_params, "adam m"));
         NGP_TRY(dalloc(t->adam_v, t->n_params, "adam v"));
         NGP_TRY(dalloc(t->adam_steps, t->n_params, "adam steps"));
@@ -452,12 +488,18 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->grid_indices, kGridCells, "grid indices"));
         NGP_TRY(dalloc(t->bitfield, kGridCells / 8u, "bitfield"));
         NGP_TRY(dalloc(t->occupied, 1, "occupied count"));
-        NGP_TRY(dalloc(t->coords, static_cast<size_t>(kMaxSamples) * 7u, "sample coords"));
-        NGP_TRY(dalloc(t->rays, static_cast<size_t>(kNetworkBatch) * 6u, "rays"));
-        NGP_TRY(dalloc(t->ray_indices, kNetworkBatch, "ray indices"));
-        NGP_TRY(dalloc(t->numsteps, static_cast<size_t>(kNetworkBatch) * 2u, "numsteps"));
+        for (MarchSet& m : t->sets) {
+            NGP_TRY(dalloc(m.coords, static_cast<size_t>(kMaxSamples) * 7u, "sample coords"));
+            NGP_TRY(dalloc(m.rays, static_cast<size_t>(kNetworkBatch) * 6u, "rays"));
+            NGP_TRY(dalloc(m.ray_indices, kNetworkBatch, "ray indices"));
+            NGP_TRY(dalloc(m.numsteps, static_cast<size_t>(kNetworkBatch) * 2u, "numsteps"));
+            NGP_TRY(dalloc(m.counters, 8, "counters"));
+            NGP_TRY(check_cuda(cudaMemsetAsync(m.counters, 0, 8 * sizeof(uint32_t), t->stream), "clear counters"));
+            NGP_TRY(check_cuda(cudaMemsetAsync(m.coords, 0, sizeof(float) * kMaxSamples * 7u, t->stream), "clear coords"));
+        }
+        t->coords = t->sets[0].coords, t->rays = t->sets[0].rays, t->ray_indices = t->sets[0].ray_indices;
+        t->numsteps = t->sets[0].numsteps, t->counters = t->sets[0].counters;
         NGP_TRY(dalloc(t->march_scratch, ngp_march_scratch_words(kNetworkBatch), "march scratch"));
-        NGP_TRY(dalloc(t->counters, 8, "counters"));
         NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
         NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));
         NGP_TRY(dalloc(t->grid_density, kGridCells, "grid density"));
@@ -481,8 +523,6 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(check_cuda(cudaMemsetAsync(t->grid_values, 0, sizeof(float) * kGridCells, s), "clear grid"));
         NGP_TRY(check_cuda(cudaMemsetAsync(t->grid_scratch, 0, sizeof(float) * kGridCells, s), "clear scratch"));
         NGP_TRY(check_cuda(cudaMemsetAsync(t->bitfield, 0xFF, kGridCells / 8u, s), "fill bitfield"));
-        NGP_TRY(check_cuda(cudaMemsetAsync(t->counters, 0, 8 * sizeof(uint32_t), s), "clear counters"));
-        NGP_TRY(check_cuda(cudaMemsetAsync(t->coords, 0, sizeof(float) * kMaxSamples * 7u, s), "clear coords"));
         NGP_TRY(init_params(t));
         return check_cuda(cudaStreamSynchronize(s), "trainer init");
     }();
