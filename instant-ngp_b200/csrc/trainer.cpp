@@ -81,13 +81,14 @@ struct ngp_trainer {
 
     // sampler and network buffers
     // Two sets of march outputs, used by alternate steps, so that the next step's march can run
-    // while this step's loss pass still reads its rays and sample counts.  Set 0 also serves
-    // evaluation and the density-grid samples.
-    MarchSet sets[2];
-    float* coords = nullptr;  // set 0: [MAX_SAMPLES][7]
-    float* rays   = nullptr;  // set 0: [BATCH][6]
-    uint32_t *ray_indices = nullptr, *numsteps = nullptr, *march_scratch = nullptr;
-    uint32_t* counters     = nullptr;  // set 0: 0 rays, 1 samples, 2 compacted
+    // while this step's loss pass still reads its rays and sample counts; a third set serves
+    // evaluation, so that a march launched for the next training step survives evaluation and
+    // rendering calls between train calls.
+    MarchSet sets[3];
+    float* coords = nullptr;  // evaluation set: [MAX_SAMPLES][7]
+    float* rays   = nullptr;  // evaluation set: [BATCH][6]
+    uint32_t *ray_indices = nullptr, *numsteps = nullptr, *march_scratch = nullptr, *eval_march_scratch = nullptr;
+    uint32_t* counters     = nullptr;  // evaluation set: 0 rays, 1 samples, 2 compacted
     uint16_t* enc          = nullptr;  // [32][MAX_SAMPLES] encoded positions
     uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output (training: raw densities)
     uint16_t* cout         = nullptr;  // [COMPACTED_ROWS][16] network output of the compacted samples
@@ -150,7 +151,7 @@ void destroy(ngp_trainer* t) {
     free_split(t->val);
     free_split(t->test);
     void* ptrs[] = {t->master, t->params, t->grads, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
-                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->enc, t->out, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
+                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table};
     for (void* p : ptrs) cudaFree(p);
     for (MarchSet& m : t->sets) cudaFree(m.coords), cudaFree(m.rays), cudaFree(m.ray_indices), cudaFree(m.numsteps), cudaFree(m.counters);
@@ -402,7 +403,7 @@ int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparis
     for (uint32_t off = 0; off < total;) {
         const uint32_t n = std::min(tile, total - off);
         NGP_TRY(ngp_make_eval_rays(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, off, n, t->rays, t->stream));
-        NGP_TRY(ngp_march_rays(n, t->rays, 0, 0, t->bitfield, kMaxSamples, t->coords, t->numsteps, t->march_scratch, t->counters + 1, t->stream));
+        NGP_TRY(ngp_march_rays(n, t->rays, 0, 0, t->bitfield, kMaxSamples, t->coords, t->numsteps, t->eval_march_scratch, t->counters + 1, t->stream));
         uint32_t used = 0;
         NGP_TRY(check_cuda(cudaMemcpyAsync(&used, t->counters + 1, sizeof(used), cudaMemcpyDeviceToHost, t->stream), "eval counter"));
         NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "eval march"));
@@ -497,8 +498,9 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
             NGP_TRY(check_cuda(cudaMemsetAsync(m.counters, 0, 8 * sizeof(uint32_t), t->stream), "clear counters"));
             NGP_TRY(check_cuda(cudaMemsetAsync(m.coords, 0, sizeof(float) * kMaxSamples * 7u, t->stream), "clear coords"));
         }
-        t->coords = t->sets[0].coords, t->rays = t->sets[0].rays, t->ray_indices = t->sets[0].ray_indices;
-        t->numsteps = t->sets[0].numsteps, t->counters = t->sets[0].counters;
+        t->coords = t->sets[2].coords, t->rays = t->sets[2].rays, t->ray_indices = t->sets[2].ray_indices;
+        t->numsteps = t->sets[2].numsteps, t->counters = t->sets[2].counters;
+        NGP_TRY(dalloc(t->eval_march_scratch, ngp_march_scratch_words(kNetworkBatch), "evaluation march scratch"));
         NGP_TRY(dalloc(t->march_scratch, ngp_march_scratch_words(kNetworkBatch), "march scratch"));
         NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
         NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));
@@ -571,7 +573,8 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
     uint32_t loss_rays = t->rays_per_batch;
     for (int32_t i = 0; i < iters; ++i) {
         loss_rays    = t->rays_per_batch;
-        const int st = train_step(t, i + 1 < iters);
+        // the last step also marches the next one: it is consumed by the next train call
+        const int st = train_step(t, true);
         if (st != NGP_OK) {
             cudaStreamSynchronize(t->march_stream);
             t->premarched = false;
