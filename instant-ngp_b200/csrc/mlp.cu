@@ -145,6 +145,27 @@ __device__ __forceinline__ bool stage_wait(uint64_t* mbar, uint32_t& phase) {
     return ok;
 }
 
+// One row's global inputs: 32 fp16 features (feature-major source, coalesced across a warp per
+// feature) and, when the colour network runs, the warped view direction of its record.
+template <bool DIR>
+struct RowInputs {
+    unsigned short x[32];
+    float dir[DIR ? 3 : 1];
+};
+
+template <bool DIR>
+__device__ __forceinline__ void load_row_inputs(const __half* __restrict__ x, uint32_t x_stride, const float* __restrict__ coords,
+                                                uint32_t coord_stride, uint32_t n, uint32_t row, RowInputs<DIR>& in) {
+    const bool valid = row < n;
+    const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+#pragma unroll
+    for (uint32_t k = 0; k < 32; ++k) in.x[k] = valid ? __ldg(xs + static_cast<uint64_t>(k) * x_stride + row) : static_cast<unsigned short>(0);
+    if constexpr (DIR) {
+        const float* c = coords + static_cast<uint64_t>(valid ? row : 0u) * coord_stride;
+        in.dir[0] = __ldg(c + 4), in.dir[1] = __ldg(c + 5), in.dir[2] = __ldg(c + 6);
+    }
+}
+
 struct MlpForwardParams {
     uint32_t n;
     const __half* params;   // packed MLP weights (10,240 halves)
@@ -188,14 +209,19 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
     bool ok         = true;
     const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
 
+    // The next tile's inputs are loaded into registers while this tile's layers run (software
+    // pipelining of the only global-memory reads of the loop).
+    RowInputs<MODE == kModeFull> cur, nxt;
+    if (blockIdx.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur);
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         const uint32_t row   = tile * kRows + t;
         const bool valid     = row < p.n;
+        if (tile + gridDim.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt);
         // ---- input row: 32 fp16 features (coalesced across the warp per feature) ----
         {
             float xv[32];
 #pragma unroll
-            for (uint32_t k = 0; k < 32; ++k) xv[k] = valid ? __half2float(p.x[static_cast<uint64_t>(k) * p.x_stride + row]) : 0.0f;
+            for (uint32_t k = 0; k < 32; ++k) xv[k] = __half2float(__ushort_as_half(cur.x[k]));
             store_row<4, false>(sx, t, xv);
         }
         stage_sync();
@@ -219,6 +245,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
         read_acc<16>(tmem, 64, dens);
         if (MODE == kModeDensity) {
             if (valid) p.out[row] = __float2half_rn(dens[0]);
+            cur = nxt;
             umma::fence_before_sync();
             if (!__syncthreads_and(ok)) break;
             umma::fence_after_sync();
@@ -228,8 +255,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
         {
             float ri[32];
             float sh[16];
-            const float* c = p.coords + static_cast<uint64_t>(valid ? row : 0u) * p.coord_stride;
-            sh16(c[4], c[5], c[6], sh);
+            sh16(cur.dir[0], cur.dir[1], cur.dir[2], sh);
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
                 ri[k]      = dens[k];
@@ -276,6 +302,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
             dst[0]     = make_uint4(pack2(o[0], o[1]), pack2(o[2], o[3]), pack2(o[4], o[5]), pack2(o[6], o[7]));
             dst[1]     = make_uint4(pack2(o[8], o[9]), pack2(o[10], o[11]), pack2(o[12], o[13]), pack2(o[14], o[15]));
         }
+        cur = nxt;
         // a timed-out wait anywhere in the CTA ends the loop for every thread together
         umma::fence_before_sync();
         if (!__syncthreads_and(ok)) break;
@@ -332,21 +359,34 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
     bool first          = true;
     const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
 
+    // next tile's inputs (features, direction, output gradient) prefetched during this tile
+    RowInputs<true> cur, nxt;
+    uint2 dy_cur = make_uint2(0, 0), dy_nxt = make_uint2(0, 0);
+    auto load_dy = [&](uint32_t r) {
+        return r < p.n ? __ldg(reinterpret_cast<const uint2*>(p.dy + static_cast<uint64_t>(r) * 16u)) : make_uint2(0, 0);
+    };
+    if (blockIdx.x < n_tiles) {
+        load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur);
+        dy_cur = load_dy(blockIdx.x * kRows + t);
+    }
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         const uint32_t row = tile * kRows + t;
         const bool valid   = row < p.n;
+        if (tile + gridDim.x < n_tiles) {
+            load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt);
+            dy_nxt = load_dy((tile + gridDim.x) * kRows + t);
+        }
         // ---------------- forward recompute ----------------
         {
             float xv[32];
 #pragma unroll
-            for (uint32_t k = 0; k < 32; ++k) xv[k] = valid ? __half2float(p.x[static_cast<uint64_t>(k) * p.x_stride + row]) : 0.0f;
+            for (uint32_t k = 0; k < 32; ++k) xv[k] = __half2float(__ushort_as_half(cur.x[k]));
             store_row<4, false>(smem + kBX, t, xv);
         }
         float g[16];
         {
             // rgb output gradient: channels 0-2 (extract_rgb_gradients, ngp.train.cu:1244-1253)
-            const uint4* src = reinterpret_cast<const uint4*>(p.dy + static_cast<uint64_t>(valid ? row : 0u) * 16u);
-            const uint4 a = valid ? src[0] : make_uint4(0, 0, 0, 0);
+            const uint2 a = dy_cur;
             const __half2* h = reinterpret_cast<const __half2*>(&a);
             const float2 g01 = __half22float2(h[0]), g23 = __half22float2(h[1]);
 #pragma unroll
@@ -376,8 +416,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         {
             float ri[32], dens[16], sh[16];
             read_acc<16>(tmem, kColD0, dens);
-            const float* c = p.coords + static_cast<uint64_t>(valid ? row : 0u) * p.coord_stride;
-            sh16(c[4], c[5], c[6], sh);
+            sh16(cur.dir[0], cur.dir[1], cur.dir[2], sh);
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
                 ri[k]      = dens[k];
@@ -502,7 +541,9 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
 #pragma unroll
                 for (uint32_t k = 0; k < 32; ++k) p.dx[static_cast<uint64_t>(k) * p.dx_stride + row] = __float2half_rn(d[k]);
         }
-        first = false;
+        first  = false;
+        cur    = nxt;
+        dy_cur = dy_nxt;
         umma::fence_before_sync();
         if (!__syncthreads_and(ok)) break;
         umma::fence_after_sync();
