@@ -47,6 +47,7 @@ int sm_count();
 // Kernel-parameter copy of ngp_grid_layout (only what the device needs).
 struct GridParams {
     uint32_t n_levels;
+    uint32_t dense_mask;  // bit l: level l is dense-indexed (r <= 0x659 and r^3 <= its size)
     uint32_t offsets[NGP_MAX_LEVELS + 1];
     uint32_t resolution[NGP_MAX_LEVELS];
     float scale[NGP_MAX_LEVELS];
@@ -59,6 +60,8 @@ inline GridParams make_grid_params(const ngp_grid_layout& layout) {
     for (uint32_t l = 0; l < layout.n_levels; ++l) {
         p.resolution[l] = layout.resolution[l];
         p.scale[l]      = layout.scale[l];
+        const uint32_t r = layout.resolution[l], size = layout.offsets[l + 1] - layout.offsets[l];
+        if (r <= 0x659u && r * r * r <= size) p.dense_mask |= 1u << l;
     }
     return p;
 }
@@ -84,6 +87,27 @@ __device__ __forceinline__ uint32_t grid_index(uint32_t hashmap_size, uint32_t r
     // +1 corners on the upper faces
     if ((hashmap_size & (hashmap_size - 1u)) == 0u) return index & (hashmap_size - 1u);
     return index < hashmap_size ? index : index % hashmap_size;
+}
+
+// The 8 corner indices of cell (x, y, z) at one level, corner c = x bit 0, y bit 1, z bit 2:
+// grid_index specialised by the level's kind, which is uniform across a warp.  Dense levels:
+// x + y*r + z*r^2 is below 2 * size for points in [0, 1] (size >= r^3 and the +1 corners add at
+// most r^2 + r + 1), so the modulo is one conditional subtraction; hashed levels have a power-of-two size (a mask).
+__device__ __forceinline__ void corner_indices(bool dense, uint32_t size, uint32_t r, uint32_t x, uint32_t y, uint32_t z, uint32_t (&idx)[8]) {
+    if (dense) {
+        const uint32_t r2 = r * r, base = x + y * r + z * r2;
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c) {
+            const uint32_t i = base + (c & 1u) + ((c >> 1) & 1u) * r + (c >> 2) * r2;
+            idx[c]           = i < size ? i : (i - size < size ? i - size : i % size);  // the last case only for points outside [0, 1]
+        }
+    } else {
+        const uint32_t hy[2] = {y * 2654435761u, (y + 1u) * 2654435761u};
+        const uint32_t hz[2] = {z * 805459861u, (z + 1u) * 805459861u};
+        const uint32_t mask  = size - 1u;
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c) idx[c] = ((x + (c & 1u)) ^ hy[(c >> 1) & 1u] ^ hz[c >> 2]) & mask;
+    }
 }
 
 // ---- PCG32 ---------------------------------------------------------------------------------

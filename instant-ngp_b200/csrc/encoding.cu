@@ -211,12 +211,10 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(c
 #pragma unroll
             for (uint32_t d = 0; d < 3; ++d) position_fraction(x[d], scale, frac[j][d], cell[d]);
             const Vec* lvl = tab + off;
+            uint32_t idx[8];
+            corner_indices((grid.dense_mask >> level) & 1u, size, res, cell[0], cell[1], cell[2], idx);
 #pragma unroll
-            for (uint32_t yz = 0; yz < 4; ++yz) {
-                const uint32_t cy = cell[1] + (yz & 1u), cz = cell[2] + (yz >> 1);
-                v[j][2 * yz]      = __ldg(lvl + grid_index(size, res, cell[0], cy, cz));
-                v[j][2 * yz + 1]  = __ldg(lvl + grid_index(size, res, cell[0] + 1u, cy, cz));
-            }
+            for (uint32_t c = 0; c < 8; ++c) v[j][c] = __ldg(lvl + idx[c]);
         }
 #pragma unroll
         for (uint32_t j = 0; j < LPI; ++j) {
@@ -271,16 +269,16 @@ __device__ __forceinline__ void scatter_level(const float (&x)[3], const float (
 #pragma unroll
     for (uint32_t d = 0; d < 3; ++d) position_fraction(x[d], scale, frac[d], cell[d]);
 
+    uint32_t idx[8];
+    corner_indices((grid.dense_mask >> level) & 1u, hashmap_size, resolution, cell[0], cell[1], cell[2], idx);
     const float wx0 = __fsub_rn(1.0f, frac[0]), wx1 = frac[0];
 #pragma unroll
     for (uint32_t yz = 0; yz < 4; ++yz) {
-        const uint32_t cy  = cell[1] + (yz & 1u), cz = cell[2] + (yz >> 1);
         const float wy     = (yz & 1u) ? frac[1] : __fsub_rn(1.0f, frac[1]);
         const float wz     = (yz & 2u) ? frac[2] : __fsub_rn(1.0f, frac[2]);
         const float w0     = __fmul_rn(__fmul_rn(wx0, wy), wz);
         const float w1     = __fmul_rn(__fmul_rn(wx1, wy), wz);
-        const uint32_t i0  = grid_index(hashmap_size, resolution, cell[0], cy, cz);
-        const uint32_t i1  = grid_index(hashmap_size, resolution, cell[0] + 1u, cy, cz);
+        const uint32_t i0  = idx[2 * yz], i1 = idx[2 * yz + 1];
         float c0[F], c1[F];
 #pragma unroll
         for (uint32_t f = 0; f < F; ++f) {
@@ -369,11 +367,11 @@ __device__ __forceinline__ void scatter_level_warp(const float (&x)[3], const fl
     }
     __syncwarp(active);
     if (!leader) return;
+    uint32_t idx[8];
+    corner_indices((grid.dense_mask >> level) & 1u, hashmap_size, resolution, cell[0], cell[1], cell[2], idx);
 #pragma unroll
     for (uint32_t yz = 0; yz < 4; ++yz) {
-        const uint32_t cy = cell[1] + (yz & 1u), cz = cell[2] + (yz >> 1);
-        const uint32_t i0 = grid_index(hashmap_size, resolution, cell[0], cy, cz);
-        const uint32_t i1 = grid_index(hashmap_size, resolution, cell[0] + 1u, cy, cz);
+        const uint32_t i0 = idx[2 * yz], i1 = idx[2 * yz + 1];
         if ((i0 ^ i1) == 1u) {
             const uint32_t lo = i0 < i1 ? i0 : i1;
             float pair[2 * F];
