@@ -169,14 +169,14 @@ COMPACTED_ROWS = BATCH + 1024
 # per unit that one ncu capture of the phase's main kernel measured (the profiles/ summaries of
 # the config-3 step: DRAM read + write of that launch / units it processed).
 PHASE_BYTES = {
-    # coords 12 B read + 32 fp16 features written
-    "encode_fwd_inference": {"unit": "pre-compaction sample", "bytes": 12 + 64, "l2_gather_bytes": 16 * 8 * 4,
-                             "kernel": "encode_forward_points_kernel", "ncu_dram_bytes_per_unit": (63.969280e6 + 56.157440e6) / 1414912},
+    # per marched sample: its record is read once (28 B) to decide how far the ray keeps samples;
+    # the densities evaluated (encoding 12 B in + 64 B out, density 64 B in + 2 B out) cover only the
+    # samples in front of each ray's stopping point, and the kept ones are compacted (92 B each)
+    "inference_compact": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "encode_forward_points_kernel + mlp_forward_kernel<density> + keep/compact"},
     # 12 B rays in + 28 B records out per sample (dominant), 8 B per ray of counts
     "march": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "march_count_kernel + march_write_kernel"},
     "encode_bwd": {"unit": "batch sample", "bytes": 12 + 64, "l2_atomic_bytes": 16 * 8 * 2 * 4, "kernel": "encode_backward_kernel"},
     "adam": {"unit": "parameter", "bytes": 40, "kernel": "adam_kernel"},
-    "compact": {"unit": "batch sample", "bytes": 2 * (28 + 64), "kernel": "keep_pass_kernel + compact_copy_kernel"},
     "mlp_fwd_loss_pad": {"unit": "batch sample", "bytes": 64 + 32 + 28 + 32, "kernel": "mlp_forward_kernel + loss_compacted_kernel"},
     "grid_update": {"unit": "grid cell", "bytes": 16, "kernel": "density grid kernels"},
 }
@@ -192,8 +192,8 @@ def phase_roofline(phases: dict, peaks: dict) -> dict:
     total = sum(ms.values())
     dom = max(ms, key=ms.get)
     t = ms[dom] * 1e-3
-    if dom in ("density_fwd_inference", "mlp_bwd"):
-        flops = (DENSITY_FWD_FLOP * n_inf) if dom == "density_fwd_inference" else (MLP_FWDBWD_FLOP * BATCH)
+    if dom == "mlp_bwd":
+        flops = MLP_FWDBWD_FLOP * BATCH
         achieved = flops / t / 1e12
         return {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": None, "share": round(ms[dom] / total, 3),

@@ -87,6 +87,13 @@ NGP_API int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n, c
  * corners of every point and level, with fp32 vector atomics.  table_grad is fp32 and is
  * accumulated into (zero it first to get the gradient of this batch alone).
  * Replaces encode_grid_backward_kernel (ngp.train.cu:923-960), which accumulates in fp16. */
+/* Forward for a list of points: point rows[r] for r < min(*n_rows, max_rows) (n_rows may be NULL:
+ * max_rows points), read from coords[rows[r]] and written to column rows[r] of out (so out_stride
+ * must exceed every listed index).  Used to encode only the samples whose density is needed. */
+NGP_API int ngp_encode_grid_forward_rows(const ngp_grid_layout* layout, uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows,
+                                         const float* coords, uint32_t coord_stride, const uint16_t* table, uint16_t* out, uint32_t out_stride,
+                                         void* stream);
+
 NGP_API int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t n, const float* coords,
                              uint32_t coord_stride, const uint16_t* dy, uint32_t dy_stride,
                              float* table_grad, void* stream);
@@ -115,6 +122,11 @@ NGP_API int ngp_mlp_forward(uint32_t n, const uint16_t* params, const uint16_t* 
 /* Density network only -> out[n] = raw density (fp16).  Replaces the density-only
  * mlp_forward_64_relu_kernel launch of update_density_grid (ngp.train.cu:1573). */
 NGP_API int ngp_density_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, uint16_t* out, void* stream);
+
+/* Density network for a list of rows: input column rows[r] of x, output out[rows[r]], for
+ * r < min(*n_rows, max_rows) (n_rows may be NULL). */
+NGP_API int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
+                                     uint32_t x_stride, uint16_t* out, void* stream);
 
 /* Number of fp32 scratch values ngp_mlp_backward needs (one weight-gradient partial per CTA). */
 NGP_API uint32_t ngp_mlp_backward_scratch_floats(void);
@@ -250,6 +262,22 @@ NGP_API int ngp_training_compact_by_density(uint32_t rays_per_batch, const uint3
                                             uint16_t* compacted_enc, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
                                             void* stream);
 
+/* Step 1 with the densities evaluated progressively (replaces the encoding + density network
+ * over all pre-compaction samples and ngp_training_compact_by_density): a ray keeps its samples
+ * up to the first whose transmittance falls below 1e-4, so the samples behind it need no density.
+ * Densities are computed for the first 48 samples of every ray, then for the remaining samples of
+ * the rays that have not stopped; every evaluated density equals the full pass's value, so the
+ * kept counts and the compacted outputs are the same.  params: packed fp16 [MLP | grid];
+ * sample_bound: the marched sample count's upper bound (the march's sample limit); enc
+ * ([32][enc_stride], enc_stride >= sample_bound), density ([sample_bound]) and rows
+ * ([sample_bound] uint32) are caller scratch; only evaluated samples' entries are written.
+ * Outputs as ngp_training_compact_by_density; scratch: ngp_loss_scratch_bytes(rays_per_batch). */
+NGP_API int ngp_training_compact_progressive(uint32_t rays_per_batch, const uint32_t* ray_counter, const ngp_grid_layout* layout,
+                                             const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
+                                             uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, float* compacted_coords,
+                                             uint16_t* compacted_enc, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
+                                             void* stream);
+
 /* Step 2, after the full network ran on the compacted rows (compacted_output fp16 [rows][16]):
  * compositing, loss and gradients as ngp_training_loss_and_compact; numsteps ends as
  * (samples in the batch, compacted base). */
@@ -370,10 +398,10 @@ NGP_API int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_
 NGP_API int ngp_nccl_unique_id(uint8_t* out, size_t bytes);
 NGP_API int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank);
 /* Per-phase device time of the training step, summed over the steps since profiling was
- * enabled (cudaEvents between phases): 0 grid update, 1 ray marching, 2 encoding of the
- * inference samples, 3 network forward of the inference samples, 4 loss + compaction + padding,
- * 5 encoding of the batch, 6 network backward, 7 encoding backward, 8 gradient all-reduce,
- * 9 Adam.  out_ms needs 10 floats; out_mean_inference_samples = mean samples evaluated per step. */
+ * enabled (cudaEvents between phases): 0 grid update, 1 ray marching, 2 density evaluation of the
+ * marched samples + compaction, 3 network forward of the compacted samples + loss + padding,
+ * 4 network backward, 5 encoding backward, 6 gradient all-reduce, 7 Adam.  out_ms needs 8 floats;
+ * out_mean_inference_samples = mean marched samples per step. */
 NGP_API int ngp_trainer_set_profiling(ngp_trainer* t, int enable);
 NGP_API int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_steps, float* out_mean_inference_samples);
 /* Occupancy bitfield (2^18 bytes) and density-grid values (2^21 floats) to the host. */

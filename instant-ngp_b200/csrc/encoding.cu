@@ -192,10 +192,13 @@ template <uint32_t F, uint32_t LPI>
 __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(const uint32_t n, const float* __restrict__ coords,
                                                                                const uint32_t coord_stride, const __half* __restrict__ table,
                                                                                __half* __restrict__ out, const uint32_t out_stride,
-                                                                               const __grid_constant__ GridParams grid) {
+                                                                               const __grid_constant__ GridParams grid,
+                                                                               const uint32_t* __restrict__ rows, const uint32_t* __restrict__ n_dev) {
     using Vec        = typename FeatureVec<F>::type;
-    const uint32_t i = blockIdx.x * kEncodeThreads + threadIdx.x;
-    if (i >= n) return;
+    const uint32_t r = blockIdx.x * kEncodeThreads + threadIdx.x;
+    if (r >= (n_dev != nullptr ? min(*n_dev, n) : n)) return;
+    // point i: row r itself, or the r-th entry of a row list (points read and written in place)
+    const uint32_t i = rows != nullptr ? __ldg(rows + r) : r;
     const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
     const float x[3] = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
     const Vec* tab   = reinterpret_cast<const Vec*>(table);
@@ -431,6 +434,21 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_backward_points_kernel(
     }
 }
 
+int launch_points_forward(const ngp_grid_layout& layout, const GridParams& grid, uint32_t n, const float* coords, uint32_t coord_stride,
+                          const uint16_t* table, uint16_t* out, uint32_t out_stride, const uint32_t* rows, const uint32_t* n_dev, cudaStream_t s) {
+    constexpr uint32_t lpi = NGP_ENC_FWD_LEVELS > 0 ? NGP_ENC_FWD_LEVELS : 2;
+    const uint32_t blocks  = (n + kEncodeThreads - 1) / kEncodeThreads;
+    const auto* t          = reinterpret_cast<const __half*>(table);
+    auto* o                = reinterpret_cast<__half*>(out);
+    switch (layout.features_per_level) {
+        case 1: encode_forward_points_kernel<1, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
+        case 2: encode_forward_points_kernel<2, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
+        case 4: encode_forward_points_kernel<4, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
+        default: encode_forward_points_kernel<8, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
+    }
+    return check_launch("encode_forward_points_kernel");
+}
+
 int validate_layout(const ngp_grid_layout* layout) {
     if (layout == nullptr) return fail(NGP_ERR_INVALID, "grid layout is null");
     if (layout->n_levels == 0 || layout->n_levels > NGP_MAX_LEVELS) return fail(NGP_ERR_INVALID, "grid layout: bad level count");
@@ -454,20 +472,7 @@ extern "C" int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n
     if (coord_stride < 3 || out_stride < n) return fail(NGP_ERR_INVALID, "encode forward: bad stride");
     const GridParams grid = make_grid_params(*layout);
 #if NGP_ENC_FWD_LEVELS > 0
-    {
-        constexpr uint32_t lpi = NGP_ENC_FWD_LEVELS;
-        const uint32_t blocks  = (n + kEncodeThreads - 1) / kEncodeThreads;
-        const auto* t          = reinterpret_cast<const __half*>(table);
-        auto* o                = reinterpret_cast<__half*>(out);
-        const cudaStream_t s   = as_stream(stream);
-        switch (layout->features_per_level) {
-            case 1: encode_forward_points_kernel<1, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-            case 2: encode_forward_points_kernel<2, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-            case 4: encode_forward_points_kernel<4, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-            default: encode_forward_points_kernel<8, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-        }
-        return check_launch("encode_forward_points_kernel");
-    }
+    return launch_points_forward(*layout, grid, n, coords, coord_stride, table, out, out_stride, nullptr, nullptr, as_stream(stream));
 #endif
     constexpr uint32_t ppt = NGP_ENC_FWD_PPT;
     const dim3 blocks = encode_grid(NGP_ENC_FWD_INTERLEAVE, (n + kEncodeThreads * ppt - 1) / (kEncodeThreads * ppt), layout->n_levels);
@@ -480,6 +485,18 @@ extern "C" int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n
         default: encode_forward_kernel<8, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
     }
     return check_launch("encode_forward_kernel");
+}
+
+extern "C" int ngp_encode_grid_forward_rows(const ngp_grid_layout* layout, uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows,
+                                            const float* coords, uint32_t coord_stride, const uint16_t* table, uint16_t* out, uint32_t out_stride,
+                                            void* stream) {
+    clear_error();
+    NGP_TRY(validate_layout(layout));
+    if (max_rows == 0) return NGP_OK;
+    if (rows == nullptr || coords == nullptr || table == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "encode forward rows: null pointer");
+    if (coord_stride < 3) return fail(NGP_ERR_INVALID, "encode forward rows: bad stride");
+    return launch_points_forward(*layout, make_grid_params(*layout), max_rows, coords, coord_stride, table, out, out_stride, rows, n_rows,
+                                 as_stream(stream));
 }
 
 extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t n, const float* coords, uint32_t coord_stride,

@@ -379,6 +379,135 @@ __global__ void __launch_bounds__(kCtaThreads) compact_copy_kernel(const __grid_
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Progressive density evaluation.  A ray keeps its samples up to the first whose transmittance
+// drops below 1e-4; the samples behind that point need no density at all, yet they are most of
+// the marched samples.  So the densities are evaluated in two rounds: the first kChunk samples
+// of every ray, then the remaining samples of the rays that have not stopped.  Each evaluated
+// sample's density is the same value the full pass computes (rows are independent), so the
+// kept counts, and everything after them, are unchanged.
+// ---------------------------------------------------------------------------------------------
+#ifndef NGP_KEEP_CHUNK
+#define NGP_KEEP_CHUNK 48
+#endif
+constexpr uint32_t kChunk      = NGP_KEEP_CHUNK;
+constexpr uint32_t kListThreads = 256u;
+
+struct ProgressParams {
+    uint32_t rays_per_batch;
+    const uint32_t* ray_counter;
+    const uint32_t* numsteps;   // [ray][2] (steps, base)
+    const __half* density;      // [samples] raw density (evaluated samples only)
+    const float* coords;
+    uint32_t* kept;             // [ray]
+    uint32_t* steps;            // [ray]
+    float* T;                   // [ray] transmittance after the evaluated samples
+    uint32_t* active;           // [ray] 1 while the ray needs more samples
+    uint32_t* list_off;         // [ray] offset of the ray's rows in its list block
+    uint32_t* list_totals;      // [ray blocks of kListThreads]
+    uint32_t* rows;             // row list (sample indices)
+    uint32_t* n_rows;           // device count of the row list
+    uint32_t* block_totals;     // [ray blocks of kRaysPerCta] kept totals for the compaction
+};
+
+__device__ __forceinline__ uint32_t progress_rays(const ProgressParams& p) {
+    return min(p.ray_counter != nullptr ? *p.ray_counter : p.rays_per_batch, p.rays_per_batch);
+}
+
+// Samples [lo, hi) of ray i evaluated in round `round`.
+__device__ __forceinline__ void round_range(const ProgressParams& p, uint32_t round, uint32_t i, uint32_t& lo, uint32_t& hi) {
+    const uint32_t steps = p.numsteps[2u * i];
+    if (round == 0) {
+        lo = 0, hi = min(steps, kChunk);
+    } else {
+        lo = kChunk, hi = p.active[i] ? steps : kChunk;
+    }
+}
+
+// Per ray: its row count in this round, exclusive offsets within blocks of kListThreads rays.
+__global__ void __launch_bounds__(kListThreads) list_count_kernel(const __grid_constant__ ProgressParams p, uint32_t round) {
+    const uint32_t n = progress_rays(p);
+    const uint32_t i = blockIdx.x * kListThreads + threadIdx.x;
+    uint32_t cnt     = 0;
+    if (i < n) {
+        uint32_t lo, hi;
+        round_range(p, round, i, lo, hi);
+        cnt = hi - lo;
+    }
+    uint32_t total;
+    const uint32_t off = block_exclusive_scan(cnt, total);
+    if (i < n) p.list_off[i] = off;
+    if (threadIdx.x == 0) p.list_totals[blockIdx.x] = total;
+}
+
+// Row list of this round: the sample indices of every ray's range, in ray order.
+__global__ void __launch_bounds__(kCtaThreads) list_write_kernel(const __grid_constant__ ProgressParams p, uint32_t round) {
+    const uint32_t n    = progress_rays(p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    if (i >= n) return;
+    uint32_t lo, hi;
+    round_range(p, round, i, lo, hi);
+    const uint32_t dst  = p.list_totals[i / kListThreads] + p.list_off[i];
+    const uint32_t base = p.numsteps[2u * i + 1u];
+    for (uint32_t j = lane; j < hi - lo; j += 32u) p.rows[dst + j] = base + lo + j;
+}
+
+// Transmittance over this round's samples (pass 1's loop, resumed where the last round ended).
+// The last round also writes the per-CTA kept totals for the compaction.
+__global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_constant__ ProgressParams p, uint32_t round) {
+    __shared__ uint32_t s_kept[kRaysPerCta];
+    const uint32_t n    = progress_rays(p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    uint32_t kept       = 0;
+    if (i < n) {
+        const uint32_t steps = p.numsteps[2u * i], base = p.numsteps[2u * i + 1u];
+        float T              = round == 0 ? 1.0f : p.T[i];
+        kept                 = round == 0 ? 0u : p.kept[i];
+        const bool run       = round == 0 || p.active[i];
+        bool stopped         = false;
+        if (run) {
+            uint32_t lo, hi;
+            round_range(p, round, i, lo, hi);
+            const __half* dens = p.density + base;
+            const float* c     = p.coords + static_cast<uint64_t>(base) * 7u;
+            for (uint32_t c0 = lo; c0 < hi; c0 += 32u) {
+                const uint32_t j  = c0 + lane;
+                const bool valid  = j < hi;
+                const float d     = valid ? __half2float(dens[j]) : 0.0f;
+                const float dt    = valid ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
+                const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
+                const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+                const bool keep   = valid && !(Tb < kTransmittanceEps);
+                const uint32_t nk = __popc(__ballot_sync(0xFFFFFFFFu, keep));
+                if (nk > 0) T = __shfl_sync(0xFFFFFFFFu, Tb * (1.0f - alpha), nk - 1u);
+                kept += nk;
+                if (nk < min(32u, hi - c0)) {
+                    stopped = true;
+                    break;
+                }
+            }
+            if (lane == 0) {
+                p.kept[i] = kept;
+                p.T[i]    = T;
+                if (round == 0) {
+                    p.steps[i]  = steps;
+                    p.active[i] = (!stopped && hi < steps) ? 1u : 0u;
+                }
+            }
+        }
+    }
+    if (round == 0) return;
+    if (lane == 0) s_kept[warp] = kept;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t total = 0;
+        for (uint32_t w = 0; w < kRaysPerCta; ++w) total += s_kept[w];
+        p.block_totals[blockIdx.x] = total;
+    }
+}
+
 struct CompactedLossParams {
     uint32_t rays_per_batch;
     uint32_t step;
@@ -528,7 +657,8 @@ __global__ void __launch_bounds__(kThreads) eval_composite_kernel(uint32_t n_pix
 }
 
 constexpr size_t loss_scratch_size(uint32_t max_rays) {
-    return static_cast<size_t>(max_rays) * 20u + ((max_rays + kRaysPerCta - 1u) / kRaysPerCta) * 4u + 256u;
+    return static_cast<size_t>(max_rays) * 20u + ((max_rays + kRaysPerCta - 1u) / kRaysPerCta) * 4u +
+           ((max_rays + kListThreads - 1u) / kListThreads) * 4u + 256u;
 }
 
 }  // namespace
@@ -617,6 +747,70 @@ extern "C" int ngp_training_compact_by_density(uint32_t rays_per_batch, const ui
     scan_kept_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, compacted_counter, kNetworkBatch);
     NGP_TRY(check_launch("scan_kept_kernel"));
     compact_copy_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
+    return check_launch("compact_copy_kernel");
+}
+
+extern "C" int ngp_training_compact_progressive(uint32_t rays_per_batch, const uint32_t* ray_counter, const ngp_grid_layout* layout,
+                                                const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
+                                                uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, float* compacted_coords,
+                                                uint16_t* compacted_enc, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
+                                                void* stream) {
+    clear_error();
+    if (rays_per_batch == 0) return NGP_OK;
+    if (layout == nullptr || params == nullptr || coords == nullptr || numsteps == nullptr || enc == nullptr || density == nullptr || rows == nullptr ||
+        compacted_coords == nullptr || compacted_counter == nullptr || scratch == nullptr || enc_stride < sample_bound)
+        return fail(NGP_ERR_INVALID, "progressive compaction: invalid input");
+    if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "progressive compaction: scratch too small");
+    if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "progressive compaction: scratch must be 16-byte aligned");
+    const cudaStream_t s       = as_stream(stream);
+    const uint32_t R           = rays_per_batch;
+    const uint32_t warp_blocks = (R + kRaysPerCta - 1) / kRaysPerCta;
+    const uint32_t list_blocks = (R + kListThreads - 1) / kListThreads;
+    unsigned char* sc          = static_cast<unsigned char*>(scratch);
+    ProgressParams p{};
+    p.rays_per_batch = R;
+    p.ray_counter    = ray_counter;
+    p.numsteps       = numsteps;
+    p.density        = reinterpret_cast<const __half*>(density);
+    p.coords         = coords;
+    p.steps          = reinterpret_cast<uint32_t*>(sc);
+    p.kept           = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 4u);
+    p.T              = reinterpret_cast<float*>(sc + static_cast<size_t>(R) * 8u);
+    p.list_off       = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 12u);
+    p.active         = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 16u);
+    p.block_totals   = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 20u);
+    p.list_totals    = p.block_totals + warp_blocks;
+    p.rows           = rows;
+    p.n_rows         = p.list_totals + list_blocks;
+    const uint32_t bounds[2] = {std::min(sample_bound, R * kChunk), sample_bound};
+    for (uint32_t round = 0; round < 2; ++round) {
+        list_count_kernel<<<list_blocks, kListThreads, 0, s>>>(p, round);
+        NGP_TRY(check_launch("list_count_kernel"));
+        scan_kept_kernel<<<1, 1024, 0, s>>>(p.list_totals, list_blocks, p.n_rows, 0xFFFFFFFFu);
+        NGP_TRY(check_launch("scan_kept_kernel"));
+        list_write_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
+        NGP_TRY(check_launch("list_write_kernel"));
+        NGP_TRY(ngp_encode_grid_forward_rows(layout, bounds[round], rows, p.n_rows, coords, 7, params + 10240u, enc, enc_stride, stream));
+        NGP_TRY(ngp_density_forward_rows(bounds[round], rows, p.n_rows, params, enc, enc_stride, density, stream));
+        keep_round_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
+        NGP_TRY(check_launch("keep_round_kernel"));
+    }
+    // compaction of the kept samples (as ngp_training_compact_by_density after its keep pass)
+    KeepParams k{};
+    k.rays_per_batch = R;
+    k.ray_counter    = ray_counter;
+    k.coords         = coords;
+    k.enc            = reinterpret_cast<const __half*>(enc);
+    k.enc_stride     = enc_stride;
+    k.numsteps       = numsteps;
+    k.coords_out     = compacted_coords;
+    k.enc_out        = reinterpret_cast<__half*>(compacted_enc);
+    k.steps          = p.steps;
+    k.kept           = p.kept;
+    k.block_totals   = p.block_totals;
+    scan_kept_kernel<<<1, 1024, 0, s>>>(k.block_totals, warp_blocks, compacted_counter, kNetworkBatch);
+    NGP_TRY(check_launch("scan_kept_kernel"));
+    compact_copy_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(k);
     return check_launch("compact_copy_kernel");
 }
 

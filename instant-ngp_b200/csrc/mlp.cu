@@ -147,21 +147,26 @@ __device__ __forceinline__ bool stage_wait(uint64_t* mbar, uint32_t& phase) {
 
 // One row's global inputs: 32 fp16 features (feature-major source, coalesced across a warp per
 // feature) and, when the colour network runs, the warped view direction of its record.
+// A row list (optional) maps tile row r to sample rows[r]: its features, record and output are
+// read and written at that sample's position.
 template <bool DIR>
 struct RowInputs {
     unsigned short x[32];
     float dir[DIR ? 3 : 1];
+    uint32_t col;  // the sample this row reads and writes
 };
 
 template <bool DIR>
 __device__ __forceinline__ void load_row_inputs(const __half* __restrict__ x, uint32_t x_stride, const float* __restrict__ coords,
-                                                uint32_t coord_stride, uint32_t n, uint32_t row, RowInputs<DIR>& in) {
+                                                uint32_t coord_stride, uint32_t n, uint32_t row, RowInputs<DIR>& in,
+                                                const uint32_t* __restrict__ rows = nullptr) {
     const bool valid = row < n;
+    in.col           = valid ? (rows != nullptr ? __ldg(rows + row) : row) : 0u;
     const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
 #pragma unroll
-    for (uint32_t k = 0; k < 32; ++k) in.x[k] = valid ? __ldg(xs + static_cast<uint64_t>(k) * x_stride + row) : static_cast<unsigned short>(0);
+    for (uint32_t k = 0; k < 32; ++k) in.x[k] = valid ? __ldg(xs + static_cast<uint64_t>(k) * x_stride + in.col) : static_cast<unsigned short>(0);
     if constexpr (DIR) {
-        const float* c = coords + static_cast<uint64_t>(valid ? row : 0u) * coord_stride;
+        const float* c = coords + static_cast<uint64_t>(in.col) * coord_stride;
         in.dir[0] = __ldg(c + 4), in.dir[1] = __ldg(c + 5), in.dir[2] = __ldg(c + 6);
     }
 }
@@ -175,6 +180,8 @@ struct MlpForwardParams {
     uint32_t coord_stride;
     __half* out;            // [n][16] row-major (MODE full) or [n] raw density (MODE density)
     __half* density_rgb_in; // optional: density outputs, feature-major [16][x_stride]
+    const uint32_t* rows;   // optional row list (see RowInputs)
+    const uint32_t* n_dev;  // optional device-side row count (<= n)
 };
 
 enum : int { kModeFull = 0, kModeDensity = 1 };
@@ -207,16 +214,17 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
     const uint32_t a_sx = umma::smem_addr(sx), a_shd = umma::smem_addr(shd), a_sw = umma::smem_addr(sw);
     uint32_t phase  = 0;
     bool ok         = true;
-    const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
+    const uint32_t n       = p.n_dev != nullptr ? min(*p.n_dev, p.n) : p.n;
+    const uint32_t n_tiles = (n + kRows - 1) / kRows;
 
     // The next tile's inputs are loaded into registers while this tile's layers run (software
     // pipelining of the only global-memory reads of the loop).
     RowInputs<MODE == kModeFull> cur, nxt;
-    if (blockIdx.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur);
+    if (blockIdx.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, blockIdx.x * kRows + t, cur, p.rows);
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         const uint32_t row   = tile * kRows + t;
-        const bool valid     = row < p.n;
-        if (tile + gridDim.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt);
+        const bool valid     = row < n;
+        if (tile + gridDim.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
         // ---- input row: 32 fp16 features (coalesced across the warp per feature) ----
         {
             float xv[32];
@@ -244,7 +252,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
         float dens[16];
         read_acc<16>(tmem, 64, dens);
         if (MODE == kModeDensity) {
-            if (valid) p.out[row] = __float2half_rn(dens[0]);
+            if (valid) p.out[cur.col] = __float2half_rn(dens[0]);
             cur = nxt;
             umma::fence_before_sync();
             if (!__syncthreads_and(ok)) break;
@@ -264,7 +272,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
             store_row<4, false>(sx, t, ri);
             if (p.density_rgb_in != nullptr && valid)
 #pragma unroll
-                for (int k = 0; k < 16; ++k) p.density_rgb_in[static_cast<uint64_t>(k) * p.x_stride + row] = __float2half_rn(dens[k]);
+                for (int k = 0; k < 16; ++k) p.density_rgb_in[static_cast<uint64_t>(k) * p.x_stride + cur.col] = __float2half_rn(dens[k]);
         }
         stage_sync();
         if (t == 0) {
@@ -298,7 +306,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
         read_acc<16>(tmem, 64, o);
         o[3] = dens[0];
         if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<uint64_t>(row) * 16u);
+            uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<uint64_t>(cur.col) * 16u);
             dst[0]     = make_uint4(pack2(o[0], o[1]), pack2(o[2], o[3]), pack2(o[4], o[5]), pack2(o[6], o[7]));
             dst[1]     = make_uint4(pack2(o[8], o[9]), pack2(o[10], o[11]), pack2(o[12], o[13]), pack2(o[14], o[15]));
         }
@@ -659,7 +667,7 @@ extern "C" int ngp_mlp_forward(uint32_t n, const uint16_t* params, const uint16_
     if (x_stride < n || coord_stride < 7) return fail(NGP_ERR_INVALID, "mlp forward: bad stride");
     NGP_TRY(ensure_attrs());
     MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
-                       reinterpret_cast<__half*>(out), reinterpret_cast<__half*>(density_rgb_in)};
+                       reinterpret_cast<__half*>(out), reinterpret_cast<__half*>(density_rgb_in), nullptr, nullptr};
     const uint32_t n_tiles = (n + kRows - 1) / kRows;
     const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull>), n_tiles, kFwdTmemCols);
     mlp_forward_kernel<kModeFull><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
@@ -673,8 +681,22 @@ extern "C" int ngp_density_forward(uint32_t n, const uint16_t* params, const uin
     if (x_stride < n) return fail(NGP_ERR_INVALID, "density forward: bad stride");
     NGP_TRY(ensure_attrs());
     MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7,
-                       reinterpret_cast<__half*>(out), nullptr};
+                       reinterpret_cast<__half*>(out), nullptr, nullptr, nullptr};
     const uint32_t n_tiles = (n + kRows - 1) / kRows;
+    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity>), n_tiles, kFwdTmemCols);
+    mlp_forward_kernel<kModeDensity><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
+    return check_launch("mlp_forward_kernel<density>");
+}
+
+extern "C" int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
+                                        uint32_t x_stride, uint16_t* out, void* stream) {
+    clear_error();
+    if (max_rows == 0) return NGP_OK;
+    if (rows == nullptr || params == nullptr || x == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "density forward rows: null pointer");
+    NGP_TRY(ensure_attrs());
+    MlpForwardParams p{max_rows, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7,
+                       reinterpret_cast<__half*>(out), nullptr, rows, n_rows};
+    const uint32_t n_tiles = (max_rows + kRows - 1) / kRows;
     const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity>), n_tiles, kFwdTmemCols);
     mlp_forward_kernel<kModeDensity><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
     return check_launch("mlp_forward_kernel<density>");

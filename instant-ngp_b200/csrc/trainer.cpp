@@ -26,7 +26,7 @@ using namespace ngp;
 namespace {
 
 constexpr uint32_t kMlpParams  = 10240;
-constexpr int kTrainPhases     = 10;  // see ngp_trainer_phase_times
+constexpr int kTrainPhases     = 8;  // see ngp_trainer_phase_times
 constexpr uint32_t kLrTableCapacity = 1u << 20;
 constexpr uint32_t kLrTableBlock    = 4096u;
 
@@ -49,6 +49,10 @@ struct Split {
 };
 
 }  // namespace
+
+#ifndef NGP_PROGRESSIVE
+#define NGP_PROGRESSIVE 1  // 0: densities of every pre-compaction sample
+#endif
 
 struct MarchSet {
     float* coords         = nullptr;  // [MAX_SAMPLES][7]
@@ -91,6 +95,7 @@ struct ngp_trainer {
     uint32_t* counters     = nullptr;  // evaluation set: 0 rays, 1 samples, 2 compacted
     uint16_t* enc          = nullptr;  // [32][MAX_SAMPLES] encoded positions
     uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output (training: raw densities)
+    uint32_t* rows         = nullptr;  // [MAX_SAMPLES] row list of the progressive density evaluation
     uint16_t* cout         = nullptr;  // [COMPACTED_ROWS][16] network output of the compacted samples
     uint16_t* grid_density = nullptr;  // [2^21] raw density of the grid samples
     float* ccoords         = nullptr;  // [COMPACTED_ROWS][7] compacted
@@ -151,7 +156,7 @@ void destroy(ngp_trainer* t) {
     free_split(t->val);
     free_split(t->test);
     void* ptrs[] = {t->master, t->params, t->grads, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
-                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
+                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->rows, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table};
     for (void* p : ptrs) cudaFree(p);
     for (MarchSet& m : t->sets) cudaFree(m.coords), cudaFree(m.rays), cudaFree(m.ray_indices), cudaFree(m.numsteps), cudaFree(m.counters);
@@ -292,34 +297,38 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     }
     const uint32_t rng_step = t->step * static_cast<uint32_t>(t->world) + static_cast<uint32_t>(t->rank);
     mark(t, 2);
-    // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524): only the density
-    // network is needed to decide which samples each ray keeps
+    // evaluate_network over the pre-compaction samples (ngp.train.cu:1494-1524) and compaction
+    // (1932-1944): only the densities decide which samples a ray keeps, and only the samples in
+    // front of each ray's stopping point need them
     const MarchSet& m = t->sets[t->step & 1u];
+#if NGP_PROGRESSIVE
+    NGP_TRY(ngp_training_compact_progressive(t->rays_per_batch, m.counters + 0, &t->layout, t->params, m.coords, t->inference_samples, m.numsteps,
+                                             t->enc, t->inference_samples, t->out, t->rows, t->ccoords, t->cenc, m.counters + 2, t->loss_scratch,
+                                             t->loss_scratch_bytes, t->stream));
+#else
     NGP_TRY(encode(t, t->inference_samples, m.coords, t->enc, t->inference_samples));
-    mark(t, 3);
     NGP_TRY(ngp_density_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->out, t->stream));
-    mark(t, 4);
-    // compaction (ngp.train.cu:1932-1944): the kept samples' records and encodings
     NGP_TRY(ngp_training_compact_by_density(t->rays_per_batch, m.counters + 0, t->out, m.coords, t->enc, t->inference_samples, m.numsteps,
                                             t->ccoords, t->cenc, m.counters + 2, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+#endif
     // the step's counters are final here: the host reads them (for the next step's batch size)
     // while the rest of the step runs
     NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, m.counters, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
     NGP_TRY(check_cuda(cudaEventRecord(t->ev_counts, t->stream), "record counters"));
-    mark(t, 5);
+    mark(t, 3);
     // the full network on the compacted rows, then compositing, loss and padding (1944-1956)
     NGP_TRY(ngp_mlp_forward(kCompactedRows, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->cout, nullptr, t->stream));
     NGP_TRY(ngp_training_loss_compacted(t->rays_per_batch, rng_step, m.counters + 0, s.pixels, s.frames, s.width, s.height, t->cout, m.ray_indices,
                                         m.rays, m.numsteps, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->loss_scratch_bytes,
                                         t->stream));
     NGP_TRY(ngp_pad_training_batch_enc(m.counters + 2, t->ccoords, t->dloss, t->cenc, kCompactedRows, t->stream));
-    mark(t, 6);
+    mark(t, 4);
     // fused MLP backward (recompute) and encoding backward on the batch
     NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
                              t->mlp_scratch_floats, t->grads, nullptr, 1.0f, t->stream));
-    mark(t, 7);
+    mark(t, 5);
     NGP_TRY(ngp_encode_grid_backward(&t->layout, kNetworkBatch, t->ccoords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams, t->stream));
-    mark(t, 8);
+    mark(t, 6);
     // adaptive batch (ngp.train.cpp:125-133): this step's counters were copied after the loss
     // pass; the host waits for them while the backward pass runs, then launches the next step's
     // march on march_stream
@@ -358,7 +367,7 @@ int train_step(ngp_trainer* t, bool premarch_next) {
         const ncclResult_t r = ncclAllReduce(t->grads16, t->grads16, t->n_params, ncclHalf, ncclSum, t->comm, t->stream);
         if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
     }
-    mark(t, 9);
+    mark(t, 7);
     // step_optimizer (ngp.train.cu:1973-1980)
     if (t->adam_calls + 1u > t->lr_table_len) {
         // extend the bias-corrected rate table by a block of step counts
@@ -375,7 +384,7 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     else
         NGP_TRY(ngp_adam_step_table(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale, t->master, t->params,
                                     t->grads, t->adam_m, t->adam_v, t->adam_steps, 1, t->lr_table, t->lr_table_len, t->stream));
-    mark(t, 10);
+    mark(t, 8);
     if (t->profiling) {
         NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train step"));
         for (int k = 0; k < kTrainPhases; ++k) {
@@ -504,6 +513,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->march_scratch, ngp_march_scratch_words(kNetworkBatch), "march scratch"));
         NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
         NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));
+        NGP_TRY(dalloc(t->rows, kMaxSamples, "row list"));
         NGP_TRY(dalloc(t->grid_density, kGridCells, "grid density"));
         NGP_TRY(dalloc(t->ccoords, static_cast<size_t>(kCompactedRows) * 7u, "compacted coords"));
         NGP_TRY(dalloc(t->cout, static_cast<size_t>(kCompactedRows) * 16u, "compacted network output"));

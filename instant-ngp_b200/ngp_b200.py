@@ -287,6 +287,15 @@ def training_compact_by_density(rays_per_batch, ray_counter, density, coords, nu
            "ngp_training_compact_by_density")
 
 
+def training_compact_progressive(rays_per_batch, ray_counter, layout, params, coords, sample_bound, numsteps, enc, density, rows,
+                                 compacted_coords, compacted_enc, compacted_counter, scratch, enc_stride=None, stream=None) -> None:
+    _check(lib().ngp_training_compact_progressive(_u32(rays_per_batch), _ptr(ray_counter), ctypes.byref(layout), _ptr(params), _ptr(coords),
+                                                  _u32(sample_bound), _ptr(numsteps), _ptr(enc), _u32(enc.shape[1] if enc_stride is None else enc_stride),
+                                                  _ptr(density), _ptr(rows), _ptr(compacted_coords), _ptr(compacted_enc), _ptr(compacted_counter),
+                                                  _ptr(scratch), ctypes.c_size_t(scratch.numel() * scratch.element_size()), _stream(stream)),
+           "ngp_training_compact_progressive")
+
+
 def training_loss_compacted(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, compacted_output, ray_indices, rays,
                             numsteps, compacted_coords, dloss_doutput, loss_values, scratch, stream=None) -> None:
     _check(lib().ngp_training_loss_compacted(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),
@@ -473,17 +482,17 @@ class InstantNGP:
         p = np.ascontiguousarray(params, np.float32)
         _check(lib().ngp_trainer_set_params(self.handle, ctypes.c_void_p(p.ctypes.data), _u32(p.size)), "ngp_trainer_set_params")
 
-    PHASES = ("grid_update", "march", "encode_fwd_inference", "density_fwd_inference", "compact", "mlp_fwd_loss_pad", "mlp_bwd",
-              "encode_bwd", "allreduce", "adam")
+    PHASES = ("grid_update", "march", "inference_compact", "mlp_fwd_loss_pad", "mlp_bwd", "encode_bwd", "allreduce", "adam")
 
     def set_profiling(self, enable: bool = True) -> None:
         _check(lib().ngp_trainer_set_profiling(self.handle, ctypes.c_int(1 if enable else 0)), "ngp_trainer_set_profiling")
 
     def phase_times(self) -> dict:
-        out = (ctypes.c_float * 10)()
+        out = (ctypes.c_float * len(self.PHASES))()
         steps = ctypes.c_uint32(0)
         mean_n = ctypes.c_float(0)
-        _check(lib().ngp_trainer_phase_times(self.handle, out, _u32(10), ctypes.byref(steps), ctypes.byref(mean_n)), "ngp_trainer_phase_times")
+        _check(lib().ngp_trainer_phase_times(self.handle, out, _u32(len(self.PHASES)), ctypes.byref(steps), ctypes.byref(mean_n)),
+               "ngp_trainer_phase_times")
         return {"steps": steps.value, "mean_inference_samples": mean_n.value, "ms": dict(zip(self.PHASES, list(out)))}
 
     def join(self, unique_id: bytes, world: int, rank: int) -> None:

@@ -486,3 +486,70 @@ def test_density_first_flow_matches_loss_and_compact(ngp, small_scene, blob_bitf
     # some rays stopped early (transmittance), so the flow's keep decision was exercised
     steps = ns.cpu().numpy()[:, 0]
     assert (kept[kept > 0] < steps[kept > 0]).any()
+
+
+def test_progressive_density_evaluation_matches_full(ngp, small_scene, blob_bitfield):
+    """Densities evaluated only in front of each ray's stopping point (first 48 samples of every
+    ray, then the rest of the rays still going) give the same kept counts, compacted records and
+    encodings as evaluating every marched sample, bit for bit, including the ray straddling the
+    2^18 end and rays that stop inside and after the first round."""
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    bits = T(blob_bitfield)
+    n, limit, step, batch = 12288, 1 << 21, 6, 1 << 18
+    rows_n = ngp.compacted_rows()
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    layout = ngp.grid_layout(16, 2, 19, 16, math.log2(128.0) / 15.0)
+    _, table, _ = workloads.encode_inputs(1, layout.n_params, 16, 2, seed=4)
+    table = (table.astype(np.float32) * 2e4).astype(np.float16)
+    mlp = workloads.xavier_mlp_params(9)
+    # raw density = positive weights . ReLU(hidden): rays stop after tens of samples, some inside
+    # the first round and some after it
+    mlp[2048:2048 + 64] = np.random.default_rng(3).uniform(0.2, 0.5, 64).astype(np.float16)
+    params = T(np.concatenate([mlp, table]).view(np.int16))
+    ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    ridx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    msc = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
+    rc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, coords, rays, ridx, ns, msc, rc, sc)
+    torch.cuda.synchronize()
+    total = int(sc.item())
+    m = (total + 127) // 128 * 128
+    scratch = torch.zeros(ngp.loss_scratch_bytes(n), dtype=torch.uint8, device="cuda")
+    # every sample
+    enc = torch.zeros((32, m), dtype=torch.float16, device="cuda")
+    ngp.encode_grid_forward(layout, coords, params[10240:], enc, n=m, coord_stride=7, out_stride=m)
+    dens = torch.zeros(m, dtype=torch.float16, device="cuda")
+    ngp.density_forward(params[:10240], enc, dens, n=m, x_stride=m)
+    ns_a, cc_a = ns.clone(), torch.zeros(1, dtype=torch.int32, device="cuda")
+    cco_a = torch.zeros((rows_n, 7), dtype=torch.float32, device="cuda")
+    cen_a = torch.zeros((32, rows_n), dtype=torch.float16, device="cuda")
+    ngp.training_compact_by_density(n, rc, dens, coords, ns_a, cco_a, cc_a, scratch, enc=enc, enc_stride=m, compacted_enc=cen_a)
+    kept_a = scratch[4 * n: 8 * n].view(torch.int32).clone()
+    # progressive
+    enc_b = torch.zeros((32, m), dtype=torch.float16, device="cuda")
+    dens_b = torch.zeros(m, dtype=torch.float16, device="cuda")
+    rows = torch.zeros(m, dtype=torch.int32, device="cuda")
+    ns_b, cc_b = ns.clone(), torch.zeros(1, dtype=torch.int32, device="cuda")
+    cco_b = torch.zeros((rows_n, 7), dtype=torch.float32, device="cuda")
+    cen_b = torch.zeros((32, rows_n), dtype=torch.float16, device="cuda")
+    ngp.training_compact_progressive(n, rc, layout, params, coords, m, ns_b, enc_b, dens_b, rows, cco_b, cen_b, cc_b, scratch)
+    kept_b = scratch[4 * n: 8 * n].view(torch.int32).clone()
+    torch.cuda.synchronize()
+    assert int(cc_a.item()) == int(cc_b.item()) == batch
+    assert (kept_a == kept_b).all()
+    assert (ns_a == ns_b).all()
+    assert cco_a.cpu().numpy().tobytes() == cco_b.cpu().numpy().tobytes()
+    assert cen_a.cpu().numpy().view(np.uint16).tobytes() == cen_b.cpu().numpy().view(np.uint16).tobytes()
+    steps = ns.cpu().numpy()[:, 0]
+    kept = kept_a.cpu().numpy()
+    stop0 = int(((kept < 48) & (kept < steps)).sum())
+    stop1 = int(((kept > 48) & (kept < steps)).sum())
+    assert stop0 > 0 and stop1 > 0, (stop0, stop1, np.percentile(kept[steps > 0], [10, 50, 90]))  # stops in both rounds
+    evaluated = int((dens_b != 0).sum().item())
+    assert evaluated < total  # densities only in front of the stopping points
