@@ -382,15 +382,27 @@ __global__ void __launch_bounds__(kCtaThreads) compact_copy_kernel(const __grid_
 // ---------------------------------------------------------------------------------------------
 // Progressive density evaluation.  A ray keeps its samples up to the first whose transmittance
 // drops below 1e-4; the samples behind that point need no density at all, yet they are most of
-// the marched samples.  So the densities are evaluated in two rounds: the first kChunk samples
-// of every ray, then the remaining samples of the rays that have not stopped.  Each evaluated
+// the marched samples.  So the densities are evaluated in rounds over growing sample windows
+// (kRoundEnd), each round only for the rays that have not stopped yet.  Each evaluated
 // sample's density is the same value the full pass computes (rows are independent), so the
 // kept counts, and everything after them, are unchanged.
 // ---------------------------------------------------------------------------------------------
-#ifndef NGP_KEEP_CHUNK
-#define NGP_KEEP_CHUNK 48
+// Round r evaluates samples [kRoundEnd[r-1], kRoundEnd[r]) of the rays still going (the last
+// round: all remaining samples).
+#ifndef NGP_KEEP_ROUND0
+#define NGP_KEEP_ROUND0 48
 #endif
-constexpr uint32_t kChunk      = NGP_KEEP_CHUNK;
+#ifndef NGP_KEEP_ROUND1
+#define NGP_KEEP_ROUND1 0  // > 0: a third round (measured slower: launch overhead)
+#endif
+#if NGP_KEEP_ROUND1 > 0
+#define NGP_KEEP_ROUND_LIST NGP_KEEP_ROUND0, NGP_KEEP_ROUND1, 0xFFFFFFFFu
+#else
+#define NGP_KEEP_ROUND_LIST NGP_KEEP_ROUND0, 0xFFFFFFFFu
+#endif
+constexpr uint32_t kRoundEnd[] = {NGP_KEEP_ROUND_LIST};
+constexpr uint32_t kRounds     = sizeof(kRoundEnd) / sizeof(kRoundEnd[0]);
+__constant__ uint32_t c_round_end[kRounds] = {NGP_KEEP_ROUND_LIST};
 constexpr uint32_t kListThreads = 256u;
 
 struct ProgressParams {
@@ -414,14 +426,11 @@ __device__ __forceinline__ uint32_t progress_rays(const ProgressParams& p) {
     return min(p.ray_counter != nullptr ? *p.ray_counter : p.rays_per_batch, p.rays_per_batch);
 }
 
-// Samples [lo, hi) of ray i evaluated in round `round`.
+// Samples [lo, hi) of ray i evaluated in round `round` (empty once the ray has stopped).
 __device__ __forceinline__ void round_range(const ProgressParams& p, uint32_t round, uint32_t i, uint32_t& lo, uint32_t& hi) {
     const uint32_t steps = p.numsteps[2u * i];
-    if (round == 0) {
-        lo = 0, hi = min(steps, kChunk);
-    } else {
-        lo = kChunk, hi = p.active[i] ? steps : kChunk;
-    }
+    lo                   = round == 0 ? 0u : min(c_round_end[round - 1], steps);
+    hi                   = (round == 0 || p.active[i]) ? min(c_round_end[round], steps) : lo;
 }
 
 // Per ray: its row count in this round, exclusive offsets within blocks of kListThreads rays.
@@ -489,16 +498,14 @@ __global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_co
                 }
             }
             if (lane == 0) {
-                p.kept[i] = kept;
-                p.T[i]    = T;
-                if (round == 0) {
-                    p.steps[i]  = steps;
-                    p.active[i] = (!stopped && hi < steps) ? 1u : 0u;
-                }
+                p.kept[i]   = kept;
+                p.T[i]      = T;
+                p.active[i] = (!stopped && hi < steps) ? 1u : 0u;
+                if (round == 0) p.steps[i] = steps;
             }
         }
     }
-    if (round == 0) return;
+    if (round + 1u < kRounds) return;
     if (lane == 0) s_kept[warp] = kept;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -782,16 +789,18 @@ extern "C" int ngp_training_compact_progressive(uint32_t rays_per_batch, const u
     p.list_totals    = p.block_totals + warp_blocks;
     p.rows           = rows;
     p.n_rows         = p.list_totals + list_blocks;
-    const uint32_t bounds[2] = {std::min(sample_bound, R * kChunk), sample_bound};
-    for (uint32_t round = 0; round < 2; ++round) {
+    for (uint32_t round = 0; round < kRounds; ++round) {
+        // rows of this round: at most its sample window per ray, and never more than all samples
+        const uint64_t window = static_cast<uint64_t>(kRoundEnd[round]) - (round == 0 ? 0u : kRoundEnd[round - 1]);
+        const uint32_t bound  = static_cast<uint32_t>(std::min<uint64_t>(sample_bound, window * R));
         list_count_kernel<<<list_blocks, kListThreads, 0, s>>>(p, round);
         NGP_TRY(check_launch("list_count_kernel"));
         scan_kept_kernel<<<1, 1024, 0, s>>>(p.list_totals, list_blocks, p.n_rows, 0xFFFFFFFFu);
         NGP_TRY(check_launch("scan_kept_kernel"));
         list_write_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
         NGP_TRY(check_launch("list_write_kernel"));
-        NGP_TRY(ngp_encode_grid_forward_rows(layout, bounds[round], rows, p.n_rows, coords, 7, params + 10240u, enc, enc_stride, stream));
-        NGP_TRY(ngp_density_forward_rows(bounds[round], rows, p.n_rows, params, enc, enc_stride, density, stream));
+        NGP_TRY(ngp_encode_grid_forward_rows(layout, bound, rows, p.n_rows, coords, 7, params + 10240u, enc, enc_stride, stream));
+        NGP_TRY(ngp_density_forward_rows(bound, rows, p.n_rows, params, enc, enc_stride, density, stream));
         keep_round_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
         NGP_TRY(check_launch("keep_round_kernel"));
     }
