@@ -82,11 +82,13 @@ __device__ __forceinline__ void load_output(const __half* o, float& r, float& g,
 
 // Transmittance before this lane's sample: T * q_0 * q_1 * ... * q_{lane-1}, multiplied in lane
 // order exactly as the sequential loop does.
-__device__ __forceinline__ float prefix_transmittance(float T, float q) {
+// Only lanes below `count` (warp-uniform) get their value: the loop stops after lane count-2.
+__device__ __forceinline__ float prefix_transmittance(float T, float q, uint32_t count) {
     const uint32_t lane = threadIdx.x & 31u;
     float Tb            = T;
 #pragma unroll
     for (uint32_t k = 0; k < 31; ++k) {
+        if (k + 1u >= count) break;
         const float qk = __shfl_sync(0xFFFFFFFFu, q, k);
         if (k < lane) Tb *= qk;
     }
@@ -123,11 +125,12 @@ __device__ __forceinline__ void ray_gradients(float3 rgb, float3 target, float s
         const float dt     = cv[3];
         const float3 col   = {sigmoidf_(mr), sigmoidf_(mg), sigmoidf_(mb)};
         const float alpha  = valid ? 1.0f - __expf(-expf(md) * dt) : 0.0f;
-        const float Tb     = prefix_transmittance(T, 1.0f - alpha);
+        const uint32_t nv  = min(32u, cn - c0);
+        const float Tb     = prefix_transmittance(T, 1.0f - alpha, nv);
         const float weight = alpha * Tb;
-        // colour prefix including this sample, accumulated in sample order
+        // colour prefix including this sample, accumulated in sample order (lanes below nv)
         float3 a = acc;
-        for (uint32_t q = 0; q < 32u; ++q) {
+        for (uint32_t q = 0; q < nv; ++q) {
             const float wq = __shfl_sync(0xFFFFFFFFu, weight, q);
             const float cx = __shfl_sync(0xFFFFFFFFu, col.x, q), cy = __shfl_sync(0xFFFFFFFFu, col.y, q), cz = __shfl_sync(0xFFFFFFFFu, col.z, q);
             if (q <= lane) {
@@ -198,7 +201,7 @@ __global__ void __launch_bounds__(kCtaThreads) loss_pass1_kernel(const __grid_co
             }
             const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
             const float3 col  = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
-            const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+            const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, steps - c0));
             const bool keep   = valid && !(Tb < kTransmittanceEps);
             const uint32_t nk = __popc(__ballot_sync(0xFFFFFFFFu, keep));
             const float w     = alpha * Tb;
@@ -323,7 +326,7 @@ __global__ void __launch_bounds__(kCtaThreads) keep_pass_kernel(const __grid_con
             const float d     = valid ? __half2float(dens[j]) : 0.0f;
             const float dt    = valid ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
             const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
-            const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+            const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, steps - c0));
             const bool keep   = valid && !(Tb < kTransmittanceEps);
             const uint32_t nk = __popc(__ballot_sync(0xFFFFFFFFu, keep));
             if (nk > 0) T = __shfl_sync(0xFFFFFFFFu, Tb * (1.0f - alpha), nk - 1u);
@@ -487,7 +490,7 @@ __global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_co
                 const float d     = valid ? __half2float(dens[j]) : 0.0f;
                 const float dt    = valid ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
                 const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
-                const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+                const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, hi - c0));
                 const bool keep   = valid && !(Tb < kTransmittanceEps);
                 const uint32_t nk = __popc(__ballot_sync(0xFFFFFFFFu, keep));
                 if (nk > 0) T = __shfl_sync(0xFFFFFFFFu, Tb * (1.0f - alpha), nk - 1u);
@@ -559,7 +562,7 @@ __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __gri
         }
         const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
         const float3 col  = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
-        const float Tb    = prefix_transmittance(T, 1.0f - alpha);
+        const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, k - c0));
         const uint32_t nk = min(32u, k - c0);
         const float w     = alpha * Tb;
         for (uint32_t q = 0; q < nk; ++q) {
