@@ -172,7 +172,11 @@ PHASE_BYTES = {
     # per marched sample: its record is read once (28 B) to decide how far the ray keeps samples;
     # the densities evaluated (encoding 12 B in + 64 B out, density 64 B in + 2 B out) cover only the
     # samples in front of each ray's stopping point, and the kept ones are compacted (92 B each)
-    "inference_compact": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "encode_forward_points_kernel + mlp_forward_kernel<density> + keep/compact"},
+    "inference_compact": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "encode_forward_points_kernel + mlp_forward_kernel<density> + keep/compact",
+                          # profiles/*__train_config3.md: DRAM read + write of the phase's launches
+                          # (two rounds of encode, density, keep and list kernels, then the copy) in
+                          # one step of 1,393,551 marched samples
+                          "ncu_dram_bytes_per_unit": 218.9e6 / 1393551},
     # 12 B rays in + 28 B records out per sample (dominant), 8 B per ray of counts
     "march": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "march_count_kernel + march_write_kernel"},
     "encode_bwd": {"unit": "batch sample", "bytes": 12 + 64, "l2_atomic_bytes": 16 * 8 * 2 * 4, "kernel": "encode_backward_kernel"},
