@@ -533,31 +533,96 @@ def bench_encode_reference(args, rank, world, local):
     }
 
 
+# ------------------------------------------------------------------------------------------------
+# render workload (config 4): large table, novel 1920x1080 views partitioned across ranks
+# ------------------------------------------------------------------------------------------------
+def bench_render_ours(args, rank, world, local):
+    import torch
+    import ngp_b200 as ngp
+    import workloads
+
+    peaks = load_peaks()
+    ds = make_dataset(args)
+    model = ngp.InstantNGP(ds, ngp.config4_trainer_config())
+    model.train(args.train_steps)  # untimed: an occupancy grid and weights of a trained model
+    poses = workloads.render_poses(max(64, args.steps * world))
+    w, h = poses["width"], poses["height"]
+    # step k renders view k * world + rank on this rank (no collective)
+    views = [poses["camera"][k * world + rank] for k in range(args.steps)]
+    out = torch.empty((h * w, 3), dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        model.render(views[0], w, h, poses["focal"], poses["principal"], out=out)
+    barrier(world)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        clocks.wait_first()
+        s.record()
+        for v in views:
+            model.render(v, w, h, poses["focal"], poses["principal"], out=out)
+        e.record()
+        e.synchronize()
+        time.sleep(0.25)
+    barrier(world)
+    ms = max_over_ranks(s.elapsed_time(e), world)
+    # e2e: the same renders with each image read back to pinned host memory
+    host = torch.empty((h * w, 3), dtype=torch.float32, pin_memory=True)
+    n_e2e = max(2, args.steps // 2)
+    barrier(world)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for v in views[:n_e2e]:
+        model.render(v, w, h, poses["focal"], poses["principal"], out=out)
+        host.copy_(out, non_blocking=True)
+    e2.record()
+    e2.synchronize()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / n_e2e, world)
+    model.close()
+    rays = w * h
+    value = world * rays * args.steps / (ms * 1e-3)
+    return {
+        "metric": "render rays/s (config 4)", "value": round(value, 1), "unit": "rays/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 params/activations, fp32 accumulation", "data": "synthetic procedural scene (64 Lambert spheres, seeded)",
+        "config": {"workload": "config4 render 1920x1080 novel views after training", "table": "L=16 F=2 log2T=22 base 16 finest 4096",
+                   "views_per_gpu": args.steps, "trained_steps": args.train_steps, "parallelism": f"views partitioned over {world} ranks, no collective",
+                   "l2": "table 268 MB fp16 > L2; no flush"},
+        "e2e": {"value": round(world * rays / (e2e_ms * 1e-3), 1), "unit": "rays/s", "h2d_bytes_per_step": 48,
+                "d2h_bytes_per_step": rays * 12, "note": "InstantNGP.render per view with the image read back to pinned host memory"},
+        "gpu_launches": None, "clocks": clocks.summary(), "roofline": None,
+    }
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["train", "encode"], default="train")
+    ap.add_argument("--workload", choices=["train", "encode", "render"], default="train")
+    ap.add_argument("--train-steps", type=int, default=1000, help="render workload: untimed training steps before rendering")
     ap.add_argument("--views", type=int, default=100)
     ap.add_argument("--test-views", type=int, default=20)
     ap.add_argument("--res", type=int, default=800)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 300 if args.workload == "train" else 500
+        args.steps = {"train": 300, "encode": 500, "render": 8}[args.workload]
     if args.warmup is None:
-        args.warmup = 300 if args.workload == "train" else 5
+        args.warmup = {"train": 300, "encode": 5, "render": 3}[args.workload]
     args.warmup = max(args.warmup, 3)
 
     rank, world, local = dist_setup()
     if args.impl == "reference":
         if rank == 0:
+            if args.workload == "render":
+                print(json.dumps({"impl": "reference", "unavailable": "the reference build's compiled grid (8x4, log2 T 19) cannot express config 4"}),
+                      flush=True)
+                return 0
             fn = bench_train_reference if args.workload == "train" else bench_encode_reference
             print(json.dumps(fn(args, rank, world, local)), flush=True)
         return 0
-    fn = bench_train_ours if args.workload == "train" else bench_encode_ours
+    fn = {"train": bench_train_ours, "encode": bench_encode_ours, "render": bench_render_ours}[args.workload]
     res = fn(args, rank, world, local)
     if rank == 0:
         print(json.dumps(res), flush=True)

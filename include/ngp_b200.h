@@ -123,6 +123,11 @@ NGP_API int ngp_mlp_forward(uint32_t n, const uint16_t* params, const uint16_t* 
  * mlp_forward_64_relu_kernel launch of update_density_grid (ngp.train.cu:1573). */
 NGP_API int ngp_density_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, uint16_t* out, void* stream);
 
+/* Full network for a list of rows: input column rows[r] of x and record rows[r] of coords, output
+ * row out[rows[r]][16], for r < min(*n_rows, max_rows) (n_rows may be NULL). */
+NGP_API int ngp_mlp_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
+                                 uint32_t x_stride, const float* coords, uint32_t coord_stride, uint16_t* out, void* stream);
+
 /* Density network for a list of rows: input column rows[r] of x, output out[rows[r]], for
  * r < min(*n_rows, max_rows) (n_rows may be NULL). */
 NGP_API int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
@@ -277,6 +282,16 @@ NGP_API int ngp_training_compact_progressive(uint32_t rays_per_batch, const uint
                                              uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, float* compacted_coords,
                                              uint16_t* compacted_enc, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
                                              void* stream);
+
+/* Evaluation (rendering) counterpart: the full network's outputs ([samples][16]) for every
+ * sample in front of its ray's stopping point (transmittance < 1e-4, where the evaluation
+ * compositing of run_evaluation stops; ngp.train.cu:676-745), evaluated in the same two rounds;
+ * outputs behind the stopping points are not written (compositing never reads them).  n_rays rays
+ * marched into numsteps/coords (ngp_march_rays); enc [32][enc_stride] and rows [sample_bound]
+ * are scratch; scratch: ngp_loss_scratch_bytes(n_rays). */
+NGP_API int ngp_eval_network_progressive(uint32_t n_rays, const ngp_grid_layout* layout, const uint16_t* params, const float* coords,
+                                         uint32_t sample_bound, const uint32_t* numsteps, uint16_t* enc, uint32_t enc_stride, uint16_t* network_output,
+                                         uint32_t* rows, void* scratch, size_t scratch_bytes, void* stream);
 
 /* Step 2, after the full network ran on the compacted rows (compacted_output fp16 [rows][16]):
  * compositing, loss and gradients as ngp_training_loss_and_compact; numsteps ends as

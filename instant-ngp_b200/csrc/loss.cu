@@ -407,12 +407,14 @@ constexpr uint32_t kRoundEnd[] = {NGP_KEEP_ROUND_LIST};
 constexpr uint32_t kRounds     = sizeof(kRoundEnd) / sizeof(kRoundEnd[0]);
 __constant__ uint32_t c_round_end[kRounds] = {NGP_KEEP_ROUND_LIST};
 constexpr uint32_t kListThreads = 256u;
+constexpr uint32_t kMlpWeights  = 10240u;  // packed MLP weights before the grid in the parameter vector
 
 struct ProgressParams {
     uint32_t rays_per_batch;
     const uint32_t* ray_counter;
     const uint32_t* numsteps;   // [ray][2] (steps, base)
-    const __half* density;      // [samples] raw density (evaluated samples only)
+    const __half* density;      // raw density of sample j at density[j * density_stride] (evaluated samples only)
+    uint32_t density_stride;    // 1 (density array) or 16 (network output rows, density in channel 3)
     const float* coords;
     uint32_t* kept;             // [ray]
     uint32_t* steps;            // [ray]
@@ -482,12 +484,12 @@ __global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_co
         if (run) {
             uint32_t lo, hi;
             round_range(p, round, i, lo, hi);
-            const __half* dens = p.density + base;
+            const __half* dens = p.density + static_cast<uint64_t>(base) * p.density_stride;
             const float* c     = p.coords + static_cast<uint64_t>(base) * 7u;
             for (uint32_t c0 = lo; c0 < hi; c0 += 32u) {
                 const uint32_t j  = c0 + lane;
                 const bool valid  = j < hi;
-                const float d     = valid ? __half2float(dens[j]) : 0.0f;
+                const float d     = valid ? __half2float(dens[static_cast<uint64_t>(j) * p.density_stride]) : 0.0f;
                 const float dt    = valid ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
                 const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
                 const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, hi - c0));
@@ -671,6 +673,52 @@ constexpr size_t loss_scratch_size(uint32_t max_rays) {
            ((max_rays + kListThreads - 1u) / kListThreads) * 4u + 256u;
 }
 
+// The rounds of the progressive evaluation: after them p.kept holds each ray's kept count and
+// every sample in front of a ray's stopping point has been evaluated, by the density network
+// (density_out: raw density [samples]) or by the full network (full_out: [samples][16]).
+int progressive_rounds(ProgressParams& p, uint32_t R, const ngp_grid_layout* layout, const uint16_t* params, const float* coords,
+                       uint32_t sample_bound, uint16_t* enc, uint32_t enc_stride, uint16_t* density_out, uint16_t* full_out, cudaStream_t s) {
+    const uint32_t warp_blocks = (R + kRaysPerCta - 1) / kRaysPerCta;
+    const uint32_t list_blocks = (R + kListThreads - 1) / kListThreads;
+    p.density        = reinterpret_cast<const __half*>(full_out != nullptr ? full_out + 3 : density_out);
+    p.density_stride = full_out != nullptr ? 16u : 1u;
+    for (uint32_t round = 0; round < kRounds; ++round) {
+        // rows of this round: at most its sample window per ray, and never more than all samples
+        const uint64_t window = static_cast<uint64_t>(kRoundEnd[round]) - (round == 0 ? 0u : kRoundEnd[round - 1]);
+        const uint32_t bound  = static_cast<uint32_t>(std::min<uint64_t>(sample_bound, window * R));
+        list_count_kernel<<<list_blocks, kListThreads, 0, s>>>(p, round);
+        NGP_TRY(check_launch("list_count_kernel"));
+        scan_kept_kernel<<<1, 1024, 0, s>>>(p.list_totals, list_blocks, p.n_rows, 0xFFFFFFFFu);
+        NGP_TRY(check_launch("scan_kept_kernel"));
+        list_write_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
+        NGP_TRY(check_launch("list_write_kernel"));
+        NGP_TRY(ngp_encode_grid_forward_rows(layout, bound, p.rows, p.n_rows, coords, 7, params + kMlpWeights, enc, enc_stride, s));
+        if (full_out != nullptr)
+            NGP_TRY(ngp_mlp_forward_rows(bound, p.rows, p.n_rows, params, enc, enc_stride, coords, 7, full_out, s));
+        else
+            NGP_TRY(ngp_density_forward_rows(bound, p.rows, p.n_rows, params, enc, enc_stride, density_out, s));
+        keep_round_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
+        NGP_TRY(check_launch("keep_round_kernel"));
+    }
+    return NGP_OK;
+}
+
+// Scratch layout of the progressive evaluation (ngp_loss_scratch_bytes(R) bytes).
+void progress_scratch(ProgressParams& p, uint32_t R, void* scratch, uint32_t* rows) {
+    const uint32_t warp_blocks = (R + kRaysPerCta - 1) / kRaysPerCta;
+    const uint32_t list_blocks = (R + kListThreads - 1) / kListThreads;
+    unsigned char* sc          = static_cast<unsigned char*>(scratch);
+    p.steps        = reinterpret_cast<uint32_t*>(sc);
+    p.kept         = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 4u);
+    p.T            = reinterpret_cast<float*>(sc + static_cast<size_t>(R) * 8u);
+    p.list_off     = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 12u);
+    p.active       = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 16u);
+    p.block_totals = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 20u);
+    p.list_totals  = p.block_totals + warp_blocks;
+    p.rows         = rows;
+    p.n_rows       = p.list_totals + list_blocks;
+}
+
 }  // namespace
 }  // namespace ngp
 
@@ -775,38 +823,13 @@ extern "C" int ngp_training_compact_progressive(uint32_t rays_per_batch, const u
     const cudaStream_t s       = as_stream(stream);
     const uint32_t R           = rays_per_batch;
     const uint32_t warp_blocks = (R + kRaysPerCta - 1) / kRaysPerCta;
-    const uint32_t list_blocks = (R + kListThreads - 1) / kListThreads;
-    unsigned char* sc          = static_cast<unsigned char*>(scratch);
     ProgressParams p{};
     p.rays_per_batch = R;
     p.ray_counter    = ray_counter;
     p.numsteps       = numsteps;
-    p.density        = reinterpret_cast<const __half*>(density);
     p.coords         = coords;
-    p.steps          = reinterpret_cast<uint32_t*>(sc);
-    p.kept           = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 4u);
-    p.T              = reinterpret_cast<float*>(sc + static_cast<size_t>(R) * 8u);
-    p.list_off       = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 12u);
-    p.active         = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 16u);
-    p.block_totals   = reinterpret_cast<uint32_t*>(sc + static_cast<size_t>(R) * 20u);
-    p.list_totals    = p.block_totals + warp_blocks;
-    p.rows           = rows;
-    p.n_rows         = p.list_totals + list_blocks;
-    for (uint32_t round = 0; round < kRounds; ++round) {
-        // rows of this round: at most its sample window per ray, and never more than all samples
-        const uint64_t window = static_cast<uint64_t>(kRoundEnd[round]) - (round == 0 ? 0u : kRoundEnd[round - 1]);
-        const uint32_t bound  = static_cast<uint32_t>(std::min<uint64_t>(sample_bound, window * R));
-        list_count_kernel<<<list_blocks, kListThreads, 0, s>>>(p, round);
-        NGP_TRY(check_launch("list_count_kernel"));
-        scan_kept_kernel<<<1, 1024, 0, s>>>(p.list_totals, list_blocks, p.n_rows, 0xFFFFFFFFu);
-        NGP_TRY(check_launch("scan_kept_kernel"));
-        list_write_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
-        NGP_TRY(check_launch("list_write_kernel"));
-        NGP_TRY(ngp_encode_grid_forward_rows(layout, bound, rows, p.n_rows, coords, 7, params + 10240u, enc, enc_stride, stream));
-        NGP_TRY(ngp_density_forward_rows(bound, rows, p.n_rows, params, enc, enc_stride, density, stream));
-        keep_round_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(p, round);
-        NGP_TRY(check_launch("keep_round_kernel"));
-    }
+    progress_scratch(p, R, scratch, rows);
+    NGP_TRY(progressive_rounds(p, R, layout, params, coords, sample_bound, enc, enc_stride, density, nullptr, s));
     // compaction of the kept samples (as ngp_training_compact_by_density after its keep pass)
     KeepParams k{};
     k.rays_per_batch = R;
@@ -824,6 +847,24 @@ extern "C" int ngp_training_compact_progressive(uint32_t rays_per_batch, const u
     NGP_TRY(check_launch("scan_kept_kernel"));
     compact_copy_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(k);
     return check_launch("compact_copy_kernel");
+}
+
+extern "C" int ngp_eval_network_progressive(uint32_t n_rays, const ngp_grid_layout* layout, const uint16_t* params, const float* coords,
+                                            uint32_t sample_bound, const uint32_t* numsteps, uint16_t* enc, uint32_t enc_stride, uint16_t* network_output,
+                                            uint32_t* rows, void* scratch, size_t scratch_bytes, void* stream) {
+    clear_error();
+    if (n_rays == 0) return NGP_OK;
+    if (layout == nullptr || params == nullptr || coords == nullptr || numsteps == nullptr || enc == nullptr || network_output == nullptr ||
+        rows == nullptr || scratch == nullptr || enc_stride < sample_bound)
+        return fail(NGP_ERR_INVALID, "progressive evaluation: invalid input");
+    if (scratch_bytes < loss_scratch_size(n_rays)) return fail(NGP_ERR_INVALID, "progressive evaluation: scratch too small");
+    if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "progressive evaluation: scratch must be 16-byte aligned");
+    ProgressParams p{};
+    p.rays_per_batch = n_rays;
+    p.numsteps       = numsteps;
+    p.coords         = coords;
+    progress_scratch(p, n_rays, scratch, rows);
+    return progressive_rounds(p, n_rays, layout, params, coords, sample_bound, enc, enc_stride, nullptr, network_output, as_stream(stream));
 }
 
 extern "C" int ngp_training_loss_compacted(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,

@@ -688,6 +688,22 @@ extern "C" int ngp_density_forward(uint32_t n, const uint16_t* params, const uin
     return check_launch("mlp_forward_kernel<density>");
 }
 
+extern "C" int ngp_mlp_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
+                                    uint32_t x_stride, const float* coords, uint32_t coord_stride, uint16_t* out, void* stream) {
+    clear_error();
+    if (max_rows == 0) return NGP_OK;
+    if (rows == nullptr || params == nullptr || x == nullptr || coords == nullptr || out == nullptr)
+        return fail(NGP_ERR_INVALID, "mlp forward rows: null pointer");
+    if (coord_stride < 7) return fail(NGP_ERR_INVALID, "mlp forward rows: bad stride");
+    NGP_TRY(ensure_attrs());
+    MlpForwardParams p{max_rows, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
+                       reinterpret_cast<__half*>(out), nullptr, rows, n_rows};
+    const uint32_t n_tiles = (max_rows + kRows - 1) / kRows;
+    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull>), n_tiles, kFwdTmemCols);
+    mlp_forward_kernel<kModeFull><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
+    return check_launch("mlp_forward_kernel");
+}
+
 extern "C" int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
                                         uint32_t x_stride, uint16_t* out, void* stream) {
     clear_error();

@@ -421,10 +421,10 @@ int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparis
             tile = std::max(4096u, tile / 4u);
             continue;
         }
-        if (used > 0) {
-            NGP_TRY(encode(t, used, t->coords, t->enc, used));
-            NGP_TRY(ngp_mlp_forward(used, t->params, t->enc, used, t->coords, 7, t->out, nullptr, t->stream));
-        }
+        // network outputs only in front of each ray's stopping point (all the compositing reads)
+        if (used > 0)
+            NGP_TRY(ngp_eval_network_progressive(n, &t->layout, t->params, t->coords, used, t->numsteps, t->enc, used, t->out, t->rows, t->loss_scratch,
+                                                 t->loss_scratch_bytes, t->stream));
         NGP_TRY(ngp_eval_composite(n, off, image, s.width, s.height, s.pixels, t->numsteps, t->coords, t->out, t->eval_sse, comparison_dev,
                                    rendered, t->stream));
         off += n;

@@ -296,6 +296,14 @@ def training_compact_progressive(rays_per_batch, ray_counter, layout, params, co
            "ngp_training_compact_progressive")
 
 
+def eval_network_progressive(n_rays, layout, params, coords, sample_bound, numsteps, enc, network_output, rows, scratch, enc_stride=None,
+                             stream=None) -> None:
+    _check(lib().ngp_eval_network_progressive(_u32(n_rays), ctypes.byref(layout), _ptr(params), _ptr(coords), _u32(sample_bound), _ptr(numsteps),
+                                              _ptr(enc), _u32(enc.shape[1] if enc_stride is None else enc_stride), _ptr(network_output),
+                                              _ptr(rows), _ptr(scratch), ctypes.c_size_t(scratch.numel() * scratch.element_size()),
+                                              _stream(stream)), "ngp_eval_network_progressive")
+
+
 def training_loss_compacted(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, compacted_output, ray_indices, rays,
                             numsteps, compacted_coords, dloss_doutput, loss_values, scratch, stream=None) -> None:
     _check(lib().ngp_training_loss_compacted(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),
@@ -367,6 +375,12 @@ def trainer_config(n_levels=8, features_per_level=4, log2_hashmap_size=19, base_
 
 def config0_trainer_config() -> TrainerConfig:
     return trainer_config(16, 2, 19, 16, math.log2(2048.0 / 16.0) / 15.0)
+
+
+def config4_trainer_config() -> TrainerConfig:
+    """the config-0 grid with log2 T = 22 (table beyond L2) and finest
+    resolution 4096, b = exp(ln(4096/16)/15)."""
+    return trainer_config(16, 2, 22, 16, math.log2(4096.0 / 16.0) / 15.0)
 
 
 class InstantNGP:

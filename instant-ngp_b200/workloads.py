@@ -162,6 +162,18 @@ def procedural_dataset(n_train: int = 100, n_test: int = 20, width: int = 800, h
     return out
 
 
+def render_poses(n: int = 64, width: int = 1920, height: int = 1080, fov_x: float = 0.69, seed: int = 4,
+                 scene_scale: float = DEFAULT_SCENE_SCALE) -> dict:
+    """Config 4 novel views: n poses on the radius-4 sphere looking at the origin, width x height,
+    horizontal FOV 0.69 rad, in the reference's camera convention."""
+    rng = np.random.default_rng(seed)
+    v = rng.standard_normal((n, 3))
+    pos = 4.0 * v / np.linalg.norm(v, axis=1, keepdims=True)
+    cams = np.stack([nerf_to_ngp_camera(look_at_c2w(p), scene_scale) for p in pos]).astype(np.float32)
+    focal = 0.5 * width / math.tan(fov_x * 0.5)
+    return {"camera": cams, "width": width, "height": height, "focal": (focal, focal), "principal": (width * 0.5, height * 0.5)}
+
+
 def march_rays_config2(n: int = 1 << 18, seed: int = 2) -> np.ndarray:
     """Config 2 rays in the unit-cube frame: origins uniform on the radius-4 sphere (world), aimed
     at the origin plus U(-0.1, 0.1)^3 jitter, normalised on the host, world -> unit x/3 + 0.5."""

@@ -553,3 +553,49 @@ def test_progressive_density_evaluation_matches_full(ngp, small_scene, blob_bitf
     assert stop0 > 0 and stop1 > 0, (stop0, stop1, np.percentile(kept[steps > 0], [10, 50, 90]))  # stops in both rounds
     evaluated = int((dens_b != 0).sum().item())
     assert evaluated < total  # densities only in front of the stopping points
+
+
+def test_progressive_evaluation_renders_identically(ngp, small_scene, blob_bitfield):
+    """Rendering with network outputs only in front of each ray's stopping point gives the same
+    image, bit for bit, as evaluating every marched sample (the compositing stops where the
+    progressive evaluation stops)."""
+    import torch
+
+    _, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    layout = ngp.grid_layout(16, 2, 19, 16, math.log2(128.0) / 15.0)
+    _, table, _ = workloads.encode_inputs(1, layout.n_params, 16, 2, seed=4)
+    table = (table.astype(np.float32) * 2e4).astype(np.float16)
+    mlp = workloads.xavier_mlp_params(9)
+    mlp[2048:2048 + 64] = np.random.default_rng(3).uniform(0.2, 0.5, 64).astype(np.float16)
+    params = T(np.concatenate([mlp, table]).view(np.int16))
+    n = W * H
+    rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    ngp.make_eval_rays(cam, 0, W, H, fx, fy, cx, cy, 0, n, rays)
+    limit = 1 << 21
+    coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    msc = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_rays(rays, T(blob_bitfield), coords, ns, msc, sc, sample_limit=limit)
+    torch.cuda.synchronize()
+    total = int(sc.item())
+    m = (total + 127) // 128 * 128
+    enc = torch.zeros((32, m), dtype=torch.float16, device="cuda")
+    full = torch.zeros((m, 16), dtype=torch.float16, device="cuda")
+    ngp.encode_grid_forward(layout, coords, params[10240:], enc, n=m, coord_stride=7, out_stride=m)
+    ngp.mlp_forward(params[:10240], enc, coords, full, n=m, x_stride=m)
+    prog = torch.zeros((m, 16), dtype=torch.float16, device="cuda")
+    enc2 = torch.zeros((32, m), dtype=torch.float16, device="cuda")
+    rows = torch.zeros(m, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(ngp.loss_scratch_bytes(n), dtype=torch.uint8, device="cuda")
+    ngp.eval_network_progressive(n, layout, params, coords, m, ns, enc2, prog, rows, scratch)
+    img_a = torch.zeros((n, 3), dtype=torch.float32, device="cuda")
+    img_b = torch.zeros((n, 3), dtype=torch.float32, device="cuda")
+    ngp.eval_composite(n, 0, 0, W, H, None, ns, coords, full, rendered=img_a)
+    ngp.eval_composite(n, 0, 0, W, H, None, ns, coords, prog, rendered=img_b)
+    torch.cuda.synchronize()
+    assert img_a.cpu().numpy().tobytes() == img_b.cpu().numpy().tobytes()
+    evaluated = int((prog[:total, 3] != 0).sum().item())
+    assert 0 < evaluated < total
