@@ -410,6 +410,8 @@ class InstantNGP:
         self._keep = []
         self.test_size = None if splits[2] is None else (splits[2].width, splits[2].height)
         self.split_frames = {i: (0 if s is None else int(s.frame_count)) for i, s in enumerate(splits)}
+        self.scene_scale = float(dataset.get("scene_scale", 0.33))
+        self.step = 0
 
     def close(self) -> None:
         if self.handle:
@@ -425,7 +427,45 @@ class InstantNGP:
     def train(self, iters: int) -> dict:
         st = TrainStats()
         _check(lib().ngp_trainer_train(self.handle, ctypes.c_int32(iters), ctypes.byref(st)), "ngp_trainer_train")
-        return st.as_dict()
+        d = st.as_dict()
+        self.step = int(d["step"])
+        return d
+
+    def layout(self) -> GridLayout:
+        c = self.config
+        return grid_layout(c.n_levels, c.features_per_level, c.log2_hashmap_size, c.base_resolution, c.log2_per_level_scale)
+
+    def export_weights(self, path) -> None:
+        """safetensors "instant-ngp-new.weights.v2" (InstantNGP::export_weights, ngp.train.cpp:231-296)."""
+        import ngp_weights as weights
+
+        weights.export_weights(path, self.get_params(), self.layout(), self.scene_scale)
+
+    def load_weights(self, path) -> None:
+        """Load a weights file before training (InstantNGP::load_weights, ngp.train.cpp:298-425);
+        the optimizer state starts from zero, as in the reference."""
+        import ngp_weights as weights
+
+        if self.step != 0:
+            raise RuntimeError("weights can only be loaded before training starts.")
+        self.set_params(weights.load_weights(path, self.layout(), self.scene_scale))
+
+    def write_test_images(self, output_dir="test") -> dict:
+        """InstantNGP::test (ngp.train.cpp:183-229): test PSNR and one side-by-side comparison PNG
+        per test image (target left, render right) as output_dir/test_NNNN.png."""
+        from pathlib import Path
+
+        from PIL import Image
+
+        out = Path(output_dir)
+        if out.exists() and not out.is_dir():
+            raise RuntimeError(f"test output path '{out}' is not a directory.")
+        out.mkdir(parents=True, exist_ok=True)
+        res = self.test(with_images=True)
+        for i, img in enumerate(res.pop("images")):
+            Image.fromarray(img, "RGB").save(out / f"test_{i:04d}.png")
+        res["output_dir"] = str(out)
+        return res
 
     def _evaluate(self, split: int, begin: int, count: int, comparison=None):
         sse = ctypes.c_double(0.0)
