@@ -466,6 +466,7 @@ def bench_encode_ours(args, rank, world, local):
     e2e_times = time_steps(e2e_step, max(3, args.steps // 2), 2, flush, stream, world)
     e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
     peaks = load_peaks()
+    probe = probe_gather_scatter(stream)
     fwd_bytes_pt = 12 + L * F * 2 + L * 8 * F * 2
     bwd_bytes_pt = 12 + L * F * 2 + L * 8 * F * 4
     dom = "forward" if fwd_ms >= bwd_ms else "backward"
@@ -482,11 +483,49 @@ def bench_encode_ours(args, rank, world, local):
         "kernels_ms": {"encode_forward": round(fwd_ms, 5), "encode_backward": round(bwd_ms, 5)},
         "roofline": {"kernel": f"encode_{dom}", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"],
-                     "note": "achieved counts HBM streams plus table bytes gathered (L2-served) per point"},
+                     "note": "achieved counts HBM streams plus table bytes gathered (L2-served) per point; the L2-resident table makes "
+                             "the kernels gather/atomic-bound: see l2_roofline"},
+        "table_access": {
+            "forward_Gaccess_s": round(n * L * 8 / (fwd_ms * 1e-3) / 1e9, 2), "backward_Gaccess_s": round(n * L * 8 / (bwd_ms * 1e-3) / 1e9, 2),
+            "random_gather_Gaccess_s": probe["gather_G_s"], "random_float2_atomic_Gaccess_s": probe["scatter_G_s"],
+            "note": "table corner accesses per second (8 corners x 16 levels per point) beside the measured rate of fully random "
+                    "4-byte loads / float2 atomics on an L2-resident table (ngp_probe_gather / ngp_probe_scatter, run live).  The kernels "
+                    "exceed the fully random rates because a cell's x-neighbour corners share sectors and the coarse levels stay L1-resident; "
+                    "their bounding resource is L1 throughput (ncu l1tex__throughput 70-85 % of peak, "
+                    "profiles/encode_forward_points_kernel__train_config3.md, profiles/encode_backward_kernel__train_config3.md)"},
         "e2e": {"value": round(world * n / (e2e_ms * 1e-3) / 1e9, 4), "unit": "Gpts/s", "h2d_bytes_per_step": coords_h.nbytes + dy_h.nbytes,
                 "d2h_bytes_per_step": feats.numel() * 2},
         "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
     }
+
+
+def probe_gather_scatter(stream) -> dict:
+    """Measured rate of random 4-byte loads from a 32 MB table and of random float2 atomic adds
+    into a 64 MB table (the L2-resident access patterns the encoding kernels are bound by)."""
+    import torch
+    import ngp_b200 as ngp
+
+    lib = ngp.lib()
+    threads, rounds = 1 << 20, 4
+    tab = torch.ones(1 << 23, dtype=torch.int32, device="cuda")
+    out = torch.empty(threads, dtype=torch.int32, device="cuda")
+    acc = torch.zeros(1 << 24, dtype=torch.float32, device="cuda")
+    s = ctypes.c_void_p(stream.cuda_stream)
+    res = {}
+    for name, call in (("gather_G_s", lambda: lib.ngp_probe_gather(ctypes.c_void_p(tab.data_ptr()), 23, threads, rounds, ctypes.c_void_p(out.data_ptr()), s)),
+                       ("scatter_G_s", lambda: lib.ngp_probe_scatter(ctypes.c_void_p(acc.data_ptr()), 23, threads, rounds, s))):
+        for _ in range(3):
+            call()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record()
+            for _ in range(10):
+                if call() != 0:
+                    raise RuntimeError(lib.ngp_last_error().decode())
+            ev1.record()
+        ev1.synchronize()
+        res[name] = round(10 * threads * rounds * 16 / (ev0.elapsed_time(ev1) * 1e-3) / 1e9, 2)
+    return res
 
 
 def bench_encode_reference(args, rank, world, local):

@@ -422,6 +422,14 @@ NGP_API int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint32_
 /* Occupancy bitfield (2^18 bytes) and density-grid values (2^21 floats) to the host. */
 NGP_API int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host, float* values_host);
 
+/* ------------------------------------------------------------------------------------------
+ * Roofline probes (used by the benchmark): random 4-byte loads from a table of 2^log2_entries
+ * uint32 entries, and random 2 x fp32 atomic adds into a table of 2^log2_entries float pairs;
+ * threads (a multiple of 256) x rounds x 16 accesses.
+ * ------------------------------------------------------------------------------------------ */
+NGP_API int ngp_probe_gather(const uint32_t* table, uint32_t log2_entries, uint32_t threads, uint32_t rounds, uint32_t* out, void* stream);
+NGP_API int ngp_probe_scatter(float* table, uint32_t log2_entries, uint32_t threads, uint32_t rounds, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
