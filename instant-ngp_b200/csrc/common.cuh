@@ -114,6 +114,28 @@ __device__ __forceinline__ void corner_indices(bool dense, uint32_t size, uint32
 // The reference's PCG32 (ngp.train.cu:85-143): O'Neill's pcg32 (XSH-RR 64/32) with the
 // default stream constants and the LCG jump-ahead of Brown (1994).  All training randomness
 // must follow it exactly so that sample positions are bit-identical to the reference's.
+// Jump table of the default stream (inc = 3): advancing the state by 2^k steps is the affine map
+// state -> mult[k] * state + plus[k] (mod 2^64).  Composing the maps of delta's set bits gives the
+// same state as Brown's loop below (LCG steps commute), with one multiply-add per set bit.
+struct PcgJumpTable {
+    uint64_t mult[64];
+    uint64_t plus[64];
+};
+
+constexpr PcgJumpTable make_pcg_jump_table() {
+    PcgJumpTable t{};
+    uint64_t m = 0x5851f42d4c957f2dULL, c = 3u;
+    for (int k = 0; k < 64; ++k) {
+        t.mult[k] = m;
+        t.plus[k] = c;
+        c         = (m + 1u) * c;
+        m *= m;
+    }
+    return t;
+}
+
+static __constant__ PcgJumpTable c_pcg_jump = make_pcg_jump_table();
+
 struct Pcg32 {
     uint64_t state;
     uint64_t inc;
@@ -139,6 +161,16 @@ struct Pcg32 {
         return value - 1.0f;
     }
     __host__ __device__ void advance(uint64_t delta) {
+#ifdef __CUDA_ARCH__
+        if (inc == 3u) {
+            while (delta != 0u) {
+                const int k = __ffsll(static_cast<long long>(delta)) - 1;
+                state       = c_pcg_jump.mult[k] * state + c_pcg_jump.plus[k];
+                delta &= delta - 1u;
+            }
+            return;
+        }
+#endif
         uint64_t cur_mult = 0x5851f42d4c957f2dULL, cur_plus = inc, acc_mult = 1u, acc_plus = 0u;
         while (delta > 0u) {
             if (delta & 1u) {
