@@ -87,6 +87,11 @@ NGP_API int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n, c
  * corners of every point and level, with fp32 vector atomics.  table_grad is fp32 and is
  * accumulated into (zero it first to get the gradient of this batch alone).
  * Replaces encode_grid_backward_kernel (ngp.train.cu:923-960), which accumulates in fp16. */
+/* Backward for a batch given as a row list: point r's record is coords[rows[r]], its gradient
+ * column r of dy. */
+NGP_API int ngp_encode_grid_backward_rows(const ngp_grid_layout* layout, uint32_t n, const uint32_t* rows, const float* coords,
+                                          uint32_t coord_stride, const uint16_t* dy, uint32_t dy_stride, float* table_grad, void* stream);
+
 /* Forward for a list of points: point rows[r] for r < min(*n_rows, max_rows) (n_rows may be NULL:
  * max_rows points), read from coords[rows[r]] and written to column rows[r] of out (so out_stride
  * must exceed every listed index).  Used to encode only the samples whose density is needed. */
@@ -147,6 +152,12 @@ NGP_API uint32_t ngp_mlp_backward_scratch_floats(void);
 NGP_API int ngp_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
                      uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, float* scratch,
                      size_t scratch_floats, float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream);
+
+/* ngp_mlp_backward for a batch given as a row list: batch row r reads the features (column
+ * rows[r] of x) and record (rows[r] of coords) of sample rows[r]; dy and dx are batch-indexed. */
+NGP_API int ngp_mlp_backward_rows(uint32_t n, const uint32_t* rows, const uint16_t* params, const uint16_t* x, uint32_t x_stride,
+                                  const float* coords, uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride,
+                                  float* scratch, size_t scratch_floats, float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream);
 
 /* Sticky device status of the MLP kernels: bit 0 = a tensor-core completion wait timed out.
  * reset != 0 clears it. */
@@ -282,6 +293,28 @@ NGP_API int ngp_training_compact_progressive(uint32_t rays_per_batch, const uint
                                              uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, float* compacted_coords,
                                              uint16_t* compacted_enc, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
                                              void* stream);
+
+/* Selection variant used by the trainer: the progressive rounds, then instead of copying the kept
+ * samples, the batch is a row list: batch_rows[cbase + j] = (sample index of) ray i's kept sample j,
+ * for every ray whose compacted base cbase lies in the batch (the straddling ray whole; batch_rows
+ * holds ngp_compacted_rows() entries), *n_selected = rows listed, *compacted_counter = min(kept
+ * total, 2^18), numsteps = (kept, cbase).  The network then runs on the listed rows in place
+ * (ngp_mlp_forward_rows), ngp_training_loss_selected composites from the samples' own positions,
+ * ngp_pad_training_rows pads the list, and the backward reads the list (ngp_mlp_backward_rows,
+ * ngp_encode_grid_backward_rows).  Identical values to the copying flow; no sample data is moved. */
+NGP_API int ngp_training_select_progressive(uint32_t rays_per_batch, const uint32_t* ray_counter, const ngp_grid_layout* layout,
+                                            const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
+                                            uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, uint32_t* batch_rows,
+                                            uint32_t* n_selected, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes, void* stream);
+/* ngp_training_loss_compacted for the selection flow: network_output [samples][16] and coords
+ * are indexed by sample (the kept samples' own positions); dloss_doutput by batch row.  scratch:
+ * the one given to ngp_training_select_progressive. */
+NGP_API int ngp_training_loss_selected(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                       uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                       const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* coords,
+                                       uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, void* stream);
+/* Padding of the selected batch to 2^18 rows (rows and gradients, as ngp_pad_training_batch). */
+NGP_API int ngp_pad_training_rows(const uint32_t* compacted_counter, uint32_t* batch_rows, uint16_t* dloss_doutput, void* stream);
 
 /* Evaluation (rendering) counterpart: the full network's outputs ([samples][16]) for every
  * sample in front of its ray's stopping point (transmittance < 1e-4, where the evaluation

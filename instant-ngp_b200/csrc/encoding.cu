@@ -397,14 +397,15 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const u
                                                                          const uint32_t coord_stride,
                                                                          const __half* __restrict__ dy, const uint32_t dy_stride,
                                                                          float* __restrict__ table_grad,
-                                                                         const __grid_constant__ GridParams grid) {
+                                                                         const __grid_constant__ GridParams grid, const uint32_t* __restrict__ rows) {
     uint32_t level, chunk;
     cta_level_chunk<NGP_ENC_BWD_INTERLEAVE>(grid.n_levels, level, chunk);
     const uint32_t i = chunk * kEncodeThreads + threadIdx.x;
     if (i >= n) return;
     float g[F];
     load_dy<F>(dy, dy_stride, level, i, g);
-    const float* c    = coords + static_cast<uint64_t>(i) * coord_stride;
+    // point i's record: row i, or the sample rows[i] of a row list
+    const float* c    = coords + static_cast<uint64_t>(rows != nullptr ? __ldg(rows + i) : i) * coord_stride;
     const float x[3]  = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
     if constexpr (F <= 2 && NGP_ENC_BWD_AGG_RES > 0) {
         if (grid.resolution[level] <= NGP_ENC_BWD_AGG_RES) {
@@ -499,9 +500,10 @@ extern "C" int ngp_encode_grid_forward_rows(const ngp_grid_layout* layout, uint3
                                  as_stream(stream));
 }
 
-extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t n, const float* coords, uint32_t coord_stride,
-                                        const uint16_t* dy, uint32_t dy_stride, float* table_grad, void* stream) {
-    clear_error();
+namespace ngp {
+namespace {
+int encode_backward_launch(const ngp_grid_layout* layout, uint32_t n, const uint32_t* rows, const float* coords, uint32_t coord_stride,
+                           const uint16_t* dy, uint32_t dy_stride, float* table_grad, void* stream) {
     NGP_TRY(validate_layout(layout));
     if (n == 0) return NGP_OK;
     if (coords == nullptr || dy == nullptr || table_grad == nullptr) return fail(NGP_ERR_INVALID, "encode backward: null pointer");
@@ -509,7 +511,7 @@ extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t 
     const GridParams grid = make_grid_params(*layout);
     const auto* g = reinterpret_cast<const __half*>(dy);
 #if NGP_ENC_BWD_POINTS
-    {
+    if (rows == nullptr) {
         const uint32_t blocks = (n + kEncodeThreads - 1) / kEncodeThreads;
         const cudaStream_t s  = as_stream(stream);
         switch (layout->features_per_level) {
@@ -521,12 +523,28 @@ extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t 
         return check_launch("encode_backward_points_kernel");
     }
 #endif
-    const dim3 blocks = encode_grid(NGP_ENC_BWD_INTERLEAVE, (n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
+    const dim3 blocks    = encode_grid(NGP_ENC_BWD_INTERLEAVE, (n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
+    const cudaStream_t s = as_stream(stream);
     switch (layout->features_per_level) {
-        case 1: encode_backward_kernel<1><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
-        case 2: encode_backward_kernel<2><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
-        case 4: encode_backward_kernel<4><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
-        default: encode_backward_kernel<8><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
+        case 1: encode_backward_kernel<1><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid, rows); break;
+        case 2: encode_backward_kernel<2><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid, rows); break;
+        case 4: encode_backward_kernel<4><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid, rows); break;
+        default: encode_backward_kernel<8><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid, rows); break;
     }
     return check_launch("encode_backward_kernel");
+}
+}  // namespace
+}  // namespace ngp
+
+extern "C" int ngp_encode_grid_backward(const ngp_grid_layout* layout, uint32_t n, const float* coords, uint32_t coord_stride,
+                                        const uint16_t* dy, uint32_t dy_stride, float* table_grad, void* stream) {
+    clear_error();
+    return encode_backward_launch(layout, n, nullptr, coords, coord_stride, dy, dy_stride, table_grad, stream);
+}
+
+extern "C" int ngp_encode_grid_backward_rows(const ngp_grid_layout* layout, uint32_t n, const uint32_t* rows, const float* coords,
+                                             uint32_t coord_stride, const uint16_t* dy, uint32_t dy_stride, float* table_grad, void* stream) {
+    clear_error();
+    if (rows == nullptr) return fail(NGP_ERR_INVALID, "encode backward rows: null row list");
+    return encode_backward_launch(layout, n, rows, coords, coord_stride, dy, dy_stride, table_grad, stream);
 }

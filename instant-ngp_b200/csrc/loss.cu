@@ -520,6 +520,33 @@ __global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_co
     }
 }
 
+// Selection instead of compaction: ray i's kept samples are listed as batch rows
+// rows[cbase + j] = base + j (the samples stay where the march wrote them); numsteps becomes
+// (kept, compacted base); *n_selected = the end of the last listed ray (the batch plus at most
+// one straddling ray).
+__global__ void __launch_bounds__(kCtaThreads) select_write_kernel(const __grid_constant__ KeepParams p, uint32_t* __restrict__ rows,
+                                                                   uint32_t* __restrict__ sample_base, uint32_t* __restrict__ n_selected) {
+    const uint32_t n    = keep_rays(p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
+    uint32_t cbase      = p.block_totals[blockIdx.x];
+    for (uint32_t w = 0; w < warp; ++w) {
+        const uint32_t q = blockIdx.x * kRaysPerCta + w;
+        cbase += q < n ? p.kept[q] : 0u;
+    }
+    if (i >= n) return;
+    const uint32_t k    = cbase < kNetworkBatch ? p.kept[i] : 0u;
+    const uint32_t base = p.numsteps[2u * i + 1u];
+    __syncwarp();
+    if (lane == 0) {
+        p.numsteps[2u * i]      = k;
+        p.numsteps[2u * i + 1u] = cbase;
+        sample_base[i]          = base;
+        if (k > 0) atomicMax(n_selected, cbase + k);
+    }
+    for (uint32_t j = lane; j < k; j += 32u) rows[cbase + j] = base + j;
+}
+
 struct CompactedLossParams {
     uint32_t rays_per_batch;
     uint32_t step;
@@ -534,6 +561,7 @@ struct CompactedLossParams {
     __half* dloss_doutput;         // [batch][16]
     float* loss_output;
     const uint32_t* steps;         // scratch from the keep pass
+    const uint32_t* sample_base;   // optional: ray i's samples are at sample_base[i] (else at its compacted base)
 };
 
 // Step 5: pass 1's compositing over the compacted outputs, then pass 2.
@@ -548,8 +576,9 @@ __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __gri
     __syncwarp();
     if (lane == 0) p.numsteps[2u * i] = cn;
     if (cn == 0) return;
-    const __half* out = p.output + static_cast<uint64_t>(cbase) * 16u;
-    const float* cin  = p.coords + static_cast<uint64_t>(cbase) * 7u;
+    const uint32_t src = p.sample_base != nullptr ? p.sample_base[i] : cbase;
+    const __half* out  = p.output + static_cast<uint64_t>(src) * 16u;
+    const float* cin   = p.coords + static_cast<uint64_t>(src) * 7u;
 
     // composite the k kept samples (pass 1)
     float T    = 1.0f;
@@ -587,6 +616,20 @@ __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __gri
         p.loss_output[i] = __fmaf_rn(diff.z, diff.z, __fmaf_rn(diff.x, diff.x, diff.y * diff.y)) / (3.0f * static_cast<float>(p.rays_per_batch));
     ray_gradients(rgb, target, kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u, cin, out, nullptr,
                   p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u, cn);
+}
+
+// Padding of a selected batch: rows [n, batch) repeat rows [0, n) and their gradients scaled by
+// n / batch (K12 + K13 on the row list instead of copied records).
+__global__ void pad_rows_kernel(const uint32_t* __restrict__ count, uint32_t* __restrict__ rows, __half* __restrict__ dloss, uint32_t batch) {
+    const uint32_t n = *count;
+    const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n == 0 || r < n || r >= batch) return;
+    const uint32_t src = r % n;
+    rows[r]            = rows[src];
+    const float s      = static_cast<float>(n) / static_cast<float>(batch);
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+        dloss[static_cast<uint64_t>(r) * 16u + q] = __float2half(__half2float(dloss[static_cast<uint64_t>(src) * 16u + q]) * s);
 }
 
 // K12 + K13 (ngp.train.cu:862-874): fill the batch tail [n, batch) by wrap-around copies of the
@@ -847,6 +890,82 @@ extern "C" int ngp_training_compact_progressive(uint32_t rays_per_batch, const u
     NGP_TRY(check_launch("scan_kept_kernel"));
     compact_copy_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(k);
     return check_launch("compact_copy_kernel");
+}
+
+extern "C" int ngp_training_select_progressive(uint32_t rays_per_batch, const uint32_t* ray_counter, const ngp_grid_layout* layout,
+                                               const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
+                                               uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, uint32_t* batch_rows,
+                                               uint32_t* n_selected, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes, void* stream) {
+    clear_error();
+    if (rays_per_batch == 0) return NGP_OK;
+    if (layout == nullptr || params == nullptr || coords == nullptr || numsteps == nullptr || enc == nullptr || density == nullptr || rows == nullptr ||
+        batch_rows == nullptr || n_selected == nullptr || compacted_counter == nullptr || scratch == nullptr || enc_stride < sample_bound)
+        return fail(NGP_ERR_INVALID, "progressive selection: invalid input");
+    if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "progressive selection: scratch too small");
+    if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "progressive selection: scratch must be 16-byte aligned");
+    const cudaStream_t s       = as_stream(stream);
+    const uint32_t R           = rays_per_batch;
+    const uint32_t warp_blocks = (R + kRaysPerCta - 1) / kRaysPerCta;
+    ProgressParams p{};
+    p.rays_per_batch = R;
+    p.ray_counter    = ray_counter;
+    p.numsteps       = numsteps;
+    p.coords         = coords;
+    progress_scratch(p, R, scratch, rows);
+    NGP_TRY(progressive_rounds(p, R, layout, params, coords, sample_bound, enc, enc_stride, density, nullptr, s));
+    KeepParams k{};
+    k.rays_per_batch = R;
+    k.ray_counter    = ray_counter;
+    k.numsteps       = numsteps;
+    k.steps          = p.steps;
+    k.kept           = p.kept;
+    k.block_totals   = p.block_totals;
+    scan_kept_kernel<<<1, 1024, 0, s>>>(k.block_totals, warp_blocks, compacted_counter, kNetworkBatch);
+    NGP_TRY(check_launch("scan_kept_kernel"));
+    NGP_TRY(check_cuda(cudaMemsetAsync(n_selected, 0, sizeof(uint32_t), s), "progressive selection: clear count"));
+    select_write_kernel<<<warp_blocks, kCtaThreads, 0, s>>>(k, batch_rows, p.list_off, n_selected);
+    return check_launch("select_write_kernel");
+}
+
+extern "C" int ngp_training_loss_selected(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                          uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                          const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* coords,
+                                          uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, void* stream) {
+    clear_error();
+    if (rays_per_batch == 0) return NGP_OK;
+    if (pixels == nullptr || network_output == nullptr || rays == nullptr || numsteps == nullptr || coords == nullptr || dloss_doutput == nullptr ||
+        scratch == nullptr || frame_count == 0 || width == 0 || height == 0)
+        return fail(NGP_ERR_INVALID, "selected loss: invalid input");
+    if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "selected loss: scratch too small");
+    const cudaStream_t s = as_stream(stream);
+    CompactedLossParams p{};
+    p.rays_per_batch = rays_per_batch;
+    p.step           = step;
+    p.ray_counter    = ray_counter;
+    p.pixels         = pixels;
+    p.frame_count    = frame_count;
+    p.width          = width;
+    p.height         = height;
+    p.output         = reinterpret_cast<const __half*>(network_output);
+    p.ray_indices    = ray_indices;
+    p.rays           = rays;
+    p.numsteps       = numsteps;
+    p.coords         = coords;
+    p.dloss_doutput  = reinterpret_cast<__half*>(dloss_doutput);
+    p.loss_output    = loss_values;
+    p.steps          = static_cast<const uint32_t*>(scratch);
+    p.sample_base    = static_cast<const uint32_t*>(scratch) + static_cast<size_t>(rays_per_batch) * 3u;  // list_off region
+    if (loss_values != nullptr) NGP_TRY(check_cuda(cudaMemsetAsync(loss_values, 0, sizeof(float) * rays_per_batch, s), "selected loss: clear"));
+    loss_compacted_kernel<<<(rays_per_batch + kRaysPerCta - 1) / kRaysPerCta, kCtaThreads, 0, s>>>(p);
+    return check_launch("loss_compacted_kernel");
+}
+
+extern "C" int ngp_pad_training_rows(const uint32_t* compacted_counter, uint32_t* batch_rows, uint16_t* dloss_doutput, void* stream) {
+    clear_error();
+    if (compacted_counter == nullptr || batch_rows == nullptr || dloss_doutput == nullptr) return fail(NGP_ERR_INVALID, "pad rows: null pointer");
+    pad_rows_kernel<<<kNetworkBatch / 256u, 256, 0, as_stream(stream)>>>(compacted_counter, batch_rows, reinterpret_cast<__half*>(dloss_doutput),
+                                                                           kNetworkBatch);
+    return check_launch("pad_rows_kernel");
 }
 
 extern "C" int ngp_eval_network_progressive(uint32_t n_rays, const ngp_grid_layout* layout, const uint16_t* params, const float* coords,

@@ -335,6 +335,7 @@ struct MlpBackwardParams {
     __half* dx;               // dL/d(encoded positions) [32][dx_stride] (may be null)
     uint32_t dx_stride;
     float* dw_partial;        // [gridDim.x][10240] per-CTA weight-gradient partials
+    const uint32_t* rows;     // optional: batch row r reads features and record of sample rows[r]
 };
 
 // TMEM columns: D0 working accumulator 0-63; weight-gradient accumulators after it.
@@ -374,14 +375,14 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         return r < p.n ? __ldg(reinterpret_cast<const uint2*>(p.dy + static_cast<uint64_t>(r) * 16u)) : make_uint2(0, 0);
     };
     if (blockIdx.x < n_tiles) {
-        load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur);
+        load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur, p.rows);
         dy_cur = load_dy(blockIdx.x * kRows + t);
     }
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         const uint32_t row = tile * kRows + t;
         const bool valid   = row < p.n;
         if (tile + gridDim.x < n_tiles) {
-            load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt);
+            load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
             dy_nxt = load_dy((tile + gridDim.x) * kRows + t);
         }
         // ---------------- forward recompute ----------------
@@ -720,13 +721,14 @@ extern "C" int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows,
 
 extern "C" uint32_t ngp_mlp_backward_scratch_floats(void) { return mlp_backward_max_ctas() * kMlpParams; }
 
-extern "C" int ngp_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
-                                uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, float* scratch,
-                                size_t scratch_floats, float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream) {
-    clear_error();
+namespace ngp {
+namespace {
+int mlp_backward_launch(uint32_t n, const uint32_t* rows, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
+                        uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, float* scratch, size_t scratch_floats,
+                        float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream) {
     if (params == nullptr || x == nullptr || coords == nullptr || dy == nullptr || scratch == nullptr)
         return fail(NGP_ERR_INVALID, "mlp backward: null pointer");
-    if (x_stride < n || coord_stride < 7 || (dx != nullptr && dx_stride < n)) return fail(NGP_ERR_INVALID, "mlp backward: bad stride");
+    if ((rows == nullptr && x_stride < n) || coord_stride < 7 || (dx != nullptr && dx_stride < n)) return fail(NGP_ERR_INVALID, "mlp backward: bad stride");
     NGP_TRY(ensure_attrs());
     const uint32_t n_tiles = (n + kRows - 1) / kRows;
     uint32_t grid          = static_cast<uint32_t>(mlp_grid(kBwdSmem, reinterpret_cast<const void*>(mlp_backward_kernel), n_tiles == 0 ? 1 : n_tiles, kBwdTmemCols));
@@ -735,12 +737,31 @@ extern "C" int ngp_mlp_backward(uint32_t n, const uint16_t* params, const uint16
         if (grid == 0) return fail(NGP_ERR_INVALID, "mlp backward: scratch too small (need ngp_mlp_backward_scratch_floats())");
     }
     MlpBackwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
-                        reinterpret_cast<const __half*>(dy), reinterpret_cast<__half*>(dx), dx_stride, scratch};
+                        reinterpret_cast<const __half*>(dy), reinterpret_cast<__half*>(dx), dx_stride, scratch, rows};
     mlp_backward_kernel<<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
     NGP_TRY(check_launch("mlp_backward_kernel"));
     mlp_reduce_partials_kernel<<<(kMlpParams + 255) / 256, 256, 0, as_stream(stream)>>>(scratch, grid, dw_scale, dw_f32,
                                                                                           reinterpret_cast<__half*>(dw_f16));
     return check_launch("mlp_reduce_partials_kernel");
+}
+}  // namespace
+}  // namespace ngp
+
+extern "C" int ngp_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
+                                uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, float* scratch,
+                                size_t scratch_floats, float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream) {
+    clear_error();
+    return mlp_backward_launch(n, nullptr, params, x, x_stride, coords, coord_stride, dy, dx, dx_stride, scratch, scratch_floats, dw_f32, dw_f16,
+                               dw_scale, stream);
+}
+
+extern "C" int ngp_mlp_backward_rows(uint32_t n, const uint32_t* rows, const uint16_t* params, const uint16_t* x, uint32_t x_stride,
+                                     const float* coords, uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride,
+                                     float* scratch, size_t scratch_floats, float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream) {
+    clear_error();
+    if (rows == nullptr) return fail(NGP_ERR_INVALID, "mlp backward rows: null row list");
+    return mlp_backward_launch(n, rows, params, x, x_stride, coords, coord_stride, dy, dx, dx_stride, scratch, scratch_floats, dw_f32, dw_f16,
+                               dw_scale, stream);
 }
 
 extern "C" int ngp_mlp_status(uint32_t* out_status, int reset) {

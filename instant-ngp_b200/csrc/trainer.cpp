@@ -50,8 +50,8 @@ struct Split {
 
 }  // namespace
 
-#ifndef NGP_PROGRESSIVE
-#define NGP_PROGRESSIVE 1  // 0: densities of every pre-compaction sample
+#ifndef NGP_SELECT
+#define NGP_SELECT 1  // 0: the kept samples' records and encodings are copied into a compacted batch
 #endif
 
 struct MarchSet {
@@ -96,6 +96,8 @@ struct ngp_trainer {
     uint16_t* enc          = nullptr;  // [32][MAX_SAMPLES] encoded positions
     uint16_t* out          = nullptr;  // [MAX_SAMPLES][16] network output (training: raw densities)
     uint32_t* rows         = nullptr;  // [MAX_SAMPLES] row list of the progressive density evaluation
+    uint32_t* batch_rows   = nullptr;  // [COMPACTED_ROWS] the batch as rows of the kept samples
+    uint16_t* dens         = nullptr;  // [MAX_SAMPLES] raw densities of the evaluated samples
     uint16_t* cout         = nullptr;  // [COMPACTED_ROWS][16] network output of the compacted samples
     uint16_t* grid_density = nullptr;  // [2^21] raw density of the grid samples
     float* ccoords         = nullptr;  // [COMPACTED_ROWS][7] compacted
@@ -156,7 +158,7 @@ void destroy(ngp_trainer* t) {
     free_split(t->val);
     free_split(t->test);
     void* ptrs[] = {t->master, t->params, t->grads, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
-                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->rows, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
+                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->rows, t->batch_rows, t->dens, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table};
     for (void* p : ptrs) cudaFree(p);
     for (MarchSet& m : t->sets) cudaFree(m.coords), cudaFree(m.rays), cudaFree(m.ray_indices), cudaFree(m.numsteps), cudaFree(m.counters);
@@ -301,34 +303,48 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     // (1932-1944): only the densities decide which samples a ray keeps, and only the samples in
     // front of each ray's stopping point need them
     const MarchSet& m = t->sets[t->step & 1u];
-#if NGP_PROGRESSIVE
-    NGP_TRY(ngp_training_compact_progressive(t->rays_per_batch, m.counters + 0, &t->layout, t->params, m.coords, t->inference_samples, m.numsteps,
-                                             t->enc, t->inference_samples, t->out, t->rows, t->ccoords, t->cenc, m.counters + 2, t->loss_scratch,
-                                             t->loss_scratch_bytes, t->stream));
+#if NGP_SELECT
+    // the batch is a list of the kept samples' rows; the samples stay in place
+    NGP_TRY(ngp_training_select_progressive(t->rays_per_batch, m.counters + 0, &t->layout, t->params, m.coords, t->inference_samples, m.numsteps,
+                                            t->enc, t->inference_samples, t->dens, t->rows, t->batch_rows, m.counters + 3, m.counters + 2,
+                                            t->loss_scratch, t->loss_scratch_bytes, t->stream));
 #else
-    NGP_TRY(encode(t, t->inference_samples, m.coords, t->enc, t->inference_samples));
-    NGP_TRY(ngp_density_forward(t->inference_samples, t->params, t->enc, t->inference_samples, t->out, t->stream));
-    NGP_TRY(ngp_training_compact_by_density(t->rays_per_batch, m.counters + 0, t->out, m.coords, t->enc, t->inference_samples, m.numsteps,
-                                            t->ccoords, t->cenc, m.counters + 2, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    NGP_TRY(ngp_training_compact_progressive(t->rays_per_batch, m.counters + 0, &t->layout, t->params, m.coords, t->inference_samples, m.numsteps,
+                                             t->enc, t->inference_samples, t->dens, t->rows, t->ccoords, t->cenc, m.counters + 2, t->loss_scratch,
+                                             t->loss_scratch_bytes, t->stream));
 #endif
     // the step's counters are final here: the host reads them (for the next step's batch size)
     // while the rest of the step runs
     NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, m.counters, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
     NGP_TRY(check_cuda(cudaEventRecord(t->ev_counts, t->stream), "record counters"));
     mark(t, 3);
-    // the full network on the compacted rows, then compositing, loss and padding (1944-1956)
+    // the full network on the kept samples, then compositing, loss and padding (1944-1956)
+#if NGP_SELECT
+    NGP_TRY(ngp_mlp_forward_rows(kCompactedRows, t->batch_rows, m.counters + 3, t->params, t->enc, t->inference_samples, m.coords, 7, t->out,
+                                 t->stream));
+    NGP_TRY(ngp_training_loss_selected(t->rays_per_batch, rng_step, m.counters + 0, s.pixels, s.frames, s.width, s.height, t->out, m.ray_indices,
+                                       m.rays, m.numsteps, m.coords, t->dloss, t->loss_values, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    NGP_TRY(ngp_pad_training_rows(m.counters + 2, t->batch_rows, t->dloss, t->stream));
+    mark(t, 4);
+    NGP_TRY(ngp_mlp_backward_rows(kNetworkBatch, t->batch_rows, t->params, t->enc, t->inference_samples, m.coords, 7, t->dloss, t->denc, kNetworkBatch,
+                                  t->mlp_scratch, t->mlp_scratch_floats, t->grads, nullptr, 1.0f, t->stream));
+    mark(t, 5);
+    NGP_TRY(ngp_encode_grid_backward_rows(&t->layout, kNetworkBatch, t->batch_rows, m.coords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams,
+                                          t->stream));
+    mark(t, 6);
+#else
     NGP_TRY(ngp_mlp_forward(kCompactedRows, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->cout, nullptr, t->stream));
     NGP_TRY(ngp_training_loss_compacted(t->rays_per_batch, rng_step, m.counters + 0, s.pixels, s.frames, s.width, s.height, t->cout, m.ray_indices,
                                         m.rays, m.numsteps, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->loss_scratch_bytes,
                                         t->stream));
     NGP_TRY(ngp_pad_training_batch_enc(m.counters + 2, t->ccoords, t->dloss, t->cenc, kCompactedRows, t->stream));
     mark(t, 4);
-    // fused MLP backward (recompute) and encoding backward on the batch
     NGP_TRY(ngp_mlp_backward(kNetworkBatch, t->params, t->cenc, kCompactedRows, t->ccoords, 7, t->dloss, t->denc, kNetworkBatch, t->mlp_scratch,
                              t->mlp_scratch_floats, t->grads, nullptr, 1.0f, t->stream));
     mark(t, 5);
     NGP_TRY(ngp_encode_grid_backward(&t->layout, kNetworkBatch, t->ccoords, 7, t->denc, kNetworkBatch, t->grads + kMlpParams, t->stream));
     mark(t, 6);
+#endif
     // adaptive batch (ngp.train.cpp:125-133): this step's counters were copied after the loss
     // pass; the host waits for them while the backward pass runs, then launches the next step's
     // march on march_stream
@@ -514,6 +530,10 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->enc, static_cast<size_t>(kMaxSamples) * 32u, "encoded positions"));
         NGP_TRY(dalloc(t->out, static_cast<size_t>(kMaxSamples) * 16u, "network output"));
         NGP_TRY(dalloc(t->rows, kMaxSamples, "row list"));
+        NGP_TRY(dalloc(t->batch_rows, kCompactedRows, "batch rows"));
+        // a batch that selects nothing still reads valid (zero) rows before the step reports it
+        NGP_TRY(check_cuda(cudaMemsetAsync(t->batch_rows, 0, sizeof(uint32_t) * kCompactedRows, t->stream), "clear batch rows"));
+        NGP_TRY(dalloc(t->dens, kMaxSamples, "densities"));
         NGP_TRY(dalloc(t->grid_density, kGridCells, "grid density"));
         NGP_TRY(dalloc(t->ccoords, static_cast<size_t>(kCompactedRows) * 7u, "compacted coords"));
         NGP_TRY(dalloc(t->cout, static_cast<size_t>(kCompactedRows) * 16u, "compacted network output"));

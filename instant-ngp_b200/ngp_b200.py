@@ -304,6 +304,45 @@ def eval_network_progressive(n_rays, layout, params, coords, sample_bound, numst
                                               _stream(stream)), "ngp_eval_network_progressive")
 
 
+def training_select_progressive(rays_per_batch, ray_counter, layout, params, coords, sample_bound, numsteps, enc, density, rows, batch_rows,
+                                n_selected, compacted_counter, scratch, enc_stride=None, stream=None) -> None:
+    _check(lib().ngp_training_select_progressive(_u32(rays_per_batch), _ptr(ray_counter), ctypes.byref(layout), _ptr(params), _ptr(coords),
+                                                 _u32(sample_bound), _ptr(numsteps), _ptr(enc), _u32(enc.shape[1] if enc_stride is None else enc_stride),
+                                                 _ptr(density), _ptr(rows), _ptr(batch_rows), _ptr(n_selected), _ptr(compacted_counter), _ptr(scratch),
+                                                 ctypes.c_size_t(scratch.numel() * scratch.element_size()), _stream(stream)),
+           "ngp_training_select_progressive")
+
+
+def training_loss_selected(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, ray_indices, rays, numsteps,
+                           coords, dloss_doutput, loss_values, scratch, stream=None) -> None:
+    _check(lib().ngp_training_loss_selected(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),
+                                            _u32(height), _ptr(network_output), _ptr(ray_indices), _ptr(rays), _ptr(numsteps), _ptr(coords),
+                                            _ptr(dloss_doutput), _ptr(loss_values), _ptr(scratch),
+                                            ctypes.c_size_t(scratch.numel() * scratch.element_size()), _stream(stream)), "ngp_training_loss_selected")
+
+
+def pad_training_rows(compacted_counter, batch_rows, dloss_doutput, stream=None) -> None:
+    _check(lib().ngp_pad_training_rows(_ptr(compacted_counter), _ptr(batch_rows), _ptr(dloss_doutput), _stream(stream)), "ngp_pad_training_rows")
+
+
+def mlp_forward_rows(max_rows, rows, n_rows, params, x, x_stride, coords, out, stream=None) -> None:
+    _check(lib().ngp_mlp_forward_rows(_u32(max_rows), _ptr(rows), _ptr(n_rows), _ptr(params), _ptr(x), _u32(x_stride), _ptr(coords),
+                                      _u32(coords.shape[1]), _ptr(out), _stream(stream)), "ngp_mlp_forward_rows")
+
+
+def mlp_backward_rows(n, rows, params, x, x_stride, coords, dy, dx, dx_stride, dw_f32, stream=None) -> None:
+    sc = mlp_backward_scratch()
+    _check(lib().ngp_mlp_backward_rows(_u32(n), _ptr(rows), _ptr(params), _ptr(x), _u32(x_stride), _ptr(coords), _u32(coords.shape[1]), _ptr(dy),
+                                       _ptr(dx), _u32(dx_stride), _ptr(sc), ctypes.c_size_t(sc.numel()), _ptr(dw_f32), None, ctypes.c_float(1.0),
+                                       _stream(stream)), "ngp_mlp_backward_rows")
+
+
+def encode_grid_backward_rows(layout, n, rows, coords, dy, table_grad, dy_stride=None, stream=None) -> None:
+    _check(lib().ngp_encode_grid_backward_rows(ctypes.byref(layout), _u32(n), _ptr(rows), _ptr(coords), _u32(coords.shape[1]), _ptr(dy),
+                                               _u32(dy.shape[1] if dy_stride is None else dy_stride), _ptr(table_grad), _stream(stream)),
+           "ngp_encode_grid_backward_rows")
+
+
 def training_loss_compacted(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, compacted_output, ray_indices, rays,
                             numsteps, compacted_coords, dloss_doutput, loss_values, scratch, stream=None) -> None:
     _check(lib().ngp_training_loss_compacted(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),

@@ -599,3 +599,80 @@ def test_progressive_evaluation_renders_identically(ngp, small_scene, blob_bitfi
     assert img_a.cpu().numpy().tobytes() == img_b.cpu().numpy().tobytes()
     evaluated = int((prog[:total, 3] != 0).sum().item())
     assert 0 < evaluated < total
+
+
+def test_selected_batch_matches_compacted_batch(ngp, small_scene, blob_bitfield):
+    """The trainer's selection flow (the batch as a list of the kept samples' rows, network,
+    loss and backward reading the samples in place) against the copying flow: same counts, the
+    listed rows are the copied records and encodings, and the loss, output gradients, MLP weight
+    gradients and input gradients are bit-identical; the grid gradient (fp32 atomics, summation
+    order free) agrees within 1e-5 relative."""
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    bits = T(blob_bitfield)
+    n, limit, step, batch = 12288, 1 << 21, 8, 1 << 18
+    rows_n = ngp.compacted_rows()
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    layout = ngp.grid_layout(16, 2, 19, 16, math.log2(128.0) / 15.0)
+    _, table, _ = workloads.encode_inputs(1, layout.n_params, 16, 2, seed=4)
+    table = (table.astype(np.float32) * 2e4).astype(np.float16)
+    mlp = workloads.xavier_mlp_params(9)
+    mlp[2048:2048 + 64] = np.random.default_rng(3).uniform(0.2, 0.5, 64).astype(np.float16)
+    params = T(np.concatenate([mlp, table]).view(np.int16))
+    ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    ridx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    msc = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
+    rc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, coords, rays, ridx, ns, msc, rc, sc)
+    torch.cuda.synchronize()
+    m = (int(sc.item()) + 127) // 128 * 128
+
+    def fresh(dtype, *shape):
+        return torch.zeros(shape, dtype=dtype, device="cuda")
+
+    # copying flow
+    sa = fresh(torch.uint8, ngp.loss_scratch_bytes(n))
+    ns_a, cc_a = ns.clone(), fresh(torch.int32, 1)
+    enc_a, dens_a, rows_a = fresh(torch.float16, 32, m), fresh(torch.float16, m), fresh(torch.int32, m)
+    cco, cen = fresh(torch.float32, rows_n, 7), fresh(torch.float16, 32, rows_n)
+    ngp.training_compact_progressive(n, rc, layout, params, coords, m, ns_a, enc_a, dens_a, rows_a, cco, cen, cc_a, sa)
+    out_a = fresh(torch.float16, rows_n, 16)
+    ngp.mlp_forward(params[:10240], cen, cco, out_a, n=rows_n, x_stride=rows_n)
+    dl_a, loss_a = fresh(torch.float16, batch, 16), fresh(torch.float32, n)
+    ngp.training_loss_compacted(n, step, rc, pix, F, W, H, out_a, ridx, rays, ns_a, cco, dl_a, loss_a, sa)
+    ngp.pad_training_batch_enc(cc_a, cco, dl_a, cen, rows_n)
+    dx_a, dw_a = fresh(torch.float16, 32, batch), fresh(torch.float32, 10240)
+    ngp.mlp_backward(params[:10240], cen, cco, dl_a, dx=dx_a, dw_f32=dw_a, n=batch, x_stride=rows_n)
+    g_a = fresh(torch.float32, layout.n_params)
+    ngp.encode_grid_backward(layout, cco, dx_a, g_a, n=batch, coord_stride=7)
+    # selection flow
+    sb = fresh(torch.uint8, ngp.loss_scratch_bytes(n))
+    ns_b, cc_b, nsel = ns.clone(), fresh(torch.int32, 1), fresh(torch.int32, 1)
+    enc_b, dens_b, rows_b, brows = fresh(torch.float16, 32, m), fresh(torch.float16, m), fresh(torch.int32, m), fresh(torch.int32, rows_n)
+    ngp.training_select_progressive(n, rc, layout, params, coords, m, ns_b, enc_b, dens_b, rows_b, brows, nsel, cc_b, sb)
+    out_b = fresh(torch.float16, m, 16)
+    ngp.mlp_forward_rows(rows_n, brows, nsel, params[:10240], enc_b, m, coords, out_b)
+    dl_b, loss_b = fresh(torch.float16, batch, 16), fresh(torch.float32, n)
+    ngp.training_loss_selected(n, step, rc, pix, F, W, H, out_b, ridx, rays, ns_b, coords, dl_b, loss_b, sb)
+    ngp.pad_training_rows(cc_b, brows, dl_b)
+    dx_b, dw_b = fresh(torch.float16, 32, batch), fresh(torch.float32, 10240)
+    ngp.mlp_backward_rows(batch, brows, params[:10240], enc_b, m, coords, dl_b, dx_b, batch, dw_b)
+    g_b = fresh(torch.float32, layout.n_params)
+    ngp.encode_grid_backward_rows(layout, batch, brows, coords, dx_b, g_b)
+    torch.cuda.synchronize()
+    assert int(cc_a.item()) == int(cc_b.item()) == batch
+    assert (ns_a == ns_b).all()
+    rb = brows[:batch].long()
+    assert cco[:batch].cpu().numpy().tobytes() == coords[rb].cpu().numpy().tobytes()
+    assert cen[:, :batch].cpu().numpy().view(np.uint16).tobytes() == enc_b[:, rb].cpu().numpy().view(np.uint16).tobytes()
+    assert loss_a.cpu().numpy().tobytes() == loss_b.cpu().numpy().tobytes()
+    assert dl_a.cpu().numpy().view(np.uint16).tobytes() == dl_b.cpu().numpy().view(np.uint16).tobytes()
+    assert dw_a.cpu().numpy().tobytes() == dw_b.cpu().numpy().tobytes()
+    assert dx_a.cpu().numpy().view(np.uint16).tobytes() == dx_b.cpu().numpy().view(np.uint16).tobytes()
+    ga, gb = g_a.cpu().numpy(), g_b.cpu().numpy()
+    assert np.abs(ga - gb).max() <= 1e-5 * np.abs(ga).max()
