@@ -590,16 +590,28 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
     if (t < 32) umma::tmem_dealloc(tmem, kBwdTmemCols);
 }
 
-// dW[j] = scale * sum over CTAs of partial[cta][j], in CTA order (deterministic).
-__global__ void mlp_reduce_partials_kernel(const float* __restrict__ partial, uint32_t n_parts, float scale, float* __restrict__ dw_f32,
-                                           __half* __restrict__ dw_f16) {
-    const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= kMlpParams) return;
-    float acc = 0.0f;
-    for (uint32_t c = 0; c < n_parts; ++c) acc += partial[static_cast<uint64_t>(c) * kMlpParams + j];
-    acc *= scale;
-    if (dw_f32 != nullptr) dw_f32[j] = acc;
-    if (dw_f16 != nullptr) dw_f16[j] = __float2half_rn(acc);
+// dW[j] = scale * sum over CTAs of partial[cta][j] in a fixed order (deterministic): the CTAs are
+// split into kReduceGroups interleaved groups (group g: CTAs g, g + G, ...) summed in CTA order by
+// their own threads, then the group sums are added in group order.
+constexpr uint32_t kReduceGroups = 8;
+
+__global__ void __launch_bounds__(32 * kReduceGroups) mlp_reduce_partials_kernel(const float* __restrict__ partial, uint32_t n_parts, float scale,
+                                                                              float* __restrict__ dw_f32, __half* __restrict__ dw_f16) {
+    __shared__ float s_sum[kReduceGroups][32];
+    const uint32_t lane = threadIdx.x & 31u, g = threadIdx.x >> 5;
+    const uint32_t j    = blockIdx.x * 32u + lane;
+    float acc           = 0.0f;
+    if (j < kMlpParams)
+        for (uint32_t c = g; c < n_parts; c += kReduceGroups) acc += partial[static_cast<uint64_t>(c) * kMlpParams + j];
+    s_sum[g][lane] = acc;
+    __syncthreads();
+    if (g != 0 || j >= kMlpParams) return;
+    float total = 0.0f;
+#pragma unroll
+    for (uint32_t q = 0; q < kReduceGroups; ++q) total += s_sum[q][lane];
+    total *= scale;
+    if (dw_f32 != nullptr) dw_f32[j] = total;
+    if (dw_f16 != nullptr) dw_f16[j] = __float2half_rn(total);
 }
 
 __global__ void sh_encode_kernel(uint32_t n, const float* __restrict__ coords, uint32_t coord_stride, __half* __restrict__ out,
@@ -740,8 +752,8 @@ int mlp_backward_launch(uint32_t n, const uint32_t* rows, const uint16_t* params
                         reinterpret_cast<const __half*>(dy), reinterpret_cast<__half*>(dx), dx_stride, scratch, rows};
     mlp_backward_kernel<<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
     NGP_TRY(check_launch("mlp_backward_kernel"));
-    mlp_reduce_partials_kernel<<<(kMlpParams + 255) / 256, 256, 0, as_stream(stream)>>>(scratch, grid, dw_scale, dw_f32,
-                                                                                          reinterpret_cast<__half*>(dw_f16));
+    mlp_reduce_partials_kernel<<<(kMlpParams + 31) / 32, 32 * kReduceGroups, 0, as_stream(stream)>>>(scratch, grid, dw_scale, dw_f32,
+                                                                                                       reinterpret_cast<__half*>(dw_f16));
     return check_launch("mlp_reduce_partials_kernel");
 }
 }  // namespace
