@@ -1,10 +1,12 @@
 // Multiresolution hash-grid encoding, forward and backward, for sm_100a.
 //
-// Thread mapping is level-major: every CTA serves one level for a chunk of points, so its
-// gathers hit one table; the coarse tables stay L1-resident while the fine ones stream through
-// L2 (the 24 MB table of the BASELINE configuration is L2-resident on B200's 126 MB L2).  A corner's F features are one vector load (F=2: 32-bit half2,
-// F=4: 64-bit), taken through the non-coherent read-only path.  Each thread handles
-// POINTS_PER_THREAD points so that 8 * POINTS_PER_THREAD independent gathers are in flight.
+// Forward: point-major, one thread per point walking the levels two at a time (16 independent
+// gathers in flight, the point read once); a corner's F features are one vector load (F=2:
+// 32-bit half2) through the non-coherent read-only path.  The table (24 MB at the BASELINE
+// configuration) is L2-resident on B200's 126 MB L2.  An optional row list selects the points.
+// Backward: level-major, every CTA scatters one level for a chunk of points, the levels
+// interleaved across consecutive CTAs; on coarse levels the lanes of a warp that share a cell sum
+// their contributions first, and x-neighbour corners that pair up share one 16-byte atomic.
 //
 // Forward follows encode_grid_forward_kernel (ngp.train.cu:876-921) with fp32 accumulation
 // (fmaf in corner order 0..7) instead of fp16 __hfma, rounded once to fp16.
@@ -12,30 +14,10 @@
 // fp32 gradient table with vector atomics (red.global.add.v2/v4.f32) instead of fp16 atomics.
 #include "common.cuh"
 
-// Tuning knobs (compile-time; the defaults are the measured best on B200).
-#ifndef NGP_ENC_FWD_PPT
-#define NGP_ENC_FWD_PPT 1  // points per thread in the forward kernel
-#endif
-#ifndef NGP_ENC_FWD_PAIR
-#define NGP_ENC_FWD_PAIR 0  // 1: one load for an aligned pair of x-neighbour entries (measured slower)
-#endif
-#ifndef NGP_ENC_FWD_INTERLEAVE
-#define NGP_ENC_FWD_INTERLEAVE 0  // 1: consecutive CTAs take consecutive levels; 0: level = blockIdx.y
-#endif
-#ifndef NGP_ENC_FWD_LEVELS
-#define NGP_ENC_FWD_LEVELS 2  // > 0: point-major forward, each thread runs all levels of its point, this many at a time
-#endif
-#ifndef NGP_ENC_BWD_POINTS
-#define NGP_ENC_BWD_POINTS 0  // 1: point-major backward (a thread scatters all levels of its point)
-#endif
+// Tuning knob (compile-time; the default is the measured best on B200): levels up to this
+// resolution pre-sum the lanes of a warp that share a cell before the backward's atomics.
 #ifndef NGP_ENC_BWD_AGG_RES
-#define NGP_ENC_BWD_AGG_RES 256  // levels up to this resolution pre-sum the lanes of a warp that share a cell
-#endif
-#ifndef NGP_ENC_BWD_INTERLEAVE
-#define NGP_ENC_BWD_INTERLEAVE 1
-#endif
-#ifndef NGP_ENC_BWD_PAIR
-#define NGP_ENC_BWD_PAIR 1  // 1: merge the x-neighbour corners into one 16-byte atomic when they pair up
+#define NGP_ENC_BWD_AGG_RES 256
 #endif
 
 namespace ngp {
@@ -46,19 +28,9 @@ constexpr uint32_t kEncodeThreads = 256u;
 // Level and point-chunk of this CTA.  Interleaving the levels across consecutive CTAs spreads
 // the atomic traffic of the small coarse tables over the whole kernel instead of issuing all of
 // a coarse level's updates in the first wave.
-template <bool INTERLEAVE>
 __device__ __forceinline__ void cta_level_chunk(uint32_t n_levels, uint32_t& level, uint32_t& chunk) {
-    if constexpr (INTERLEAVE) {
-        level = blockIdx.x % n_levels;
-        chunk = blockIdx.x / n_levels;
-    } else {
-        level = blockIdx.y;
-        chunk = blockIdx.x;
-    }
-}
-
-inline dim3 encode_grid(bool interleave, uint32_t chunks, uint32_t n_levels) {
-    return interleave ? dim3(chunks * n_levels, 1u) : dim3(chunks, n_levels);
+    level = blockIdx.x % n_levels;
+    chunk = blockIdx.x / n_levels;
 }
 
 template <uint32_t F>
@@ -105,85 +77,6 @@ __device__ __forceinline__ void position_fraction(float x, float scale, float& f
     const float floored = floorf(pos);
     cell                = static_cast<uint32_t>(static_cast<int>(floored));
     frac                = __fsub_rn(pos, floored);
-}
-
-template <uint32_t F, uint32_t PPT>
-__global__ void __launch_bounds__(kEncodeThreads) encode_forward_kernel(const uint32_t n, const float* __restrict__ coords,
-                                                                        const uint32_t coord_stride,
-                                                                        const __half* __restrict__ table,
-                                                                        __half* __restrict__ out, const uint32_t out_stride,
-                                                                        const __grid_constant__ GridParams grid) {
-    using Vec = typename FeatureVec<F>::type;
-    uint32_t level, chunk;
-    cta_level_chunk<NGP_ENC_FWD_INTERLEAVE>(grid.n_levels, level, chunk);
-    const uint32_t level_offset  = grid.offsets[level];
-    const uint32_t hashmap_size  = grid.offsets[level + 1] - level_offset;
-    const uint32_t resolution    = grid.resolution[level];
-    const float scale            = grid.scale[level];
-    const Vec* __restrict__ lvl  = reinterpret_cast<const Vec*>(table) + level_offset;
-    const uint32_t base          = chunk * (kEncodeThreads * PPT) + threadIdx.x;
-
-    float frac[PPT][3];
-    uint32_t cell[PPT][3];
-    bool valid[PPT];
-#pragma unroll
-    for (uint32_t p = 0; p < PPT; ++p) {
-        const uint32_t i = base + p * kEncodeThreads;
-        valid[p]         = i < n;
-        const float* c   = coords + static_cast<uint64_t>(valid[p] ? i : 0u) * coord_stride;
-#pragma unroll
-        for (uint32_t d = 0; d < 3; ++d) position_fraction(__ldg(c + d), scale, frac[p][d], cell[p][d]);
-    }
-
-    // Issue all 8 * PPT gathers before any arithmetic depends on them.  For F <= 4 the x-neighbour
-    // corners often share one aligned pair of entries (dense levels: idx and idx + 1 with idx even;
-    // hashed levels: x even, so (x ^ h) and ((x + 1) ^ h) differ in bit 0 only): one load of the
-    // pair containing corner x serves both, and corner x + 1 is loaded separately only otherwise.
-    Vec v[PPT][8];
-#pragma unroll
-    for (uint32_t p = 0; p < PPT; ++p) {
-#pragma unroll
-        for (uint32_t yz = 0; yz < 4; ++yz) {
-            const uint32_t cy = cell[p][1] + (yz & 1u), cz = cell[p][2] + (yz >> 1);
-            const uint32_t i0 = grid_index(hashmap_size, resolution, cell[p][0], cy, cz);
-            const uint32_t i1 = grid_index(hashmap_size, resolution, cell[p][0] + 1u, cy, cz);
-#if NGP_ENC_FWD_PAIR
-            if constexpr (F <= 4) {
-                using Pair          = typename FeatureVec<2 * F>::type;
-                const Pair pr       = __ldg(reinterpret_cast<const Pair*>(lvl + (i0 & ~1u)));
-                const Vec* pv       = reinterpret_cast<const Vec*>(&pr);
-                v[p][2 * yz]        = pv[i0 & 1u];
-                v[p][2 * yz + 1]    = ((i0 ^ i1) == 1u) ? pv[i1 & 1u] : __ldg(lvl + i1);
-                continue;
-            }
-#endif
-            v[p][2 * yz]     = __ldg(lvl + i0);
-            v[p][2 * yz + 1] = __ldg(lvl + i1);
-        }
-    }
-
-#pragma unroll
-    for (uint32_t p = 0; p < PPT; ++p) {
-        float acc[F];
-#pragma unroll
-        for (uint32_t f = 0; f < F; ++f) acc[f] = 0.0f;
-#pragma unroll
-        for (uint32_t corner = 0; corner < 8; ++corner) {
-            const float wx = (corner & 1u) ? frac[p][0] : __fsub_rn(1.0f, frac[p][0]);
-            const float wy = (corner & 2u) ? frac[p][1] : __fsub_rn(1.0f, frac[p][1]);
-            const float wz = (corner & 4u) ? frac[p][2] : __fsub_rn(1.0f, frac[p][2]);
-            const float w  = __fmul_rn(__fmul_rn(wx, wy), wz);
-            float val[F];
-            unpack<F>(v[p][corner], val);
-#pragma unroll
-            for (uint32_t f = 0; f < F; ++f) acc[f] = __fmaf_rn(w, val[f], acc[f]);
-        }
-        if (valid[p]) {
-            const uint32_t i = base + p * kEncodeThreads;
-#pragma unroll
-            for (uint32_t f = 0; f < F; ++f) out[static_cast<uint64_t>(level * F + f) * out_stride + i] = __float2half_rn(acc[f]);
-        }
-    }
 }
 
 // Point-major forward: a thread reads its point once and walks the levels LPI at a time (8 * LPI
@@ -288,7 +181,6 @@ __device__ __forceinline__ void scatter_level(const float (&x)[3], const float (
             c0[f] = __fmul_rn(w0, g[f]);
             c1[f] = __fmul_rn(w1, g[f]);
         }
-#if NGP_ENC_BWD_PAIR
         if constexpr (F <= 2) {
             // Entries 2k and 2k+1 share one 16-byte (F=2) / 8-byte (F=1) aligned slot: one atomic.
             if ((i0 ^ i1) == 1u) {
@@ -303,7 +195,6 @@ __device__ __forceinline__ void scatter_level(const float (&x)[3], const float (
                 continue;
             }
         }
-#endif
         scatter_add<F>(lvl + static_cast<uint64_t>(i0) * F, c0);
         scatter_add<F>(lvl + static_cast<uint64_t>(i1) * F, c1);
     }
@@ -399,7 +290,7 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const u
                                                                          float* __restrict__ table_grad,
                                                                          const __grid_constant__ GridParams grid, const uint32_t* __restrict__ rows) {
     uint32_t level, chunk;
-    cta_level_chunk<NGP_ENC_BWD_INTERLEAVE>(grid.n_levels, level, chunk);
+    cta_level_chunk(grid.n_levels, level, chunk);
     const uint32_t i = chunk * kEncodeThreads + threadIdx.x;
     if (i >= n) return;
     float g[F];
@@ -417,27 +308,9 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_backward_kernel(const u
     scatter_level<F>(x, g, table_grad, grid, level);
 }
 
-// Point-major backward: a thread reads its point once and scatters every level.
-template <uint32_t F>
-__global__ void __launch_bounds__(kEncodeThreads) encode_backward_points_kernel(const uint32_t n, const float* __restrict__ coords,
-                                                                                const uint32_t coord_stride,
-                                                                                const __half* __restrict__ dy, const uint32_t dy_stride,
-                                                                                float* __restrict__ table_grad,
-                                                                                const __grid_constant__ GridParams grid) {
-    const uint32_t i = blockIdx.x * kEncodeThreads + threadIdx.x;
-    if (i >= n) return;
-    const float* c   = coords + static_cast<uint64_t>(i) * coord_stride;
-    const float x[3] = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
-    for (uint32_t level = 0; level < grid.n_levels; ++level) {
-        float g[F];
-        load_dy<F>(dy, dy_stride, level, i, g);
-        scatter_level<F>(x, g, table_grad, grid, level);
-    }
-}
-
 int launch_points_forward(const ngp_grid_layout& layout, const GridParams& grid, uint32_t n, const float* coords, uint32_t coord_stride,
                           const uint16_t* table, uint16_t* out, uint32_t out_stride, const uint32_t* rows, const uint32_t* n_dev, cudaStream_t s) {
-    constexpr uint32_t lpi = NGP_ENC_FWD_LEVELS > 0 ? NGP_ENC_FWD_LEVELS : 2;
+    constexpr uint32_t lpi = 2;  // levels in flight per thread (1 and 4 measured slower)
     const uint32_t blocks  = (n + kEncodeThreads - 1) / kEncodeThreads;
     const auto* t          = reinterpret_cast<const __half*>(table);
     auto* o                = reinterpret_cast<__half*>(out);
@@ -472,20 +345,7 @@ extern "C" int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n
     if (coords == nullptr || table == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "encode forward: null pointer");
     if (coord_stride < 3 || out_stride < n) return fail(NGP_ERR_INVALID, "encode forward: bad stride");
     const GridParams grid = make_grid_params(*layout);
-#if NGP_ENC_FWD_LEVELS > 0
     return launch_points_forward(*layout, grid, n, coords, coord_stride, table, out, out_stride, nullptr, nullptr, as_stream(stream));
-#endif
-    constexpr uint32_t ppt = NGP_ENC_FWD_PPT;
-    const dim3 blocks = encode_grid(NGP_ENC_FWD_INTERLEAVE, (n + kEncodeThreads * ppt - 1) / (kEncodeThreads * ppt), layout->n_levels);
-    const auto* t = reinterpret_cast<const __half*>(table);
-    auto* o       = reinterpret_cast<__half*>(out);
-    switch (layout->features_per_level) {
-        case 1: encode_forward_kernel<1, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-        case 2: encode_forward_kernel<2, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-        case 4: encode_forward_kernel<4, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-        default: encode_forward_kernel<8, ppt><<<blocks, kEncodeThreads, 0, as_stream(stream)>>>(n, coords, coord_stride, t, o, out_stride, grid); break;
-    }
-    return check_launch("encode_forward_kernel");
 }
 
 extern "C" int ngp_encode_grid_forward_rows(const ngp_grid_layout* layout, uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows,
@@ -510,20 +370,7 @@ int encode_backward_launch(const ngp_grid_layout* layout, uint32_t n, const uint
     if (coord_stride < 3 || dy_stride < n) return fail(NGP_ERR_INVALID, "encode backward: bad stride");
     const GridParams grid = make_grid_params(*layout);
     const auto* g = reinterpret_cast<const __half*>(dy);
-#if NGP_ENC_BWD_POINTS
-    if (rows == nullptr) {
-        const uint32_t blocks = (n + kEncodeThreads - 1) / kEncodeThreads;
-        const cudaStream_t s  = as_stream(stream);
-        switch (layout->features_per_level) {
-            case 1: encode_backward_points_kernel<1><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
-            case 2: encode_backward_points_kernel<2><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
-            case 4: encode_backward_points_kernel<4><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
-            default: encode_backward_points_kernel<8><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid); break;
-        }
-        return check_launch("encode_backward_points_kernel");
-    }
-#endif
-    const dim3 blocks    = encode_grid(NGP_ENC_BWD_INTERLEAVE, (n + kEncodeThreads - 1) / kEncodeThreads, layout->n_levels);
+    const dim3 blocks    = dim3(((n + kEncodeThreads - 1) / kEncodeThreads) * layout->n_levels);
     const cudaStream_t s = as_stream(stream);
     switch (layout->features_per_level) {
         case 1: encode_backward_kernel<1><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, g, dy_stride, table_grad, grid, rows); break;

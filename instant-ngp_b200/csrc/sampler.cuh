@@ -138,51 +138,6 @@ __device__ __forceinline__ bool make_train_ray(uint32_t i, uint32_t rays_per_bat
     return true;
 }
 
-// Count the occupied cone steps along a ray (at most kMarchSteps).
-__device__ __forceinline__ uint32_t march_count(float3 o, float3 d, float start_t, const uint8_t* __restrict__ bits) {
-    const float3 inv = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
-    uint32_t n       = 0;
-    float t          = start_t;
-    while (n < kMarchSteps) {
-        const float3 pos = ray_point(o, d, t);
-        if (!inside_unit_cube(pos)) break;
-        if (occupied(pos, bits)) {
-            ++n;
-            t += kConeStep;
-        } else {
-            t = skip_empty_voxel(t, pos, d, inv);
-        }
-    }
-    return n;
-}
-
-// Re-march and write `n` 7-float sample records {pos, dt, (dir + 1) / 2} starting at `out`.
-__device__ __forceinline__ void march_write(float3 o, float3 d, float start_t, uint32_t n, const uint8_t* __restrict__ bits,
-                                            float* __restrict__ out) {
-    const float3 inv  = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
-    const float3 warp = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
-    float t           = start_t;
-    uint32_t j        = 0;
-    while (j < n) {
-        const float3 pos = ray_point(o, d, t);
-        if (!inside_unit_cube(pos)) break;
-        if (occupied(pos, bits)) {
-            float* c = out + static_cast<uint64_t>(j) * 7u;
-            c[0]     = pos.x;
-            c[1]     = pos.y;
-            c[2]     = pos.z;
-            c[3]     = kConeStep;
-            c[4]     = warp.x;
-            c[5]     = warp.y;
-            c[6]     = warp.z;
-            ++j;
-            t += kConeStep;
-        } else {
-            t = skip_empty_voxel(t, pos, d, inv);
-        }
-    }
-}
-
 // ---- block-wide exclusive scan of one uint32 per thread (blockDim.x multiple of 32, <= 1024) ----
 __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t& total) {
     __shared__ uint32_t warp_sums[32];
