@@ -175,7 +175,8 @@ namespace ngp {
 // A group of G adjacent lanes marches one ray (32 / G rays per warp).  Each round the group
 // speculates on the occupancy of the next G positions of the sequential march and keeps the
 // prefix whose speculation held, so every accepted position is computed by exactly the
-// sequential march's float operations (results are bit-identical to march_count / march_write):
+// sequential march's float operations (results are bit-identical to a one-thread loop that
+// steps by dt on occupied cells and skips empty voxels, as the reference's K7 does):
 //  * run mode (the last position seen was occupied): lane g takes t_g = ((t + dt) + dt) ...
 //    (g sequential additions), i.e. it assumes the lanes before it were occupied.  Lanes before
 //    the first unoccupied lane f are samples; lane f's position decides the skip (or the end).
