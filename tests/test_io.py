@@ -209,3 +209,50 @@ def test_cli_argument_errors(tmp_path, capsys):
         cli.main(["--steps", "0", str(tmp_path)])
     with pytest.raises(SystemExit):
         cli.main([str(tmp_path), "--dataset", str(tmp_path)])
+
+
+# ---- scene-scale sweep (benchmark.cpp) ----------------------------------------------------------
+import scale_sweep
+
+
+def test_sweep_coarse_parsing():
+    assert scale_sweep.parse_coarse("0.5,0.25,1") == [0.25, 0.5, 1.0]
+    for bad in ("1", "0.5,-1", "0.5,,1", "0.5,0.5000001", "a,1"):
+        with pytest.raises(ValueError):
+            scale_sweep.parse_coarse(bad)
+
+
+def test_sweep_refine_candidates():
+    coarse = scale_sweep.parse_coarse(scale_sweep.DEFAULT_COARSE)
+    # interior best: between its neighbours, log-spaced, the best in the middle
+    c = scale_sweep.refine_candidates(coarse, 0.5, 5)
+    lo, hi = 0.3535534, 0.7071068
+    want = [math.exp(math.log(lo) * (1 - t) + math.log(0.5) * t) for t in (0.0, 0.5)] + [0.5] + \
+           [math.exp(math.log(0.5) * (1 - t) + math.log(hi) * t) for t in (0.5, 1.0)]
+    np.testing.assert_allclose(c, want, rtol=1e-12)
+    # edge best: the missing neighbour is extrapolated by the neighbouring ratio
+    c0 = scale_sweep.refine_candidates(coarse, 0.125, 3)
+    np.testing.assert_allclose([c0[0], c0[1], c0[2]], [0.125 / (0.1767767 / 0.125), 0.125, 0.1767767], rtol=1e-12)
+    cn = scale_sweep.refine_candidates(coarse, 4.0, 3)
+    np.testing.assert_allclose([cn[0], cn[2]], [2.8284271, 4.0 * (4.0 / 2.8284271)], rtol=1e-12)
+
+
+def test_sweep_best_and_csv():
+    rows = [{"stage": "coarse", "failed": False, "final_psnr": 30.0, "scene_scale": 0.5},
+            {"stage": "coarse", "failed": False, "final_psnr": 30.04, "scene_scale": 0.25},   # within 0.05 dB, smaller: wins
+            {"stage": "coarse", "failed": True, "final_psnr": 40.0, "scene_scale": 1.0},
+            {"stage": "refine", "failed": False, "final_psnr": 99.0, "scene_scale": 2.0}]
+    assert scale_sweep.best_index(rows, "coarse") == 1
+    r = {"stage": "coarse", "rank": 3, "scene_scale": 0.35355338, "failed": True, "error": 'bad "x"', "final_step": 10, "best_validation_step": 5,
+         "final_psnr": 21.123456789, "final_mse": 0.0077, "best_psnr": 22.0, "best_mse": 0.006, "final_loss": 0.01, "occupancy_ratio": 0.25,
+         "occupied_cells": 524288, "average_samples": 1000, "average_compacted": 500, "train_ms": 1234.5, "validation_ms": 12.0,
+         "steps_per_second": 8.1}
+    assert scale_sweep.csv_row(r) == 'coarse,3,0.353553,failed,"bad ""x""",10,5,21.1235,0.0077,22,0.006,0.01,0.25,524288,1000,500,1234.5,12,8.1'
+    assert scale_sweep.CSV_HEADER.split(",")[0:4] == ["stage", "rank", "scene_scale", "status"]
+
+
+def test_sweep_argument_errors(tmp_path):
+    assert scale_sweep.main(["--dataset", str(tmp_path / "none")]) == 2
+    assert scale_sweep.main(["--dataset", str(tmp_path), "--refine-count", "4"]) == 2
+    assert scale_sweep.main(["--dataset", str(tmp_path), "--coarse-scales", "1"]) == 2
+    assert scale_sweep.main(["--dataset", str(tmp_path)]) == 2  # no marker set

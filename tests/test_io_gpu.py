@@ -70,3 +70,17 @@ def test_weights_roundtrip_through_trainer(tmp_path):
     with pytest.raises(RuntimeError, match="before training"):
         b.load_weights(tmp_path / "w.safetensors")
     b.close()
+
+
+def test_scale_sweep_runs_and_writes_csv(tmp_path):
+    import scale_sweep
+
+    scene = tmp_path / "scene"
+    write_scene(scene, counts=(4, 1, 1), size=48)
+    out = tmp_path / "sweep.csv"
+    rc = scale_sweep.main(["--dataset", str(scene), "--steps", "20", "--chunk-steps", "10", "--validation-interval", "10",
+                           "--coarse-scales", "0.25,0.33", "--refine-count", "3", "--output-csv", str(out)])
+    lines = out.read_text().splitlines()
+    assert lines[0] == scale_sweep.CSV_HEADER
+    assert [ln.split(",")[0] for ln in lines[1:]] == ["coarse", "coarse", "refine", "refine", "refine"]
+    assert rc == 0 and all(",ok," in ln for ln in lines[1:])
