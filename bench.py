@@ -233,7 +233,9 @@ def bench_train_ours(args, rank, world, local):
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         clocks.wait_first()
+        launches0 = ngp.kernel_launch_count()
         stats = model.train(args.steps)
+        launches = ngp.kernel_launch_count() - launches0
         time.sleep(0.25)
     torch.cuda.synchronize()
     barrier(world)
@@ -287,16 +289,10 @@ def bench_train_ours(args, rank, world, local):
         "gpu_launches": None,
         "clocks": clocks.summary(),
     }
-    res["gpu_launches"] = res_launch_count(phases, args.steps)
+    res["gpu_launches"] = launches
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_train(args)
     return res
-
-
-def res_launch_count(phases, steps):
-    # kernels of one steady-state step: march 3, encode 1, mlp fwd 1, loss 3 (+memset), pad 1,
-    # encode 1, mlp bwd 2, encode bwd 1, adam 1; grid update (every 16 steps) 6
-    return int(steps * 14 + steps // 16 * 6)
 
 
 def cpu_baseline_train(args, budget_s: float = 15.0) -> dict:
@@ -575,6 +571,40 @@ def bench_encode_reference(args, rank, world, local):
 # ------------------------------------------------------------------------------------------------
 # render workload (config 4): large table, novel 1920x1080 views partitioned across ranks
 # ------------------------------------------------------------------------------------------------
+def render_encode_roofline(ngp, workloads, peaks, n: int = 1 << 22) -> dict:
+    """Config 4's encode HBM rate: the encoding forward over the config-4 table (log2 T = 22,
+    finest resolution 4096; larger than L2) on n uniformly random points, the gather pattern with
+    the least reuse, timed with CUDA events after an L2 flush."""
+    import torch
+
+    layout = ngp.grid_layout(16, 2, 22, 16, math.log2(4096.0 / 16.0) / 15.0)
+    coords_h, table_h, _ = workloads.encode_inputs(n, layout.n_params, 16, 2, seed=77)
+    coords = torch.from_numpy(coords_h).cuda()
+    table = torch.from_numpy(table_h.view(np.int16)).cuda()
+    feats = torch.empty((32, n), dtype=torch.float16, device="cuda")
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    times = []
+    for k in range(8):
+        flush_buf.fill_(1.0)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        ngp.encode_grid_forward(layout, coords, table, feats, stream=stream)
+        e.record(stream)
+        e.synchronize()
+        if k >= 3:
+            times.append(s.elapsed_time(e))
+    t_ms = statistics.median(times)
+    per_point = 12 + 64 + 16 * 8 * 4  # coordinates, features out, 8 corners x 16 levels x 2 fp16
+    achieved = per_point * n / (t_ms * 1e-3) / 1e9
+    return {"kernel": "encode_forward_points_kernel (config-4 table)", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+            "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"] + " (HBM copy bandwidth)",
+            "per_unit": f"{per_point} algorithmic bytes per point (table bytes gathered, counted once), {n} random points per launch, "
+                        f"{t_ms * 1e3:.1f} us per launch",
+            "table_MB": round(layout.n_params * 2 / 1e6, 1),
+            "note": "the coarse levels of the table stay L2-resident; the finer hashed levels miss L2 and are read from HBM"}
+
+
 def bench_render_ours(args, rank, world, local):
     import torch
     import ngp_b200 as ngp
@@ -596,11 +626,13 @@ def bench_render_ours(args, rank, world, local):
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         clocks.wait_first()
+        launches0 = ngp.kernel_launch_count()
         s.record()
         for v in views:
             model.render(v, w, h, poses["focal"], poses["principal"], out=out)
         e.record()
         e.synchronize()
+        launches = ngp.kernel_launch_count() - launches0
         time.sleep(0.25)
     barrier(world)
     ms = max_over_ranks(s.elapsed_time(e), world)
@@ -617,6 +649,7 @@ def bench_render_ours(args, rank, world, local):
     e2.synchronize()
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / n_e2e, world)
     model.close()
+    roofline = render_encode_roofline(ngp, workloads, peaks)
     rays = w * h
     value = world * rays * args.steps / (ms * 1e-3)
     return {
@@ -628,7 +661,7 @@ def bench_render_ours(args, rank, world, local):
                    "l2": "table 268 MB fp16 > L2; no flush"},
         "e2e": {"value": round(world * rays / (e2e_ms * 1e-3), 1), "unit": "rays/s", "h2d_bytes_per_step": 48,
                 "d2h_bytes_per_step": rays * 12, "note": "InstantNGP.render per view with the image read back to pinned host memory"},
-        "gpu_launches": None, "clocks": clocks.summary(), "roofline": None,
+        "gpu_launches": launches, "clocks": clocks.summary(), "roofline": roofline,
     }
 
 

@@ -48,6 +48,9 @@ extern "C" {
 NGP_API const char* ngp_last_error(void);
 /* Library version string. */
 NGP_API const char* ngp_version(void);
+/* Kernel launches made by this library in this process so far, all threads and devices
+ * (diagnostics for benchmarks; no counterpart in the reference). */
+NGP_API uint64_t ngp_kernel_launch_count(void);
 
 /* ------------------------------------------------------------------------------------------
  * Multiresolution hash-grid layout.
@@ -220,6 +223,25 @@ NGP_API int ngp_march_training_rays(const float* camera, uint32_t frame_count, u
 NGP_API int ngp_march_rays(uint32_t n_rays, const float* rays, int jitter, uint32_t step, const uint8_t* bitfield, uint32_t sample_limit,
                            float* coords, uint32_t* numsteps, uint32_t* scratch, uint32_t* sample_counter, void* stream);
 
+/* Segmented marching of evaluation rays: the reference marches every occupied step of a pixel
+ * ray (up to 1024) before compositing, although compositing stops once the transmittance falls
+ * below 1e-4.  This marches at most `cap` further samples of each listed ray (list NULL: entry k
+ * is ray k of `rays`), continuing each ray where the previous segment stopped, so a ray that
+ * stops early is never marched past its first segment; the samples of a ray over all its
+ * segments are those of ngp_march_rays (jitter 0), bit for bit.
+ *   max_entries / n_entries: entry count (n_entries, optional, on the device, <= max_entries);
+ *   t_state, marched: per ray, where it continues and how many samples it has had (both NULL for
+ *     the first segment, which must fit: cap * max_entries <= sample_limit);
+ *   numsteps[2k], numsteps[2k+1]: entry k's samples in this segment and their first record;
+ *   t_out[k]: where entry k's ray continues, -1 if its march has ended;
+ *   counters[0] = the segment's samples before the limit, counters[1] = entries [0, n) that fit
+ *     under sample_limit (a prefix; the rest were not marched and have numsteps 0);
+ *   scratch: ngp_march_scratch_words(max_entries) words.
+ * Replaces generate_evaluation_samples_kernel (ngp.train.cu:580-667) in the render loop. */
+NGP_API int ngp_march_rays_segment(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* list, const float* rays,
+                                   const uint8_t* bitfield, const float* t_state, const uint32_t* marched, uint32_t cap, uint32_t sample_limit,
+                                   float* coords, uint32_t* numsteps, float* t_out, uint32_t* scratch, uint32_t* counters, void* stream);
+
 /* Pixel rays [n][6] (origin, unit direction) of pixels [pixel_offset, pixel_offset + n) of image
  * `image`.  Replaces the ray set-up of generate_evaluation_samples_kernel (ngp.train.cu:587-614). */
 NGP_API int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,
@@ -343,6 +365,20 @@ NGP_API int ngp_pad_training_batch_enc(const uint32_t* compacted_counter, float*
  * count / 2^18.  Replaces K12/K13 (ngp.train.cu:862-874, 1946-1956). */
 NGP_API int ngp_pad_training_batch(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, void* stream);
 
+/* Compositing of one segment of a segmented march (ngp_march_rays_segment, same list, numsteps,
+ * t_out and counters + 1 as `complete`): each marched entry continues its ray's state
+ * (state [ray][4] = T, r, g, b, 16-byte aligned; t_state; marched) over the segment's network
+ * outputs.  A ray whose transmittance fell below 1e-4 or whose march ended writes its pixel
+ * (pixel_offset + ray) exactly as ngp_eval_composite does; the other rays, and the entries past
+ * the segment's sample limit, are appended to next_list (*next_count, cleared by the caller) in
+ * no fixed order.  The first segment (list NULL) starts every ray at T = 1.
+ * Replaces accumulate_evaluation_loss_kernel (ngp.train.cu:676-745) in the render loop. */
+NGP_API int ngp_eval_composite_segment(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* complete, const uint32_t* list,
+                                       const uint32_t* numsteps, const float* coords, const uint16_t* network_output, const float* t_out,
+                                       float* t_state, uint32_t* marched, float* state, uint32_t* next_list, uint32_t* next_count,
+                                       uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels, double* sse,
+                                       uint8_t* comparison, float* rendered, void* stream);
+
 /* Evaluation compositing of n_pixels pixels: *sse += squared error vs the sRGB target (fp64; no
  * target when pixels is NULL), optional comparison image [height][2*width][3] (target | render)
  * and rendered [pixel][3].  Replaces accumulate_evaluation_loss_kernel (ngp.train.cu:676-745). */
@@ -433,6 +469,11 @@ NGP_API int ngp_trainer_evaluate(ngp_trainer* t, int split, uint32_t image_begin
 /* Render a novel view (camera: 12 floats, host) into rgb_device [height*width][3] (fp32, [0,1]). */
 NGP_API int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint32_t width, uint32_t height, float fx, float fy, float cx,
                                float cy, float* rgb_device);
+/* Evaluation and rendering by segmented marching (enabled != 0, the default: rays are marched a
+ * segment at a time and no further than their transmittance lasts) or, as the reference does,
+ * by marching every occupied step of each tile before the network runs (0).  Both give the same
+ * images bit for bit.  run_evaluation (ngp.train.cu:1597-1658). */
+NGP_API int ngp_trainer_set_segmented_eval(ngp_trainer* t, int enabled);
 NGP_API uint32_t ngp_trainer_param_count(const ngp_trainer* t);
 /* fp32 master parameters [MLP | grid] to / from the host (export_weights / load_weights;
  * loading resets the optimizer and is allowed only before training, ngp.train.cpp:312). */

@@ -21,7 +21,11 @@ inline int fail(int code, const std::string& message) {
     return code;
 }
 
+void count_launch();
+
+// Called once after every kernel launch of the library (also counts it).
 inline int check_launch(const char* what) {
+    count_launch();
     const cudaError_t status = cudaGetLastError();
     if (status != cudaSuccess) return fail(NGP_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(status));
     return NGP_OK;

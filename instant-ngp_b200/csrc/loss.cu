@@ -651,54 +651,58 @@ __global__ void pad_batch_kernel(const uint32_t* __restrict__ count, float* __re
         dloss[static_cast<uint64_t>(r) * 16u + q] = __float2half(__half2float(dloss[static_cast<uint64_t>(src) * 16u + q]) * s);
 }
 
-// Evaluation compositing (K10, ngp.train.cu:676-745) for a set of pixels of one image: clamp to
-// [0,1], squared error against the sRGB target (fp64 block sums), optional side-by-side
-// comparison pixels (target left, render right) and rendered colours.
-__global__ void __launch_bounds__(kThreads) eval_composite_kernel(uint32_t n_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width,
-                                                                  uint32_t height, const uint8_t* __restrict__ pixels,
-                                                                  const uint32_t* __restrict__ numsteps, const float* __restrict__ coords,
-                                                                  const __half* __restrict__ network_output, double* __restrict__ sse,
-                                                                  uint8_t* __restrict__ comparison, float* __restrict__ rendered) {
-    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
-    double se        = 0.0;
-    if (i < n_pixels) {
-        const uint32_t gp = pixel_offset + i, px = gp % width, py = gp / width;
-        const uint32_t steps = numsteps[2u * i], base = numsteps[2u * i + 1u];
-        float T    = 1.0f;
-        float3 rgb = {0.0f, 0.0f, 0.0f};
-        for (uint32_t j = 0; j < steps; ++j) {
-            float r, g, b, d;
-            load_output(network_output + (static_cast<uint64_t>(base) + j) * 16u, r, g, b, d);
-            const float alpha  = 1.0f - __expf(-expf(d) * coords[(static_cast<uint64_t>(base) + j) * 7u + 3u]);
-            const float weight = alpha * T;
-            rgb.x              = __fmaf_rn(weight, sigmoidf_(r), rgb.x);
-            rgb.y              = __fmaf_rn(weight, sigmoidf_(g), rgb.y);
-            rgb.z              = __fmaf_rn(weight, sigmoidf_(b), rgb.z);
-            T *= 1.0f - alpha;
-            if (T < kTransmittanceEps) break;
-        }
-        const float3 pr = {fminf(fmaxf(rgb.x, 0.0f), 1.0f), fminf(fmaxf(rgb.y, 0.0f), 1.0f), fminf(fmaxf(rgb.z, 0.0f), 1.0f)};
-        if (pixels != nullptr) {
-            const float4 tx = read_texel(px, py, image, width, height, pixels);
-            const float3 tg = {fminf(fmaxf(linear_to_srgb_c(tx.x), 0.0f), 1.0f), fminf(fmaxf(linear_to_srgb_c(tx.y), 0.0f), 1.0f),
-                               fminf(fmaxf(linear_to_srgb_c(tx.z), 0.0f), 1.0f)};
-            const double dr = static_cast<double>(pr.x) - tg.x, dg = static_cast<double>(pr.y) - tg.y, db = static_cast<double>(pr.z) - tg.z;
-            se              = dr * dr + dg * dg + db * db;
-            if (comparison != nullptr) {
-                const uint64_t row = static_cast<uint64_t>(py) * width * 6u;
-                uint8_t* t         = comparison + row + px * 3u;
-                uint8_t* q         = comparison + row + (static_cast<uint64_t>(width) + px) * 3u;
-                t[0] = static_cast<uint8_t>(tg.x * 255.0f + 0.5f), t[1] = static_cast<uint8_t>(tg.y * 255.0f + 0.5f),
-                t[2] = static_cast<uint8_t>(tg.z * 255.0f + 0.5f);
-                q[0] = static_cast<uint8_t>(pr.x * 255.0f + 0.5f), q[1] = static_cast<uint8_t>(pr.y * 255.0f + 0.5f),
-                q[2] = static_cast<uint8_t>(pr.z * 255.0f + 0.5f);
-            }
-        }
-        if (rendered != nullptr) {
-            float* o = rendered + static_cast<uint64_t>(gp) * 3u;
-            o[0] = pr.x, o[1] = pr.y, o[2] = pr.z;
+// Final colour of one evaluation pixel (K10's epilogue, ngp.train.cu:715-745): clamp to [0,1],
+// squared error against the sRGB target (returned), optional side-by-side comparison pixels
+// (target left, render right) and rendered colour.
+__device__ __forceinline__ double eval_pixel_out(uint32_t gp, float3 rgb, uint32_t image, uint32_t width, uint32_t height,
+                                                 const uint8_t* __restrict__ pixels, uint8_t* __restrict__ comparison,
+                                                 float* __restrict__ rendered) {
+    const uint32_t px = gp % width, py = gp / width;
+    double se         = 0.0;
+    const float3 pr   = {fminf(fmaxf(rgb.x, 0.0f), 1.0f), fminf(fmaxf(rgb.y, 0.0f), 1.0f), fminf(fmaxf(rgb.z, 0.0f), 1.0f)};
+    if (pixels != nullptr) {
+        const float4 tx = read_texel(px, py, image, width, height, pixels);
+        const float3 tg = {fminf(fmaxf(linear_to_srgb_c(tx.x), 0.0f), 1.0f), fminf(fmaxf(linear_to_srgb_c(tx.y), 0.0f), 1.0f),
+                           fminf(fmaxf(linear_to_srgb_c(tx.z), 0.0f), 1.0f)};
+        const double dr = static_cast<double>(pr.x) - tg.x, dg = static_cast<double>(pr.y) - tg.y, db = static_cast<double>(pr.z) - tg.z;
+        se              = dr * dr + dg * dg + db * db;
+        if (comparison != nullptr) {
+            const uint64_t row = static_cast<uint64_t>(py) * width * 6u;
+            uint8_t* t         = comparison + row + px * 3u;
+            uint8_t* q         = comparison + row + (static_cast<uint64_t>(width) + px) * 3u;
+            t[0] = static_cast<uint8_t>(tg.x * 255.0f + 0.5f), t[1] = static_cast<uint8_t>(tg.y * 255.0f + 0.5f),
+            t[2] = static_cast<uint8_t>(tg.z * 255.0f + 0.5f);
+            q[0] = static_cast<uint8_t>(pr.x * 255.0f + 0.5f), q[1] = static_cast<uint8_t>(pr.y * 255.0f + 0.5f),
+            q[2] = static_cast<uint8_t>(pr.z * 255.0f + 0.5f);
         }
     }
+    if (rendered != nullptr) {
+        float* o = rendered + static_cast<uint64_t>(gp) * 3u;
+        o[0] = pr.x, o[1] = pr.y, o[2] = pr.z;
+    }
+    return se;
+}
+
+// Front-to-back compositing of samples [base, base + steps) onto (T, rgb), stopping once the
+// transmittance falls below 1e-4 (K10's loop, ngp.train.cu:690-713).  Returns true if it stopped.
+__device__ __forceinline__ bool composite_samples(uint32_t base, uint32_t steps, const float* __restrict__ coords,
+                                                  const __half* __restrict__ network_output, float& T, float3& rgb) {
+    for (uint32_t j = 0; j < steps; ++j) {
+        float r, g, b, d;
+        load_output(network_output + (static_cast<uint64_t>(base) + j) * 16u, r, g, b, d);
+        const float alpha  = 1.0f - __expf(-expf(d) * coords[(static_cast<uint64_t>(base) + j) * 7u + 3u]);
+        const float weight = alpha * T;
+        rgb.x              = __fmaf_rn(weight, sigmoidf_(r), rgb.x);
+        rgb.y              = __fmaf_rn(weight, sigmoidf_(g), rgb.y);
+        rgb.z              = __fmaf_rn(weight, sigmoidf_(b), rgb.z);
+        T *= 1.0f - alpha;
+        if (T < kTransmittanceEps) return true;
+    }
+    return false;
+}
+
+// Block sum of the per-thread squared errors, one fp64 atomic per CTA.
+__device__ __forceinline__ void add_block_sse(double se, double* __restrict__ sse) {
 #pragma unroll
     for (uint32_t o = 16; o > 0; o >>= 1) se += __shfl_down_sync(0xFFFFFFFFu, se, o);
     __shared__ double ws[kThreads / 32];
@@ -709,6 +713,95 @@ __global__ void __launch_bounds__(kThreads) eval_composite_kernel(uint32_t n_pix
         for (uint32_t w = 0; w < kThreads / 32; ++w) tot += ws[w];
         atomicAdd(sse, tot);
     }
+}
+
+// Evaluation compositing (K10, ngp.train.cu:676-745) for a set of pixels of one image.
+__global__ void __launch_bounds__(kThreads) eval_composite_kernel(uint32_t n_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width,
+                                                                  uint32_t height, const uint8_t* __restrict__ pixels,
+                                                                  const uint32_t* __restrict__ numsteps, const float* __restrict__ coords,
+                                                                  const __half* __restrict__ network_output, double* __restrict__ sse,
+                                                                  uint8_t* __restrict__ comparison, float* __restrict__ rendered) {
+    const uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+    double se        = 0.0;
+    if (i < n_pixels) {
+        float T    = 1.0f;
+        float3 rgb = {0.0f, 0.0f, 0.0f};
+        composite_samples(numsteps[2u * i + 1u], numsteps[2u * i], coords, network_output, T, rgb);
+        se = eval_pixel_out(pixel_offset + i, rgb, image, width, height, pixels, comparison, rendered);
+    }
+    add_block_sse(se, sse);
+}
+
+// Segmented evaluation compositing: entry k (ray list[k]) of a segmented march continues its
+// ray's compositing state (T, rgb) over the segment's samples -- the same sequence of float
+// operations as one pass over all samples.  A ray whose transmittance fell below 1e-4, or whose
+// march ended, writes its pixel; the others keep their state and are listed for the next
+// segment, as are the entries past the segment's sample limit (not marched).
+struct SegCompositeParams {
+    uint32_t max_entries;
+    const uint32_t* n_entries;  // device entry count (null: max_entries)
+    const uint32_t* complete;   // entries [0, *complete) were marched
+    const uint32_t* list;       // null: entry k is ray k (first segment)
+    const uint32_t* numsteps;
+    const float* coords;
+    const __half* output;
+    const float* t_out;
+    float* t_state;
+    uint32_t* marched;
+    float4* state;              // [ray] (T, r, g, b)
+    int first;
+    uint32_t* next_list;
+    uint32_t* next_count;
+    uint32_t pixel_offset, image, width, height;
+    const uint8_t* pixels;
+    double* sse;
+    uint8_t* comparison;
+    float* rendered;
+};
+
+__global__ void __launch_bounds__(kThreads) seg_composite_kernel(const __grid_constant__ SegCompositeParams p) {
+    const uint32_t k = blockIdx.x * kThreads + threadIdx.x;
+    const uint32_t n = p.n_entries != nullptr ? min(*p.n_entries, p.max_entries) : p.max_entries;
+    double se        = 0.0;
+    bool carry       = false;
+    uint32_t i       = 0;
+    if (k < n) {
+        i = p.list != nullptr ? p.list[k] : k;
+        if (k < *p.complete) {
+            float T    = 1.0f;
+            float3 rgb = {0.0f, 0.0f, 0.0f};
+            uint32_t done = 0;
+            if (!p.first) {
+                const float4 st = p.state[i];
+                T = st.x, rgb = {st.y, st.z, st.w};
+                done = p.marched[i];
+            }
+            const uint32_t steps = p.numsteps[2u * k];
+            const bool stopped   = composite_samples(p.numsteps[2u * k + 1u], steps, p.coords, p.output, T, rgb);
+            const float t_next   = p.t_out[k];
+            if (stopped || t_next < 0.0f) {
+                se = eval_pixel_out(p.pixel_offset + i, rgb, p.image, p.width, p.height, p.pixels, p.comparison, p.rendered);
+            } else {
+                p.state[i]   = make_float4(T, rgb.x, rgb.y, rgb.z);
+                p.t_state[i] = t_next;
+                p.marched[i] = done + steps;
+                carry        = true;
+            }
+        } else {
+            carry = true;  // not marched in this segment: unchanged
+        }
+    }
+    // warp-aggregated append of the carried rays
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t bal  = __ballot_sync(0xFFFFFFFFu, carry);
+    uint32_t slot       = 0;
+    if (bal != 0u) {
+        const uint32_t leader = static_cast<uint32_t>(__ffs(bal)) - 1u;
+        if (lane == leader) slot = atomicAdd(p.next_count, static_cast<uint32_t>(__popc(bal)));
+        slot = __shfl_sync(0xFFFFFFFFu, slot, leader);
+        if (carry) p.next_list[slot + __popc(bal & ((1u << lane) - 1u))] = i;
+    }
+    add_block_sse(se, p.sse);
 }
 
 constexpr size_t loss_scratch_size(uint32_t max_rays) {
@@ -1034,6 +1127,44 @@ extern "C" int ngp_pad_training_batch_enc(const uint32_t* compacted_counter, flo
     pad_batch_kernel<<<kNetworkBatch / 256u, 256, 0, as_stream(stream)>>>(compacted_counter, compacted_coords, reinterpret_cast<__half*>(dloss_doutput),
                                                                             kNetworkBatch, reinterpret_cast<__half*>(enc), enc_stride);
     return check_launch("pad_batch_kernel");
+}
+
+extern "C" int ngp_eval_composite_segment(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* complete, const uint32_t* list,
+                                          const uint32_t* numsteps, const float* coords, const uint16_t* network_output, const float* t_out,
+                                          float* t_state, uint32_t* marched, float* state, uint32_t* next_list, uint32_t* next_count,
+                                          uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels, double* sse,
+                                          uint8_t* comparison, float* rendered, void* stream) {
+    clear_error();
+    if (max_entries == 0) return NGP_OK;
+    if (complete == nullptr || numsteps == nullptr || coords == nullptr || network_output == nullptr || t_out == nullptr || t_state == nullptr ||
+        marched == nullptr || state == nullptr || next_list == nullptr || next_count == nullptr || width == 0 || height == 0)
+        return fail(NGP_ERR_INVALID, "segment composite: invalid input");
+    if (reinterpret_cast<uintptr_t>(state) % 16u != 0) return fail(NGP_ERR_INVALID, "segment composite: state must be 16-byte aligned");
+    SegCompositeParams p{};
+    p.max_entries  = max_entries;
+    p.n_entries    = n_entries;
+    p.complete     = complete;
+    p.list         = list;
+    p.numsteps     = numsteps;
+    p.coords       = coords;
+    p.output       = reinterpret_cast<const __half*>(network_output);
+    p.t_out        = t_out;
+    p.t_state      = t_state;
+    p.marched      = marched;
+    p.state        = reinterpret_cast<float4*>(state);
+    p.first        = list == nullptr ? 1 : 0;
+    p.next_list    = next_list;
+    p.next_count   = next_count;
+    p.pixel_offset = pixel_offset;
+    p.image        = image;
+    p.width        = width;
+    p.height       = height;
+    p.pixels       = pixels;
+    p.sse          = sse;
+    p.comparison   = comparison;
+    p.rendered     = rendered;
+    seg_composite_kernel<<<(max_entries + kThreads - 1) / kThreads, kThreads, 0, as_stream(stream)>>>(p);
+    return check_launch("seg_composite_kernel");
 }
 
 extern "C" int ngp_eval_composite(uint32_t n_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,

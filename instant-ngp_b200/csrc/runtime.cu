@@ -1,4 +1,5 @@
 // Library runtime: per-thread error state, device queries and the hash-grid layout.
+#include <atomic>
 #include <cmath>
 #include <limits>
 
@@ -10,6 +11,8 @@ namespace {
 thread_local std::string g_last_error;
 }
 
+std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 void set_error(const std::string& message) { g_last_error = message; }
 void clear_error() { g_last_error.clear(); }
 
@@ -28,6 +31,8 @@ int sm_count() {
 using namespace ngp;
 
 extern "C" const char* ngp_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" uint64_t ngp_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char* ngp_version(void) { return "ngp_b200 0.1 (sm_100a)"; }
 

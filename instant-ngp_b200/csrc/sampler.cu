@@ -186,6 +186,13 @@ struct MarchParams {
     uint32_t sample_limit;
     uint32_t* ray_counter;
     uint32_t* sample_counter;     // total samples before the limit
+    // segmented marching (rendering); unused by the other marches
+    const uint32_t* list;         // entry k marches ray list[k] (null: ray k)
+    const float* t_state;         // [ray] where the ray continues (null: from its start)
+    const uint32_t* marched;      // [ray] samples marched before this call (null: 0)
+    uint32_t cap;                 // samples per ray in this call
+    float* t_out;                 // [entry] where the ray continues after this call, -1 = ended
+    uint32_t* complete;           // entries [0, *complete) fitted into the sample limit
 };
 
 __device__ __forceinline__ uint32_t march_ray_count(const MarchParams& p) { return p.n_rays_dev != nullptr ? min(*p.n_rays_dev, p.n_rays) : p.n_rays; }
@@ -291,6 +298,81 @@ __global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_c
     group_march_write(r.origin, r.dir, r.start_t, overflow ? kept : 0u, p.bits, out);
 }
 
+// Segmented marching of evaluation rays: each call marches at most `cap` further samples of the
+// listed rays, continuing where the previous call stopped (see group_march_count_runs_seg).  The
+// write pass keeps the entries whose samples fit under the sample limit -- a prefix of the list,
+// since bases grow with the entry -- and reports its length in *complete; the first entry that
+// does not fit is the one whose samples cross the limit.
+__device__ __forceinline__ bool seg_ray(const MarchParams& p, uint32_t k, uint32_t n, uint32_t& i, TrainRay& r, uint32_t& limit, bool& final_limit) {
+    if (k >= n) return false;
+    i                    = p.list != nullptr ? p.list[k] : k;
+    const uint32_t done  = p.marched != nullptr ? p.marched[i] : 0u;
+    const uint32_t left  = kMarchSteps - min(done, kMarchSteps);
+    limit                = min(p.cap, left);
+    final_limit          = limit == left;
+    if (!setup_ray(p, i, 0u, r)) return false;
+    if (p.t_state != nullptr) r.start_t = p.t_state[i];
+    return true;
+}
+
+__global__ void __launch_bounds__(kCtaThreads) seg_march_count_kernel(const __grid_constant__ MarchParams p) {
+    __shared__ uint32_t s_steps[kRaysPerCta];
+    const uint32_t n    = march_ray_count(p);
+    const uint32_t slot = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
+    const uint32_t k    = blockIdx.x * kRaysPerCta + slot;
+    TrainRay r{};
+    uint32_t i = 0, limit = 0;
+    bool final_limit  = true;
+    const bool active = seg_ray(p, k, n, i, r, limit, final_limit);
+    uint32_t n_runs;
+    float t_after;
+    const uint32_t steps = group_march_count_runs_seg(r.origin, r.dir, r.start_t, active, p.bits, limit, final_limit,
+                                                      p.runs + static_cast<uint64_t>(k) * kMaxRuns, n_runs, t_after);
+    if (k < n && g == 0) {
+        p.numsteps[2u * k]      = steps;
+        p.numsteps[2u * k + 1u] = n_runs;
+        p.t_out[k]              = t_after;
+    }
+    if (g == 0) s_steps[slot] = steps;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        uint32_t total = 0;
+        for (uint32_t w = threadIdx.x; w < kRaysPerCta; w += 32) total += s_steps[w];
+#pragma unroll
+        for (uint32_t o = 16; o > 0; o >>= 1) total += __shfl_down_sync(0xFFFFFFFFu, total, o);
+        if (threadIdx.x == 0) p.block_totals[blockIdx.x] = total;
+    }
+}
+
+__global__ void __launch_bounds__(kCtaThreads) seg_march_write_kernel(const __grid_constant__ MarchParams p) {
+    __shared__ uint32_t s_base[kRaysPerCta];
+    const uint32_t n      = march_ray_count(p);
+    const uint32_t slot   = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
+    const uint32_t k      = blockIdx.x * kRaysPerCta + slot;
+    const uint32_t steps  = k < n ? p.numsteps[2u * k] : 0u;
+    const uint32_t n_runs = k < n ? p.numsteps[2u * k + 1u] : 0u;
+    uint32_t total;
+    const uint32_t ex = block_exclusive_scan(g == 0 ? steps : 0u, total);
+    if (g == 0) s_base[slot] = ex;
+    __syncthreads();
+    const uint32_t base = p.block_totals[blockIdx.x] + s_base[slot];
+    const bool fits     = base + steps <= p.sample_limit;
+    const uint32_t kept = (k < n && fits) ? steps : 0u;
+    if (k < n && g == 0) {
+        p.numsteps[2u * k]      = kept;
+        p.numsteps[2u * k + 1u] = kept ? base : 0u;
+        if (!fits && base <= p.sample_limit) *p.complete = k;  // the one entry that crosses the limit
+    }
+    TrainRay r{};
+    uint32_t i = 0, limit = 0;
+    bool final_limit = true;
+    if (kept > 0) seg_ray(p, k, n, i, r, limit, final_limit);
+    float* out          = p.coords + static_cast<uint64_t>(base) * 7u;
+    const bool overflow = n_runs == kRunsOverflow;
+    group_expand_runs(r.dir, r.origin, p.runs + static_cast<uint64_t>(k) * kMaxRuns, n_runs, kept, !overflow, out);
+    group_march_write(r.origin, r.dir, r.start_t, overflow ? kept : 0u, p.bits, out);
+}
+
 // Evaluation pixel rays (ngp.train.cu:587-614): pixel centre through the pinhole camera,
 // normalised direction.  A degenerate ray gets a NaN origin, which yields no samples.
 __global__ void eval_rays_kernel(const CameraSet cam, uint32_t image, uint32_t pixel_offset, uint32_t n, float* __restrict__ rays) {
@@ -328,6 +410,19 @@ int launch_march(MarchParams p, uint32_t* scratch, cudaStream_t s) {
     NGP_TRY(check_launch("scan_totals_kernel"));
     march_write_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
     return check_launch("march_write_kernel");
+}
+
+int launch_seg_march(MarchParams p, uint32_t* scratch, cudaStream_t s) {
+    const uint32_t blocks = march_blocks(p.n_rays);
+    p.block_totals        = scratch;
+    p.runs                = reinterpret_cast<uint2*>(scratch + ((blocks + 1u) & ~1u));
+    seg_march_count_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
+    NGP_TRY(check_launch("seg_march_count_kernel"));
+    // totals, and *complete = the entry count until an entry crosses the limit
+    scan_totals_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, p.n_rays_dev, p.n_rays, p.sample_counter, p.complete);
+    NGP_TRY(check_launch("scan_totals_kernel"));
+    seg_march_write_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
+    return check_launch("seg_march_write_kernel");
 }
 
 CameraSet camera_set(const float* camera, uint32_t frame_count, uint32_t width, uint32_t height, float fx, float fy, float cx, float cy) {
@@ -430,6 +525,36 @@ extern "C" int ngp_march_rays(uint32_t n_rays, const float* rays, int jitter, ui
     p.sample_limit   = sample_limit;
     p.sample_counter = sample_counter;
     return launch_march(p, scratch, as_stream(stream));
+}
+
+extern "C" int ngp_march_rays_segment(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* list, const float* rays,
+                                      const uint8_t* bitfield, const float* t_state, const uint32_t* marched, uint32_t cap, uint32_t sample_limit,
+                                      float* coords, uint32_t* numsteps, float* t_out, uint32_t* scratch, uint32_t* counters, void* stream) {
+    clear_error();
+    if (max_entries == 0) return NGP_OK;
+    if (rays == nullptr || bitfield == nullptr || coords == nullptr || numsteps == nullptr || t_out == nullptr || scratch == nullptr ||
+        counters == nullptr || sample_limit == 0 || cap == 0 || (t_state == nullptr) != (marched == nullptr))
+        return fail(NGP_ERR_INVALID, "segment march: invalid input");
+    // the first segment starts every ray: all of it must fit (later segments keep what does not)
+    if (t_state == nullptr && static_cast<uint64_t>(cap) * max_entries > sample_limit)
+        return fail(NGP_ERR_INVALID, "segment march: the first segment (cap x rays) must fit the sample limit");
+    MarchParams p{};
+    p.n_rays         = max_entries;
+    p.n_rays_dev     = n_entries;
+    p.rays_in        = rays;
+    p.jitter         = 0;
+    p.bits           = bitfield;
+    p.numsteps       = numsteps;
+    p.coords         = coords;
+    p.sample_limit   = sample_limit;
+    p.sample_counter = counters;
+    p.complete       = counters + 1;
+    p.list           = list;
+    p.t_state        = t_state;
+    p.marched        = marched;
+    p.cap            = cap;
+    p.t_out          = t_out;
+    return launch_seg_march(p, scratch, as_stream(stream));
 }
 
 extern "C" int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,

@@ -212,6 +212,7 @@ struct MarchRound {
     bool emit;       // this lane's position is an emitted sample ...
     uint32_t slot;   // ... the slot-th of this round
     float3 pos;      // this lane's position
+    float t;         // this lane's t
     bool cont;       // the next round's first position directly follows the last emitted sample
 };
 
@@ -230,6 +231,7 @@ __device__ __forceinline__ MarchRound group_march_round(GroupMarch& m, const uin
     }
     MarchRound r;
     r.pos                = ray_point(m.o, m.d, tk);
+    r.t                  = tk;
     const bool ins       = !m.done && inside_unit_cube(r.pos);
     const bool oc        = ins && occupied(r.pos, bits);
     const bool stop_here = skip_mode ? (!ins || oc) : !oc;
@@ -322,6 +324,46 @@ __device__ __forceinline__ uint32_t group_march_count_runs(float3 o, float3 d, f
         }
     }
     if (n_runs > kMaxRuns) n_runs = kRunsOverflow;
+    return m.n;
+}
+
+// Segmented marching (rendering): the same count pass with a per-call sample limit, which also
+// returns where the sequential march would continue.  After a sample at t the sequential march
+// evaluates t + dt next, so a march started at `t_after` in run mode continues the sequence
+// exactly.  `t_after` is -1 when the ray has ended (it left the grid, or `limit` was the ray's
+// remaining step allowance) and nothing follows.
+__device__ __forceinline__ uint32_t group_march_count_runs_seg(float3 o, float3 d, float start_t, bool active, const uint8_t* __restrict__ bits,
+                                                               uint32_t limit, bool limit_is_final, uint2* __restrict__ runs, uint32_t& n_runs,
+                                                               float& t_after) {
+    const uint32_t lane     = threadIdx.x & 31u;
+    const uint32_t g        = lane % kMarchGroup;
+    const uint32_t group_lo = lane - g;
+    GroupMarch m;
+    group_march_begin(m, o, d, start_t, active && limit > 0);
+    float run_t0   = 0.0f;
+    uint32_t run_n = 0;
+    float t_last   = 0.0f;
+    n_runs         = 0;
+    while (__any_sync(0xFFFFFFFFu, !m.done)) {
+        const MarchRound r = group_march_round(m, bits, limit);
+        // t of the round's last emitted sample, from the lane that emitted it
+        const bool is_last  = r.emit && r.slot + 1u == r.k;
+        const uint32_t lb   = (__ballot_sync(0xFFFFFFFFu, is_last) >> group_lo) & ((1u << kMarchGroup) - 1u);
+        const float t_emit  = __shfl_sync(0xFFFFFFFFu, r.t, group_lo + (lb ? static_cast<uint32_t>(__ffs(lb)) - 1u : 0u));
+        if (r.k > 0) {
+            t_last = t_emit;
+            if (run_n == 0) run_t0 = r.first_t;
+            run_n += r.k;
+        }
+        if (!r.cont && run_n > 0) {
+            if (n_runs < kMaxRuns && g == 0) runs[n_runs] = make_uint2(__float_as_uint(run_t0), run_n);
+            ++n_runs;
+            run_n = 0;
+        }
+    }
+    if (n_runs > kMaxRuns) n_runs = kRunsOverflow;
+    // the march stopped at the limit (not at the grid's edge) and the limit was only this call's
+    t_after = (active && limit > 0 && m.n >= limit && !limit_is_final) ? t_last + kConeStep : -1.0f;
     return m.n;
 }
 

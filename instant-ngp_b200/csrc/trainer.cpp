@@ -9,7 +9,8 @@
 // * the network forward of the compacted batch is not run: the backward recomputes its
 //   activations on chip from the encoded inputs;
 // * gradients are fp32 and Adam clears the grid gradient in the same pass;
-// * evaluation renders whole 2^18-pixel tiles instead of 4096-pixel tiles.
+// * evaluation marches 2^16-pixel tiles a segment at a time and stops marching a ray once its
+//   transmittance is spent, instead of marching every occupied step of 4096-pixel tiles.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -29,6 +30,10 @@ constexpr uint32_t kMlpParams  = 10240;
 constexpr int kTrainPhases     = 8;  // see ngp_trainer_phase_times
 constexpr uint32_t kLrTableCapacity = 1u << 20;
 constexpr uint32_t kLrTableBlock    = 4096u;
+// Segmented evaluation: tiles of 2^16 pixel rays; the first segment marches at most
+// MAX_SAMPLES / tile = 64 samples per ray (so it always fits), later ones 256, then the rest.
+constexpr uint32_t kSegTile         = 1u << 16;
+constexpr uint32_t kSegCaps[]       = {kMaxSamples / kSegTile, 256u, kMarchSteps};
 
 template <typename T>
 int dalloc(T*& p, size_t count, const char* what) {
@@ -114,6 +119,15 @@ struct ngp_trainer {
     size_t mlp_scratch_floats = 0;
     double* eval_sse          = nullptr;
     uint8_t* comparison       = nullptr;
+    // segmented evaluation (tiles of kSegTile pixels): per-ray state carried between segments
+    bool eval_segmented    = true;
+    float* seg_tout        = nullptr;  // [tile entry] where the ray continues
+    float* seg_tstate      = nullptr;  // [tile ray]
+    uint32_t* seg_marched  = nullptr;  // [tile ray]
+    float* seg_state       = nullptr;  // [tile ray][4] T, r, g, b
+    uint32_t* seg_lists    = nullptr;  // [2][tile] ray lists of alternate segments
+    uint32_t* seg_counters = nullptr;  // 0 samples, 1 fitted entries, 2/3 list counts of alternate segments
+    uint32_t* seg_host     = nullptr;  // pinned copy of seg_counters
 
     // host state (ngp.train.ixx:79-89)
     uint32_t step              = 0;
@@ -162,7 +176,8 @@ void destroy(ngp_trainer* t) {
     free_split(t->test);
     void* ptrs[] = {t->master, t->params, t->grads, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
                     t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->rows, t->batch_rows, t->dens, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
-                    t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table};
+                    t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table, t->seg_tout, t->seg_tstate, t->seg_marched, t->seg_state,
+                    t->seg_lists, t->seg_counters};
     for (void* p : ptrs) cudaFree(p);
     for (MarchSet& m : t->sets) cudaFree(m.coords), cudaFree(m.rays), cudaFree(m.ray_indices), cudaFree(m.numsteps), cudaFree(m.counters);
     if (t->comm) ncclCommDestroy(t->comm);
@@ -173,6 +188,7 @@ void destroy(ngp_trainer* t) {
     if (t->ev_counts) cudaEventDestroy(t->ev_counts);
     if (t->ev_march) cudaEventDestroy(t->ev_march);
     if (t->host_counters) cudaFreeHost(t->host_counters);
+    if (t->seg_host) cudaFreeHost(t->seg_host);
     if (t->march_stream) cudaStreamDestroy(t->march_stream);
     if (t->stream) cudaStreamDestroy(t->stream);
     delete t;
@@ -451,6 +467,51 @@ int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparis
     return NGP_OK;
 }
 
+// One image by segmented marching: each tile's rays are marched a segment at a time (64 samples,
+// then 256, then the rest), the network evaluated on the segment's samples, and the compositing
+// continued; rays stop being marched once their transmittance falls below 1e-4.  Same samples,
+// network outputs and compositing operations per pixel as eval_image, so the same image bit for
+// bit; the march no longer runs through the (typically most) samples behind each ray's stopping
+// point, and the tiles need no re-march when their samples exceed the budget.
+int eval_image_segmented(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparison_dev, float* rendered) {
+    const uint32_t total = s.width * s.height;
+    const cudaStream_t st = t->stream;
+    for (uint32_t off = 0; off < total; off += kSegTile) {
+        const uint32_t n = std::min(kSegTile, total - off);
+        NGP_TRY(ngp_make_eval_rays(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, off, n, t->rays, st));
+        uint32_t max_entries = n;
+        for (uint32_t seg = 0;; ++seg) {
+            const bool first         = seg == 0;
+            const uint32_t* list     = first ? nullptr : t->seg_lists + static_cast<size_t>((seg - 1u) & 1u) * kSegTile;
+            const uint32_t* n_dev    = first ? nullptr : t->seg_counters + 2u + ((seg - 1u) & 1u);
+            const uint32_t cap       = kSegCaps[std::min<uint32_t>(seg, 2u)];
+            NGP_TRY(ngp_march_rays_segment(max_entries, n_dev, list, t->rays, t->bitfield, first ? nullptr : t->seg_tstate,
+                                           first ? nullptr : t->seg_marched, cap, kMaxSamples, t->coords, t->numsteps, t->seg_tout,
+                                           t->eval_march_scratch, t->seg_counters, st));
+            NGP_TRY(check_cuda(cudaMemcpyAsync(t->seg_host, t->seg_counters, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost, st), "segment counters"));
+            NGP_TRY(check_cuda(cudaStreamSynchronize(st), "segment march"));
+            const uint32_t complete = t->seg_host[1];
+            if (complete == 0) break;  // no rays left in this tile
+            const uint32_t used = std::min(t->seg_host[0], kMaxSamples);
+            if (used > 0)
+                NGP_TRY(ngp_eval_network_progressive(complete, &t->layout, t->params, t->coords, used, t->numsteps, t->enc, used, t->out, t->rows,
+                                                     t->loss_scratch, t->loss_scratch_bytes, st));
+            uint32_t* next_count = t->seg_counters + 2u + (seg & 1u);
+            NGP_TRY(check_cuda(cudaMemsetAsync(next_count, 0, sizeof(uint32_t), st), "segment list count"));
+            NGP_TRY(ngp_eval_composite_segment(max_entries, n_dev, t->seg_counters + 1, list, t->numsteps, t->coords, t->out, t->seg_tout,
+                                               t->seg_tstate, t->seg_marched, t->seg_state, t->seg_lists + static_cast<size_t>(seg & 1u) * kSegTile,
+                                               next_count, off, image, s.width, s.height, s.pixels, t->eval_sse, comparison_dev, rendered, st));
+            // the next list holds at most this segment's entries
+            if (!first) max_entries = t->seg_host[2u + ((seg - 1u) & 1u)];
+        }
+    }
+    return NGP_OK;
+}
+
+int eval_one(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparison_dev, float* rendered) {
+    return t->eval_segmented ? eval_image_segmented(t, s, image, comparison_dev, rendered) : eval_image(t, s, image, comparison_dev, rendered);
+}
+
 int run_eval(ngp_trainer* t, const Split& s, uint32_t begin, uint32_t count, uint8_t* comparison_host, double* out_sse) {
     if (s.frames == 0) return fail(NGP_ERR_STATE, "no images in this split");
     if (begin >= s.frames || count > s.frames - begin) return fail(NGP_ERR_INVALID, "evaluation image range is out of bounds");
@@ -460,7 +521,7 @@ int run_eval(ngp_trainer* t, const Split& s, uint32_t begin, uint32_t count, uin
         NGP_TRY(dalloc(t->comparison, static_cast<size_t>(s.width) * s.height * 6u, "comparison image"));
     }
     NGP_TRY(check_cuda(cudaMemsetAsync(t->eval_sse, 0, sizeof(double), t->stream), "eval clear"));
-    for (uint32_t k = 0; k < count; ++k) NGP_TRY(eval_image(t, s, begin + k, comparison_host != nullptr ? t->comparison : nullptr, nullptr));
+    for (uint32_t k = 0; k < count; ++k) NGP_TRY(eval_one(t, s, begin + k, comparison_host != nullptr ? t->comparison : nullptr, nullptr));
     NGP_TRY(check_cuda(cudaMemcpyAsync(out_sse, t->eval_sse, sizeof(double), cudaMemcpyDeviceToHost, t->stream), "eval sse"));
     if (comparison_host != nullptr)
         NGP_TRY(check_cuda(cudaMemcpyAsync(comparison_host, t->comparison, static_cast<size_t>(s.width) * s.height * 6u, cudaMemcpyDeviceToHost,
@@ -549,6 +610,13 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         t->mlp_scratch_floats = ngp_mlp_backward_scratch_floats();
         NGP_TRY(dalloc(t->mlp_scratch, t->mlp_scratch_floats, "mlp scratch"));
         NGP_TRY(dalloc(t->eval_sse, 1, "eval sse"));
+        NGP_TRY(dalloc(t->seg_tout, kSegTile, "segment t"));
+        NGP_TRY(dalloc(t->seg_tstate, kSegTile, "segment ray t"));
+        NGP_TRY(dalloc(t->seg_marched, kSegTile, "segment ray counts"));
+        NGP_TRY(dalloc(t->seg_state, static_cast<size_t>(kSegTile) * 4u, "segment ray state"));
+        NGP_TRY(dalloc(t->seg_lists, static_cast<size_t>(kSegTile) * 2u, "segment lists"));
+        NGP_TRY(dalloc(t->seg_counters, 4, "segment counters"));
+        NGP_TRY(check_cuda(cudaMallocHost(&t->seg_host, 4 * sizeof(uint32_t)), "segment host counters"));
         NGP_TRY(dalloc(t->lr_table, kLrTableCapacity, "adam rate table"));
         const cudaStream_t s = t->stream;
         NGP_TRY(check_cuda(cudaMemsetAsync(t->grads, 0, sizeof(float) * t->n_params, s), "clear grads"));
@@ -661,10 +729,17 @@ extern "C" int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint
     s.frames = 1, s.width = width, s.height = height, s.fx = fx, s.fy = fy, s.cx = cx, s.cy = cy;
     NGP_TRY(dalloc(s.camera, 12, "render camera"));
     int st = check_cuda(cudaMemcpyAsync(s.camera, camera_host, sizeof(float) * 12u, cudaMemcpyHostToDevice, t->stream), "render camera");
-    if (st == NGP_OK) st = eval_image(t, s, 0, nullptr, rgb_device);
+    if (st == NGP_OK) st = eval_one(t, s, 0, nullptr, rgb_device);
     if (st == NGP_OK) st = check_cuda(cudaStreamSynchronize(t->stream), "render");
     free_split(s);
     return st;
+}
+
+extern "C" int ngp_trainer_set_segmented_eval(ngp_trainer* t, int enabled) {
+    clear_error();
+    if (t == nullptr) return fail(NGP_ERR_INVALID, "segmented eval: null trainer");
+    t->eval_segmented = enabled != 0;
+    return NGP_OK;
 }
 
 extern "C" uint32_t ngp_trainer_param_count(const ngp_trainer* t) { return t == nullptr ? 0u : t->n_params; }

@@ -70,6 +70,12 @@ def _check(status: int, what: str) -> None:
         raise RuntimeError(f"{what} failed (status {status}): {msg}")
 
 
+def kernel_launch_count() -> int:
+    """Kernel launches made by the library in this process so far."""
+    lib().ngp_kernel_launch_count.restype = ctypes.c_uint64
+    return int(lib().ngp_kernel_launch_count())
+
+
 def _ptr(t) -> ctypes.c_void_p:
     """Device pointer of a torch tensor (or None)."""
     if t is None:
@@ -248,6 +254,23 @@ def march_rays(rays, bitfield, coords, numsteps, scratch, sample_counter, sample
     n = rays.shape[0] if n is None else n
     _check(lib().ngp_march_rays(_u32(n), _ptr(rays), ctypes.c_int(1 if jitter else 0), _u32(step), _ptr(bitfield), _u32(sample_limit), _ptr(coords),
                                 _ptr(numsteps), _ptr(scratch), _ptr(sample_counter), _stream(stream)), "ngp_march_rays")
+
+
+def march_rays_segment(rays, bitfield, coords, numsteps, t_out, scratch, counters, cap, max_entries=None, n_entries=None, ray_list=None,
+                       t_state=None, marched=None, sample_limit=MAX_SAMPLES, stream=None) -> None:
+    max_entries = rays.shape[0] if max_entries is None else max_entries
+    _check(lib().ngp_march_rays_segment(_u32(max_entries), _ptr(n_entries), _ptr(ray_list), _ptr(rays), _ptr(bitfield), _ptr(t_state), _ptr(marched),
+                                        _u32(cap), _u32(sample_limit), _ptr(coords), _ptr(numsteps), _ptr(t_out), _ptr(scratch), _ptr(counters),
+                                        _stream(stream)), "ngp_march_rays_segment")
+
+
+def eval_composite_segment(max_entries, complete, numsteps, coords, network_output, t_out, t_state, marched, state, next_list, next_count,
+                           pixel_offset, image, width, height, n_entries=None, ray_list=None, pixels=None, sse=None, comparison=None,
+                           rendered=None, stream=None) -> None:
+    _check(lib().ngp_eval_composite_segment(_u32(max_entries), _ptr(n_entries), _ptr(complete), _ptr(ray_list), _ptr(numsteps), _ptr(coords),
+                                            _ptr(network_output), _ptr(t_out), _ptr(t_state), _ptr(marched), _ptr(state), _ptr(next_list),
+                                            _ptr(next_count), _u32(pixel_offset), _u32(image), _u32(width), _u32(height), _ptr(pixels), _ptr(sse),
+                                            _ptr(comparison), _ptr(rendered), _stream(stream)), "ngp_eval_composite_segment")
 
 
 def make_eval_rays(camera, image, width, height, fx, fy, cx, cy, pixel_offset, n, rays, stream=None) -> None:
@@ -557,6 +580,11 @@ class InstantNGP:
         _check(lib().ngp_trainer_render(self.handle, ctypes.c_void_p(cam.ctypes.data), _u32(width), _u32(height), _f32(focal[0]), _f32(focal[1]),
                                         _f32(principal[0]), _f32(principal[1]), _ptr(out)), "ngp_trainer_render")
         return out
+
+    def set_segmented_eval(self, enabled: bool) -> None:
+        """Segmented marching for evaluation and rendering (default) or the reference's
+        march-everything-first flow; the images are identical."""
+        _check(lib().ngp_trainer_set_segmented_eval(self.handle, ctypes.c_int(1 if enabled else 0)), "ngp_trainer_set_segmented_eval")
 
     def param_count(self) -> int:
         lib().ngp_trainer_param_count.restype = ctypes.c_uint32
