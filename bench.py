@@ -658,7 +658,7 @@ def bench_render_ours(args, rank, world, local):
         "dtype": "fp16 params/activations, fp32 accumulation", "data": "synthetic procedural scene (64 Lambert spheres, seeded)",
         "config": {"workload": "config4 render 1920x1080 novel views after training", "table": "L=16 F=2 log2T=22 base 16 finest 4096",
                    "views_per_gpu": args.steps, "trained_steps": args.train_steps, "parallelism": f"views partitioned over {world} ranks, no collective",
-                   "l2": "table 268 MB fp16 > L2; no flush"},
+                   "l2": "table 170 MB fp16 > L2; no flush"},
         "e2e": {"value": round(world * rays / (e2e_ms * 1e-3), 1), "unit": "rays/s", "h2d_bytes_per_step": 48,
                 "d2h_bytes_per_step": rays * 12, "note": "InstantNGP.render per view with the image read back to pinned host memory"},
         "gpu_launches": launches, "clocks": clocks.summary(), "roofline": roofline,

@@ -759,17 +759,53 @@ struct SegCompositeParams {
     float* rendered;
 };
 
+// Compositing of one ray's segment by one warp, lane j on sample c0 + j: the transmittance
+// prefix and the colour sum are taken in sample order (prefix_transmittance and ordered
+// shuffles), so T and rgb are those of the sequential loop, bit for bit; stops after the first
+// sample whose transmittance falls below 1e-4, as the loop does.  Returns true if it stopped.
+__device__ __forceinline__ bool composite_samples_warp(uint32_t base, uint32_t steps, const float* __restrict__ coords,
+                                                       const __half* __restrict__ network_output, float& T, float3& rgb) {
+    const uint32_t lane = threadIdx.x & 31u;
+    for (uint32_t c0 = 0; c0 < steps; c0 += 32u) {
+        const uint32_t j   = c0 + lane;
+        const uint32_t nv  = min(32u, steps - c0);
+        const bool valid   = lane < nv;
+        float r = 0.f, g = 0.f, b = 0.f, d = 0.f, dt = 0.f;
+        if (valid) {
+            load_output(network_output + (static_cast<uint64_t>(base) + j) * 16u, r, g, b, d);
+            dt = coords[(static_cast<uint64_t>(base) + j) * 7u + 3u];
+        }
+        const float alpha   = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
+        const float Tb      = prefix_transmittance(T, 1.0f - alpha, nv);
+        const float Ta      = Tb * (1.0f - alpha);
+        const float w       = alpha * Tb;
+        const float3 col    = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
+        const uint32_t stop = __ballot_sync(0xFFFFFFFFu, valid && Ta < kTransmittanceEps);
+        const uint32_t nk   = stop ? static_cast<uint32_t>(__ffs(stop)) : nv;
+        for (uint32_t q = 0; q < nk; ++q) {
+            const float wq = __shfl_sync(0xFFFFFFFFu, w, q);
+            rgb.x          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.x, q), rgb.x);
+            rgb.y          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.y, q), rgb.y);
+            rgb.z          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.z, q), rgb.z);
+        }
+        T = __shfl_sync(0xFFFFFFFFu, Ta, nk - 1u);
+        if (stop) return true;
+    }
+    return false;
+}
+
+// One warp per entry (kThreads / 32 entries per CTA).
 __global__ void __launch_bounds__(kThreads) seg_composite_kernel(const __grid_constant__ SegCompositeParams p) {
-    const uint32_t k = blockIdx.x * kThreads + threadIdx.x;
-    const uint32_t n = p.n_entries != nullptr ? min(*p.n_entries, p.max_entries) : p.max_entries;
-    double se        = 0.0;
-    bool carry       = false;
-    uint32_t i       = 0;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t k    = blockIdx.x * (kThreads / 32u) + (threadIdx.x >> 5);
+    const uint32_t n    = p.n_entries != nullptr ? min(*p.n_entries, p.max_entries) : p.max_entries;
+    double se           = 0.0;
     if (k < n) {
-        i = p.list != nullptr ? p.list[k] : k;
+        const uint32_t i = p.list != nullptr ? p.list[k] : k;
+        bool carry       = true;  // entries past the segment's limit were not marched: unchanged
         if (k < *p.complete) {
-            float T    = 1.0f;
-            float3 rgb = {0.0f, 0.0f, 0.0f};
+            float T       = 1.0f;
+            float3 rgb    = {0.0f, 0.0f, 0.0f};
             uint32_t done = 0;
             if (!p.first) {
                 const float4 st = p.state[i];
@@ -777,29 +813,20 @@ __global__ void __launch_bounds__(kThreads) seg_composite_kernel(const __grid_co
                 done = p.marched[i];
             }
             const uint32_t steps = p.numsteps[2u * k];
-            const bool stopped   = composite_samples(p.numsteps[2u * k + 1u], steps, p.coords, p.output, T, rgb);
+            const bool stopped   = composite_samples_warp(p.numsteps[2u * k + 1u], steps, p.coords, p.output, T, rgb);
             const float t_next   = p.t_out[k];
-            if (stopped || t_next < 0.0f) {
-                se = eval_pixel_out(p.pixel_offset + i, rgb, p.image, p.width, p.height, p.pixels, p.comparison, p.rendered);
-            } else {
-                p.state[i]   = make_float4(T, rgb.x, rgb.y, rgb.z);
-                p.t_state[i] = t_next;
-                p.marched[i] = done + steps;
-                carry        = true;
+            carry                = !(stopped || t_next < 0.0f);
+            if (lane == 0) {
+                if (!carry) {
+                    se = eval_pixel_out(p.pixel_offset + i, rgb, p.image, p.width, p.height, p.pixels, p.comparison, p.rendered);
+                } else {
+                    p.state[i]   = make_float4(T, rgb.x, rgb.y, rgb.z);
+                    p.t_state[i] = t_next;
+                    p.marched[i] = done + steps;
+                }
             }
-        } else {
-            carry = true;  // not marched in this segment: unchanged
         }
-    }
-    // warp-aggregated append of the carried rays
-    const uint32_t lane = threadIdx.x & 31u;
-    const uint32_t bal  = __ballot_sync(0xFFFFFFFFu, carry);
-    uint32_t slot       = 0;
-    if (bal != 0u) {
-        const uint32_t leader = static_cast<uint32_t>(__ffs(bal)) - 1u;
-        if (lane == leader) slot = atomicAdd(p.next_count, static_cast<uint32_t>(__popc(bal)));
-        slot = __shfl_sync(0xFFFFFFFFu, slot, leader);
-        if (carry) p.next_list[slot + __popc(bal & ((1u << lane) - 1u))] = i;
+        if (carry && lane == 0) p.next_list[atomicAdd(p.next_count, 1u)] = i;
     }
     add_block_sse(se, p.sse);
 }
@@ -1163,7 +1190,8 @@ extern "C" int ngp_eval_composite_segment(uint32_t max_entries, const uint32_t* 
     p.sse          = sse;
     p.comparison   = comparison;
     p.rendered     = rendered;
-    seg_composite_kernel<<<(max_entries + kThreads - 1) / kThreads, kThreads, 0, as_stream(stream)>>>(p);
+    constexpr uint32_t per_cta = kThreads / 32u;
+    seg_composite_kernel<<<(max_entries + per_cta - 1) / per_cta, kThreads, 0, as_stream(stream)>>>(p);
     return check_launch("seg_composite_kernel");
 }
 

@@ -31,9 +31,15 @@ constexpr int kTrainPhases     = 8;  // see ngp_trainer_phase_times
 constexpr uint32_t kLrTableCapacity = 1u << 20;
 constexpr uint32_t kLrTableBlock    = 4096u;
 // Segmented evaluation: tiles of 2^16 pixel rays; the first segment marches at most
-// MAX_SAMPLES / tile = 64 samples per ray (so it always fits), later ones 256, then the rest.
-constexpr uint32_t kSegTile         = 1u << 16;
-constexpr uint32_t kSegCaps[]       = {kMaxSamples / kSegTile, 256u, kMarchSteps};
+// MAX_SAMPLES / tile = 64 samples per ray (so it always fits), later ones 128, then the rest.
+#ifndef NGP_SEG_TILE_LOG2
+#define NGP_SEG_TILE_LOG2 16
+#endif
+#ifndef NGP_SEG_CAP1
+#define NGP_SEG_CAP1 128
+#endif
+constexpr uint32_t kSegTile         = 1u << NGP_SEG_TILE_LOG2;
+constexpr uint32_t kSegCaps[]       = {kMaxSamples / kSegTile, NGP_SEG_CAP1, kMarchSteps};
 
 template <typename T>
 int dalloc(T*& p, size_t count, const char* what) {
@@ -57,6 +63,9 @@ struct Split {
 
 #ifndef NGP_OVERLAP_MARCH
 #define NGP_OVERLAP_MARCH 1  // 0: every step marches on its own stream (no cross-step overlap; measured 0.87 vs 0.75 ms)
+#endif
+#ifndef NGP_DP_PRIORITY
+#define NGP_DP_PRIORITY 0  // 1: high-priority training stream; the all-reduce does not wait for the next step's march
 #endif
 #ifndef NGP_SELECT
 #define NGP_SELECT 1  // 0: the kept samples' records and encodings are copied into a compacted batch
@@ -397,7 +406,7 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     // The gradient crosses NVLink in fp16 (the reference's gradient format, loss-scaled by 128):
     // half the bytes of fp32; the fp32 accumulation buffer is cleared by the conversion.
     if (t->comm != nullptr) {
-        if (premarch) NGP_TRY(check_cuda(cudaStreamWaitEvent(t->stream, t->ev_march, 0), "all-reduce after march"));
+        if (premarch && !NGP_DP_PRIORITY) NGP_TRY(check_cuda(cudaStreamWaitEvent(t->stream, t->ev_march, 0), "all-reduce after march"));
         NGP_TRY(ngp_gradients_to_half(t->n_params, t->grads, t->grads16, 1, t->stream));
         const ncclResult_t r = ncclAllReduce(t->grads16, t->grads16, t->n_params, ncclHalf, ncclSum, t->comm, t->stream);
         if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
@@ -468,7 +477,7 @@ int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparis
 }
 
 // One image by segmented marching: each tile's rays are marched a segment at a time (64 samples,
-// then 256, then the rest), the network evaluated on the segment's samples, and the compositing
+// then 128, then the rest), the network evaluated on the segment's samples, and the compositing
 // continued; rays stop being marched once their transmittance falls below 1e-4.  Same samples,
 // network outputs and compositing operations per pixel as eval_image, so the same image bit for
 // bit; the march no longer runs through the (typically most) samples behind each ray's stopping
@@ -555,8 +564,16 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
     const int st = [&]() -> int {
         NGP_TRY(ngp_grid_layout_make(cfg->n_levels, cfg->features_per_level, cfg->log2_hashmap_size, cfg->base_resolution,
                                      cfg->log2_per_level_scale, &t->layout));
+#if NGP_DP_PRIORITY
+        // the training stream (with the gradient all-reduce) takes SM slots before the march
+        int prio_low = 0, prio_high = 0;
+        NGP_TRY(check_cuda(cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high), "stream priorities"));
+        NGP_TRY(check_cuda(cudaStreamCreateWithPriority(&t->stream, cudaStreamNonBlocking, prio_high), "stream"));
+        NGP_TRY(check_cuda(cudaStreamCreateWithPriority(&t->march_stream, cudaStreamNonBlocking, prio_low), "march stream"));
+#else
         NGP_TRY(check_cuda(cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking), "stream"));
         NGP_TRY(check_cuda(cudaStreamCreateWithFlags(&t->march_stream, cudaStreamNonBlocking), "march stream"));
+#endif
         NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_counts, cudaEventDisableTiming), "event"));
         NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_march, cudaEventDisableTiming), "event"));
         NGP_TRY(check_cuda(cudaMallocHost(&t->host_counters, 4 * sizeof(uint32_t)), "pinned counters"));
