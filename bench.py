@@ -1,6 +1,6 @@
 """Benchmark of the B200-native NeRF hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload train|encode]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload train|encode|mlp|march|render]
 
 Workloads (BASELINE configurations; seeded synthetic inputs stand in for the reference's
 NeRF-synthetic datasets, which are not available here):
@@ -11,6 +11,9 @@ NeRF-synthetic datasets, which are not available here):
           compaction, backward, Adam); data parallel over N GPUs with one NCCL gradient
           all-reduce per step (weak scaling: 2^18 samples per GPU).
   encode  config 0: hash-grid encoding forward + backward, 2^18 points per GPU.
+  mlp     config 1: fused density + colour MLPs forward + backward, 2^18 rows per GPU.
+  march   config 2: density-grid update + marching of 2^18 rays per GPU.
+  render  config 4: 1920x1080 novel views of a model trained with log2 T = 22.
 
 Timing: W untimed warm-up steps, then K steps timed on the device with CUDA events on the
 stream that runs them, bracketed by a barrier and a device synchronize; the max over ranks is
@@ -571,6 +574,162 @@ def bench_encode_reference(args, rank, world, local):
 # ------------------------------------------------------------------------------------------------
 # render workload (config 4): large table, novel 1920x1080 views partitioned across ranks
 # ------------------------------------------------------------------------------------------------
+def bench_mlp_ours(args, rank, world, local):
+    """Config 1: the fused density + colour MLPs, forward + backward (input and weight gradients)
+    over 2^18 rows per GPU; L2 flushed before every step."""
+    import torch
+    import ngp_b200 as ngp
+    import workloads
+
+    n = BATCH
+    x_h, c_h, dy_h = workloads.mlp_inputs(n, seed=31 + rank)
+    params = torch.from_numpy(workloads.xavier_mlp_params(1).view(np.int16)).cuda()
+    x, coords, dy = torch.from_numpy(x_h).cuda(), torch.from_numpy(c_h).cuda(), torch.from_numpy(dy_h).cuda()
+    out = torch.empty((n, 16), dtype=torch.float16, device="cuda")
+    dx = torch.empty((32, n), dtype=torch.float16, device="cuda")
+    dw = torch.empty(10240, dtype=torch.float32, device="cuda")
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    ngp.mlp_backward_scratch()
+
+    def flush():
+        flush_buf.fill_(1.0)
+
+    def fwd():
+        ngp.mlp_forward(params, x, coords, out, stream=stream)
+
+    def bwd():
+        ngp.mlp_backward(params, x, coords, dy, dx=dx, dw_f32=dw, stream=stream)
+
+    def step():
+        fwd()
+        bwd()
+
+    with ClockSampler(local) as clocks:
+        clocks.wait_first()
+        launches0 = ngp.kernel_launch_count()
+        times = time_steps(step, args.steps, args.warmup, flush, stream, world)
+        launches = ngp.kernel_launch_count() - launches0
+        time.sleep(0.25)
+    ms = max_over_ranks(sum(times) / len(times), world)
+    fwd_ms = statistics.median(time_steps(fwd, 20, 2, flush, stream, 1))
+    bwd_ms = statistics.median(time_steps(bwd, 20, 2, flush, stream, 1))
+    # e2e: inputs from pinned host memory, outputs and weight gradients read back
+    pins = [torch.from_numpy(a).pin_memory() for a in (x_h, c_h, dy_h)]
+    out_h = torch.empty((n, 16), dtype=torch.float16).pin_memory()
+    dw_h = torch.empty(10240, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        for dst, src in zip((x, coords, dy), pins):
+            dst.copy_(src, non_blocking=True)
+        step()
+        out_h.copy_(out, non_blocking=True)
+        dw_h.copy_(dw, non_blocking=True)
+
+    e2e_ms = max_over_ranks(statistics.mean(time_steps(e2e_step, max(3, args.steps // 4), 2, flush, stream, world)), world)
+    peaks = load_peaks()
+    tflops = MLP_FWDBWD_FLOP * n / (ms * 1e-3) / 1e12
+    return {
+        "metric": "fused MLP fwd+bwd rows/s (config 1)", "value": round(world * n / (ms * 1e-3), 1), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 weights/activations, fp32 accumulation (tcgen05 kind::f16)",
+        "data": "synthetic (U(-1,1) fp16 inputs, directions uniform on S^2, N(0,1) dL/dy, Xavier weights; seeded)",
+        "config": {"workload": "config1 fused MLP fwd+bwd", "rows_per_gpu": n, "density": "32-64-16", "colour": "32-64-64-16",
+                   "parallelism": f"dp{world} (no collective)", "l2": "flushed (256 MB write) before every timed step"},
+        "kernels_ms": {"mlp_forward": round(fwd_ms, 5), "mlp_backward": round(bwd_ms, 5)},
+        "roofline": {"kernel": "mlp_forward_kernel + mlp_backward_kernel", "bound": "tensor", "achieved": round(tflops, 2),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": None,
+                     "peak_source": peaks["source"] + " (dense bf16 burst; fp16 has the same tensor rate)",
+                     "per_unit": f"{MLP_FWDBWD_FLOP} FLOP per row (forward 20,480, input gradients 20,480, weight gradients 20,480)"},
+        "e2e": {"value": round(world * n / (e2e_ms * 1e-3), 1), "unit": "rows/s",
+                "h2d_bytes_per_step": int(x_h.nbytes + c_h.nbytes + dy_h.nbytes), "d2h_bytes_per_step": n * 32 + 10240 * 4},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+
+
+def bench_march_ours(args, rank, world, local):
+    """Config 2: density-grid update (EMA, mean, bitfield) of the 128^3 grid with the blob
+    field's optical thickness as the step's observations, then marching 2^18 rays through it
+    (counts and sample records); L2 flushed before every step."""
+    import torch
+    import ngp_b200 as ngp
+    import workloads
+
+    n = 1 << 18
+    obs = torch.from_numpy(workloads.blob_grid_values(workloads.gaussian_blob_density())).cuda()
+    values = obs.clone()
+    scratch = torch.zeros_like(obs)
+    partial = torch.zeros(ngp.density_grid_partials(), dtype=torch.float32, device="cuda")
+    mean = torch.zeros(1, dtype=torch.float32, device="cuda")
+    bits = torch.zeros(128 ** 3 // 8, dtype=torch.uint8, device="cuda")
+    occ = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rays = torch.from_numpy(workloads.march_rays_config2(n, seed=2 + rank)).cuda()
+    limit = 1 << 24
+    coords = torch.empty((limit, 7), dtype=torch.float32, device="cuda")
+    numsteps = torch.empty((n, 2), dtype=torch.int32, device="cuda")
+    msc = torch.empty(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def flush():
+        flush_buf.fill_(1.0)
+        scratch.copy_(obs)  # the step's observations (the splat's output)
+
+    def grid():
+        ngp.density_grid_update(values, scratch, partial, mean, bits, occ, stream=stream)
+
+    def march():
+        ngp.march_rays(rays, bits, coords, numsteps, msc, counter, sample_limit=limit, stream=stream)
+
+    def step():
+        grid()
+        march()
+
+    with ClockSampler(local) as clocks:
+        clocks.wait_first()
+        launches0 = ngp.kernel_launch_count()
+        times = time_steps(step, args.steps, args.warmup, flush, stream, world)
+        launches = ngp.kernel_launch_count() - launches0
+        time.sleep(0.25)
+    ms = max_over_ranks(sum(times) / len(times), world)
+    grid_ms = statistics.median(time_steps(grid, 10, 2, flush, stream, 1))
+    march_ms = statistics.median(time_steps(march, 10, 2, flush, stream, 1))
+    samples = int(counter.item())
+    # e2e: rays from pinned host memory, per-ray counts and the samples read back
+    rays_pin = rays.cpu().pin_memory()
+    ns_h = torch.empty((n, 2), dtype=torch.int32).pin_memory()
+    co_h = torch.empty((samples, 7), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        rays.copy_(rays_pin, non_blocking=True)
+        step()
+        ns_h.copy_(numsteps, non_blocking=True)
+        co_h.copy_(coords[:samples], non_blocking=True)
+
+    e2e_ms = max_over_ranks(statistics.mean(time_steps(e2e_step, max(3, args.steps // 4), 2, flush, stream, world)), world)
+    peaks = load_peaks()
+    march_bytes = n * (24 + 8) + samples * 28
+    achieved = march_bytes / (march_ms * 1e-3) / 1e9
+    return {
+        "metric": "density-grid update + march rays/s (config 2)", "value": round(world * n / (ms * 1e-3), 1), "unit": "rays/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 positions, uint32 counts, uint8 bitfield",
+        "data": "synthetic (8 seeded Gaussian blobs, rays from the radius-4 sphere aimed near the origin)",
+        "config": {"workload": "config2 density-grid update + ray marching", "rays_per_gpu": n, "grid": "128^3, 1 cascade, EMA 0.95",
+                   "samples_per_step": samples, "parallelism": f"dp{world} (no collective)", "l2": "flushed (256 MB write) before every timed step"},
+        "kernels_ms": {"grid_update": round(grid_ms, 5), "march": round(march_ms, 5)},
+        "samples_per_s": round(world * samples / (ms * 1e-3), 1),
+        "roofline": {"kernel": "march_count_kernel + march_write_kernel", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": peaks["source"] + " (HBM copy bandwidth)",
+                     "per_unit": f"24 B in + 8 B counts per ray, 28 B per emitted sample; {n} rays, {samples} samples per launch"},
+        "e2e": {"value": round(world * n / (e2e_ms * 1e-3), 1), "unit": "rays/s", "h2d_bytes_per_step": n * 24,
+                "d2h_bytes_per_step": n * 8 + samples * 28},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+
+
 def render_encode_roofline(ngp, workloads, peaks, n: int = 1 << 22) -> dict:
     """Config 4's encode HBM rate: the encoding forward over the config-4 table (log2 T = 22,
     finest resolution 4096; larger than L2) on n uniformly random points, the gather pattern with
@@ -627,10 +786,12 @@ def bench_render_ours(args, rank, world, local):
     with ClockSampler(local) as clocks:
         clocks.wait_first()
         launches0 = ngp.kernel_launch_count()
+        torch.cuda.nvtx.range_push("render")  # lets a profiler select the timed renders
         s.record()
         for v in views:
             model.render(v, w, h, poses["focal"], poses["principal"], out=out)
         e.record()
+        torch.cuda.nvtx.range_pop()
         e.synchronize()
         launches = ngp.kernel_launch_count() - launches0
         time.sleep(0.25)
@@ -671,7 +832,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["train", "encode", "render"], default="train")
+    ap.add_argument("--workload", choices=["train", "encode", "mlp", "march", "render"], default="train")
     ap.add_argument("--train-steps", type=int, default=1000, help="render workload: untimed training steps before rendering")
     ap.add_argument("--views", type=int, default=100)
     ap.add_argument("--test-views", type=int, default=20)
@@ -679,9 +840,9 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"train": 300, "encode": 500, "render": 8}[args.workload]
+        args.steps = {"train": 300, "encode": 500, "mlp": 200, "march": 100, "render": 8}[args.workload]
     if args.warmup is None:
-        args.warmup = {"train": 300, "encode": 5, "render": 3}[args.workload]
+        args.warmup = {"train": 300, "encode": 5, "mlp": 5, "march": 5, "render": 3}[args.workload]
     args.warmup = max(args.warmup, 3)
 
     rank, world, local = dist_setup()
@@ -691,10 +852,15 @@ def main() -> int:
                 print(json.dumps({"impl": "reference", "unavailable": "the reference build's compiled grid (8x4, log2 T 19) cannot express config 4"}),
                       flush=True)
                 return 0
+            if args.workload in ("mlp", "march"):
+                print(json.dumps({"impl": "reference", "unavailable": f"no reference arm for the {args.workload} workload; "
+                                                                      "its kernels run inside the train workload's reference step"}), flush=True)
+                return 0
             fn = bench_train_reference if args.workload == "train" else bench_encode_reference
             print(json.dumps(fn(args, rank, world, local)), flush=True)
         return 0
-    fn = {"train": bench_train_ours, "encode": bench_encode_ours, "render": bench_render_ours}[args.workload]
+    fn = {"train": bench_train_ours, "encode": bench_encode_ours, "mlp": bench_mlp_ours, "march": bench_march_ours,
+          "render": bench_render_ours}[args.workload]
     res = fn(args, rank, world, local)
     if rank == 0:
         print(json.dumps(res), flush=True)
