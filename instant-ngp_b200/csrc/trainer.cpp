@@ -161,6 +161,7 @@ struct ngp_trainer {
     cudaStream_t march_stream = nullptr;
     cudaEvent_t ev_counts = nullptr, ev_march = nullptr;
     uint32_t* host_counters = nullptr;  // pinned copy of counters 0..2
+    float* host_loss        = nullptr;  // pinned copy of the last step's per-ray loss [BATCH]
     bool premarched         = false;    // step `step` was marched on march_stream
     // Adam: bias-corrected rate per step count, entries [1, lr_table_len] filled
     float* lr_table       = nullptr;
@@ -197,6 +198,7 @@ void destroy(ngp_trainer* t) {
     if (t->ev_counts) cudaEventDestroy(t->ev_counts);
     if (t->ev_march) cudaEventDestroy(t->ev_march);
     if (t->host_counters) cudaFreeHost(t->host_counters);
+    if (t->host_loss) cudaFreeHost(t->host_loss);
     if (t->seg_host) cudaFreeHost(t->seg_host);
     if (t->march_stream) cudaStreamDestroy(t->march_stream);
     if (t->stream) cudaStreamDestroy(t->stream);
@@ -579,6 +581,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_counts, cudaEventDisableTiming), "event"));
         NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_march, cudaEventDisableTiming), "event"));
         NGP_TRY(check_cuda(cudaMallocHost(&t->host_counters, 4 * sizeof(uint32_t)), "pinned counters"));
+        NGP_TRY(check_cuda(cudaMallocHost(&t->host_loss, kNetworkBatch * sizeof(float)), "pinned loss"));
         NGP_TRY(upload_split(t->train, train, "train"));
         NGP_TRY(upload_split(t->val, validation, "validation"));
         NGP_TRY(upload_split(t->test, test, "test"));
@@ -704,8 +707,7 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
         }
     }
     cudaEventRecord(e1, t->stream);
-    std::vector<float> losses(loss_rays);
-    NGP_TRY(check_cuda(cudaMemcpyAsync(losses.data(), t->loss_values, sizeof(float) * loss_rays, cudaMemcpyDeviceToHost, t->stream), "read loss"));
+    NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_loss, t->loss_values, sizeof(float) * loss_rays, cudaMemcpyDeviceToHost, t->stream), "read loss"));
     NGP_TRY(check_cuda(cudaMemcpyAsync(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read occupied"));
     NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train"));
     collect_grid_times(t);
@@ -714,7 +716,7 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     float loss_sum = 0.0f;
-    for (float l : losses) loss_sum += l;
+    for (uint32_t r = 0; r < loss_rays; ++r) loss_sum += t->host_loss[r];
     if (stats != nullptr) {
         stats->step                                    = t->step;
         stats->rays_per_batch                          = t->rays_per_batch;
