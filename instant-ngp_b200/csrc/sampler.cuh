@@ -186,7 +186,7 @@ namespace ngp {
 //    ray; with all G empty the march continues from the skip after lane G-1.
 // Up to G occupied steps or G empty voxels are resolved per round.
 #ifndef NGP_MARCH_GROUP
-#define NGP_MARCH_GROUP 4
+#define NGP_MARCH_GROUP 8
 #endif
 #ifndef NGP_MARCH_SKIP_SPEC
 #define NGP_MARCH_SKIP_SPEC 1  // 0: empty voxels are skipped one per round
