@@ -272,6 +272,7 @@ __global__ void __launch_bounds__(1024) scan_totals_kernel(uint32_t* __restrict_
 
 __global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_constant__ MarchParams p) {
     __shared__ uint32_t s_base[kRaysPerCta];
+    __shared__ float s_stage[kCtaThreads * 7u];  // per warp: 32 staged sample records
     const uint32_t n    = march_ray_count(p);
     const uint32_t slot = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
     const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_c
     float* out          = p.coords + static_cast<uint64_t>(base) * 7u;
     const bool overflow = n_runs == kRunsOverflow;
     // rays with few runs expand them; the rare ray with more runs than recorded marches again
-    group_expand_runs(r.dir, r.origin, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs, kept, !overflow, out);
+    group_expand_runs(r.dir, r.origin, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs, kept, !overflow, out, s_stage + (threadIdx.x & ~31u) * 7u);
     group_march_write(r.origin, r.dir, r.start_t, overflow ? kept : 0u, p.bits, out);
 }
 
@@ -346,6 +347,7 @@ __global__ void __launch_bounds__(kCtaThreads) seg_march_count_kernel(const __gr
 
 __global__ void __launch_bounds__(kCtaThreads) seg_march_write_kernel(const __grid_constant__ MarchParams p) {
     __shared__ uint32_t s_base[kRaysPerCta];
+    __shared__ float s_stage[kCtaThreads * 7u];  // per warp: 32 staged sample records
     const uint32_t n      = march_ray_count(p);
     const uint32_t slot   = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
     const uint32_t k      = blockIdx.x * kRaysPerCta + slot;
@@ -369,7 +371,7 @@ __global__ void __launch_bounds__(kCtaThreads) seg_march_write_kernel(const __gr
     if (kept > 0) seg_ray(p, k, n, i, r, limit, final_limit);
     float* out          = p.coords + static_cast<uint64_t>(base) * 7u;
     const bool overflow = n_runs == kRunsOverflow;
-    group_expand_runs(r.dir, r.origin, p.runs + static_cast<uint64_t>(k) * kMaxRuns, n_runs, kept, !overflow, out);
+    group_expand_runs(r.dir, r.origin, p.runs + static_cast<uint64_t>(k) * kMaxRuns, n_runs, kept, !overflow, out, s_stage + (threadIdx.x & ~31u) * 7u);
     group_march_write(r.origin, r.dir, r.start_t, overflow ? kept : 0u, p.bits, out);
 }
 

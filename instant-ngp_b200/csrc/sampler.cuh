@@ -368,8 +368,11 @@ __device__ __forceinline__ uint32_t group_march_count_runs_seg(float3 o, float3 
 }
 
 // Expand this group's runs into `n` sample records at `out` (active = the ray's runs are valid).
+// Each round the group's lanes compute up to kMarchGroup consecutive records, stage them in this
+// warp's 32 x 7 floats of shared memory (`stage`), and copy them out as consecutive floats, so a
+// store instruction writes whole 32-byte sectors instead of one float every 28 bytes.
 __device__ __forceinline__ void group_expand_runs(float3 d_unit, float3 o, const uint2* __restrict__ runs, uint32_t n_runs, uint32_t n,
-                                                  bool active, float* __restrict__ out) {
+                                                  bool active, float* __restrict__ out, float* __restrict__ stage) {
     const float3 w3         = {(d_unit.x + 1.0f) * 0.5f, (d_unit.y + 1.0f) * 0.5f, (d_unit.z + 1.0f) * 0.5f};
     const uint32_t lane     = threadIdx.x & 31u;
     const uint32_t g        = lane % kMarchGroup;
@@ -386,27 +389,33 @@ __device__ __forceinline__ void group_expand_runs(float3 d_unit, float3 o, const
         float tk = t;
         for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
         const float t_last = __shfl_sync(0xFFFFFFFFu, tk, group_lo + kMarchGroup - 1u);
-        if (!active) continue;
-        const uint32_t adv = min(min(kMarchGroup, cnt - in_run), n - written);
+        const uint32_t adv = active ? min(min(kMarchGroup, cnt - in_run), n - written) : 0u;
         if (g < adv) {
             const float3 p = ray_point(o, d_unit, tk);
-            float* c       = out + static_cast<uint64_t>(written + g) * 7u;
+            float* c       = stage + lane * 7u;
             c[0] = p.x, c[1] = p.y, c[2] = p.z, c[3] = kConeStep, c[4] = w3.x, c[5] = w3.y, c[6] = w3.z;
         }
-        written += adv;
-        in_run += adv;
-        t = t_last + kConeStep;
-        if (in_run == cnt) {
-            ++r;
-            in_run = 0;
-            if (r == n_runs || written >= n) {
-                active = false;
-            } else {
-                const uint2 run = runs[r];
-                t               = __uint_as_float(run.x);
-                cnt             = run.y;
+        __syncwarp();
+        if (active) {
+            float* dst       = out + static_cast<uint64_t>(written) * 7u;
+            const float* src = stage + group_lo * 7u;
+            for (uint32_t q = g; q < 7u * adv; q += kMarchGroup) dst[q] = src[q];
+            written += adv;
+            in_run += adv;
+            t = t_last + kConeStep;
+            if (in_run == cnt) {
+                ++r;
+                in_run = 0;
+                if (r == n_runs || written >= n) {
+                    active = false;
+                } else {
+                    const uint2 run = runs[r];
+                    t               = __uint_as_float(run.x);
+                    cnt             = run.y;
+                }
             }
         }
+        __syncwarp();
     }
 }
 
