@@ -220,7 +220,10 @@ __device__ __forceinline__ bool setup_ray(const MarchParams& p, uint32_t i, uint
 
 // A group of kMarchGroup lanes per ray, kRaysPerCta rays per CTA.  Count pass: per-ray step
 // counts and per-CTA totals.
-constexpr uint32_t kCtaThreads = 256u;
+#ifndef NGP_MARCH_CTA
+#define NGP_MARCH_CTA 256
+#endif
+constexpr uint32_t kCtaThreads = NGP_MARCH_CTA;
 constexpr uint32_t kRaysPerCta = kCtaThreads / kMarchGroup;
 
 __global__ void __launch_bounds__(kCtaThreads) march_count_kernel(const __grid_constant__ MarchParams p) {
