@@ -471,8 +471,9 @@ inline float skip_voxel(float t, V3 pos, V3 d, V3 inv) {
 
 inline V3 at(V3 o, V3 d, float t) { return {std::fmaf(d.x, t, o.x), std::fmaf(d.y, t, o.y), std::fmaf(d.z, t, o.z)}; }
 
-// March one ray; write up to `limit` records into out (may be null to count only).
-uint32_t march(V3 o, V3 d, float start, const uint8_t* bits, float* out, uint32_t limit) {
+// March one ray; write up to `limit` records into out (may be null to count only).  t_last
+// (optional) receives the t of the last sample.
+uint32_t march(V3 o, V3 d, float start, const uint8_t* bits, float* out, uint32_t limit, float* t_last = nullptr) {
     const V3 inv  = {1.0f / d.x, 1.0f / d.y, 1.0f / d.z};
     const V3 warp = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
     uint32_t n    = 0;
@@ -486,6 +487,7 @@ uint32_t march(V3 o, V3 d, float start, const uint8_t* bits, float* out, uint32_
                 c[0] = p.x, c[1] = p.y, c[2] = p.z, c[3] = kDt, c[4] = warp.x, c[5] = warp.y, c[6] = warp.z;
             }
             ++n;
+            if (t_last != nullptr) *t_last = t;
             t += kDt;
         } else {
             t = skip_voxel(t, p, d, inv);
@@ -527,6 +529,37 @@ uint32_t oracle_march_rays(uint32_t n, const float* rays, int jitter, uint32_t s
         numsteps[2 * i]     = keep ? steps : 0u;
         numsteps[2 * i + 1] = keep ? base : 0u;
         if (keep) march(o, d, start, bits, coords + static_cast<uint64_t>(base) * 7u, steps);
+        base += steps;
+    }
+    return base;
+}
+
+// One segment of a segmented march (test oracle of ngp_march_rays_segment): ray list[k] (or k)
+// marches at most min(cap, 1024 - marched) samples from t_state (or, for the first segment, from
+// tmin + dt/2, the evaluation start of ngp.train.cu:613); t_out[k] = t of its last sample + dt
+// when the segment's cap stopped it short of the ray's 1024-sample allowance, else -1.  The
+// samples of all entries are written in entry order; returns their count.  A sequential march
+// in state t after a sample at t_s continues at t_s + dt, so segments started at t_out
+// concatenate to the single march (the property the segmented render relies on).
+uint32_t oracle_march_segment(uint32_t n, const uint32_t* list, const float* rays, const uint8_t* bits, const float* t_state,
+                              const uint32_t* marched, uint32_t cap, uint32_t* numsteps, float* coords, float* t_out) {
+    uint32_t base = 0;
+    for (uint32_t k = 0; k < n; ++k) {
+        const uint32_t i = list != nullptr ? list[k] : k;
+        const float* q   = rays + static_cast<uint64_t>(i) * 6u;
+        const V3 o = {q[0], q[1], q[2]}, d = {q[3], q[4], q[5]};
+        const uint32_t done  = marched != nullptr ? marched[i] : 0u;
+        const uint32_t left  = 1024u - std::min(done, 1024u);
+        const uint32_t limit = std::min(cap, left);
+        float tmin = 0.0f, t_last = 0.0f;
+        uint32_t steps = 0;
+        if (limit > 0 && hit_cube(o, d, tmin)) {
+            const float start = t_state != nullptr ? t_state[i] : tmin + 0.5f * kDt;
+            steps             = march(o, d, start, bits, coords + static_cast<uint64_t>(base) * 7u, limit, &t_last);
+        }
+        numsteps[2 * k]     = steps;
+        numsteps[2 * k + 1] = base;
+        t_out[k]            = (steps == limit && limit > 0 && limit < left) ? t_last + kDt : -1.0f;
         base += steps;
     }
     return base;

@@ -228,6 +228,23 @@ def _oracle_sampler_methods():
                                            ctypes.c_uint32(sample_limit), _p(numsteps), _p(coords))
         return numsteps, coords, int(total)
 
+    def march_segment(self, rays, bitfield, cap, ray_list=None, t_state=None, marched=None):
+        """One segment of the segmented evaluation march; returns (numsteps [k][2], records, t_out)."""
+        rays = np.ascontiguousarray(rays, np.float32)
+        bits = np.ascontiguousarray(bitfield, np.uint8)
+        lst = None if ray_list is None else np.ascontiguousarray(ray_list, np.uint32)
+        n = rays.shape[0] if lst is None else lst.size
+        ts = None if t_state is None else np.ascontiguousarray(t_state, np.float32)
+        mk = None if marched is None else np.ascontiguousarray(marched, np.uint32)
+        numsteps = np.zeros((n, 2), np.uint32)
+        coords = np.zeros((max(1, n * min(cap, 1024)), 7), np.float32)
+        t_out = np.zeros(n, np.float32)
+        self.lib.oracle_march_segment.restype = ctypes.c_uint32
+        total = self.lib.oracle_march_segment(ctypes.c_uint32(n), None if lst is None else _p(lst), _p(rays), _p(bits),
+                                              None if ts is None else _p(ts), None if mk is None else _p(mk), ctypes.c_uint32(cap),
+                                              _p(numsteps), _p(coords), _p(t_out))
+        return numsteps, coords[:total], t_out
+
     def grid_samples(self, n_uniform, n_nonuniform, ema_step, values):
         values = np.ascontiguousarray(values, np.float32)
         n = n_uniform + n_nonuniform
@@ -253,7 +270,7 @@ def _oracle_sampler_methods():
         arrs[1] = arrs[1].view(np.float16)
         return [arrs[i] for i in (0, 1, 3, 4, 5)]
 
-    for f in (march_rays, grid_samples, grid_update, adam):
+    for f in (march_rays, march_segment, grid_samples, grid_update, adam):
         setattr(Oracle, f.__name__, f)
 
 

@@ -243,3 +243,42 @@ def test_trainer_segmented_eval_identical(ngp):
     a, b = results[False], results[True]
     assert a[0] == b[0] and a[1] == b[1]
     assert abs(a[2] - b[2]) <= 1e-12 * a[2] and abs(a[3] - b[3]) <= 1e-12 * a[3]
+
+
+def test_segment_outputs_match_oracle(ngp, oracle):
+    """Per segment, the library's counts, records and continuation t equal the oracle's
+    restatement bit for bit (first segment, then a listed continuation segment)."""
+    import torch
+
+    occ = np.random.default_rng(7).random(128 ** 3) < 0.3
+    bits_h = np.packbits(occ.reshape(-1, 8), axis=1, bitorder="little").reshape(-1)
+    n, cap0, cap1 = 2048, 9, 40
+    rays_h = workloads.march_rays_config2(n, seed=23)
+    rays, bits = T(rays_h), T(bits_h)
+    coords = torch.zeros((n * cap1, 7), dtype=torch.float32, device="cuda")
+    ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    t_out = torch.zeros(n, dtype=torch.float32, device="cuda")
+    msc = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
+    counters = torch.zeros(4, dtype=torch.int32, device="cuda")
+    ngp.march_rays_segment(rays, bits, coords, ns, t_out, msc, counters, cap0, sample_limit=n * cap1)
+    torch.cuda.synchronize()
+    ons, ocoords, ot = oracle.march_segment(rays_h, bits_h, cap0)
+    g_ns = ns.cpu().numpy().view(np.uint32)
+    assert (g_ns == ons).all() and int(counters[1].item()) == n
+    assert coords.cpu().numpy()[: ocoords.shape[0]].tobytes() == ocoords.tobytes()
+    g_t = t_out.cpu().numpy()
+    assert g_t.tobytes() == ot.tobytes()
+    # continuation of the rays the cap stopped, listed in reverse order
+    lst = np.nonzero(ot >= 0.0)[0][::-1].astype(np.uint32)
+    assert lst.size > 100
+    t_state = np.zeros(n, np.float32)
+    t_state[lst] = ot[lst]
+    marched = np.zeros(n, np.uint32)
+    marched[lst] = cap0
+    ngp.march_rays_segment(rays, bits, coords, ns, t_out, msc, counters, cap1, max_entries=int(lst.size), ray_list=T(lst.view(np.int32)),
+                           t_state=T(t_state), marched=T(marched.view(np.int32)), sample_limit=n * cap1)
+    torch.cuda.synchronize()
+    ons, ocoords, ot2 = oracle.march_segment(rays_h, bits_h, cap1, ray_list=lst, t_state=t_state, marched=marched)
+    assert (ns.cpu().numpy().view(np.uint32)[: lst.size] == ons).all()
+    assert coords.cpu().numpy()[: ocoords.shape[0]].tobytes() == ocoords.tobytes()
+    assert t_out.cpu().numpy()[: lst.size].tobytes() == ot2.tobytes()
