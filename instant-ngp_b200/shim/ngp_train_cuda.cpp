@@ -19,8 +19,9 @@
 //  * samples and compacted samples are placed in ray order (deterministic) instead of the
 //    order of a global atomic;
 //  * parameter gradients are accumulated in fp32 and rounded to the fp16 gradient buffer once;
-//  * evaluation tiles hold up to 2^18 pixels instead of 4096 (allocate_evaluation_buffers sizes
-//    its per-ray buffer accordingly; a tile whose samples exceed the budget is split).
+//  * evaluation marches tiles of 2^16 pixels a segment at a time and stops marching a ray once
+//    its transmittance is spent (the same images; allocate_evaluation_buffers sizes its per-ray
+//    buffer for the larger tiles); network outputs behind a ray's stopping point are not written.
 #include <algorithm>
 #include <chrono>
 #include <cmath>
@@ -42,7 +43,10 @@ constexpr uint32_t kGridCells       = 128u * 128u * 128u;
 constexpr uint32_t kSampleFloats    = 7u;
 constexpr uint32_t kRayFloats       = 6u;
 constexpr uint32_t kEvalTile        = 1u << 18;
-constexpr uint32_t kMinEvalTile     = 4096u;
+// Segmented evaluation (as the library's trainer renders): tiles of 2^16 pixel rays, marched
+// 64 samples per ray first (MAX_SAMPLES / tile, so the first segment always fits), then 128, then
+// the rest; rays stop being marched once their transmittance is spent.
+constexpr uint32_t kSegTile         = 1u << 16;
 constexpr uint32_t kLrTableCapacity = 1u << 20;
 constexpr uint32_t kLrTableBlock    = 4096u;
 constexpr float kLossScale          = 128.0f;
@@ -81,6 +85,14 @@ struct Context {
     float* grid_partial     = nullptr;
     float* eval_rays        = nullptr;  // [kEvalTile][6]
     float* lr_table         = nullptr;
+    // segmented evaluation: per-ray state carried between segments, row list of the evaluation
+    float* seg_tout         = nullptr;  // [kSegTile]
+    float* seg_tstate       = nullptr;  // [kSegTile]
+    uint32_t* seg_marched   = nullptr;  // [kSegTile]
+    float* seg_state        = nullptr;  // [kSegTile][4]
+    uint32_t* seg_lists     = nullptr;  // [2][kSegTile]
+    uint32_t* seg_counters  = nullptr;  // [4]
+    uint32_t* eval_rows     = nullptr;  // [MAX_SAMPLES]
     uint32_t lr_table_len   = 0;
     uint32_t adam_calls     = 0;
 };
@@ -110,9 +122,18 @@ Context* context() {
         device_alloc(c->grid_partial, ngp_density_grid_partials(), "cudaMalloc grid partial sums");
         device_alloc(c->eval_rays, static_cast<size_t>(kEvalTile) * kRayFloats, "cudaMalloc evaluation rays");
         device_alloc(c->lr_table, kLrTableCapacity, "cudaMalloc adam rate table");
+        device_alloc(c->seg_tout, kSegTile, "cudaMalloc segment t");
+        device_alloc(c->seg_tstate, kSegTile, "cudaMalloc segment ray t");
+        device_alloc(c->seg_marched, kSegTile, "cudaMalloc segment ray counts");
+        device_alloc(c->seg_state, static_cast<size_t>(kSegTile) * 4u, "cudaMalloc segment ray state");
+        device_alloc(c->seg_lists, static_cast<size_t>(kSegTile) * 2u, "cudaMalloc segment lists");
+        device_alloc(c->seg_counters, 4, "cudaMalloc segment counters");
+        device_alloc(c->eval_rows, cfg::MAX_SAMPLES, "cudaMalloc evaluation rows");
     } catch (...) {
         cudaFree(c->march_scratch), cudaFree(c->loss_scratch), cudaFree(c->mlp_scratch), cudaFree(c->grid_grad), cudaFree(c->grid_partial);
         cudaFree(c->eval_rays), cudaFree(c->lr_table);
+        cudaFree(c->seg_tout), cudaFree(c->seg_tstate), cudaFree(c->seg_marched), cudaFree(c->seg_state), cudaFree(c->seg_lists),
+            cudaFree(c->seg_counters), cudaFree(c->eval_rows);
         delete c;
         throw;
     }
@@ -124,6 +145,8 @@ void destroy_context(Context* c) {
     if (c == nullptr) return;
     cudaFree(c->march_scratch), cudaFree(c->loss_scratch), cudaFree(c->mlp_scratch), cudaFree(c->grid_grad), cudaFree(c->grid_partial);
     cudaFree(c->eval_rays), cudaFree(c->lr_table);
+    cudaFree(c->seg_tout), cudaFree(c->seg_tstate), cudaFree(c->seg_marched), cudaFree(c->seg_state), cudaFree(c->seg_lists),
+        cudaFree(c->seg_counters), cudaFree(c->eval_rows);
     if (g_context == c) g_context = nullptr;
     delete c;
 }
@@ -316,30 +339,39 @@ void run_evaluation(const std::uint8_t* evaluation_pixels, const float* evaluati
     check_cuda(cudaMemset(evaluation_overflow_counter, 0, sizeof(uint32_t)), "cudaMemset evaluation overflow counter");
     for (uint32_t k = 0; k < evaluation_image_count; ++k) {
         const uint32_t image = evaluation_image_begin + k;
-        uint32_t tile        = kEvalTile;
-        for (uint32_t offset = 0; offset < total;) {
-            const uint32_t n = std::min(tile, total - offset);
+        for (uint32_t offset = 0; offset < total; offset += kSegTile) {
+            const uint32_t n = std::min(kSegTile, total - offset);
             check(ngp_make_eval_rays(evaluation_camera, image, width, height, focal_x, focal_y, principal_x, principal_y, offset, n, c->eval_rays, nullptr),
                   "evaluation rays");
-            check(ngp_march_rays(n, c->eval_rays, 0, 0, occupancy, cfg::MAX_SAMPLES, sample_coords, evaluation_numsteps, c->march_scratch,
-                                 evaluation_sample_counter, nullptr),
-                  "evaluation march");
-            uint32_t used = 0;
-            check_cuda(cudaMemcpy(&used, evaluation_sample_counter, sizeof(used), cudaMemcpyDeviceToHost), "cudaMemcpy evaluation sample counter");
-            if (used > cfg::MAX_SAMPLES) {  // the tile's samples exceed the budget: split it
-                if (tile <= kMinEvalTile) throw std::runtime_error{"Evaluation sample budget overflowed."};
-                tile /= 4u;
-                continue;
+            uint32_t max_entries = n;
+            for (uint32_t seg = 0;; ++seg) {
+                const bool first      = seg == 0;
+                const uint32_t* list  = first ? nullptr : c->seg_lists + static_cast<size_t>((seg - 1u) & 1u) * kSegTile;
+                const uint32_t* n_dev = first ? nullptr : c->seg_counters + 2u + ((seg - 1u) & 1u);
+                const uint32_t cap    = seg == 0 ? cfg::MAX_SAMPLES / kSegTile : (seg == 1 ? 128u : 1024u);
+                check(ngp_march_rays_segment(max_entries, n_dev, list, c->eval_rays, occupancy, first ? nullptr : c->seg_tstate,
+                                             first ? nullptr : c->seg_marched, cap, cfg::MAX_SAMPLES, sample_coords, evaluation_numsteps, c->seg_tout,
+                                             c->march_scratch, c->seg_counters, nullptr),
+                      "evaluation march");
+                uint32_t h[4] = {};
+                check_cuda(cudaMemcpy(h, c->seg_counters, sizeof(h), cudaMemcpyDeviceToHost), "cudaMemcpy evaluation counters");
+                const uint32_t complete = h[1];
+                if (complete == 0) break;  // no rays left in this tile
+                const uint32_t used = std::min(h[0], cfg::MAX_SAMPLES);
+                if (used > 0)
+                    check(ngp_eval_network_progressive(complete, &c->layout, params, sample_coords, used, evaluation_numsteps, density_input, used,
+                                                       network_output, c->eval_rows, c->loss_scratch, c->loss_scratch_bytes, nullptr),
+                          "evaluation network");
+                uint32_t* next_count = c->seg_counters + 2u + (seg & 1u);
+                check_cuda(cudaMemset(next_count, 0, sizeof(uint32_t)), "cudaMemset evaluation list count");
+                check(ngp_eval_composite_segment(max_entries, n_dev, c->seg_counters + 1, list, evaluation_numsteps, sample_coords, network_output,
+                                                 c->seg_tout, c->seg_tstate, c->seg_marched, c->seg_state,
+                                                 c->seg_lists + static_cast<size_t>(seg & 1u) * kSegTile, next_count, offset, image, width, height,
+                                                 evaluation_pixels, evaluation_loss_sum, writes_comparison ? test_comparison_pixels : nullptr, nullptr,
+                                                 nullptr),
+                      "evaluation compositing");
+                if (!first) max_entries = h[2u + ((seg - 1u) & 1u)];
             }
-            if (used > 0) {
-                const uint32_t g      = cfg::NETWORK_BATCH_GRANULARITY;
-                const uint32_t padded = std::min((used + g - 1u) / g * g, cfg::MAX_SAMPLES);
-                run_network(padded, sample_coords, params, density_input, network_output);
-            }
-            check(ngp_eval_composite(n, offset, image, width, height, evaluation_pixels, evaluation_numsteps, sample_coords, network_output,
-                                     evaluation_loss_sum, writes_comparison ? test_comparison_pixels : nullptr, nullptr, nullptr),
-                  "evaluation compositing");
-            offset += n;
         }
     }
     check_cuda(cudaDeviceSynchronize(), "evaluation synchronization");
