@@ -176,9 +176,11 @@ PHASE_BYTES = {
     # the densities evaluated (encoding 12 B in + 64 B out, density 64 B in + 2 B out) cover only the
     # samples in front of each ray's stopping point, and the kept ones are compacted (92 B each)
     "inference_compact": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "encode_forward_points_kernel + mlp_forward_kernel<density> + keep/compact",
-                          # profiles/*__train_config3.md: DRAM read + write of the phase's launches
-                          # (two rounds of encode, density, keep and list kernels, then the copy) in
-                          # one step of 1,393,551 marched samples
+                          # DRAM read + write of the phase's launches in one ncu-captured step of
+                          # 1,393,551 marched samples (two rounds of encode, density, keep and list
+                          # kernels, then the compaction copy that the selection flow has since
+                          # replaced; the selection flow's step in profiles/*__train_config3.md
+                          # reads and writes 176 MB)
                           "ncu_dram_bytes_per_unit": 218.9e6 / 1393551},
     # 12 B rays in + 28 B records out per sample (dominant), 8 B per ray of counts
     "march": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "march_count_kernel + march_write_kernel"},
