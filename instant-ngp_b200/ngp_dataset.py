@@ -142,7 +142,7 @@ def load_dd_nerf(path, scene_scale: float = DEFAULT_SCENE_SCALE) -> dict:
         splits["test" if k == 0 else "validation" if k == 1 else "train"].append(frame)
     for name, frames in splits.items():
         if not frames:
-            raise RuntimeError(f"DD-NeRF split produced no {name} frames.")
+            raise RuntimeError(f"DD-NeRF split produced no {'training' if name == 'train' else name} frames.")
     return {name: _split(frames, name) for name, frames in splits.items()} | {"scene_scale": float(np.float32(scene_scale))}
 
 
