@@ -307,8 +307,7 @@ def cpu_baseline_train(args, pre_compaction: int, budget_s: float = 4.0) -> dict
     samples of each part of a config-3 training step, combined into the time of one step at this
     run's per-step counts: marching of every pre-compaction sample, the encoding + full network
     forward on all of them (the reference's inference pass), the encoding + network forward and
-    backward of the 2^18-sample batch, and Adam over every parameter.  Parts without a threaded
-    oracle are divided by the core count (ideal scaling), so the rate is an upper bound."""
+    backward of the 2^18-sample batch, and Adam over every parameter, each on all host cores."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import ngp_b200 as ngp
     import workloads
@@ -336,22 +335,22 @@ def cpu_baseline_train(args, pre_compaction: int, budget_s: float = 4.0) -> dict
     # encoding + full network forward (threaded oracle)
     fwd = rate(lambda: ora.mlp_forward(params, ora.encode_forward(layt, coords, table, 2, mode=0, threads=cores), coords, threads=cores), n)
 
-    # network backward (single-threaded oracle) + encoding backward (threaded)
+    # network backward + encoding backward
     x = ora.encode_forward(layt, coords, table, 2, mode=0, threads=cores)
-    mlp_bwd = rate(lambda: ora.mlp_backward(params, x, coords, dy), n) * cores
+    mlp_bwd = rate(lambda: ora.mlp_backward(params, x, coords, dy, threads=cores), n)
     enc_bwd = rate(lambda: ora.encode_backward(layt, coords, dy_enc, 2, threads=cores), n)
-    # marching (single-threaded oracle), per emitted sample
+    # marching, per emitted sample
     vals = workloads.blob_grid_values(workloads.gaussian_blob_density())
     bits = np.packbits((vals > 0.01).reshape(-1, 8), axis=1, bitorder="little").reshape(-1)
-    rays = workloads.march_rays_config2(512, seed=3)
-    per_call = ora.march_rays(rays, bits)[2]
-    march = rate(lambda: ora.march_rays(rays, bits), per_call) * cores
-    # Adam (single-threaded oracle), every parameter touched
+    rays = workloads.march_rays_config2(4096, seed=3)
+    per_call = ora.march_rays_mt(rays, bits, cores)[2]
+    march = rate(lambda: ora.march_rays_mt(rays, bits, cores), per_call)
+    # Adam, every parameter touched
     m_p = 1 << 20
     master = np.random.default_rng(1).uniform(-1e-4, 1e-4, m_p).astype(np.float32)
     adam_state = [master, master.astype(np.float16), np.full(m_p, 1e-3, np.float32), np.zeros(m_p, np.float32), np.zeros(m_p, np.float32),
                   np.zeros(m_p, np.uint32)]
-    adam = rate(lambda: ora.adam(10240, *adam_state), m_p) * cores
+    adam = rate(lambda: ora.adam(10240, *adam_state, threads=cores), m_p)
 
     n_params = 12_206_480
     t_step = (pre_compaction / march + pre_compaction / fwd + BATCH / fwd + BATCH / mlp_bwd + BATCH / enc_bwd + n_params / adam)
@@ -359,7 +358,7 @@ def cpu_baseline_train(args, pre_compaction: int, budget_s: float = 4.0) -> dict
             "sample": (f"one config-3 step ({pre_compaction} marched samples, {BATCH} batch samples, {n_params} parameters) timed part by "
                        f"part on bounded samples of the scalar oracle ({budget_s:.0f} s each): march {march / 1e6:.2f} M samples/s, "
                        f"encode + network forward {fwd / 1e6:.2f} M/s, network backward {mlp_bwd / 1e6:.2f} M/s, encode backward "
-                       f"{enc_bwd / 1e6:.2f} M/s, Adam {adam / 1e6:.1f} M params/s; single-threaded parts scaled by {cores} cores"),
+                       f"{enc_bwd / 1e6:.2f} M/s, Adam {adam / 1e6:.1f} M params/s; every part on {cores} host threads"),
             "step_s": round(t_step, 3)}
 
 

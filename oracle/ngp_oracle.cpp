@@ -359,10 +359,14 @@ void oracle_density_forward(uint32_t n, const uint16_t* params, const uint16_t* 
 // Network backward (backward_network, ngp.train.cu:1686-1903) for n rows:
 // dy fp16 [n][16] (ch 0-2 rgb, ch 3 density; others ignored as extract_rgb_gradients does)
 // -> dx fp16 [32][dx_stride] (gradient w.r.t. the encoded input) and dW fp64 [10240] (summed).
-void oracle_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords, uint32_t coord_stride,
-                         const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, double* dW) {
+}  // extern "C"
+
+namespace {
+// Rows [begin, end) of the network backward; dW accumulates in row order.
+void mlp_backward_rows(uint32_t begin, uint32_t end, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords,
+                       uint32_t coord_stride, const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, double* dW) {
     const uint16_t* P = params;
-    for (uint32_t i = 0; i < n; ++i) {
+    for (uint32_t i = begin; i < end; ++i) {
         float xr[32];
         for (int k = 0; k < 32; ++k) xr[k] = h2f(x[static_cast<uint64_t>(k) * x_stride + i]);
         RowActs a;
@@ -408,6 +412,31 @@ void oracle_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, 
         for (int j = 0; j < 64; ++j)
             for (int k = 0; k < 32; ++k) dW[kWdIn + j * 32 + k] += static_cast<double>(dhd[j]) * a.x[k];
     }
+}
+}  // namespace
+
+extern "C" {
+
+void oracle_mlp_backward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords, uint32_t coord_stride,
+                         const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, double* dW) {
+    mlp_backward_rows(0, n, params, x, x_stride, coords, coord_stride, dy, dx, dx_stride, dW);
+}
+
+// The same over `threads` host threads (CPU baseline timing): each thread sums its rows' weight
+// gradients, the partial sums are added in thread order.
+void oracle_mlp_backward_mt(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const float* coords, uint32_t coord_stride,
+                            const uint16_t* dy, uint16_t* dx, uint32_t dx_stride, double* dW, int threads) {
+    const int t_count = std::max(1, threads);
+    std::vector<std::vector<double>> partial(static_cast<size_t>(t_count), std::vector<double>(10240, 0.0));
+    std::vector<std::thread> pool;
+    const uint32_t chunk = (n + t_count - 1) / t_count;
+    for (int t = 0; t < t_count; ++t) {
+        const uint32_t b = std::min(n, t * chunk), e = std::min(n, b + chunk);
+        pool.emplace_back([&, t, b, e] { mlp_backward_rows(b, e, params, x, x_stride, coords, coord_stride, dy, dx, dx_stride, partial[t].data()); });
+    }
+    for (auto& th : pool) th.join();
+    for (int t = 0; t < t_count; ++t)
+        for (int k = 0; k < 10240; ++k) dW[k] += partial[t][k];
 }
 
 }  // extern "C"
@@ -534,6 +563,39 @@ uint32_t oracle_march_rays(uint32_t n, const float* rays, int jitter, uint32_t s
     return base;
 }
 
+// oracle_march_rays over `threads` host threads (CPU baseline timing): per-ray counts in
+// parallel, their prefix sum, then the records in parallel; the same output.
+uint32_t oracle_march_rays_mt(uint32_t n, const float* rays, const uint8_t* bits, uint32_t sample_limit, uint32_t* numsteps, float* coords,
+                              int threads) {
+    std::vector<uint32_t> steps(n, 0u);
+    std::vector<float> start(n, 0.0f);
+    parallel_for(n, threads, [&](uint32_t b, uint32_t e) {
+        for (uint32_t i = b; i < e; ++i) {
+            const float* q = rays + static_cast<uint64_t>(i) * 6u;
+            const V3 o = {q[0], q[1], q[2]}, d = {q[3], q[4], q[5]};
+            float tmin = 0.0f;
+            if (!hit_cube(o, d, tmin)) continue;
+            start[i] = tmin + 0.5f * kDt;
+            steps[i] = march(o, d, start[i], bits, nullptr, 1024u);
+        }
+    }, 64);
+    uint32_t base = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const bool keep     = steps[i] > 0 && base + steps[i] <= sample_limit;
+        numsteps[2 * i]     = keep ? steps[i] : 0u;
+        numsteps[2 * i + 1] = keep ? base : 0u;
+        base += steps[i];
+    }
+    parallel_for(n, threads, [&](uint32_t b, uint32_t e) {
+        for (uint32_t i = b; i < e; ++i) {
+            if (numsteps[2 * i] == 0u) continue;
+            const float* q = rays + static_cast<uint64_t>(i) * 6u;
+            march({q[0], q[1], q[2]}, {q[3], q[4], q[5]}, start[i], bits, coords + static_cast<uint64_t>(numsteps[2 * i + 1]) * 7u, numsteps[2 * i]);
+        }
+    }, 64);
+    return base;
+}
+
 // One segment of a segmented march (test oracle of ngp_march_rays_segment): ray list[k] (or k)
 // marches at most min(cap, 1024 - marched) samples from t_state (or, for the first segment, from
 // tmin + dt/2, the evaluation start of ngp.train.cu:613); t_out[k] = t of its last sample + dt
@@ -611,10 +673,12 @@ uint32_t oracle_grid_update(float* values, const float* scratch, float decay, fl
     return count;
 }
 
-// Adam on fp32 gradients (ngp.train.cu:1261-1280), fp64-free restatement in fp32 with libm.
-void oracle_adam(uint32_t n, uint32_t n_mlp, float lr, float b1, float b2, float eps, float l2, float loss_scale, float* master, uint16_t* params,
-                 const float* grads, float* m, float* v, uint32_t* steps) {
-    for (uint32_t i = 0; i < n; ++i) {
+// Adam on fp32 gradients (ngp.train.cu:1261-1280), fp64-free restatement in fp32 with libm;
+// parameters are independent, so `threads` (oracle_adam_mt) changes nothing but the time.
+void oracle_adam_mt(uint32_t n, uint32_t n_mlp, float lr, float b1, float b2, float eps, float l2, float loss_scale, float* master, uint16_t* params,
+                    const float* grads, float* m, float* v, uint32_t* steps, int threads) {
+    parallel_for(n, threads, [&](uint32_t b, uint32_t e) {
+    for (uint32_t i = b; i < e; ++i) {
         float g = grads[i] / loss_scale;
         if (i >= n_mlp && g == 0.0f) continue;
         const float w = master[i];
@@ -626,6 +690,12 @@ void oracle_adam(uint32_t n, uint32_t n_mlp, float lr, float b1, float b2, float
         master[i]        = w - lrt * m[i] / (std::sqrt(v[i]) + eps);
         params[i]        = f2h(master[i]);
     }
+    });
+}
+
+void oracle_adam(uint32_t n, uint32_t n_mlp, float lr, float b1, float b2, float eps, float l2, float loss_scale, float* master, uint16_t* params,
+                 const float* grads, float* m, float* v, uint32_t* steps) {
+    oracle_adam_mt(n, n_mlp, lr, b1, b2, eps, l2, loss_scale, master, params, grads, m, v, steps, 1);
 }
 
 }  // extern "C"

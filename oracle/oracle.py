@@ -197,7 +197,7 @@ def _oracle_mlp_methods():
         self.lib.oracle_density_forward(ctypes.c_uint32(n), _p(params), _p(x), ctypes.c_uint32(x.shape[1]), _p(out))
         return out.view(np.float16)
 
-    def mlp_backward(self, params, x, coords, dy):
+    def mlp_backward(self, params, x, coords, dy, threads: int = 1):
         params = np.ascontiguousarray(params.view(np.uint16))
         x = np.ascontiguousarray(x.view(np.uint16))
         dy = np.ascontiguousarray(dy.view(np.uint16))
@@ -205,8 +205,12 @@ def _oracle_mlp_methods():
         n = coords.shape[0]
         dx = np.zeros((32, n), np.uint16)
         dw = np.zeros(10240, np.float64)
-        self.lib.oracle_mlp_backward(ctypes.c_uint32(n), _p(params), _p(x), ctypes.c_uint32(x.shape[1]), _p(coords),
-                                     ctypes.c_uint32(coords.shape[1]), _p(dy), _p(dx), ctypes.c_uint32(n), _p(dw))
+        if threads <= 1:
+            self.lib.oracle_mlp_backward(ctypes.c_uint32(n), _p(params), _p(x), ctypes.c_uint32(x.shape[1]), _p(coords),
+                                         ctypes.c_uint32(coords.shape[1]), _p(dy), _p(dx), ctypes.c_uint32(n), _p(dw))
+        else:  # weight gradients summed per thread, then in thread order (CPU baseline timing)
+            self.lib.oracle_mlp_backward_mt(ctypes.c_uint32(n), _p(params), _p(x), ctypes.c_uint32(x.shape[1]), _p(coords),
+                                            ctypes.c_uint32(coords.shape[1]), _p(dy), _p(dx), ctypes.c_uint32(n), _p(dw), ctypes.c_int(threads))
         return dx.view(np.float16), dw
 
     for f in (sh_encode, mlp_forward, density_forward, mlp_backward):
@@ -226,6 +230,19 @@ def _oracle_sampler_methods():
         self.lib.oracle_march_rays.restype = ctypes.c_uint32
         total = self.lib.oracle_march_rays(ctypes.c_uint32(n), _p(rays), ctypes.c_int(int(jitter)), ctypes.c_uint32(step), _p(bits),
                                            ctypes.c_uint32(sample_limit), _p(numsteps), _p(coords))
+        return numsteps, coords, int(total)
+
+    def march_rays_mt(self, rays, bitfield, threads: int, sample_limit=1 << 22):
+        """Evaluation-rule march (start tmin + dt/2) over `threads` host threads; same output as
+        march_rays(jitter=False)."""
+        rays = np.ascontiguousarray(rays, np.float32)
+        bits = np.ascontiguousarray(bitfield, np.uint8)
+        n = rays.shape[0]
+        numsteps = np.zeros((n, 2), np.uint32)
+        coords = np.zeros((min(sample_limit, n * 1024), 7), np.float32)
+        self.lib.oracle_march_rays_mt.restype = ctypes.c_uint32
+        total = self.lib.oracle_march_rays_mt(ctypes.c_uint32(n), _p(rays), _p(bits), ctypes.c_uint32(sample_limit), _p(numsteps), _p(coords),
+                                              ctypes.c_int(threads))
         return numsteps, coords, int(total)
 
     def march_segment(self, rays, bitfield, cap, ray_list=None, t_state=None, marched=None):
@@ -263,14 +280,14 @@ def _oracle_sampler_methods():
         cnt = self.lib.oracle_grid_update(_p(values), _p(scratch), ctypes.c_float(decay), _p(mean), _p(bits))
         return values, float(mean[0]), bits, int(cnt)
 
-    def adam(self, n_mlp, master, params, grads, m, v, steps, lr=1e-2, b1=0.9, b2=0.99, eps=1e-15, l2=1e-6, loss_scale=128.0):
+    def adam(self, n_mlp, master, params, grads, m, v, steps, lr=1e-2, b1=0.9, b2=0.99, eps=1e-15, l2=1e-6, loss_scale=128.0, threads: int = 1):
         arrs = [np.array(a) for a in (master, params.view(np.uint16), grads, m, v, steps)]
-        self.lib.oracle_adam(ctypes.c_uint32(arrs[0].size), ctypes.c_uint32(n_mlp), ctypes.c_float(lr), ctypes.c_float(b1), ctypes.c_float(b2),
-                             ctypes.c_float(eps), ctypes.c_float(l2), ctypes.c_float(loss_scale), *[_p(a) for a in arrs])
+        self.lib.oracle_adam_mt(ctypes.c_uint32(arrs[0].size), ctypes.c_uint32(n_mlp), ctypes.c_float(lr), ctypes.c_float(b1), ctypes.c_float(b2),
+                                ctypes.c_float(eps), ctypes.c_float(l2), ctypes.c_float(loss_scale), *[_p(a) for a in arrs], ctypes.c_int(threads))
         arrs[1] = arrs[1].view(np.float16)
         return [arrs[i] for i in (0, 1, 3, 4, 5)]
 
-    for f in (march_rays, march_segment, grid_samples, grid_update, adam):
+    for f in (march_rays, march_rays_mt, march_segment, grid_samples, grid_update, adam):
         setattr(Oracle, f.__name__, f)
 
 

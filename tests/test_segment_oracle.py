@@ -74,3 +74,26 @@ def test_segments_match_single_march_scattered_grid(oracle, caps):
     assert total > 512 * 64  # long rays: several segments each
     per_ray, _ = segmented(oracle, rays, bits, caps)
     check(per_ray, ns, coords)
+
+
+def test_threaded_oracle_variants_match(oracle):
+    """The threaded oracle paths the CPU baseline times give the single-threaded results."""
+    vals = workloads.blob_grid_values(workloads.gaussian_blob_density())
+    bits = np.packbits((vals > 0.01).reshape(-1, 8), axis=1, bitorder="little").reshape(-1)
+    rays = workloads.march_rays_config2(3000, seed=4)
+    a = oracle.march_rays(rays, bits, sample_limit=150000)
+    b = oracle.march_rays_mt(rays, bits, 4, sample_limit=150000)
+    assert a[2] == b[2] and (a[0] == b[0]).all() and a[1].tobytes() == b[1].tobytes()
+    x, coords, dy = workloads.mlp_inputs(3000, seed=1)
+    params = workloads.xavier_mlp_params(2)
+    dx1, dw1 = oracle.mlp_backward(params, x, coords, dy)
+    dx4, dw4 = oracle.mlp_backward(params, x, coords, dy, threads=4)
+    assert dx1.tobytes() == dx4.tobytes()
+    np.testing.assert_allclose(dw4, dw1, rtol=1e-12, atol=1e-12)
+    rng = np.random.default_rng(0)
+    n = 50000
+    state = [rng.uniform(-1, 1, n).astype(np.float32), rng.uniform(-1, 1, n).astype(np.float16), rng.normal(size=n).astype(np.float32),
+             np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.uint32)]
+    r1 = oracle.adam(10240, *state)
+    r4 = oracle.adam(10240, *state, threads=4)
+    assert all(p.tobytes() == q.tobytes() for p, q in zip(r1, r4))
