@@ -474,6 +474,12 @@ NGP_API int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint32_
  * by marching every occupied step of each tile before the network runs (0).  Both give the same
  * images bit for bit.  run_evaluation (ngp.train.cu:1597-1658). */
 NGP_API int ngp_trainer_set_segmented_eval(ngp_trainer* t, int enabled);
+/* The adaptive batch of the next step from this step's counts (InstantNGP::train,
+ * ngp.train.cpp:132-133): inference samples = pre-compaction count (at most MAX_SAMPLES) rounded
+ * up to 128; rays = rays * 2^18 / compacted count (at most 2^18), rounded up to 128, within
+ * [128, 2^18].  Host-only arithmetic. */
+NGP_API void ngp_adaptive_batch(uint32_t rays_per_batch, uint32_t measured_before, uint32_t measured, uint32_t* next_rays,
+                                uint32_t* next_inference_samples);
 NGP_API uint32_t ngp_trainer_param_count(const ngp_trainer* t);
 /* fp32 master parameters [MLP | grid] to / from the host (export_weights / load_weights;
  * loading resets the optimizer and is allowed only before training, ngp.train.cpp:312). */

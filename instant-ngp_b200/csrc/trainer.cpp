@@ -386,11 +386,9 @@ int train_step(ngp_trainer* t, bool premarch_next) {
         cudaMemcpy(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost);
         return fail(NGP_ERR_STATE, "Training stopped unexpectedly. density_grid_occupied_cells=" + std::to_string(t->occupied_cells));
     }
-    const uint32_t g           = kBatchGranule;
     const uint32_t next_step   = t->step + 1u;
-    const uint32_t next_infer  = ((std::min(t->measured_before, kMaxSamples) + g - 1u) / g) * g;
-    const uint64_t want        = std::min<uint64_t>((static_cast<uint64_t>(t->rays_per_batch) * kNetworkBatch) / t->measured, kNetworkBatch);
-    const uint32_t next_rays   = std::min(std::max(static_cast<uint32_t>((want + g - 1u) / g * g), g), kNetworkBatch);
+    uint32_t next_rays = 0, next_infer = 0;
+    ngp_adaptive_batch(t->rays_per_batch, t->measured_before, t->measured, &next_rays, &next_infer);
     const bool premarch        = NGP_OVERLAP_MARCH && premarch_next && !t->profiling && !grid_update_due(next_step);
     if (premarch) {
         // the march writes the other set of march outputs, last read by the previous step (which
@@ -754,6 +752,18 @@ extern "C" int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint
     if (st == NGP_OK) st = check_cuda(cudaStreamSynchronize(t->stream), "render");
     free_split(s);
     return st;
+}
+
+extern "C" void ngp_adaptive_batch(uint32_t rays_per_batch, uint32_t measured_before, uint32_t measured, uint32_t* next_rays,
+                                   uint32_t* next_inference_samples) {
+    const uint32_t g = kBatchGranule;
+    *next_inference_samples = ((std::min(measured_before, kMaxSamples) + g - 1u) / g) * g;
+    if (measured == 0u) {  // no step follows (the trainer stops); keep the batch
+        *next_rays = rays_per_batch;
+        return;
+    }
+    const uint64_t want = std::min<uint64_t>((static_cast<uint64_t>(rays_per_batch) * kNetworkBatch) / measured, kNetworkBatch);
+    *next_rays          = std::min(std::max(static_cast<uint32_t>((want + g - 1u) / g * g), g), kNetworkBatch);
 }
 
 extern "C" int ngp_trainer_set_segmented_eval(ngp_trainer* t, int enabled) {

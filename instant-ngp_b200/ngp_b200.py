@@ -70,6 +70,13 @@ def _check(status: int, what: str) -> None:
         raise RuntimeError(f"{what} failed (status {status}): {msg}")
 
 
+def adaptive_batch(rays_per_batch: int, measured_before: int, measured: int) -> tuple[int, int]:
+    """(next rays per batch, next inference sample count) of the adaptive batch rule."""
+    r, i = ctypes.c_uint32(0), ctypes.c_uint32(0)
+    lib().ngp_adaptive_batch(_u32(rays_per_batch), _u32(measured_before), _u32(measured), ctypes.byref(r), ctypes.byref(i))
+    return int(r.value), int(i.value)
+
+
 def kernel_launch_count() -> int:
     """Kernel launches made by the library in this process so far."""
     lib().ngp_kernel_launch_count.restype = ctypes.c_uint64

@@ -61,3 +61,4 @@ def test_pcg32_advance_is_skip(oracle):
     u2, f2 = oracle.pcg32(1337, 1, 37, 63)
     assert (u[37:] == u2).all() and (f[37:] == f2).all()
     assert ((f >= 0) & (f < 1)).all()
+
