@@ -130,4 +130,24 @@ int probe_lifecycle(std::uint32_t w, std::uint32_t h, std::uint32_t n_train, con
     }
 }
 
+// Construction errors surface as std::runtime_error with the library's message (the reference's
+// constructor throws on a failed device set-up): an empty dataset, or no usable device.
+int probe_construct_error(int empty_dataset, char* err, std::size_t en) {
+    ngp::b200::dataset::NGPDataset ds;
+    if (!empty_dataset) {
+        ngp::b200::dataset::NGPDataset::Frame f;
+        f.width = f.height = 4;
+        f.rgba.assign(64, 255);
+        f.focal_x = f.focal_y = 4.0f, f.principal_x = f.principal_y = 2.0f;
+        f.camera = {1, 0, 0, 0, 1, 0, 0, 0, 1, 0.5f, 0.5f, 2.0f};
+        ds.train = {f, f};
+    }
+    try {
+        ngp::b200::train::InstantNGP model{ds};
+        return 0;
+    } catch (const std::runtime_error& e) {
+        return fail(err, en, e.what());
+    }
+}
+
 }  // extern "C"

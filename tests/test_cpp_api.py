@@ -123,6 +123,17 @@ def test_png_decodes_to_the_pixels(probe, tmp_path, w, h):
     assert (_decode_png(path.read_bytes()) == rgb).all()
 
 
+def test_constructor_errors_are_runtime_errors(probe):
+    err = _err()
+    assert probe.probe_construct_error(1, err, ctypes.c_size_t(1024)) == 1
+    assert b"no training images" in err.value
+    import torch
+
+    if not torch.cuda.is_available():  # no device: the trainer's set-up fails and says why
+        assert probe.probe_construct_error(0, err, ctypes.c_size_t(1024)) == 1
+        assert err.value
+
+
 @pytest.mark.gpu
 def test_instant_ngp_lifecycle_through_cpp_api(probe, tmp_path):
     scene = workloads.procedural_dataset(n_train=8, n_test=2, width=96, height=96, seed=17)
