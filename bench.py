@@ -167,63 +167,114 @@ DENSITY_FWD_FLOP = 6144
 COMPACTED_ROWS = BATCH + 1024
 
 
-# Algorithmic HBM bytes per unit of each training-step phase (inputs read once, outputs written
-# once; table gathers and atomics are L1/L2-served and counted separately), and the DRAM bytes
-# per unit that one ncu capture of the phase's main kernel measured (the profiles/ summaries of
-# the config-3 step: DRAM read + write of that launch / units it processed).
-PHASE_BYTES = {
-    # per marched sample: its record is read once (28 B) to decide how far the ray keeps samples;
-    # the densities evaluated (encoding 12 B in + 64 B out, density 64 B in + 2 B out) cover only the
-    # samples in front of each ray's stopping point, and the kept ones are compacted (92 B each)
-    "inference_compact": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "encode_forward_points_kernel + mlp_forward_kernel<density> + keep/compact",
-                          # DRAM read + write of the phase's launches in one ncu-captured step of
-                          # 1,393,551 marched samples (two rounds of encode, density, keep and list
-                          # kernels, then the compaction copy that the selection flow has since
-                          # replaced; the selection flow's step in profiles/*__train_config3.md
-                          # reads and writes 176 MB)
-                          "ncu_dram_bytes_per_unit": 218.9e6 / 1393551},
-    # 12 B rays in + 28 B records out per sample (dominant), 8 B per ray of counts
-    "march": {"unit": "pre-compaction sample", "bytes": 28, "kernel": "march_count_kernel + march_write_kernel"},
-    "encode_bwd": {"unit": "batch sample", "bytes": 12 + 64, "l2_atomic_bytes": 16 * 8 * 2 * 4, "kernel": "encode_backward_kernel"},
-    "adam": {"unit": "parameter", "bytes": 40, "kernel": "adam_kernel"},
-    "mlp_fwd_loss_pad": {"unit": "batch sample", "bytes": 64 + 32 + 28 + 32, "kernel": "mlp_forward_kernel + loss_compacted_kernel"},
-    "grid_update": {"unit": "grid cell", "bytes": 16, "kernel": "density grid kernels"},
+# Algorithmic work per unit of the kernels that can dominate the training step, as they are timed
+# by the trainer's profiling events (kernel = the launches between two events).  Bytes are HBM
+# bytes that must move (inputs read once, outputs written once); table gathers are L2-served and
+# reported separately against the measured L2 read rate.
+GRID_KERNELS = {
+    # encode_forward_points_kernel over the grid-update samples: x, y, z of each 28-byte record
+    # (12 B) in, 16 levels x 2 fp16 features (64 B) out; 16 x 8 corner gathers of 4 B (512 B, L2)
+    "grid_encode": {"kernel": "encode_forward_points_kernel (density-grid samples)", "hbm_bytes": 12 + 64, "l2_bytes": 16 * 8 * 4},
+    # mlp_forward_kernel<density> over the grid-update samples: 64 B features in, 2 B density out
+    "grid_density": {"kernel": "mlp_forward_kernel<density> (density-grid samples)", "hbm_bytes": 64 + 2, "flop": DENSITY_FWD_FLOP},
+    # generate_grid_samples_kernel: one 28-byte record + 4-byte cell index out per sample
+    "grid_samples": {"kernel": "generate_grid_samples_kernel", "hbm_bytes": 28 + 4},
+    # splat_kernel: 4 B index + 2 B density in, one 4-byte atomicMax per sample
+    "grid_splat": {"kernel": "splat_kernel", "hbm_bytes": 4 + 2 + 4},
+}
+# DRAM bytes (read + write) per unit that ncu measured for these launches (one capture each, see
+# profiles/ for the command); None until captured.
+NCU_TRAFFIC_PER_UNIT = {
+    "grid_encode": None,
 }
 
 
-def phase_roofline(phases: dict, peaks: dict) -> dict:
-    """Roofline of the dominant phase of the training step.  Phase durations come from CUDA events
-    recorded on the trainer's stream between the phases of profiled steps (run right after the
-    timed steps, on the same model); units per launch are the step's sample counts."""
+def train_roofline(phases: dict, grid: dict, peaks: dict, l2: dict | None) -> dict:
+    """Roofline of the kernel that takes the largest share of the timed steps.  Kernel times come
+    from CUDA events recorded on the trainer's stream around each kernel of the grid update and
+    between the phases of the step, on a twin model that runs the same steps as the timed one."""
     steps = max(phases["steps"], 1)
-    ms = {k: v / steps for k, v in phases["ms"].items()}
-    n_inf = phases["mean_inference_samples"]
-    total = sum(ms.values())
-    # the profiled steps march serially; in the timed steps the march runs on its own stream
-    # during the previous step's backward pass, so the dominant phase is taken among the others
-    dom = max((k for k in ms if k != "march"), key=ms.get)
-    t = ms[dom] * 1e-3
-    if dom == "mlp_bwd":
-        flops = MLP_FWDBWD_FLOP * BATCH
-        achieved = flops / t / 1e12
-        return {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": None, "share": round(ms[dom] / total, 3),
-                "peak_source": peaks["source"] + " (sustained dense bf16; fp16 has the same tensor rate)"}
-    info = PHASE_BYTES.get(dom, {"unit": "?", "bytes": 0, "kernel": dom})
-    units = {"pre-compaction sample": n_inf, "batch sample": BATCH, "parameter": 12_206_480, "grid cell": 128 ** 3 * 2}.get(info["unit"], 0)
-    achieved = info["bytes"] * units / t / 1e9
-    res = {"kernel": info["kernel"], "phase": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-           "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "share": round(ms[dom] / total, 3),
-           "peak_source": peaks["source"] + " (HBM copy bandwidth)",
-           "per_unit": f"{info['bytes']} algorithmic HBM bytes per {info['unit']}, {units:.0f} units per launch, {ms[dom] * 1e3:.1f} us per launch"}
-    if "ncu_dram_bytes_per_unit" in info:
-        res["traffic"] = round(info["ncu_dram_bytes_per_unit"] * units)
-        res["traffic_note"] = "ncu DRAM read+write of one launch of this kernel in the config-3 step, per unit, times this launch's units"
-    if "l2_gather_bytes" in info:
-        res["l2_gather_GBps"] = round(info["l2_gather_bytes"] * units / t / 1e9, 1)
-        res["note"] = ("the table (24 MB) is L2-resident: the kernel is bound by L1/L2 gather issue (16 levels x 8 corner loads per "
-                       "sample), not by HBM; l2_gather_GBps counts the gathered table bytes")
+    ms_step = {k: v / steps for k, v in phases["ms"].items()}
+    cands = {}
+    if grid["updates"]:
+        for k, v in grid["ms"].items():
+            if k in GRID_KERNELS:
+                cands[k] = v / grid["updates"]  # ms per launch
+    dom = max(cands, key=cands.get) if cands else None
+    if dom is None:
+        return {"kernel": None, "note": "no grid update in the profiled steps"}
+    info = GRID_KERNELS[dom]
+    t = cands[dom] * 1e-3
+    units = grid["mean_samples"]
+    share = cands[dom] * grid["updates"] / steps / max(sum(ms_step.values()), 1e-9)
+    achieved = info["hbm_bytes"] * units / t / 1e9
+    res = {"kernel": info["kernel"], "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+           "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"] + " (HBM copy bandwidth)",
+           "share_of_step": round(share, 3), "launch_us": round(cands[dom] * 1e3, 1),
+           "per_unit": f"{info['hbm_bytes']} algorithmic HBM bytes per sample x {units:.0f} samples per launch, {cands[dom] * 1e3:.1f} us per launch "
+                       "(CUDA events on the trainer's stream, twin model, same steps as the timed region)"}
+    if NCU_TRAFFIC_PER_UNIT.get(dom) is not None:
+        res["traffic"] = round(NCU_TRAFFIC_PER_UNIT[dom] * units)
+    if "l2_bytes" in info and l2:
+        l2_rate = info["l2_bytes"] * units / t / 1e9
+        res["l2"] = {"achieved": round(l2_rate, 1), "unit": "GB/s", "gathered_bytes_per_unit": info["l2_bytes"],
+                     "peak_stream_read": l2.get("l2_read_GBps"), "frac_of_stream_read": round(l2_rate / l2["l2_read_GBps"], 4) if l2.get("l2_read_GBps") else None,
+                     "random_gather_GBps": l2.get("gather_GBps"),
+                     "frac_of_random_gather": round(l2_rate / l2["gather_GBps"], 4) if l2.get("gather_GBps") else None,
+                     "note": "table corner bytes gathered per second against the measured L2 streaming-read rate and the measured rate of fully "
+                             "random 4-byte loads from an L2-resident table (bench_probes, run live)"}
     return res
+
+
+def _trained_twin(ngp, ds, cfg, world, warmup):
+    """A trainer at step `warmup`: every twin built from the same dataset and config takes the same
+    steps (the training is deterministic), so timed, end-to-end and profiled runs cover equal work."""
+    model = ngp.InstantNGP(ds, cfg)
+    if world > 1:
+        model.join_process_group()
+    model.train(warmup)
+    return model
+
+
+def params_checksum(model) -> str:
+    import hashlib
+
+    return hashlib.sha256(model.get_params().tobytes()).hexdigest()[:16]
+
+
+def gather_floats(vals: list[float], world: int) -> list[list[float]]:
+    if world == 1:
+        return [vals]
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.cpu().tolist() for o in out]
+
+
+def timed_train(model, steps: int, world: int, local: int):
+    """K training steps through one train() call, timed by the trainer's CUDA events on its own
+    stream; the clock sampler runs and every rank has passed the barrier before the region."""
+    import torch
+    import ngp_b200 as ngp
+
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        clocks.wait_first()
+        barrier(world)
+        torch.cuda.synchronize()
+        t_enter = time.time()
+        launches0 = ngp.kernel_launch_count()
+        torch.cuda.nvtx.range_push("timed")  # lets a profiler select the timed steps
+        stats = model.train(steps)
+        torch.cuda.nvtx.range_pop()
+        launches = ngp.kernel_launch_count() - launches0
+        torch.cuda.synchronize()
+        barrier(world)
+        time.sleep(0.25)
+    return stats, launches, clocks.summary(), t_enter
 
 
 def bench_train_ours(args, rank, world, local):
@@ -232,41 +283,44 @@ def bench_train_ours(args, rank, world, local):
 
     peaks = load_peaks()
     ds = make_dataset(args)
-    model = ngp.InstantNGP(ds, ngp.config0_trainer_config())
-    if world > 1:
-        model.join_process_group()
-    model.train(args.warmup)
-    barrier(world)
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        clocks.wait_first()
-        launches0 = ngp.kernel_launch_count()
-        stats = model.train(args.steps)
-        launches = ngp.kernel_launch_count() - launches0
-        time.sleep(0.25)
-    torch.cuda.synchronize()
-    barrier(world)
+    cfg = ngp.config0_trainer_config()
+    model = _trained_twin(ngp, ds, cfg, world, args.warmup)
+    stats, launches, clocks, t_enter = timed_train(model, args.steps, world, local)
     ms = max_over_ranks(stats["elapsed_ms"], world)
-    # per-phase breakdown (separate, profiled steps; not part of the timed number)
-    model.set_profiling(True)
-    model.train(min(args.steps, 50))
-    phases = model.phase_times()
-    model.set_profiling(False)
-    # e2e through the public API: one train(1) call per step (host round trip, counters and loss
-    # read back every step), timed with events around the whole loop
-    n_e2e = max(3, args.steps // 4)
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    rays = 0
-    for _ in range(n_e2e):
-        st = model.train(1)
-        rays = st["rays_per_batch"]
-    e.record()
-    e.synchronize()
-    e2e_ms = max_over_ranks(s.elapsed_time(e) / n_e2e, world)
+    per_rank = gather_floats([stats["elapsed_ms"] / args.steps, t_enter], world)
+    checksum = params_checksum(model)
+    sums = gather_floats([float(int(checksum, 16) % (1 << 52))], world)
+    replicas_equal = all(r[0] == sums[0][0] for r in sums)
     psnr = model.test(count=min(4, args.test_views))["psnr"] if rank == 0 else None
     model.close()
+    # end to end through the public API, on a twin at the same steps: one train(1) call per step,
+    # each reading back the step's counters and per-ray loss; wall clock, max over ranks
+    twin = _trained_twin(ngp, ds, cfg, world, args.warmup)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    rays = []
+    for _ in range(args.steps):
+        rays.append(twin.train(1)["rays_per_batch"])
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    twin.close()
+    # per-phase and per-kernel breakdown: another twin, same steps, with events between phases
+    # (the march of each step then runs on the trainer's stream instead of overlapping)
+    prof = _trained_twin(ngp, ds, cfg, world, args.warmup)
+    prof.set_profiling(True)
+    prof.train(args.steps)
+    phases = prof.phase_times()
+    grid = prof.grid_phase_times()
+    prof.close()
+    # like-for-like with the reference arm: the library at the reference's compiled layout (8 levels
+    # x 4 features, log2 T 19, scale 2) on the same scene and steps
+    same = _trained_twin(ngp, ds, ngp.trainer_config(), world, args.warmup)
+    st_same, _, _, _ = timed_train(same, args.steps, world, local)
+    ms_same = max_over_ranks(st_same["elapsed_ms"], world)
+    same.close()
+    l2 = l2_probes()
     value = world * BATCH * args.steps / (ms * 1e-3)
+    mean_rays = sum(rays) / len(rays)
     res = {
         "metric": "NeRF train samples/s (config 3)",
         "value": round(value, 1),
@@ -282,32 +336,95 @@ def bench_train_ours(args, rank, world, local):
         "data": "synthetic procedural scene (64 Lambert spheres, seeded), rendered on the device",
         "config": {"workload": "config3 end-to-end training", "views": args.views, "resolution": args.res, "batch_samples_per_gpu": BATCH,
                    "grid": "L=16 F=2 log2T=19 base 16 b=1.3819", "mlp": "density 32-64-16, colour 32-64-64-16",
-                   "parallelism": f"dp{world} (NCCL all-reduce of the fp32 gradient per step)",
+                   "parallelism": f"dp{world} (NCCL all-reduce of the fp16 gradient sum per step)" if world > 1 else "dp1",
                    "l2": "working set > L2 (samples 117 MB, encodings 268 MB, dataset 256 MB); no flush",
                    "pre_compaction_samples_per_step": stats["measured_sample_count_before_compaction"],
                    "rays_per_batch": stats["rays_per_batch"], "test_psnr_after_run": psnr,
                    "steps_trained": args.warmup + args.steps},
         "phase_ms_per_step": {k: round(v / max(phases["steps"], 1), 4) for k, v in phases["ms"].items()},
-        "roofline": phase_roofline(phases, peaks),
-        "e2e": {"value": round(world * BATCH / (e2e_ms * 1e-3), 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 12 + 4 * rays,
-                "note": "InstantNGP.train(1) per step; the dataset is uploaded once at construction (as the reference does), each step "
-                        "reads back its 3 counters and the per-ray loss"},
-        "gpu_launches": None,
-        "clocks": clocks.summary(),
+        "grid_update_kernels_ms_per_update": {k: round(v / max(grid["updates"], 1), 4) for k, v in grid["ms"].items()},
+        "grid_updates_in_timed_steps": grid["updates"], "grid_samples_per_update": grid["mean_samples"],
+        "roofline": train_roofline(phases, grid, peaks, l2),
+        "same_layout_as_reference": {
+            "grid": "L=8 F=4 log2T=19 base 16 b=2 (the reference's compiled layout)", "value": round(world * BATCH * args.steps / (ms_same * 1e-3), 1),
+            "unit": "samples/s", "ms_per_step": round(ms_same / args.steps, 5), "steps": args.steps, "warmup": args.warmup,
+            "note": "the library on the reference arm's configuration (same scene, batch, steps and layout), timed like the headline"},
+        "e2e": {"value": round(world * BATCH * args.steps / e2e_s, 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": int(12 + 4 + 4 * mean_rays),
+                "copies": [{"dir": "d2h", "bytes": 12, "what": "the step's ray / sample / compacted counters (pinned)"},
+                           {"dir": "d2h", "bytes": int(4 * mean_rays), "what": "per-ray loss of the step (pinned), rays_per_batch x 4 B"},
+                           {"dir": "d2h", "bytes": 4, "what": "occupied-cell count"}],
+                "note": "InstantNGP.train(1) per step on a twin model at the same steps as the timed region (wall clock, max over ranks). "
+                        "A training step has no per-step host input: the dataset is uploaded once when the trainer is built, as the "
+                        "reference does (InstantNGP constructor, ngp.train.cu:1283-1300)"},
+        "gpu_launches": launches,
+        "clocks": clocks,
     }
-    res["gpu_launches"] = launches
+    if world > 1:
+        res["ranks"] = {"ms_per_step": [round(r[0], 4) for r in per_rank], "timed_region_entry_skew_ms": round(1e3 * (max(r[1] for r in per_rank) - min(r[1] for r in per_rank)), 3),
+                        "params_sha256_16": checksum, "replicas_identical": replicas_equal}
+    else:
+        res["params_sha256_16"] = checksum
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline_train(args, int(stats["measured_sample_count_before_compaction"]))
+        res["cpu_baseline"] = cpu_baseline_train(args, int(stats["measured_sample_count_before_compaction"]),
+                                                 grid["mean_samples"] * grid["updates"] / max(phases["steps"], 1))
     return res
 
 
-def cpu_baseline_train(args, pre_compaction: int, budget_s: float = 4.0) -> dict:
+def l2_probes() -> dict:
+    """Measured L2 rates on this GPU (bench-only probe library): streaming 16-byte reads over a
+    64 MB L2-resident buffer, and random 4-byte gathers from a 32 MB table."""
+    import torch
+
+    lib = probes_lib()
+    stream = torch.cuda.current_stream()
+    s = ctypes.c_void_p(stream.cuda_stream)
+    buf = torch.ones(64 << 18, dtype=torch.int32, device="cuda")  # 64 MB
+    sink = torch.zeros(1, dtype=torch.int32, device="cuda")
+    passes = 20
+
+    def run_read():
+        rc = lib.probe_l2_read(ctypes.c_void_p(buf.data_ptr()), ctypes.c_size_t(buf.numel() * 4), ctypes.c_uint32(passes),
+                               ctypes.c_void_p(sink.data_ptr()), s)
+        if rc != 0:
+            raise RuntimeError(f"probe_l2_read: cuda error {rc}")
+
+    res = {}
+    for _ in range(3):
+        run_read()
+    times = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run_read()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    res["l2_read_GBps"] = round(passes * buf.numel() * 4 / (min(times) * 1e-3) / 1e9, 1)
+    g = probe_gather_scatter(stream)
+    res["gather_GBps"] = round(g["gather_G_s"] * 4, 1)
+    res["gather_G_s"] = g["gather_G_s"]
+    res["scatter_G_s"] = g["scatter_G_s"]
+    return res
+
+
+def probes_lib():
+    so = ROOT / "instant-ngp_b200" / "bench_probes" / "libngp_bench_probes.so"
+    if not so.exists():
+        import build as build_mod
+
+        build_mod.build_probes()
+    return ctypes.CDLL(str(so))
+
+
+def cpu_baseline_train(args, pre_compaction: int, grid_samples: float = 0.0, budget_s: float = 4.0) -> dict:
     """The scalar C++ oracle (the reference's algorithm restated on the host) timed on bounded
     samples of each part of a config-3 training step, combined into the time of one step at this
     run's per-step counts: marching of every pre-compaction sample, the encoding + full network
     forward on all of them (the reference's inference pass), the encoding + network forward and
-    backward of the 2^18-sample batch, and Adam over every parameter, each on all host cores."""
+    backward of the 2^18-sample batch, Adam over every parameter, and the density-grid update's
+    samples of the timed steps (encoding + network forward per grid sample: an upper bound, since the
+    update runs only the density network), each on all host cores."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import ngp_b200 as ngp
     import workloads
@@ -353,12 +470,13 @@ def cpu_baseline_train(args, pre_compaction: int, budget_s: float = 4.0) -> dict
     adam = rate(lambda: ora.adam(10240, *adam_state, threads=cores), m_p)
 
     n_params = 12_206_480
-    t_step = (pre_compaction / march + pre_compaction / fwd + BATCH / fwd + BATCH / mlp_bwd + BATCH / enc_bwd + n_params / adam)
+    t_step = (pre_compaction / march + pre_compaction / fwd + BATCH / fwd + BATCH / mlp_bwd + BATCH / enc_bwd + n_params / adam + grid_samples / fwd)
     return {"value": round(BATCH / t_step, 1), "unit": "samples/s", "cores": cores, "kind": "port",
             "sample": (f"one config-3 step ({pre_compaction} marched samples, {BATCH} batch samples, {n_params} parameters) timed part by "
                        f"part on bounded samples of the scalar oracle ({budget_s:.0f} s each): march {march / 1e6:.2f} M samples/s, "
                        f"encode + network forward {fwd / 1e6:.2f} M/s, network backward {mlp_bwd / 1e6:.2f} M/s, encode backward "
-                       f"{enc_bwd / 1e6:.2f} M/s, Adam {adam / 1e6:.1f} M params/s; every part on {cores} host threads"),
+                       f"{enc_bwd / 1e6:.2f} M/s, Adam {adam / 1e6:.1f} M params/s, {grid_samples:.0f} density-grid samples per step at the "
+                       f"encode + forward rate; every part on {cores} host threads"),
             "step_s": round(t_step, 3)}
 
 
@@ -498,15 +616,19 @@ def bench_encode_ours(args, rank, world, local):
         step()
         feats_pin.copy_(feats, non_blocking=True)
 
-    e2e_times = time_steps(e2e_step, max(3, args.steps // 2), 2, flush, stream, world)
+    e2e_times = time_steps(e2e_step, args.steps, args.warmup, flush, stream, world)
     e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
     peaks = load_peaks()
-    probe = probe_gather_scatter(stream)
-    fwd_bytes_pt = 12 + L * F * 2 + L * 8 * F * 2
-    bwd_bytes_pt = 12 + L * F * 2 + L * 8 * F * 4
+    l2 = l2_probes()
+    hbm_fwd_pt = 12 + L * F * 2  # coordinates in, features out
+    hbm_bwd_pt = 12 + L * F * 2  # coordinates and dL/dy in (the fp32 table gradient stays L2-resident)
+    l2_fwd_pt = L * 8 * F * 2  # corner bytes gathered
+    l2_bwd_pt = L * 8 * F * 4  # fp32 corner gradients scattered
     dom = "forward" if fwd_ms >= bwd_ms else "backward"
-    dom_bytes = (fwd_bytes_pt if dom == "forward" else bwd_bytes_pt) * n
-    achieved = dom_bytes / (max(fwd_ms, bwd_ms) * 1e-3) / 1e9
+    t_dom = max(fwd_ms, bwd_ms) * 1e-3
+    hbm_b, l2_b = (hbm_fwd_pt, l2_fwd_pt) if dom == "forward" else (hbm_bwd_pt, l2_bwd_pt)
+    achieved = hbm_b * n / t_dom / 1e9
+    l2_rate = l2_b * n / t_dom / 1e9
     return {
         "metric": "hash-encode fwd+bwd Gpts/s (config 0)", "value": round(world * n / (ms * 1e-3) / 1e9, 4), "unit": "Gpts/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
@@ -517,17 +639,16 @@ def bench_encode_ours(args, rank, world, local):
                    "l2": "flushed (256 MB write) before every timed step"},
         "kernels_ms": {"encode_forward": round(fwd_ms, 5), "encode_backward": round(bwd_ms, 5)},
         "roofline": {"kernel": f"encode_{dom}", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"],
-                     "note": "achieved counts HBM streams plus table bytes gathered (L2-served) per point; the L2-resident table makes "
-                             "the kernels gather/atomic-bound: see l2_roofline"},
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"] + " (HBM copy bandwidth)",
+                     "per_unit": f"{hbm_b} algorithmic HBM bytes per point (the 24 MB table is L2-resident), {n} points per launch",
+                     "l2": {"achieved": round(l2_rate, 1), "unit": "GB/s", "bytes_per_unit": l2_b, "peak_stream_read": l2["l2_read_GBps"],
+                            "frac_of_stream_read": round(l2_rate / l2["l2_read_GBps"], 4), "random_gather_GBps": l2["gather_GBps"],
+                            "frac_of_random_gather": round(l2_rate / l2["gather_GBps"], 4),
+                            "note": "table bytes gathered (forward) or scattered as fp32 (backward) per second, against the measured L2 "
+                                    "streaming-read rate and the measured rate of random 4-byte loads (bench_probes, run live)"}},
         "table_access": {
             "forward_Gaccess_s": round(n * L * 8 / (fwd_ms * 1e-3) / 1e9, 2), "backward_Gaccess_s": round(n * L * 8 / (bwd_ms * 1e-3) / 1e9, 2),
-            "random_gather_Gaccess_s": probe["gather_G_s"], "random_float2_atomic_Gaccess_s": probe["scatter_G_s"],
-            "note": "table corner accesses per second (8 corners x 16 levels per point) beside the measured rate of fully random "
-                    "4-byte loads / float2 atomics on an L2-resident table (ngp_probe_gather / ngp_probe_scatter, run live).  The kernels "
-                    "exceed the fully random rates because a cell's x-neighbour corners share sectors and the coarse levels stay L1-resident; "
-                    "their bounding resource is L1 throughput (ncu l1tex__throughput 70-85 % of peak, "
-                    "profiles/encode_forward_points_kernel__train_config3.md, profiles/encode_backward_kernel__train_config3.md)"},
+            "random_gather_Gaccess_s": l2["gather_G_s"], "random_float2_atomic_Gaccess_s": l2["scatter_G_s"]},
         "e2e": {"value": round(world * n / (e2e_ms * 1e-3) / 1e9, 4), "unit": "Gpts/s", "h2d_bytes_per_step": coords_h.nbytes + dy_h.nbytes,
                 "d2h_bytes_per_step": feats.numel() * 2},
         "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
@@ -538,25 +659,25 @@ def probe_gather_scatter(stream) -> dict:
     """Measured rate of random 4-byte loads from a 32 MB table and of random float2 atomic adds
     into a 64 MB table (the L2-resident access patterns the encoding kernels are bound by)."""
     import torch
-    import ngp_b200 as ngp
 
-    lib = ngp.lib()
+    lib = probes_lib()
     threads, rounds = 1 << 20, 4
     tab = torch.ones(1 << 23, dtype=torch.int32, device="cuda")
     out = torch.empty(threads, dtype=torch.int32, device="cuda")
     acc = torch.zeros(1 << 24, dtype=torch.float32, device="cuda")
     s = ctypes.c_void_p(stream.cuda_stream)
     res = {}
-    for name, call in (("gather_G_s", lambda: lib.ngp_probe_gather(ctypes.c_void_p(tab.data_ptr()), 23, threads, rounds, ctypes.c_void_p(out.data_ptr()), s)),
-                       ("scatter_G_s", lambda: lib.ngp_probe_scatter(ctypes.c_void_p(acc.data_ptr()), 23, threads, rounds, s))):
+    for name, call in (("gather_G_s", lambda: lib.probe_gather(ctypes.c_void_p(tab.data_ptr()), 23, threads, rounds, ctypes.c_void_p(out.data_ptr()), s)),
+                       ("scatter_G_s", lambda: lib.probe_scatter(ctypes.c_void_p(acc.data_ptr()), 23, threads, rounds, s))):
         for _ in range(3):
             call()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             ev0.record()
             for _ in range(10):
-                if call() != 0:
-                    raise RuntimeError(lib.ngp_last_error().decode())
+                rc = call()
+                if rc != 0:
+                    raise RuntimeError(f"{name} probe: cuda error {rc}")
             ev1.record()
         ev1.synchronize()
         res[name] = round(10 * threads * rounds * 16 / (ev0.elapsed_time(ev1) * 1e-3) / 1e9, 2)
@@ -662,7 +783,7 @@ def bench_mlp_ours(args, rank, world, local):
         out_h.copy_(out, non_blocking=True)
         dw_h.copy_(dw, non_blocking=True)
 
-    e2e_ms = max_over_ranks(statistics.mean(time_steps(e2e_step, max(3, args.steps // 4), 2, flush, stream, world)), world)
+    e2e_ms = max_over_ranks(statistics.mean(time_steps(e2e_step, args.steps, args.warmup, flush, stream, world)), world)
     peaks = load_peaks()
     tflops = MLP_FWDBWD_FLOP * n / (ms * 1e-3) / 1e12
     return {
@@ -743,7 +864,7 @@ def bench_march_ours(args, rank, world, local):
         ns_h.copy_(numsteps, non_blocking=True)
         co_h.copy_(coords[:samples], non_blocking=True)
 
-    e2e_ms = max_over_ranks(statistics.mean(time_steps(e2e_step, max(3, args.steps // 4), 2, flush, stream, world)), world)
+    e2e_ms = max_over_ranks(statistics.mean(time_steps(e2e_step, args.steps, args.warmup, flush, stream, world)), world)
     peaks = load_peaks()
     march_bytes = n * (24 + 8) + samples * 28
     achieved = march_bytes / (march_ms * 1e-3) / 1e9

@@ -9,8 +9,9 @@
  *
  * The functions replace the device layer of the reference's `ngp::cuda` namespace
  * (ngp.train.h:107-161, implemented in ngp.train.cu); each declaration names the reference
- * symbol it stands in for.  The C++ header `ngp.train.h` in this directory re-exports the
- * reference's exact `ngp::cuda` signatures on top of these functions.
+ * symbol it stands in for.  The drop-in layer instant-ngp_b200/shim/ngp_train_cuda.cpp defines
+ * the reference's exact `ngp::cuda` signatures on top of these functions; it is compiled against
+ * the reference's own ngp.train.h (no copy of that header ships here).
  *
  * Data layouts (identical to the reference's, ngp.train.cu:38, 563-570, 917-920, 1241):
  *   sample record      7 x fp32 {x, y, z, dt, (dx+1)/2, (dy+1)/2, (dz+1)/2}, array of structs
@@ -250,7 +251,7 @@ NGP_API int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t wid
 /* ------------------------------------------------------------------------------------------
  * Compositing, loss and compaction (batch = 2^18 samples).
  * ------------------------------------------------------------------------------------------ */
-NGP_API uint32_t ngp_loss_scratch_bytes(uint32_t max_rays);
+NGP_API uint32_t ngp_loss_scratch_bytes(uint32_t max_rays); /* 0 (error set) when the size exceeds 32 bits */
 
 /* Front-to-back compositing with early stop at transmittance < 1e-4, random background, L2
  * loss, analytic compositing backward -> dloss_doutput fp16 [2^18][16] (scaled by
@@ -271,9 +272,11 @@ NGP_API int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t step
  * 5 MiB that each GPU loading the library keeps until the process exits.  Limit: rays_per_batch
  * <= ngp_training_loss_and_compact_noalloc_max_rays() (2^18); larger requests fail with
  * NGP_ERR_INVALID.  The first call on a device looks up the array's device address (with that
- * device current) and should come before any stream capture.  All calls on a device share the
- * array: calls whose work overlaps on the GPU race with each other.  The scratch needs no
- * clearing between calls (every byte read is written earlier in the same call). */
+ * device current) and should come before any stream capture; the address is kept per device and
+ * context, so after a device reset (or a new primary context) the next call looks it up again
+ * and should also come before any capture.  All calls on a device share the array: calls whose
+ * work overlaps on the GPU race with each other.  The scratch needs no clearing between calls
+ * (every byte read is written earlier in the same call). */
 NGP_API uint32_t ngp_training_loss_and_compact_noalloc_max_rays(void);
 NGP_API int ngp_training_loss_and_compact_noalloc(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
                                                   uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
@@ -499,16 +502,12 @@ NGP_API int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world
  * out_mean_inference_samples = mean marched samples per step. */
 NGP_API int ngp_trainer_set_profiling(ngp_trainer* t, int enable);
 NGP_API int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_steps, float* out_mean_inference_samples);
+/* Profiled grid updates (no reference counterpart; update_density_grid, ngp.train.cu:1526-1595,
+ * split by kernel): accumulated ms of [0] sample generation, [1] encoding, [2] density network,
+ * [3] splat, [4] EMA + mean + bitfield (n >= 5), the number of updates and their mean sample count. */
+NGP_API int ngp_trainer_grid_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_updates, float* out_mean_samples);
 /* Occupancy bitfield (2^18 bytes) and density-grid values (2^21 floats) to the host. */
 NGP_API int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host, float* values_host);
-
-/* ------------------------------------------------------------------------------------------
- * Roofline probes (used by the benchmark): random 4-byte loads from a table of 2^log2_entries
- * uint32 entries, and random 2 x fp32 atomic adds into a table of 2^log2_entries float pairs;
- * threads (a multiple of 256) x rounds x 16 accesses.
- * ------------------------------------------------------------------------------------------ */
-NGP_API int ngp_probe_gather(const uint32_t* table, uint32_t log2_entries, uint32_t threads, uint32_t rounds, uint32_t* out, void* stream);
-NGP_API int ngp_probe_scatter(float* table, uint32_t log2_entries, uint32_t threads, uint32_t rounds, void* stream);
 
 #ifdef __cplusplus
 }

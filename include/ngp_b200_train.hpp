@@ -535,3 +535,13 @@ private:
 
 }  // namespace train
 }  // namespace ngp::b200
+
+// The reference's callers name these types ngp::train::InstantNGP and ngp::dataset::NGPDataset
+// (ngp.train.ixx:40, ngp.dataset.ixx:7): the aliases let that code compile unchanged.  Define
+// NGP_B200_NO_REFERENCE_NAMES to leave them out (e.g. beside the reference's own modules).
+#ifndef NGP_B200_NO_REFERENCE_NAMES
+namespace ngp {
+namespace train   = ngp::b200::train;
+namespace dataset = ngp::b200::dataset;
+}  // namespace ngp
+#endif

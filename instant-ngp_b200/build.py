@@ -2,6 +2,8 @@
 
 Usage: ``python instant-ngp_b200/build.py [--force] [--jobs N]``.
 
+The bench-only probes (``bench_probes/probes.cu``) build into their own library.
+
 Each ``csrc/*.cu`` / ``csrc/*.cpp`` is compiled to an object under ``_build/`` (skipped when
 the object is newer than the source and every header), then linked into
 ``instant-ngp_b200/libngp_b200.so`` next to this file.  The library is loaded from that path by
@@ -22,6 +24,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libngp_b200.so"
+PROBES_SRC = PKG / "bench_probes" / "probes.cu"
+PROBES_LIB = PKG / "bench_probes" / "libngp_bench_probes.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
@@ -73,7 +77,20 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
         os.replace(tmp, LIB)
+    build_probes(force)
     return LIB
+
+
+def build_probes(force: bool = False) -> Path:
+    """The bench-only probe library (bench_probes/libngp_bench_probes.so), separate from the
+    product library; only bench.py loads it."""
+    if force or not PROBES_LIB.exists() or PROBES_SRC.stat().st_mtime > PROBES_LIB.stat().st_mtime:
+        cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared",
+               "-o", str(PROBES_LIB), str(PROBES_SRC), "-lcudart"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {PROBES_SRC.name}:\n{res.stdout}\n{res.stderr}")
+    return PROBES_LIB
 
 
 if __name__ == "__main__":

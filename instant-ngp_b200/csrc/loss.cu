@@ -887,7 +887,16 @@ void progress_scratch(ProgressParams& p, uint32_t R, void* scratch, uint32_t* ro
 
 using namespace ngp;
 
-extern "C" uint32_t ngp_loss_scratch_bytes(uint32_t max_rays) { return static_cast<uint32_t>(loss_scratch_size(max_rays)); }
+extern "C" uint32_t ngp_loss_scratch_bytes(uint32_t max_rays) {
+    clear_error();
+    const size_t bytes = loss_scratch_size(max_rays);
+    if (bytes > 0xFFFFFFFFull) {
+        fail(NGP_ERR_INVALID, "loss scratch: " + std::to_string(max_rays) + " rays need " + std::to_string(bytes) +
+                                  " bytes, more than a uint32 can state");
+        return 0;
+    }
+    return static_cast<uint32_t>(bytes);
+}
 
 extern "C" int ngp_training_loss_and_compact(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
                                              uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
@@ -1225,20 +1234,53 @@ static __device__ __align__(256) unsigned char g_noalloc_loss_scratch[kNoAllocSc
 
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kMaxDevices] = {};
+void* g_noalloc_ptr[kMaxDevices]             = {};
+unsigned long long g_noalloc_ctx[kMaxDevices] = {};
 
-// Device address of this GPU's copy of the array, looked up once per device with that device
-// current.  The host-side name of the array is not a device address and must never be passed to
-// a kernel.
+// Identity of the context current on this thread (cuCtxGetId through the runtime's driver entry
+// point, so that the library needs no link against libcuda).  A device reset, or the release and
+// re-creation of the primary context, gives a new identity; the module and its static array are
+// then loaded again, possibly at another address.
+int current_context_id(unsigned long long* id) {
+    using GetCurrent = int (*)(void**);
+    using GetId      = int (*)(void*, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id           = nullptr;
+    if (get_current == nullptr || get_id == nullptr) {
+        void* a                            = nullptr;
+        void* b                            = nullptr;
+        cudaDriverEntryPointQueryResult qa = cudaDriverEntryPointSymbolNotFound, qb = cudaDriverEntryPointSymbolNotFound;
+        NGP_TRY(check_cuda(cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa), "no-alloc loss: cuCtxGetCurrent entry point"));
+        NGP_TRY(check_cuda(cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb), "no-alloc loss: cuCtxGetId entry point"));
+        if (a == nullptr || b == nullptr || qa != cudaDriverEntryPointSuccess || qb != cudaDriverEntryPointSuccess)
+            return fail(NGP_ERR_CUDA, "no-alloc loss: the driver exports no cuCtxGetCurrent / cuCtxGetId");
+        get_current = reinterpret_cast<GetCurrent>(a);
+        get_id      = reinterpret_cast<GetId>(b);
+    }
+    void* ctx = nullptr;
+    if (get_current(&ctx) != 0 || ctx == nullptr) return fail(NGP_ERR_CUDA, "no-alloc loss: no current context");
+    if (get_id(ctx, id) != 0) return fail(NGP_ERR_CUDA, "no-alloc loss: cuCtxGetId failed");
+    return NGP_OK;
+}
+
+// Device address of this GPU's copy of the array, looked up with that device current: once per
+// device and context (again after a device reset).  The host-side name of the array is not a
+// device address and must never be passed to a kernel.
 int noalloc_scratch(void** out) {
     int device = 0;
     NGP_TRY(check_cuda(cudaGetDevice(&device), "no-alloc loss: cudaGetDevice"));
     if (device < 0 || device >= kMaxDevices) return fail(NGP_ERR_INVALID, "no-alloc loss: device index out of range");
+    // cudaSetDevice makes the device's primary context current on this thread (creating it if
+    // needed), so that its identity can be read
+    NGP_TRY(check_cuda(cudaSetDevice(device), "no-alloc loss: cudaSetDevice"));
+    unsigned long long ctx = 0;
+    NGP_TRY(current_context_id(&ctx));
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (g_noalloc_ptr[device] == nullptr) {
+    if (g_noalloc_ptr[device] == nullptr || g_noalloc_ctx[device] != ctx) {
         void* p = nullptr;
         NGP_TRY(check_cuda(cudaGetSymbolAddress(&p, g_noalloc_loss_scratch), "no-alloc loss: cudaGetSymbolAddress"));
         g_noalloc_ptr[device] = p;
+        g_noalloc_ctx[device] = ctx;
     }
     *out = g_noalloc_ptr[device];
     return NGP_OK;

@@ -28,6 +28,7 @@ namespace {
 
 constexpr uint32_t kMlpParams  = 10240;
 constexpr int kTrainPhases     = 8;  // see ngp_trainer_phase_times
+constexpr int kGridPhases      = 5;  // see ngp_trainer_grid_phase_times
 constexpr uint32_t kLrTableCapacity = 1u << 20;
 constexpr uint32_t kLrTableBlock    = 4096u;
 // Segmented evaluation: tiles of 2^16 pixel rays; the first segment marches at most
@@ -167,7 +168,16 @@ struct ngp_trainer {
     float* lr_table       = nullptr;
     uint32_t lr_table_len = 0;
     uint32_t adam_calls   = 0;  // bounds every parameter's step count
-    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> grid_events;  // pending grid-update timings
+    // grid-update timing: a pool of event pairs created once and reused by every train call
+    // (grid_events_used pairs are pending in the current call)
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> grid_events;
+    size_t grid_events_used = 0;
+    // profiling: events around the kernels of a grid update (samples, encode, density network,
+    // splat, EMA + mean + bitfield), their accumulated times and the samples they processed
+    cudaEvent_t grid_marks[kGridPhases + 1] = {};
+    double grid_phase_ms[kGridPhases]       = {};
+    double grid_samples_sum                 = 0.0;
+    uint32_t profiled_grid_updates          = 0;
 };
 
 namespace {
@@ -195,6 +205,8 @@ void destroy(ngp_trainer* t) {
     for (cudaEvent_t e : t->marks)
         if (e) cudaEventDestroy(e);
     for (auto& pr : t->grid_events) cudaEventDestroy(pr.first), cudaEventDestroy(pr.second);
+    for (cudaEvent_t e : t->grid_marks)
+        if (e) cudaEventDestroy(e);
     if (t->ev_counts) cudaEventDestroy(t->ev_counts);
     if (t->ev_march) cudaEventDestroy(t->ev_march);
     if (t->host_counters) cudaFreeHost(t->host_counters);
@@ -258,14 +270,25 @@ bool grid_update_due(uint32_t step) {
     return step % skip == 0u;
 }
 
+void grid_mark(ngp_trainer* t, int k) {
+    if (t->profiling) cudaEventRecord(t->grid_marks[k], t->stream);
+}
+
 // update_density_grid (ngp.train.cu:1526-1595).
 int update_grid(ngp_trainer* t) {
     if (!grid_update_due(t->step)) return NGP_OK;
-    cudaEvent_t e0, e1;
-    cudaEventCreate(&e0);
-    cudaEventCreate(&e1);
-    t->grid_events.emplace_back(e0, e1);
-    cudaEventRecord(e0, t->stream);
+    if (t->grid_events_used == t->grid_events.size()) {
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        NGP_TRY(check_cuda(cudaEventCreate(&e0), "grid timing event"));
+        if (const int st = check_cuda(cudaEventCreate(&e1), "grid timing event"); st != NGP_OK) {
+            cudaEventDestroy(e0);
+            return st;
+        }
+        t->grid_events.emplace_back(e0, e1);
+    }
+    const auto& ev = t->grid_events[t->grid_events_used++];
+    cudaEventRecord(ev.first, t->stream);
+    grid_mark(t, 0);
     const Split& s = t->train;
     if (t->step == 0) {
         t->ema_step = 0;
@@ -276,24 +299,38 @@ int update_grid(ngp_trainer* t) {
     const uint32_t n         = n_uniform + n_nonuni;
     float* coords = t->sets[t->step & 1u].coords;
     NGP_TRY(ngp_density_grid_samples(n_uniform, n_nonuni, t->ema_step, t->grid_values, coords, t->grid_indices, t->stream));
+    grid_mark(t, 1);
     NGP_TRY(encode(t, n, coords, t->enc, n));
+    grid_mark(t, 2);
     NGP_TRY(ngp_density_forward(n, t->params, t->enc, n, t->grid_density, t->stream));
+    grid_mark(t, 3);
     NGP_TRY(ngp_density_grid_splat(n, t->grid_indices, t->grid_density, t->grid_scratch, t->stream));
+    grid_mark(t, 4);
     NGP_TRY(ngp_density_grid_update(t->grid_values, t->grid_scratch, 0.95f, t->grid_partial, t->grid_mean, t->bitfield, t->occupied, t->stream));
+    grid_mark(t, 5);
     ++t->ema_step;
-    cudaEventRecord(e1, t->stream);
+    cudaEventRecord(ev.second, t->stream);
+    if (t->profiling) {
+        NGP_TRY(check_cuda(cudaEventSynchronize(t->grid_marks[kGridPhases]), "grid update"));
+        for (int k = 0; k < kGridPhases; ++k) {
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, t->grid_marks[k], t->grid_marks[k + 1]);
+            t->grid_phase_ms[k] += ms;
+        }
+        t->grid_samples_sum += n;
+        ++t->profiled_grid_updates;
+    }
     return NGP_OK;
 }
 
 // Adds the finished grid updates' durations to grid_update_ms.
 void collect_grid_times(ngp_trainer* t) {
-    for (auto& pr : t->grid_events) {
-        float ms = 0.0f;
+    for (size_t i = 0; i < t->grid_events_used; ++i) {
+        const auto& pr = t->grid_events[i];
+        float ms       = 0.0f;
         if (cudaEventSynchronize(pr.second) == cudaSuccess && cudaEventElapsedTime(&ms, pr.first, pr.second) == cudaSuccess) t->grid_update_ms += ms;
-        cudaEventDestroy(pr.first);
-        cudaEventDestroy(pr.second);
     }
-    t->grid_events.clear();
+    t->grid_events_used = 0;
 }
 
 int march_step(ngp_trainer* t, uint32_t step, cudaStream_t stream) {
@@ -806,12 +843,27 @@ extern "C" int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host
 extern "C" int ngp_trainer_set_profiling(ngp_trainer* t, int enable) {
     clear_error();
     if (t == nullptr) return fail(NGP_ERR_INVALID, "profiling: null trainer");
-    if (enable && t->marks[0] == nullptr)
+    if (enable && t->marks[0] == nullptr) {
         for (cudaEvent_t& e : t->marks) NGP_TRY(check_cuda(cudaEventCreate(&e), "profiling events"));
+        for (cudaEvent_t& e : t->grid_marks) NGP_TRY(check_cuda(cudaEventCreate(&e), "profiling events"));
+    }
     t->profiling = enable != 0;
     for (double& v : t->phase_ms) v = 0.0;
+    for (double& v : t->grid_phase_ms) v = 0.0;
     t->inference_samples_sum = 0.0;
     t->profiled_steps        = 0;
+    t->grid_samples_sum      = 0.0;
+    t->profiled_grid_updates = 0;
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_grid_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_updates, float* out_mean_samples) {
+    clear_error();
+    if (t == nullptr || out_ms == nullptr || n < static_cast<uint32_t>(kGridPhases)) return fail(NGP_ERR_INVALID, "grid phase times: bad arguments");
+    for (int k = 0; k < kGridPhases; ++k) out_ms[k] = static_cast<float>(t->grid_phase_ms[k]);
+    if (out_updates != nullptr) *out_updates = t->profiled_grid_updates;
+    if (out_mean_samples != nullptr)
+        *out_mean_samples = t->profiled_grid_updates ? static_cast<float>(t->grid_samples_sum / t->profiled_grid_updates) : 0.0f;
     return NGP_OK;
 }
 

@@ -287,7 +287,10 @@ def make_eval_rays(camera, image, width, height, fx, fy, cx, cy, pixel_offset, n
 
 def loss_scratch_bytes(max_rays: int) -> int:
     lib().ngp_loss_scratch_bytes.restype = ctypes.c_uint32
-    return int(lib().ngp_loss_scratch_bytes(_u32(max_rays)))
+    n = int(lib().ngp_loss_scratch_bytes(_u32(max_rays)))
+    if n == 0:
+        raise RuntimeError(f"ngp_loss_scratch_bytes: {lib().ngp_last_error().decode()}")
+    return n
 
 
 def training_loss_and_compact(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, compacted_counter,
@@ -392,6 +395,17 @@ def eval_composite(n_pixels, pixel_offset, image, width, height, pixels, numstep
     _check(lib().ngp_eval_composite(_u32(n_pixels), _u32(pixel_offset), _u32(image), _u32(width), _u32(height), _ptr(pixels), _ptr(numsteps),
                                     _ptr(coords), _ptr(network_output), _ptr(sse), _ptr(comparison), _ptr(rendered), _stream(stream)),
            "ngp_eval_composite")
+
+
+def init_mlp_parameters(master, params, stream=None) -> None:
+    """Xavier-uniform MLP weights from PCG32(1337) into master[0:10240] / params[0:10240]
+    (initialize_mlp_parameters, ngp.train.cu:1423-1461)."""
+    _check(lib().ngp_init_mlp_parameters(_ptr(master), _ptr(params), _stream(stream)), "ngp_init_mlp_parameters")
+
+
+def init_grid_parameters(n_grid, master_grid, params_grid, stream=None) -> None:
+    """U(-1e-4, 1e-4) grid entries (initialize_grid_params_kernel, ngp.train.cu:1002-1017)."""
+    _check(lib().ngp_init_grid_parameters(_u32(n_grid), _ptr(master_grid), _ptr(params_grid), _stream(stream)), "ngp_init_grid_parameters")
 
 
 def adam_step(n_mlp, master, params, grads, m, v, steps, lr=1e-2, beta1=0.9, beta2=0.99, eps=1e-15, l2_reg=1e-6, loss_scale=128.0,
@@ -622,6 +636,18 @@ class InstantNGP:
         _check(lib().ngp_trainer_phase_times(self.handle, out, _u32(len(self.PHASES)), ctypes.byref(steps), ctypes.byref(mean_n)),
                "ngp_trainer_phase_times")
         return {"steps": steps.value, "mean_inference_samples": mean_n.value, "ms": dict(zip(self.PHASES, list(out)))}
+
+    GRID_PHASES = ("grid_samples", "grid_encode", "grid_density", "grid_splat", "grid_ema_bitfield")
+
+    def grid_phase_times(self) -> dict:
+        """Per-kernel times of the profiled steps' grid updates (accumulated ms), the number of
+        updates and their mean sample count."""
+        out = (ctypes.c_float * len(self.GRID_PHASES))()
+        updates = ctypes.c_uint32(0)
+        mean_n = ctypes.c_float(0)
+        _check(lib().ngp_trainer_grid_phase_times(self.handle, out, _u32(len(self.GRID_PHASES)), ctypes.byref(updates), ctypes.byref(mean_n)),
+               "ngp_trainer_grid_phase_times")
+        return {"updates": updates.value, "mean_samples": mean_n.value, "ms": dict(zip(self.GRID_PHASES, list(out)))}
 
     def join(self, unique_id: bytes, world: int, rank: int) -> None:
         """Join a data-parallel group of `world` trainers (one per GPU) before the first step."""

@@ -220,3 +220,29 @@ def blob_grid_values(blobs: dict) -> np.ndarray:
     vals = np.zeros(128 ** 3, np.float32)
     vals[morton.astype(np.int64)] = thick
     return vals
+
+
+def eval_composite_inputs(width: int = 64, height: int = 48, n_images: int = 2, max_steps: int = 40, seed: int = 0):
+    """Inputs of evaluation compositing for every pixel of image 1: per-pixel (count, base) with
+    counts in [0, max_steps] and ragged bases, sample records whose dt is U(0.5, 8) x sqrt(3)/1024,
+    raw network outputs ~ N(0, 2) fp16 [samples][16] (density raw N(2, 2)), and RGBA8 target
+    images with a mix of opaque, transparent and partial alpha."""
+    rng = np.random.default_rng(seed)
+    n = width * height
+    counts = rng.integers(0, max_steps + 1, n).astype(np.uint32)
+    counts[rng.random(n) < 0.1] = 0
+    gaps = rng.integers(0, 3, n).astype(np.uint32)
+    bases = (np.cumsum(counts + gaps) - counts).astype(np.uint32)
+    total = int(bases[-1] + counts[-1]) + 1
+    numsteps = np.stack([counts, bases], axis=1).astype(np.uint32)
+    coords = np.zeros((total, 7), np.float32)
+    coords[:, :3] = rng.random((total, 3), dtype=np.float32)
+    coords[:, 3] = (rng.uniform(0.5, 8.0, total) * math.sqrt(3.0) / 1024.0).astype(np.float32)
+    coords[:, 4:7] = rng.random((total, 3), dtype=np.float32)
+    out = rng.normal(0.0, 2.0, (total, 16)).astype(np.float16)
+    out[:, 3] = rng.normal(2.0, 2.0, total).astype(np.float16)
+    pixels = rng.integers(0, 256, (n_images, height, width, 4)).astype(np.uint8)
+    alpha = pixels[..., 3]
+    alpha[rng.random(alpha.shape) < 0.3] = 0
+    alpha[rng.random(alpha.shape) < 0.3] = 255
+    return numsteps, coords, out, pixels

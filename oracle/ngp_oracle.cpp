@@ -698,4 +698,90 @@ void oracle_adam(uint32_t n, uint32_t n_mlp, float lr, float b1, float b2, float
     oracle_adam_mt(n, n_mlp, lr, b1, b2, eps, l2, loss_scale, master, params, grads, m, v, steps, 1);
 }
 
+// ---- evaluation compositing (accumulate_evaluation_loss_kernel, ngp.train.cu:676-745) ------
+// Per pixel i of a tile starting at pixel_offset: front-to-back compositing of its samples
+// (numsteps[2i] = count, numsteps[2i+1] = base; stop once the transmittance falls below 1e-4),
+// the target read as premultiplied linear RGBA and converted back to sRGB (ngp.train.cu:264-293),
+// both clamped to [0, 1]; the fp64 squared error is summed in pixel order into *sse, and the
+// comparison image [height][2*width][3] (target left, render right) is written when given.
+// exp / pow come from libm (the reference uses the device's expf, __expf and powf), so results
+// agree with the GPU to a few ulp per operation, not bit for bit.
+namespace {
+inline float sigmoid_ref(float x) { return 1.0f / (1.0f + std::exp(-x)); }
+inline float srgb_to_linear_ref(float v) { return v <= 0.04045f ? v / 12.92f : std::pow((v + 0.055f) / 1.055f, 2.4f); }
+inline float linear_to_srgb_ref(float v) { return v < 0.0031308f ? 12.92f * v : std::fmaf(1.055f, std::pow(v, 0.41666f), -0.055f); }
+inline float clamp01(float v) { return std::fmin(std::fmax(v, 0.0f), 1.0f); }
+}  // namespace
+
+void oracle_eval_composite(uint32_t tile_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,
+                           const uint32_t* numsteps, const float* coords, const uint16_t* network_output, double* sse, uint8_t* comparison) {
+    double total = 0.0;
+    for (uint32_t i = 0; i < tile_pixels; ++i) {
+        const uint32_t gp = pixel_offset + i, px = gp % width, py = gp / width;
+        const uint32_t count = numsteps[2u * i], base = numsteps[2u * i + 1u];
+        float T = 1.0f, rgb[3] = {0.0f, 0.0f, 0.0f};
+        for (uint32_t j = 0; j < count; ++j) {
+            const uint16_t* o   = network_output + (static_cast<uint64_t>(base) + j) * 16u;
+            const float dt      = coords[(static_cast<uint64_t>(base) + j) * 7u + 3u];
+            const float density = std::exp(h2f(o[3]));
+            const float alpha   = 1.0f - std::exp(-density * dt);
+            const float weight  = alpha * T;
+            for (int c = 0; c < 3; ++c) rgb[c] = std::fmaf(weight, sigmoid_ref(h2f(o[c])), rgb[c]);
+            T *= 1.0f - alpha;
+            if (T < 1e-4f) break;
+        }
+        const uint8_t* t8 = pixels + 4u * (px + static_cast<uint64_t>(py) * width + static_cast<uint64_t>(image) * width * height);
+        const float a     = static_cast<float>(t8[3]) * (1.0f / 255.0f);
+        float target[3], pred[3];
+        for (int c = 0; c < 3; ++c) {
+            const float lin = srgb_to_linear_ref(static_cast<float>(t8[c]) * (1.0f / 255.0f)) * a;
+            target[c]       = clamp01(linear_to_srgb_ref(lin));
+            pred[c]         = clamp01(rgb[c]);
+            const double d  = static_cast<double>(pred[c]) - static_cast<double>(target[c]);
+            total += d * d;
+        }
+        if (comparison != nullptr) {
+            const uint64_t row = static_cast<uint64_t>(py) * width * 6u;
+            for (int c = 0; c < 3; ++c) {
+                comparison[row + px * 3u + c]                                      = static_cast<uint8_t>(target[c] * 255.0f + 0.5f);
+                comparison[row + (static_cast<uint64_t>(width) + px) * 3u + c] = static_cast<uint8_t>(pred[c] * 255.0f + 0.5f);
+            }
+        }
+    }
+    *sse += total;
+}
+
+// ---- seeded initialisation (ngp.train.cu:1002-1017, 1423-1490) -----------------------------
+// master[0, 10240): the MLP matrices in packed order (density W_in 64x32, W_out 16x64, rgb W_in
+// 64x32, W_h 64x64, W_out 16x64), each Xavier-uniform with scale sqrt(6 / (fan_in + fan_out)),
+// drawn one after another from one PCG32(1337) stream (initialize_mlp_parameters).
+// master[10240, 10240 + n_grid): U(-1e-4, 1e-4) grid entries; thread slot i of the reference's
+// launch (n_slots = ceil(ceil(n_grid / 4) / 128) * 128 threads) continues the stream after the
+// MLP's 10240 draws at offset 4i and writes entries i + n_slots * j, j < 4
+// (initialize_grid_params_kernel).  params = fp16 of master (round to nearest even).
+void oracle_init_params(uint32_t n_grid, float* master, uint16_t* params) {
+    const uint32_t shapes[5][2] = {{64, 32}, {16, 64}, {64, 32}, {64, 64}, {16, 64}};
+    Pcg rng(1337u);
+    uint32_t off = 0;
+    for (const auto& sh : shapes) {
+        const float scale = std::sqrt(6.0f / static_cast<float>(sh[0] + sh[1]));
+        for (uint32_t i = 0; i < sh[0] * sh[1]; ++i) {
+            const float u    = rng.next_float() * 2.0f;
+            master[off + i] = u * scale - scale;
+        }
+        off += sh[0] * sh[1];
+    }
+    const uint32_t slots = (((n_grid + 3u) / 4u + 127u) / 128u) * 128u;
+    for (uint32_t i = 0; i < slots; ++i) {
+        Pcg g(1337u);
+        g.advance(10240ull + 4ull * i);
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint64_t idx = i + static_cast<uint64_t>(slots) * j;
+            if (idx >= n_grid) break;
+            master[off + idx] = std::fmaf(g.next_float(), 2e-4f, -1e-4f);
+        }
+    }
+    for (uint32_t i = 0; i < off + n_grid; ++i) params[i] = f2h(master[i]);
+}
+
 }  // extern "C"

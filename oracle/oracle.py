@@ -22,6 +22,22 @@ SHIM_REPLAY_SO = HERE / "_ref" / "libngp_shim_replay.so"
 _u32p = ctypes.POINTER(ctypes.c_uint32)
 
 
+def reference_dir() -> Path | None:
+    """The reference's source tree: $NGP_REFERENCE_DIR, else BASELINE.json's reference_path; None
+    when neither names an existing tree (as on a GPU box, which uses the prebuilt _ref/)."""
+    import json
+    import os
+
+    cand = os.environ.get("NGP_REFERENCE_DIR")
+    if not cand:
+        baseline = HERE.parent / "BASELINE.json"
+        if baseline.exists():
+            cand = json.loads(baseline.read_text()).get("reference_path")
+    if cand and (Path(cand) / "ngp.train.cu").exists():
+        return Path(cand)
+    return None
+
+
 def build_oracle() -> Path:
     subprocess.run(["make", "-s", "-C", str(HERE), "libngp_oracle.so"], check=True)
     return ORACLE_SO
@@ -29,9 +45,10 @@ def build_oracle() -> Path:
 
 def build_ref() -> Path | None:
     """Build oracle/_ref from the reference sources when they are present (not on a GPU box)."""
-    if not Path("/root/reference/ngp.train.cu").exists():
+    ref = reference_dir()
+    if ref is None:
         return REF_SO if REF_SO.exists() else None
-    subprocess.run(["make", "-s", "-C", str(HERE), "ref", "shim"], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE), f"REF_DIR={ref}", "ref", "shim"], check=True)
     return REF_SO
 
 
@@ -262,6 +279,28 @@ def _oracle_sampler_methods():
                                               _p(numsteps), _p(coords), _p(t_out))
         return numsteps, coords[:total], t_out
 
+    def eval_composite(self, numsteps, coords, network_output, pixels, image, width, height, pixel_offset=0, n=None, comparison=True):
+        """Evaluation compositing of pixels [pixel_offset, pixel_offset + n) of `image`
+        (accumulate_evaluation_loss_kernel): returns (sse, comparison [height][2*width][3] or None)."""
+        numsteps = np.ascontiguousarray(numsteps, np.uint32)
+        n = numsteps.shape[0] if n is None else n
+        coords = np.ascontiguousarray(coords, np.float32)
+        out = np.ascontiguousarray(network_output).view(np.uint16)
+        pixels = np.ascontiguousarray(pixels, np.uint8)
+        sse = np.zeros(1, np.float64)
+        comp = np.zeros((height, 2 * width, 3), np.uint8) if comparison else None
+        self.lib.oracle_eval_composite(ctypes.c_uint32(n), ctypes.c_uint32(pixel_offset), ctypes.c_uint32(image), ctypes.c_uint32(width),
+                                       ctypes.c_uint32(height), _p(pixels), _p(numsteps), _p(coords), _p(out), _p(sse), _p(comp))
+        return float(sse[0]), comp
+
+    def init_params(self, n_grid: int):
+        """Seeded initial parameters (initialize_mlp_parameters + initialize_grid_params_kernel):
+        (fp32 master, fp16 params as uint16) of 10240 + n_grid entries."""
+        master = np.zeros(10240 + n_grid, np.float32)
+        params = np.zeros(10240 + n_grid, np.uint16)
+        self.lib.oracle_init_params(ctypes.c_uint32(n_grid), _p(master), _p(params))
+        return master, params
+
     def grid_samples(self, n_uniform, n_nonuniform, ema_step, values):
         values = np.ascontiguousarray(values, np.float32)
         n = n_uniform + n_nonuniform
@@ -287,7 +326,7 @@ def _oracle_sampler_methods():
         arrs[1] = arrs[1].view(np.float16)
         return [arrs[i] for i in (0, 1, 3, 4, 5)]
 
-    for f in (march_rays, march_rays_mt, march_segment, grid_samples, grid_update, adam):
+    for f in (march_rays, march_rays_mt, march_segment, eval_composite, init_params, grid_samples, grid_update, adam):
         setattr(Oracle, f.__name__, f)
 
 

@@ -152,6 +152,28 @@ int ref_adam(float* master, uint16_t* params, const uint16_t* grads, float* m, f
     return status_of(cudaDeviceSynchronize());
 }
 
+// accumulate_evaluation_loss_kernel (ngp.train.cu:676-745) with the reference's launch shape
+// (ngp.train.cu:1647): adds the tile's squared error to *sse, writes the comparison image when
+// given (the caller zeroes sse).
+int ref_eval_composite(uint32_t tile_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,
+                       const uint32_t* numsteps, const float* coords, const uint16_t* network_output, double* sse, uint8_t* comparison) {
+    ref::accumulate_evaluation_loss_kernel<<<(tile_pixels + ref::THREADS_PER_BLOCK - 1u) / ref::THREADS_PER_BLOCK, ref::THREADS_PER_BLOCK>>>(
+        tile_pixels, pixel_offset, image, width, height, pixels, numsteps, coords, reinterpret_cast<const __half*>(network_output), sse, comparison);
+    return status_of(cudaDeviceSynchronize());
+}
+
+// initialize_mlp_parameters + initialize_grid_parameters (ngp.train.cu:1423-1490) on the
+// reference's full parameter vector (total_param_count fp32 master, fp16 params and gradients).
+int ref_init_params(float* master, uint16_t* params, uint16_t* grads) {
+    try {
+        ref::initialize_mlp_parameters(master, params, grads);
+        ref::initialize_grid_parameters(master, params, grads);
+    } catch (const std::exception&) {
+        return 1;
+    }
+    return status_of(cudaDeviceSynchronize());
+}
+
 // PCG32 as the reference's device code runs it (ngp.train.cu:89-143), for pinning.
 int ref_pcg32(uint64_t initstate, uint64_t initseq, uint64_t advance, uint32_t count, uint32_t* out_uint, float* out_float) {
     ref::Pcg32 a{initstate, initseq};

@@ -98,9 +98,9 @@ int probe_write_png(const char* path, const std::uint8_t* rgb, std::uint32_t w, 
 int probe_lifecycle(std::uint32_t w, std::uint32_t h, std::uint32_t n_train, const std::uint8_t* train_px, const float* train_cam,
                     std::uint32_t n_test, const std::uint8_t* test_px, const float* test_cam, const float* intrinsics, std::int32_t steps,
                     const char* out_dir, double* results, char* err, std::size_t en) {
-    using ngp::b200::train::InstantNGP;
+    using ngp::train::InstantNGP;  // the reference's names (aliases of ngp::b200::*)
     try {
-        ngp::b200::dataset::NGPDataset ds;
+        ngp::dataset::NGPDataset ds;
         ds.train       = frames(n_train, w, h, train_px, train_cam, intrinsics);
         ds.validation  = frames(n_test, w, h, test_px, test_cam, intrinsics);
         ds.test        = frames(n_test, w, h, test_px, test_cam, intrinsics);

@@ -41,3 +41,14 @@ def test_version_and_error_state(ngp):
 def test_struct_size_matches_header(ngp):
     # 4 u32 + double + 33 u32 + 32 u32 + 32 f32 + 2 u32 (+ alignment padding)
     assert ctypes.sizeof(ngp.GridLayout) == 4 * 4 + 8 + 33 * 4 + 32 * 4 + 32 * 4 + 2 * 4 + 4
+
+
+def test_loss_scratch_size_refuses_sizes_beyond_32_bits(ngp):
+    """The exported scratch size is a uint32: sizes that do not fit are refused (0, error set)
+    instead of wrapping to a buffer that is too small."""
+    lib = ngp.lib()
+    lib.ngp_loss_scratch_bytes.restype = ctypes.c_uint32
+    assert lib.ngp_loss_scratch_bytes(ctypes.c_uint32(1 << 18)) > 20 * (1 << 18)
+    assert lib.ngp_last_error() == b""
+    assert lib.ngp_loss_scratch_bytes(ctypes.c_uint32(0xFFFFFFFF)) == 0
+    assert b"uint32" in lib.ngp_last_error()
