@@ -40,6 +40,7 @@ extern "C" {
 #define NGP_ERR_CUDA 2      /* a CUDA runtime call or kernel launch failed                  */
 #define NGP_ERR_OVERFLOW 3  /* a device-side budget overflowed (e.g. evaluation samples)    */
 #define NGP_ERR_STATE 4     /* call out of order (e.g. training stopped: no samples)        */
+#define NGP_ERR_TIMEOUT 5   /* a collective did not complete in time; the communicator was aborted */
 
 #define NGP_MAX_LEVELS 32
 #define NGP_SAMPLE_FLOATS 7
@@ -49,6 +50,15 @@ extern "C" {
 NGP_API const char* ngp_last_error(void);
 /* Library version string. */
 NGP_API const char* ngp_version(void);
+
+/* Host-side fault injection for testing callers' error paths (no reference counterpart: the
+ * reference throws std::runtime_error on a failed CUDA call, ngp.train.cu:1290, and its trainer
+ * turns that into std::unexpected, ngp.train.cpp:152-154).  Arms `site` (1 = device allocation of
+ * the trainer, 2 = kernel launch, 3 = collective) so that its countdown-th event from now returns
+ * NGP_ERR_CUDA with the message "... injected fault (...)"; 0 disarms.  The injected failure is a
+ * status returned by the host: no GPU fault is raised.  The environment variable
+ * NGP_FAULT_INJECT="alloc:N" | "launch:N" | "collective:N" arms a site when the library loads. */
+NGP_API int ngp_fault_inject(int site, int64_t countdown);
 /* Kernel launches made by this library in this process so far, all threads and devices
  * (diagnostics for benchmarks; no counterpart in the reference). */
 NGP_API uint64_t ngp_kernel_launch_count(void);
@@ -183,6 +193,15 @@ NGP_API int ngp_density_grid_mark_untrained(const float* camera, uint32_t frame_
  * and cell indices.  Replaces generate_density_grid_samples_kernel (ngp.train.cu:383-424). */
 NGP_API int ngp_density_grid_samples(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords,
                                      uint32_t* indices, void* stream);
+/* The same samples as ngp_density_grid_samples (identical records and cell indices), placed in
+ * Morton cell order of each sample's first hashed cell instead of sample order, so that the
+ * encoding of the samples reads neighbouring table entries across a warp.  Each set holds at
+ * most 2^21 samples.  counter: one device word of scratch (unused when n_uniform = 2^21 and
+ * n_nonuniform = 0); the order within a warp is fixed, the order of warps is not.  The density
+ * grid update consumes the samples with an order-independent atomic max, so its result is the
+ * reference's (generate_density_grid_samples_kernel, ngp.train.cu:383-424). */
+NGP_API int ngp_density_grid_samples_cell_order(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords,
+                                                uint32_t* indices, uint32_t* counter, void* stream);
 
 /* scratch[indices[i]] = max(scratch[indices[i]], exp(density[i]) * sqrt(3)/1024).
  * Replaces splat_density_grid_samples_kernel (ngp.train.cu:426-432). */
@@ -418,6 +437,15 @@ NGP_API int ngp_adam_step_f16(uint32_t n_params, uint32_t n_mlp, float lr, float
                               float* params_full_precision, uint16_t* params, const uint16_t* gradients, float* first_moments,
                               float* second_moments, uint32_t* param_steps, const float* lr_table, uint32_t table_len, void* stream);
 
+/* ngp_adam_step_f16 on the range [first, first + count) of the packed vector (one rank's shard
+ * of the data-parallel exchange): every pointer points at element `first`; first is a multiple
+ * of 4; elements with packed index < n_mlp are the dense MLP weights.  Replaces the part of
+ * adam_step_kernel (ngp.train.cu:1261-1280) that this rank owns. */
+NGP_API int ngp_adam_step_f16_range(uint32_t count, uint32_t first, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg,
+                                    float loss_scale, float* params_full_precision, uint16_t* params, const uint16_t* gradients,
+                                    float* first_moments, float* second_moments, uint32_t* param_steps, const float* lr_table,
+                                    uint32_t table_len, void* stream);
+
 /* fp32 gradients -> fp16 (round to nearest); clear != 0 zeroes the fp32 source. */
 NGP_API int ngp_gradients_to_half(uint32_t n, float* gradients, uint16_t* out, int clear, void* stream);
 
@@ -486,19 +514,28 @@ NGP_API void ngp_adaptive_batch(uint32_t rays_per_batch, uint32_t measured_befor
 NGP_API uint32_t ngp_trainer_param_count(const ngp_trainer* t);
 /* fp32 master parameters [MLP | grid] to / from the host (export_weights / load_weights;
  * loading resets the optimizer and is allowed only before training, ngp.train.cpp:312). */
-NGP_API int ngp_trainer_get_params(const ngp_trainer* t, float* host_out, uint32_t count);
+NGP_API int ngp_trainer_get_params(ngp_trainer* t, float* host_out, uint32_t count);
 NGP_API int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_t count);
 /* Data parallelism over NVLink (no counterpart in the single-GPU reference; hooks between
  * backward_network and step_optimizer, ngp.train.cpp:123-124).  Rank 0 creates an NCCL unique id
  * (ngp_nccl_unique_id, 128 bytes), the caller shares it with every rank, and each rank's trainer
  * joins before its first step.  Each rank then marches its own rays (PCG32 stream step*world +
- * rank) and the fp32 gradient is averaged with one all-reduce per step. */
+ * rank); per step the fp32 gradients are rounded to fp16 (loss-scaled, the reference's gradient
+ * format) and reduce-scattered, each rank takes the Adam step on its 1/world shard, and the fp16
+ * parameters are all-gathered (replicas stay bit-identical).  The communicator is non-blocking:
+ * a collective, or a wait for the stream that runs it, that does not complete within the
+ * collective timeout (default 120 s, $NGP_COLLECTIVE_TIMEOUT_MS, or
+ * ngp_trainer_set_collective_timeout) aborts the communicator and returns NGP_ERR_TIMEOUT; an
+ * asynchronous NCCL error aborts it and returns NGP_ERR_CUDA.  After a data-parallel join,
+ * ngp_trainer_get_params is a collective (every rank calls it). */
 NGP_API int ngp_nccl_unique_id(uint8_t* out, size_t bytes);
 NGP_API int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank);
+NGP_API int ngp_trainer_set_collective_timeout(ngp_trainer* t, double timeout_ms);
 /* Per-phase device time of the training step, summed over the steps since profiling was
  * enabled (cudaEvents between phases): 0 grid update, 1 ray marching, 2 density evaluation of the
  * marched samples + compaction, 3 network forward of the compacted samples + loss + padding,
- * 4 network backward, 5 encoding backward, 6 gradient all-reduce, 7 Adam.  out_ms needs 8 floats;
+ * 4 network backward, 5 encoding backward, 6 gradient exchange (fp16 conversion +
+ * reduce-scatter), 7 Adam (+ all-gather of the fp16 parameters).  out_ms needs 8 floats;
  * out_mean_inference_samples = mean marched samples per step. */
 NGP_API int ngp_trainer_set_profiling(ngp_trainer* t, int enable);
 NGP_API int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_steps, float* out_mean_inference_samples);

@@ -28,6 +28,7 @@ struct AdamParams {
     int clear_grid_grad;
     const float* lr_table;  // optional: lr_table[t] = bias-corrected rate after t steps, t <= table_len
     uint32_t table_len;
+    uint32_t first;  // index of element 0 in the packed vector (a shard of it; a multiple of 4)
 };
 
 // Bias-corrected learning rate after `step` steps (ngp.train.cu:1275).
@@ -37,10 +38,11 @@ __device__ __forceinline__ float corrected_lr(float lr, float beta1, float beta2
 
 __device__ __forceinline__ void adam_one(const AdamParams& p, uint32_t i, float& master, float graw, float& m, float& v, uint32_t& step,
                                          __half& out) {
-    float g = graw * p.inv_loss_scale;
-    if (i >= p.n_mlp && g == 0.0f) return;
+    float g          = graw * p.inv_loss_scale;
+    const bool dense = p.first + i < p.n_mlp;
+    if (!dense && g == 0.0f) return;
     const float w = master;
-    if (i < p.n_mlp) g = __fmaf_rn(p.l2, w, g);
+    if (dense) g = __fmaf_rn(p.l2, w, g);
     m = __fmaf_rn(p.beta1, m, (1.0f - p.beta1) * g);
     v = __fmaf_rn(p.beta2, v, (1.0f - p.beta2) * (g * g));
     step += 1u;
@@ -70,7 +72,7 @@ __global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamP
     if (i0 >= p.n_params) return;
     if (i0 + 4u <= p.n_params) {
         const float4 g  = load_grad4<HALF_GRAD>(p, q);
-        const bool grid = i0 >= p.n_mlp;
+        const bool grid = p.first + i0 >= p.n_mlp;
         if (grid && g.x == 0.0f && g.y == 0.0f && g.z == 0.0f && g.w == 0.0f) return;  // untouched entries: one 16-byte read
         float4 w  = reinterpret_cast<float4*>(p.master)[q];
         float4 m  = reinterpret_cast<float4*>(p.m)[q];
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(256) adam_kernel(const __grid_constant__ AdamP
     for (uint32_t i = i0; i < p.n_params; ++i) {
         const float g = HALF_GRAD ? __half2float(p.grad16[i]) : p.grad[i];
         adam_one(p, i, p.master[i], g, p.m[i], p.v[i], p.steps[i], p.params[i]);
-        if (!HALF_GRAD && i >= p.n_mlp && p.clear_grid_grad) p.grad[i] = 0.0f;
+        if (!HALF_GRAD && p.first + i >= p.n_mlp && p.clear_grid_grad) p.grad[i] = 0.0f;
     }
 }
 
@@ -104,10 +106,12 @@ __global__ void lr_table_kernel(float* __restrict__ table, uint32_t first, uint3
 
 int adam_launch(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg, float loss_scale,
                 float* params_full_precision, uint16_t* params, float* gradients, const uint16_t* gradients16, float* first_moments,
-                float* second_moments, uint32_t* param_steps, int clear_grid_gradients, const float* lr_table, uint32_t table_len, void* stream) {
+                float* second_moments, uint32_t* param_steps, int clear_grid_gradients, const float* lr_table, uint32_t table_len, void* stream,
+                uint32_t first = 0) {
     if (n_params == 0) return NGP_OK;
+    if (first % 4u != 0) return fail(NGP_ERR_INVALID, "adam: the first index of a range must be a multiple of 4");
     if (params_full_precision == nullptr || params == nullptr || (gradients == nullptr) == (gradients16 == nullptr) || first_moments == nullptr ||
-        second_moments == nullptr || param_steps == nullptr || n_mlp > n_params || n_mlp % 4u != 0 || loss_scale == 0.0f ||
+        second_moments == nullptr || param_steps == nullptr || (first == 0 && n_mlp > n_params) || n_mlp % 4u != 0 || loss_scale == 0.0f ||
         (table_len > 0 && lr_table == nullptr))
         return fail(NGP_ERR_INVALID, "adam: invalid input");
     if ((reinterpret_cast<uintptr_t>(params_full_precision) | reinterpret_cast<uintptr_t>(gradients) | reinterpret_cast<uintptr_t>(first_moments) |
@@ -116,7 +120,8 @@ int adam_launch(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float 
         return fail(NGP_ERR_INVALID, "adam: buffers must be 16-byte aligned (fp16 buffers 8-byte)");
     AdamParams p{n_params,      n_mlp,     lr,       beta1,    beta2,       eps,
                  l2_reg,        1.0f / loss_scale, params_full_precision, reinterpret_cast<__half*>(params), gradients,
-                 reinterpret_cast<const __half*>(gradients16), first_moments, second_moments, param_steps, clear_grid_gradients, lr_table, table_len};
+                 reinterpret_cast<const __half*>(gradients16), first_moments, second_moments, param_steps, clear_grid_gradients, lr_table, table_len,
+                 first};
     const uint32_t groups = (n_params + 3u) / 4u;
     if (gradients16 != nullptr)
         adam_kernel<true><<<(groups + 255u) / 256u, 256, 0, as_stream(stream)>>>(p);
@@ -169,6 +174,16 @@ extern "C" int ngp_adam_step_f16(uint32_t n_params, uint32_t n_mlp, float lr, fl
     if (gradients == nullptr) return fail(NGP_ERR_INVALID, "adam: null gradients");
     return adam_launch(n_params, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, nullptr, gradients,
                        first_moments, second_moments, param_steps, 0, lr_table, table_len, stream);
+}
+
+extern "C" int ngp_adam_step_f16_range(uint32_t count, uint32_t first, uint32_t n_mlp, float lr, float beta1, float beta2, float eps, float l2_reg,
+                                       float loss_scale, float* params_full_precision, uint16_t* params, const uint16_t* gradients,
+                                       float* first_moments, float* second_moments, uint32_t* param_steps, const float* lr_table,
+                                       uint32_t table_len, void* stream) {
+    clear_error();
+    if (gradients == nullptr) return fail(NGP_ERR_INVALID, "adam: null gradients");
+    return adam_launch(count, n_mlp, lr, beta1, beta2, eps, l2_reg, loss_scale, params_full_precision, params, nullptr, gradients, first_moments,
+                       second_moments, param_steps, 0, lr_table, table_len, stream, first);
 }
 
 extern "C" int ngp_gradients_to_half(uint32_t n, float* gradients, uint16_t* out, int clear, void* stream) {

@@ -23,9 +23,19 @@ inline int fail(int code, const std::string& message) {
 
 void count_launch();
 
+// Host-side fault injection (ngp_fault_inject / $NGP_FAULT_INJECT): true when the armed
+// countdown of `site` reaches this event, which then reports an error instead of its result.
+// No device code is involved: the injected failure is a status the host returns.
+enum FaultSite : int { kFaultAlloc = 1, kFaultLaunch = 2, kFaultCollective = 3 };
+bool fault_due(FaultSite site);
+
 // Called once after every kernel launch of the library (also counts it).
 inline int check_launch(const char* what) {
     count_launch();
+    if (fault_due(kFaultLaunch)) {
+        (void)cudaGetLastError();
+        return fail(NGP_ERR_CUDA, std::string(what) + ": injected fault (launch)");
+    }
     const cudaError_t status = cudaGetLastError();
     if (status != cudaSuccess) return fail(NGP_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(status));
     return NGP_OK;

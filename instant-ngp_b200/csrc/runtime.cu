@@ -1,6 +1,8 @@
 // Library runtime: per-thread error state, device queries and the hash-grid layout.
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 #include <limits>
 
 #include "common.cuh"
@@ -15,6 +17,31 @@ std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 void set_error(const std::string& message) { g_last_error = message; }
 void clear_error() { g_last_error.clear(); }
+
+// Fault injection: countdown[site] > 0 arms the site; the event that brings it to zero fails.
+namespace {
+std::atomic<int64_t> g_fault_countdown[4] = {};
+
+// $NGP_FAULT_INJECT = "<site>:<n>" (site alloc | launch | collective) arms one site at load.
+struct FaultEnv {
+    FaultEnv() {
+        const char* v = std::getenv("NGP_FAULT_INJECT");
+        if (v == nullptr) return;
+        const char* colon = std::strchr(v, ':');
+        if (colon == nullptr) return;
+        const std::string site(v, colon);
+        const long long n = std::atoll(colon + 1);
+        const int idx     = site == "alloc" ? kFaultAlloc : site == "launch" ? kFaultLaunch : site == "collective" ? kFaultCollective : 0;
+        if (idx != 0 && n > 0) g_fault_countdown[idx].store(n);
+    }
+} g_fault_env;
+}  // namespace
+
+bool fault_due(FaultSite site) {
+    std::atomic<int64_t>& c = g_fault_countdown[site];
+    if (c.load(std::memory_order_relaxed) <= 0) return false;
+    return c.fetch_sub(1) == 1;
+}
 
 int sm_count() {
     static int cached = [] {
@@ -33,6 +60,13 @@ using namespace ngp;
 extern "C" const char* ngp_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" uint64_t ngp_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+extern "C" int ngp_fault_inject(int site, int64_t countdown) {
+    clear_error();
+    if (site < kFaultAlloc || site > kFaultCollective || countdown < 0) return fail(NGP_ERR_INVALID, "fault inject: bad site or countdown");
+    g_fault_countdown[site].store(countdown);
+    return NGP_OK;
+}
 
 extern "C" const char* ngp_version(void) { return "ngp_b200 0.1 (sm_100a)"; }
 

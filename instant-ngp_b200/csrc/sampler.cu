@@ -93,6 +93,92 @@ __global__ void generate_grid_samples_kernel(uint32_t n_uniform, uint32_t n_nonu
     indices[g] = idx;
 }
 
+// K2 in cell order.  Sample i's first cell is ((i + ema_step * count) * 56924617 + 96925573) mod
+// 2^21 (the reference's hash with j = 0): an odd multiplier makes this a bijection of [0, 2^21),
+// so every cell g is the first cell of exactly one index i = (g - 96925573) * 56924617^-1 -
+// ema_step * count (mod 2^21) of each sample set, and that sample exists iff i < count.  Thread g
+// generates those samples (the same records and cell indices as generate_grid_samples_kernel:
+// same PCG32 draws, same retries), so consecutive samples lie in consecutive Morton cells and the
+// encoding of the grid samples gathers neighbouring table entries across a warp instead of
+// random ones.  Only the order of the samples differs, which the update does not see: each
+// sample's density is splatted with an atomic max into its own cell.
+// With all 2^21 samples uniform (the first 256 steps) thread g writes slot g; otherwise a warp
+// reserves its slots with one atomic on *counter (zeroed by the caller): the warp's samples stay
+// in cell order, warps in any order.
+constexpr uint32_t kGridHashMul    = 56924617u;
+constexpr uint32_t kGridHashMulInv = 53369u;  // inverse of 56924617 modulo 2^21
+constexpr uint32_t kGridHashAdd    = 96925573u;
+
+__device__ __forceinline__ void grid_sample_record(uint32_t i, uint32_t count, uint32_t ema_step, float thresh, uint64_t base_state,
+                                                   const uint64_t* __restrict__ jm, const uint64_t* __restrict__ jp,
+                                                   const float* __restrict__ values, float* __restrict__ c, uint32_t* __restrict__ index) {
+    uint32_t idx = 0;
+    for (uint32_t j = 0; j < 10; ++j) {
+        idx = static_cast<uint32_t>(((static_cast<uint64_t>(i) + static_cast<uint64_t>(ema_step) * count) * 56924617ull +
+                                     static_cast<uint64_t>(j) * 19349663ull + 96925573ull) %
+                                    kGridCells);
+        if (values[idx] > thresh) break;
+    }
+    // the stream of sample i: the set's base state advanced by 4 i steps (shared-memory jump
+    // table: one multiply-add per set bit of 4 i)
+    uint64_t state = base_state;
+    for (uint64_t delta = static_cast<uint64_t>(i) * 4ull; delta != 0u; delta &= delta - 1u) {
+        const int k = __ffsll(static_cast<long long>(delta)) - 1;
+        state       = jm[k] * state + jp[k];
+    }
+    Pcg32 rng{0u};
+    rng.state = state;
+    rng.inc   = 3u;
+    const uint32_t x = morton_compact(idx), y = morton_compact(idx >> 1), z = morton_compact(idx >> 2);
+    c[0]   = (static_cast<float>(x) + rng.next_float()) / 128.0f;
+    c[1]   = (static_cast<float>(y) + rng.next_float()) / 128.0f;
+    c[2]   = (static_cast<float>(z) + rng.next_float()) / 128.0f;
+    c[3]   = kConeStep;
+    c[4]   = 0.5f;
+    c[5]   = 0.5f;
+    c[6]   = 0.5f;
+    *index = idx;
+}
+
+__global__ void __launch_bounds__(256) generate_grid_samples_ordered_kernel(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step,
+                                                                            uint64_t base_uniform, uint64_t base_nonuniform,
+                                                                            const float* __restrict__ values, float* __restrict__ coords,
+                                                                            uint32_t* __restrict__ indices, uint32_t* __restrict__ counter) {
+    __shared__ uint64_t jm[64], jp[64];
+    if (threadIdx.x < 64) jm[threadIdx.x] = c_pcg_jump.mult[threadIdx.x];
+    else if (threadIdx.x < 128) jp[threadIdx.x - 64] = c_pcg_jump.plus[threadIdx.x - 64];
+    __syncthreads();
+    const uint32_t g   = blockIdx.x * blockDim.x + threadIdx.x;  // cell (Morton index)
+    const uint32_t rel = (g - (kGridHashAdd & (kGridCells - 1u))) * kGridHashMulInv;  // i + ema_step * count (mod 2^21)
+    const uint32_t iu  = (rel - ema_step * n_uniform) & (kGridCells - 1u);
+    const uint32_t in  = (rel - ema_step * n_nonuniform) & (kGridCells - 1u);
+    const bool has_u   = iu < n_uniform;
+    const bool has_n   = in < n_nonuniform;
+    uint32_t slot      = g;
+    if (counter != nullptr) {
+        const uint32_t lane = threadIdx.x & 31u;
+        const uint32_t cnt  = static_cast<uint32_t>(has_u) + static_cast<uint32_t>(has_n);
+        uint32_t incl       = cnt;
+#pragma unroll
+        for (uint32_t o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+        uint32_t base        = 0;
+        if (lane == 31 && total > 0) base = atomicAdd(counter, total);
+        base = __shfl_sync(0xFFFFFFFFu, base, 31);
+        slot = base + incl - cnt;
+    }
+    if (has_u) {
+        grid_sample_record(iu, n_uniform, ema_step, -0.01f, base_uniform, jm, jp, values, coords + static_cast<uint64_t>(slot) * 7u, indices + slot);
+        ++slot;
+    }
+    if (has_n)
+        grid_sample_record(in, n_nonuniform, ema_step, kMinOpticalThick, base_nonuniform, jm, jp, values, coords + static_cast<uint64_t>(slot) * 7u,
+                           indices + slot);
+}
+
 // K3 (ngp.train.cu:426-432): scratch[cell] = max(scratch[cell], exp(raw density) * dt).
 __global__ void splat_kernel(uint32_t n, const uint32_t* __restrict__ indices, const __half* __restrict__ density, float* __restrict__ scratch) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -462,6 +548,26 @@ extern "C" int ngp_density_grid_samples(uint32_t n_uniform, uint32_t n_nonunifor
     if (values == nullptr || coords == nullptr || indices == nullptr) return fail(NGP_ERR_INVALID, "grid samples: null pointer");
     generate_grid_samples_kernel<<<(n + 127) / 128, 128, 0, as_stream(stream)>>>(n_uniform, n_nonuniform, ema_step, values, coords, indices);
     return check_launch("generate_grid_samples_kernel");
+}
+
+extern "C" int ngp_density_grid_samples_cell_order(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords,
+                                                   uint32_t* indices, uint32_t* counter, void* stream) {
+    clear_error();
+    const uint32_t n = n_uniform + n_nonuniform;
+    if (n == 0) return NGP_OK;
+    if (values == nullptr || coords == nullptr || indices == nullptr) return fail(NGP_ERR_INVALID, "grid samples: null pointer");
+    if (n_uniform > kGridCells || n_nonuniform > kGridCells) return fail(NGP_ERR_INVALID, "grid samples (cell order): at most 2^21 samples per set");
+    const bool direct = n_uniform == kGridCells && n_nonuniform == 0;
+    if (!direct && counter == nullptr) return fail(NGP_ERR_INVALID, "grid samples (cell order): counter needed unless all 2^21 samples are uniform");
+    const cudaStream_t s = as_stream(stream);
+    if (!direct) NGP_TRY(check_cuda(cudaMemsetAsync(counter, 0, sizeof(uint32_t), s), "grid samples: clear counter"));
+    // the sets' streams before the per-sample jump: PCG32(1337) advanced by (2 ema_step + phase + 1) << 32
+    Pcg32 u{kTrainSeed}, v{kTrainSeed};
+    u.advance((static_cast<uint64_t>(ema_step) * 2ull + 1ull) << 32u);
+    v.advance((static_cast<uint64_t>(ema_step) * 2ull + 2ull) << 32u);
+    generate_grid_samples_ordered_kernel<<<kGridCells / 256u, 256, 0, s>>>(n_uniform, n_nonuniform, ema_step, u.state, v.state, values, coords, indices,
+                                                                           direct ? nullptr : counter);
+    return check_launch("generate_grid_samples_ordered_kernel");
 }
 
 extern "C" int ngp_density_grid_splat(uint32_t n, const uint32_t* indices, const uint16_t* density, float* scratch, void* stream) {

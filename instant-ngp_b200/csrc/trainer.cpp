@@ -12,9 +12,12 @@
 // * evaluation marches 2^16-pixel tiles a segment at a time and stops marching a ray once its
 //   transmittance is spent, instead of marching every occupied step of 4096-pixel tiles.
 #include <algorithm>
+#include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -46,6 +49,7 @@ template <typename T>
 int dalloc(T*& p, size_t count, const char* what) {
     p = nullptr;
     if (count == 0) return NGP_OK;
+    if (fault_due(kFaultAlloc)) return fail(NGP_ERR_CUDA, std::string("cudaMalloc ") + what + ": injected fault (alloc)");
     void* raw           = nullptr;
     const cudaError_t e = cudaMalloc(&raw, count * sizeof(T));
     if (e != cudaSuccess) return fail(NGP_ERR_CUDA, std::string("cudaMalloc ") + what + ": " + cudaGetErrorString(e));
@@ -100,6 +104,7 @@ struct ngp_trainer {
     uint32_t* grid_indices = nullptr;
     uint8_t* bitfield      = nullptr;
     uint32_t* occupied     = nullptr;
+    uint32_t* grid_counter = nullptr;  // slot counter of the cell-ordered grid samples
 
     // sampler and network buffers
     // Two sets of march outputs, used by alternate steps, so that the next step's march can run
@@ -144,6 +149,13 @@ struct ngp_trainer {
     // data parallelism: one trainer per GPU, rays split by rank, gradients all-reduced
     ncclComm_t comm = nullptr;
     int world = 1, rank = 0;
+    // the gradient exchange: fp16 gradients [n_padded] are reduce-scattered, each rank's Adam
+    // updates its shard [rank * shard, rank * shard + shard) and the fp16 parameters [n_padded]
+    // are all-gathered; n_padded = n_params rounded up to a multiple of 4 * world
+    uint32_t n_padded = 0, shard = 0;
+    // a collective (or a wait on a stream that runs one) that takes longer fails: the
+    // communicator is aborted and the call returns NGP_ERR_TIMEOUT
+    double collective_timeout_ms = 120000.0;
     // optional per-phase timing (cudaEvents between the phases of a step)
     bool profiling = false;
     cudaEvent_t marks[kTrainPhases + 1] = {};
@@ -195,12 +207,26 @@ void destroy(ngp_trainer* t) {
     free_split(t->val);
     free_split(t->test);
     void* ptrs[] = {t->master, t->params, t->grads, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->grid_values, t->grid_scratch, t->grid_partial,
-                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->rows, t->batch_rows, t->dens, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
+                    t->grid_mean, t->grid_indices, t->bitfield, t->occupied, t->grid_counter, t->march_scratch, t->eval_march_scratch, t->enc, t->out, t->rows, t->batch_rows, t->dens, t->cout, t->grid_density, t->ccoords, t->dloss, t->loss_values, t->loss_scratch, t->cenc, t->denc,
                     t->mlp_scratch, t->eval_sse, t->comparison, t->lr_table, t->seg_tout, t->seg_tstate, t->seg_marched, t->seg_state,
                     t->seg_lists, t->seg_counters};
     for (void* p : ptrs) cudaFree(p);
     for (MarchSet& m : t->sets) cudaFree(m.coords), cudaFree(m.rays), cudaFree(m.ray_indices), cudaFree(m.numsteps), cudaFree(m.counters);
-    if (t->comm) ncclCommDestroy(t->comm);
+    if (t->comm) {
+        // non-blocking communicator: finalize (bounded wait), then destroy; abort if it hangs
+        const ncclResult_t fr = ncclCommFinalize(t->comm);
+        bool finalized        = fr == ncclSuccess || fr == ncclInProgress;
+        const auto start      = std::chrono::steady_clock::now();
+        ncclResult_t a        = ncclInProgress;
+        while (finalized && a == ncclInProgress) {
+            ncclCommGetAsyncError(t->comm, &a);
+            if (std::chrono::steady_clock::now() - start > std::chrono::seconds(10)) finalized = false;
+        }
+        if (finalized && a == ncclSuccess)
+            ncclCommDestroy(t->comm);
+        else
+            ncclCommAbort(t->comm);
+    }
     if (t->march_stream) cudaStreamSynchronize(t->march_stream);
     for (cudaEvent_t e : t->marks)
         if (e) cudaEventDestroy(e);
@@ -298,7 +324,10 @@ int update_grid(ngp_trainer* t) {
     const uint32_t n_nonuni  = t->step < 256u ? 0u : kGridCells / 4u;
     const uint32_t n         = n_uniform + n_nonuni;
     float* coords = t->sets[t->step & 1u].coords;
-    NGP_TRY(ngp_density_grid_samples(n_uniform, n_nonuni, t->ema_step, t->grid_values, coords, t->grid_indices, t->stream));
+    // the reference's samples in Morton cell order (the encoding below then gathers neighbouring
+    // table entries); the splat's atomic max does not depend on their order
+    NGP_TRY(ngp_density_grid_samples_cell_order(n_uniform, n_nonuni, t->ema_step, t->grid_values, coords, t->grid_indices, t->grid_counter,
+                                                t->stream));
     grid_mark(t, 1);
     NGP_TRY(encode(t, n, coords, t->enc, n));
     grid_mark(t, 2);
@@ -344,6 +373,81 @@ int march_step(ngp_trainer* t, uint32_t step, cudaStream_t stream) {
 
 void mark(ngp_trainer* t, int k) {
     if (t->profiling) cudaEventRecord(t->marks[k], t->stream);
+}
+
+// ---- collectives with a host deadline ------------------------------------------------------
+// The communicator is non-blocking (ncclCommInitRankConfig, blocking = 0): an NCCL call may
+// return ncclInProgress while it is enqueued, and a peer that has left or hangs shows up as an
+// asynchronous error or as a wait that never ends.  Every wait on a communicator (its
+// initialisation, a call in progress, the stream that runs its kernels) polls
+// ncclCommGetAsyncError until the trainer's collective timeout; on expiry or error the
+// communicator is aborted (ncclCommAbort ends its kernels) and the call returns an error.
+int abort_comm(ngp_trainer* t, int code, const std::string& message) {
+    if (t->comm != nullptr) {
+        ncclCommAbort(t->comm);
+        t->comm = nullptr;
+    }
+    return fail(code, message);
+}
+
+template <typename Done>
+int wait_comm(ngp_trainer* t, Done&& done, const char* what) {
+    const auto start = std::chrono::steady_clock::now();
+    for (uint32_t spin = 0;; ++spin) {
+        const int d = done();
+        if (d > 0) return NGP_OK;
+        if (d < 0) return abort_comm(t, NGP_ERR_CUDA, std::string(what) + ": " + ngp_last_error());
+        if (t->comm != nullptr) {
+            ncclResult_t async = ncclSuccess;
+            ncclCommGetAsyncError(t->comm, &async);
+            if (async != ncclSuccess && async != ncclInProgress)
+                return abort_comm(t, NGP_ERR_CUDA, std::string(what) + ": NCCL error " + ncclGetErrorString(async) + "; communicator aborted");
+        }
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - start).count();
+        if (ms > t->collective_timeout_ms)
+            return abort_comm(t, NGP_ERR_TIMEOUT, std::string(what) + ": not complete after " + std::to_string(static_cast<long long>(ms)) +
+                                                    " ms (a peer rank may have left); communicator aborted");
+        if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(spin > 4096 ? 200 : 5));
+    }
+}
+
+// Waits for an event recorded on a stream that may run collectives (plain synchronisation when
+// the trainer has no communicator).
+int wait_event(ngp_trainer* t, cudaEvent_t ev, const char* what) {
+    if (t->comm == nullptr) return check_cuda(cudaEventSynchronize(ev), what);
+    return wait_comm(t, [&]() -> int {
+        const cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return 1;
+        if (e == cudaErrorNotReady) return 0;
+        check_cuda(e, what);
+        return -1;
+    }, what);
+}
+
+int wait_stream(ngp_trainer* t, cudaStream_t s, const char* what) {
+    if (t->comm == nullptr) return check_cuda(cudaStreamSynchronize(s), what);
+    return wait_comm(t, [&]() -> int {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return 1;
+        if (e == cudaErrorNotReady) return 0;
+        check_cuda(e, what);
+        return -1;
+    }, what);
+}
+
+// Result of an NCCL call on the non-blocking communicator: waits while it is in progress.
+int nccl_done(ngp_trainer* t, ncclResult_t r, const char* what) {
+    if (fault_due(kFaultCollective)) return abort_comm(t, NGP_ERR_CUDA, std::string(what) + ": injected fault (collective)");
+    if (r == ncclSuccess) return NGP_OK;
+    if (r != ncclInProgress) return abort_comm(t, NGP_ERR_CUDA, std::string(what) + ": " + ncclGetErrorString(r) + "; communicator aborted");
+    return wait_comm(t, [&]() -> int {
+        ncclResult_t a = ncclSuccess;
+        ncclCommGetAsyncError(t->comm, &a);
+        if (a == ncclSuccess) return 1;
+        if (a == ncclInProgress) return 0;
+        set_error(ncclGetErrorString(a));
+        return -1;
+    }, what);
 }
 
 // One training step.  `premarch_next`: march step + 1 on march_stream once this step's counters
@@ -415,7 +519,7 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     // adaptive batch (ngp.train.cpp:125-133): this step's counters were copied after the loss
     // pass; the host waits for them while the backward pass runs, then launches the next step's
     // march on march_stream
-    NGP_TRY(check_cuda(cudaEventSynchronize(t->ev_counts), "train step counters"));
+    NGP_TRY(wait_event(t, t->ev_counts, "train step counters"));
     const uint32_t c[3] = {t->host_counters[0], t->host_counters[1], t->host_counters[2]};
     t->measured_before  = c[1];
     t->measured         = c[2];
@@ -436,19 +540,19 @@ int train_step(ngp_trainer* t, bool premarch_next) {
         NGP_TRY(march_step(t, next_step, t->march_stream));
         NGP_TRY(check_cuda(cudaEventRecord(t->ev_march, t->march_stream), "record march"));
     }
-    // data parallel: average the fp32 gradient over ranks (one all-reduce per step); every rank
-    // then takes the identical Adam step, so the replicas (and their density grids) stay equal.
+    // data parallel: the fp32 gradients are rounded to fp16 (the reference's gradient format,
+    // loss-scaled by 128: half the bytes of fp32; the fp32 accumulation buffer is cleared by the
+    // conversion) and reduce-scattered: each rank receives the sum over ranks of its shard, takes
+    // the Adam step on that shard only, and the fp16 parameters are all-gathered, so every
+    // replica (and the density grid it builds from them) stays identical.
     // NCCL's kernels must not wait for SM slots behind a long-running kernel of another stream (a
     // delayed rank stalls every rank): the training stream has the higher priority, so its
-    // collective is scheduled before the next step's march blocks (without priorities the
-    // collective waits for the march instead).
-    // The gradient crosses NVLink in fp16 (the reference's gradient format, loss-scaled by 128):
-    // half the bytes of fp32; the fp32 accumulation buffer is cleared by the conversion.
+    // collectives are scheduled before the next step's march blocks.
     if (t->comm != nullptr) {
-        if (premarch && !NGP_DP_PRIORITY) NGP_TRY(check_cuda(cudaStreamWaitEvent(t->stream, t->ev_march, 0), "all-reduce after march"));
+        if (premarch && !NGP_DP_PRIORITY) NGP_TRY(check_cuda(cudaStreamWaitEvent(t->stream, t->ev_march, 0), "exchange after march"));
         NGP_TRY(ngp_gradients_to_half(t->n_params, t->grads, t->grads16, 1, t->stream));
-        const ncclResult_t r = ncclAllReduce(t->grads16, t->grads16, t->n_params, ncclHalf, ncclSum, t->comm, t->stream);
-        if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+        uint16_t* mine = t->grads16 + static_cast<size_t>(t->rank) * t->shard;
+        NGP_TRY(nccl_done(t, ncclReduceScatter(t->grads16, mine, t->shard, ncclHalf, ncclSum, t->comm, t->stream), "ncclReduceScatter"));
     }
     mark(t, 7);
     // step_optimizer (ngp.train.cu:1973-1980)
@@ -461,15 +565,20 @@ int train_step(ngp_trainer* t, bool premarch_next) {
         }
     }
     ++t->adam_calls;
-    if (t->comm != nullptr)
-        NGP_TRY(ngp_adam_step_f16(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale * static_cast<float>(t->world),
-                                  t->master, t->params, t->grads16, t->adam_m, t->adam_v, t->adam_steps, t->lr_table, t->lr_table_len, t->stream));
-    else
+    if (t->comm != nullptr) {
+        const uint32_t first = static_cast<uint32_t>(t->rank) * t->shard;
+        const uint32_t count = first < t->n_params ? std::min(t->shard, t->n_params - first) : 0u;
+        NGP_TRY(ngp_adam_step_f16_range(count, first, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f,
+                                        kLossScale * static_cast<float>(t->world), t->master + first, t->params + first, t->grads16 + first,
+                                        t->adam_m + first, t->adam_v + first, t->adam_steps + first, t->lr_table, t->lr_table_len, t->stream));
+        NGP_TRY(nccl_done(t, ncclAllGather(t->params + first, t->params, t->shard, ncclHalf, t->comm, t->stream), "ncclAllGather"));
+    } else {
         NGP_TRY(ngp_adam_step_table(t->n_params, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f, kLossScale, t->master, t->params,
                                     t->grads, t->adam_m, t->adam_v, t->adam_steps, 1, t->lr_table, t->lr_table_len, t->stream));
+    }
     mark(t, 8);
     if (t->profiling) {
-        NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train step"));
+        NGP_TRY(wait_stream(t, t->stream, "train step"));
         for (int k = 0; k < kTrainPhases; ++k) {
             float ms = 0.0f;
             cudaEventElapsedTime(&ms, t->marks[k], t->marks[k + 1]);
@@ -600,6 +709,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
     if (cfg->n_levels * cfg->features_per_level != 32) return fail(NGP_ERR_INVALID, "trainer: the encoding must produce 32 features (levels x F)");
     auto* t      = new ngp_trainer{};
     t->cfg       = *cfg;
+    if (const char* env = std::getenv("NGP_COLLECTIVE_TIMEOUT_MS"); env != nullptr && std::atof(env) > 0.0) t->collective_timeout_ms = std::atof(env);
     const int st = [&]() -> int {
         NGP_TRY(ngp_grid_layout_make(cfg->n_levels, cfg->features_per_level, cfg->log2_hashmap_size, cfg->base_resolution,
                                      cfg->log2_per_level_scale, &t->layout));
@@ -635,6 +745,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
         NGP_TRY(dalloc(t->grid_indices, kGridCells, "grid indices"));
         NGP_TRY(dalloc(t->bitfield, kGridCells / 8u, "bitfield"));
         NGP_TRY(dalloc(t->occupied, 1, "occupied count"));
+        NGP_TRY(dalloc(t->grid_counter, 1, "grid sample counter"));
         for (MarchSet& m : t->sets) {
             NGP_TRY(dalloc(m.coords, static_cast<size_t>(kMaxSamples) * 7u, "sample coords"));
             NGP_TRY(dalloc(m.rays, static_cast<size_t>(kNetworkBatch) * 6u, "rays"));
@@ -710,13 +821,60 @@ extern "C" int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int wo
     clear_error();
     if (t == nullptr || unique_id == nullptr || world < 1 || rank < 0 || rank >= world) return fail(NGP_ERR_INVALID, "trainer join: bad arguments");
     if (t->step != 0) return fail(NGP_ERR_STATE, "trainer join: only before training");
+    if (t->comm != nullptr) return fail(NGP_ERR_STATE, "trainer join: already joined");
     if (world == 1) return NGP_OK;
+    // padded exchange buffers: the fp16 parameters and gradients hold n_padded entries so that
+    // every rank's shard has the same length (a multiple of 4 for Adam's vector loads)
+    const uint64_t unit   = 4ull * static_cast<uint64_t>(world);
+    const uint64_t padded = (static_cast<uint64_t>(t->n_params) + unit - 1u) / unit * unit;
+    if (padded > 0xFFFFFFFFull) return fail(NGP_ERR_INVALID, "trainer join: too many parameters for the exchange");
+    uint16_t *params = nullptr, *grads16 = nullptr;
+    NGP_TRY(dalloc(params, padded, "padded fp16 params"));
+    if (const int st = dalloc(grads16, padded, "padded fp16 gradients"); st != NGP_OK) {
+        cudaFree(params);
+        return st;
+    }
+    cudaMemsetAsync(params, 0, padded * sizeof(uint16_t), t->stream);
+    cudaMemsetAsync(grads16, 0, padded * sizeof(uint16_t), t->stream);
+    cudaMemcpyAsync(params, t->params, sizeof(uint16_t) * t->n_params, cudaMemcpyDeviceToDevice, t->stream);
+    if (const int st = check_cuda(cudaStreamSynchronize(t->stream), "trainer join: padded buffers"); st != NGP_OK) {
+        cudaFree(params), cudaFree(grads16);
+        return st;
+    }
+    cudaFree(t->params), cudaFree(t->grads16);
+    t->params   = params;
+    t->grads16  = grads16;
+    t->n_padded = static_cast<uint32_t>(padded);
+    t->shard    = static_cast<uint32_t>(padded / static_cast<uint64_t>(world));
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
-    const ncclResult_t r = ncclCommInitRank(&t->comm, world, id, rank);
-    if (r != ncclSuccess) return fail(NGP_ERR_CUDA, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+    config.blocking     = 0;
+    ncclComm_t comm     = nullptr;
+    const ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &config);
+    if (r != ncclSuccess && r != ncclInProgress) return fail(NGP_ERR_CUDA, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+    t->comm  = comm;
     t->world = world;
     t->rank  = rank;
+    const int st = wait_comm(t, [&]() -> int {
+        ncclResult_t a = ncclSuccess;
+        ncclCommGetAsyncError(t->comm, &a);
+        if (a == ncclSuccess) return 1;
+        if (a == ncclInProgress) return 0;
+        set_error(ncclGetErrorString(a));
+        return -1;
+    }, "ncclCommInitRankConfig");
+    if (st != NGP_OK) {
+        t->world = 1, t->rank = 0;
+        return st;
+    }
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_set_collective_timeout(ngp_trainer* t, double timeout_ms) {
+    clear_error();
+    if (t == nullptr || !(timeout_ms > 0.0)) return fail(NGP_ERR_INVALID, "collective timeout: bad arguments");
+    t->collective_timeout_ms = timeout_ms;
     return NGP_OK;
 }
 
@@ -744,7 +902,7 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
     cudaEventRecord(e1, t->stream);
     NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_loss, t->loss_values, sizeof(float) * loss_rays, cudaMemcpyDeviceToHost, t->stream), "read loss"));
     NGP_TRY(check_cuda(cudaMemcpyAsync(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read occupied"));
-    NGP_TRY(check_cuda(cudaStreamSynchronize(t->stream), "train"));
+    NGP_TRY(wait_stream(t, t->stream, "train"));
     collect_grid_times(t);
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, e0, e1);
@@ -812,10 +970,23 @@ extern "C" int ngp_trainer_set_segmented_eval(ngp_trainer* t, int enabled) {
 
 extern "C" uint32_t ngp_trainer_param_count(const ngp_trainer* t) { return t == nullptr ? 0u : t->n_params; }
 
-extern "C" int ngp_trainer_get_params(const ngp_trainer* t, float* host_out, uint32_t count) {
+extern "C" int ngp_trainer_get_params(ngp_trainer* t, float* host_out, uint32_t count) {
     clear_error();
     if (t == nullptr || host_out == nullptr || count != t->n_params) return fail(NGP_ERR_INVALID, "get params: bad arguments");
-    return check_cuda(cudaMemcpy(host_out, t->master, sizeof(float) * count, cudaMemcpyDeviceToHost), "download params");
+    if (t->comm == nullptr) return check_cuda(cudaMemcpy(host_out, t->master, sizeof(float) * count, cudaMemcpyDeviceToHost), "download params");
+    // data parallel: each rank's fp32 master is current only on its own shard; the shards are
+    // all-gathered into a temporary buffer (a collective: every rank calls this)
+    float* full = nullptr;
+    NGP_TRY(dalloc(full, t->n_padded, "gathered params"));
+    const size_t first = static_cast<size_t>(t->rank) * t->shard;
+    const size_t mine  = first < t->n_params ? std::min<size_t>(t->shard, t->n_params - first) : 0;
+    int st             = check_cuda(cudaMemsetAsync(full, 0, sizeof(float) * t->n_padded, t->stream), "gather params");
+    if (st == NGP_OK && mine > 0) st = check_cuda(cudaMemcpyAsync(full + first, t->master + first, sizeof(float) * mine, cudaMemcpyDeviceToDevice, t->stream), "gather params");
+    if (st == NGP_OK) st = nccl_done(t, ncclAllGather(full + first, full, t->shard, ncclFloat32, t->comm, t->stream), "ncclAllGather params");
+    if (st == NGP_OK) st = wait_stream(t, t->stream, "gather params");
+    if (st == NGP_OK) st = check_cuda(cudaMemcpy(host_out, full, sizeof(float) * count, cudaMemcpyDeviceToHost), "download params");
+    cudaFree(full);
+    return st;
 }
 
 extern "C" int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_t count) {

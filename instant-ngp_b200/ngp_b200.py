@@ -229,6 +229,11 @@ def density_grid_samples(n_uniform, n_nonuniform, ema_step, values, coords, indi
                                           _stream(stream)), "ngp_density_grid_samples")
 
 
+def density_grid_samples_cell_order(n_uniform, n_nonuniform, ema_step, values, coords, indices, counter=None, stream=None) -> None:
+    _check(lib().ngp_density_grid_samples_cell_order(_u32(n_uniform), _u32(n_nonuniform), _u32(ema_step), _ptr(values), _ptr(coords), _ptr(indices),
+                                                     _ptr(counter), _stream(stream)), "ngp_density_grid_samples_cell_order")
+
+
 def density_grid_splat(n, indices, density, scratch, stream=None) -> None:
     _check(lib().ngp_density_grid_splat(_u32(n), _ptr(indices), _ptr(density), _ptr(scratch), _stream(stream)), "ngp_density_grid_splat")
 
@@ -624,7 +629,7 @@ class InstantNGP:
         p = np.ascontiguousarray(params, np.float32)
         _check(lib().ngp_trainer_set_params(self.handle, ctypes.c_void_p(p.ctypes.data), _u32(p.size)), "ngp_trainer_set_params")
 
-    PHASES = ("grid_update", "march", "inference_compact", "mlp_fwd_loss_pad", "mlp_bwd", "encode_bwd", "allreduce", "adam")
+    PHASES = ("grid_update", "march", "inference_compact", "mlp_fwd_loss_pad", "mlp_bwd", "encode_bwd", "exchange", "adam")
 
     def set_profiling(self, enable: bool = True) -> None:
         _check(lib().ngp_trainer_set_profiling(self.handle, ctypes.c_int(1 if enable else 0)), "ngp_trainer_set_profiling")
@@ -654,6 +659,20 @@ class InstantNGP:
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id[:128].ljust(128, b"\0"))
         _check(lib().ngp_trainer_join(self.handle, buf, ctypes.c_int(world), ctypes.c_int(rank)), "ngp_trainer_join")
 
+    def train_guarded(self, iters: int, health: RankHealth) -> dict:
+        """train(1) `iters` times, each after health.before_step: a rank that left (or stopped) is
+        reported on the host before this rank launches the step's collectives."""
+        st = {}
+        for _ in range(iters):
+            health.before_step(self.step)
+            st = self.train(1)
+        return st
+
+    def set_collective_timeout(self, ms: float) -> None:
+        """Collectives (and waits for the stream that runs them) that take longer abort the
+        communicator and raise (NGP_ERR_TIMEOUT)."""
+        _check(lib().ngp_trainer_set_collective_timeout(self.handle, ctypes.c_double(ms)), "ngp_trainer_set_collective_timeout")
+
     def join_process_group(self) -> None:
         """Join using the current torch.distributed process group to share the NCCL id."""
         import torch.distributed as dist
@@ -672,6 +691,50 @@ class InstantNGP:
         return bits, vals
 
 
+class RankHealth:
+    """Host-side liveness of the ranks of a data-parallel job, kept in a torch.distributed store (no
+    GPU involved; no counterpart in the single-GPU reference).
+
+    Before a step that runs collectives, each rank calls before_step(step): it publishes the step
+    and waits until every other rank has published that step or a later one.  A rank that leaves
+    the job calls leave() between steps; the others raise RuntimeError naming it at their next
+    before_step.  A rank that stops without leaving is reported once `timeout_s` expires.  Either
+    way the remaining ranks learn of it on the host, before they launch a collective that could
+    not complete (the trainer's collective timeout is the second line of defence)."""
+
+    def __init__(self, store=None, world: int | None = None, rank: int | None = None, timeout_s: float = 30.0, prefix: str = "ngp_health"):
+        import torch.distributed as dist
+
+        self.store = store if store is not None else dist.distributed_c10d._get_default_store()
+        self.world = dist.get_world_size() if world is None else world
+        self.rank = dist.get_rank() if rank is None else rank
+        self.timeout_s = timeout_s
+        self.prefix = prefix
+
+    def _key(self, kind: str, rank: int) -> str:
+        return f"{self.prefix}/{kind}/{rank}"
+
+    def before_step(self, step: int) -> None:
+        import time
+
+        self.store.set(self._key("step", self.rank), str(step))
+        pending = [r for r in range(self.world) if r != self.rank]
+        deadline = time.monotonic() + self.timeout_s
+        while pending:
+            for r in list(pending):
+                if self.store.check([self._key("left", r)]):
+                    raise RuntimeError(f"rank {r} left the data-parallel job before step {step}")
+                if self.store.check([self._key("step", r)]) and int(self.store.get(self._key("step", r))) >= step:
+                    pending.remove(r)
+            if pending and time.monotonic() > deadline:
+                raise RuntimeError(f"ranks {pending} did not reach step {step} within {self.timeout_s} s")
+            if pending:
+                time.sleep(0.001)
+
+    def leave(self) -> None:
+        self.store.set(self._key("left", self.rank), "1")
+
+
 def share_nccl_id() -> bytes:
     """Rank 0 creates an NCCL unique id and broadcasts it over the current torch.distributed group
     (any backend: the id travels in a CPU tensor for gloo, a device tensor for nccl)."""
@@ -684,6 +747,15 @@ def share_nccl_id() -> bytes:
     t = torch.tensor(list(uid), dtype=torch.uint8, device=device)
     dist.broadcast(t, src=0)
     return bytes(t.cpu().tolist())
+
+
+FAULT_SITES = {"alloc": 1, "launch": 2, "collective": 3}
+
+
+def fault_inject(site: str, countdown: int) -> None:
+    """Arm host-side fault injection: the countdown-th allocation / kernel launch / collective of
+    the library from now fails with an "injected fault" error (0 disarms).  No GPU fault is raised."""
+    _check(lib().ngp_fault_inject(ctypes.c_int(FAULT_SITES[site]), ctypes.c_int64(countdown)), "ngp_fault_inject")
 
 
 def nccl_unique_id() -> bytes:

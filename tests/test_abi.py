@@ -52,3 +52,12 @@ def test_loss_scratch_size_refuses_sizes_beyond_32_bits(ngp):
     assert lib.ngp_last_error() == b""
     assert lib.ngp_loss_scratch_bytes(ctypes.c_uint32(0xFFFFFFFF)) == 0
     assert b"uint32" in lib.ngp_last_error()
+
+
+def test_fault_injection_arguments(ngp):
+    """Arming and disarming needs no GPU; bad sites are refused."""
+    lib = ngp.lib()
+    assert lib.ngp_fault_inject(ctypes.c_int(9), ctypes.c_int64(1)) == 1
+    assert b"fault inject" in lib.ngp_last_error()
+    ngp.fault_inject("launch", 0)
+    ngp.fault_inject("alloc", 0)

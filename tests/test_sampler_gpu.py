@@ -676,3 +676,37 @@ def test_selected_batch_matches_compacted_batch(ngp, small_scene, blob_bitfield)
     assert dx_a.cpu().numpy().view(np.uint16).tobytes() == dx_b.cpu().numpy().view(np.uint16).tobytes()
     ga, gb = g_a.cpu().numpy(), g_b.cpu().numpy()
     assert np.abs(ga - gb).max() <= 1e-5 * np.abs(ga).max()
+
+
+@pytest.mark.parametrize("sets", [(1 << 21, 0), (1 << 19, 1 << 19), (1 << 16, 3000)], ids=["warm-up", "steady", "ragged"])
+def test_grid_samples_cell_order_is_a_permutation_of_the_reference(ngp, reflib, sets):
+    """The cell-ordered samples are the reference kernel's samples (same records and cell indices,
+    bit for bit) in another order; warps hold consecutive first cells."""
+    import torch
+
+    nu, nn = sets
+    vals0 = workloads.blob_grid_values(workloads.gaussian_blob_density())
+    vals0[::97] = -1.0  # untrained cells: the uniform samples there retry elsewhere
+    values = T(vals0)
+    n = nu + nn
+    coords = torch.zeros((n, 7), dtype=torch.float32, device="cuda")
+    idx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.density_grid_samples_cell_order(nu, nn, 7, values, coords, idx, counter)
+    rcoords = torch.zeros_like(coords)
+    ridx = torch.zeros_like(idx)
+    reflib.call("ref_grid_samples", ctypes.c_uint32(nu), ctypes.c_uint32(nn), ctypes.c_uint32(7), P(values), P(rcoords), P(ridx))
+    torch.cuda.synchronize()
+    if nn:
+        assert int(counter.item()) == n
+
+    def rows(c, i):
+        return np.concatenate([c.cpu().numpy().view(np.uint32), i.cpu().numpy().view(np.uint32)[:, None]], axis=1)
+
+    a, b = rows(coords, idx), rows(rcoords, ridx)
+    a, b = a[np.lexsort(a.T[::-1])], b[np.lexsort(b.T[::-1])]
+    assert np.array_equal(a, b)
+    if nu == 1 << 21 and nn == 0:
+        # slot g holds the sample whose first cell is g: cells ascend wherever no retry happened
+        cells = idx.cpu().numpy().view(np.uint32)
+        assert (cells == np.arange(n, dtype=np.uint32)).mean() > 0.95
