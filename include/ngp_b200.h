@@ -357,6 +357,15 @@ NGP_API int ngp_training_loss_selected(uint32_t rays_per_batch, uint32_t step, c
                                        uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
                                        const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* coords,
                                        uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, void* stream);
+/* ngp_training_loss_selected with a choice of loss (no reference counterpart; the reference's L2
+ * is at ngp.train.cu:817-820): loss_kind 0 = L2 (the reference's), 1 = Huber (delta 0.1, divided
+ * by 5 so that it equals the L2 loss for residuals |d| <= 0.1: loss d^2 there, 0.2 |d| - 0.01
+ * beyond, gradient 2 d there, 0.2 sign(d) beyond). */
+NGP_API int ngp_training_loss_selected_kind(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                            uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                            const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* coords,
+                                            uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, int loss_kind,
+                                            void* stream);
 /* Padding of the selected batch to 2^18 rows (rows and gradients, as ngp_pad_training_batch). */
 NGP_API int ngp_pad_training_rows(const uint32_t* compacted_counter, uint32_t* batch_rows, uint16_t* dloss_doutput, void* stream);
 
@@ -531,6 +540,9 @@ NGP_API int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_
 NGP_API int ngp_nccl_unique_id(uint8_t* out, size_t bytes);
 NGP_API int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank);
 NGP_API int ngp_trainer_set_collective_timeout(ngp_trainer* t, double timeout_ms);
+/* Training loss (no reference counterpart; the reference trains with L2, ngp.train.cu:817-820):
+ * 0 = L2 (default), 1 = Huber (as ngp_training_loss_selected_kind). */
+NGP_API int ngp_trainer_set_loss(ngp_trainer* t, int loss_kind);
 /* Per-phase device time of the training step, summed over the steps since profiling was
  * enabled (cudaEvents between phases): 0 grid update, 1 ray marching, 2 density evaluation of the
  * marched samples + compaction, 3 network forward of the compacted samples + loss + padding,

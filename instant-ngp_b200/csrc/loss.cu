@@ -37,6 +37,7 @@ struct LossParams {
     float* coords_out;              // compacted records [NETWORK_BATCH_SIZE][7]
     __half* dloss_doutput;          // [NETWORK_BATCH_SIZE][16]
     float* loss_output;             // [ray] (may be null)
+    int loss_kind;                  // kLossL2 (the reference) or kLossHuber
     float4* ray_rgb;                // scratch [ray]: composited colour, pass 1 -> pass 2
     uint32_t* kept;                 // scratch [ray]: samples kept by compositing
     uint32_t* block_totals;         // scratch [ray blocks]
@@ -95,14 +96,36 @@ __device__ __forceinline__ float prefix_transmittance(float T, float q, uint32_t
     return Tb;
 }
 
+// Loss of a ray's composited colour against its target, per colour channel residual d.
+//  L2 (the reference, ngp.train.cu:817-819): d^2, gradient 2 d.
+//  Huber (the loss of the original instant-ngp NeRF, delta = 0.1, divided by 5 so that it equals
+//  the L2 loss for residuals below delta): (|d| <= 0.1 ? 5 d^2 : |d| - 0.05) / 5, gradient
+//  |d| <= 0.1 ? 2 d : sign(d) / 5.
+enum : int { kLossL2 = 0, kLossHuber = 1 };
+
+__device__ __forceinline__ float3 loss_gradient(float3 d, int kind) {
+    if (kind == kLossHuber) {
+        auto g = [](float v) { return fabsf(v) <= 0.1f ? 2.0f * v : copysignf(0.2f, v); };
+        return {g(d.x), g(d.y), g(d.z)};
+    }
+    return {2.0f * d.x, 2.0f * d.y, 2.0f * d.z};
+}
+
+// Per-ray loss value: the mean over the 3 channels, divided by the ray count (ngp.train.cu:820).
+__device__ __forceinline__ float loss_value(float3 d, int kind, uint32_t rays_per_batch) {
+    if (kind == kLossHuber) {
+        auto h = [](float v) { const float a = fabsf(v); return a <= 0.1f ? v * v : __fmaf_rn(a, 0.2f, -0.01f); };
+        return (h(d.x) + h(d.y) + h(d.z)) / (3.0f * static_cast<float>(rays_per_batch));
+    }
+    return __fmaf_rn(d.z, d.z, __fmaf_rn(d.x, d.x, d.y * d.y)) / (3.0f * static_cast<float>(rays_per_batch));
+}
+
 // Gradients of one ray's first cn samples (rest of K11, ngp.train.cu:804-859): dL/d(raw rgb) and
 // dL/d(raw density) per sample, times `scale`; the sample records are also copied to cout when
 // it is not null.  The whole warp calls it for one ray.
-__device__ __forceinline__ void ray_gradients(float3 rgb, float3 target, float scale, const float* __restrict__ ray, const float* __restrict__ cin,
+__device__ __forceinline__ void ray_gradients(float3 rgb, float3 grad, float scale, const float* __restrict__ ray, const float* __restrict__ cin,
                                               const __half* __restrict__ out, float* __restrict__ cout, __half* __restrict__ dout, uint32_t cn) {
     const uint32_t lane = threadIdx.x & 31u;
-    const float3 diff   = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
-    const float3 grad   = {2.0f * diff.x, 2.0f * diff.y, 2.0f * diff.z};
     const float3 origin = {ray[0], ray[1], ray[2]};
     float T             = 1.0f;
     float3 acc          = {0.0f, 0.0f, 0.0f};
@@ -264,9 +287,8 @@ __global__ void __launch_bounds__(kCtaThreads) loss_pass2_kernel(const __grid_co
     const float4 rr   = p.ray_rgb[i];
     const float3 rgb  = {rr.x, rr.y, rr.z};
     const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
-    if (p.loss_output != nullptr && lane == 0)
-        p.loss_output[i] = __fmaf_rn(diff.z, diff.z, __fmaf_rn(diff.x, diff.x, diff.y * diff.y)) / (3.0f * static_cast<float>(p.rays_per_batch));
-    ray_gradients(rgb, target, kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u,
+    if (p.loss_output != nullptr && lane == 0) p.loss_output[i] = loss_value(diff, p.loss_kind, p.rays_per_batch);
+    ray_gradients(rgb, loss_gradient(diff, p.loss_kind), kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u,
                   p.coords + static_cast<uint64_t>(base) * 7u, p.network_output + static_cast<uint64_t>(base) * 16u,
                   p.coords_out + static_cast<uint64_t>(cbase) * 7u, p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u, cn);
 }
@@ -562,6 +584,7 @@ struct CompactedLossParams {
     float* loss_output;
     const uint32_t* steps;         // scratch from the keep pass
     const uint32_t* sample_base;   // optional: ray i's samples are at sample_base[i] (else at its compacted base)
+    int loss_kind;                 // kLossL2 (the reference) or kLossHuber
 };
 
 // Step 5: pass 1's compositing over the compacted outputs, then pass 2.
@@ -612,9 +635,8 @@ __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __gri
         rgb.z = __fmaf_rn(T, bg.z, rgb.z);
     }
     const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
-    if (p.loss_output != nullptr && lane == 0)
-        p.loss_output[i] = __fmaf_rn(diff.z, diff.z, __fmaf_rn(diff.x, diff.x, diff.y * diff.y)) / (3.0f * static_cast<float>(p.rays_per_batch));
-    ray_gradients(rgb, target, kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u, cin, out, nullptr,
+    if (p.loss_output != nullptr && lane == 0) p.loss_output[i] = loss_value(diff, p.loss_kind, p.rays_per_batch);
+    ray_gradients(rgb, loss_gradient(diff, p.loss_kind), kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u, cin, out, nullptr,
                   p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u, cn);
 }
 
@@ -1056,11 +1078,13 @@ extern "C" int ngp_training_select_progressive(uint32_t rays_per_batch, const ui
     return check_launch("select_write_kernel");
 }
 
-extern "C" int ngp_training_loss_selected(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
-                                          uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
-                                          const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* coords,
-                                          uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, void* stream) {
+extern "C" int ngp_training_loss_selected_kind(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                               uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                               const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* coords,
+                                               uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, int loss_kind,
+                                               void* stream) {
     clear_error();
+    if (loss_kind != kLossL2 && loss_kind != kLossHuber) return fail(NGP_ERR_INVALID, "selected loss: unknown loss kind");
     if (rays_per_batch == 0) return NGP_OK;
     if (pixels == nullptr || network_output == nullptr || rays == nullptr || numsteps == nullptr || coords == nullptr || dloss_doutput == nullptr ||
         scratch == nullptr || frame_count == 0 || width == 0 || height == 0)
@@ -1084,9 +1108,18 @@ extern "C" int ngp_training_loss_selected(uint32_t rays_per_batch, uint32_t step
     p.loss_output    = loss_values;
     p.steps          = static_cast<const uint32_t*>(scratch);
     p.sample_base    = static_cast<const uint32_t*>(scratch) + static_cast<size_t>(rays_per_batch) * 3u;  // list_off region
+    p.loss_kind      = loss_kind;
     if (loss_values != nullptr) NGP_TRY(check_cuda(cudaMemsetAsync(loss_values, 0, sizeof(float) * rays_per_batch, s), "selected loss: clear"));
     loss_compacted_kernel<<<(rays_per_batch + kRaysPerCta - 1) / kRaysPerCta, kCtaThreads, 0, s>>>(p);
     return check_launch("loss_compacted_kernel");
+}
+
+extern "C" int ngp_training_loss_selected(uint32_t rays_per_batch, uint32_t step, const uint32_t* ray_counter, const uint8_t* pixels,
+                                          uint32_t frame_count, uint32_t width, uint32_t height, const uint16_t* network_output,
+                                          const uint32_t* ray_indices, const float* rays, uint32_t* numsteps, const float* coords,
+                                          uint16_t* dloss_doutput, float* loss_values, const void* scratch, size_t scratch_bytes, void* stream) {
+    return ngp_training_loss_selected_kind(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, ray_indices, rays,
+                                           numsteps, coords, dloss_doutput, loss_values, scratch, scratch_bytes, kLossL2, stream);
 }
 
 extern "C" int ngp_pad_training_rows(const uint32_t* compacted_counter, uint32_t* batch_rows, uint16_t* dloss_doutput, void* stream) {

@@ -156,6 +156,7 @@ struct ngp_trainer {
     // a collective (or a wait on a stream that runs one) that takes longer fails: the
     // communicator is aborted and the call returns NGP_ERR_TIMEOUT
     double collective_timeout_ms = 120000.0;
+    int loss_kind                = 0;  // 0 L2 (the reference's), 1 Huber
     // optional per-phase timing (cudaEvents between the phases of a step)
     bool profiling = false;
     cudaEvent_t marks[kTrainPhases + 1] = {};
@@ -493,8 +494,9 @@ int train_step(ngp_trainer* t, bool premarch_next) {
 #if NGP_SELECT
     NGP_TRY(ngp_mlp_forward_rows(kCompactedRows, t->batch_rows, m.counters + 3, t->params, t->enc, t->inference_samples, m.coords, 7, t->out,
                                  t->stream));
-    NGP_TRY(ngp_training_loss_selected(t->rays_per_batch, rng_step, m.counters + 0, s.pixels, s.frames, s.width, s.height, t->out, m.ray_indices,
-                                       m.rays, m.numsteps, m.coords, t->dloss, t->loss_values, t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    NGP_TRY(ngp_training_loss_selected_kind(t->rays_per_batch, rng_step, m.counters + 0, s.pixels, s.frames, s.width, s.height, t->out,
+                                            m.ray_indices, m.rays, m.numsteps, m.coords, t->dloss, t->loss_values, t->loss_scratch,
+                                            t->loss_scratch_bytes, t->loss_kind, t->stream));
     NGP_TRY(ngp_pad_training_rows(m.counters + 2, t->batch_rows, t->dloss, t->stream));
     mark(t, 4);
     NGP_TRY(ngp_mlp_backward_rows(kNetworkBatch, t->batch_rows, t->params, t->enc, t->inference_samples, m.coords, 7, t->dloss, t->denc, kNetworkBatch,
@@ -868,6 +870,13 @@ extern "C" int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int wo
         t->world = 1, t->rank = 0;
         return st;
     }
+    return NGP_OK;
+}
+
+extern "C" int ngp_trainer_set_loss(ngp_trainer* t, int loss_kind) {
+    clear_error();
+    if (t == nullptr || (loss_kind != 0 && loss_kind != 1)) return fail(NGP_ERR_INVALID, "set loss: bad arguments (0 = L2, 1 = Huber)");
+    t->loss_kind = loss_kind;
     return NGP_OK;
 }
 

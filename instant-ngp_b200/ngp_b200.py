@@ -351,6 +351,14 @@ def training_select_progressive(rays_per_batch, ray_counter, layout, params, coo
            "ngp_training_select_progressive")
 
 
+def training_loss_selected_kind(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, ray_indices, rays, numsteps,
+                                coords, dloss, loss_values, scratch, loss_kind, stream=None) -> None:
+    _check(lib().ngp_training_loss_selected_kind(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),
+                                                 _u32(height), _ptr(network_output), _ptr(ray_indices), _ptr(rays), _ptr(numsteps), _ptr(coords),
+                                                 _ptr(dloss), _ptr(loss_values), _ptr(scratch), ctypes.c_size_t(scratch.numel() * scratch.element_size()),
+                                                 ctypes.c_int(loss_kind), _stream(stream)), "ngp_training_loss_selected_kind")
+
+
 def training_loss_selected(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, ray_indices, rays, numsteps,
                            coords, dloss_doutput, loss_values, scratch, stream=None) -> None:
     _check(lib().ngp_training_loss_selected(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),
@@ -667,6 +675,12 @@ class InstantNGP:
             health.before_step(self.step)
             st = self.train(1)
         return st
+
+    LOSSES = {"l2": 0, "huber": 1}
+
+    def set_loss(self, kind: str) -> None:
+        """Training loss: "l2" (the reference's, default) or "huber" (delta 0.1, scaled by 1/5)."""
+        _check(lib().ngp_trainer_set_loss(self.handle, ctypes.c_int(self.LOSSES[kind])), "ngp_trainer_set_loss")
 
     def set_collective_timeout(self, ms: float) -> None:
         """Collectives (and waits for the stream that runs them) that take longer abort the
