@@ -185,7 +185,9 @@ GRID_KERNELS = {
 # DRAM bytes (read + write) per unit that ncu measured for these launches (one capture each, see
 # profiles/ for the command); None until captured.
 NCU_TRAFFIC_PER_UNIT = {
-    "grid_encode": None,
+    # profiles/encode_forward_points_kernel__grid_update_config3.md: 85.15 MB read + 98.25 MB
+    # written by the launch over 2^21 cell-ordered grid samples
+    "grid_encode": (85.150464e6 + 98.249984e6) / 2097152,
 }
 
 
@@ -215,6 +217,7 @@ def train_roofline(phases: dict, grid: dict, peaks: dict, l2: dict | None) -> di
                        "(CUDA events on the trainer's stream, twin model, same steps as the timed region)"}
     if NCU_TRAFFIC_PER_UNIT.get(dom) is not None:
         res["traffic"] = round(NCU_TRAFFIC_PER_UNIT[dom] * units)
+        res["traffic_note"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel (2^21 samples), per sample x this launch's samples"
     if "l2_bytes" in info and l2:
         l2_rate = info["l2_bytes"] * units / t / 1e9
         res["l2"] = {"achieved": round(l2_rate, 1), "unit": "GB/s", "gathered_bytes_per_unit": info["l2_bytes"],
@@ -922,6 +925,9 @@ def render_encode_roofline(ngp, workloads, peaks, n: int = 1 << 22) -> dict:
 
 
 def bench_render_ours(args, rank, world, local):
+    """Config 4: after training (untimed), 1920 x 1080 novel views; each view is split into 64 x 64
+    tiles and rank r of N renders tiles r, r + N, ... (no collective).  A step is one view rendered
+    by all ranks: strong scaling (the views are fixed; more GPUs share each view)."""
     import torch
     import ngp_b200 as ngp
     import workloads
@@ -930,55 +936,58 @@ def bench_render_ours(args, rank, world, local):
     ds = make_dataset(args)
     model = ngp.InstantNGP(ds, ngp.config4_trainer_config())
     model.train(args.train_steps)  # untimed: an occupancy grid and weights of a trained model
-    poses = workloads.render_poses(max(64, args.steps * world))
+    poses = workloads.render_poses(max(64, args.steps))
     w, h = poses["width"], poses["height"]
-    # step k renders view k * world + rank on this rank (no collective)
-    views = [poses["camera"][k * world + rank] for k in range(args.steps)]
-    out = torch.empty((h * w, 3), dtype=torch.float32, device="cuda")
-    for _ in range(args.warmup):
-        model.render(views[0], w, h, poses["focal"], poses["principal"], out=out)
-    barrier(world)
+    views = [poses["camera"][k % len(poses["camera"])] for k in range(args.steps)]
+    out = torch.zeros((h * w, 3), dtype=torch.float32, device="cuda")
+
+    def render(v):
+        model.render_tiles(v, w, h, poses["focal"], poses["principal"], rank, world, out)
+
+    for k in range(args.warmup):
+        render(views[k % len(views)])
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         clocks.wait_first()
+        barrier(world)
+        torch.cuda.synchronize()
         launches0 = ngp.kernel_launch_count()
-        torch.cuda.nvtx.range_push("render")  # lets a profiler select the timed renders
+        torch.cuda.nvtx.range_push("timed")  # lets a profiler select the timed renders
         s.record()
         for v in views:
-            model.render(v, w, h, poses["focal"], poses["principal"], out=out)
+            render(v)
         e.record()
         torch.cuda.nvtx.range_pop()
         e.synchronize()
         launches = ngp.kernel_launch_count() - launches0
+        barrier(world)
         time.sleep(0.25)
-    barrier(world)
     ms = max_over_ranks(s.elapsed_time(e), world)
-    # e2e: the same renders with each image read back to pinned host memory
+    # e2e: the same views, each rank reading its image buffer back to pinned host memory per view
     host = torch.empty((h * w, 3), dtype=torch.float32, pin_memory=True)
-    n_e2e = max(2, args.steps // 2)
+    torch.cuda.synchronize()
     barrier(world)
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for v in views[:n_e2e]:
-        model.render(v, w, h, poses["focal"], poses["principal"], out=out)
-        host.copy_(out, non_blocking=True)
-    e2.record()
-    e2.synchronize()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / n_e2e, world)
+    t0 = time.perf_counter()
+    for v in views:
+        render(v)
+        host.copy_(out, non_blocking=False)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
     model.close()
     roofline = render_encode_roofline(ngp, workloads, peaks)
     rays = w * h
-    value = world * rays * args.steps / (ms * 1e-3)
+    value = rays * args.steps / (ms * 1e-3)
     return {
         "metric": "render rays/s (config 4)", "value": round(value, 1), "unit": "rays/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "fp16 params/activations, fp32 accumulation", "data": "synthetic procedural scene (64 Lambert spheres, seeded)",
         "config": {"workload": "config4 render 1920x1080 novel views after training", "table": "L=16 F=2 log2T=22 base 16 finest 4096",
-                   "views_per_gpu": args.steps, "trained_steps": args.train_steps, "parallelism": f"views partitioned over {world} ranks, no collective",
+                   "views": args.steps, "trained_steps": args.train_steps,
+                   "parallelism": f"64x64 tiles round-robin over {world} ranks (tile t on rank t mod {world}), no collective",
                    "l2": "table 170 MB fp16 > L2; no flush"},
-        "e2e": {"value": round(world * rays / (e2e_ms * 1e-3), 1), "unit": "rays/s", "h2d_bytes_per_step": 48,
-                "d2h_bytes_per_step": rays * 12, "note": "InstantNGP.render per view with the image read back to pinned host memory"},
+        "e2e": {"value": round(rays * args.steps / e2e_s, 1), "unit": "rays/s", "h2d_bytes_per_step": 48, "d2h_bytes_per_step": rays * 12,
+                "note": "render_tiles per view with the rank's image buffer read back to pinned host memory (wall clock, max over ranks); "
+                        "h2d: the 12-float camera"},
         "gpu_launches": launches, "clocks": clocks.summary(), "roofline": roofline,
     }
 
@@ -990,14 +999,14 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["train", "encode", "mlp", "march", "render"], default="train")
-    ap.add_argument("--train-steps", type=int, default=1000, help="render workload: untimed training steps before rendering")
+    ap.add_argument("--train-steps", type=int, default=10000, help="render workload: untimed training steps before rendering (config 4: 10k)")
     ap.add_argument("--views", type=int, default=100)
     ap.add_argument("--test-views", type=int, default=20)
     ap.add_argument("--res", type=int, default=800)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"train": 300, "encode": 500, "mlp": 200, "march": 100, "render": 8}[args.workload]
+        args.steps = {"train": 300, "encode": 500, "mlp": 200, "march": 100, "render": 64}[args.workload]
     if args.warmup is None:
         args.warmup = {"train": 300, "encode": 5, "mlp": 5, "march": 5, "render": 3}[args.workload]
     args.warmup = max(args.warmup, 3)

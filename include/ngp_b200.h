@@ -266,6 +266,13 @@ NGP_API int ngp_march_rays_segment(uint32_t max_entries, const uint32_t* n_entri
  * `image`.  Replaces the ray set-up of generate_evaluation_samples_kernel (ngp.train.cu:587-614). */
 NGP_API int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,
                                float principal_x, float principal_y, uint32_t pixel_offset, uint32_t n, float* rays, void* stream);
+/* Evaluation rays of slots [slot_offset, slot_offset + n) of a tile set: slot j is pixel
+ * (j % 4096) (row-major inside the tile) of the set's tile j / 4096, the set being 64 x 64 tiles
+ * first_tile, first_tile + tile_stride, ... of the row-major tile grid.  Slots outside the image
+ * get a ray that marches no samples. */
+NGP_API int ngp_make_eval_rays_tiles(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,
+                                     float principal_x, float principal_y, uint32_t first_tile, uint32_t tile_stride, uint32_t slot_offset, uint32_t n,
+                                     float* rays, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Compositing, loss and compaction (batch = 2^18 samples).
@@ -409,6 +416,14 @@ NGP_API int ngp_eval_composite_segment(uint32_t max_entries, const uint32_t* n_e
                                        float* t_state, uint32_t* marched, float* state, uint32_t* next_list, uint32_t* next_count,
                                        uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels, double* sse,
                                        uint8_t* comparison, float* rendered, void* stream);
+/* ngp_eval_composite_segment whose rays are the slots of a tile set (as ngp_make_eval_rays_tiles;
+ * pixel_offset is the slot offset; first_tile = 0xFFFFFFFF: every pixel, row-major). */
+NGP_API int ngp_eval_composite_segment_tiles(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* complete, const uint32_t* list,
+                                             const uint32_t* numsteps, const float* coords, const uint16_t* network_output, const float* t_out,
+                                             float* t_state, uint32_t* marched, float* state, uint32_t* next_list, uint32_t* next_count,
+                                             uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,
+                                             double* sse, uint8_t* comparison, float* rendered, uint32_t first_tile, uint32_t tile_stride,
+                                             void* stream);
 
 /* Evaluation compositing of n_pixels pixels: *sse += squared error vs the sRGB target (fp64; no
  * target when pixels is NULL), optional comparison image [height][2*width][3] (target | render)
@@ -509,6 +524,13 @@ NGP_API int ngp_trainer_evaluate(ngp_trainer* t, int split, uint32_t image_begin
 /* Render a novel view (camera: 12 floats, host) into rgb_device [height*width][3] (fp32, [0,1]). */
 NGP_API int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint32_t width, uint32_t height, float fx, float fy, float cx,
                                float cy, float* rgb_device);
+/* ngp_trainer_render of a set of 64 x 64 image tiles: tiles first_tile, first_tile + tile_stride,
+ * ... of the row-major tile grid (ceil(width / 64) tiles per row; the right and bottom tiles are
+ * clipped to the image).  Only those tiles' pixels of rgb_device are written.  The tile loop of the
+ * reference's run_evaluation (ngp.train.cu:1616-1620) partitioned across GPUs: rank r of N renders
+ * tiles r, r + N, ... with no collective. */
+NGP_API int ngp_trainer_render_tiles(ngp_trainer* t, const float* camera_host, uint32_t width, uint32_t height, float fx, float fy, float cx, float cy,
+                                     uint32_t first_tile, uint32_t tile_stride, float* rgb_device);
 /* Evaluation and rendering by segmented marching (enabled != 0, the default: rays are marched a
  * segment at a time and no further than their transmittance lasts) or, as the reference does,
  * by marching every occupied step of each tile before the network runs (0).  Both give the same

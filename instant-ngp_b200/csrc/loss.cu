@@ -779,6 +779,7 @@ struct SegCompositeParams {
     double* sse;
     uint8_t* comparison;
     float* rendered;
+    PixelMap map;               // pixel of slot pixel_offset + ray (linear unless tiles)
 };
 
 // Compositing of one ray's segment by one warp, lane j on sample c0 + j: the transmittance
@@ -839,8 +840,10 @@ __global__ void __launch_bounds__(kThreads) seg_composite_kernel(const __grid_co
             const float t_next   = p.t_out[k];
             carry                = !(stopped || t_next < 0.0f);
             if (lane == 0) {
+                uint32_t gp = 0;
                 if (!carry) {
-                    se = eval_pixel_out(p.pixel_offset + i, rgb, p.image, p.width, p.height, p.pixels, p.comparison, p.rendered);
+                    if (map_pixel(p.map, p.pixel_offset + i, p.width, p.height, gp))
+                        se = eval_pixel_out(gp, rgb, p.image, p.width, p.height, p.pixels, p.comparison, p.rendered);
                 } else {
                     p.state[i]   = make_float4(T, rgb.x, rgb.y, rgb.z);
                     p.t_state[i] = t_next;
@@ -1198,12 +1201,14 @@ extern "C" int ngp_pad_training_batch_enc(const uint32_t* compacted_counter, flo
     return check_launch("pad_batch_kernel");
 }
 
-extern "C" int ngp_eval_composite_segment(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* complete, const uint32_t* list,
-                                          const uint32_t* numsteps, const float* coords, const uint16_t* network_output, const float* t_out,
-                                          float* t_state, uint32_t* marched, float* state, uint32_t* next_list, uint32_t* next_count,
-                                          uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels, double* sse,
-                                          uint8_t* comparison, float* rendered, void* stream) {
+extern "C" int ngp_eval_composite_segment_tiles(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* complete, const uint32_t* list,
+                                                const uint32_t* numsteps, const float* coords, const uint16_t* network_output, const float* t_out,
+                                                float* t_state, uint32_t* marched, float* state, uint32_t* next_list, uint32_t* next_count,
+                                                uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,
+                                                double* sse, uint8_t* comparison, float* rendered, uint32_t first_tile, uint32_t tile_stride,
+                                                void* stream) {
     clear_error();
+    if (tile_stride == 0) return fail(NGP_ERR_INVALID, "segment composite: tile stride 0");
     if (max_entries == 0) return NGP_OK;
     if (complete == nullptr || numsteps == nullptr || coords == nullptr || network_output == nullptr || t_out == nullptr || t_state == nullptr ||
         marched == nullptr || state == nullptr || next_list == nullptr || next_count == nullptr || width == 0 || height == 0)
@@ -1232,9 +1237,20 @@ extern "C" int ngp_eval_composite_segment(uint32_t max_entries, const uint32_t* 
     p.sse          = sse;
     p.comparison   = comparison;
     p.rendered     = rendered;
+    p.map          = first_tile == 0xFFFFFFFFu ? PixelMap{0u, 0u, 0u} : PixelMap{(width + kTileSide - 1u) / kTileSide, first_tile, tile_stride};
     constexpr uint32_t per_cta = kThreads / 32u;
     seg_composite_kernel<<<(max_entries + per_cta - 1) / per_cta, kThreads, 0, as_stream(stream)>>>(p);
     return check_launch("seg_composite_kernel");
+}
+
+extern "C" int ngp_eval_composite_segment(uint32_t max_entries, const uint32_t* n_entries, const uint32_t* complete, const uint32_t* list,
+                                          const uint32_t* numsteps, const float* coords, const uint16_t* network_output, const float* t_out,
+                                          float* t_state, uint32_t* marched, float* state, uint32_t* next_list, uint32_t* next_count,
+                                          uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels, double* sse,
+                                          uint8_t* comparison, float* rendered, void* stream) {
+    return ngp_eval_composite_segment_tiles(max_entries, n_entries, complete, list, numsteps, coords, network_output, t_out, t_state, marched, state,
+                                            next_list, next_count, pixel_offset, image, width, height, pixels, sse, comparison, rendered, 0xFFFFFFFFu,
+                                            1u, stream);
 }
 
 extern "C" int ngp_eval_composite(uint32_t n_pixels, uint32_t pixel_offset, uint32_t image, uint32_t width, uint32_t height, const uint8_t* pixels,

@@ -466,17 +466,24 @@ __global__ void __launch_bounds__(kCtaThreads) seg_march_write_kernel(const __gr
 
 // Evaluation pixel rays (ngp.train.cu:587-614): pixel centre through the pinhole camera,
 // normalised direction.  A degenerate ray gets a NaN origin, which yields no samples.
-__global__ void eval_rays_kernel(const CameraSet cam, uint32_t image, uint32_t pixel_offset, uint32_t n, float* __restrict__ rays) {
+__global__ void eval_rays_kernel(const CameraSet cam, uint32_t image, uint32_t pixel_offset, uint32_t n, float* __restrict__ rays, const PixelMap map) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const uint32_t gp = pixel_offset + i, px = gp % cam.width, py = gp / cam.width;
+    uint32_t gp = 0;
+    float* o    = rays + static_cast<uint64_t>(i) * 6u;
+    if (!map_pixel(map, pixel_offset + i, cam.width, cam.height, gp)) {
+        // no pixel: a ray with no origin marches no samples
+        o[0] = o[1] = o[2] = __int_as_float(0x7fc00000);
+        o[3] = 1.0f, o[4] = 0.0f, o[5] = 0.0f;
+        return;
+    }
+    const uint32_t px = gp % cam.width, py = gp / cam.width;
     const float* f    = cam.camera + static_cast<uint64_t>(image) * 12u;
     const float rx    = (static_cast<float>(px) + 0.5f - cam.principal_x) / cam.focal_x;
     const float ry    = (static_cast<float>(py) + 0.5f - cam.principal_y) / cam.focal_y;
     float3 d          = {__fmaf_rn(f[0], rx, f[3] * ry) + f[6], __fmaf_rn(f[1], rx, f[4] * ry) + f[7], __fmaf_rn(f[2], rx, f[5] * ry) + f[8]};
     if (d.x == 0.0f && d.y == 0.0f && d.z == 0.0f) d = {f[6], f[7], f[8]};
     const float len = norm3df(d.x, d.y, d.z);
-    float* o        = rays + static_cast<uint64_t>(i) * 6u;
     if (len == 0.0f) {
         o[0] = o[1] = o[2] = __int_as_float(0x7fc00000);
         o[3] = 1.0f, o[4] = 0.0f, o[5] = 0.0f;
@@ -675,6 +682,19 @@ extern "C" int ngp_make_eval_rays(const float* camera, uint32_t image, uint32_t 
     if (!camera_ok(camera, image + 1u, width, height, focal_x, focal_y, principal_x, principal_y) || rays == nullptr)
         return fail(NGP_ERR_INVALID, "eval rays: invalid input");
     eval_rays_kernel<<<(n + 127) / 128, 128, 0, as_stream(stream)>>>(camera_set(camera, image + 1u, width, height, focal_x, focal_y, principal_x, principal_y),
-                                                                    image, pixel_offset, n, rays);
+                                                                    image, pixel_offset, n, rays, PixelMap{0u, 0u, 0u});
+    return check_launch("eval_rays_kernel");
+}
+
+extern "C" int ngp_make_eval_rays_tiles(const float* camera, uint32_t image, uint32_t width, uint32_t height, float focal_x, float focal_y,
+                                        float principal_x, float principal_y, uint32_t first_tile, uint32_t tile_stride, uint32_t slot_offset,
+                                        uint32_t n, float* rays, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (!camera_ok(camera, image + 1u, width, height, focal_x, focal_y, principal_x, principal_y) || rays == nullptr || tile_stride == 0)
+        return fail(NGP_ERR_INVALID, "eval rays (tiles): invalid input");
+    const PixelMap map{(width + kTileSide - 1u) / kTileSide, first_tile, tile_stride};
+    eval_rays_kernel<<<(n + 127) / 128, 128, 0, as_stream(stream)>>>(camera_set(camera, image + 1u, width, height, focal_x, focal_y, principal_x, principal_y),
+                                                                    image, slot_offset, n, rays, map);
     return check_launch("eval_rays_kernel");
 }

@@ -96,6 +96,28 @@ __device__ __forceinline__ float4 read_texel(uint32_t px, uint32_t py, uint32_t 
     return r;
 }
 
+// Pixel enumeration of an evaluation / render: linear (slot j = pixel j, tiles_x = 0), or a set
+// of 64 x 64 tiles -- tiles first, first + stride, ... of the image's row-major tile grid
+// (tiles_x tiles per row) -- with slot j = pixel (j & 4095) of the set's tile j >> 12, row-major
+// inside the tile.  Slots that fall outside the image (the partial tiles at the right and bottom
+// edges) map to no pixel.
+struct PixelMap {
+    uint32_t tiles_x, first, stride;
+};
+
+constexpr uint32_t kTileSide = 64u, kTilePixels = kTileSide * kTileSide;
+
+__device__ __forceinline__ bool map_pixel(const PixelMap& m, uint32_t j, uint32_t width, uint32_t height, uint32_t& gp) {
+    if (m.tiles_x == 0) {
+        gp = j;
+        return j < width * height;
+    }
+    const uint32_t tile = m.first + (j / kTilePixels) * m.stride, q = j % kTilePixels;
+    const uint32_t x = (tile % m.tiles_x) * kTileSide + q % kTileSide, y = (tile / m.tiles_x) * kTileSide + q / kTileSide;
+    gp = y * width + x;
+    return x < width && y < height;
+}
+
 // Camera frames: 12 floats per frame = three axis columns and the origin (ngp.dataset.cpp:63).
 struct CameraSet {
     const float* camera;

@@ -632,12 +632,24 @@ int eval_image(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparis
 // network outputs and compositing operations per pixel as eval_image, so the same image bit for
 // bit; the march no longer runs through the (typically most) samples behind each ray's stopping
 // point, and the tiles need no re-march when their samples exceed the budget.
-int eval_image_segmented(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparison_dev, float* rendered) {
-    const uint32_t total = s.width * s.height;
-    const cudaStream_t st = t->stream;
+// Tile set of a render: 64 x 64 tiles first, first + stride, ... (first = kAllPixels: every
+// pixel in row-major order).
+constexpr uint32_t kAllPixels = 0xFFFFFFFFu;
+
+int eval_image_segmented(ngp_trainer* t, const Split& s, uint32_t image, uint8_t* comparison_dev, float* rendered, uint32_t first_tile = kAllPixels,
+                         uint32_t tile_stride = 1u) {
+    const bool tiled      = first_tile != kAllPixels;
+    const uint32_t tiles_x = (s.width + 63u) / 64u, tiles_y = (s.height + 63u) / 64u;
+    const uint32_t n_tiles = tiles_x * tiles_y;
+    const uint32_t mine    = tiled ? (first_tile < n_tiles ? (n_tiles - first_tile + tile_stride - 1u) / tile_stride : 0u) : 0u;
+    const uint32_t total   = tiled ? mine * 4096u : s.width * s.height;
+    const cudaStream_t st  = t->stream;
     for (uint32_t off = 0; off < total; off += kSegTile) {
         const uint32_t n = std::min(kSegTile, total - off);
-        NGP_TRY(ngp_make_eval_rays(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, off, n, t->rays, st));
+        if (tiled)
+            NGP_TRY(ngp_make_eval_rays_tiles(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, first_tile, tile_stride, off, n, t->rays, st));
+        else
+            NGP_TRY(ngp_make_eval_rays(s.camera, image, s.width, s.height, s.fx, s.fy, s.cx, s.cy, off, n, t->rays, st));
         uint32_t max_entries = n;
         for (uint32_t seg = 0;; ++seg) {
             const bool first         = seg == 0;
@@ -657,9 +669,10 @@ int eval_image_segmented(ngp_trainer* t, const Split& s, uint32_t image, uint8_t
                                                      t->loss_scratch, t->loss_scratch_bytes, st));
             uint32_t* next_count = t->seg_counters + 2u + (seg & 1u);
             NGP_TRY(check_cuda(cudaMemsetAsync(next_count, 0, sizeof(uint32_t), st), "segment list count"));
-            NGP_TRY(ngp_eval_composite_segment(max_entries, n_dev, t->seg_counters + 1, list, t->numsteps, t->coords, t->out, t->seg_tout,
-                                               t->seg_tstate, t->seg_marched, t->seg_state, t->seg_lists + static_cast<size_t>(seg & 1u) * kSegTile,
-                                               next_count, off, image, s.width, s.height, s.pixels, t->eval_sse, comparison_dev, rendered, st));
+            NGP_TRY(ngp_eval_composite_segment_tiles(max_entries, n_dev, t->seg_counters + 1, list, t->numsteps, t->coords, t->out, t->seg_tout,
+                                                     t->seg_tstate, t->seg_marched, t->seg_state,
+                                                     t->seg_lists + static_cast<size_t>(seg & 1u) * kSegTile, next_count, off, image, s.width,
+                                                     s.height, s.pixels, t->eval_sse, comparison_dev, rendered, first_tile, tile_stride, st));
             // the next list holds at most this segment's entries
             if (!first) max_entries = t->seg_host[2u + ((seg - 1u) & 1u)];
         }
@@ -953,6 +966,21 @@ extern "C" int ngp_trainer_render(ngp_trainer* t, const float* camera_host, uint
     NGP_TRY(dalloc(s.camera, 12, "render camera"));
     int st = check_cuda(cudaMemcpyAsync(s.camera, camera_host, sizeof(float) * 12u, cudaMemcpyHostToDevice, t->stream), "render camera");
     if (st == NGP_OK) st = eval_one(t, s, 0, nullptr, rgb_device);
+    if (st == NGP_OK) st = check_cuda(cudaStreamSynchronize(t->stream), "render");
+    free_split(s);
+    return st;
+}
+
+extern "C" int ngp_trainer_render_tiles(ngp_trainer* t, const float* camera_host, uint32_t width, uint32_t height, float fx, float fy, float cx,
+                                        float cy, uint32_t first_tile, uint32_t tile_stride, float* rgb_device) {
+    clear_error();
+    if (t == nullptr || camera_host == nullptr || rgb_device == nullptr || width == 0 || height == 0 || !(fx > 0) || !(fy > 0) || tile_stride == 0)
+        return fail(NGP_ERR_INVALID, "render tiles: bad input");
+    Split s{};
+    s.frames = 1, s.width = width, s.height = height, s.fx = fx, s.fy = fy, s.cx = cx, s.cy = cy;
+    NGP_TRY(dalloc(s.camera, 12, "render camera"));
+    int st = check_cuda(cudaMemcpyAsync(s.camera, camera_host, sizeof(float) * 12u, cudaMemcpyHostToDevice, t->stream), "render camera");
+    if (st == NGP_OK) st = eval_image_segmented(t, s, 0, nullptr, rgb_device, first_tile, tile_stride);
     if (st == NGP_OK) st = check_cuda(cudaStreamSynchronize(t->stream), "render");
     free_split(s);
     return st;

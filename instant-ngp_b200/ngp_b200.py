@@ -615,6 +615,17 @@ class InstantNGP:
                                         _f32(principal[0]), _f32(principal[1]), _ptr(out)), "ngp_trainer_render")
         return out
 
+    def render_tiles(self, camera, width: int, height: int, focal, principal, first_tile: int, tile_stride: int, out):
+        """Render 64 x 64 tiles first_tile, first_tile + tile_stride, ... of the row-major tile grid
+        into out [height * width][3] (other pixels untouched): rank r of N renders r, r + N, ..."""
+        import numpy as np
+
+        cam = np.ascontiguousarray(camera, np.float32)
+        _check(lib().ngp_trainer_render_tiles(self.handle, ctypes.c_void_p(cam.ctypes.data), _u32(width), _u32(height), _f32(focal[0]),
+                                              _f32(focal[1]), _f32(principal[0]), _f32(principal[1]), _u32(first_tile), _u32(tile_stride),
+                                              _ptr(out)), "ngp_trainer_render_tiles")
+        return out
+
     def set_segmented_eval(self, enabled: bool) -> None:
         """Segmented marching for evaluation and rendering (default) or the reference's
         march-everything-first flow; the images are identical."""

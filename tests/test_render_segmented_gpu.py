@@ -282,3 +282,26 @@ def test_segment_outputs_match_oracle(ngp, oracle):
     assert (ns.cpu().numpy().view(np.uint32)[: lst.size] == ons).all()
     assert coords.cpu().numpy()[: ocoords.shape[0]].tobytes() == ocoords.tobytes()
     assert t_out.cpu().numpy()[: lst.size].tobytes() == ot2.tobytes()
+
+
+@pytest.mark.parametrize("ranks", [1, 3, 4])
+def test_tile_partitioned_render_assembles_the_image(ngp, ranks):
+    """Inference partitioned by 64 x 64 tiles (rank r of N renders tiles r, r + N, ...; the tile
+    loop of run_evaluation, ngp.train.cu:1616-1620): the ranks' tiles, rendered one after another
+    on this GPU, fill the image exactly once and give the whole-image render bit for bit,
+    including the clipped tiles at the right and bottom edges (200 x 150 is not a multiple of 64)."""
+    import torch
+
+    scene = workloads.procedural_dataset(n_train=8, n_test=1, width=200, height=150, seed=17, device="cuda")
+    m = ngp.InstantNGP(scene)
+    m.train(100)
+    cam = scene["test"]["camera"][0]
+    f, p = scene["test"]["focal"], scene["test"]["principal"]
+    full = m.render(cam, 200, 150, f, p)
+    tiled = torch.full((200 * 150, 3), -1.0, dtype=torch.float32, device="cuda")
+    for r in range(ranks):
+        m.render_tiles(cam, 200, 150, f, p, r, ranks, tiled)
+    torch.cuda.synchronize()
+    m.close()
+    assert (tiled >= 0).all()
+    assert tiled.cpu().numpy().tobytes() == full.cpu().numpy().tobytes()
