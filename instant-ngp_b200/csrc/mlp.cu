@@ -63,15 +63,35 @@ __device__ void load_weight_tile(unsigned char* tile, const __half* W, uint32_t 
     }
 }
 
+// Two fp32 values to packed fp16 (a low, b high), rounded to nearest, negative values to +0: one
+// cvt.rn.relu.f16x2.f32 instead of two max + one conversion.
+__device__ __forceinline__ uint32_t pack2_relu(float a, float b) {
+    uint32_t d;
+    asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+    return d;
+}
+
 // Store 8*nchunks fp32 values of this thread's row (ReLU optional) as fp16 into a tile.
 template <uint32_t NCHUNK, bool RELU>
 __device__ __forceinline__ void store_row(unsigned char* tile, uint32_t r, const float* v) {
 #pragma unroll
     for (uint32_t c = 0; c < NCHUNK; ++c) {
-        float a[8];
+        const float* a = v + c * 8;
+        if constexpr (RELU)
+            store_chunk(tile, r, c, NCHUNK, make_uint4(pack2_relu(a[0], a[1]), pack2_relu(a[2], a[3]), pack2_relu(a[4], a[5]), pack2_relu(a[6], a[7])));
+        else
+            store_chunk(tile, r, c, NCHUNK, make_uint4(pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7])));
+    }
+}
+
+// Store a row of 32 fp16 values (already rounded) into a 4-chunk tile.
+__device__ __forceinline__ void store_row_half32(unsigned char* tile, uint32_t r, const unsigned short* x) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) a[j] = RELU ? fmaxf(v[c * 8 + j], 0.0f) : v[c * 8 + j];
-        store_chunk(tile, r, c, NCHUNK, make_uint4(pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7])));
+    for (uint32_t c = 0; c < 4; ++c) {
+        const unsigned short* h = x + c * 8;
+        store_chunk(tile, r, c, 4,
+                    make_uint4(h[0] | (static_cast<uint32_t>(h[1]) << 16), h[2] | (static_cast<uint32_t>(h[3]) << 16),
+                               h[4] | (static_cast<uint32_t>(h[5]) << 16), h[6] | (static_cast<uint32_t>(h[7]) << 16)));
     }
 }
 
@@ -226,12 +246,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
         const bool valid     = row < n;
         if (tile + gridDim.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
         // ---- input row: 32 fp16 features (coalesced across the warp per feature) ----
-        {
-            float xv[32];
-#pragma unroll
-            for (uint32_t k = 0; k < 32; ++k) xv[k] = __half2float(__ushort_as_half(cur.x[k]));
-            store_row<4, false>(sx, t, xv);
-        }
+        store_row_half32(sx, t, cur.x);
         stage_sync();
         if (t == 0) {
             gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
@@ -386,12 +401,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
             dy_nxt = load_dy((tile + gridDim.x) * kRows + t);
         }
         // ---------------- forward recompute ----------------
-        {
-            float xv[32];
-#pragma unroll
-            for (uint32_t k = 0; k < 32; ++k) xv[k] = __half2float(__ushort_as_half(cur.x[k]));
-            store_row<4, false>(smem + kBX, t, xv);
-        }
+        store_row_half32(smem + kBX, t, cur.x);
         float g[16];
         {
             // rgb output gradient: channels 0-2 (extract_rgb_gradients, ngp.train.cu:1244-1253)
