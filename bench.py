@@ -593,22 +593,16 @@ def bench_encode_ours(args, rank, world, local):
         times = time_steps(step, args.steps, args.warmup, flush, stream, world)
         time.sleep(0.25)
     ms = max_over_ranks(sum(times) / len(times), world)
-    fw, bw = [], []
-    for _ in range(20):
-        for which, acc in (("f", fw), ("b", bw)):
-            flush()
-            if which == "b":
-                grad.zero_()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            if which == "f":
-                ngp.encode_grid_forward(layout, coords, table, feats, stream=stream)
-            else:
-                ngp.encode_grid_backward(layout, coords, dy, grad, stream=stream)
-            e.record(stream)
-            e.synchronize()
-            acc.append(s.elapsed_time(e))
+    fw, bw = encode_kernel_times(ngp, layout, coords, table, dy, feats, grad, stream, flush)
     fwd_ms, bwd_ms = statistics.median(fw), statistics.median(bw)
+    # the same kernels at the reference's compiled layout (8 levels x 4 features, scale 2) on the
+    # reference arm's inputs (7-float sample records), for a like-for-like kernel comparison
+    lay_ref = ngp.grid_layout(8, 4, 19, 16, 1.0)
+    c7, t7, d7 = workloads.encode_inputs(n, lay_ref.n_params, 8, 4, seed=1000, coord_stride=7)
+    c7, t7, d7 = torch.from_numpy(c7).cuda(), torch.from_numpy(t7.view(np.int16)).cuda(), torch.from_numpy(d7).cuda()
+    f7 = torch.empty((32, n), dtype=torch.float16, device="cuda")
+    g7 = torch.empty(lay_ref.n_params, dtype=torch.float32, device="cuda")
+    fw7, bw7 = encode_kernel_times(ngp, lay_ref, c7, t7, d7, f7, g7, stream, flush)
     coords_pin = torch.from_numpy(coords_h).pin_memory()
     dy_pin = torch.from_numpy(dy_h).pin_memory()
     feats_pin = torch.empty((L * F, n), dtype=torch.float16).pin_memory()
@@ -641,6 +635,10 @@ def bench_encode_ours(args, rank, world, local):
                    "base_resolution": 16, "per_level_scale": round(2 ** (7 / 15), 6), "parallelism": f"dp{world}",
                    "l2": "flushed (256 MB write) before every timed step"},
         "kernels_ms": {"encode_forward": round(fwd_ms, 5), "encode_backward": round(bwd_ms, 5)},
+        "same_layout_as_reference": {"layout": "L=8 F=4 log2T=19 base 16 b=2, 7-float records (the reference arm's inputs)",
+                                     "encode_forward_ms": round(statistics.median(fw7), 5), "encode_backward_ms": round(statistics.median(bw7), 5),
+                                     "value": round(n / ((statistics.median(fw7) + statistics.median(bw7)) * 1e-3) / 1e9, 4), "unit": "Gpts/s",
+                                     "note": "kernel times with the L2 flushed before each launch, medians of 20"},
         "roofline": {"kernel": f"encode_{dom}", "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"] + " (HBM copy bandwidth)",
                      "per_unit": f"{hbm_b} algorithmic HBM bytes per point (the 24 MB table is L2-resident), {n} points per launch",
@@ -656,6 +654,28 @@ def bench_encode_ours(args, rank, world, local):
                 "d2h_bytes_per_step": feats.numel() * 2},
         "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
     }
+
+
+def encode_kernel_times(ngp, layout, coords, table, dy, feats, grad, stream, flush, reps: int = 20):
+    """CUDA-event times (ms) of the encoding forward and backward launches, L2 flushed before each."""
+    import torch
+
+    fw, bw = [], []
+    for _ in range(reps):
+        for which, acc in (("f", fw), ("b", bw)):
+            flush()
+            if which == "b":
+                grad.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            if which == "f":
+                ngp.encode_grid_forward(layout, coords, table, feats, stream=stream)
+            else:
+                ngp.encode_grid_backward(layout, coords, dy, grad, stream=stream)
+            e.record(stream)
+            e.synchronize()
+            acc.append(s.elapsed_time(e))
+    return fw, bw
 
 
 def probe_gather_scatter(stream) -> dict:
@@ -744,6 +764,8 @@ def bench_mlp_ours(args, rank, world, local):
     n = BATCH
     x_h, c_h, dy_h = workloads.mlp_inputs(n, seed=31 + rank)
     params = torch.from_numpy(workloads.xavier_mlp_params(1).view(np.int16)).cuda()
+    # row-major encoded inputs [n][32] (NGP_ROWS), the layout the trainer keeps its encodings in
+    x_h = np.ascontiguousarray(x_h.T)
     x, coords, dy = torch.from_numpy(x_h).cuda(), torch.from_numpy(c_h).cuda(), torch.from_numpy(dy_h).cuda()
     out = torch.empty((n, 16), dtype=torch.float16, device="cuda")
     dx = torch.empty((32, n), dtype=torch.float16, device="cuda")
@@ -756,10 +778,10 @@ def bench_mlp_ours(args, rank, world, local):
         flush_buf.fill_(1.0)
 
     def fwd():
-        ngp.mlp_forward(params, x, coords, out, stream=stream)
+        ngp.mlp_forward(params, x, coords, out, x_stride=ngp.ROWS, stream=stream)
 
     def bwd():
-        ngp.mlp_backward(params, x, coords, dy, dx=dx, dw_f32=dw, stream=stream)
+        ngp.mlp_backward(params, x, coords, dy, dx=dx, dw_f32=dw, x_stride=ngp.ROWS, stream=stream)
 
     def step():
         fwd()
@@ -795,6 +817,7 @@ def bench_mlp_ours(args, rank, world, local):
         "vs_baseline": None, "dtype": "fp16 weights/activations, fp32 accumulation (tcgen05 kind::f16)",
         "data": "synthetic (U(-1,1) fp16 inputs, directions uniform on S^2, N(0,1) dL/dy, Xavier weights; seeded)",
         "config": {"workload": "config1 fused MLP fwd+bwd", "rows_per_gpu": n, "density": "32-64-16", "colour": "32-64-64-16",
+                   "input_layout": "row-major [n][32] fp16 (NGP_ROWS, the trainer's layout)",
                    "parallelism": f"dp{world} (no collective)", "l2": "flushed (256 MB write) before every timed step"},
         "kernels_ms": {"mlp_forward": round(fwd_ms, 5), "mlp_backward": round(bwd_ms, 5)},
         "roofline": {"kernel": "mlp_forward_kernel + mlp_backward_kernel", "bound": "tensor", "achieved": round(tflops, 2),

@@ -40,6 +40,13 @@ extern "C" {
 #define NGP_ERR_CUDA 2      /* a CUDA runtime call or kernel launch failed                  */
 #define NGP_ERR_OVERFLOW 3  /* a device-side budget overflowed (e.g. evaluation samples)    */
 #define NGP_ERR_STATE 4     /* call out of order (e.g. training stopped: no samples)        */
+/* Layout flag for the stride argument of encoded-feature buffers (encoding outputs and network
+ * inputs): a stride with this bit set means the buffer is row-major [rows][n_levels * F] (the
+ * features of one sample contiguous: 64 bytes at the 32-feature configurations) instead of the
+ * reference's feature-major [n_levels * F][stride].  With row-major inputs the networks fetch
+ * each 64-byte row by asynchronous 16-byte copies.  (The trainer keeps feature-major encodings:
+ * the encoding kernel, bound by its gathers' L1 traffic, writes them more cheaply.) */
+#define NGP_ROWS 0x80000000u
 #define NGP_ERR_TIMEOUT 5   /* a collective did not complete in time; the communicator was aborted */
 
 #define NGP_MAX_LEVELS 32

@@ -54,6 +54,10 @@ inline int check_cuda(cudaError_t status, const char* what) {
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
 
+// Encoded-feature buffers: feature-major [features][stride] (the reference's layout) or, with
+// NGP_ROWS set in the stride argument, row-major [rows][features].
+__host__ __device__ inline bool rows_layout(uint32_t stride) { return (stride & NGP_ROWS) != 0u; }
+
 // Number of SMs of the current device (148 on B200), cached per process.
 int sm_count();
 

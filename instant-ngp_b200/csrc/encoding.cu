@@ -79,23 +79,46 @@ __device__ __forceinline__ void position_fraction(float x, float scale, float& f
     frac                = __fsub_rn(pos, floored);
 }
 
+// Store N consecutive halves (N * 2 bytes, aligned to that size up to 16) with vector stores.
+template <uint32_t N>
+__device__ __forceinline__ void store_halves(__half* dst, const __half* v) {
+    if constexpr (N * 2 >= 16) {
+#pragma unroll
+        for (uint32_t k = 0; k < N / 8; ++k) reinterpret_cast<uint4*>(dst)[k] = *reinterpret_cast<const uint4*>(v + 8 * k);
+    } else if constexpr (N * 2 == 8) {
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(v);
+    } else if constexpr (N * 2 == 4) {
+        *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(v);
+    } else {
+        dst[0] = v[0];
+    }
+}
+
 // Point-major forward: a thread reads its point once and walks the levels LPI at a time (8 * LPI
 // gathers in flight).  Same per-(point, level) arithmetic as encode_forward_kernel.
-template <uint32_t F, uint32_t LPI>
+template <uint32_t F, uint32_t LPI, bool ROWS>
 __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(const uint32_t n, const float* __restrict__ coords,
                                                                                const uint32_t coord_stride, const __half* __restrict__ table,
                                                                                __half* __restrict__ out, const uint32_t out_stride,
                                                                                const __grid_constant__ GridParams grid,
                                                                                const uint32_t* __restrict__ rows, const uint32_t* __restrict__ n_dev) {
     using Vec        = typename FeatureVec<F>::type;
-    const uint32_t r = blockIdx.x * kEncodeThreads + threadIdx.x;
-    if (r >= (n_dev != nullptr ? min(*n_dev, n) : n)) return;
+    const uint32_t r    = blockIdx.x * kEncodeThreads + threadIdx.x;
+    const bool live     = r < (n_dev != nullptr ? min(*n_dev, n) : n);
+    if (!ROWS && !live) return;  // (row-major output: every lane takes part in the warp's write-out)
     // point i: row r itself, or the r-th entry of a row list (points read and written in place)
-    const uint32_t i = rows != nullptr ? __ldg(rows + r) : r;
+    const uint32_t i = live ? (rows != nullptr ? __ldg(rows + r) : r) : 0u;
     const float* c = coords + static_cast<uint64_t>(i) * coord_stride;
-    const float x[3] = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
+    const float x[3] = {live ? __ldg(c) : 0.0f, live ? __ldg(c + 1) : 0.0f, live ? __ldg(c + 2) : 0.0f};
     const Vec* tab   = reinterpret_cast<const Vec*>(table);
-    for (uint32_t l0 = 0; l0 < grid.n_levels; l0 += LPI) {
+    __half pair_out[ROWS ? LPI * F : 1];
+    // staging of row-major output rows (rows of 8, 16 or 32 halves), so that a warp writes whole
+    // rows per store instruction
+    constexpr uint32_t kStageHalves = 32;
+    __shared__ __align__(16) __half stage[ROWS ? kEncodeThreads : 1][ROWS ? kStageHalves : 1];
+    const uint32_t row_halves = grid.n_levels * F;
+    const bool staged = ROWS && row_halves <= kStageHalves && row_halves % 8u == 0u && 32u % (row_halves / 8u) == 0u;
+    for (uint32_t l0 = 0; live && l0 < grid.n_levels; l0 += LPI) {
         float frac[LPI][3];
         Vec v[LPI][8];
 #pragma unroll
@@ -130,8 +153,42 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(c
 #pragma unroll
                 for (uint32_t f = 0; f < F; ++f) acc[f] = __fmaf_rn(w, val[f], acc[f]);
             }
+            if constexpr (ROWS) {
+                // this level's F features into the pair's vector, written once per level pair
 #pragma unroll
-            for (uint32_t f = 0; f < F; ++f) out[static_cast<uint64_t>(level * F + f) * out_stride + i] = __float2half_rn(acc[f]);
+                for (uint32_t f = 0; f < F; ++f) pair_out[j * F + f] = __float2half_rn(acc[f]);
+            } else {
+#pragma unroll
+                for (uint32_t f = 0; f < F; ++f) out[static_cast<uint64_t>(level * F + f) * out_stride + i] = __float2half_rn(acc[f]);
+            }
+        }
+        if constexpr (ROWS) {
+            // row-major [i][n_levels * F]: the level pair's LPI * F halves go to this thread's
+            // staged row (written out coalesced below), or straight to the row when not staged
+            __half* dst = staged ? &stage[threadIdx.x][l0 * F] : out + static_cast<uint64_t>(i) * (grid.n_levels * F) + l0 * F;
+            if (l0 + LPI <= grid.n_levels) {
+                store_halves<LPI * F>(dst, pair_out);
+            } else {
+                for (uint32_t k = 0; k < (grid.n_levels - l0) * F; ++k) dst[k] = pair_out[k];
+            }
+        }
+    }
+    if constexpr (ROWS) {
+        if (staged) {
+            // The warp's rows leave as 16-byte chunks: in round k, lane l writes chunk l % C of the
+            // row of lane k * (32 / C) + l / C (C chunks per row), so each store instruction writes
+            // 32 / C whole rows instead of one strided piece of every row.
+            const uint32_t lane = threadIdx.x & 31u, wbase = threadIdx.x & ~31u;
+            __syncwarp();  // the warp's staged rows are visible to every lane
+            const uint32_t live_lanes = __ballot_sync(0xFFFFFFFFu, live);
+            const uint32_t C = (grid.n_levels * F) / 8u, per = 32u / C;
+            for (uint32_t k = 0; k < C; ++k) {
+                const uint32_t src = k * per + lane / C, chunk = lane % C;
+                const uint32_t row = __shfl_sync(0xFFFFFFFFu, i, src);
+                if ((live_lanes >> src) & 1u)
+                    reinterpret_cast<uint4*>(out + static_cast<uint64_t>(row) * (C * 8u))[chunk] =
+                        *reinterpret_cast<const uint4*>(&stage[wbase + src][chunk * 8u]);
+            }
         }
     }
 }
@@ -314,12 +371,17 @@ int launch_points_forward(const ngp_grid_layout& layout, const GridParams& grid,
     const uint32_t blocks  = (n + kEncodeThreads - 1) / kEncodeThreads;
     const auto* t          = reinterpret_cast<const __half*>(table);
     auto* o                = reinterpret_cast<__half*>(out);
+    const bool row_major   = rows_layout(out_stride);
+#define NGP_ENC_FWD(FF)                                                                                                              \
+    (row_major ? encode_forward_points_kernel<FF, lpi, true><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev) \
+               : encode_forward_points_kernel<FF, lpi, false><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev))
     switch (layout.features_per_level) {
-        case 1: encode_forward_points_kernel<1, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
-        case 2: encode_forward_points_kernel<2, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
-        case 4: encode_forward_points_kernel<4, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
-        default: encode_forward_points_kernel<8, lpi><<<blocks, kEncodeThreads, 0, s>>>(n, coords, coord_stride, t, o, out_stride, grid, rows, n_dev); break;
+        case 1: NGP_ENC_FWD(1); break;
+        case 2: NGP_ENC_FWD(2); break;
+        case 4: NGP_ENC_FWD(4); break;
+        default: NGP_ENC_FWD(8); break;
     }
+#undef NGP_ENC_FWD
     return check_launch("encode_forward_points_kernel");
 }
 
@@ -343,7 +405,7 @@ extern "C" int ngp_encode_grid_forward(const ngp_grid_layout* layout, uint32_t n
     NGP_TRY(validate_layout(layout));
     if (n == 0) return NGP_OK;
     if (coords == nullptr || table == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "encode forward: null pointer");
-    if (coord_stride < 3 || out_stride < n) return fail(NGP_ERR_INVALID, "encode forward: bad stride");
+    if (coord_stride < 3 || (!rows_layout(out_stride) && out_stride < n)) return fail(NGP_ERR_INVALID, "encode forward: bad stride");
     const GridParams grid = make_grid_params(*layout);
     return launch_points_forward(*layout, grid, n, coords, coord_stride, table, out, out_stride, nullptr, nullptr, as_stream(stream));
 }

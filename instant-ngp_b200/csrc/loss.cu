@@ -390,7 +390,12 @@ __global__ void __launch_bounds__(kCtaThreads) compact_copy_kernel(const __grid_
     const float* __restrict__ cin = p.coords + static_cast<uint64_t>(base) * 7u;
     float* __restrict__ cout      = p.coords_out + static_cast<uint64_t>(cbase) * 7u;
     for (uint32_t j = lane; j < k * 7u; j += 32u) cout[j] = __ldg(cin + j);
-    if (p.enc_out != nullptr) {
+    if (p.enc_out != nullptr && rows_layout(p.enc_stride)) {
+        // row-major encodings: a sample's 64-byte row is copied to its compacted row
+        const uint4* __restrict__ src = reinterpret_cast<const uint4*>(p.enc) + static_cast<uint64_t>(base) * 4u;
+        uint4* __restrict__ dst       = reinterpret_cast<uint4*>(p.enc_out) + static_cast<uint64_t>(cbase) * 4u;
+        for (uint32_t j = lane; j < k * 4u; j += 32u) dst[j] = __ldg(src + j);
+    } else if (p.enc_out != nullptr) {
         // all 32 features of a sample are loaded before any is stored (independent loads in flight)
         const unsigned short* __restrict__ src = reinterpret_cast<const unsigned short*>(p.enc) + base;
         unsigned short* __restrict__ dst       = reinterpret_cast<unsigned short*>(p.enc_out) + cbase;
@@ -662,9 +667,14 @@ __global__ void pad_batch_kernel(const uint32_t* __restrict__ count, float* __re
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;  // row of the batch
     if (n == 0 || r < n || r >= batch) return;
     const uint32_t src = r % n;
-    if (enc != nullptr)
+    if (enc != nullptr && rows_layout(enc_stride)) {
+        uint4* e = reinterpret_cast<uint4*>(enc);
+#pragma unroll
+        for (uint32_t q = 0; q < 4u; ++q) e[static_cast<uint64_t>(r) * 4u + q] = e[static_cast<uint64_t>(src) * 4u + q];
+    } else if (enc != nullptr) {
 #pragma unroll 8
         for (uint32_t f = 0; f < 32u; ++f) enc[static_cast<uint64_t>(f) * enc_stride + r] = enc[static_cast<uint64_t>(f) * enc_stride + src];
+    }
 #pragma unroll
     for (int q = 0; q < 7; ++q) coords[static_cast<uint64_t>(r) * 7u + q] = coords[static_cast<uint64_t>(src) * 7u + q];
     const float s = static_cast<float>(n) / static_cast<float>(batch);
@@ -1013,7 +1023,7 @@ extern "C" int ngp_training_compact_progressive(uint32_t rays_per_batch, const u
     clear_error();
     if (rays_per_batch == 0) return NGP_OK;
     if (layout == nullptr || params == nullptr || coords == nullptr || numsteps == nullptr || enc == nullptr || density == nullptr || rows == nullptr ||
-        compacted_coords == nullptr || compacted_counter == nullptr || scratch == nullptr || enc_stride < sample_bound)
+        compacted_coords == nullptr || compacted_counter == nullptr || scratch == nullptr || (!rows_layout(enc_stride) && enc_stride < sample_bound))
         return fail(NGP_ERR_INVALID, "progressive compaction: invalid input");
     if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "progressive compaction: scratch too small");
     if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "progressive compaction: scratch must be 16-byte aligned");
@@ -1053,7 +1063,7 @@ extern "C" int ngp_training_select_progressive(uint32_t rays_per_batch, const ui
     clear_error();
     if (rays_per_batch == 0) return NGP_OK;
     if (layout == nullptr || params == nullptr || coords == nullptr || numsteps == nullptr || enc == nullptr || density == nullptr || rows == nullptr ||
-        batch_rows == nullptr || n_selected == nullptr || compacted_counter == nullptr || scratch == nullptr || enc_stride < sample_bound)
+        batch_rows == nullptr || n_selected == nullptr || compacted_counter == nullptr || scratch == nullptr || (!rows_layout(enc_stride) && enc_stride < sample_bound))
         return fail(NGP_ERR_INVALID, "progressive selection: invalid input");
     if (scratch_bytes < loss_scratch_size(rays_per_batch)) return fail(NGP_ERR_INVALID, "progressive selection: scratch too small");
     if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "progressive selection: scratch must be 16-byte aligned");
@@ -1139,7 +1149,7 @@ extern "C" int ngp_eval_network_progressive(uint32_t n_rays, const ngp_grid_layo
     clear_error();
     if (n_rays == 0) return NGP_OK;
     if (layout == nullptr || params == nullptr || coords == nullptr || numsteps == nullptr || enc == nullptr || network_output == nullptr ||
-        rows == nullptr || scratch == nullptr || enc_stride < sample_bound)
+        rows == nullptr || scratch == nullptr || (!rows_layout(enc_stride) && enc_stride < sample_bound))
         return fail(NGP_ERR_INVALID, "progressive evaluation: invalid input");
     if (scratch_bytes < loss_scratch_size(n_rays)) return fail(NGP_ERR_INVALID, "progressive evaluation: scratch too small");
     if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "progressive evaluation: scratch must be 16-byte aligned");
@@ -1194,7 +1204,7 @@ extern "C" int ngp_pad_training_batch(const uint32_t* compacted_counter, float* 
 extern "C" int ngp_pad_training_batch_enc(const uint32_t* compacted_counter, float* compacted_coords, uint16_t* dloss_doutput, uint16_t* enc,
                                           uint32_t enc_stride, void* stream) {
     clear_error();
-    if (compacted_counter == nullptr || compacted_coords == nullptr || dloss_doutput == nullptr || enc == nullptr || enc_stride < kNetworkBatch)
+    if (compacted_counter == nullptr || compacted_coords == nullptr || dloss_doutput == nullptr || enc == nullptr || (!rows_layout(enc_stride) && enc_stride < kNetworkBatch))
         return fail(NGP_ERR_INVALID, "pad batch: invalid input");
     pad_batch_kernel<<<kNetworkBatch / 256u, 256, 0, as_stream(stream)>>>(compacted_counter, compacted_coords, reinterpret_cast<__half*>(dloss_doutput),
                                                                             kNetworkBatch, reinterpret_cast<__half*>(enc), enc_stride);

@@ -49,6 +49,24 @@ __device__ __forceinline__ uint4 load_chunk(const unsigned char* tile, uint32_t 
     return *reinterpret_cast<const uint4*>(tile + tile_off(r, c, cpr));
 }
 
+// Asynchronous 16-byte global -> shared copy (cp.async, L2 only); src_bytes = 0 zero-fills.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(umma::smem_addr(smem_dst)), "l"(gsrc), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Row-major encoded inputs ([rows][32] fp16, NGP_ROWS): tile row r's 64 bytes arrive as four
+// 16-byte asynchronous copies straight into the interleaved operand tile (chunk c of row r at
+// tile_off(r, c, 4)); rows past the end are zero-filled.  One commit group per call.
+__device__ __forceinline__ void issue_row_copy(unsigned char* tile, uint32_t r, const __half* x, uint32_t col, bool valid) {
+    const __half* src = x + static_cast<uint64_t>(valid ? col : 0u) * 32u;
+#pragma unroll
+    for (uint32_t c = 0; c < 4; ++c) cp_async16(tile + tile_off(r, c, 4), src + c * 8u, valid ? 16u : 0u);
+    cp_async_commit();
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
@@ -96,16 +114,18 @@ __device__ __forceinline__ void store_row_half32(unsigned char* tile, uint32_t r
 }
 
 // Read N fp32 accumulator columns [col, col+N) of this thread's lane.
+// All N / 16 reads are issued before the one wait, so their latencies overlap.
 template <uint32_t N>
 __device__ __forceinline__ void read_acc(uint32_t tmem, uint32_t col, float* v) {
     const uint32_t lane_base = (threadIdx.x & ~31u) << 16;
+    uint32_t r[N / 16][16];
 #pragma unroll
-    for (uint32_t c = 0; c < N; c += 16) {
-        float t[16];
-        umma::tmem_ld16(tmem + lane_base + col + c, t);
+    for (uint32_t c = 0; c < N / 16; ++c) umma::tmem_ld16_async(tmem + lane_base + col + c * 16, r[c]);
+    umma::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[c + j] = t[j];
-    }
+    for (uint32_t c = 0; c < N / 16; ++c)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[c * 16 + j] = __uint_as_float(r[c][j]);
 }
 
 // Issue D(+)= A * B^T over K (multiple of 16) from one thread.
@@ -169,22 +189,24 @@ __device__ __forceinline__ bool stage_wait(uint64_t* mbar, uint32_t& phase) {
 // feature) and, when the colour network runs, the warped view direction of its record.
 // A row list (optional) maps tile row r to sample rows[r]: its features, record and output are
 // read and written at that sample's position.
-template <bool DIR>
+template <bool DIR, bool XROWS = false>
 struct RowInputs {
-    unsigned short x[32];
+    unsigned short x[XROWS ? 1 : 32];  // feature-major inputs only (row-major rows arrive by cp.async)
     float dir[DIR ? 3 : 1];
     uint32_t col;  // the sample this row reads and writes
 };
 
-template <bool DIR>
+template <bool DIR, bool XROWS = false>
 __device__ __forceinline__ void load_row_inputs(const __half* __restrict__ x, uint32_t x_stride, const float* __restrict__ coords,
-                                                uint32_t coord_stride, uint32_t n, uint32_t row, RowInputs<DIR>& in,
+                                                uint32_t coord_stride, uint32_t n, uint32_t row, RowInputs<DIR, XROWS>& in,
                                                 const uint32_t* __restrict__ rows = nullptr) {
     const bool valid = row < n;
     in.col           = valid ? (rows != nullptr ? __ldg(rows + row) : row) : 0u;
     const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+    if constexpr (!XROWS) {
 #pragma unroll
-    for (uint32_t k = 0; k < 32; ++k) in.x[k] = valid ? __ldg(xs + static_cast<uint64_t>(k) * x_stride + in.col) : static_cast<unsigned short>(0);
+        for (uint32_t k = 0; k < 32; ++k) in.x[k] = valid ? __ldg(xs + static_cast<uint64_t>(k) * x_stride + in.col) : static_cast<unsigned short>(0);
+    }
     if constexpr (DIR) {
         const float* c = coords + static_cast<uint64_t>(in.col) * coord_stride;
         in.dir[0] = __ldg(c + 4), in.dir[1] = __ldg(c + 5), in.dir[2] = __ldg(c + 6);
@@ -207,14 +229,15 @@ struct MlpForwardParams {
 enum : int { kModeFull = 0, kModeDensity = 1 };
 
 constexpr uint32_t kFwdTmemCols = 128;  // D0: cols 0-63, D1: cols 64-79
-constexpr uint32_t kFwdSmem     = kSWeights + 8192 + 16384 + 1024;
+// weights | input tile 0 | input tile 1 (row-major inputs: the next tile's copies land here) | hidden
+constexpr uint32_t kFwdSmem     = kSWeights + 8192 + 8192 + 16384 + 1024;
 
-template <int MODE>
+template <int MODE, bool XROWS>
 __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
     extern __shared__ __align__(1024) unsigned char smem[];
-    unsigned char* sw  = smem;                      // weights
-    unsigned char* sx  = smem + kSWeights;          // 128 x 32 input tile (X, then rgb input)
-    unsigned char* shd = sx + 8192;                 // 128 x 64 hidden tile
+    unsigned char* sw    = smem;                      // weights
+    unsigned char* sxb[2] = {smem + kSWeights, smem + kSWeights + 8192};  // 128 x 32 input tiles (X, then rgb input)
+    unsigned char* shd   = smem + kSWeights + 16384;  // 128 x 64 hidden tile
     __shared__ uint64_t mbar;
     __shared__ uint32_t tmem_slot;
 
@@ -231,7 +254,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
     stage_sync();
     const uint32_t tmem = tmem_slot;
     const uint32_t d0 = tmem, d1 = tmem + 64;
-    const uint32_t a_sx = umma::smem_addr(sx), a_shd = umma::smem_addr(shd), a_sw = umma::smem_addr(sw);
+    const uint32_t a_shd = umma::smem_addr(shd), a_sw = umma::smem_addr(sw);
     uint32_t phase  = 0;
     bool ok         = true;
     const uint32_t n       = p.n_dev != nullptr ? min(*p.n_dev, p.n) : p.n;
@@ -239,14 +262,30 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
 
     // The next tile's inputs are loaded into registers while this tile's layers run (software
     // pipelining of the only global-memory reads of the loop).
-    RowInputs<MODE == kModeFull> cur, nxt;
-    if (blockIdx.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, blockIdx.x * kRows + t, cur, p.rows);
-    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    // Row-major inputs (XROWS) arrive by cp.async one tile ahead into the other input buffer;
+    // feature-major inputs are gathered into registers one tile ahead and stored here.
+    RowInputs<MODE == kModeFull, XROWS> cur, nxt;
+    if (blockIdx.x < n_tiles) {
+        load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, blockIdx.x * kRows + t, cur, p.rows);
+        if constexpr (XROWS) issue_row_copy(sxb[0], t, p.x, cur.col, blockIdx.x * kRows + t < n);
+    }
+    uint32_t it = 0;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row   = tile * kRows + t;
         const bool valid     = row < n;
-        if (tile + gridDim.x < n_tiles) load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
-        // ---- input row: 32 fp16 features (coalesced across the warp per feature) ----
-        store_row_half32(sx, t, cur.x);
+        unsigned char* sx    = XROWS ? sxb[it & 1u] : sxb[0];
+        const uint32_t a_sx  = umma::smem_addr(sx);
+        if (tile + gridDim.x < n_tiles) {
+            load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
+            if constexpr (XROWS) issue_row_copy(sxb[(it + 1u) & 1u], t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
+        } else if constexpr (XROWS) {
+            cp_async_commit();  // an empty group keeps the wait count below uniform
+        }
+        // ---- input row: 32 fp16 features ----
+        if constexpr (XROWS)
+            cp_async_wait<1>();  // this tile's copies (all but the group just issued) have landed
+        else
+            store_row_half32(sx, t, cur.x);
         stage_sync();
         if (t == 0) {
             gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
@@ -331,6 +370,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
         if (!__syncthreads_and(ok)) break;
         umma::fence_after_sync();
     }
+    if constexpr (XROWS) cp_async_wait<0>();  // no copy may still target shared memory at exit
     umma::fence_before_sync();
     __syncthreads();
     if (t < 32) umma::tmem_dealloc(tmem, kFwdTmemCols);
@@ -357,9 +397,12 @@ struct MlpBackwardParams {
 constexpr uint32_t kColD0 = 0, kColWrOut = 64, kColWrH = 80, kColWrIn = 144, kColWdOut = 176, kColWdIn = 192;
 constexpr uint32_t kBwdTmemCols = 256;
 // shared memory tiles (bytes)
+// (kBX2: the second input tile; row-major inputs of the next tile are copied into the tile the
+// current one does not use)
 constexpr uint32_t kBX = kSWeights, kBHd = kBX + 8192, kBRi = kBHd + 16384, kBH1 = kBRi + 8192, kBH2 = kBH1 + 16384, kBDy = kBH2 + 16384,
-                   kBGuard = kBDy + 4096, kBwdSmem = kBGuard + 4096;
+                   kBGuard = kBDy + 4096, kBX2 = kBGuard + 4096, kBwdSmem = kBX2 + 8192;
 
+template <bool XROWS>
 __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_constant__ MlpBackwardParams p) {
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ uint64_t mbar;
@@ -384,24 +427,34 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
     const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
 
     // next tile's inputs (features, direction, output gradient) prefetched during this tile
-    RowInputs<true> cur, nxt;
+    RowInputs<true, XROWS> cur, nxt;
     uint2 dy_cur = make_uint2(0, 0), dy_nxt = make_uint2(0, 0);
     auto load_dy = [&](uint32_t r) {
         return r < p.n ? __ldg(reinterpret_cast<const uint2*>(p.dy + static_cast<uint64_t>(r) * 16u)) : make_uint2(0, 0);
     };
+    unsigned char* xbuf[2] = {smem + kBX, smem + kBX2};
     if (blockIdx.x < n_tiles) {
         load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur, p.rows);
+        if constexpr (XROWS) issue_row_copy(xbuf[0], t, p.x, cur.col, blockIdx.x * kRows + t < p.n);
         dy_cur = load_dy(blockIdx.x * kRows + t);
     }
-    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    uint32_t it = 0;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row = tile * kRows + t;
         const bool valid   = row < p.n;
+        const uint32_t bx  = XROWS && (it & 1u) ? kBX2 : kBX;  // this tile's input tile
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
+            if constexpr (XROWS) issue_row_copy(xbuf[(it + 1u) & 1u], t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < p.n);
             dy_nxt = load_dy((tile + gridDim.x) * kRows + t);
+        } else if constexpr (XROWS) {
+            cp_async_commit();  // an empty group keeps the wait count below uniform
         }
         // ---------------- forward recompute ----------------
-        store_row_half32(smem + kBX, t, cur.x);
+        if constexpr (XROWS)
+            cp_async_wait<1>();  // this tile's copies have landed
+        else
+            store_row_half32(smem + kBX, t, cur.x);
         float g[16];
         {
             // rgb output gradient: channels 0-2 (extract_rgb_gradients, ngp.train.cu:1244-1253)
@@ -417,7 +470,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         }
         stage_sync();
         if (t == 0) {
-            gemm(tmem + kColD0, 64, 32, s0 + kBX, false, 4, s0 + kSWdIn, false, 4, false);
+            gemm(tmem + kColD0, 64, 32, s0 + bx, false, 4, s0 + kSWdIn, false, 4, false);
             umma::commit(&mbar);
         }
         ok = stage_wait(&mbar, phase);
@@ -549,7 +602,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         stage_sync();
         if (t == 0) {
             gemm(tmem + kColD0, 32, 64, s0 + kBHd, false, 8, s0 + kSWdIn, true, 4, false);
-            gemm(tmem + kColWdIn, 32, 128, s0 + kBHd, true, 8, s0 + kBX, true, 4, !first);
+            gemm(tmem + kColWdIn, 32, 128, s0 + kBHd, true, 8, s0 + bx, true, 4, !first);
             umma::commit(&mbar);
         }
         ok = ok && stage_wait(&mbar, phase);
@@ -568,6 +621,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         umma::fence_after_sync();
     }
 
+    if constexpr (XROWS) cp_async_wait<0>();  // no copy may still target shared memory
     // ---- write this CTA's weight-gradient partial (rows 0-63 of the M = 128 accumulators) ----
     umma::fence_before_sync();
     __syncthreads();
@@ -672,13 +726,31 @@ using namespace ngp;
 namespace {
 int ensure_attrs() {
     static int status = [] {
-        cudaError_t e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+        cudaError_t e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
         return static_cast<int>(e);
     }();
     if (status != 0) return fail(NGP_ERR_CUDA, std::string("mlp: cudaFuncSetAttribute: ") + cudaGetErrorString(static_cast<cudaError_t>(status)));
     return NGP_OK;
+}
+}  // namespace
+
+namespace {
+template <int MODE>
+int launch_forward(const MlpForwardParams& p, uint32_t n_rows, cudaStream_t stream, const char* what) {
+    const uint32_t n_tiles = (n_rows + kRows - 1) / kRows;
+    if (rows_layout(p.x_stride)) {
+        const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<MODE, true>), n_tiles, kFwdTmemCols);
+        mlp_forward_kernel<MODE, true><<<grid, kThreads, kFwdSmem, stream>>>(p);
+    } else {
+        const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<MODE, false>), n_tiles, kFwdTmemCols);
+        mlp_forward_kernel<MODE, false><<<grid, kThreads, kFwdSmem, stream>>>(p);
+    }
+    return check_launch(what);
 }
 }  // namespace
 
@@ -687,28 +759,22 @@ extern "C" int ngp_mlp_forward(uint32_t n, const uint16_t* params, const uint16_
     clear_error();
     if (n == 0) return NGP_OK;
     if (params == nullptr || x == nullptr || coords == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "mlp forward: null pointer");
-    if (x_stride < n || coord_stride < 7) return fail(NGP_ERR_INVALID, "mlp forward: bad stride");
+    if ((!rows_layout(x_stride) && x_stride < n) || coord_stride < 7) return fail(NGP_ERR_INVALID, "mlp forward: bad stride");
     NGP_TRY(ensure_attrs());
     MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
                        reinterpret_cast<__half*>(out), reinterpret_cast<__half*>(density_rgb_in), nullptr, nullptr};
-    const uint32_t n_tiles = (n + kRows - 1) / kRows;
-    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull>), n_tiles, kFwdTmemCols);
-    mlp_forward_kernel<kModeFull><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
-    return check_launch("mlp_forward_kernel");
+    return launch_forward<kModeFull>(p, n, as_stream(stream), "mlp_forward_kernel");
 }
 
 extern "C" int ngp_density_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, uint16_t* out, void* stream) {
     clear_error();
     if (n == 0) return NGP_OK;
     if (params == nullptr || x == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "density forward: null pointer");
-    if (x_stride < n) return fail(NGP_ERR_INVALID, "density forward: bad stride");
+    if (!rows_layout(x_stride) && x_stride < n) return fail(NGP_ERR_INVALID, "density forward: bad stride");
     NGP_TRY(ensure_attrs());
     MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7,
                        reinterpret_cast<__half*>(out), nullptr, nullptr, nullptr};
-    const uint32_t n_tiles = (n + kRows - 1) / kRows;
-    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity>), n_tiles, kFwdTmemCols);
-    mlp_forward_kernel<kModeDensity><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
-    return check_launch("mlp_forward_kernel<density>");
+    return launch_forward<kModeDensity>(p, n, as_stream(stream), "mlp_forward_kernel<density>");
 }
 
 extern "C" int ngp_mlp_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
@@ -721,10 +787,7 @@ extern "C" int ngp_mlp_forward_rows(uint32_t max_rows, const uint32_t* rows, con
     NGP_TRY(ensure_attrs());
     MlpForwardParams p{max_rows, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
                        reinterpret_cast<__half*>(out), nullptr, rows, n_rows};
-    const uint32_t n_tiles = (max_rows + kRows - 1) / kRows;
-    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull>), n_tiles, kFwdTmemCols);
-    mlp_forward_kernel<kModeFull><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
-    return check_launch("mlp_forward_kernel");
+    return launch_forward<kModeFull>(p, max_rows, as_stream(stream), "mlp_forward_kernel");
 }
 
 extern "C" int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,
@@ -735,10 +798,7 @@ extern "C" int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows,
     NGP_TRY(ensure_attrs());
     MlpForwardParams p{max_rows, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7,
                        reinterpret_cast<__half*>(out), nullptr, rows, n_rows};
-    const uint32_t n_tiles = (max_rows + kRows - 1) / kRows;
-    const int grid         = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity>), n_tiles, kFwdTmemCols);
-    mlp_forward_kernel<kModeDensity><<<grid, kThreads, kFwdSmem, as_stream(stream)>>>(p);
-    return check_launch("mlp_forward_kernel<density>");
+    return launch_forward<kModeDensity>(p, max_rows, as_stream(stream), "mlp_forward_kernel<density>");
 }
 
 extern "C" uint32_t ngp_mlp_backward_scratch_floats(void) { return mlp_backward_max_ctas() * kMlpParams; }
@@ -750,17 +810,23 @@ int mlp_backward_launch(uint32_t n, const uint32_t* rows, const uint16_t* params
                         float* dw_f32, uint16_t* dw_f16, float dw_scale, void* stream) {
     if (params == nullptr || x == nullptr || coords == nullptr || dy == nullptr || scratch == nullptr)
         return fail(NGP_ERR_INVALID, "mlp backward: null pointer");
-    if ((rows == nullptr && x_stride < n) || coord_stride < 7 || (dx != nullptr && dx_stride < n)) return fail(NGP_ERR_INVALID, "mlp backward: bad stride");
+    if ((rows == nullptr && !rows_layout(x_stride) && x_stride < n) || coord_stride < 7 || (dx != nullptr && dx_stride < n))
+        return fail(NGP_ERR_INVALID, "mlp backward: bad stride");
     NGP_TRY(ensure_attrs());
     const uint32_t n_tiles = (n + kRows - 1) / kRows;
-    uint32_t grid          = static_cast<uint32_t>(mlp_grid(kBwdSmem, reinterpret_cast<const void*>(mlp_backward_kernel), n_tiles == 0 ? 1 : n_tiles, kBwdTmemCols));
+    const bool xrows       = rows_layout(x_stride);
+    const void* kern       = xrows ? reinterpret_cast<const void*>(mlp_backward_kernel<true>) : reinterpret_cast<const void*>(mlp_backward_kernel<false>);
+    uint32_t grid          = static_cast<uint32_t>(mlp_grid(kBwdSmem, kern, n_tiles == 0 ? 1 : n_tiles, kBwdTmemCols));
     if (static_cast<size_t>(grid) * kMlpParams > scratch_floats) {
         grid = static_cast<uint32_t>(scratch_floats / kMlpParams);
         if (grid == 0) return fail(NGP_ERR_INVALID, "mlp backward: scratch too small (need ngp_mlp_backward_scratch_floats())");
     }
     MlpBackwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
                         reinterpret_cast<const __half*>(dy), reinterpret_cast<__half*>(dx), dx_stride, scratch, rows};
-    mlp_backward_kernel<<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
+    if (xrows)
+        mlp_backward_kernel<true><<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
+    else
+        mlp_backward_kernel<false><<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
     NGP_TRY(check_launch("mlp_backward_kernel"));
     mlp_reduce_partials_kernel<<<(kMlpParams + 31) / 32, 32 * kReduceGroups, 0, as_stream(stream)>>>(scratch, grid, dw_scale, dw_f32,
                                                                                                        reinterpret_cast<__half*>(dw_f16));

@@ -208,6 +208,7 @@ def mlp_status(reset: bool = False) -> int:
 # ---------------------------------------------------------------------------------------------
 GRID_CELLS = 128 ** 3
 NETWORK_BATCH = 1 << 18
+ROWS = 0x80000000  # NGP_ROWS: pass as a feature-buffer stride for row-major [rows][features] buffers
 MAX_SAMPLES = NETWORK_BATCH * 16
 
 
@@ -369,6 +370,16 @@ def training_loss_selected(rays_per_batch, step, ray_counter, pixels, frame_coun
 
 def pad_training_rows(compacted_counter, batch_rows, dloss_doutput, stream=None) -> None:
     _check(lib().ngp_pad_training_rows(_ptr(compacted_counter), _ptr(batch_rows), _ptr(dloss_doutput), _stream(stream)), "ngp_pad_training_rows")
+
+
+def encode_grid_forward_rows(layout: GridLayout, max_rows, rows, n_rows, coords, table, out, out_stride, stream=None) -> None:
+    _check(lib().ngp_encode_grid_forward_rows(ctypes.byref(layout), _u32(max_rows), _ptr(rows), _ptr(n_rows), _ptr(coords), _u32(coords.shape[1]),
+                                              _ptr(table), _ptr(out), _u32(out_stride), _stream(stream)), "ngp_encode_grid_forward_rows")
+
+
+def density_forward_rows(max_rows, rows, n_rows, params, x, x_stride, out, stream=None) -> None:
+    _check(lib().ngp_density_forward_rows(_u32(max_rows), _ptr(rows), _ptr(n_rows), _ptr(params), _ptr(x), _u32(x_stride), _ptr(out),
+                                          _stream(stream)), "ngp_density_forward_rows")
 
 
 def mlp_forward_rows(max_rows, rows, n_rows, params, x, x_stride, coords, out, stream=None) -> None:

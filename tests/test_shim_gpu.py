@@ -1,24 +1,21 @@
 """The drop-in `ngp::cuda` layer (instant-ngp_b200/shim/ngp_train_cuda.cpp): the reference's own
 training loop (InstantNGP::train, ngp.train.cpp:108-155, replayed through ngp.train.h's interface
-by oracle/train_replay.inc) runs once on the reference's ngp.train.cu and once on this library,
-on the same seeded scene.  Sample placement differs (ray order vs atomic order) and gradients are
-summed in fp32 instead of fp16, so the runs are compared statistically: both train, the
-adaptive batch settles to similar ray and sample counts (within 0.6-1.7x), and the test PSNR after
-1000 steps is at least the reference's minus 1.5 dB: on scenes this small single runs of either
-implementation vary by about a dB (measured on 12-view 160x160 scenes: drop-in 20.3 vs reference
-19.0, 23.5 vs 20.9 and 20.4 vs 21.2 dB)."""
+by oracle/train_replay.inc) runs once on the reference's ngp.train.cu and once on this library.
+
+Sample placement differs (ray order vs atomic order) and gradients are summed in fp32 instead of
+fp16, so the runs are compared statistically:
+* on a small scene the adaptive batch settles to similar ray and sample counts (within 0.6-1.7x);
+* on the config-3 scene (100 train / 20 test views of 800 x 800), over three scenes (seeds) and
+  2000 steps each, the drop-in layer's mean test PSNR is at least the reference's minus 0.2 dB
+  (north_star: final PSNR within 0.2 dB)."""
 from __future__ import annotations
 
+import numpy as np
 import pytest
 
 import workloads
 
 pytestmark = pytest.mark.gpu
-
-
-@pytest.fixture(scope="module")
-def scene():
-    return workloads.procedural_dataset(n_train=20, n_test=3, width=192, height=192, seed=11)
 
 
 def _replay(so, scene, steps):
@@ -33,14 +30,29 @@ def _replay(so, scene, steps):
     return stats, psnr
 
 
-def test_reference_loop_on_drop_in_layer(reflib, scene):
+def test_reference_loop_on_drop_in_layer_settles_alike(reflib):
     from oracle import REF_SO, SHIM_REPLAY_SO
 
+    scene = workloads.procedural_dataset(n_train=20, n_test=3, width=192, height=192, seed=11)
     ref_stats, ref_psnr = _replay(REF_SO, scene, 1000)
     our_stats, our_psnr = _replay(SHIM_REPLAY_SO, scene, 1000)
     print(f"reference {ref_psnr:.2f} dB {ref_stats}; drop-in {our_psnr:.2f} dB {our_stats}")
     assert our_stats["measured"] > 0 and ref_stats["measured"] > 0
     assert 0.6 < our_stats["rays_per_batch"] / ref_stats["rays_per_batch"] < 1.7
     assert 0.6 < our_stats["measured_before"] / ref_stats["measured_before"] < 1.7
-    assert our_psnr >= ref_psnr - 1.5
     assert our_psnr > 15.0
+
+
+def test_drop_in_layer_psnr_within_0p2_db_over_three_scenes(reflib):
+    from oracle import REF_SO, SHIM_REPLAY_SO
+
+    ours, ref = [], []
+    for seed in (3, 13, 23):
+        scene = workloads.procedural_dataset(n_train=100, n_test=20, width=800, height=800, seed=seed, device="cuda")
+        ref.append(_replay(REF_SO, scene, 2000)[1])
+        ours.append(_replay(SHIM_REPLAY_SO, scene, 2000)[1])
+    delta = np.array(ours) - np.array(ref)
+    print(f"test PSNR after 2000 steps: drop-in {np.round(ours, 3).tolist()} reference {np.round(ref, 3).tolist()} "
+          f"mean delta {delta.mean():+.3f} dB")
+    assert min(ours) > 20.0
+    assert delta.mean() >= -0.2
