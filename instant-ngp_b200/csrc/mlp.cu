@@ -876,257 +876,6 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
     if (t < 32) umma::tmem_dealloc(tmem, kBwdTmemCols);
 }
 
-// ---------------------------------------------------------------------------------------------
-// Backward with two threads per row (256 threads): as mlp_backward_kernel, each epilogue split
-// into column halves between warps w and w + 4 (same TMEM lanes).  Same MMAs and rounding:
-// identical input and weight gradients.
-// ---------------------------------------------------------------------------------------------
-// Half a row's gradient (32 columns, chunks c0 .. c0 + 3 of an 8-chunk tile) masked by the
-// forward activation stored in the same chunks of `act` (ReLU derivative), written over `act`.
-__device__ __forceinline__ void relu_grad_half(unsigned char* act, uint32_t r, uint32_t c0, float* d) {
-#pragma unroll
-    for (uint32_t c = 0; c < 4; ++c) {
-        const uint4 hv   = load_chunk(act, r, c0 + c, 8);
-        const __half* hh = reinterpret_cast<const __half*>(&hv);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) d[c * 8 + j] = __half2float(hh[j]) > 0.0f ? d[c * 8 + j] : 0.0f;
-    }
-#pragma unroll
-    for (uint32_t c = 0; c < 4; ++c) store_chunk(act, r, c0 + c, 8, pack8(d + c * 8));
-}
-
-template <bool XROWS>
-__global__ void __launch_bounds__(kThreads2, 2) mlp_backward2_kernel(const __grid_constant__ MlpBackwardParams p) {
-    extern __shared__ __align__(1024) unsigned char smem[];
-    __shared__ uint64_t mbar;
-    __shared__ uint32_t tmem_slot;
-    const uint32_t t = threadIdx.x;
-    const uint32_t r = t & 127u;  // row of the tile = TMEM lane
-    const uint32_t h = t >> 7;    // half of the row's columns
-
-    load_weight_tile(smem + kSWdIn, p.params + kWdIn, 64, 32);
-    load_weight_tile(smem + kSWdOut, p.params + kWdOut, 16, 64);
-    load_weight_tile(smem + kSWrIn, p.params + kWrIn, 64, 32);
-    load_weight_tile(smem + kSWrH, p.params + kWrH, 64, 64);
-    load_weight_tile(smem + kSWrOut, p.params + kWrOut, 16, 64);
-    for (uint32_t i = t; i < 4096 / 16; i += kThreads2) reinterpret_cast<uint4*>(smem + kBGuard)[i] = make_uint4(0, 0, 0, 0);
-    if (t < 32) umma::tmem_alloc(&tmem_slot, kBwdTmemCols);
-    if (t == 0) umma::mbar_init(&mbar, 1);
-    stage_sync();
-    const uint32_t tmem    = tmem_slot;
-    const uint32_t s0      = umma::smem_addr(smem);
-    uint32_t phase         = 0;
-    bool ok                = true;
-    bool first             = true;
-    const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
-
-    MlpForwardParams fp{};  // the input-side fields, for load_half_row
-    fp.x = p.x, fp.x_stride = p.x_stride, fp.coords = p.coords, fp.coord_stride = p.coord_stride, fp.rows = p.rows;
-    HalfRowInputs<XROWS> cur, nxt;
-    uint2 dy_cur = make_uint2(0, 0), dy_nxt = make_uint2(0, 0);
-    auto load_dy = [&](uint32_t row) {
-        return (h == 0 && row < p.n) ? __ldg(reinterpret_cast<const uint2*>(p.dy + static_cast<uint64_t>(row) * 16u)) : make_uint2(0, 0);
-    };
-    unsigned char* const xbuf0 = smem + kBX, *const xbuf1 = smem + kBX2;
-    auto issue_half = [&](unsigned char* tile, uint32_t col, bool valid) {
-        const __half* src = p.x + static_cast<uint64_t>(valid ? col : 0u) * 32u;
-#pragma unroll
-        for (uint32_t c = 2 * h; c < 2 * h + 2; ++c) cp_async16(tile + tile_off(r, c, 4), src + c * 8u, valid ? 16u : 0u);
-        cp_async_commit();
-    };
-    if (blockIdx.x < n_tiles) {
-        load_half_row<true, XROWS>(fp, p.n, blockIdx.x * kRows + r, h, cur);
-        if constexpr (XROWS) issue_half(xbuf0, cur.col, blockIdx.x * kRows + r < p.n);
-        dy_cur = load_dy(blockIdx.x * kRows + r);
-    }
-    uint32_t it = 0;
-    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-        const uint32_t row = tile * kRows + r;
-        const bool valid   = row < p.n;
-        const uint32_t bx  = XROWS && (it & 1u) ? kBX2 : kBX;
-        if (tile + gridDim.x < n_tiles) {
-            load_half_row<true, XROWS>(fp, p.n, (tile + gridDim.x) * kRows + r, h, nxt);
-            if constexpr (XROWS) issue_half((it & 1u) ? xbuf0 : xbuf1, nxt.col, (tile + gridDim.x) * kRows + r < p.n);
-            dy_nxt = load_dy((tile + gridDim.x) * kRows + r);
-        } else if constexpr (XROWS) {
-            cp_async_commit();
-        }
-        // ---------------- forward recompute ----------------
-        if constexpr (XROWS) {
-            cp_async_wait<1>();
-        } else {
-#pragma unroll
-            for (uint32_t c = 0; c < 2; ++c) {
-                const unsigned short* q = cur.x + c * 8;
-                store_chunk(smem + kBX, r, 2 * h + c, 4,
-                            make_uint4(q[0] | (static_cast<uint32_t>(q[1]) << 16), q[2] | (static_cast<uint32_t>(q[3]) << 16),
-                                       q[4] | (static_cast<uint32_t>(q[5]) << 16), q[6] | (static_cast<uint32_t>(q[7]) << 16)));
-            }
-        }
-        // output gradient (half 0): rgb channels 0-2 (extract_rgb_gradients, ngp.train.cu:1244-1253)
-        // and the density gradient (channel 3), added to the density-output gradient below
-        float g[4];
-        {
-            const uint2 a    = dy_cur;
-            const __half2* q = reinterpret_cast<const __half2*>(&a);
-            const float2 g01 = __half22float2(q[0]), g23 = __half22float2(q[1]);
-            g[0] = g01.x, g[1] = g01.y, g[2] = g23.x, g[3] = g23.y;
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 64, 32, s0 + bx, false, 4, s0 + kSWdIn, false, 4, false);
-            umma::commit(&mbar);
-        }
-        ok = stage_wait(&mbar, phase);
-        {
-            float v[32];
-            read_acc_lane<4>(tmem, r, kColD0 + 32u * h, v);
-            store_half_row_relu(smem + kBHd, r, 4u * h, v);
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 16, 64, s0 + kBHd, false, 8, s0 + kSWdOut, false, 8, false);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float dens[8], sh[16], s8[8];
-            read_acc_lane<1>(tmem, r, kColD0 + 8u * h, dens);
-            sh16(cur.dir[0], cur.dir[1], cur.dir[2], sh);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) s8[k] = h ? sh[8 + k] : sh[k];
-            store_chunk(smem + kBRi, r, h, 4, pack8(dens));
-            store_chunk(smem + kBRi, r, 2u + h, 4, pack8(s8));
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 64, 32, s0 + kBRi, false, 4, s0 + kSWrIn, false, 4, false);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float v[32];
-            read_acc_lane<4>(tmem, r, kColD0 + 32u * h, v);
-            store_half_row_relu(smem + kBH1, r, 4u * h, v);
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 64, 64, s0 + kBH1, false, 8, s0 + kSWrH, false, 8, false);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float v[32];
-            read_acc_lane<4>(tmem, r, kColD0 + 32u * h, v);
-            store_half_row_relu(smem + kBH2, r, 4u * h, v);
-            // rgb output gradient tile (K = 16): channels 0-2 (half 0's chunk), zeros elsewhere
-            float gy[8] = {h == 0 ? g[0] : 0.0f, h == 0 ? g[1] : 0.0f, h == 0 ? g[2] : 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-            store_chunk(smem + kBDy, r, h, 2, pack8(gy));
-        }
-        // ---------------- backward ----------------
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 64, 16, s0 + kBDy, false, 2, s0 + kSWrOut, true, 8, false);
-            gemm(tmem + kColWrOut, 16, 128, s0 + kBH2, true, 8, s0 + kBDy, true, 2, !first);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float d[32];
-            read_acc_lane<4>(tmem, r, kColD0 + 32u * h, d);
-            relu_grad_half(smem + kBH2, r, 4u * h, d);  // dH2 replaces H2
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 64, 64, s0 + kBH2, false, 8, s0 + kSWrH, true, 8, false);
-            gemm(tmem + kColWrH, 64, 128, s0 + kBH2, true, 8, s0 + kBH1, true, 8, !first);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float d[32];
-            read_acc_lane<4>(tmem, r, kColD0 + 32u * h, d);
-            relu_grad_half(smem + kBH1, r, 4u * h, d);  // dH1 replaces H1
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 32, 64, s0 + kBH1, false, 8, s0 + kSWrIn, true, 4, false);
-            gemm(tmem + kColWrIn, 32, 128, s0 + kBH1, true, 8, s0 + kBRi, true, 4, !first);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            // the density-output gradient: columns 0-15 of dRi (half h: 8h .. 8h + 7)
-            float d[8];
-            read_acc_lane<1>(tmem, r, kColD0 + 8u * h, d);
-            if (h == 0) d[0] += g[3];  // add_density_gradient_kernel (ngp.train.cu:1255-1259)
-            store_chunk(smem + kBDy, r, h, 2, pack8(d));  // dDensityOut (16) replaces dY
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 64, 16, s0 + kBDy, false, 2, s0 + kSWdOut, true, 8, false);
-            gemm(tmem + kColWdOut, 16, 128, s0 + kBHd, true, 8, s0 + kBDy, true, 2, !first);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float d[32];
-            read_acc_lane<4>(tmem, r, kColD0 + 32u * h, d);
-            relu_grad_half(smem + kBHd, r, 4u * h, d);  // dHd replaces Hd
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(tmem + kColD0, 32, 64, s0 + kBHd, false, 8, s0 + kSWdIn, true, 4, false);
-            gemm(tmem + kColWdIn, 32, 128, s0 + kBHd, true, 8, s0 + bx, true, 4, !first);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float d[16];
-            read_acc_lane<2>(tmem, r, kColD0 + 16u * h, d);
-            if (valid && p.dx != nullptr)
-#pragma unroll
-                for (uint32_t k = 0; k < 16; ++k) p.dx[static_cast<uint64_t>(16u * h + k) * p.dx_stride + row] = __float2half_rn(d[k]);
-        }
-        first  = false;
-        cur    = nxt;
-        dy_cur = dy_nxt;
-        umma::fence_before_sync();
-        if (!__syncthreads_and(ok)) break;
-        umma::fence_after_sync();
-    }
-    if constexpr (XROWS) cp_async_wait<0>();
-    // ---- this CTA's weight-gradient partial (rows 0-63 of the M = 128 accumulators) ----
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
-    float* part = p.dw_partial + static_cast<uint64_t>(blockIdx.x) * kMlpParams;
-    if (t < 64) {
-        if (first) {
-            for (uint32_t i = 0; i < 64; ++i) {
-                if (i < 32) part[kWdIn + t * 32 + i] = 0.0f, part[kWrIn + t * 32 + i] = 0.0f;
-                part[kWrH + t * 64 + i] = 0.0f;
-                if (i < 16) part[kWrOut + i * 64 + t] = 0.0f, part[kWdOut + i * 64 + t] = 0.0f;
-            }
-        } else {
-            float v[64];
-            read_acc<16>(tmem, kColWrOut, v);
-            for (uint32_t o = 0; o < 16; ++o) part[kWrOut + o * 64 + t] = v[o];
-            read_acc<64>(tmem, kColWrH, v);
-            for (uint32_t i = 0; i < 64; ++i) part[kWrH + t * 64 + i] = v[i];
-            read_acc<32>(tmem, kColWrIn, v);
-            for (uint32_t i = 0; i < 32; ++i) part[kWrIn + t * 32 + i] = v[i];
-            read_acc<16>(tmem, kColWdOut, v);
-            for (uint32_t o = 0; o < 16; ++o) part[kWdOut + o * 64 + t] = v[o];
-            read_acc<32>(tmem, kColWdIn, v);
-            for (uint32_t i = 0; i < 32; ++i) part[kWdIn + t * 32 + i] = v[i];
-        }
-    }
-    umma::fence_before_sync();
-    __syncthreads();
-    if (t < 32) umma::tmem_dealloc(tmem, kBwdTmemCols);
-}
-
 // dW[j] = scale * sum over CTAs of partial[cta][j] in a fixed order (deterministic): the CTAs are
 // split into kReduceGroups interleaved groups (group g: CTAs g, g + G, ...) summed in CTA order by
 // their own threads, then the group sums are added in group order.
@@ -1204,8 +953,6 @@ int ensure_attrs() {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward2_kernel<kModeFull, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward2_kernel<kModeDensity, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward2_kernel<kModeFull, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
@@ -1314,21 +1061,15 @@ int mlp_backward_launch(uint32_t n, const uint32_t* rows, const uint16_t* params
     NGP_TRY(ensure_attrs());
     const uint32_t n_tiles = (n + kRows - 1) / kRows;
     const bool xrows       = rows_layout(x_stride);
-    const bool two         = forward_threads_per_row() == 2;
-    const void* kern       = two ? (xrows ? reinterpret_cast<const void*>(mlp_backward2_kernel<true>) : reinterpret_cast<const void*>(mlp_backward2_kernel<false>))
-                                 : (xrows ? reinterpret_cast<const void*>(mlp_backward_kernel<true>) : reinterpret_cast<const void*>(mlp_backward_kernel<false>));
-    uint32_t grid          = static_cast<uint32_t>(mlp_grid(kBwdSmem, kern, n_tiles == 0 ? 1 : n_tiles, kBwdTmemCols, two ? kThreads2 : kThreads));
+    const void* kern       = xrows ? reinterpret_cast<const void*>(mlp_backward_kernel<true>) : reinterpret_cast<const void*>(mlp_backward_kernel<false>);
+    uint32_t grid          = static_cast<uint32_t>(mlp_grid(kBwdSmem, kern, n_tiles == 0 ? 1 : n_tiles, kBwdTmemCols));
     if (static_cast<size_t>(grid) * kMlpParams > scratch_floats) {
         grid = static_cast<uint32_t>(scratch_floats / kMlpParams);
         if (grid == 0) return fail(NGP_ERR_INVALID, "mlp backward: scratch too small (need ngp_mlp_backward_scratch_floats())");
     }
     MlpBackwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, coords, coord_stride,
                         reinterpret_cast<const __half*>(dy), reinterpret_cast<__half*>(dx), dx_stride, scratch, rows};
-    if (two && xrows)
-        mlp_backward2_kernel<true><<<grid, kThreads2, kBwdSmem, as_stream(stream)>>>(p);
-    else if (two)
-        mlp_backward2_kernel<false><<<grid, kThreads2, kBwdSmem, as_stream(stream)>>>(p);
-    else if (xrows)
+    if (xrows)
         mlp_backward_kernel<true><<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
     else
         mlp_backward_kernel<false><<<grid, kThreads, kBwdSmem, as_stream(stream)>>>(p);
