@@ -764,6 +764,8 @@ def bench_mlp_ours(args, rank, world, local):
     n = BATCH
     x_h, c_h, dy_h = workloads.mlp_inputs(n, seed=31 + rank)
     params = torch.from_numpy(workloads.xavier_mlp_params(1).view(np.int16)).cuda()
+    # row-major encoded inputs [n][32] (NGP_ROWS), the layout the trainer keeps its encodings in
+    x_h = np.ascontiguousarray(x_h.T)
     x, coords, dy = torch.from_numpy(x_h).cuda(), torch.from_numpy(c_h).cuda(), torch.from_numpy(dy_h).cuda()
     out = torch.empty((n, 16), dtype=torch.float16, device="cuda")
     dx = torch.empty((32, n), dtype=torch.float16, device="cuda")
@@ -776,10 +778,10 @@ def bench_mlp_ours(args, rank, world, local):
         flush_buf.fill_(1.0)
 
     def fwd():
-        ngp.mlp_forward(params, x, coords, out, stream=stream)
+        ngp.mlp_forward(params, x, coords, out, x_stride=ngp.ROWS, stream=stream)
 
     def bwd():
-        ngp.mlp_backward(params, x, coords, dy, dx=dx, dw_f32=dw, stream=stream)
+        ngp.mlp_backward(params, x, coords, dy, dx=dx, dw_f32=dw, x_stride=ngp.ROWS, stream=stream)
 
     def step():
         fwd()
@@ -815,7 +817,7 @@ def bench_mlp_ours(args, rank, world, local):
         "vs_baseline": None, "dtype": "fp16 weights/activations, fp32 accumulation (tcgen05 kind::f16)",
         "data": "synthetic (U(-1,1) fp16 inputs, directions uniform on S^2, N(0,1) dL/dy, Xavier weights; seeded)",
         "config": {"workload": "config1 fused MLP fwd+bwd", "rows_per_gpu": n, "density": "32-64-16", "colour": "32-64-64-16",
-                   "input_layout": "feature-major [32][n] fp16 (the reference's layout, as the trainer keeps it)",
+                   "input_layout": "row-major [n][32] fp16 (NGP_ROWS, the trainer's layout)",
                    "parallelism": f"dp{world} (no collective)", "l2": "flushed (256 MB write) before every timed step"},
         "kernels_ms": {"mlp_forward": round(fwd_ms, 5), "mlp_backward": round(bwd_ms, 5)},
         "roofline": {"kernel": "mlp_forward_kernel + mlp_backward_kernel", "bound": "tensor", "achieved": round(tflops, 2),

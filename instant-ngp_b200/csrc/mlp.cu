@@ -19,8 +19,6 @@
 // weight gradients in TMEM across every tile the CTA processes.  Each CTA writes its weight-
 // gradient partial once; a second small kernel sums the partials in a fixed order
 // (deterministic).  Weight-gradient GEMMs use M = 128 with the 64 real rows in lanes 0-63.
-#include <cstdlib>
-
 #include "common.cuh"
 #include "umma.cuh"
 
@@ -238,7 +236,7 @@ template <int MODE, bool XROWS>
 __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* sw    = smem;                      // weights
-    unsigned char* const sxb0 = smem + kSWeights, *const sxb1 = smem + kSWeights + 8192;  // 128 x 32 input tiles (X, then rgb input)
+    unsigned char* sxb[2] = {smem + kSWeights, smem + kSWeights + 8192};  // 128 x 32 input tiles (X, then rgb input)
     unsigned char* shd   = smem + kSWeights + 16384;  // 128 x 64 hidden tile
     __shared__ uint64_t mbar;
     __shared__ uint32_t tmem_slot;
@@ -269,17 +267,17 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
     RowInputs<MODE == kModeFull, XROWS> cur, nxt;
     if (blockIdx.x < n_tiles) {
         load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, blockIdx.x * kRows + t, cur, p.rows);
-        if constexpr (XROWS) issue_row_copy(sxb0, t, p.x, cur.col, blockIdx.x * kRows + t < n);
+        if constexpr (XROWS) issue_row_copy(sxb[0], t, p.x, cur.col, blockIdx.x * kRows + t < n);
     }
     uint32_t it = 0;
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row   = tile * kRows + t;
         const bool valid     = row < n;
-        unsigned char* sx    = XROWS && (it & 1u) ? sxb1 : sxb0;
+        unsigned char* sx    = XROWS ? sxb[it & 1u] : sxb[0];
         const uint32_t a_sx  = umma::smem_addr(sx);
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
-            if constexpr (XROWS) issue_row_copy((it & 1u) ? sxb0 : sxb1, t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
+            if constexpr (XROWS) issue_row_copy(sxb[(it + 1u) & 1u], t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
         } else if constexpr (XROWS) {
             cp_async_commit();  // an empty group keeps the wait count below uniform
         }
@@ -379,226 +377,6 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------------------------
-// Forward with two threads per row (256 threads, eight warps per tile).  Warps w and w + 4 share
-// TMEM lanes 32 (w % 4) .. + 31 and split every row's columns in halves, so each thread's share of
-// an epilogue (TMEM reads, activation, conversion, shared-memory stores) is half as long and
-// twice as many warps hide the latencies of the tile's dependent chain.  Same MMAs, operand tiles
-// and rounding as mlp_forward_kernel: identical outputs.
-// ---------------------------------------------------------------------------------------------
-constexpr uint32_t kThreads2 = 256;
-
-// Read 8 * NB fp32 columns [col, col + 8 NB) of TMEM lane `lane` (this warp's lane group).
-template <uint32_t NB>
-__device__ __forceinline__ void read_acc_lane(uint32_t tmem, uint32_t lane, uint32_t col, float* v) {
-    const uint32_t base = ((lane & ~31u) << 16) + col;
-    if constexpr (NB % 2 == 0) {
-        uint32_t r[NB / 2][16];
-#pragma unroll
-        for (uint32_t c = 0; c < NB / 2; ++c) umma::tmem_ld16_async(tmem + base + c * 16, r[c]);
-        umma::tmem_wait_ld();
-#pragma unroll
-        for (uint32_t c = 0; c < NB / 2; ++c)
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[c * 16 + j] = __uint_as_float(r[c][j]);
-    } else {
-        static_assert(NB == 1, "8 or a multiple of 16 columns");
-        uint32_t r[8];
-        umma::tmem_ld8_async(tmem + base, r);
-        umma::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[j]);
-    }
-}
-
-// Half a row: 32 fp32 values -> ReLU -> fp16 -> chunks [c0, c0 + 4) of an 8-chunk (64-wide) tile.
-__device__ __forceinline__ void store_half_row_relu(unsigned char* tile, uint32_t r, uint32_t c0, const float* v) {
-#pragma unroll
-    for (uint32_t c = 0; c < 4; ++c) {
-        const float* a = v + c * 8;
-        store_chunk(tile, r, c0 + c, 8, make_uint4(pack2_relu(a[0], a[1]), pack2_relu(a[2], a[3]), pack2_relu(a[4], a[5]), pack2_relu(a[6], a[7])));
-    }
-}
-
-__device__ __forceinline__ uint4 pack8(const float* a) {
-    return make_uint4(pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7]));
-}
-
-// This thread's half of a row's inputs: 16 fp16 features (feature-major sources), the view
-// direction and the sample the row reads and writes.
-template <bool XROWS>
-struct HalfRowInputs {
-    unsigned short x[XROWS ? 1 : 16];
-    float dir[3];
-    uint32_t col;
-};
-
-template <bool DIR, bool XROWS>
-__device__ __forceinline__ void load_half_row(const MlpForwardParams& p, uint32_t n, uint32_t row, uint32_t h, HalfRowInputs<XROWS>& in) {
-    const bool valid = row < n;
-    in.col           = valid ? (p.rows != nullptr ? __ldg(p.rows + row) : row) : 0u;
-    if constexpr (!XROWS) {
-        const unsigned short* xs = reinterpret_cast<const unsigned short*>(p.x);
-#pragma unroll
-        for (uint32_t k = 0; k < 16; ++k)
-            in.x[k] = valid ? __ldg(xs + static_cast<uint64_t>(16u * h + k) * p.x_stride + in.col) : static_cast<unsigned short>(0);
-    }
-    if constexpr (DIR) {
-        const float* c = p.coords + static_cast<uint64_t>(in.col) * p.coord_stride;
-        in.dir[0] = __ldg(c + 4), in.dir[1] = __ldg(c + 5), in.dir[2] = __ldg(c + 6);
-    }
-}
-
-template <int MODE, bool XROWS>
-__global__ void __launch_bounds__(kThreads2, 4) mlp_forward2_kernel(const __grid_constant__ MlpForwardParams p) {
-    extern __shared__ __align__(1024) unsigned char smem[];
-    unsigned char* sw     = smem;
-    unsigned char* const sxb0 = smem + kSWeights;
-    unsigned char* const sxb1 = smem + kSWeights + 8192;
-    unsigned char* shd    = smem + kSWeights + 16384;
-    __shared__ uint64_t mbar;
-    __shared__ uint32_t tmem_slot;
-
-    const uint32_t t = threadIdx.x;
-    const uint32_t r = t & 127u;  // row of the tile = TMEM lane
-    const uint32_t h = t >> 7;    // half of the row's columns
-    load_weight_tile(sw + kSWdIn, p.params + kWdIn, 64, 32);
-    load_weight_tile(sw + kSWdOut, p.params + kWdOut, 16, 64);
-    if (MODE == kModeFull) {
-        load_weight_tile(sw + kSWrIn, p.params + kWrIn, 64, 32);
-        load_weight_tile(sw + kSWrH, p.params + kWrH, 64, 64);
-        load_weight_tile(sw + kSWrOut, p.params + kWrOut, 16, 64);
-    }
-    if (t < 32) umma::tmem_alloc(&tmem_slot, kFwdTmemCols);
-    if (t == 0) umma::mbar_init(&mbar, 1);
-    stage_sync();
-    const uint32_t tmem = tmem_slot;
-    const uint32_t d0 = tmem, d1 = tmem + 64;
-    const uint32_t a_shd = umma::smem_addr(shd), a_sw = umma::smem_addr(sw);
-    uint32_t phase         = 0;
-    bool ok                = true;
-    const uint32_t n       = p.n_dev != nullptr ? min(*p.n_dev, p.n) : p.n;
-    const uint32_t n_tiles = (n + kRows - 1) / kRows;
-    constexpr bool kDir    = MODE == kModeFull;
-
-    auto issue_half = [&](unsigned char* tile, uint32_t col, bool valid) {
-        const __half* src = p.x + static_cast<uint64_t>(valid ? col : 0u) * 32u;
-#pragma unroll
-        for (uint32_t c = 2 * h; c < 2 * h + 2; ++c) cp_async16(tile + tile_off(r, c, 4), src + c * 8u, valid ? 16u : 0u);
-        cp_async_commit();
-    };
-
-    HalfRowInputs<XROWS> cur, nxt;
-    if (blockIdx.x < n_tiles) {
-        load_half_row<kDir, XROWS>(p, n, blockIdx.x * kRows + r, h, cur);
-        if constexpr (XROWS) issue_half(sxb0, cur.col, blockIdx.x * kRows + r < n);
-    }
-    uint32_t it = 0;
-    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-        const uint32_t row  = tile * kRows + r;
-        const bool valid    = row < n;
-        unsigned char* sx   = XROWS && (it & 1u) ? sxb1 : sxb0;
-        const uint32_t a_sx = umma::smem_addr(sx);
-        if (tile + gridDim.x < n_tiles) {
-            load_half_row<kDir, XROWS>(p, n, (tile + gridDim.x) * kRows + r, h, nxt);
-            if constexpr (XROWS) issue_half((it & 1u) ? sxb0 : sxb1, nxt.col, (tile + gridDim.x) * kRows + r < n);
-        } else if constexpr (XROWS) {
-            cp_async_commit();
-        }
-        if constexpr (XROWS) {
-            cp_async_wait<1>();
-        } else {
-#pragma unroll
-            for (uint32_t c = 0; c < 2; ++c) {
-                const unsigned short* q = cur.x + c * 8;
-                store_chunk(sx, r, 2 * h + c, 4,
-                            make_uint4(q[0] | (static_cast<uint32_t>(q[1]) << 16), q[2] | (static_cast<uint32_t>(q[3]) << 16),
-                                       q[4] | (static_cast<uint32_t>(q[5]) << 16), q[6] | (static_cast<uint32_t>(q[7]) << 16)));
-            }
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
-            umma::commit(&mbar);
-        }
-        ok = stage_wait(&mbar, phase);
-        {
-            float v[32];
-            read_acc_lane<4>(tmem, r, 32u * h, v);
-            store_half_row_relu(shd, r, 4u * h, v);
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(d1, 16, 64, a_shd, false, 8, a_sw + kSWdOut, false, 8, false);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        float dens[8];  // density-network outputs 8h .. 8h + 7
-        read_acc_lane<1>(tmem, r, 64u + 8u * h, dens);
-        if (MODE == kModeDensity) {
-            if (valid && h == 0) p.out[cur.col] = __float2half_rn(dens[0]);
-            cur = nxt;
-            umma::fence_before_sync();
-            if (!__syncthreads_and(ok)) break;
-            umma::fence_after_sync();
-            continue;
-        }
-        // ---- colour network input: [16 density outputs | 16 SH]; this half: chunks h, 2 + h ----
-        {
-            float sh[16];
-            sh16(cur.dir[0], cur.dir[1], cur.dir[2], sh);
-            store_chunk(sx, r, h, 4, pack8(dens));
-            float s8[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) s8[k] = h ? sh[8 + k] : sh[k];  // (no dynamic register indexing)
-            store_chunk(sx, r, 2u + h, 4, pack8(s8));
-            if (p.density_rgb_in != nullptr && valid)
-#pragma unroll
-                for (int k = 0; k < 8; ++k) p.density_rgb_in[static_cast<uint64_t>(8u * h + k) * p.x_stride + cur.col] = __float2half_rn(dens[k]);
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWrIn, false, 4, false);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float v[32];
-            read_acc_lane<4>(tmem, r, 32u * h, v);
-            store_half_row_relu(shd, r, 4u * h, v);
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(d0, 64, 64, a_shd, false, 8, a_sw + kSWrH, false, 8, false);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        {
-            float v[32];
-            read_acc_lane<4>(tmem, r, 32u * h, v);
-            store_half_row_relu(shd, r, 4u * h, v);  // the layer-2 MMA that read shd has completed
-        }
-        stage_sync();
-        if (t == 0) {
-            gemm(d1, 16, 64, a_shd, false, 8, a_sw + kSWrOut, false, 8, false);
-            umma::commit(&mbar);
-        }
-        ok = ok && stage_wait(&mbar, phase);
-        float o[8];
-        read_acc_lane<1>(tmem, r, 64u + 8u * h, o);
-        if (h == 0) o[3] = dens[0];
-        if (valid) reinterpret_cast<uint4*>(p.out + static_cast<uint64_t>(cur.col) * 16u)[h] = pack8(o);
-        cur = nxt;
-        umma::fence_before_sync();
-        if (!__syncthreads_and(ok)) break;
-        umma::fence_after_sync();
-    }
-    if constexpr (XROWS) cp_async_wait<0>();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (t < 32) umma::tmem_dealloc(tmem, kFwdTmemCols);
-}
-
-// ---------------------------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------------------------
 struct MlpBackwardParams {
@@ -654,10 +432,10 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
     auto load_dy = [&](uint32_t r) {
         return r < p.n ? __ldg(reinterpret_cast<const uint2*>(p.dy + static_cast<uint64_t>(r) * 16u)) : make_uint2(0, 0);
     };
-    unsigned char* const xbuf0 = smem + kBX, *const xbuf1 = smem + kBX2;
+    unsigned char* xbuf[2] = {smem + kBX, smem + kBX2};
     if (blockIdx.x < n_tiles) {
         load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur, p.rows);
-        if constexpr (XROWS) issue_row_copy(xbuf0, t, p.x, cur.col, blockIdx.x * kRows + t < p.n);
+        if constexpr (XROWS) issue_row_copy(xbuf[0], t, p.x, cur.col, blockIdx.x * kRows + t < p.n);
         dy_cur = load_dy(blockIdx.x * kRows + t);
     }
     uint32_t it = 0;
@@ -667,7 +445,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         const uint32_t bx  = XROWS && (it & 1u) ? kBX2 : kBX;  // this tile's input tile
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
-            if constexpr (XROWS) issue_row_copy((it & 1u) ? xbuf0 : xbuf1, t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < p.n);
+            if constexpr (XROWS) issue_row_copy(xbuf[(it + 1u) & 1u], t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < p.n);
             dy_nxt = load_dy((tile + gridDim.x) * kRows + t);
         } else if constexpr (XROWS) {
             cp_async_commit();  // an empty group keeps the wait count below uniform
@@ -911,7 +689,7 @@ __global__ void sh_encode_kernel(uint32_t n, const float* __restrict__ coords, u
     for (uint32_t k = 0; k < 16; ++k) out[static_cast<uint64_t>(k) * out_stride + i] = __float2half_rn(sh[k]);
 }
 
-int mlp_grid(int smem_bytes, const void* kernel, uint32_t n_tiles, uint32_t tmem_cols, uint32_t threads = kThreads) {
+int mlp_grid(int smem_bytes, const void* kernel, uint32_t n_tiles, uint32_t tmem_cols) {
     // CTAs per SM from shared memory (1 KB per CTA is reserved by the hardware), registers and
     // TMEM columns (512 per SM).
     static int smem_per_sm = [] {
@@ -925,7 +703,7 @@ int mlp_grid(int smem_bytes, const void* kernel, uint32_t n_tiles, uint32_t tmem
     const int per_cta_smem = smem_bytes + static_cast<int>(attr.sharedSizeBytes) + 1024;
     int per_sm            = smem_per_sm / per_cta_smem;
     const int regs        = attr.numRegs > 0 ? attr.numRegs : 64;
-    const int by_regs     = 65536 / (regs * static_cast<int>(threads));
+    const int by_regs     = 65536 / (regs * static_cast<int>(kThreads));
     per_sm                = per_sm < by_regs ? per_sm : by_regs;
     if (per_sm < 1) per_sm = 1;
     const int by_tmem = static_cast<int>(512u / tmem_cols);
@@ -953,10 +731,6 @@ int ensure_attrs() {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward2_kernel<kModeFull, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward2_kernel<kModeDensity, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward2_kernel<kModeFull, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward2_kernel<kModeDensity, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
         return static_cast<int>(e);
     }();
@@ -966,29 +740,9 @@ int ensure_attrs() {
 }  // namespace
 
 namespace {
-// Threads per row of the forward: 2 (mlp_forward2_kernel, default) or 1 (mlp_forward_kernel),
-// from $NGP_MLP_TPR at the first launch.
-int forward_threads_per_row() {
-    static int tpr = [] {
-        const char* v = std::getenv("NGP_MLP_TPR");
-        return (v != nullptr && std::atoi(v) == 1) ? 1 : 2;
-    }();
-    return tpr;
-}
-
 template <int MODE>
 int launch_forward(const MlpForwardParams& p, uint32_t n_rows, cudaStream_t stream, const char* what) {
     const uint32_t n_tiles = (n_rows + kRows - 1) / kRows;
-    if (forward_threads_per_row() == 2) {
-        if (rows_layout(p.x_stride)) {
-            const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward2_kernel<MODE, true>), n_tiles, kFwdTmemCols, kThreads2);
-            mlp_forward2_kernel<MODE, true><<<grid, kThreads2, kFwdSmem, stream>>>(p);
-        } else {
-            const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward2_kernel<MODE, false>), n_tiles, kFwdTmemCols, kThreads2);
-            mlp_forward2_kernel<MODE, false><<<grid, kThreads2, kFwdSmem, stream>>>(p);
-        }
-        return check_launch(what);
-    }
     if (rows_layout(p.x_stride)) {
         const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<MODE, true>), n_tiles, kFwdTmemCols);
         mlp_forward_kernel<MODE, true><<<grid, kThreads, kFwdSmem, stream>>>(p);
