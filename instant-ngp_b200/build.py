@@ -86,7 +86,7 @@ def build_probes(force: bool = False) -> Path:
     product library; only bench.py loads it."""
     if force or not PROBES_LIB.exists() or PROBES_SRC.stat().st_mtime > PROBES_LIB.stat().st_mtime:
         cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared",
-               "-o", str(PROBES_LIB), str(PROBES_SRC), "-lcudart"]
+               "-I", str(CSRC), "-o", str(PROBES_LIB), str(PROBES_SRC), "-lcudart"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"nvcc failed for {PROBES_SRC.name}:\n{res.stdout}\n{res.stderr}")

@@ -19,6 +19,8 @@
 // weight gradients in TMEM across every tile the CTA processes.  Each CTA writes its weight-
 // gradient partial once; a second small kernel sums the partials in a fixed order
 // (deterministic).  Weight-gradient GEMMs use M = 128 with the 64 real rows in lanes 0-63.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "umma.cuh"
 
@@ -708,6 +710,13 @@ int mlp_grid(int smem_bytes, const void* kernel, uint32_t n_tiles, uint32_t tmem
     if (per_sm < 1) per_sm = 1;
     const int by_tmem = static_cast<int>(512u / tmem_cols);
     per_sm            = per_sm < by_tmem ? per_sm : by_tmem;
+    // $NGP_MLP_CTAS_PER_SM caps the resident CTAs per SM (measurement of how the kernels scale
+    // with the number of tiles in flight)
+    static int cap = [] {
+        const char* v = std::getenv("NGP_MLP_CTAS_PER_SM");
+        return v != nullptr ? std::atoi(v) : 0;
+    }();
+    if (cap > 0 && per_sm > cap) per_sm = cap;
     const uint32_t g  = static_cast<uint32_t>(per_sm * sm_count());
     return static_cast<int>(n_tiles < g ? n_tiles : g);
 }
