@@ -12,7 +12,7 @@
 // (fmaf in corner order 0..7) instead of fp16 __hfma, rounded once to fp16.
 // Backward follows encode_grid_backward_kernel (ngp.train.cu:923-960) but scatters into an
 // fp32 gradient table with vector atomics (red.global.add.v2/v4.f32) instead of fp16 atomics.
-#include "common.cuh"
+#include "encoding.cuh"
 
 // Tuning knob (compile-time; the default is the measured best on B200): levels up to this
 // resolution pre-sum the lanes of a warp that share a cell before the backward's atomics.
@@ -31,52 +31,6 @@ constexpr uint32_t kEncodeThreads = 256u;
 __device__ __forceinline__ void cta_level_chunk(uint32_t n_levels, uint32_t& level, uint32_t& chunk) {
     level = blockIdx.x % n_levels;
     chunk = blockIdx.x / n_levels;
-}
-
-template <uint32_t F>
-struct FeatureVec;
-template <>
-struct FeatureVec<1> {
-    using type = __half;
-};
-template <>
-struct FeatureVec<2> {
-    using type = uint32_t;
-};
-template <>
-struct FeatureVec<4> {
-    using type = uint2;
-};
-template <>
-struct FeatureVec<8> {
-    using type = uint4;
-};
-template <>
-struct FeatureVec<16> {
-    using type = uint4;  // unused: pairs are formed for F <= 4 only
-};
-
-template <uint32_t F>
-__device__ __forceinline__ void unpack(const typename FeatureVec<F>::type& v, float (&out)[F]) {
-    if constexpr (F == 1) {
-        out[0] = __half2float(v);
-    } else {
-        const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-        for (uint32_t k = 0; k < F / 2; ++k) {
-            const float2 f = __half22float2(h[k]);
-            out[2 * k]     = f.x;
-            out[2 * k + 1] = f.y;
-        }
-    }
-}
-
-// pos = fmaf(scale, x, 0.5); cell = floor(pos); frac = pos - cell (ngp.train.cu:188-193).
-__device__ __forceinline__ void position_fraction(float x, float scale, float& frac, uint32_t& cell) {
-    const float pos     = __fmaf_rn(scale, x, 0.5f);
-    const float floored = floorf(pos);
-    cell                = static_cast<uint32_t>(static_cast<int>(floored));
-    frac                = __fsub_rn(pos, floored);
 }
 
 // Store N consecutive halves (N * 2 bytes, aligned to that size up to 16) with vector stores.
@@ -122,37 +76,13 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(c
         float frac[LPI][3];
         Vec v[LPI][8];
 #pragma unroll
-        for (uint32_t j = 0; j < LPI; ++j) {
-            const uint32_t level = min(l0 + j, grid.n_levels - 1u);
-            const uint32_t off = grid.offsets[level], size = grid.offsets[level + 1] - off, res = grid.resolution[level];
-            const float scale = grid.scale[level];
-            uint32_t cell[3];
-#pragma unroll
-            for (uint32_t d = 0; d < 3; ++d) position_fraction(x[d], scale, frac[j][d], cell[d]);
-            const Vec* lvl = tab + off;
-            uint32_t idx[8];
-            corner_indices((grid.dense_mask >> level) & 1u, size, res, cell[0], cell[1], cell[2], idx);
-#pragma unroll
-            for (uint32_t c = 0; c < 8; ++c) v[j][c] = __ldg(lvl + idx[c]);
-        }
+        for (uint32_t j = 0; j < LPI; ++j) gather_level<F>(grid, tab, min(l0 + j, grid.n_levels - 1u), x, frac[j], v[j]);
 #pragma unroll
         for (uint32_t j = 0; j < LPI; ++j) {
             const uint32_t level = l0 + j;
             if (level >= grid.n_levels) break;
             float acc[F];
-#pragma unroll
-            for (uint32_t f = 0; f < F; ++f) acc[f] = 0.0f;
-#pragma unroll
-            for (uint32_t corner = 0; corner < 8; ++corner) {
-                const float wx = (corner & 1u) ? frac[j][0] : __fsub_rn(1.0f, frac[j][0]);
-                const float wy = (corner & 2u) ? frac[j][1] : __fsub_rn(1.0f, frac[j][1]);
-                const float wz = (corner & 4u) ? frac[j][2] : __fsub_rn(1.0f, frac[j][2]);
-                const float w  = __fmul_rn(__fmul_rn(wx, wy), wz);
-                float val[F];
-                unpack<F>(v[j][corner], val);
-#pragma unroll
-                for (uint32_t f = 0; f < F; ++f) acc[f] = __fmaf_rn(w, val[f], acc[f]);
-            }
+            interp_level<F>(frac[j], v[j], acc);
             if constexpr (ROWS) {
                 // this level's F features into the pair's vector, written once per level pair
 #pragma unroll
