@@ -213,14 +213,7 @@ NGP_API int ngp_density_grid_samples_cell_order(uint32_t n_uniform, uint32_t n_n
 /* scratch[indices[i]] = max(scratch[indices[i]], exp(density[i]) * sqrt(3)/1024).
  * Replaces splat_density_grid_samples_kernel (ngp.train.cu:426-432). */
 NGP_API int ngp_density_grid_splat(uint32_t n, const uint32_t* indices, const uint16_t* density, float* scratch, void* stream);
-/* The density-grid update's sample evaluation in one kernel: hash-grid encoding of the n sample
- * records (7 floats each), the density network (params: the packed [MLP | grid] fp16 vector of
- * `layout`, whose encoding must have 32 features of 2 or 4 per level) and the splat of
- * exp(density) * dt into scratch[indices[i]] (atomic max).  Same values as
- * ngp_encode_grid_forward + ngp_density_forward + ngp_density_grid_splat, without the encodings
- * and densities leaving the SM.  Replaces update_density_grid's evaluation (ngp.train.cu:1569-1576). */
-NGP_API int ngp_density_grid_encode_splat(const ngp_grid_layout* layout, uint32_t n, const float* coords, const uint16_t* params,
-                                          const uint32_t* indices, float* scratch, void* stream);
+
 
 /* Size (floats) of the `partial` buffer of ngp_density_grid_update. */
 NGP_API uint32_t ngp_density_grid_partials(void);

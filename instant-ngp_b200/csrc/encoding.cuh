@@ -1,5 +1,5 @@
 // Hash-grid encoding: per-level gather and trilinear interpolation shared by the encoding kernels
-// (encoding.cu) and the fused density-grid kernel (mlp.cu).  The arithmetic follows
+// (encoding.cu).  The arithmetic follows
 // encode_grid_forward_kernel (ngp.train.cu:876-921) with fp32 accumulation: corner weights
 // (wx * wy) * wz, fmaf over corners 0..7, one rounding to fp16 by the caller.
 #pragma once
@@ -84,32 +84,6 @@ __device__ __forceinline__ void interp_level(const float (&frac)[3], const typen
         unpack<F>(v[corner], val);
 #pragma unroll
         for (uint32_t f = 0; f < F; ++f) acc[f] = __fmaf_rn(w, val[f], acc[f]);
-    }
-}
-
-// All 32 / F levels of one point (the trainer's 32-feature encodings), two levels' gathers in
-// flight at a time, as fp16 pairs: packed[k] holds features 2k and 2k + 1.
-template <uint32_t F>
-__device__ __forceinline__ void encode_point32(const GridParams& grid, const __half* __restrict__ table, const float (&x)[3], uint32_t (&packed)[16]) {
-    using Vec        = typename FeatureVec<F>::type;
-    constexpr uint32_t L = 32u / F;
-    const Vec* tab   = reinterpret_cast<const Vec*>(table);
-#pragma unroll
-    for (uint32_t l0 = 0; l0 < L; l0 += 2) {
-        float frac[2][3];
-        Vec v[2][8];
-#pragma unroll
-        for (uint32_t j = 0; j < 2; ++j) gather_level<F>(grid, tab, l0 + j, x, frac[j], v[j]);
-#pragma unroll
-        for (uint32_t j = 0; j < 2; ++j) {
-            float acc[F];
-            interp_level<F>(frac[j], v[j], acc);
-#pragma unroll
-            for (uint32_t f = 0; f < F; f += 2) {
-                const __half2 h = __floats2half2_rn(acc[f], acc[f + 1]);
-                packed[((l0 + j) * F + f) / 2] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-        }
     }
 }
 

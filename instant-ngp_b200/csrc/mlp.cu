@@ -22,8 +22,7 @@
 #include <algorithm>
 #include <cstdlib>
 
-#include "encoding.cuh"
-#include "sampler.cuh"
+#include "common.cuh"
 #include "umma.cuh"
 
 namespace ngp {
@@ -130,27 +129,6 @@ __device__ __forceinline__ void read_acc(uint32_t tmem, uint32_t col, float* v) 
     for (uint32_t c = 0; c < N / 16; ++c)
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[c * 16 + j] = __uint_as_float(r[c][j]);
-}
-
-// Reads of TMEM lane `lane` (this warp's lane group 32 (w % 4) .. + 31) for CTAs of more than one
-// warpgroup: 64 or 16 fp32 columns from taddr (all reads issued before one wait).
-__device__ __forceinline__ void read_acc_lane64(uint32_t taddr, uint32_t lane, float* v) {
-    const uint32_t base = taddr + ((lane & ~31u) << 16);
-    uint32_t q[4][16];
-#pragma unroll
-    for (uint32_t c = 0; c < 4; ++c) umma::tmem_ld16_async(base + c * 16u, q[c]);
-    umma::tmem_wait_ld();
-#pragma unroll
-    for (uint32_t c = 0; c < 4; ++c)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[c * 16 + j] = __uint_as_float(q[c][j]);
-}
-__device__ __forceinline__ void read_acc_lane16(uint32_t taddr, uint32_t lane, float* v) {
-    uint32_t q[16];
-    umma::tmem_ld16_async(taddr + ((lane & ~31u) << 16), q);
-    umma::tmem_wait_ld();
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(q[j]);
 }
 
 // Issue D(+)= A * B^T over K (multiple of 16) from one thread.
@@ -399,93 +377,6 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
     umma::fence_before_sync();
     __syncthreads();
     if (t < 32) umma::tmem_dealloc(tmem, kFwdTmemCols);
-}
-
-// ---------------------------------------------------------------------------------------------
-// Density-grid update, fused: encoding -> density network -> splat (update_density_grid's
-// encode_grid_forward_kernel, mlp_forward_64_relu_kernel and splat_density_grid_samples_kernel,
-// ngp.train.cu:1569-1576).  Each thread encodes one grid sample straight into its row of a
-// 128-row operand tile in shared memory; the CTA's four tiles run the density network on the
-// tensor cores (fp32 TMEM accumulation, one fp16 rounding per layer, as mlp_forward_kernel); the
-// raw density, rounded to fp16 as the reference stores it, gives the optical thickness
-// exp(density) * dt whose bits are max-ed into the sample's cell.  No encoding or density leaves
-// the SM.  Same arithmetic at every step as the unfused kernels: the scratch grid is identical.
-// ---------------------------------------------------------------------------------------------
-constexpr uint32_t kGridTiles    = 4;                      // 128-row tiles per CTA (512 threads)
-constexpr uint32_t kGridThreads  = kGridTiles * kRows;
-constexpr uint32_t kGridTmemCols = 256;                    // tile k: cols 64k .. 64k + 63 (D1 in the first 16)
-constexpr uint32_t kGridX        = 6144;                   // weights: density W_in (4 KB) | W_out (2 KB)
-constexpr uint32_t kGridH        = kGridX + kGridTiles * 8192;
-constexpr uint32_t kGridSmem     = kGridH + kGridTiles * 16384 + 1024;
-
-template <uint32_t F>
-__global__ void __launch_bounds__(kGridThreads, 2) grid_density_splat_kernel(uint32_t n, const float* __restrict__ coords, const __half* __restrict__ params,
-                                                                             const __grid_constant__ GridParams grid, const uint32_t* __restrict__ indices,
-                                                                             float* __restrict__ scratch) {
-    extern __shared__ __align__(1024) unsigned char smem[];
-    __shared__ uint64_t mbar;
-    __shared__ uint32_t tmem_slot;
-    const uint32_t t    = threadIdx.x;
-    const uint32_t tile = t >> 7, r = t & 127u;  // tile of this thread's row; row = TMEM lane r
-    load_weight_tile(smem + kSWdIn, params + kWdIn, 64, 32);
-    load_weight_tile(smem + kSWdOut, params + kWdOut, 16, 64);
-    if (t < 32) umma::tmem_alloc(&tmem_slot, kGridTmemCols);
-    if (t == 0) umma::mbar_init(&mbar, 1);
-    stage_sync();
-    const uint32_t tmem = tmem_slot;
-    const uint32_t s0   = umma::smem_addr(smem);
-    unsigned char* xt   = smem + kGridX + tile * 8192u;
-    unsigned char* ht   = smem + kGridH + tile * 16384u;
-    const __half* table = params + kMlpParams;
-    uint32_t phase      = 0;
-    bool ok             = true;
-    for (uint32_t base = blockIdx.x * kGridThreads; base < n; base += gridDim.x * kGridThreads) {
-        const uint32_t i  = base + t;
-        const bool valid  = i < n;
-        {
-            uint32_t packed[16] = {};
-            if (valid) {
-                const float* c   = coords + static_cast<uint64_t>(i) * 7u;
-                const float x[3] = {__ldg(c), __ldg(c + 1), __ldg(c + 2)};
-                encode_point32<F>(grid, table, x, packed);
-            }
-#pragma unroll
-            for (uint32_t q = 0; q < 4; ++q) store_chunk(xt, r, q, 4, make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]));
-        }
-        stage_sync();
-        if (t == 0) {
-            for (uint32_t k = 0; k < kGridTiles; ++k)
-                gemm(tmem + 64u * k, 64, 32, s0 + kGridX + k * 8192u, false, 4, s0 + kSWdIn, false, 4, false);
-            umma::commit(&mbar);
-        }
-        ok = stage_wait(&mbar, phase) && ok;
-        {
-            float h[64];
-            read_acc_lane64(tmem + 64u * tile, r, h);
-            store_row<8, true>(ht, r, h);
-        }
-        stage_sync();
-        if (t == 0) {
-            for (uint32_t k = 0; k < kGridTiles; ++k)
-                gemm(tmem + 64u * k, 16, 64, s0 + kGridH + k * 16384u, false, 8, s0 + kSWdOut, false, 8, false);
-            umma::commit(&mbar);
-        }
-        ok = stage_wait(&mbar, phase) && ok;
-        {
-            float d[16];
-            read_acc_lane16(tmem + 64u * tile, r, d);
-            if (valid) {
-                const float thickness = expf(__half2float(__float2half_rn(d[0]))) * kConeStep;
-                atomicMax(reinterpret_cast<uint32_t*>(scratch + __ldg(indices + i)), __float_as_uint(thickness));
-            }
-        }
-        umma::fence_before_sync();
-        if (!__syncthreads_and(ok)) break;
-        umma::fence_after_sync();
-    }
-    umma::fence_before_sync();
-    __syncthreads();
-    if (t < 32) umma::tmem_dealloc(tmem, kGridTmemCols);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -918,31 +809,6 @@ extern "C" int ngp_density_forward_rows(uint32_t max_rows, const uint32_t* rows,
     MlpForwardParams p{max_rows, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7,
                        reinterpret_cast<__half*>(out), nullptr, rows, n_rows};
     return launch_forward<kModeDensity>(p, max_rows, as_stream(stream), "mlp_forward_kernel<density>");
-}
-
-extern "C" int ngp_density_grid_encode_splat(const ngp_grid_layout* layout, uint32_t n, const float* coords, const uint16_t* params,
-                                             const uint32_t* indices, float* scratch, void* stream) {
-    clear_error();
-    if (n == 0) return NGP_OK;
-    if (layout == nullptr || coords == nullptr || params == nullptr || indices == nullptr || scratch == nullptr)
-        return fail(NGP_ERR_INVALID, "grid encode+splat: null pointer");
-    if (layout->n_levels * layout->features_per_level != 32 || (layout->features_per_level != 2 && layout->features_per_level != 4))
-        return fail(NGP_ERR_INVALID, "grid encode+splat: needs 32 features of 2 or 4 per level");
-    static int attr = [] {
-        cudaError_t e = cudaFuncSetAttribute(grid_density_splat_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGridSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(grid_density_splat_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGridSmem);
-        return static_cast<int>(e);
-    }();
-    if (attr != 0) return fail(NGP_ERR_CUDA, std::string("grid encode+splat: cudaFuncSetAttribute: ") + cudaGetErrorString(static_cast<cudaError_t>(attr)));
-    const GridParams grid = make_grid_params(*layout);
-    const uint32_t chunks = (n + kGridThreads - 1) / kGridThreads;
-    const uint32_t ctas   = std::min<uint32_t>(chunks, static_cast<uint32_t>(sm_count()) * (512u / kGridTmemCols));
-    const auto* P         = reinterpret_cast<const __half*>(params);
-    if (layout->features_per_level == 2)
-        grid_density_splat_kernel<2><<<ctas, kGridThreads, kGridSmem, as_stream(stream)>>>(n, coords, P, grid, indices, scratch);
-    else
-        grid_density_splat_kernel<4><<<ctas, kGridThreads, kGridSmem, as_stream(stream)>>>(n, coords, P, grid, indices, scratch);
-    return check_launch("grid_density_splat_kernel");
 }
 
 extern "C" uint32_t ngp_mlp_backward_scratch_floats(void) { return mlp_backward_max_ctas() * kMlpParams; }

@@ -72,9 +72,6 @@ struct Split {
 #ifndef NGP_DP_PRIORITY
 #define NGP_DP_PRIORITY 1  // 0: equal stream priorities; the all-reduce waits for the next step's march (measured 0.935 vs 0.914 ms at 4 GPUs)
 #endif
-#ifndef NGP_FUSED_GRID
-#define NGP_FUSED_GRID 1  // 0: the grid update encodes, runs the density network and splats in three kernels
-#endif
 #ifndef NGP_SELECT
 #define NGP_SELECT 1  // 0: the kept samples' records and encodings are copied into a compacted batch
 #endif
@@ -333,18 +330,11 @@ int update_grid(ngp_trainer* t) {
     NGP_TRY(ngp_density_grid_samples_cell_order(n_uniform, n_nonuni, t->ema_step, t->grid_values, coords, t->grid_indices, t->grid_counter,
                                                 t->stream));
     grid_mark(t, 1);
-#if NGP_FUSED_GRID
-    // encoding, density network and splat in one kernel (no encoding or density leaves the SM)
-    NGP_TRY(ngp_density_grid_encode_splat(&t->layout, n, coords, t->params, t->grid_indices, t->grid_scratch, t->stream));
-    grid_mark(t, 2);
-    grid_mark(t, 3);
-#else
     NGP_TRY(encode(t, n, coords, t->enc, n));
     grid_mark(t, 2);
     NGP_TRY(ngp_density_forward(n, t->params, t->enc, n, t->grid_density, t->stream));
     grid_mark(t, 3);
     NGP_TRY(ngp_density_grid_splat(n, t->grid_indices, t->grid_density, t->grid_scratch, t->stream));
-#endif
     grid_mark(t, 4);
     NGP_TRY(ngp_density_grid_update(t->grid_values, t->grid_scratch, 0.95f, t->grid_partial, t->grid_mean, t->bitfield, t->occupied, t->stream));
     grid_mark(t, 5);

@@ -235,11 +235,6 @@ def density_grid_samples_cell_order(n_uniform, n_nonuniform, ema_step, values, c
                                                      _ptr(counter), _stream(stream)), "ngp_density_grid_samples_cell_order")
 
 
-def density_grid_encode_splat(layout: GridLayout, n, coords, params, indices, scratch, stream=None) -> None:
-    _check(lib().ngp_density_grid_encode_splat(ctypes.byref(layout), _u32(n), _ptr(coords), _ptr(params), _ptr(indices), _ptr(scratch),
-                                               _stream(stream)), "ngp_density_grid_encode_splat")
-
-
 def density_grid_splat(n, indices, density, scratch, stream=None) -> None:
     _check(lib().ngp_density_grid_splat(_u32(n), _ptr(indices), _ptr(density), _ptr(scratch), _stream(stream)), "ngp_density_grid_splat")
 

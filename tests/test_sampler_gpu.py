@@ -710,36 +710,3 @@ def test_grid_samples_cell_order_is_a_permutation_of_the_reference(ngp, reflib, 
         # slot g holds the sample whose first cell is g: cells ascend wherever no retry happened
         cells = idx.cpu().numpy().view(np.uint32)
         assert (cells == np.arange(n, dtype=np.uint32)).mean() > 0.95
-
-
-@pytest.mark.parametrize("layout_args", [(16, 2, 19, 16, math.log2(128.0) / 15.0), (8, 4, 19, 16, 1.0)], ids=["16x2", "8x4"])
-@pytest.mark.parametrize("n", [1 << 21, 5000])
-def test_fused_grid_encode_splat_equals_three_kernels(ngp, layout_args, n):
-    """ngp_density_grid_encode_splat (encoding -> density network -> splat in one kernel) leaves the
-    scratch grid bit-identical to the separate encoding, density-network and splat kernels."""
-    import torch
-
-    layout = ngp.grid_layout(*layout_args)
-    vals = workloads.blob_grid_values(workloads.gaussian_blob_density())
-    values = T(vals)
-    nu = min(n, 1 << 21)
-    coords = torch.zeros((nu, 7), dtype=torch.float32, device="cuda")
-    idx = torch.zeros(nu, dtype=torch.int32, device="cuda")
-    cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
-    ngp.density_grid_samples_cell_order(nu, 0, 3, values, coords, idx, cnt)
-    _, table, _ = workloads.encode_inputs(1, layout.n_params, 16, 2, seed=5)
-    table = (table.astype(np.float32) * 3e4).astype(np.float16)  # densities spread over a useful range
-    mlp = workloads.xavier_mlp_params(4)
-    params = T(np.concatenate([mlp, table]).view(np.int16))
-    enc = torch.zeros((32, nu), dtype=torch.float16, device="cuda")
-    dens = torch.zeros(nu, dtype=torch.float16, device="cuda")
-    a = torch.zeros(128 ** 3, dtype=torch.float32, device="cuda")
-    b = torch.zeros_like(a)
-    ngp.encode_grid_forward(layout, coords, params[10240:], enc, n=nu, coord_stride=7)
-    ngp.density_forward(params[:10240], enc, dens)
-    ngp.density_grid_splat(nu, idx, dens, a)
-    ngp.density_grid_encode_splat(layout, nu, coords, params, idx, b)
-    torch.cuda.synchronize()
-    assert ngp.mlp_status(reset=True) == 0
-    assert int((a > 0).sum().item()) > nu // 2
-    assert torch.equal(a, b)
