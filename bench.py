@@ -288,6 +288,7 @@ def bench_train_ours(args, rank, world, local):
     ds = make_dataset(args)
     cfg = ngp.config0_trainer_config()
     model = _trained_twin(ngp, ds, cfg, world, args.warmup)
+    exchange = model.exchange_mode()
     stats, launches, clocks, t_enter = timed_train(model, args.steps, world, local)
     ms = max_over_ranks(stats["elapsed_ms"], world)
     per_rank = gather_floats([stats["elapsed_ms"] / args.steps, t_enter], world)
@@ -339,7 +340,8 @@ def bench_train_ours(args, rank, world, local):
         "data": "synthetic procedural scene (64 Lambert spheres, seeded), rendered on the device",
         "config": {"workload": "config3 end-to-end training", "views": args.views, "resolution": args.res, "batch_samples_per_gpu": BATCH,
                    "grid": "L=16 F=2 log2T=19 base 16 b=1.3819", "mlp": "density 32-64-16, colour 32-64-64-16",
-                   "parallelism": f"dp{world} (NCCL all-reduce of the fp16 gradient sum per step)" if world > 1 else "dp1",
+                   "parallelism": (f"dp{world} (fp16 gradient reduce-scatter, Adam on the rank's shard, fp16 parameter all-gather: "
+                                   + ("one kernel over NVLink peer memory)" if exchange == "peer" else "NCCL)")) if world > 1 else "dp1",
                    "l2": "working set > L2 (samples 117 MB, encodings 268 MB, dataset 256 MB); no flush",
                    "pre_compaction_samples_per_step": stats["measured_sample_count_before_compaction"],
                    "rays_per_batch": stats["rays_per_batch"], "test_psnr_after_run": psnr,

@@ -570,6 +570,10 @@ NGP_API int ngp_trainer_set_params(ngp_trainer* t, const float* host_in, uint32_
 NGP_API int ngp_nccl_unique_id(uint8_t* out, size_t bytes);
 NGP_API int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank);
 NGP_API int ngp_trainer_set_collective_timeout(ngp_trainer* t, double timeout_ms);
+/* The gradient exchange a joined trainer uses: 0 none (not joined), 1 NCCL reduce-scatter +
+ * Adam on the shard + all-gather, 2 the same three steps in one kernel over NVLink peer memory
+ * (the default when every rank can map every peer's buffers; $NGP_EXCHANGE=nccl selects 1). */
+NGP_API int ngp_trainer_exchange_mode(const ngp_trainer* t);
 /* Training loss (no reference counterpart; the reference trains with L2, ngp.train.cu:817-820):
  * 0 = L2 (default), 1 = Huber (as ngp_training_loss_selected_kind). */
 NGP_API int ngp_trainer_set_loss(ngp_trainer* t, int loss_kind);

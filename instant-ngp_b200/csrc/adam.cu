@@ -137,7 +137,102 @@ __global__ void grad_to_half_kernel(uint32_t n, float* __restrict__ src, __half*
     if (clear) src[i] = 0.0f;
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Gradient reduce-scatter + Adam + parameter all-gather in one kernel over NVLink peer memory
+// (the data-parallel hook between backward_network and step_optimizer, ngp.train.cpp:123-124).
+// ---------------------------------------------------------------------------------------------
+constexpr uint32_t kExchangeThreads = 256;
+constexpr uint64_t kExchangeWaitNs  = 2000000000ull;  // 2 s per cross-GPU wait, then an error status
+
+__device__ __forceinline__ void store_release_sys(uint32_t* addr, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* addr) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits (one thread) until flags[base + q] >= epoch for every rank q; false after the time bound.
+__device__ bool wait_all_ranks(const uint32_t* flags, uint32_t base, uint32_t world, uint32_t epoch) {
+    const uint64_t start = now_ns();
+    for (uint32_t q = 0; q < world; ++q) {
+        while (static_cast<int32_t>(load_acquire_sys(flags + base + q) - epoch) < 0) {
+            if (now_ns() - start > kExchangeWaitNs) return false;
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kExchangeThreads) peer_exchange_adam_kernel(const __grid_constant__ PeerExchangeArgs a) {
+    uint32_t* mine = a.flags[a.rank];
+    __shared__ int s_ok;
+    // arrival: this rank's gradients are complete (the conversion kernel ran before this one)
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        __threadfence_system();
+        for (uint32_t q = 0; q < a.world; ++q) store_release_sys(a.flags[q] + a.rank, a.epoch);
+    }
+    if (threadIdx.x == 0) {
+        s_ok = wait_all_ranks(mine, 0, a.world, a.epoch);
+        if (!s_ok) atomicOr(a.status, 1u);
+    }
+    __syncthreads();
+    if (s_ok) {
+        AdamParams p{};
+        p.n_mlp = a.n_mlp, p.lr = a.lr, p.beta1 = a.beta1, p.beta2 = a.beta2, p.eps = a.eps, p.l2 = a.l2;
+        p.inv_loss_scale = 1.0f / a.loss_scale, p.lr_table = a.lr_table, p.table_len = a.table_len, p.first = 0;
+        const uint32_t first = a.rank * a.shard;
+        const uint32_t end   = min(first + a.shard, a.n_params);
+        for (uint32_t i0 = first + (blockIdx.x * kExchangeThreads + threadIdx.x) * 4u; i0 < end; i0 += gridDim.x * kExchangeThreads * 4u) {
+            // the shard's gradient: the ranks' fp16 sums added in rank order (fp32)
+            float g[4] = {0.f, 0.f, 0.f, 0.f};
+            for (uint32_t q = 0; q < a.world; ++q) {
+                const uint2 raw  = *reinterpret_cast<const uint2*>(a.grads[q] + i0);
+                const float2 lo  = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                const float2 hi  = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                g[0] += lo.x, g[1] += lo.y, g[2] += hi.x, g[3] += hi.y;
+            }
+            const bool grid = i0 >= a.n_mlp;
+            if (grid && g[0] == 0.0f && g[1] == 0.0f && g[2] == 0.0f && g[3] == 0.0f) continue;  // untouched: params unchanged everywhere
+            const uint32_t cnt = min(4u, end - i0);
+            uint2 hv           = *reinterpret_cast<const uint2*>(a.params[a.rank] + i0);
+            __half* h          = reinterpret_cast<__half*>(&hv);
+            for (uint32_t k = 0; k < cnt; ++k) adam_one(p, i0 + k, a.master[i0 + k], g[k], a.m[i0 + k], a.v[i0 + k], a.steps[i0 + k], h[k]);
+            // all-gather: the new parameters go to every rank's buffer
+            for (uint32_t q = 0; q < a.world; ++q) *reinterpret_cast<uint2*>(a.params[q] + i0) = hv;
+        }
+    }
+    // completion: after every CTA's writes, the last CTA tells every rank and waits for them all
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const uint32_t done = atomicAdd(mine + 2u * a.world, 1u);
+        if (done == gridDim.x - 1u) {
+            mine[2u * a.world] = 0u;
+            __threadfence_system();
+            for (uint32_t q = 0; q < a.world; ++q) store_release_sys(a.flags[q] + a.world + a.rank, a.epoch);
+            if (!wait_all_ranks(mine, a.world, a.world, a.epoch)) atomicOr(a.status, 2u);
+        }
+    }
+}
 }  // namespace
+
+int peer_exchange_adam(const PeerExchangeArgs& a, cudaStream_t stream) {
+    const uint32_t groups = (a.shard + 3u) / 4u;
+    uint32_t ctas         = (groups + kExchangeThreads - 1u) / kExchangeThreads;
+    const uint32_t cap    = static_cast<uint32_t>(sm_count()) * 4u;
+    ctas                  = ctas < 1u ? 1u : (ctas > cap ? cap : ctas);
+    peer_exchange_adam_kernel<<<ctas, kExchangeThreads, 0, stream>>>(a);
+    return check_launch("peer_exchange_adam_kernel");
+}
+
 }  // namespace ngp
 
 using namespace ngp;

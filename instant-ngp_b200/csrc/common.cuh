@@ -61,6 +61,27 @@ __host__ __device__ inline bool rows_layout(uint32_t stride) { return (stride & 
 // Number of SMs of the current device (148 on B200), cached per process.
 int sm_count();
 
+// Data-parallel gradient exchange fused with Adam over NVLink peer memory (adam.cu): every rank
+// reads the fp16 gradients of its parameter shard from all ranks' buffers, sums them in rank
+// order, takes the Adam step on its shard and writes the new fp16 parameters into every rank's
+// parameter buffer.  Cross-GPU ordering uses per-rank flag words in peer memory (an arrival
+// barrier before the reads, a completion barrier after the writes), each wait bounded in time.
+struct PeerExchangeArgs {
+    uint32_t rank, world, shard, n_params, n_mlp, epoch;
+    float lr, beta1, beta2, eps, l2, loss_scale;
+    const __half* const* grads;  // [world] device pointers (this rank's entry: its own buffer)
+    __half* const* params;       // [world]
+    uint32_t* const* flags;      // [world]: 2 * world flag words + one CTA counter each
+    float* master;
+    float* m;
+    float* v;
+    uint32_t* steps;
+    const float* lr_table;
+    uint32_t table_len;
+    uint32_t* status;  // bit 0: arrival wait timed out, bit 1: completion wait timed out
+};
+int peer_exchange_adam(const PeerExchangeArgs& a, cudaStream_t stream);
+
 // ---- hash grid -----------------------------------------------------------------------------
 // Kernel-parameter copy of ngp_grid_layout (only what the device needs).
 struct GridParams {

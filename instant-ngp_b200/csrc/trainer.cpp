@@ -156,6 +156,15 @@ struct ngp_trainer {
     // a collective (or a wait on a stream that runs one) that takes longer fails: the
     // communicator is aborted and the call returns NGP_ERR_TIMEOUT
     double collective_timeout_ms = 120000.0;
+    // fused exchange over NVLink peer memory (peer_exchange_adam): the ranks' fp16 gradient,
+    // fp16 parameter and flag buffers mapped into this process (CUDA IPC); used when every rank
+    // could map every peer, else the NCCL reduce-scatter / all-gather path
+    bool peer_exchange       = false;
+    uint32_t* peer_flags     = nullptr;  // this rank's 2 * world flags + CTA counter
+    void** peer_table        = nullptr;  // device: [3][world] grads, params, flags
+    std::vector<void*> peer_opened;      // IPC mappings to close
+    uint32_t peer_epoch      = 0;
+    uint32_t* peer_status    = nullptr;  // device error word of the fused exchange
     int loss_kind                = 0;  // 0 L2 (the reference's), 1 Huber
     // optional per-phase timing (cudaEvents between the phases of a step)
     bool profiling = false;
@@ -213,6 +222,8 @@ void destroy(ngp_trainer* t) {
                     t->seg_lists, t->seg_counters};
     for (void* p : ptrs) cudaFree(p);
     for (MarchSet& m : t->sets) cudaFree(m.coords), cudaFree(m.rays), cudaFree(m.ray_indices), cudaFree(m.numsteps), cudaFree(m.counters);
+    for (void* q : t->peer_opened) cudaIpcCloseMemHandle(q);
+    cudaFree(t->peer_flags), cudaFree(t->peer_table), cudaFree(t->peer_status);
     if (t->comm) {
         // non-blocking communicator: finalize (bounded wait), then destroy; abort if it hangs
         const ncclResult_t fr = ncclCommFinalize(t->comm);
@@ -553,8 +564,10 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     if (t->comm != nullptr) {
         if (premarch && !NGP_DP_PRIORITY) NGP_TRY(check_cuda(cudaStreamWaitEvent(t->stream, t->ev_march, 0), "exchange after march"));
         NGP_TRY(ngp_gradients_to_half(t->n_params, t->grads, t->grads16, 1, t->stream));
-        uint16_t* mine = t->grads16 + static_cast<size_t>(t->rank) * t->shard;
-        NGP_TRY(nccl_done(t, ncclReduceScatter(t->grads16, mine, t->shard, ncclHalf, ncclSum, t->comm, t->stream), "ncclReduceScatter"));
+        if (!t->peer_exchange) {
+            uint16_t* mine = t->grads16 + static_cast<size_t>(t->rank) * t->shard;
+            NGP_TRY(nccl_done(t, ncclReduceScatter(t->grads16, mine, t->shard, ncclHalf, ncclSum, t->comm, t->stream), "ncclReduceScatter"));
+        }
     }
     mark(t, 7);
     // step_optimizer (ngp.train.cu:1973-1980)
@@ -567,7 +580,19 @@ int train_step(ngp_trainer* t, bool premarch_next) {
         }
     }
     ++t->adam_calls;
-    if (t->comm != nullptr) {
+    if (t->comm != nullptr && t->peer_exchange) {
+        // reduce-scatter, Adam on this rank's shard and all-gather in one kernel over NVLink
+        PeerExchangeArgs a{};
+        a.rank = static_cast<uint32_t>(t->rank), a.world = static_cast<uint32_t>(t->world), a.shard = t->shard, a.n_params = t->n_params;
+        a.n_mlp = kMlpParams, a.epoch = ++t->peer_epoch, a.lr = t->cfg.learning_rate, a.beta1 = 0.9f, a.beta2 = 0.99f, a.eps = 1e-15f;
+        a.l2 = 1e-6f, a.loss_scale = kLossScale * static_cast<float>(t->world);
+        a.grads  = reinterpret_cast<const __half* const*>(t->peer_table);
+        a.params = reinterpret_cast<__half* const*>(t->peer_table + t->world);
+        a.flags  = reinterpret_cast<uint32_t* const*>(t->peer_table + 2 * t->world);
+        a.master = t->master, a.m = t->adam_m, a.v = t->adam_v, a.steps = t->adam_steps, a.lr_table = t->lr_table, a.table_len = t->lr_table_len;
+        a.status = t->peer_status;
+        NGP_TRY(peer_exchange_adam(a, t->stream));
+    } else if (t->comm != nullptr) {
         const uint32_t first = static_cast<uint32_t>(t->rank) * t->shard;
         const uint32_t count = first < t->n_params ? std::min(t->shard, t->n_params - first) : 0u;
         NGP_TRY(ngp_adam_step_f16_range(count, first, kMlpParams, t->cfg.learning_rate, 0.9f, 0.99f, 1e-15f, 1e-6f,
@@ -832,6 +857,76 @@ extern "C" int ngp_nccl_unique_id(uint8_t* out, size_t bytes) {
     return NGP_OK;
 }
 
+namespace {
+// Maps every rank's fp16 gradient, fp16 parameter and flag buffers into this process (CUDA IPC;
+// the handles travel through an NCCL all-gather) and enables the fused exchange when every rank
+// succeeded (an NCCL min-reduction of the ranks' outcomes).  Otherwise the mappings are closed
+// and the NCCL path stays in use.
+int setup_peer_exchange(ngp_trainer* t) {
+    const int W = t->world;
+    NGP_TRY(dalloc(t->peer_flags, 2u * static_cast<uint32_t>(W) + 1u, "peer flags"));
+    NGP_TRY(dalloc(t->peer_status, 1, "peer exchange status"));
+    NGP_TRY(check_cuda(cudaMemset(t->peer_flags, 0, sizeof(uint32_t) * (2u * W + 1u)), "peer flags"));
+    NGP_TRY(check_cuda(cudaMemset(t->peer_status, 0, sizeof(uint32_t)), "peer status"));
+    constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+    std::vector<unsigned char> mine(3 * kH), all(static_cast<size_t>(W) * 3 * kH);
+    int ok = 1;
+    void* bufs[3] = {t->grads16, t->params, t->peer_flags};
+    for (int k = 0; k < 3; ++k) {
+        cudaIpcMemHandle_t h{};
+        if (cudaIpcGetMemHandle(&h, bufs[k]) != cudaSuccess) ok = 0;
+        std::memcpy(mine.data() + k * kH, &h, kH);
+    }
+    (void)cudaGetLastError();
+    unsigned char* dev = nullptr;
+    NGP_TRY(dalloc(dev, all.size() + 16, "peer handles"));
+    int st = check_cuda(cudaMemcpy(dev + static_cast<size_t>(t->rank) * 3 * kH, mine.data(), mine.size(), cudaMemcpyHostToDevice), "peer handles");
+    if (st == NGP_OK)
+        st = nccl_done(t, ncclAllGather(dev + static_cast<size_t>(t->rank) * 3 * kH, dev, 3 * kH, ncclUint8, t->comm, t->stream), "ncclAllGather handles");
+    if (st == NGP_OK) st = wait_stream(t, t->stream, "peer handles");
+    if (st == NGP_OK) st = check_cuda(cudaMemcpy(all.data(), dev, all.size(), cudaMemcpyDeviceToHost), "peer handles");
+    if (st != NGP_OK) {
+        cudaFree(dev);
+        return st;
+    }
+    std::vector<void*> table(3 * static_cast<size_t>(W), nullptr);
+    for (int q = 0; q < W; ++q)
+        for (int k = 0; k < 3; ++k) {
+            if (q == t->rank) {
+                table[k * W + q] = bufs[k];
+                continue;
+            }
+            cudaIpcMemHandle_t h{};
+            std::memcpy(&h, all.data() + (static_cast<size_t>(q) * 3 + k) * kH, kH);
+            void* p = nullptr;
+            if (ok && cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess) {
+                table[k * W + q] = p;
+                t->peer_opened.push_back(p);
+            } else {
+                ok = 0;
+            }
+        }
+    (void)cudaGetLastError();
+    // every rank must be able to use the fused path
+    int* agree = reinterpret_cast<int*>(dev + all.size());
+    st = check_cuda(cudaMemcpy(agree, &ok, sizeof(int), cudaMemcpyHostToDevice), "peer agreement");
+    if (st == NGP_OK) st = nccl_done(t, ncclAllReduce(agree, agree, 1, ncclInt32, ncclMin, t->comm, t->stream), "ncclAllReduce agreement");
+    if (st == NGP_OK) st = wait_stream(t, t->stream, "peer agreement");
+    if (st == NGP_OK) st = check_cuda(cudaMemcpy(&ok, agree, sizeof(int), cudaMemcpyDeviceToHost), "peer agreement");
+    cudaFree(dev);
+    NGP_TRY(st);
+    if (!ok) {
+        for (void* q : t->peer_opened) cudaIpcCloseMemHandle(q);
+        t->peer_opened.clear();
+        return NGP_OK;
+    }
+    NGP_TRY(dalloc(t->peer_table, table.size(), "peer table"));
+    NGP_TRY(check_cuda(cudaMemcpy(t->peer_table, table.data(), sizeof(void*) * table.size(), cudaMemcpyHostToDevice), "peer table"));
+    t->peer_exchange = true;
+    return NGP_OK;
+}
+}  // namespace
+
 extern "C" int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int world, int rank) {
     clear_error();
     if (t == nullptr || unique_id == nullptr || world < 1 || rank < 0 || rank >= world) return fail(NGP_ERR_INVALID, "trainer join: bad arguments");
@@ -883,6 +978,8 @@ extern "C" int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int wo
         t->world = 1, t->rank = 0;
         return st;
     }
+    const char* mode = std::getenv("NGP_EXCHANGE");
+    if (mode == nullptr || std::string(mode) != "nccl") NGP_TRY(setup_peer_exchange(t));
     return NGP_OK;
 }
 
@@ -891,6 +988,11 @@ extern "C" int ngp_trainer_set_loss(ngp_trainer* t, int loss_kind) {
     if (t == nullptr || (loss_kind != 0 && loss_kind != 1)) return fail(NGP_ERR_INVALID, "set loss: bad arguments (0 = L2, 1 = Huber)");
     t->loss_kind = loss_kind;
     return NGP_OK;
+}
+
+extern "C" int ngp_trainer_exchange_mode(const ngp_trainer* t) {
+    if (t == nullptr || t->comm == nullptr) return 0;
+    return t->peer_exchange ? 2 : 1;
 }
 
 extern "C" int ngp_trainer_set_collective_timeout(ngp_trainer* t, double timeout_ms) {
@@ -925,6 +1027,13 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
     NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_loss, t->loss_values, sizeof(float) * loss_rays, cudaMemcpyDeviceToHost, t->stream), "read loss"));
     NGP_TRY(check_cuda(cudaMemcpyAsync(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read occupied"));
     NGP_TRY(wait_stream(t, t->stream, "train"));
+    if (t->peer_exchange) {
+        uint32_t status = 0;
+        NGP_TRY(check_cuda(cudaMemcpy(&status, t->peer_status, sizeof(status), cudaMemcpyDeviceToHost), "peer exchange status"));
+        if (status != 0)
+            return abort_comm(t, NGP_ERR_TIMEOUT, "peer exchange: a rank did not arrive within 2 s (status " + std::to_string(status) +
+                                                      "); communicator aborted");
+    }
     collect_grid_times(t);
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, e0, e1);

@@ -704,6 +704,11 @@ class InstantNGP:
         """Training loss: "l2" (the reference's, default) or "huber" (delta 0.1, scaled by 1/5)."""
         _check(lib().ngp_trainer_set_loss(self.handle, ctypes.c_int(self.LOSSES[kind])), "ngp_trainer_set_loss")
 
+    def exchange_mode(self) -> str:
+        """The joined trainer's gradient exchange: "none", "nccl" or "peer" (one fused kernel
+        over NVLink peer memory)."""
+        return {0: "none", 1: "nccl", 2: "peer"}[int(lib().ngp_trainer_exchange_mode(self.handle))]
+
     def set_collective_timeout(self, ms: float) -> None:
         """Collectives (and waits for the stream that runs them) that take longer abort the
         communicator and raise (NGP_ERR_TIMEOUT)."""
