@@ -311,16 +311,22 @@ __device__ __forceinline__ bool setup_ray(const MarchParams& p, uint32_t i, uint
 #endif
 constexpr uint32_t kCtaThreads = NGP_MARCH_CTA;
 constexpr uint32_t kRaysPerCta = kCtaThreads / kMarchGroup;
+// below this many threads per SM at kMarchGroup lanes per ray, training marches use 32 lanes per ray
+#ifndef NGP_WIDE_MARCH_THREADS
+#define NGP_WIDE_MARCH_THREADS 2048
+#endif
+constexpr uint32_t kWideMarchThreadsPerSm = NGP_WIDE_MARCH_THREADS;
 
-__global__ void __launch_bounds__(kCtaThreads) march_count_kernel(const __grid_constant__ MarchParams p) {
+template <uint32_t G>
+__global__ void __launch_bounds__(kRaysPerCta * G) march_count_kernel(const __grid_constant__ MarchParams p) {
     __shared__ uint32_t s_steps[kRaysPerCta];
     const uint32_t n    = march_ray_count(p);
-    const uint32_t slot = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
+    const uint32_t slot = threadIdx.x / G, g = threadIdx.x % G;
     const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
     TrainRay r{};
     const bool active    = i < n && setup_ray(p, i, n, r);
     uint32_t n_runs;
-    const uint32_t steps = group_march_count_runs(r.origin, r.dir, r.start_t, active, p.bits, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs);
+    const uint32_t steps = group_march_count_runs<G>(r.origin, r.dir, r.start_t, active, p.bits, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs);
     if (i < n && g == 0) {
         p.numsteps[2u * i]      = steps;
         p.numsteps[2u * i + 1u] = n_runs;  // read back by the write pass, then replaced by the base
@@ -359,11 +365,12 @@ __global__ void __launch_bounds__(1024) scan_totals_kernel(uint32_t* __restrict_
     }
 }
 
-__global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_constant__ MarchParams p) {
+template <uint32_t G>
+__global__ void __launch_bounds__(kRaysPerCta * G) march_write_kernel(const __grid_constant__ MarchParams p) {
     __shared__ uint32_t s_base[kRaysPerCta];
-    __shared__ float s_stage[kCtaThreads * 7u];  // per warp: 32 staged sample records
+    __shared__ float s_stage[kRaysPerCta * G * 7u];  // per warp: 32 staged sample records
     const uint32_t n    = march_ray_count(p);
-    const uint32_t slot = threadIdx.x / kMarchGroup, g = threadIdx.x % kMarchGroup;
+    const uint32_t slot = threadIdx.x / G, g = threadIdx.x % G;
     const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
     // this ray's first sample: CTA base + counts of the CTA's earlier rays (exclusive scan)
     const uint32_t steps  = i < n ? p.numsteps[2u * i] : 0u;
@@ -384,8 +391,8 @@ __global__ void __launch_bounds__(kCtaThreads) march_write_kernel(const __grid_c
     float* out          = p.coords + static_cast<uint64_t>(base) * 7u;
     const bool overflow = n_runs == kRunsOverflow;
     // rays with few runs expand them; the rare ray with more runs than recorded marches again
-    group_expand_runs(r.dir, r.origin, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs, kept, !overflow, out, s_stage + (threadIdx.x & ~31u) * 7u);
-    group_march_write(r.origin, r.dir, r.start_t, overflow ? kept : 0u, p.bits, out);
+    group_expand_runs<G>(r.dir, r.origin, p.runs + static_cast<uint64_t>(i) * kMaxRuns, n_runs, kept, !overflow, out, s_stage + (threadIdx.x & ~31u) * 7u);
+    group_march_write<G>(r.origin, r.dir, r.start_t, overflow ? kept : 0u, p.bits, out);
 }
 
 // Segmented marching of evaluation rays: each call marches at most `cap` further samples of the
@@ -502,11 +509,21 @@ int launch_march(MarchParams p, uint32_t* scratch, cudaStream_t s) {
     const uint32_t blocks = march_blocks(p.n_rays);
     p.block_totals        = scratch;
     p.runs                = reinterpret_cast<uint2*>(scratch + ((blocks + 1u) & ~1u));
-    march_count_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
+    // Few rays (the first training steps march ~4096 long rays): a whole warp per ray instead of
+    // kMarchGroup lanes, so that the SMs have enough warps to hide each round's latency.  The
+    // positions are the sequential march's either way; only the speculation width differs.
+    const bool wide = static_cast<uint64_t>(p.n_rays) * kMarchGroup < static_cast<uint64_t>(sm_count()) * kWideMarchThreadsPerSm;
+    if (wide)
+        march_count_kernel<32><<<blocks, kRaysPerCta * 32u, 0, s>>>(p);
+    else
+        march_count_kernel<kMarchGroup><<<blocks, kCtaThreads, 0, s>>>(p);
     NGP_TRY(check_launch("march_count_kernel"));
     scan_totals_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, p.n_rays_dev, p.n_rays, p.sample_counter, p.ray_counter);
     NGP_TRY(check_launch("scan_totals_kernel"));
-    march_write_kernel<<<blocks, kCtaThreads, 0, s>>>(p);
+    if (wide)
+        march_write_kernel<32><<<blocks, kRaysPerCta * 32u, 0, s>>>(p);
+    else
+        march_write_kernel<kMarchGroup><<<blocks, kCtaThreads, 0, s>>>(p);
     return check_launch("march_write_kernel");
 }
 

@@ -238,9 +238,9 @@ struct MarchRound {
     bool cont;       // the next round's first position directly follows the last emitted sample
 };
 
-// One round for every group of the warp (all 32 lanes call it together).
+// One round for every group of the warp (all 32 lanes call it together); G lanes per ray.
+template <uint32_t G = kMarchGroup>
 __device__ __forceinline__ MarchRound group_march_round(GroupMarch& m, const uint8_t* __restrict__ bits, uint32_t limit) {
-    constexpr uint32_t G    = kMarchGroup;
     const uint32_t lane     = threadIdx.x & 31u;
     const uint32_t g        = lane % G;
     const uint32_t group_lo = lane - g;
@@ -257,7 +257,7 @@ __device__ __forceinline__ MarchRound group_march_round(GroupMarch& m, const uin
     const bool ins       = !m.done && inside_unit_cube(r.pos);
     const bool oc        = ins && occupied(r.pos, bits);
     const bool stop_here = skip_mode ? (!ins || oc) : !oc;
-    const uint32_t stop  = (__ballot_sync(0xFFFFFFFFu, stop_here) >> group_lo) & ((1u << G) - 1u);
+    const uint32_t stop  = (__ballot_sync(0xFFFFFFFFu, stop_here) >> group_lo) & (G == 32u ? 0xFFFFFFFFu : ((1u << G) - 1u));
     const uint32_t f     = stop ? static_cast<uint32_t>(__ffs(stop)) - 1u : G;
     const uint32_t fl    = group_lo + (f < G ? f : G - 1u);
     const float next     = skip_empty_voxel(tk, r.pos, m.d, m.inv);
@@ -300,6 +300,7 @@ __device__ __forceinline__ MarchRound group_march_round(GroupMarch& m, const uin
 }
 
 // Writes exactly `n` records (n = this ray's count) starting at `out`; n = 0 for inactive groups.
+template <uint32_t G = kMarchGroup>
 __device__ __forceinline__ void group_march_write(float3 o, float3 d, float start_t, uint32_t n, const uint8_t* __restrict__ bits,
                                                   float* __restrict__ out) {
     const float3 w3 = {(d.x + 1.0f) * 0.5f, (d.y + 1.0f) * 0.5f, (d.z + 1.0f) * 0.5f};
@@ -307,7 +308,7 @@ __device__ __forceinline__ void group_march_write(float3 o, float3 d, float star
     group_march_begin(m, o, d, start_t, n > 0);
     while (__any_sync(0xFFFFFFFFu, !m.done)) {
         const uint32_t before = m.n;
-        const MarchRound r    = group_march_round(m, bits, n);
+        const MarchRound r    = group_march_round<G>(m, bits, n);
         if (r.emit) {
             float* c = out + static_cast<uint64_t>(before + r.slot) * 7u;
             c[0] = r.pos.x, c[1] = r.pos.y, c[2] = r.pos.z, c[3] = kConeStep, c[4] = w3.x, c[5] = w3.y, c[6] = w3.z;
@@ -325,16 +326,17 @@ constexpr uint32_t kRunsOverflow = 0xFFFFFFFFu;
 
 // Sample count of this group's ray (all lanes of the warp call it; inactive groups pass
 // active=false); its runs go to `runs`, their number (or kRunsOverflow) to n_runs.
+template <uint32_t G = kMarchGroup>
 __device__ __forceinline__ uint32_t group_march_count_runs(float3 o, float3 d, float start_t, bool active, const uint8_t* __restrict__ bits,
                                                            uint2* __restrict__ runs, uint32_t& n_runs) {
-    const uint32_t g = (threadIdx.x & 31u) % kMarchGroup;
+    const uint32_t g = (threadIdx.x & 31u) % G;
     GroupMarch m;
     group_march_begin(m, o, d, start_t, active);
     float run_t0   = 0.0f;
     uint32_t run_n = 0;
     n_runs         = 0;
     while (__any_sync(0xFFFFFFFFu, !m.done)) {
-        const MarchRound r = group_march_round(m, bits, kMarchSteps);
+        const MarchRound r = group_march_round<G>(m, bits, kMarchSteps);
         if (r.k > 0) {
             if (run_n == 0) run_t0 = r.first_t;
             run_n += r.k;
@@ -393,11 +395,12 @@ __device__ __forceinline__ uint32_t group_march_count_runs_seg(float3 o, float3 
 // Each round the group's lanes compute up to kMarchGroup consecutive records, stage them in this
 // warp's 32 x 7 floats of shared memory (`stage`), and copy them out as consecutive floats, so a
 // store instruction writes whole 32-byte sectors instead of one float every 28 bytes.
+template <uint32_t G = kMarchGroup>
 __device__ __forceinline__ void group_expand_runs(float3 d_unit, float3 o, const uint2* __restrict__ runs, uint32_t n_runs, uint32_t n,
                                                   bool active, float* __restrict__ out, float* __restrict__ stage) {
     const float3 w3         = {(d_unit.x + 1.0f) * 0.5f, (d_unit.y + 1.0f) * 0.5f, (d_unit.z + 1.0f) * 0.5f};
     const uint32_t lane     = threadIdx.x & 31u;
-    const uint32_t g        = lane % kMarchGroup;
+    const uint32_t g        = lane % G;
     const uint32_t group_lo = lane - g;
     uint32_t r = 0, in_run = 0, written = 0, cnt = 0;
     float t = 0.0f;
@@ -410,8 +413,8 @@ __device__ __forceinline__ void group_expand_runs(float3 d_unit, float3 o, const
     while (__any_sync(0xFFFFFFFFu, active)) {
         float tk = t;
         for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
-        const float t_last = __shfl_sync(0xFFFFFFFFu, tk, group_lo + kMarchGroup - 1u);
-        const uint32_t adv = active ? min(min(kMarchGroup, cnt - in_run), n - written) : 0u;
+        const float t_last = __shfl_sync(0xFFFFFFFFu, tk, group_lo + G - 1u);
+        const uint32_t adv = active ? min(min(G, cnt - in_run), n - written) : 0u;
         if (g < adv) {
             const float3 p = ray_point(o, d_unit, tk);
             float* c       = stage + lane * 7u;
@@ -421,7 +424,7 @@ __device__ __forceinline__ void group_expand_runs(float3 d_unit, float3 o, const
         if (active) {
             float* dst       = out + static_cast<uint64_t>(written) * 7u;
             const float* src = stage + group_lo * 7u;
-            for (uint32_t q = g; q < 7u * adv; q += kMarchGroup) dst[q] = src[q];
+            for (uint32_t q = g; q < 7u * adv; q += G) dst[q] = src[q];
             written += adv;
             in_run += adv;
             t = t_last + kConeStep;
