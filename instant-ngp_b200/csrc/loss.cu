@@ -592,57 +592,216 @@ struct CompactedLossParams {
     int loss_kind;                 // kLossL2 (the reference) or kLossHuber
 };
 
-// Step 5: pass 1's compositing over the compacted outputs, then pass 2.
+// Inclusive warp scans (Kogge-Stone over shfl_up): lane l gets x_0 * ... * x_l (or the sum).
+__device__ __forceinline__ float warp_scan_mul(float x) {
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (uint32_t d = 1; d < 32u; d <<= 1) {
+        const float y = __shfl_up_sync(0xFFFFFFFFu, x, d);
+        if (lane >= d) x *= y;
+    }
+    return x;
+}
+__device__ __forceinline__ float3 warp_scan_add3(float3 v) {
+    const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+    for (uint32_t d = 1; d < 32u; d <<= 1) {
+        const float x = __shfl_up_sync(0xFFFFFFFFu, v.x, d), y = __shfl_up_sync(0xFFFFFFFFu, v.y, d), z = __shfl_up_sync(0xFFFFFFFFu, v.z, d);
+        if (lane >= d) v.x += x, v.y += y, v.z += z;
+    }
+    return v;
+}
+
+// One 32-sample chunk of a ray (samples c0 + lane < k): opacity and colour of this lane's sample.
+__device__ __forceinline__ void chunk_sample(const __half* __restrict__ out, const float* __restrict__ cin, uint32_t j, bool valid, float& alpha,
+                                             float3& col, float& md, float& dt) {
+    float r = 0.f, g = 0.f, b = 0.f;
+    md = 0.f, dt = 0.f;
+    if (valid) {
+        load_output(out + static_cast<uint64_t>(j) * 16u, r, g, b, md);
+        dt = cin[static_cast<uint64_t>(j) * 7u + 3u];
+    }
+    alpha = valid ? 1.0f - __expf(-expf(md) * dt) : 0.0f;
+    col   = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
+}
+
+// Step 5: compositing over the compacted outputs (pass 1), the loss, then the per-sample gradients
+// (pass 2), for the kRaysPerCta rays of a CTA.
+//
+// Work split: the rays' 32-sample chunks, in ray order, form one list that is cut into
+// kRaysPerCta equal contiguous ranges, one per warp, so that a long ray (hundreds of samples in
+// the first steps, when the whole grid is occupied) is composited by several warps at once
+// instead of one warp walking it alone.  A warp's range is a sequence of pieces, the chunks of
+// one ray inside the range.  Pass 1 composites each piece from transmittance 1 (its transmittance
+// product P and colour sum S); the pieces of a ray are then joined in order (transmittance and
+// colour at the start of each piece; the ray's colour sum_pieces T_start * S); pass 2 recomputes
+// each piece's samples from its start values.  Within a chunk the transmittance prefix and the
+// colour prefix are warp scans.  (The reference walks each ray sequentially in one thread,
+// ngp.train.cu:804-859; the products and sums here associate differently, a relative change of
+// the order of 1e-7.)
 __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __grid_constant__ CompactedLossParams p) {
+    __shared__ uint32_t s_k[kRaysPerCta], s_cn[kRaysPerCta], s_src[kRaysPerCta], s_cbase[kRaysPerCta], s_first[kRaysPerCta + 1];
+    __shared__ float s_P[kRaysPerCta][kRaysPerCta], s_T0[kRaysPerCta][kRaysPerCta];  // [warp][ray]
+    __shared__ float3 s_S[kRaysPerCta][kRaysPerCta], s_A0[kRaysPerCta][kRaysPerCta];
+    __shared__ float3 s_rgb[kRaysPerCta], s_grad[kRaysPerCta];
     const uint32_t n    = min(p.ray_counter != nullptr ? *p.ray_counter : p.rays_per_batch, p.rays_per_batch);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t i    = blockIdx.x * kRaysPerCta + warp;
-    if (i >= n) return;
-    const uint32_t k     = p.numsteps[2u * i];
-    const uint32_t cbase = p.numsteps[2u * i + 1u];
-    const uint32_t cn    = cbase < kNetworkBatch ? min(k, kNetworkBatch - cbase) : 0u;
-    __syncwarp();
-    if (lane == 0) p.numsteps[2u * i] = cn;
-    if (cn == 0) return;
-    const uint32_t src = p.sample_base != nullptr ? p.sample_base[i] : cbase;
-    const __half* out  = p.output + static_cast<uint64_t>(src) * 16u;
-    const float* cin   = p.coords + static_cast<uint64_t>(src) * 7u;
+    if (blockIdx.x * kRaysPerCta >= n) return;  // uniform over the CTA
+    if (threadIdx.x < kRaysPerCta) {
+        const uint32_t i = blockIdx.x * kRaysPerCta + threadIdx.x;
+        uint32_t k = 0, cn = 0, cbase = 0;
+        if (i < n) {
+            k     = p.numsteps[2u * i];
+            cbase = p.numsteps[2u * i + 1u];
+            cn    = cbase < kNetworkBatch ? min(k, kNetworkBatch - cbase) : 0u;
+            p.numsteps[2u * i] = cn;
+        }
+        s_k[threadIdx.x]     = cn == 0 ? 0u : k;  // a ray with no sample in the batch is skipped
+        s_cn[threadIdx.x]    = cn;
+        s_cbase[threadIdx.x] = cbase;
+        s_src[threadIdx.x]   = (i < n && p.sample_base != nullptr) ? p.sample_base[i] : cbase;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t c = 0;
+        for (uint32_t r = 0; r < kRaysPerCta; ++r) {
+            s_first[r] = c;
+            c += (s_k[r] + 31u) / 32u;
+        }
+        s_first[kRaysPerCta] = c;
+    }
+    __syncthreads();
+    const uint32_t total = s_first[kRaysPerCta];
+    const uint32_t len   = (total + kRaysPerCta - 1u) / kRaysPerCta;
+    const uint32_t lo = min(total, warp * len), hi = min(total, lo + len);
 
-    // composite the k kept samples (pass 1)
-    float T    = 1.0f;
-    float3 rgb = {0.0f, 0.0f, 0.0f};
-    for (uint32_t c0 = 0; c0 < k; c0 += 32u) {
-        const uint32_t j = c0 + lane;
-        const bool valid = j < k;
-        float r = 0.f, g = 0.f, b = 0.f, d = 0.f, dt = 0.f;
-        if (valid) {
-            load_output(out + static_cast<uint64_t>(j) * 16u, r, g, b, d);
-            dt = cin[static_cast<uint64_t>(j) * 7u + 3u];
+    // this warp's ray (for the join and the loss): its target and background, drawn while the
+    // compositing runs
+    const uint32_t my_i = blockIdx.x * kRaysPerCta + warp;
+    float3 bg{}, target{};
+    if (s_k[warp] > 0)
+        ray_target(p.step, p.rays_per_batch, p.pixels, p.frame_count, p.width, p.height, p.ray_indices != nullptr ? p.ray_indices[my_i] : my_i, bg,
+                   target);
+
+    // ---- pass 1: each piece composited from transmittance 1 ----
+    {
+        uint32_t r = 0;
+        for (uint32_t c = lo; c < hi;) {
+            while (c >= s_first[r + 1u]) ++r;
+            const uint32_t e = min(hi, s_first[r + 1u]);
+            const __half* out = p.output + static_cast<uint64_t>(s_src[r]) * 16u;
+            const float* cin  = p.coords + static_cast<uint64_t>(s_src[r]) * 7u;
+            const uint32_t k  = s_k[r];
+            float P   = 1.0f;
+            float3 S  = {0.f, 0.f, 0.f};
+            for (; c < e; ++c) {
+                const uint32_t j = (c - s_first[r]) * 32u + lane;
+                float alpha, md, dt;
+                float3 col;
+                chunk_sample(out, cin, j, j < k, alpha, col, md, dt);
+                const float Q  = warp_scan_mul(1.0f - alpha);            // product through this sample
+                const float Qu = __shfl_up_sync(0xFFFFFFFFu, Q, 1);  // every lane takes part in the shuffle
+                const float Qx = lane == 0 ? 1.0f : Qu;           // product before this sample
+                const float w  = alpha * (P * Qx);
+                const float3 a = warp_scan_add3({w * col.x, w * col.y, w * col.z});
+                S.x += __shfl_sync(0xFFFFFFFFu, a.x, 31);
+                S.y += __shfl_sync(0xFFFFFFFFu, a.y, 31);
+                S.z += __shfl_sync(0xFFFFFFFFu, a.z, 31);
+                P *= __shfl_sync(0xFFFFFFFFu, Q, 31);
+            }
+            if (lane == 0) {
+                s_P[warp][r] = P;
+                s_S[warp][r] = S;
+            }
         }
-        const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
-        const float3 col  = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
-        const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, k - c0));
-        const uint32_t nk = min(32u, k - c0);
-        const float w     = alpha * Tb;
-        for (uint32_t q = 0; q < nk; ++q) {
-            const float wq = __shfl_sync(0xFFFFFFFFu, w, q);
-            rgb.x          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.x, q), rgb.x);
-            rgb.y          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.y, q), rgb.y);
-            rgb.z          = __fmaf_rn(wq, __shfl_sync(0xFFFFFFFFu, col.z, q), rgb.z);
+    }
+    __syncthreads();
+
+    // ---- join the pieces of this warp's ray; loss and its gradient ----
+    if (s_k[warp] > 0) {
+        const uint32_t r = warp;
+        float T          = 1.0f;
+        float3 rgb       = {0.f, 0.f, 0.f};
+        for (uint32_t w = s_first[r] / len; w * len < s_first[r + 1u]; ++w) {
+            if (lane == 0) {
+                s_T0[w][r] = T;
+                s_A0[w][r] = rgb;
+            }
+            const float3 S = s_S[w][r];
+            rgb.x          = __fmaf_rn(T, S.x, rgb.x);
+            rgb.y          = __fmaf_rn(T, S.y, rgb.y);
+            rgb.z          = __fmaf_rn(T, S.z, rgb.z);
+            T *= s_P[w][r];
         }
-        T = __shfl_sync(0xFFFFFFFFu, Tb * (1.0f - alpha), nk - 1u);
+        if (s_k[r] == p.steps[my_i]) {
+            rgb.x = __fmaf_rn(T, bg.x, rgb.x);
+            rgb.y = __fmaf_rn(T, bg.y, rgb.y);
+            rgb.z = __fmaf_rn(T, bg.z, rgb.z);
+        }
+        const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
+        if (p.loss_output != nullptr && lane == 0) p.loss_output[my_i] = loss_value(diff, p.loss_kind, p.rays_per_batch);
+        if (lane == 0) {
+            s_rgb[r]  = rgb;
+            s_grad[r] = loss_gradient(diff, p.loss_kind);
+        }
     }
-    float3 bg, target;
-    ray_target(p.step, p.rays_per_batch, p.pixels, p.frame_count, p.width, p.height, p.ray_indices != nullptr ? p.ray_indices[i] : i, bg, target);
-    if (k == p.steps[i]) {
-        rgb.x = __fmaf_rn(T, bg.x, rgb.x);
-        rgb.y = __fmaf_rn(T, bg.y, rgb.y);
-        rgb.z = __fmaf_rn(T, bg.z, rgb.z);
+    __syncthreads();
+
+    // ---- pass 2: per-sample gradients of the first cn samples of each ray ----
+    const float scale = kLossScale / static_cast<float>(p.rays_per_batch);
+    {
+        uint32_t r = 0;
+        for (uint32_t c = lo; c < hi;) {
+            while (c >= s_first[r + 1u]) ++r;
+            const uint32_t e  = min(hi, s_first[r + 1u]);
+            const uint32_t cn = s_cn[r], k = s_k[r];
+            const __half* out = p.output + static_cast<uint64_t>(s_src[r]) * 16u;
+            const float* cin  = p.coords + static_cast<uint64_t>(s_src[r]) * 7u;
+            __half* dout      = p.dloss_doutput + static_cast<uint64_t>(s_cbase[r]) * 16u;
+            const float* ray  = p.rays + static_cast<uint64_t>(blockIdx.x * kRaysPerCta + r) * 6u;
+            const float3 origin = {ray[0], ray[1], ray[2]};
+            const float3 rgb = s_rgb[r], grad = s_grad[r];
+            float T          = s_T0[warp][r];
+            float3 acc       = s_A0[warp][r];
+            for (; c < e; ++c) {
+                const uint32_t c0 = (c - s_first[r]) * 32u;
+                if (c0 >= cn) {
+                    c = e;
+                    break;
+                }
+                const uint32_t j = c0 + lane;
+                float alpha, md, dt;
+                float3 col;
+                chunk_sample(out, cin, j, j < k, alpha, col, md, dt);
+                const float Q      = warp_scan_mul(1.0f - alpha);
+                const float Qu     = __shfl_up_sync(0xFFFFFFFFu, Q, 1);
+                const float Qx     = lane == 0 ? 1.0f : Qu;
+                const float Tb     = T * Qx;
+                const float weight = alpha * Tb;
+                float3 a           = warp_scan_add3({weight * col.x, weight * col.y, weight * col.z});
+                a                  = {acc.x + a.x, acc.y + a.y, acc.z + a.z};  // colour prefix including this sample
+                const float Ta     = Tb * (1.0f - alpha);
+                if (j < cn) {
+                    const float* cv     = cin + static_cast<uint64_t>(j) * 7u;
+                    const float depth   = norm3df(cv[0] - origin.x, cv[1] - origin.y, cv[2] - origin.z);
+                    const float3 suffix = {rgb.x - a.x, rgb.y - a.y, rgb.z - a.z};
+                    const float g0      = scale * (weight * grad.x * (col.x * (1.0f - col.x)));
+                    const float g1      = scale * (weight * grad.y * (col.y * (1.0f - col.y)));
+                    const float g2      = scale * (weight * grad.z * (col.z * (1.0f - col.z)));
+                    const float dd      = expf(fminf(fmaxf(md, -15.0f), 15.0f));
+                    const float sum = __fmaf_rn(grad.z, __fmaf_rn(Ta, col.z, -suffix.z),
+                                                __fmaf_rn(grad.x, __fmaf_rn(Ta, col.x, -suffix.x), grad.y * __fmaf_rn(Ta, col.y, -suffix.y)));
+                    const float g3 = __fmaf_rn(scale, dd * (dt * sum), (md > -10.0f && depth < 0.1f) ? 1e-4f : 0.0f);
+                    uint4* d       = reinterpret_cast<uint4*>(dout + static_cast<uint64_t>(j) * 16u);
+                    __half2 h01 = __floats2half2_rn(g0, g1), h23 = __floats2half2_rn(g2, g3);
+                    d[0]        = make_uint4(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23), 0u, 0u);
+                    d[1]        = make_uint4(0u, 0u, 0u, 0u);
+                }
+                T   = __shfl_sync(0xFFFFFFFFu, Ta, 31);
+                acc = {__shfl_sync(0xFFFFFFFFu, a.x, 31), __shfl_sync(0xFFFFFFFFu, a.y, 31), __shfl_sync(0xFFFFFFFFu, a.z, 31)};
+            }
+        }
     }
-    const float3 diff = {rgb.x - target.x, rgb.y - target.y, rgb.z - target.z};
-    if (p.loss_output != nullptr && lane == 0) p.loss_output[i] = loss_value(diff, p.loss_kind, p.rays_per_batch);
-    ray_gradients(rgb, loss_gradient(diff, p.loss_kind), kLossScale / static_cast<float>(p.rays_per_batch), p.rays + static_cast<uint64_t>(i) * 6u, cin, out, nullptr,
-                  p.dloss_doutput + static_cast<uint64_t>(cbase) * 16u, cn);
 }
 
 // Padding of a selected batch: rows [n, batch) repeat rows [0, n) and their gradients scaled by

@@ -41,6 +41,17 @@ constexpr uint32_t kSWdIn = 0, kSWdOut = 4096, kSWrIn = 6144, kSWrH = 10240, kSW
 // Device status word: set (never cleared by kernels) when an mbarrier wait times out.
 __device__ uint32_t g_mlp_status;
 
+#ifdef NGP_MLP_TRACE
+// Development-only timeline of CTA 0 of the last forward launch (SM clock at fixed points).
+__device__ unsigned long long g_mlp_trace[64];
+#define MLP_TRACE(i) do { if (blockIdx.x == 0 && threadIdx.x == 0 && ((i) < 60 || (i) == 63)) g_mlp_trace[(i)] = clock64(); } while (0)
+extern "C" __attribute__((visibility("default"))) int ngp_mlp_trace_read(unsigned long long* out) {
+    return static_cast<int>(cudaMemcpyFromSymbol(out, g_mlp_trace, sizeof(g_mlp_trace)));
+}
+#else
+#define MLP_TRACE(i) do { } while (0)
+#endif
+
 // ---- tile helpers --------------------------------------------------------------------------
 // Byte offset of 16-byte chunk c of row r in a tile with `cpr` chunks per row.
 __device__ __forceinline__ uint32_t tile_off(uint32_t r, uint32_t c, uint32_t cpr) { return (r & 7u) * 16u + (r >> 3) * (128u * cpr) + c * 128u; }
@@ -75,12 +86,15 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Copy a row-major fp16 matrix [rows][cols] from global memory into an interleaved tile.
-__device__ void load_weight_tile(unsigned char* tile, const __half* W, uint32_t rows, uint32_t cols) {
+// Copy a row-major fp16 matrix [rows][cols] from global memory into an interleaved tile with
+// 16-byte asynchronous copies: every chunk of every weight matrix is in flight at once (a
+// load-then-store loop through registers serialises on each load's L2 latency).  The caller
+// commits the group and waits for it before the first MMA reads the tile.
+__device__ __forceinline__ void load_weight_tile(unsigned char* tile, const __half* W, uint32_t rows, uint32_t cols) {
     const uint32_t cpr = cols / 8u;
     for (uint32_t q = threadIdx.x; q < rows * cpr; q += blockDim.x) {
         const uint32_t r = q / cpr, c = q % cpr;
-        store_chunk(tile, r, c, cpr, *reinterpret_cast<const uint4*>(W + r * cols + c * 8u));
+        cp_async16(tile + tile_off(r, c, cpr), W + r * cols + c * 8u, 16u);
     }
 }
 
@@ -144,6 +158,48 @@ __device__ __forceinline__ void gemm(uint32_t d_tmem, uint32_t N, uint32_t K, ui
         const uint64_t bd = umma::make_desc(b_saddr + ks * 2u * b_lbo, b_lbo, b_sbo);
         umma::mma_f16(d_tmem, ad, bd, idesc, (accumulate || ks > 0) ? 1u : 0u);
     }
+}
+
+// Issue D(+)= A * B^T over K (multiple of 16) from one thread, A (128 rows x K fp16) read from
+// tensor memory at a_tmem (8 columns per K step of 16), B K-major in shared memory.
+__device__ __forceinline__ void gemm_ta(uint32_t d_tmem, uint32_t N, uint32_t K, uint32_t a_tmem, uint32_t b_saddr, uint32_t b_cpr) {
+    const uint32_t idesc = umma::make_idesc_f16(128u, N, false, false);
+    for (uint32_t ks = 0; ks < K / 16u; ++ks) {
+        const uint64_t bd = umma::make_desc(b_saddr + ks * 256u, 128u, 128u * b_cpr);
+        umma::mma_f16_ta(d_tmem, a_tmem + ks * 8u, bd, idesc, ks > 0 ? 1u : 0u);
+    }
+}
+
+// Store 8*NCHUNK fp32 values of this thread's row (ReLU optional) as fp16 into its TMEM lane,
+// from column col on (two values per column, the even one low): the A operand of the next
+// layer's MMA.  NCHUNK is 4 or 8 (16 or 32 columns).  Waits for its own stores.
+template <uint32_t NCHUNK, bool RELU>
+__device__ __forceinline__ void store_row_tmem(uint32_t tmem, uint32_t col, const float* v) {
+    const uint32_t lane_base = (threadIdx.x & ~31u) << 16;
+#pragma unroll
+    for (uint32_t g = 0; g < NCHUNK / 4; ++g) {
+        uint32_t r[16];
+#pragma unroll
+        for (uint32_t j = 0; j < 16; ++j) r[j] = RELU ? pack2_relu(v[g * 32 + 2 * j], v[g * 32 + 2 * j + 1]) : pack2(v[g * 32 + 2 * j], v[g * 32 + 2 * j + 1]);
+        umma::tmem_st16(tmem + lane_base + col + g * 16u, r);
+    }
+    umma::tmem_wait_st();
+}
+
+// Store a row of 32 fp16 values (already rounded) into this thread's TMEM lane at column col.
+__device__ __forceinline__ void store_half32_tmem(uint32_t tmem, uint32_t col, const unsigned short* x) {
+    uint32_t r[16];
+#pragma unroll
+    for (uint32_t j = 0; j < 16; ++j) r[j] = x[2 * j] | (static_cast<uint32_t>(x[2 * j + 1]) << 16);
+    umma::tmem_st16(tmem + ((threadIdx.x & ~31u) << 16) + col, r);
+    umma::tmem_wait_st();
+}
+
+// All threads' TMEM stores (or reads) are complete before the MMA issued after it.
+__device__ __forceinline__ void stage_sync_tmem() {
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
 }
 
 // Degree-4 SH of dir = 2 * warped - 1 (ngp.train.cu:962-993), one IEEE operation at a time with
@@ -231,20 +287,25 @@ struct MlpForwardParams {
 
 enum : int { kModeFull = 0, kModeDensity = 1 };
 
-constexpr uint32_t kFwdTmemCols = 128;  // D0: cols 0-63, D1: cols 64-79
-// weights | input tile 0 | input tile 1 (row-major inputs: the next tile's copies land here) | hidden
-constexpr uint32_t kFwdSmem     = kSWeights + 8192 + 8192 + 16384 + 1024;
+// TMEM columns: D0 (64-wide accumulator) 0-63, D1 (16-wide) 64-79, and the A operand of the
+// hidden layers (128 rows x up to 64 fp16 = 32 columns) at kFwdA: activations never pass
+// through shared memory.
+constexpr uint32_t kFwdTmemCols = 128, kFwdA = 96;
+// weights | input tile 0 | input tile 1 (row-major inputs: the next tile's copies land here)
+constexpr uint32_t kFwdSmem     = kSWeights + 8192 + 8192 + 1024;
 
 template <int MODE, bool XROWS>
-__global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
+__global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* sw    = smem;                      // weights
-    unsigned char* sxb[2] = {smem + kSWeights, smem + kSWeights + 8192};  // 128 x 32 input tiles (X, then rgb input)
-    unsigned char* shd   = smem + kSWeights + 16384;  // 128 x 64 hidden tile
+    // row-major inputs: two 128 x 32 input tiles, tile b at sxb(b) (an offset, not an indexed
+    // array, so the choice stays in registers)
+    auto sxb = [&](uint32_t b) { return smem + kSWeights + (b & 1u) * 8192u; };
     __shared__ uint64_t mbar;
     __shared__ uint32_t tmem_slot;
 
     const uint32_t t = threadIdx.x;
+    MLP_TRACE(0);
     load_weight_tile(sw + kSWdIn, p.params + kWdIn, 64, 32);
     load_weight_tile(sw + kSWdOut, p.params + kWdOut, 16, 64);
     if (MODE == kModeFull) {
@@ -252,14 +313,7 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
         load_weight_tile(sw + kSWrH, p.params + kWrH, 64, 64);
         load_weight_tile(sw + kSWrOut, p.params + kWrOut, 16, 64);
     }
-    if (t < 32) umma::tmem_alloc(&tmem_slot, kFwdTmemCols);
-    if (t == 0) umma::mbar_init(&mbar, 1);
-    stage_sync();
-    const uint32_t tmem = tmem_slot;
-    const uint32_t d0 = tmem, d1 = tmem + 64;
-    const uint32_t a_shd = umma::smem_addr(shd), a_sw = umma::smem_addr(sw);
-    uint32_t phase  = 0;
-    bool ok         = true;
+    cp_async_commit();  // the weights: waited for with the first tile's inputs
     const uint32_t n       = p.n_dev != nullptr ? min(*p.n_dev, p.n) : p.n;
     const uint32_t n_tiles = (n + kRows - 1) / kRows;
 
@@ -267,45 +321,62 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
     // pipelining of the only global-memory reads of the loop).
     // Row-major inputs (XROWS) arrive by cp.async one tile ahead into the other input buffer;
     // feature-major inputs are gathered into registers one tile ahead and stored here.
+    // The first tile's loads are in flight with the weights' during the set-up below.
     RowInputs<MODE == kModeFull, XROWS> cur, nxt;
     if (blockIdx.x < n_tiles) {
         load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, blockIdx.x * kRows + t, cur, p.rows);
-        if constexpr (XROWS) issue_row_copy(sxb[0], t, p.x, cur.col, blockIdx.x * kRows + t < n);
+        if constexpr (XROWS) issue_row_copy(sxb(0), t, p.x, cur.col, blockIdx.x * kRows + t < n);
     }
+    if (t < 32) umma::tmem_alloc(&tmem_slot, kFwdTmemCols);
+    if (t == 0) umma::mbar_init(&mbar, 1);
+    stage_sync();
+    MLP_TRACE(1);
+    const uint32_t tmem = tmem_slot;
+    const uint32_t d0 = tmem, d1 = tmem + 64;
+    const uint32_t a_act = tmem + kFwdA, a_sw = umma::smem_addr(sw);
+    uint32_t phase  = 0;
+    bool ok         = true;
     uint32_t it = 0;
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row   = tile * kRows + t;
         const bool valid     = row < n;
-        unsigned char* sx    = XROWS ? sxb[it & 1u] : sxb[0];
-        const uint32_t a_sx  = umma::smem_addr(sx);
+        const uint32_t a_sx  = umma::smem_addr(sxb(it));  // row-major inputs only
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
-            if constexpr (XROWS) issue_row_copy(sxb[(it + 1u) & 1u], t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
+            if constexpr (XROWS) issue_row_copy(sxb(it + 1u), t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
         } else if constexpr (XROWS) {
             cp_async_commit();  // an empty group keeps the wait count below uniform
         }
         // ---- input row: 32 fp16 features ----
         if constexpr (XROWS)
             cp_async_wait<1>();  // this tile's copies (all but the group just issued) have landed
-        else
-            store_row_half32(sx, t, cur.x);
+        else {
+            cp_async_wait<0>();  // the weights (first tile only; later tiles have none pending)
+            store_half32_tmem(tmem, kFwdA, cur.x);
+        }
+        MLP_TRACE(2 + it * 8);
         stage_sync();
         if (t == 0) {
-            gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
+            if constexpr (XROWS)
+                gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
+            else
+                gemm_ta(d0, 64, 32, a_act, a_sw + kSWdIn, 4);
             umma::commit(&mbar);
         }
         ok = stage_wait(&mbar, phase);
+        MLP_TRACE(2 + it * 8 + 1);
         {
             float h[64];
             read_acc<64>(tmem, 0, h);
-            store_row<8, true>(shd, t, h);
+            store_row_tmem<8, true>(tmem, kFwdA, h);
         }
-        stage_sync();
+        stage_sync_tmem();
         if (t == 0) {
-            gemm(d1, 16, 64, a_shd, false, 8, a_sw + kSWdOut, false, 8, false);
+            gemm_ta(d1, 16, 64, a_act, a_sw + kSWdOut, 8);
             umma::commit(&mbar);
         }
         ok = ok && stage_wait(&mbar, phase);
+        MLP_TRACE(2 + it * 8 + 2);
         float dens[16];
         read_acc<16>(tmem, 64, dens);
         if (MODE == kModeDensity) {
@@ -326,39 +397,42 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
                 ri[k]      = dens[k];
                 ri[16 + k] = sh[k];
             }
-            store_row<4, false>(sx, t, ri);
+            store_row_tmem<4, false>(tmem, kFwdA, ri);
             if (p.density_rgb_in != nullptr && valid)
 #pragma unroll
                 for (int k = 0; k < 16; ++k) p.density_rgb_in[static_cast<uint64_t>(k) * p.x_stride + cur.col] = __float2half_rn(dens[k]);
         }
-        stage_sync();
+        stage_sync_tmem();
         if (t == 0) {
-            gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWrIn, false, 4, false);
+            gemm_ta(d0, 64, 32, a_act, a_sw + kSWrIn, 4);
             umma::commit(&mbar);
         }
         ok = ok && stage_wait(&mbar, phase);
+        MLP_TRACE(2 + it * 8 + 3);
         {
             float h[64];
             read_acc<64>(tmem, 0, h);
-            store_row<8, true>(shd, t, h);
+            store_row_tmem<8, true>(tmem, kFwdA, h);
         }
-        stage_sync();
+        stage_sync_tmem();
         if (t == 0) {
-            gemm(d0, 64, 64, a_shd, false, 8, a_sw + kSWrH, false, 8, false);
+            gemm_ta(d0, 64, 64, a_act, a_sw + kSWrH, 8);
             umma::commit(&mbar);
         }
         ok = ok && stage_wait(&mbar, phase);
+        MLP_TRACE(2 + it * 8 + 4);
         {
             float h[64];
             read_acc<64>(tmem, 0, h);
-            store_row<8, true>(shd, t, h);  // the layer-2 MMA that read shd has completed
+            store_row_tmem<8, true>(tmem, kFwdA, h);  // the layer-2 MMA that read them has completed
         }
-        stage_sync();
+        stage_sync_tmem();
         if (t == 0) {
-            gemm(d1, 16, 64, a_shd, false, 8, a_sw + kSWrOut, false, 8, false);
+            gemm_ta(d1, 16, 64, a_act, a_sw + kSWrOut, 8);
             umma::commit(&mbar);
         }
         ok = ok && stage_wait(&mbar, phase);
+        MLP_TRACE(2 + it * 8 + 5);
         float o[16];
         read_acc<16>(tmem, 64, o);
         o[3] = dens[0];
@@ -368,15 +442,17 @@ __global__ void __launch_bounds__(kThreads) mlp_forward_kernel(const __grid_cons
             dst[1]     = make_uint4(pack2(o[8], o[9]), pack2(o[10], o[11]), pack2(o[12], o[13]), pack2(o[14], o[15]));
         }
         cur = nxt;
+        MLP_TRACE(2 + it * 8 + 7);
         // a timed-out wait anywhere in the CTA ends the loop for every thread together
         umma::fence_before_sync();
         if (!__syncthreads_and(ok)) break;
         umma::fence_after_sync();
     }
-    if constexpr (XROWS) cp_async_wait<0>();  // no copy may still target shared memory at exit
+    cp_async_wait<0>();  // no copy (weights or inputs) may still target shared memory at exit
     umma::fence_before_sync();
     __syncthreads();
     if (t < 32) umma::tmem_dealloc(tmem, kFwdTmemCols);
+    MLP_TRACE(63);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -417,8 +493,24 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
     load_weight_tile(smem + kSWrIn, p.params + kWrIn, 64, 32);
     load_weight_tile(smem + kSWrH, p.params + kWrH, 64, 64);
     load_weight_tile(smem + kSWrOut, p.params + kWrOut, 16, 64);
+    cp_async_commit();  // the weights: waited for with the first tile's inputs
     // the padded (M = 128) weight-gradient GEMMs read up to 2 KB past the last activation tile
     for (uint32_t i = t; i < 4096 / 16; i += kThreads) reinterpret_cast<uint4*>(smem + kBGuard)[i] = make_uint4(0, 0, 0, 0);
+    const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
+
+    // next tile's inputs (features, direction, output gradient) prefetched during this tile; the
+    // first tile's loads are in flight with the weights' during the set-up below
+    RowInputs<true, XROWS> cur, nxt;
+    uint2 dy_cur = make_uint2(0, 0), dy_nxt = make_uint2(0, 0);
+    auto load_dy = [&](uint32_t r) {
+        return r < p.n ? __ldg(reinterpret_cast<const uint2*>(p.dy + static_cast<uint64_t>(r) * 16u)) : make_uint2(0, 0);
+    };
+    auto xbuf = [&](uint32_t b) { return smem + ((b & 1u) ? kBX2 : kBX); };
+    if (blockIdx.x < n_tiles) {
+        load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur, p.rows);
+        if constexpr (XROWS) issue_row_copy(xbuf(0), t, p.x, cur.col, blockIdx.x * kRows + t < p.n);
+        dy_cur = load_dy(blockIdx.x * kRows + t);
+    }
     if (t < 32) umma::tmem_alloc(&tmem_slot, kBwdTmemCols);
     if (t == 0) umma::mbar_init(&mbar, 1);
     stage_sync();
@@ -427,20 +519,6 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
     uint32_t phase      = 0;
     bool ok             = true;
     bool first          = true;
-    const uint32_t n_tiles = (p.n + kRows - 1) / kRows;
-
-    // next tile's inputs (features, direction, output gradient) prefetched during this tile
-    RowInputs<true, XROWS> cur, nxt;
-    uint2 dy_cur = make_uint2(0, 0), dy_nxt = make_uint2(0, 0);
-    auto load_dy = [&](uint32_t r) {
-        return r < p.n ? __ldg(reinterpret_cast<const uint2*>(p.dy + static_cast<uint64_t>(r) * 16u)) : make_uint2(0, 0);
-    };
-    unsigned char* xbuf[2] = {smem + kBX, smem + kBX2};
-    if (blockIdx.x < n_tiles) {
-        load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, blockIdx.x * kRows + t, cur, p.rows);
-        if constexpr (XROWS) issue_row_copy(xbuf[0], t, p.x, cur.col, blockIdx.x * kRows + t < p.n);
-        dy_cur = load_dy(blockIdx.x * kRows + t);
-    }
     uint32_t it = 0;
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row = tile * kRows + t;
@@ -448,7 +526,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         const uint32_t bx  = XROWS && (it & 1u) ? kBX2 : kBX;  // this tile's input tile
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, p.n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
-            if constexpr (XROWS) issue_row_copy(xbuf[(it + 1u) & 1u], t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < p.n);
+            if constexpr (XROWS) issue_row_copy(xbuf(it + 1u), t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < p.n);
             dy_nxt = load_dy((tile + gridDim.x) * kRows + t);
         } else if constexpr (XROWS) {
             cp_async_commit();  // an empty group keeps the wait count below uniform
@@ -456,8 +534,10 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         // ---------------- forward recompute ----------------
         if constexpr (XROWS)
             cp_async_wait<1>();  // this tile's copies have landed
-        else
+        else {
+            cp_async_wait<0>();  // the weights (first tile only; later tiles have none pending)
             store_row_half32(smem + kBX, t, cur.x);
+        }
         float g[16];
         {
             // rgb output gradient: channels 0-2 (extract_rgb_gradients, ngp.train.cu:1244-1253)
@@ -624,7 +704,7 @@ __global__ void __launch_bounds__(kThreads) mlp_backward_kernel(const __grid_con
         umma::fence_after_sync();
     }
 
-    if constexpr (XROWS) cp_async_wait<0>();  // no copy may still target shared memory
+    cp_async_wait<0>();  // no copy (weights or inputs) may still target shared memory
     // ---- write this CTA's weight-gradient partial (rows 0-63 of the M = 128 accumulators) ----
     umma::fence_before_sync();
     __syncthreads();

@@ -417,8 +417,11 @@ def test_training_loss_vs_reference_kernel(ngp, reflib, small_scene, blob_bitfie
 def test_density_first_flow_matches_loss_and_compact(ngp, small_scene, blob_bitfield):
     """The trainer's density-first flow (density network on every sample, compaction, full network
     on the compacted rows, loss) against the one-pass entry point given the full network's
-    outputs: counts, compacted records, encodings (after padding), gradients and losses
-    bit-identical, including the ray that straddles the end of the 2^18 batch."""
+    outputs: counts, compacted records and encodings (after padding) bit-identical, including the
+    ray that straddles the end of the 2^18 batch; losses and output gradients equal up to the
+    association of the compositing sums (the one-pass kernel walks each ray in one warp, the
+    compacted one splits long rays across warps and scans each chunk): 1e-5 relative on the
+    loss, 2e-3 relative on the fp16 gradients, as against the reference kernel."""
     import torch
 
     pix, cam, tr = _scene_tensors(small_scene)
@@ -480,8 +483,9 @@ def test_density_first_flow_matches_loss_and_compact(ngp, small_scene, blob_bitf
     kept = ns_a.cpu().numpy()[:, 0]
     assert 0 < (kept > 0).sum() < n  # rays beyond the batch end were dropped
     assert ccoords_a.cpu().numpy().tobytes() == ccoords_b[:batch].cpu().numpy().tobytes()
-    assert dloss_a.cpu().numpy().view(np.uint16).tobytes() == dloss_b.cpu().numpy().view(np.uint16).tobytes()
-    assert loss_a.cpu().numpy().tobytes() == loss_b.cpu().numpy().tobytes()
+    x, y = dloss_a.float().cpu().numpy(), dloss_b.float().cpu().numpy()
+    assert (np.abs(x - y) <= 2e-3 * np.abs(y) + 1e-7).all()
+    np.testing.assert_allclose(loss_a.cpu().numpy(), loss_b.cpu().numpy(), rtol=1e-5, atol=1e-9)
     assert cenc_a.cpu().numpy().view(np.uint16).tobytes() == cenc_b[:, :batch].cpu().numpy().view(np.uint16).tobytes()
     # some rays stopped early (transmittance), so the flow's keep decision was exercised
     steps = ns.cpu().numpy()[:, 0]
