@@ -143,6 +143,7 @@ __global__ void grad_to_half_kernel(uint32_t n, float* __restrict__ src, __half*
 // (the data-parallel hook between backward_network and step_optimizer, ngp.train.cpp:123-124).
 // ---------------------------------------------------------------------------------------------
 constexpr uint32_t kExchangeThreads = 256;
+constexpr uint32_t kExchangeUnroll  = 8;  // ranks whose loads are unrolled (more: a loop)
 constexpr uint64_t kExchangeWaitNs  = 2000000000ull;  // 2 s per cross-GPU wait, then an error status
 
 __device__ __forceinline__ void store_release_sys(uint32_t* addr, uint32_t v) {
@@ -190,23 +191,58 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_exchange_adam_kernel(co
         p.inv_loss_scale = 1.0f / a.loss_scale, p.lr_table = a.lr_table, p.table_len = a.table_len, p.first = 0;
         const uint32_t first = a.rank * a.shard;
         const uint32_t end   = min(first + a.shard, a.n_params);
-        for (uint32_t i0 = first + (blockIdx.x * kExchangeThreads + threadIdx.x) * 4u; i0 < end; i0 += gridDim.x * kExchangeThreads * 4u) {
-            // the shard's gradient: the ranks' fp16 sums added in rank order (fp32)
-            float g[4] = {0.f, 0.f, 0.f, 0.f};
-            for (uint32_t q = 0; q < a.world; ++q) {
-                const uint2 raw  = *reinterpret_cast<const uint2*>(a.grads[q] + i0);
-                const float2 lo  = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-                const float2 hi  = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-                g[0] += lo.x, g[1] += lo.y, g[2] += hi.x, g[3] += hi.y;
+        // eight parameters per thread and iteration: one 16-byte load per rank, all ranks' loads
+        // in flight before the (rank-ordered) sum
+        for (uint32_t i0 = first + (blockIdx.x * kExchangeThreads + threadIdx.x) * 8u; i0 < end; i0 += gridDim.x * kExchangeThreads * 8u) {
+            float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            auto add = [&](const uint4& raw) {
+                const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+                for (uint32_t k = 0; k < 4; ++k) {
+                    const float2 f = __half22float2(h[k]);
+                    g[2 * k] += f.x, g[2 * k + 1] += f.y;
+                }
+            };
+            if (a.world <= kExchangeUnroll) {
+                uint4 raw[kExchangeUnroll];
+#pragma unroll
+                for (uint32_t q = 0; q < kExchangeUnroll; ++q)
+                    if (q < a.world) raw[q] = __ldcg(reinterpret_cast<const uint4*>(a.grads[q] + i0));
+#pragma unroll
+                for (uint32_t q = 0; q < kExchangeUnroll; ++q)
+                    if (q < a.world) add(raw[q]);
+            } else {
+                for (uint32_t q = 0; q < a.world; ++q) add(__ldcg(reinterpret_cast<const uint4*>(a.grads[q] + i0)));
             }
             const bool grid = i0 >= a.n_mlp;
-            if (grid && g[0] == 0.0f && g[1] == 0.0f && g[2] == 0.0f && g[3] == 0.0f) continue;  // untouched: params unchanged everywhere
-            const uint32_t cnt = min(4u, end - i0);
-            uint2 hv           = *reinterpret_cast<const uint2*>(a.params[a.rank] + i0);
-            __half* h          = reinterpret_cast<__half*>(&hv);
-            for (uint32_t k = 0; k < cnt; ++k) adam_one(p, i0 + k, a.master[i0 + k], g[k], a.m[i0 + k], a.v[i0 + k], a.steps[i0 + k], h[k]);
+            bool zero       = true;
+#pragma unroll
+            for (uint32_t k = 0; k < 8; ++k) zero = zero && g[k] == 0.0f;
+            if (grid && zero) continue;  // untouched: params unchanged everywhere
+            uint4 hv  = *reinterpret_cast<const uint4*>(a.params[a.rank] + i0);
+            __half* h = reinterpret_cast<__half*>(&hv);
+            if (i0 + 8u <= end) {
+                float4* w4 = reinterpret_cast<float4*>(a.master + i0);
+                float4* m4 = reinterpret_cast<float4*>(a.m + i0);
+                float4* v4 = reinterpret_cast<float4*>(a.v + i0);
+                uint4* s4  = reinterpret_cast<uint4*>(a.steps + i0);
+                float4 w[2] = {w4[0], w4[1]}, m[2] = {m4[0], m4[1]}, v[2] = {v4[0], v4[1]};
+                uint4 st[2] = {s4[0], s4[1]};
+#pragma unroll
+                for (uint32_t k = 0; k < 2; ++k) {
+                    adam_one(p, i0 + 4u * k + 0u, w[k].x, g[4 * k + 0], m[k].x, v[k].x, st[k].x, h[4 * k + 0]);
+                    adam_one(p, i0 + 4u * k + 1u, w[k].y, g[4 * k + 1], m[k].y, v[k].y, st[k].y, h[4 * k + 1]);
+                    adam_one(p, i0 + 4u * k + 2u, w[k].z, g[4 * k + 2], m[k].z, v[k].z, st[k].z, h[4 * k + 2]);
+                    adam_one(p, i0 + 4u * k + 3u, w[k].w, g[4 * k + 3], m[k].w, v[k].w, st[k].w, h[4 * k + 3]);
+                }
+                w4[0] = w[0], w4[1] = w[1], m4[0] = m[0], m4[1] = m[1], v4[0] = v[0], v4[1] = v[1], s4[0] = st[0], s4[1] = st[1];
+            } else {
+#pragma unroll
+                for (uint32_t k = 0; k < 8; ++k)
+                    if (i0 + k < end) adam_one(p, i0 + k, a.master[i0 + k], g[k], a.m[i0 + k], a.v[i0 + k], a.steps[i0 + k], h[k]);
+            }
             // all-gather: the new parameters go to every rank's buffer
-            for (uint32_t q = 0; q < a.world; ++q) *reinterpret_cast<uint2*>(a.params[q] + i0) = hv;
+            for (uint32_t q = 0; q < a.world; ++q) *reinterpret_cast<uint4*>(a.params[q] + i0) = hv;
         }
     }
     // completion: after every CTA's writes, the last CTA tells every rank and waits for them all
@@ -225,9 +261,9 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_exchange_adam_kernel(co
 }  // namespace
 
 int peer_exchange_adam(const PeerExchangeArgs& a, cudaStream_t stream) {
-    const uint32_t groups = (a.shard + 3u) / 4u;
+    const uint32_t groups = (a.shard + 7u) / 8u;
     uint32_t ctas         = (groups + kExchangeThreads - 1u) / kExchangeThreads;
-    const uint32_t cap    = static_cast<uint32_t>(sm_count()) * 4u;
+    const uint32_t cap    = static_cast<uint32_t>(sm_count()) * 2u;  // two resident CTAs per SM (102 registers a thread)
     ctas                  = ctas < 1u ? 1u : (ctas > cap ? cap : ctas);
     peer_exchange_adam_kernel<<<ctas, kExchangeThreads, 0, stream>>>(a);
     return check_launch("peer_exchange_adam_kernel");

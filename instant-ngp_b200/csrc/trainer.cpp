@@ -934,8 +934,9 @@ extern "C" int ngp_trainer_join(ngp_trainer* t, const uint8_t* unique_id, int wo
     if (t->comm != nullptr) return fail(NGP_ERR_STATE, "trainer join: already joined");
     if (world == 1) return NGP_OK;
     // padded exchange buffers: the fp16 parameters and gradients hold n_padded entries so that
-    // every rank's shard has the same length (a multiple of 4 for Adam's vector loads)
-    const uint64_t unit   = 4ull * static_cast<uint64_t>(world);
+    // every rank's shard has the same length (a multiple of 8: the exchange kernel moves 16-byte
+    // groups of fp16 values)
+    const uint64_t unit   = 8ull * static_cast<uint64_t>(world);
     const uint64_t padded = (static_cast<uint64_t>(t->n_params) + unit - 1u) / unit * unit;
     if (padded > 0xFFFFFFFFull) return fail(NGP_ERR_INVALID, "trainer join: too many parameters for the exchange");
     uint16_t *params = nullptr, *grads16 = nullptr;
