@@ -317,12 +317,12 @@ constexpr uint32_t kRaysPerCta = kCtaThreads / kMarchGroup;
 #endif
 constexpr uint32_t kWideMarchThreadsPerSm = NGP_WIDE_MARCH_THREADS;
 
-template <uint32_t G>
-__global__ void __launch_bounds__(kRaysPerCta * G) march_count_kernel(const __grid_constant__ MarchParams p) {
-    __shared__ uint32_t s_steps[kRaysPerCta];
+template <uint32_t G, uint32_t RPC>
+__global__ void __launch_bounds__(RPC * G) march_count_kernel(const __grid_constant__ MarchParams p) {
+    __shared__ uint32_t s_steps[RPC];
     const uint32_t n    = march_ray_count(p);
     const uint32_t slot = threadIdx.x / G, g = threadIdx.x % G;
-    const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
+    const uint32_t i    = blockIdx.x * RPC + slot;
     TrainRay r{};
     const bool active    = i < n && setup_ray(p, i, n, r);
     uint32_t n_runs;
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kRaysPerCta * G) march_count_kernel(const __gr
     __syncthreads();
     if (threadIdx.x < 32) {
         uint32_t total = 0;
-        for (uint32_t w = threadIdx.x; w < kRaysPerCta; w += 32) total += s_steps[w];
+        for (uint32_t w = threadIdx.x; w < RPC; w += 32) total += s_steps[w];
 #pragma unroll
         for (uint32_t o = 16; o > 0; o >>= 1) total += __shfl_down_sync(0xFFFFFFFFu, total, o);
         if (threadIdx.x == 0) p.block_totals[blockIdx.x] = total;
@@ -365,13 +365,13 @@ __global__ void __launch_bounds__(1024) scan_totals_kernel(uint32_t* __restrict_
     }
 }
 
-template <uint32_t G>
-__global__ void __launch_bounds__(kRaysPerCta * G) march_write_kernel(const __grid_constant__ MarchParams p) {
-    __shared__ uint32_t s_base[kRaysPerCta];
-    __shared__ float s_stage[kRaysPerCta * G * 7u];  // per warp: 32 staged sample records
+template <uint32_t G, uint32_t RPC>
+__global__ void __launch_bounds__(RPC * G) march_write_kernel(const __grid_constant__ MarchParams p) {
+    __shared__ uint32_t s_base[RPC];
+    __shared__ float s_stage[RPC * G * 7u];  // per warp: 32 staged sample records
     const uint32_t n    = march_ray_count(p);
     const uint32_t slot = threadIdx.x / G, g = threadIdx.x % G;
-    const uint32_t i    = blockIdx.x * kRaysPerCta + slot;
+    const uint32_t i    = blockIdx.x * RPC + slot;
     // this ray's first sample: CTA base + counts of the CTA's earlier rays (exclusive scan)
     const uint32_t steps  = i < n ? p.numsteps[2u * i] : 0u;
     const uint32_t n_runs = i < n ? p.numsteps[2u * i + 1u] : 0u;
@@ -502,28 +502,34 @@ __global__ void eval_rays_kernel(const CameraSet cam, uint32_t image, uint32_t p
 
 uint32_t march_blocks(uint32_t n_rays) { return (n_rays + kRaysPerCta - 1) / kRaysPerCta; }
 
-// Scratch: per-CTA totals, then (8-byte aligned) kMaxRuns run records per ray.
-uint64_t march_scratch_words(uint32_t n_rays) { return ((march_blocks(n_rays) + 1ull) & ~1ull) + 2ull * kMaxRuns * n_rays; }
+// The wide training march (32 lanes per ray) runs kWideRaysPerCta rays per 256-thread CTA: small
+// CTAs, so that an SM is not held by one CTA waiting for its longest ray.
+constexpr uint32_t kWideRaysPerCta = 8;
+uint32_t wide_march_blocks(uint32_t n_rays) { return (n_rays + kWideRaysPerCta - 1) / kWideRaysPerCta; }
+
+// Scratch: per-CTA totals (room for the wide march's count), then (8-byte aligned) kMaxRuns run
+// records per ray.
+uint64_t march_scratch_words(uint32_t n_rays) { return ((wide_march_blocks(n_rays) + 1ull) & ~1ull) + 2ull * kMaxRuns * n_rays; }
 
 int launch_march(MarchParams p, uint32_t* scratch, cudaStream_t s) {
-    const uint32_t blocks = march_blocks(p.n_rays);
-    p.block_totals        = scratch;
-    p.runs                = reinterpret_cast<uint2*>(scratch + ((blocks + 1u) & ~1u));
     // Few rays (the first training steps march ~4096 long rays): a whole warp per ray instead of
     // kMarchGroup lanes, so that the SMs have enough warps to hide each round's latency.  The
     // positions are the sequential march's either way; only the speculation width differs.
     const bool wide = static_cast<uint64_t>(p.n_rays) * kMarchGroup < static_cast<uint64_t>(sm_count()) * kWideMarchThreadsPerSm;
+    const uint32_t blocks = wide ? wide_march_blocks(p.n_rays) : march_blocks(p.n_rays);
+    p.block_totals        = scratch;
+    p.runs                = reinterpret_cast<uint2*>(scratch + ((wide_march_blocks(p.n_rays) + 1u) & ~1u));
     if (wide)
-        march_count_kernel<32><<<blocks, kRaysPerCta * 32u, 0, s>>>(p);
+        march_count_kernel<32, kWideRaysPerCta><<<blocks, kWideRaysPerCta * 32u, 0, s>>>(p);
     else
-        march_count_kernel<kMarchGroup><<<blocks, kCtaThreads, 0, s>>>(p);
+        march_count_kernel<kMarchGroup, kRaysPerCta><<<blocks, kCtaThreads, 0, s>>>(p);
     NGP_TRY(check_launch("march_count_kernel"));
     scan_totals_kernel<<<1, 1024, 0, s>>>(p.block_totals, blocks, p.n_rays_dev, p.n_rays, p.sample_counter, p.ray_counter);
     NGP_TRY(check_launch("scan_totals_kernel"));
     if (wide)
-        march_write_kernel<32><<<blocks, kRaysPerCta * 32u, 0, s>>>(p);
+        march_write_kernel<32, kWideRaysPerCta><<<blocks, kWideRaysPerCta * 32u, 0, s>>>(p);
     else
-        march_write_kernel<kMarchGroup><<<blocks, kCtaThreads, 0, s>>>(p);
+        march_write_kernel<kMarchGroup, kRaysPerCta><<<blocks, kCtaThreads, 0, s>>>(p);
     return check_launch("march_write_kernel");
 }
 

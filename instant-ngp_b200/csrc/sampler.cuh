@@ -74,6 +74,35 @@ __device__ __forceinline__ float skip_empty_voxel(float t, float3 pos, float3 di
     return __fmaf_rn(ceilf(fmaxf((t_target - t) / kConeStep, 0.5f)), kConeStep, t);
 }
 
+// t after k sequential additions of kConeStep (((t + dt) + dt) + ...), the march's step rule.
+// Inside one binade [2^E, 2^(E+1)) every addition to a value on that binade's grid (spacing u)
+// adds the same rounded increment d = round(dt / u) * u (round to nearest; a tie, where the
+// rounding would depend on the parity, is excluded), so while every partial sum stays below
+// 2^(E+1) the k-th value is exactly t + k * d, one fused multiply-add.  Otherwise (the sum
+// crosses a power of two, or t is tiny) the additions run one by one.  Bit-identical to the loop.
+// (the plain loop: cheaper for the few additions of a narrow group)
+__device__ __forceinline__ float cone_steps_loop(float t, uint32_t k) {
+    for (uint32_t j = 0; j < k; ++j) t += kConeStep;
+    return t;
+}
+
+__device__ __forceinline__ float cone_steps(float t, uint32_t k) {
+    const uint32_t e = __float_as_uint(t) & 0x7F800000u;
+    if (k != 0 && t > 0.0f && e >= (24u << 23) && e < 0x7F000000u) {
+        const float u   = __uint_as_float(e - (23u << 23));  // 2^(E-23)
+        const float top = __uint_as_float(e + (1u << 23));   // 2^(E+1)
+        const float m   = kConeStep / u;                      // exact: u is a power of two
+        const float mf  = floorf(m), fr = m - mf;
+        if (fr != 0.5f && m < 8388608.0f) {
+            const float d    = (fr > 0.5f ? mf + 1.0f : mf) * u;
+            const float last = __fmaf_rn(static_cast<float>(k), d, t);
+            if (last + u <= top) return last;
+        }
+    }
+    for (uint32_t j = 0; j < k; ++j) t += kConeStep;
+    return t;
+}
+
 __device__ __forceinline__ float3 ray_point(float3 o, float3 d, float t) {
     return {__fmaf_rn(d.x, t, o.x), __fmaf_rn(d.y, t, o.y), __fmaf_rn(d.z, t, o.z)};
 }
@@ -249,7 +278,7 @@ __device__ __forceinline__ MarchRound group_march_round(GroupMarch& m, const uin
     if (skip_mode) {
         for (uint32_t j = 0; j < g; ++j) tk = skip_empty_voxel(tk, ray_point(m.o, m.d, tk), m.d, m.inv);
     } else {
-        for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
+        tk = G > 8u ? cone_steps(tk, g) : cone_steps_loop(tk, g);
     }
     MarchRound r;
     r.pos                = ray_point(m.o, m.d, tk);
@@ -412,7 +441,7 @@ __device__ __forceinline__ void group_expand_runs(float3 d_unit, float3 o, const
     }
     while (__any_sync(0xFFFFFFFFu, active)) {
         float tk = t;
-        for (uint32_t j = 0; j < g; ++j) tk += kConeStep;
+        tk = G > 8u ? cone_steps(tk, g) : cone_steps_loop(tk, g);
         const float t_last = __shfl_sync(0xFFFFFFFFu, tk, group_lo + G - 1u);
         const uint32_t adv = active ? min(min(G, cnt - in_run), n - written) : 0u;
         if (g < adv) {
