@@ -81,6 +81,21 @@ __device__ __forceinline__ void issue_row_copy(unsigned char* tile, uint32_t r, 
     cp_async_commit();
 }
 
+// Feature-major inputs of contiguous rows ([32][x_stride] fp16, no row list): feature k of the
+// tile's rows r0 .. r0 + 127 is one 256-byte run, copied as 16 chunks of 16 bytes into the
+// tile as the MN-major A operand (tile row k, the 128 rows along it: chunk (k, c) at
+// tile_off(k, c, 16)); rows past n are zero-filled.  Four copies per thread, one commit group.
+__device__ __forceinline__ void issue_col_copy(unsigned char* tile, const __half* x, uint32_t x_stride, uint32_t r0, uint32_t n) {
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t q = threadIdx.x + j * 128u, k = q >> 4, c = q & 15u;
+        const uint32_t first = r0 + c * 8u;
+        const uint32_t bytes = first < n ? min(8u, n - first) * 2u : 0u;
+        cp_async16(tile + tile_off(k, c, 16), x + static_cast<uint64_t>(k) * x_stride + (bytes ? first : 0u), bytes);
+    }
+    cp_async_commit();
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
@@ -250,7 +265,7 @@ __device__ __forceinline__ bool stage_wait(uint64_t* mbar, uint32_t& phase) {
 // read and written at that sample's position.
 template <bool DIR, bool XROWS = false>
 struct RowInputs {
-    unsigned short x[XROWS ? 1 : 32];  // feature-major inputs only (row-major rows arrive by cp.async)
+    unsigned short x[XROWS ? 1 : 32];  // register-gathered inputs only (none when the tile arrives by cp.async)
     float dir[DIR ? 3 : 1];
     uint32_t col;  // the sample this row reads and writes
 };
@@ -286,6 +301,9 @@ struct MlpForwardParams {
 };
 
 enum : int { kModeFull = 0, kModeDensity = 1 };
+// how a forward kernel reads its inputs: feature-major through registers (any row list),
+// row-major by cp.async, or feature-major contiguous rows by cp.async
+enum : int { kXRegs = 0, kXRows = 1, kXCols = 2 };
 
 // TMEM columns: D0 (64-wide accumulator) 0-63, D1 (16-wide) 64-79, and the A operand of the
 // hidden layers (128 rows x up to 64 fp16 = 32 columns) at kFwdA: activations never pass
@@ -294,11 +312,13 @@ constexpr uint32_t kFwdTmemCols = 128, kFwdA = 96;
 // weights | input tile 0 | input tile 1 (row-major inputs: the next tile's copies land here)
 constexpr uint32_t kFwdSmem     = kSWeights + 8192 + 8192 + 1024;
 
-template <int MODE, bool XROWS>
+template <int MODE, int XIN>
 __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
+    constexpr bool XROWS  = XIN == kXRows;
+    constexpr bool XASYNC = XIN != kXRegs;  // inputs staged by cp.async one tile ahead
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* sw    = smem;                      // weights
-    // row-major inputs: two 128 x 32 input tiles, tile b at sxb(b) (an offset, not an indexed
+    // cp.async inputs: two 128 x 32 input tiles, tile b at sxb(b) (an offset, not an indexed
     // array, so the choice stays in registers)
     auto sxb = [&](uint32_t b) { return smem + kSWeights + (b & 1u) * 8192u; };
     __shared__ uint64_t mbar;
@@ -319,13 +339,15 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
 
     // The next tile's inputs are loaded into registers while this tile's layers run (software
     // pipelining of the only global-memory reads of the loop).
-    // Row-major inputs (XROWS) arrive by cp.async one tile ahead into the other input buffer;
-    // feature-major inputs are gathered into registers one tile ahead and stored here.
+    // Row-major inputs (kXRows) and feature-major inputs of contiguous rows (kXCols) arrive by
+    // cp.async one tile ahead into the other input buffer; feature-major inputs of a row list
+    // (kXRegs) are gathered into registers one tile ahead.
     // The first tile's loads are in flight with the weights' during the set-up below.
-    RowInputs<MODE == kModeFull, XROWS> cur, nxt;
+    RowInputs<MODE == kModeFull, XASYNC> cur, nxt;
     if (blockIdx.x < n_tiles) {
         load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, blockIdx.x * kRows + t, cur, p.rows);
         if constexpr (XROWS) issue_row_copy(sxb(0), t, p.x, cur.col, blockIdx.x * kRows + t < n);
+        if constexpr (XIN == kXCols) issue_col_copy(sxb(0), p.x, p.x_stride, blockIdx.x * kRows, n);
     }
     if (t < 32) umma::tmem_alloc(&tmem_slot, kFwdTmemCols);
     if (t == 0) umma::mbar_init(&mbar, 1);
@@ -340,15 +362,16 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row   = tile * kRows + t;
         const bool valid     = row < n;
-        const uint32_t a_sx  = umma::smem_addr(sxb(it));  // row-major inputs only
+        const uint32_t a_sx  = umma::smem_addr(sxb(it));  // cp.async inputs only
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
             if constexpr (XROWS) issue_row_copy(sxb(it + 1u), t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
-        } else if constexpr (XROWS) {
+            if constexpr (XIN == kXCols) issue_col_copy(sxb(it + 1u), p.x, p.x_stride, (tile + gridDim.x) * kRows, n);
+        } else if constexpr (XASYNC) {
             cp_async_commit();  // an empty group keeps the wait count below uniform
         }
         // ---- input row: 32 fp16 features ----
-        if constexpr (XROWS)
+        if constexpr (XASYNC)
             cp_async_wait<1>();  // this tile's copies (all but the group just issued) have landed
         else {
             cp_async_wait<0>();  // the weights (first tile only; later tiles have none pending)
@@ -359,6 +382,8 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
         if (t == 0) {
             if constexpr (XROWS)
                 gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
+            else if constexpr (XIN == kXCols)
+                gemm(d0, 64, 32, a_sx, true, 16, a_sw + kSWdIn, false, 4, false);  // MN-major A
             else
                 gemm_ta(d0, 64, 32, a_act, a_sw + kSWdIn, 4);
             umma::commit(&mbar);
@@ -816,10 +841,11 @@ using namespace ngp;
 namespace {
 int ensure_attrs() {
     static int status = [] {
-        cudaError_t e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeFull, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_forward_kernel<kModeDensity, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+        cudaError_t e = cudaSuccess;
+        for (const void* f : {reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull, kXRegs>), reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity, kXRegs>),
+                              reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull, kXRows>), reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity, kXRows>),
+                              reinterpret_cast<const void*>(mlp_forward_kernel<kModeFull, kXCols>), reinterpret_cast<const void*>(mlp_forward_kernel<kModeDensity, kXCols>)})
+            if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(mlp_backward_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
         return static_cast<int>(e);
@@ -833,13 +859,20 @@ namespace {
 template <int MODE>
 int launch_forward(const MlpForwardParams& p, uint32_t n_rows, cudaStream_t stream, const char* what) {
     const uint32_t n_tiles = (n_rows + kRows - 1) / kRows;
-    if (rows_layout(p.x_stride)) {
-        const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<MODE, true>), n_tiles, kFwdTmemCols);
-        mlp_forward_kernel<MODE, true><<<grid, kThreads, kFwdSmem, stream>>>(p);
-    } else {
-        const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(mlp_forward_kernel<MODE, false>), n_tiles, kFwdTmemCols);
-        mlp_forward_kernel<MODE, false><<<grid, kThreads, kFwdSmem, stream>>>(p);
-    }
+    // feature-major inputs of contiguous rows go by cp.async when every 16-byte chunk is aligned
+    // (full network only: the density network's two layers were measured faster with the
+    // register gather, 2^20 rows 39.8 against 45.1 us)
+    const bool cols = MODE == kModeFull && !rows_layout(p.x_stride) && p.rows == nullptr && (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0u && p.x_stride % 8u == 0u;
+    auto run = [&](auto kernel) {
+        const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(kernel), n_tiles, kFwdTmemCols);
+        kernel<<<grid, kThreads, kFwdSmem, stream>>>(p);
+    };
+    if (rows_layout(p.x_stride))
+        run(mlp_forward_kernel<MODE, kXRows>);
+    else if (cols)
+        run(mlp_forward_kernel<MODE, kXCols>);
+    else
+        run(mlp_forward_kernel<MODE, kXRegs>);
     return check_launch(what);
 }
 }  // namespace
