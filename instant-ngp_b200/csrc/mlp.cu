@@ -309,18 +309,21 @@ enum : int { kXRegs = 0, kXRows = 1, kXCols = 2 };
 // hidden layers (128 rows x up to 64 fp16 = 32 columns) at kFwdA: activations never pass
 // through shared memory.
 constexpr uint32_t kFwdTmemCols = 128, kFwdA = 96;
-// weights | input tile 0 | input tile 1 (row-major inputs: the next tile's copies land here)
-constexpr uint32_t kFwdSmem     = kSWeights + 8192 + 8192 + 1024;
+// weights | a ring of up to four 8 KB input tiles (cp.async inputs: the next tiles' copies land there)
+constexpr uint32_t kFwdSmem     = kSWeights + 4 * 8192 + 1024;
 
 template <int MODE, int XIN>
 __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
     constexpr bool XROWS  = XIN == kXRows;
-    constexpr bool XASYNC = XIN != kXRegs;  // inputs staged by cp.async one tile ahead
+    constexpr bool XASYNC = XIN != kXRegs;  // inputs staged by cp.async
+    // tiles in flight ahead of the one computed: the density network's two layers take less time
+    // than a tile's DRAM reads, so its contiguous inputs are fetched three tiles ahead
+    constexpr uint32_t kAhead = (XIN == kXCols && MODE == kModeDensity) ? 3u : 1u;
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* sw    = smem;                      // weights
-    // cp.async inputs: two 128 x 32 input tiles, tile b at sxb(b) (an offset, not an indexed
-    // array, so the choice stays in registers)
-    auto sxb = [&](uint32_t b) { return smem + kSWeights + (b & 1u) * 8192u; };
+    // cp.async inputs: a ring of kAhead + 1 input tiles of 128 x 32, tile b at sxb(b) (an offset,
+    // not an indexed array, so the choice stays in registers)
+    auto sxb = [&](uint32_t b) { return smem + kSWeights + (b & kAhead) * 8192u; };
     __shared__ uint64_t mbar;
     __shared__ uint32_t tmem_slot;
 
@@ -348,6 +351,15 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
         load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, blockIdx.x * kRows + t, cur, p.rows);
         if constexpr (XROWS) issue_row_copy(sxb(0), t, p.x, cur.col, blockIdx.x * kRows + t < n);
         if constexpr (XIN == kXCols) issue_col_copy(sxb(0), p.x, p.x_stride, blockIdx.x * kRows, n);
+    } else if constexpr (XASYNC) {
+        cp_async_commit();
+    }
+#pragma unroll
+    for (uint32_t j = 1; j < kAhead; ++j) {  // deeper rings: tiles 1 .. kAhead - 1 as well
+        if (blockIdx.x + j * gridDim.x < n_tiles)
+            issue_col_copy(sxb(j), p.x, p.x_stride, (blockIdx.x + j * gridDim.x) * kRows, n);
+        else
+            cp_async_commit();
     }
     if (t < 32) umma::tmem_alloc(&tmem_slot, kFwdTmemCols);
     if (t == 0) umma::mbar_init(&mbar, 1);
@@ -366,13 +378,18 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
             if constexpr (XROWS) issue_row_copy(sxb(it + 1u), t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
-            if constexpr (XIN == kXCols) issue_col_copy(sxb(it + 1u), p.x, p.x_stride, (tile + gridDim.x) * kRows, n);
-        } else if constexpr (XASYNC) {
-            cp_async_commit();  // an empty group keeps the wait count below uniform
+        }
+        if constexpr (XIN == kXCols) {
+            if (tile + kAhead * gridDim.x < n_tiles)
+                issue_col_copy(sxb(it + kAhead), p.x, p.x_stride, (tile + kAhead * gridDim.x) * kRows, n);
+            else
+                cp_async_commit();  // an empty group keeps the wait count below uniform
+        } else if constexpr (XROWS) {
+            if (tile + gridDim.x >= n_tiles) cp_async_commit();
         }
         // ---- input row: 32 fp16 features ----
         if constexpr (XASYNC)
-            cp_async_wait<1>();  // this tile's copies (all but the group just issued) have landed
+            cp_async_wait<kAhead>();  // this tile's copies (all but the kAhead groups issued after them) have landed
         else {
             cp_async_wait<0>();  // the weights (first tile only; later tiles have none pending)
             store_half32_tmem(tmem, kFwdA, cur.x);
@@ -860,9 +877,7 @@ template <int MODE>
 int launch_forward(const MlpForwardParams& p, uint32_t n_rows, cudaStream_t stream, const char* what) {
     const uint32_t n_tiles = (n_rows + kRows - 1) / kRows;
     // feature-major inputs of contiguous rows go by cp.async when every 16-byte chunk is aligned
-    // (full network only: the density network's two layers were measured faster with the
-    // register gather, 2^20 rows 39.8 against 45.1 us)
-    const bool cols = MODE == kModeFull && !rows_layout(p.x_stride) && p.rows == nullptr && (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0u && p.x_stride % 8u == 0u;
+    const bool cols = !rows_layout(p.x_stride) && p.rows == nullptr && (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0u && p.x_stride % 8u == 0u;
     auto run = [&](auto kernel) {
         const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(kernel), n_tiles, kFwdTmemCols);
         kernel<<<grid, kThreads, kFwdSmem, stream>>>(p);
