@@ -513,11 +513,20 @@ __global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_co
             round_range(p, round, i, lo, hi);
             const __half* dens = p.density + static_cast<uint64_t>(base) * p.density_stride;
             const float* c     = p.coords + static_cast<uint64_t>(base) * 7u;
+            // the next chunk's density and dt are loaded before this chunk is walked, so a long
+            // ray pays one memory latency, not one per chunk
+            auto load = [&](uint32_t j, float& d, float& dt) {
+                const bool v = j < hi;
+                d            = v ? __half2float(dens[static_cast<uint64_t>(j) * p.density_stride]) : 0.0f;
+                dt           = v ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
+            };
+            float d_next, dt_next;
+            load(lo + lane, d_next, dt_next);
             for (uint32_t c0 = lo; c0 < hi; c0 += 32u) {
                 const uint32_t j  = c0 + lane;
                 const bool valid  = j < hi;
-                const float d     = valid ? __half2float(dens[static_cast<uint64_t>(j) * p.density_stride]) : 0.0f;
-                const float dt    = valid ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
+                const float d = d_next, dt = dt_next;
+                load(j + 32u, d_next, dt_next);
                 const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
                 const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, hi - c0));
                 const bool keep   = valid && !(Tb < kTransmittanceEps);
@@ -612,17 +621,27 @@ __device__ __forceinline__ float3 warp_scan_add3(float3 v) {
     return v;
 }
 
-// One 32-sample chunk of a ray (samples c0 + lane < k): opacity and colour of this lane's sample.
-__device__ __forceinline__ void chunk_sample(const __half* __restrict__ out, const float* __restrict__ cin, uint32_t j, bool valid, float& alpha,
-                                             float3& col, float& md, float& dt) {
-    float r = 0.f, g = 0.f, b = 0.f;
-    md = 0.f, dt = 0.f;
+// One 32-sample chunk of a ray: this lane's raw network output (rgb, density) and dt, loaded a
+// chunk ahead of their use; then its opacity and colour.
+struct ChunkRaw {
+    uint2 o;
+    float dt;
+};
+__device__ __forceinline__ ChunkRaw chunk_load(const __half* __restrict__ out, const float* __restrict__ cin, uint32_t j, bool valid) {
+    ChunkRaw raw{make_uint2(0u, 0u), 0.0f};
     if (valid) {
-        load_output(out + static_cast<uint64_t>(j) * 16u, r, g, b, md);
-        dt = cin[static_cast<uint64_t>(j) * 7u + 3u];
+        raw.o  = *reinterpret_cast<const uint2*>(out + static_cast<uint64_t>(j) * 16u);
+        raw.dt = cin[static_cast<uint64_t>(j) * 7u + 3u];
     }
+    return raw;
+}
+__device__ __forceinline__ void chunk_sample(const ChunkRaw& raw, bool valid, float& alpha, float3& col, float& md, float& dt) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw.o);
+    const float2 rg = __half22float2(h[0]), bd = __half22float2(h[1]);
+    md    = bd.y;
+    dt    = raw.dt;
     alpha = valid ? 1.0f - __expf(-expf(md) * dt) : 0.0f;
-    col   = {sigmoidf_(r), sigmoidf_(g), sigmoidf_(b)};
+    col   = {sigmoidf_(rg.x), sigmoidf_(rg.y), sigmoidf_(bd.x)};
 }
 
 // Step 5: compositing over the compacted outputs (pass 1), the loss, then the per-sample gradients
@@ -694,11 +713,14 @@ __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __gri
             const uint32_t k  = s_k[r];
             float P   = 1.0f;
             float3 S  = {0.f, 0.f, 0.f};
+            ChunkRaw next = chunk_load(out, cin, (c - s_first[r]) * 32u + lane, (c - s_first[r]) * 32u + lane < k);
             for (; c < e; ++c) {
                 const uint32_t j = (c - s_first[r]) * 32u + lane;
+                const ChunkRaw raw = next;
+                if (c + 1u < e) next = chunk_load(out, cin, j + 32u, j + 32u < k);
                 float alpha, md, dt;
                 float3 col;
-                chunk_sample(out, cin, j, j < k, alpha, col, md, dt);
+                chunk_sample(raw, j < k, alpha, col, md, dt);
                 const float Q  = warp_scan_mul(1.0f - alpha);            // product through this sample
                 const float Qu = __shfl_up_sync(0xFFFFFFFFu, Q, 1);  // every lane takes part in the shuffle
                 const float Qx = lane == 0 ? 1.0f : Qu;           // product before this sample
@@ -763,6 +785,7 @@ __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __gri
             const float3 rgb = s_rgb[r], grad = s_grad[r];
             float T          = s_T0[warp][r];
             float3 acc       = s_A0[warp][r];
+            ChunkRaw next = chunk_load(out, cin, (c - s_first[r]) * 32u + lane, (c - s_first[r]) * 32u + lane < k);
             for (; c < e; ++c) {
                 const uint32_t c0 = (c - s_first[r]) * 32u;
                 if (c0 >= cn) {
@@ -770,9 +793,11 @@ __global__ void __launch_bounds__(kCtaThreads) loss_compacted_kernel(const __gri
                     break;
                 }
                 const uint32_t j = c0 + lane;
+                const ChunkRaw raw = next;
+                if (c + 1u < e) next = chunk_load(out, cin, j + 32u, j + 32u < k);
                 float alpha, md, dt;
                 float3 col;
-                chunk_sample(out, cin, j, j < k, alpha, col, md, dt);
+                chunk_sample(raw, j < k, alpha, col, md, dt);
                 const float Q      = warp_scan_mul(1.0f - alpha);
                 const float Qu     = __shfl_up_sync(0xFFFFFFFFu, Q, 1);
                 const float Qx     = lane == 0 ? 1.0f : Qu;
