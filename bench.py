@@ -172,11 +172,13 @@ COMPACTED_ROWS = BATCH + 1024
 # bytes that must move (inputs read once, outputs written once); table gathers are L2-served and
 # reported separately against the measured L2 read rate.
 GRID_KERNELS = {
-    # encode_forward_points_kernel over the grid-update samples: x, y, z of each 28-byte record
-    # (12 B) in, 16 levels x 2 fp16 features (64 B) out; 16 x 8 corner gathers of 4 B (512 B, L2)
-    "grid_encode": {"kernel": "encode_forward_points_kernel (density-grid samples)", "hbm_bytes": 12 + 64, "l2_bytes": 16 * 8 * 4},
-    # mlp_forward_kernel<density> over the grid-update samples: 64 B features in, 2 B density out
-    "grid_density": {"kernel": "mlp_forward_kernel<density> (density-grid samples)", "hbm_bytes": 64 + 2, "flop": DENSITY_FWD_FLOP},
+    # encode_grid_samples_kernel over the warm-up grid samples (made inside the kernel: no
+    # positions in memory): 16 levels x 2 fp16 features (64 B) and the 4-byte cell index out;
+    # 16 x 8 corner gathers of 4 B (512 B, L2)
+    "grid_encode": {"kernel": "encode_grid_samples_kernel (density-grid samples generated and encoded)", "hbm_bytes": 64 + 4, "l2_bytes": 16 * 8 * 4},
+    # mlp_forward_kernel<density> over the grid-update samples with the splat in its epilogue:
+    # 64 B features and the 4-byte cell index in, one 4-byte atomicMax per sample
+    "grid_density": {"kernel": "mlp_forward_kernel<density> + splat (density-grid samples)", "hbm_bytes": 64 + 4 + 4, "flop": DENSITY_FWD_FLOP},
     # generate_grid_samples_kernel: one 28-byte record + 4-byte cell index out per sample
     "grid_samples": {"kernel": "generate_grid_samples_kernel", "hbm_bytes": 28 + 4},
     # splat_kernel: 4 B index + 2 B density in, one 4-byte atomicMax per sample

@@ -148,6 +148,13 @@ NGP_API int ngp_mlp_forward(uint32_t n, const uint16_t* params, const uint16_t* 
 /* Density network only -> out[n] = raw density (fp16).  Replaces the density-only
  * mlp_forward_64_relu_kernel launch of update_density_grid (ngp.train.cu:1573). */
 NGP_API int ngp_density_forward(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, uint16_t* out, void* stream);
+/* Density network with the density-grid splat in its epilogue: for each row i, the raw density d
+ * (rounded to fp16 as ngp_density_forward writes it) gives scratch[indices[i]] =
+ * max(scratch[indices[i]], exp(d) * sqrt(3)/1024) -- ngp_density_forward followed by
+ * ngp_density_grid_splat, bit for bit, without the density array.  Replaces the update's
+ * mlp_forward_64_relu_kernel launch and splat_kernel (ngp.train.cu:1573, 426-432). */
+NGP_API int ngp_density_forward_splat(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const uint32_t* indices,
+                                      float* scratch, void* stream);
 
 /* Full network for a list of rows: input column rows[r] of x and record rows[r] of coords, output
  * row out[rows[r]][16], for r < min(*n_rows, max_rows) (n_rows may be NULL). */
@@ -209,6 +216,14 @@ NGP_API int ngp_density_grid_samples(uint32_t n_uniform, uint32_t n_nonuniform, 
  * reference's (generate_density_grid_samples_kernel, ngp.train.cu:383-424). */
 NGP_API int ngp_density_grid_samples_cell_order(uint32_t n_uniform, uint32_t n_nonuniform, uint32_t ema_step, const float* values, float* coords,
                                                 uint32_t* indices, uint32_t* counter, void* stream);
+/* The warm-up update's samples (n_uniform = 2^21, n_nonuniform = 0: the first 256 steps) generated
+ * and encoded in one pass: out[f][i] (feature-major, out_stride >= 2^21) = the hash-grid encoding of
+ * sample i of ngp_density_grid_samples_cell_order(2^21, 0, ema_step, ...) and indices[i] its cell
+ * index; the positions are not written.  Equal, bit for bit, to that call followed by
+ * ngp_encode_grid_forward on its records.  Replaces generate_density_grid_samples_kernel plus the
+ * update's encoding (ngp.train.cu:383-424, 876-921). */
+NGP_API int ngp_density_grid_encode_samples(const ngp_grid_layout* layout, uint32_t ema_step, const float* values, const uint16_t* table,
+                                            uint16_t* out, uint32_t out_stride, uint32_t* indices, void* stream);
 
 /* scratch[indices[i]] = max(scratch[indices[i]], exp(density[i]) * sqrt(3)/1024).
  * Replaces splat_density_grid_samples_kernel (ngp.train.cu:426-432). */

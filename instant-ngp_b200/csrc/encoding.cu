@@ -13,6 +13,7 @@
 // Backward follows encode_grid_backward_kernel (ngp.train.cu:923-960) but scatters into an
 // fp32 gradient table with vector atomics (red.global.add.v2/v4.f32) instead of fp16 atomics.
 #include "encoding.cuh"
+#include "sampler.cuh"
 
 // Tuning knob (compile-time; the default is the measured best on B200): levels up to this
 // resolution pre-sum the lanes of a warp that share a cell before the backward's atomics.
@@ -48,6 +49,27 @@ __device__ __forceinline__ void store_halves(__half* dst, const __half* v) {
     }
 }
 
+// Feature-major encoding of one point: levels LPI at a time, features to out[level * F + f][i].
+template <uint32_t F, uint32_t LPI>
+__device__ __forceinline__ void encode_point_features(const float (&x)[3], uint32_t i, const typename FeatureVec<F>::type* __restrict__ tab,
+                                                      __half* __restrict__ out, uint32_t out_stride, const GridParams& grid) {
+    for (uint32_t l0 = 0; l0 < grid.n_levels; l0 += LPI) {
+        float frac[LPI][3];
+        typename FeatureVec<F>::type v[LPI][8];
+#pragma unroll
+        for (uint32_t j = 0; j < LPI; ++j) gather_level<F>(grid, tab, min(l0 + j, grid.n_levels - 1u), x, frac[j], v[j]);
+#pragma unroll
+        for (uint32_t j = 0; j < LPI; ++j) {
+            const uint32_t level = l0 + j;
+            if (level >= grid.n_levels) break;
+            float acc[F];
+            interp_level<F>(frac[j], v[j], acc);
+#pragma unroll
+            for (uint32_t f = 0; f < F; ++f) out[static_cast<uint64_t>(level * F + f) * out_stride + i] = __float2half_rn(acc[f]);
+        }
+    }
+}
+
 // Point-major forward: a thread reads its point once and walks the levels LPI at a time (8 * LPI
 // gathers in flight).  Same per-(point, level) arithmetic as encode_forward_kernel.
 template <uint32_t F, uint32_t LPI, bool ROWS>
@@ -72,6 +94,10 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(c
     __shared__ __align__(16) __half stage[ROWS ? kEncodeThreads : 1][ROWS ? kStageHalves : 1];
     const uint32_t row_halves = grid.n_levels * F;
     const bool staged = ROWS && row_halves <= kStageHalves && row_halves % 8u == 0u && 32u % (row_halves / 8u) == 0u;
+    if constexpr (!ROWS) {
+        encode_point_features<F, LPI>(x, i, tab, out, out_stride, grid);
+        return;
+    }
     for (uint32_t l0 = 0; live && l0 < grid.n_levels; l0 += LPI) {
         float frac[LPI][3];
         Vec v[LPI][8];
@@ -83,27 +109,20 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(c
             if (level >= grid.n_levels) break;
             float acc[F];
             interp_level<F>(frac[j], v[j], acc);
-            if constexpr (ROWS) {
-                // this level's F features into the pair's vector, written once per level pair
+            // this level's F features into the pair's vector, written once per level pair
 #pragma unroll
-                for (uint32_t f = 0; f < F; ++f) pair_out[j * F + f] = __float2half_rn(acc[f]);
-            } else {
-#pragma unroll
-                for (uint32_t f = 0; f < F; ++f) out[static_cast<uint64_t>(level * F + f) * out_stride + i] = __float2half_rn(acc[f]);
-            }
+            for (uint32_t f = 0; f < F; ++f) pair_out[j * F + f] = __float2half_rn(acc[f]);
         }
-        if constexpr (ROWS) {
-            // row-major [i][n_levels * F]: the level pair's LPI * F halves go to this thread's
-            // staged row (written out coalesced below), or straight to the row when not staged
-            __half* dst = staged ? &stage[threadIdx.x][l0 * F] : out + static_cast<uint64_t>(i) * (grid.n_levels * F) + l0 * F;
-            if (l0 + LPI <= grid.n_levels) {
-                store_halves<LPI * F>(dst, pair_out);
-            } else {
-                for (uint32_t k = 0; k < (grid.n_levels - l0) * F; ++k) dst[k] = pair_out[k];
-            }
+        // row-major [i][n_levels * F]: the level pair's LPI * F halves go to this thread's staged
+        // row (written out coalesced below), or straight to the row when not staged
+        __half* dst = staged ? &stage[threadIdx.x][l0 * F] : out + static_cast<uint64_t>(i) * (grid.n_levels * F) + l0 * F;
+        if (l0 + LPI <= grid.n_levels) {
+            store_halves<LPI * F>(dst, pair_out);
+        } else {
+            for (uint32_t k = 0; k < (grid.n_levels - l0) * F; ++k) dst[k] = pair_out[k];
         }
     }
-    if constexpr (ROWS) {
+    {
         if (staged) {
             // The warp's rows leave as 16-byte chunks: in round k, lane l writes chunk l % C of the
             // row of lane k * (32 / C) + l / C (C chunks per row), so each store instruction writes
@@ -121,6 +140,29 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_forward_points_kernel(c
             }
         }
     }
+}
+
+// K2 + encoding of the warm-up grid samples (all 2^21 samples uniform, the first 256 steps):
+// thread g makes the sample whose first cell is g (cell order, as
+// generate_grid_samples_ordered_kernel: the same position and cell as K2's sample) and encodes
+// it directly, writing its cell index; the position never goes to memory.
+template <uint32_t F, uint32_t LPI>
+__global__ void __launch_bounds__(kEncodeThreads) encode_grid_samples_kernel(uint32_t ema_step, uint64_t base_state, const float* __restrict__ values,
+                                                                             uint32_t* __restrict__ indices, const __half* __restrict__ table,
+                                                                             __half* __restrict__ out, const uint32_t out_stride,
+                                                                             const __grid_constant__ GridParams grid) {
+    __shared__ uint64_t jm[64], jp[64];
+    if (threadIdx.x < 64) jm[threadIdx.x] = c_pcg_jump.mult[threadIdx.x];
+    else if (threadIdx.x < 128) jp[threadIdx.x - 64] = c_pcg_jump.plus[threadIdx.x - 64];
+    __syncthreads();
+    const uint32_t g   = blockIdx.x * kEncodeThreads + threadIdx.x;  // cell (Morton index), < 2^21
+    const uint32_t rel = (g - (kGridHashAdd & (kGridCells - 1u))) * kGridHashMulInv;
+    const uint32_t i   = (rel - ema_step * kGridCells) & (kGridCells - 1u);
+    float x[3];
+    uint32_t idx;
+    grid_sample_position(i, kGridCells, ema_step, -0.01f, base_state, jm, jp, values, x, idx);
+    indices[g] = idx;
+    encode_point_features<F, LPI>(x, g, reinterpret_cast<const typename FeatureVec<F>::type*>(table), out, out_stride, grid);
 }
 
 template <uint32_t F>
@@ -386,4 +428,27 @@ extern "C" int ngp_encode_grid_backward_rows(const ngp_grid_layout* layout, uint
     clear_error();
     if (rows == nullptr) return fail(NGP_ERR_INVALID, "encode backward rows: null row list");
     return encode_backward_launch(layout, n, rows, coords, coord_stride, dy, dy_stride, table_grad, stream);
+}
+
+extern "C" int ngp_density_grid_encode_samples(const ngp_grid_layout* layout, uint32_t ema_step, const float* values, const uint16_t* table,
+                                               uint16_t* out, uint32_t out_stride, uint32_t* indices, void* stream) {
+    clear_error();
+    NGP_TRY(validate_layout(layout));
+    if (values == nullptr || table == nullptr || out == nullptr || indices == nullptr) return fail(NGP_ERR_INVALID, "grid encode samples: null pointer");
+    if (out_stride < kGridCells) return fail(NGP_ERR_INVALID, "grid encode samples: bad stride");
+    const GridParams grid = make_grid_params(*layout);
+    // the set's stream before the per-sample jump: PCG32(1337) advanced by (2 ema_step + 1) << 32
+    Pcg32 u{kTrainSeed};
+    u.advance((static_cast<uint64_t>(ema_step) * 2ull + 1ull) << 32u);
+    const auto* t      = reinterpret_cast<const __half*>(table);
+    auto* o            = reinterpret_cast<__half*>(out);
+    const uint32_t blk = kGridCells / kEncodeThreads;
+    const cudaStream_t s = as_stream(stream);
+    switch (layout->features_per_level) {
+        case 1: encode_grid_samples_kernel<1, 2><<<blk, kEncodeThreads, 0, s>>>(ema_step, u.state, values, indices, t, o, out_stride, grid); break;
+        case 2: encode_grid_samples_kernel<2, 2><<<blk, kEncodeThreads, 0, s>>>(ema_step, u.state, values, indices, t, o, out_stride, grid); break;
+        case 4: encode_grid_samples_kernel<4, 2><<<blk, kEncodeThreads, 0, s>>>(ema_step, u.state, values, indices, t, o, out_stride, grid); break;
+        default: encode_grid_samples_kernel<8, 2><<<blk, kEncodeThreads, 0, s>>>(ema_step, u.state, values, indices, t, o, out_stride, grid); break;
+    }
+    return check_launch("encode_grid_samples_kernel");
 }

@@ -23,6 +23,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "sampler.cuh"
 #include "umma.cuh"
 
 namespace ngp {
@@ -298,6 +299,10 @@ struct MlpForwardParams {
     __half* density_rgb_in; // optional: density outputs, feature-major [16][x_stride]
     const uint32_t* rows;   // optional row list (see RowInputs)
     const uint32_t* n_dev;  // optional device-side row count (<= n)
+    // optional (density mode): the density-grid splat (K3) of row i's density into
+    // splat_scratch[splat_indices[i]] instead of writing out
+    const uint32_t* splat_indices;
+    float* splat_scratch;
 };
 
 enum : int { kModeFull = 0, kModeDensity = 1 };
@@ -422,7 +427,16 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
         float dens[16];
         read_acc<16>(tmem, 64, dens);
         if (MODE == kModeDensity) {
-            if (valid) p.out[cur.col] = __float2half_rn(dens[0]);
+            if (valid) {
+                const __half d = __float2half_rn(dens[0]);
+                if (p.splat_scratch != nullptr) {
+                    // K3 (ngp.train.cu:426-432) on the rounded density, as splat_kernel computes it
+                    const float thickness = expf(__half2float(d)) * kConeStep;
+                    atomicMax(reinterpret_cast<uint32_t*>(p.splat_scratch + __ldg(p.splat_indices + cur.col)), __float_as_uint(thickness));
+                } else {
+                    p.out[cur.col] = d;
+                }
+            }
             cur = nxt;
             umma::fence_before_sync();
             if (!__syncthreads_and(ok)) break;
@@ -913,6 +927,18 @@ extern "C" int ngp_density_forward(uint32_t n, const uint16_t* params, const uin
     MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7,
                        reinterpret_cast<__half*>(out), nullptr, nullptr, nullptr};
     return launch_forward<kModeDensity>(p, n, as_stream(stream), "mlp_forward_kernel<density>");
+}
+
+extern "C" int ngp_density_forward_splat(uint32_t n, const uint16_t* params, const uint16_t* x, uint32_t x_stride, const uint32_t* indices,
+                                         float* scratch, void* stream) {
+    clear_error();
+    if (n == 0) return NGP_OK;
+    if (params == nullptr || x == nullptr || indices == nullptr || scratch == nullptr) return fail(NGP_ERR_INVALID, "density forward splat: null pointer");
+    if (!rows_layout(x_stride) && x_stride < n) return fail(NGP_ERR_INVALID, "density forward splat: bad stride");
+    NGP_TRY(ensure_attrs());
+    MlpForwardParams p{n, reinterpret_cast<const __half*>(params), reinterpret_cast<const __half*>(x), x_stride, nullptr, 7, nullptr, nullptr, nullptr,
+                       nullptr, indices, scratch};
+    return launch_forward<kModeDensity>(p, n, as_stream(stream), "mlp_forward_kernel<density, splat>");
 }
 
 extern "C" int ngp_mlp_forward_rows(uint32_t max_rows, const uint32_t* rows, const uint32_t* n_rows, const uint16_t* params, const uint16_t* x,

@@ -105,34 +105,15 @@ __global__ void generate_grid_samples_kernel(uint32_t n_uniform, uint32_t n_nonu
 // With all 2^21 samples uniform (the first 256 steps) thread g writes slot g; otherwise a warp
 // reserves its slots with one atomic on *counter (zeroed by the caller): the warp's samples stay
 // in cell order, warps in any order.
-constexpr uint32_t kGridHashMul    = 56924617u;
-constexpr uint32_t kGridHashMulInv = 53369u;  // inverse of 56924617 modulo 2^21
-constexpr uint32_t kGridHashAdd    = 96925573u;
-
 __device__ __forceinline__ void grid_sample_record(uint32_t i, uint32_t count, uint32_t ema_step, float thresh, uint64_t base_state,
                                                    const uint64_t* __restrict__ jm, const uint64_t* __restrict__ jp,
                                                    const float* __restrict__ values, float* __restrict__ c, uint32_t* __restrict__ index) {
-    uint32_t idx = 0;
-    for (uint32_t j = 0; j < 10; ++j) {
-        idx = static_cast<uint32_t>(((static_cast<uint64_t>(i) + static_cast<uint64_t>(ema_step) * count) * 56924617ull +
-                                     static_cast<uint64_t>(j) * 19349663ull + 96925573ull) %
-                                    kGridCells);
-        if (values[idx] > thresh) break;
-    }
-    // the stream of sample i: the set's base state advanced by 4 i steps (shared-memory jump
-    // table: one multiply-add per set bit of 4 i)
-    uint64_t state = base_state;
-    for (uint64_t delta = static_cast<uint64_t>(i) * 4ull; delta != 0u; delta &= delta - 1u) {
-        const int k = __ffsll(static_cast<long long>(delta)) - 1;
-        state       = jm[k] * state + jp[k];
-    }
-    Pcg32 rng{0u};
-    rng.state = state;
-    rng.inc   = 3u;
-    const uint32_t x = morton_compact(idx), y = morton_compact(idx >> 1), z = morton_compact(idx >> 2);
-    c[0]   = (static_cast<float>(x) + rng.next_float()) / 128.0f;
-    c[1]   = (static_cast<float>(y) + rng.next_float()) / 128.0f;
-    c[2]   = (static_cast<float>(z) + rng.next_float()) / 128.0f;
+    float pos[3];
+    uint32_t idx;
+    grid_sample_position(i, count, ema_step, thresh, base_state, jm, jp, values, pos, idx);
+    c[0]   = pos[0];
+    c[1]   = pos[1];
+    c[2]   = pos[2];
     c[3]   = kConeStep;
     c[4]   = 0.5f;
     c[5]   = 0.5f;

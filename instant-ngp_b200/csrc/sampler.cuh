@@ -41,6 +41,40 @@ __host__ __device__ __forceinline__ uint32_t morton_compact(uint32_t v) {
     return v;
 }
 
+// K2's cell hash (ngp.train.cu:383-424): sample i of a set of `count` (try j) takes cell
+// ((i + ema_step * count) * 56924617 + j * 19349663 + 96925573) mod 2^21.  The multiplier is odd,
+// so with j = 0 this is a bijection of [0, 2^21) (inverse multiplier 53369).
+constexpr uint32_t kGridHashMul    = 56924617u;
+constexpr uint32_t kGridHashMulInv = 53369u;  // inverse of 56924617 modulo 2^21
+constexpr uint32_t kGridHashAdd    = 96925573u;
+
+// Position and cell of grid sample i of its set (K2's body): up to 10 hashed tries for a cell
+// whose value exceeds `thresh`, then the cell corner plus three PCG32 draws of sample i's stream
+// (the set's base state advanced by 4 i steps; jm / jp: the 2^k jump table in shared memory).
+__device__ __forceinline__ void grid_sample_position(uint32_t i, uint32_t count, uint32_t ema_step, float thresh, uint64_t base_state,
+                                                     const uint64_t* __restrict__ jm, const uint64_t* __restrict__ jp,
+                                                     const float* __restrict__ values, float (&pos)[3], uint32_t& idx) {
+    idx = 0;
+    for (uint32_t j = 0; j < 10; ++j) {
+        idx = static_cast<uint32_t>(((static_cast<uint64_t>(i) + static_cast<uint64_t>(ema_step) * count) * kGridHashMul +
+                                     static_cast<uint64_t>(j) * 19349663ull + kGridHashAdd) %
+                                    kGridCells);
+        if (values[idx] > thresh) break;
+    }
+    uint64_t state = base_state;
+    for (uint64_t delta = static_cast<uint64_t>(i) * 4ull; delta != 0u; delta &= delta - 1u) {
+        const int k = __ffsll(static_cast<long long>(delta)) - 1;
+        state       = jm[k] * state + jp[k];
+    }
+    Pcg32 rng{0u};
+    rng.state = state;
+    rng.inc   = 3u;
+    const uint32_t x = morton_compact(idx), y = morton_compact(idx >> 1), z = morton_compact(idx >> 2);
+    pos[0] = (static_cast<float>(x) + rng.next_float()) / 128.0f;
+    pos[1] = (static_cast<float>(y) + rng.next_float()) / 128.0f;
+    pos[2] = (static_cast<float>(z) + rng.next_float()) / 128.0f;
+}
+
 __device__ __forceinline__ bool inside_unit_cube(float3 p) {
     return p.x >= 0.0f && p.x <= 1.0f && p.y >= 0.0f && p.y <= 1.0f && p.z >= 0.0f && p.z <= 1.0f;
 }

@@ -337,15 +337,22 @@ int update_grid(ngp_trainer* t) {
     const uint32_t n         = n_uniform + n_nonuni;
     float* coords = t->sets[t->step & 1u].coords;
     // the reference's samples in Morton cell order (the encoding below then gathers neighbouring
-    // table entries); the splat's atomic max does not depend on their order
-    NGP_TRY(ngp_density_grid_samples_cell_order(n_uniform, n_nonuni, t->ema_step, t->grid_values, coords, t->grid_indices, t->grid_counter,
+    // table entries); the splat's atomic max does not depend on their order.  In the warm-up (all
+    // 2^21 samples uniform) the samples are made inside the encoding kernel.
+    if (n_nonuni == 0 && n_uniform == kGridCells) {
+        grid_mark(t, 1);
+        NGP_TRY(ngp_density_grid_encode_samples(&t->layout, t->ema_step, t->grid_values, t->params + kMlpParams, t->enc, n, t->grid_indices,
                                                 t->stream));
-    grid_mark(t, 1);
-    NGP_TRY(encode(t, n, coords, t->enc, n));
+    } else {
+        NGP_TRY(ngp_density_grid_samples_cell_order(n_uniform, n_nonuni, t->ema_step, t->grid_values, coords, t->grid_indices, t->grid_counter,
+                                                    t->stream));
+        grid_mark(t, 1);
+        NGP_TRY(encode(t, n, coords, t->enc, n));
+    }
     grid_mark(t, 2);
-    NGP_TRY(ngp_density_forward(n, t->params, t->enc, n, t->grid_density, t->stream));
+    // density network with the splat (K3) in its epilogue: scratch[cell] = max(..., exp(d) * dt)
+    NGP_TRY(ngp_density_forward_splat(n, t->params, t->enc, n, t->grid_indices, t->grid_scratch, t->stream));
     grid_mark(t, 3);
-    NGP_TRY(ngp_density_grid_splat(n, t->grid_indices, t->grid_density, t->grid_scratch, t->stream));
     grid_mark(t, 4);
     NGP_TRY(ngp_density_grid_update(t->grid_values, t->grid_scratch, 0.95f, t->grid_partial, t->grid_mean, t->bitfield, t->occupied, t->stream));
     grid_mark(t, 5);

@@ -172,6 +172,14 @@ def density_forward(params, x, out, n: int | None = None, x_stride: int | None =
            "ngp_density_forward")
 
 
+def density_forward_splat(params, x, indices, scratch, n: int | None = None, x_stride: int | None = None, stream=None) -> None:
+    """Density network + the density-grid splat into scratch[indices[i]] (atomic max)."""
+    n = indices.shape[0] if n is None else n
+    x_stride = x.shape[1] if x_stride is None else x_stride
+    _check(lib().ngp_density_forward_splat(ctypes.c_uint32(n), _ptr(params), _ptr(x), ctypes.c_uint32(x_stride), _ptr(indices), _ptr(scratch),
+                                           _stream(stream)), "ngp_density_forward_splat")
+
+
 def mlp_backward_scratch(device=None):
     """The (cached) fp32 scratch buffer ngp_mlp_backward needs on `device`."""
     import torch
@@ -233,6 +241,13 @@ def density_grid_samples(n_uniform, n_nonuniform, ema_step, values, coords, indi
 def density_grid_samples_cell_order(n_uniform, n_nonuniform, ema_step, values, coords, indices, counter=None, stream=None) -> None:
     _check(lib().ngp_density_grid_samples_cell_order(_u32(n_uniform), _u32(n_nonuniform), _u32(ema_step), _ptr(values), _ptr(coords), _ptr(indices),
                                                      _ptr(counter), _stream(stream)), "ngp_density_grid_samples_cell_order")
+
+
+def density_grid_encode_samples(layout: GridLayout, ema_step, values, table, out, indices, out_stride=None, stream=None) -> None:
+    """Warm-up grid samples generated and encoded in one pass (no positions written)."""
+    out_stride = out.shape[1] if out_stride is None else out_stride
+    _check(lib().ngp_density_grid_encode_samples(ctypes.byref(layout), _u32(ema_step), _ptr(values), _ptr(table), _ptr(out), _u32(out_stride),
+                                                 _ptr(indices), _stream(stream)), "ngp_density_grid_encode_samples")
 
 
 def density_grid_splat(n, indices, density, scratch, stream=None) -> None:

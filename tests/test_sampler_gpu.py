@@ -714,3 +714,56 @@ def test_grid_samples_cell_order_is_a_permutation_of_the_reference(ngp, reflib, 
         # slot g holds the sample whose first cell is g: cells ascend wherever no retry happened
         cells = idx.cpu().numpy().view(np.uint32)
         assert (cells == np.arange(n, dtype=np.uint32)).mean() > 0.95
+
+
+@pytest.mark.parametrize("layout_args", [(16, 2, 19, 16, math.log2(2048.0 / 16.0) / 15.0), (8, 4, 19, 16, 1.0)], ids=["16x2", "8x4"])
+@pytest.mark.parametrize("ema_step", [0, 7])
+def test_grid_encode_samples_equals_samples_then_encode(ngp, layout_args, ema_step):
+    """ngp_density_grid_encode_samples (warm-up samples made inside the encoding kernel) against
+    the cell-ordered samples followed by the encoding of their records: encodings and cell
+    indices bit for bit, untrained cells (retries) included."""
+    import torch
+
+    n = 1 << 21
+    layout = ngp.grid_layout(*layout_args)
+    _, table, _ = workloads.encode_inputs(1, layout.n_params, layout_args[0], layout_args[1], seed=11)
+    table_t = T(table.view(np.int16))
+    vals0 = workloads.blob_grid_values(workloads.gaussian_blob_density())
+    vals0[::97] = -1.0
+    values = T(vals0)
+    coords = torch.zeros((n, 7), dtype=torch.float32, device="cuda")
+    idx_a = torch.zeros(n, dtype=torch.int32, device="cuda")
+    ngp.density_grid_samples_cell_order(n, 0, ema_step, values, coords, idx_a)
+    F = layout_args[0] * layout_args[1]
+    enc_a = torch.zeros((F, n), dtype=torch.float16, device="cuda")
+    ngp.encode_grid_forward(layout, coords, table_t, enc_a, n=n, coord_stride=7, out_stride=n)
+    enc_b = torch.zeros_like(enc_a)
+    idx_b = torch.zeros_like(idx_a)
+    ngp.density_grid_encode_samples(layout, ema_step, values, table_t, enc_b, idx_b)
+    torch.cuda.synchronize()
+    assert torch.equal(idx_a, idx_b)
+    assert enc_a.cpu().numpy().view(np.uint16).tobytes() == enc_b.cpu().numpy().view(np.uint16).tobytes()
+
+
+def test_density_forward_splat_equals_forward_then_splat(ngp):
+    """The density network with the grid splat in its epilogue against ngp_density_forward followed
+    by ngp_density_grid_splat: the splatted grid bit for bit (cells hit by several samples
+    included)."""
+    import torch
+
+    n = 1 << 20
+    x_h, _, _ = workloads.mlp_inputs(n, seed=21)
+    params = T(workloads.xavier_mlp_params(3).view(np.int16))
+    x = T(x_h)
+    rng = np.random.default_rng(5)
+    cells = rng.integers(0, 128 ** 3, n).astype(np.int32)  # random cells: some repeat
+    idx = T(cells)
+    dens = torch.zeros(n, dtype=torch.float16, device="cuda")
+    ngp.density_forward(params, x, dens, n=n)
+    a = torch.zeros(128 ** 3, dtype=torch.float32, device="cuda")
+    ngp.density_grid_splat(n, idx, dens, a)
+    b = torch.zeros_like(a)
+    ngp.density_forward_splat(params, x, idx, b, n=n)
+    torch.cuda.synchronize()
+    assert (a > 0).sum().item() > 0.3 * n
+    assert a.cpu().numpy().tobytes() == b.cpu().numpy().tobytes()
