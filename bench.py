@@ -187,9 +187,10 @@ GRID_KERNELS = {
 # DRAM bytes (read + write) per unit that ncu measured for these launches (one capture each, see
 # profiles/ for the command); None until captured.
 NCU_TRAFFIC_PER_UNIT = {
-    # profiles/encode_forward_points_kernel__grid_update_config3.md: 85.15 MB read + 98.25 MB
-    # written by the launch over 2^21 cell-ordered grid samples
-    "grid_encode": (85.150464e6 + 98.249984e6) / 2097152,
+    # profiles/encode_grid_samples_kernel__grid_update_config3.md: 33.92 MB read + 97.03 MB
+    # written by the launch over the 2^21 warm-up grid samples (part of the written features are
+    # still in L2 when the kernel ends)
+    "grid_encode": (33.917440e6 + 97.028352e6) / 2097152,
 }
 
 

@@ -27,9 +27,9 @@ def grid(updates=10, **ms):
 
 def test_roofline_names_the_longest_grid_kernel():
     r = bench.train_roofline(phases(grid_update=0.6, march=0.2, adam=0.07), grid(grid_samples=0.05, grid_encode=0.3, grid_density=0.1), PEAKS, L2)
-    assert r["kernel"].startswith("encode_forward_points_kernel") and r["bound"] == "hbm"
-    # 76 algorithmic HBM bytes per grid sample over the kernel's event-timed launch
-    want = 76 * (1 << 21) / 0.3e-3 / 1e9
+    assert r["kernel"].startswith("encode_grid_samples_kernel") and r["bound"] == "hbm"
+    # 68 algorithmic HBM bytes per grid sample (64 B features + 4 B cell index out) over the launch
+    want = 68 * (1 << 21) / 0.3e-3 / 1e9
     assert r["achieved"] == pytest.approx(want, rel=1e-3)
     assert r["frac"] == pytest.approx(want / PEAKS["hbm_gbs"], rel=1e-2)
     assert 0 < r["share_of_step"] < 1
