@@ -274,7 +274,7 @@ namespace ngp {
 #define NGP_MARCH_GROUP 8
 #endif
 #ifndef NGP_MARCH_SKIP_WIDTH
-#define NGP_MARCH_SKIP_WIDTH 8  // empty voxels speculated per skip round (wide groups)
+#define NGP_MARCH_SKIP_WIDTH 4  // empty voxels speculated per skip round (measured: 2, 3, 4, 8, 16)
 #endif
 #ifndef NGP_MARCH_SKIP_SPEC
 #define NGP_MARCH_SKIP_SPEC 1  // 0: empty voxels are skipped one per round
@@ -313,9 +313,9 @@ __device__ __forceinline__ MarchRound group_march_round(GroupMarch& m, const uin
     const bool skip_mode    = NGP_MARCH_SKIP_SPEC && m.skip;
     float tk                = m.t;
     if (skip_mode) {
-        // a wide group speculates on kSkipWidth voxels only (lanes past it repeat the last one's
-        // position, so they never stop first): empty stretches are short while the grid is
-        // mostly occupied, and every lane's chain of skips costs the warp its longest chain
+        // a group speculates on kSkipWidth voxels only (lanes past it repeat the last one's
+        // position, so they never stop first): empty stretches are mostly short, and every
+        // lane's chain of skips costs the warp its longest chain
         constexpr uint32_t kSkipWidth = G > NGP_MARCH_SKIP_WIDTH ? NGP_MARCH_SKIP_WIDTH : G;
         const uint32_t gs = g < kSkipWidth ? g : kSkipWidth - 1u;
         for (uint32_t j = 0; j < gs; ++j) tk = skip_empty_voxel(tk, ray_point(m.o, m.d, tk), m.d, m.inv);
