@@ -317,18 +317,34 @@ constexpr uint32_t kFwdTmemCols = 128, kFwdA = 96;
 // weights | a ring of up to four 8 KB input tiles (cp.async inputs: the next tiles' copies land there)
 constexpr uint32_t kFwdSmem     = kSWeights + 4 * 8192 + 1024;
 
+// The density network alone (two layers) is light: 64 TMEM columns (D0 0-63; its ReLU output
+// goes back into columns 32-63 as the A operand of the output layer, whose 16-wide result lands
+// in columns 0-15), only its two weight matrices and a small input ring in shared memory, so
+// that up to six CTAs share an SM and more tile chains overlap.
+constexpr uint32_t kDensTmemCols = 64, kDensA = 32, kDensXBase = kSWdOut + 2048;
+__host__ __device__ constexpr uint32_t fwd_ahead(int mode, int xin) { return (xin == kXCols && mode == kModeDensity) ? 2u : 1u; }
+__host__ __device__ constexpr uint32_t fwd_smem(int mode, int xin) {
+    return mode == kModeDensity ? kDensXBase + (fwd_ahead(mode, xin) + 1u) * 8192u + 1024u : kFwdSmem;
+}
+
 template <int MODE, int XIN>
-__global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
+__global__ void __launch_bounds__(kThreads, MODE == kModeDensity ? (XIN == kXRegs ? 5 : 6) : 4) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
     constexpr bool XROWS  = XIN == kXRows;
     constexpr bool XASYNC = XIN != kXRegs;  // inputs staged by cp.async
+    constexpr bool DENS   = MODE == kModeDensity;
     // tiles in flight ahead of the one computed: the density network's two layers take less time
-    // than a tile's DRAM reads, so its contiguous inputs are fetched three tiles ahead
-    constexpr uint32_t kAhead = (XIN == kXCols && MODE == kModeDensity) ? 3u : 1u;
+    // than a tile's DRAM reads, so its contiguous inputs are fetched two tiles ahead
+    constexpr uint32_t kAhead = fwd_ahead(MODE, XIN);
+    constexpr uint32_t kBufs  = kAhead + 1u;
+    constexpr uint32_t kCols  = DENS ? kDensTmemCols : kFwdTmemCols;
+    constexpr uint32_t kA     = DENS ? kDensA : kFwdA;  // TMEM column of the hidden layers' A operand
+    constexpr uint32_t kD1    = DENS ? 0u : 64u;        // TMEM column of the 16-wide output accumulator
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* sw    = smem;                      // weights
-    // cp.async inputs: a ring of kAhead + 1 input tiles of 128 x 32, tile b at sxb(b) (an offset,
-    // not an indexed array, so the choice stays in registers)
-    auto sxb = [&](uint32_t b) { return smem + kSWeights + (b & kAhead) * 8192u; };
+    // input tiles: a ring of kBufs tiles of 128 x 32, tile b at sxb(b) (an offset, not an indexed
+    // array, so the choice stays in registers); the density network's register-gathered inputs
+    // are stored into tile 0
+    auto sxb = [&](uint32_t b) { return smem + (DENS ? kDensXBase : kSWeights) + (b % kBufs) * 8192u; };
     __shared__ uint64_t mbar;
     __shared__ uint32_t tmem_slot;
 
@@ -366,20 +382,20 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
         else
             cp_async_commit();
     }
-    if (t < 32) umma::tmem_alloc(&tmem_slot, kFwdTmemCols);
+    if (t < 32) umma::tmem_alloc(&tmem_slot, kCols);
     if (t == 0) umma::mbar_init(&mbar, 1);
     stage_sync();
     MLP_TRACE(1);
     const uint32_t tmem = tmem_slot;
-    const uint32_t d0 = tmem, d1 = tmem + 64;
-    const uint32_t a_act = tmem + kFwdA, a_sw = umma::smem_addr(sw);
+    const uint32_t d0 = tmem, d1 = tmem + kD1;
+    const uint32_t a_act = tmem + kA, a_sw = umma::smem_addr(sw);
     uint32_t phase  = 0;
     bool ok         = true;
     uint32_t it = 0;
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row   = tile * kRows + t;
         const bool valid     = row < n;
-        const uint32_t a_sx  = umma::smem_addr(sxb(it));  // cp.async inputs only
+        const uint32_t a_sx  = umma::smem_addr(sxb(XASYNC ? it : 0u));  // input tile in shared memory
         if (tile + gridDim.x < n_tiles) {
             load_row_inputs(p.x, p.x_stride, p.coords, p.coord_stride, n, (tile + gridDim.x) * kRows + t, nxt, p.rows);
             if constexpr (XROWS) issue_row_copy(sxb(it + 1u), t, p.x, nxt.col, (tile + gridDim.x) * kRows + t < n);
@@ -397,12 +413,15 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
             cp_async_wait<kAhead>();  // this tile's copies (all but the kAhead groups issued after them) have landed
         else {
             cp_async_wait<0>();  // the weights (first tile only; later tiles have none pending)
-            store_half32_tmem(tmem, kFwdA, cur.x);
+            if constexpr (DENS)
+                store_row_half32(sxb(0), t, cur.x);  // (its TMEM holds no room beside D0)
+            else
+                store_half32_tmem(tmem, kFwdA, cur.x);
         }
         MLP_TRACE(2 + it * 8);
         stage_sync();
         if (t == 0) {
-            if constexpr (XROWS)
+            if constexpr (XROWS || (DENS && XIN == kXRegs))
                 gemm(d0, 64, 32, a_sx, false, 4, a_sw + kSWdIn, false, 4, false);
             else if constexpr (XIN == kXCols)
                 gemm(d0, 64, 32, a_sx, true, 16, a_sw + kSWdIn, false, 4, false);  // MN-major A
@@ -415,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
         {
             float h[64];
             read_acc<64>(tmem, 0, h);
-            store_row_tmem<8, true>(tmem, kFwdA, h);
+            store_row_tmem<8, true>(tmem, kA, h);
         }
         stage_sync_tmem();
         if (t == 0) {
@@ -425,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
         ok = ok && stage_wait(&mbar, phase);
         MLP_TRACE(2 + it * 8 + 2);
         float dens[16];
-        read_acc<16>(tmem, 64, dens);
+        read_acc<16>(tmem, kD1, dens);
         if (MODE == kModeDensity) {
             if (valid) {
                 const __half d = __float2half_rn(dens[0]);
@@ -438,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
                 }
             }
             cur = nxt;
+            MLP_TRACE(2 + it * 8 + 7);
             umma::fence_before_sync();
             if (!__syncthreads_and(ok)) break;
             umma::fence_after_sync();
@@ -507,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 4) mlp_forward_kernel(const __grid_c
     cp_async_wait<0>();  // no copy (weights or inputs) may still target shared memory at exit
     umma::fence_before_sync();
     __syncthreads();
-    if (t < 32) umma::tmem_dealloc(tmem, kFwdTmemCols);
+    if (t < 32) umma::tmem_dealloc(tmem, kCols);
     MLP_TRACE(63);
 }
 
@@ -892,16 +912,17 @@ int launch_forward(const MlpForwardParams& p, uint32_t n_rows, cudaStream_t stre
     const uint32_t n_tiles = (n_rows + kRows - 1) / kRows;
     // feature-major inputs of contiguous rows go by cp.async when every 16-byte chunk is aligned
     const bool cols = !rows_layout(p.x_stride) && p.rows == nullptr && (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0u && p.x_stride % 8u == 0u;
-    auto run = [&](auto kernel) {
-        const int grid = mlp_grid(kFwdSmem, reinterpret_cast<const void*>(kernel), n_tiles, kFwdTmemCols);
-        kernel<<<grid, kThreads, kFwdSmem, stream>>>(p);
+    constexpr uint32_t cols_tmem = MODE == kModeDensity ? kDensTmemCols : kFwdTmemCols;
+    auto run = [&](auto kernel, uint32_t smem) {
+        const int grid = mlp_grid(static_cast<int>(smem), reinterpret_cast<const void*>(kernel), n_tiles, cols_tmem);
+        kernel<<<grid, kThreads, smem, stream>>>(p);
     };
     if (rows_layout(p.x_stride))
-        run(mlp_forward_kernel<MODE, kXRows>);
+        run(mlp_forward_kernel<MODE, kXRows>, fwd_smem(MODE, kXRows));
     else if (cols)
-        run(mlp_forward_kernel<MODE, kXCols>);
+        run(mlp_forward_kernel<MODE, kXCols>, fwd_smem(MODE, kXCols));
     else
-        run(mlp_forward_kernel<MODE, kXRegs>);
+        run(mlp_forward_kernel<MODE, kXRegs>, fwd_smem(MODE, kXRegs));
     return check_launch(what);
 }
 }  // namespace
