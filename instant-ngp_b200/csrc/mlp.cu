@@ -327,8 +327,12 @@ __host__ __device__ constexpr uint32_t fwd_smem(int mode, int xin) {
     return mode == kModeDensity ? kDensXBase + (fwd_ahead(mode, xin) + 1u) * 8192u + 1024u : kFwdSmem;
 }
 
+// resident CTAs per SM the register allocation must allow
 template <int MODE, int XIN>
-__global__ void __launch_bounds__(kThreads, MODE == kModeDensity ? (XIN == kXRegs ? 5 : 6) : 4) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
+constexpr int kFwdMinCtas = MODE == kModeDensity ? (XIN == kXRegs ? 5 : 6) : 4;
+
+template <int MODE, int XIN>
+__global__ void __launch_bounds__(kThreads, kFwdMinCtas<MODE, XIN>) mlp_forward_kernel(const __grid_constant__ MlpForwardParams p) {
     constexpr bool XROWS  = XIN == kXRows;
     constexpr bool XASYNC = XIN != kXRegs;  // inputs staged by cp.async
     constexpr bool DENS   = MODE == kModeDensity;
