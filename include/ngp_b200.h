@@ -493,7 +493,8 @@ NGP_API int ngp_adam_step_f16_range(uint32_t count, uint32_t first, uint32_t n_m
                                     float* first_moments, float* second_moments, uint32_t* param_steps, const float* lr_table,
                                     uint32_t table_len, void* stream);
 
-/* fp32 gradients -> fp16 (round to nearest); clear != 0 zeroes the fp32 source. */
+/* fp32 gradients -> fp16 (round to nearest); clear != 0 zeroes the fp32 source.  Both buffers
+ * 16-byte aligned.  (The conversion before the data-parallel exchange, ngp.train.cpp:123-124.) */
 NGP_API int ngp_gradients_to_half(uint32_t n, float* gradients, uint16_t* out, int clear, void* stream);
 
 /* ------------------------------------------------------------------------------------------

@@ -130,11 +130,28 @@ int adam_launch(uint32_t n_params, uint32_t n_mlp, float lr, float beta1, float 
     return check_launch("adam_kernel");
 }
 
+// Eight gradients per thread: two 16-byte fp32 loads, one 16-byte fp16 store and (clear) two
+// 16-byte zero stores; the tail of n past a multiple of 8 one by one.
 __global__ void grad_to_half_kernel(uint32_t n, float* __restrict__ src, __half* __restrict__ dst, int clear) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;  // group of 8
+    const uint32_t i = q * 8u;
     if (i >= n) return;
-    dst[i] = __float2half_rn(src[i]);
-    if (clear) src[i] = 0.0f;
+    if (i + 8u <= n) {
+        const float4 a = reinterpret_cast<const float4*>(src)[2u * q], b = reinterpret_cast<const float4*>(src)[2u * q + 1u];
+        const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w), h2 = __floats2half2_rn(b.x, b.y),
+                      h3 = __floats2half2_rn(b.z, b.w);
+        reinterpret_cast<uint4*>(dst)[q] = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                                                      *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+        if (clear) {
+            reinterpret_cast<float4*>(src)[2u * q]      = make_float4(0.f, 0.f, 0.f, 0.f);
+            reinterpret_cast<float4*>(src)[2u * q + 1u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        return;
+    }
+    for (uint32_t k = i; k < n; ++k) {
+        dst[k] = __float2half_rn(src[k]);
+        if (clear) src[k] = 0.0f;
+    }
 }
 
 
@@ -321,6 +338,8 @@ extern "C" int ngp_gradients_to_half(uint32_t n, float* gradients, uint16_t* out
     clear_error();
     if (n == 0) return NGP_OK;
     if (gradients == nullptr || out == nullptr) return fail(NGP_ERR_INVALID, "gradients to half: null pointer");
-    grad_to_half_kernel<<<(n + 255u) / 256u, 256, 0, as_stream(stream)>>>(n, gradients, reinterpret_cast<__half*>(out), clear);
+    if ((reinterpret_cast<uintptr_t>(gradients) | reinterpret_cast<uintptr_t>(out)) % 16u != 0)
+        return fail(NGP_ERR_INVALID, "gradients to half: buffers must be 16-byte aligned");
+    grad_to_half_kernel<<<(n + 8u * 256u - 1u) / (8u * 256u), 256, 0, as_stream(stream)>>>(n, gradients, reinterpret_cast<__half*>(out), clear);
     return check_launch("grad_to_half_kernel");
 }

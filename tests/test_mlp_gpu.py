@@ -216,3 +216,21 @@ def test_backward_full_size_vs_torch_fp32(ngp):
     err = np.abs(dx.float().cpu().numpy() - dxw)
     scale = np.abs(dxw).max()
     assert (err <= 1e-2 * scale).mean() > 0.9999 and err.mean() <= 1e-4 * scale
+
+
+@pytest.mark.parametrize("n", [8, 1000, 12206485])
+def test_gradients_to_half_rounds_and_clears(ngp, n):
+    """ngp_gradients_to_half (the conversion before the data-parallel exchange): fp16 rounding to
+    nearest as torch's, the fp32 source zeroed, a tail past a multiple of 8 included."""
+    import ctypes
+
+    import torch
+
+    g = torch.randn(n, dtype=torch.float32, device="cuda") * 100.0
+    want = g.half()
+    out = torch.zeros(n, dtype=torch.float16, device="cuda")
+    rc = ngp.lib().ngp_gradients_to_half(ctypes.c_uint32(n), ctypes.c_void_p(g.data_ptr()), ctypes.c_void_p(out.data_ptr()), 1, None)
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert torch.equal(out.view(torch.int16), want.view(torch.int16))
+    assert int(torch.count_nonzero(g)) == 0
