@@ -175,7 +175,11 @@ GRID_KERNELS = {
     # encode_grid_samples_kernel over the warm-up grid samples (made inside the kernel: no
     # positions in memory): 16 levels x 2 fp16 features (64 B) and the 4-byte cell index out;
     # 16 x 8 corner gathers of 4 B (512 B, L2)
-    "grid_encode": {"kernel": "encode_grid_samples_kernel (density-grid samples generated and encoded)", "hbm_bytes": 64 + 4, "l2_bytes": 16 * 8 * 4},
+    # (l2_requests: L1 misses sent to L2 per sample, ncu l1tex__t_sectors_pipe_lsu_mem_global_op_ld_lookup_miss
+    # of one launch over 2^21 samples, 64,620,418 / 2^21: about one per x-edge of the 8 levels finer
+    # than the sample grid; profiles/encode_grid_samples_kernel__grid_update_config3.md)
+    "grid_encode": {"kernel": "encode_grid_samples_kernel (density-grid samples generated and encoded)", "hbm_bytes": 64 + 4, "l2_bytes": 16 * 8 * 4,
+                    "l2_requests": 64620418 / 2097152},
     # mlp_forward_kernel<density> over the grid-update samples with the splat in its epilogue:
     # 64 B features and the 4-byte cell index in, one 4-byte atomicMax per sample
     "grid_density": {"kernel": "mlp_forward_kernel<density> + splat (density-grid samples)", "hbm_bytes": 64 + 4 + 4, "flop": DENSITY_FWD_FLOP},
@@ -229,6 +233,15 @@ def train_roofline(phases: dict, grid: dict, peaks: dict, l2: dict | None) -> di
                      "frac_of_random_gather": round(l2_rate / l2["gather_GBps"], 4) if l2.get("gather_GBps") else None,
                      "note": "table corner bytes gathered per second against the measured L2 streaming-read rate and the measured rate of fully "
                              "random 4-byte loads from an L2-resident table (bench_probes, run live)"}
+        if "l2_requests" in info and l2.get("gather_GBps"):
+            # the random-gather probe sends one one-sector L2 request per 4-byte load: its rate is the
+            # measured ceiling of the L1 -> L2 request path that bounds this kernel
+            req = info["l2_requests"] * units / t / 1e9
+            peak_req = l2["gather_GBps"] / 4.0
+            res["l2"]["requests"] = {"per_unit": round(info["l2_requests"], 2), "achieved_G_per_s": round(req, 1), "probe_G_per_s": round(peak_req, 1),
+                                     "frac": round(req / peak_req, 4),
+                                     "note": "L1 misses sent to L2 per second (ncu count per sample x samples / event-timed launch) against the "
+                                             "random-gather probe's request rate: the path ncu shows saturated (l1tex__m_l1tex2xbar_req_cycles_active)"}
     return res
 
 

@@ -47,3 +47,12 @@ def test_peaks_come_from_the_measured_file_or_the_stated_fallback():
     p = bench.load_peaks()
     assert p["source"] in ("measured", "fallback")
     assert p["hbm_gbs"] > 1000 and p["bf16_tflops"] > 100
+
+
+def test_roofline_reports_the_request_path():
+    r = bench.train_roofline(phases(grid_update=0.6, march=0.2, adam=0.07), grid(grid_samples=0.05, grid_encode=0.3, grid_density=0.1), PEAKS, L2)
+    req = r["l2"]["requests"]
+    per = bench.GRID_KERNELS["grid_encode"]["l2_requests"]
+    assert req["achieved_G_per_s"] == pytest.approx(per * (1 << 21) / 0.3e-3 / 1e9, rel=1e-3)
+    assert req["probe_G_per_s"] == pytest.approx(L2["gather_GBps"] / 4.0)
+    assert req["frac"] == pytest.approx(req["achieved_G_per_s"] / req["probe_G_per_s"], rel=1e-2)
