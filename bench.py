@@ -371,8 +371,8 @@ def bench_train_ours(args, rank, world, local):
             "unit": "samples/s", "ms_per_step": round(ms_same / args.steps, 5), "steps": args.steps, "warmup": args.warmup,
             "note": "the library on the reference arm's configuration (same scene, batch, steps and layout), timed like the headline"},
         "e2e": {"value": round(world * BATCH * args.steps / e2e_s, 1), "unit": "samples/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": int(12 + 4 + 4 * mean_rays),
-                "copies": [{"dir": "d2h", "bytes": 12, "what": "the step's ray / sample / compacted counters (pinned)"},
+                "d2h_bytes_per_step": int(20 + 4 + 4 * mean_rays),
+                "copies": [{"dir": "d2h", "bytes": 20, "what": "the step's ray / sample / compacted / selected / still-active counters (pinned)"},
                            {"dir": "d2h", "bytes": int(4 * mean_rays), "what": "per-ray loss of the step (pinned), rays_per_batch x 4 B"},
                            {"dir": "d2h", "bytes": 4, "what": "occupied-cell count"}],
                 "note": "InstantNGP.train(1) per step on a twin model at the same steps as the timed region (wall clock, max over ranks). "

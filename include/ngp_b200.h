@@ -380,6 +380,17 @@ NGP_API int ngp_training_select_progressive(uint32_t rays_per_batch, const uint3
                                             const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
                                             uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, uint32_t* batch_rows,
                                             uint32_t* n_selected, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes, void* stream);
+/* The same with the first round's window chosen by the caller: round 0 evaluates the first
+ * first_window samples of every ray (ngp_training_select_progressive: 48), round 1 the rest of the
+ * rays still going; first_window = 0xFFFFFFFF evaluates every sample in one round.  The results
+ * do not depend on the window (each sample's density is the same value whichever round computes
+ * it); only the work does.  still_active (optional device word, cleared by the call): the number
+ * of rays still going after round 0, for choosing the next call's window. */
+NGP_API int ngp_training_select_progressive_window(uint32_t rays_per_batch, const uint32_t* ray_counter, const ngp_grid_layout* layout,
+                                                   const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
+                                                   uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, uint32_t* batch_rows,
+                                                   uint32_t* n_selected, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
+                                                   uint32_t first_window, uint32_t* still_active, void* stream);
 /* ngp_training_loss_compacted for the selection flow: network_output [samples][16] and coords
  * are indexed by sample (the kept samples' own positions); dloss_doutput by batch row.  scratch:
  * the one given to ngp_training_select_progressive. */

@@ -413,26 +413,16 @@ __global__ void __launch_bounds__(kCtaThreads) compact_copy_kernel(const __grid_
 // Progressive density evaluation.  A ray keeps its samples up to the first whose transmittance
 // drops below 1e-4; the samples behind that point need no density at all, yet they are most of
 // the marched samples.  So the densities are evaluated in rounds over growing sample windows
-// (kRoundEnd), each round only for the rays that have not stopped yet.  Each evaluated
+// (below), each round only for the rays that have not stopped yet.  Each evaluated
 // sample's density is the same value the full pass computes (rows are independent), so the
 // kept counts, and everything after them, are unchanged.
 // ---------------------------------------------------------------------------------------------
-// Round r evaluates samples [kRoundEnd[r-1], kRoundEnd[r]) of the rays still going (the last
-// round: all remaining samples).
-#ifndef NGP_KEEP_ROUND0
-#define NGP_KEEP_ROUND0 48
-#endif
-#ifndef NGP_KEEP_ROUND1
-#define NGP_KEEP_ROUND1 0  // > 0: a third round (measured slower: launch overhead)
-#endif
-#if NGP_KEEP_ROUND1 > 0
-#define NGP_KEEP_ROUND_LIST NGP_KEEP_ROUND0, NGP_KEEP_ROUND1, 0xFFFFFFFFu
-#else
-#define NGP_KEEP_ROUND_LIST NGP_KEEP_ROUND0, 0xFFFFFFFFu
-#endif
-constexpr uint32_t kRoundEnd[] = {NGP_KEEP_ROUND_LIST};
-constexpr uint32_t kRounds     = sizeof(kRoundEnd) / sizeof(kRoundEnd[0]);
-__constant__ uint32_t c_round_end[kRounds] = {NGP_KEEP_ROUND_LIST};
+// Two rounds: round 0 evaluates the first `first_window` samples of every ray (by default
+// kFirstWindow), round 1 all remaining samples of the rays still going.  A caller whose rays
+// rarely stop inside the first window (the first training steps, while every density is low)
+// passes first_window = all, and the evaluation takes one round.
+constexpr uint32_t kFirstWindow = 48u;
+constexpr uint32_t kAllSamples  = 0xFFFFFFFFu;
 constexpr uint32_t kListThreads = 256u;
 constexpr uint32_t kMlpWeights  = 10240u;  // packed MLP weights before the grid in the parameter vector
 
@@ -452,6 +442,9 @@ struct ProgressParams {
     uint32_t* rows;             // row list (sample indices)
     uint32_t* n_rows;           // device count of the row list
     uint32_t* block_totals;     // [ray blocks of kRaysPerCta] kept totals for the compaction
+    uint32_t first_window;      // samples per ray in round 0
+    uint32_t n_rounds;          // 1 (first_window covers every sample) or 2
+    uint32_t* still_active;     // optional: += the rays still going after round 0
 };
 
 __device__ __forceinline__ uint32_t progress_rays(const ProgressParams& p) {
@@ -461,8 +454,8 @@ __device__ __forceinline__ uint32_t progress_rays(const ProgressParams& p) {
 // Samples [lo, hi) of ray i evaluated in round `round` (empty once the ray has stopped).
 __device__ __forceinline__ void round_range(const ProgressParams& p, uint32_t round, uint32_t i, uint32_t& lo, uint32_t& hi) {
     const uint32_t steps = p.numsteps[2u * i];
-    lo                   = round == 0 ? 0u : min(c_round_end[round - 1], steps);
-    hi                   = (round == 0 || p.active[i]) ? min(c_round_end[round], steps) : lo;
+    lo                   = round == 0 ? 0u : min(p.first_window, steps);
+    hi                   = round == 0 ? min(p.first_window, steps) : (p.active[i] ? steps : lo);
 }
 
 // Per ray: its row count in this round, exclusive offsets within blocks of kListThreads rays.
@@ -546,7 +539,19 @@ __global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_co
             }
         }
     }
-    if (round + 1u < kRounds) return;
+    if (round + 1u < p.n_rounds) {
+        // rays still going after this round (one atomic per CTA)
+        if (p.still_active != nullptr) {
+            if (lane == 0) s_kept[warp] = (i < n && p.active[i]) ? 1u : 0u;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                uint32_t a = 0;
+                for (uint32_t w = 0; w < kRaysPerCta; ++w) a += s_kept[w];
+                if (a) atomicAdd(p.still_active, a);
+            }
+        }
+        return;
+    }
     if (lane == 0) s_kept[warp] = kept;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1064,9 +1069,10 @@ int progressive_rounds(ProgressParams& p, uint32_t R, const ngp_grid_layout* lay
     const uint32_t list_blocks = (R + kListThreads - 1) / kListThreads;
     p.density        = reinterpret_cast<const __half*>(full_out != nullptr ? full_out + 3 : density_out);
     p.density_stride = full_out != nullptr ? 16u : 1u;
-    for (uint32_t round = 0; round < kRounds; ++round) {
+    p.n_rounds = p.first_window == kAllSamples ? 1u : 2u;
+    for (uint32_t round = 0; round < p.n_rounds; ++round) {
         // rows of this round: at most its sample window per ray, and never more than all samples
-        const uint64_t window = static_cast<uint64_t>(kRoundEnd[round]) - (round == 0 ? 0u : kRoundEnd[round - 1]);
+        const uint64_t window = round == 0 ? p.first_window : static_cast<uint64_t>(kAllSamples) - p.first_window;
         const uint32_t bound  = static_cast<uint32_t>(std::min<uint64_t>(sample_bound, window * R));
         list_count_kernel<<<list_blocks, kListThreads, 0, s>>>(p, round);
         NGP_TRY(check_launch("list_count_kernel"));
@@ -1215,6 +1221,7 @@ extern "C" int ngp_training_compact_progressive(uint32_t rays_per_batch, const u
     const uint32_t R           = rays_per_batch;
     const uint32_t warp_blocks = (R + kRaysPerCta - 1) / kRaysPerCta;
     ProgressParams p{};
+    p.first_window = kFirstWindow;
     p.rays_per_batch = R;
     p.ray_counter    = ray_counter;
     p.numsteps       = numsteps;
@@ -1244,7 +1251,17 @@ extern "C" int ngp_training_select_progressive(uint32_t rays_per_batch, const ui
                                                const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
                                                uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, uint32_t* batch_rows,
                                                uint32_t* n_selected, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes, void* stream) {
+    return ngp_training_select_progressive_window(rays_per_batch, ray_counter, layout, params, coords, sample_bound, numsteps, enc, enc_stride, density,
+                                                  rows, batch_rows, n_selected, compacted_counter, scratch, scratch_bytes, kFirstWindow, nullptr, stream);
+}
+
+extern "C" int ngp_training_select_progressive_window(uint32_t rays_per_batch, const uint32_t* ray_counter, const ngp_grid_layout* layout,
+                                                      const uint16_t* params, const float* coords, uint32_t sample_bound, uint32_t* numsteps,
+                                                      uint16_t* enc, uint32_t enc_stride, uint16_t* density, uint32_t* rows, uint32_t* batch_rows,
+                                                      uint32_t* n_selected, uint32_t* compacted_counter, void* scratch, size_t scratch_bytes,
+                                                      uint32_t first_window, uint32_t* still_active, void* stream) {
     clear_error();
+    if (first_window == 0) return fail(NGP_ERR_INVALID, "progressive selection: the first window must hold at least one sample");
     if (rays_per_batch == 0) return NGP_OK;
     if (layout == nullptr || params == nullptr || coords == nullptr || numsteps == nullptr || enc == nullptr || density == nullptr || rows == nullptr ||
         batch_rows == nullptr || n_selected == nullptr || compacted_counter == nullptr || scratch == nullptr || (!rows_layout(enc_stride) && enc_stride < sample_bound))
@@ -1255,11 +1272,15 @@ extern "C" int ngp_training_select_progressive(uint32_t rays_per_batch, const ui
     const uint32_t R           = rays_per_batch;
     const uint32_t warp_blocks = (R + kRaysPerCta - 1) / kRaysPerCta;
     ProgressParams p{};
+    p.first_window = kFirstWindow;
     p.rays_per_batch = R;
     p.ray_counter    = ray_counter;
     p.numsteps       = numsteps;
     p.coords         = coords;
     progress_scratch(p, R, scratch, rows);
+    p.first_window = first_window;
+    p.still_active = first_window == kAllSamples ? nullptr : still_active;
+    if (still_active != nullptr) NGP_TRY(check_cuda(cudaMemsetAsync(still_active, 0, sizeof(uint32_t), s), "progressive selection: clear active count"));
     NGP_TRY(progressive_rounds(p, R, layout, params, coords, sample_bound, enc, enc_stride, density, nullptr, s));
     KeepParams k{};
     k.rays_per_batch = R;
@@ -1338,6 +1359,7 @@ extern "C" int ngp_eval_network_progressive(uint32_t n_rays, const ngp_grid_layo
     if (scratch_bytes < loss_scratch_size(n_rays)) return fail(NGP_ERR_INVALID, "progressive evaluation: scratch too small");
     if (reinterpret_cast<uintptr_t>(scratch) % 16u != 0) return fail(NGP_ERR_INVALID, "progressive evaluation: scratch must be 16-byte aligned");
     ProgressParams p{};
+    p.first_window = kFirstWindow;
     p.rays_per_batch = n_rays;
     p.numsteps       = numsteps;
     p.coords         = coords;

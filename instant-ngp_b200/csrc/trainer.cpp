@@ -183,7 +183,8 @@ struct ngp_trainer {
     // optimizer run (marching reads only the bitfield, which changes only on grid-update steps).
     cudaStream_t march_stream = nullptr;
     cudaEvent_t ev_counts = nullptr, ev_march = nullptr;
-    uint32_t* host_counters = nullptr;  // pinned copy of counters 0..2
+    uint32_t* host_counters = nullptr;  // pinned copy of counters 0..4
+    bool one_round          = false;    // progressive evaluation in one round (see train_step)
     float* host_loss        = nullptr;  // pinned copy of the last step's per-ray loss [BATCH]
     bool premarched         = false;    // step `step` was marched on march_stream
     // Adam: bias-corrected rate per step count, entries [1, lr_table_len] filled
@@ -495,9 +496,12 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     const MarchSet& m = t->sets[t->step & 1u];
 #if NGP_SELECT
     // the batch is a list of the kept samples' rows; the samples stay in place
-    NGP_TRY(ngp_training_select_progressive(t->rays_per_batch, m.counters + 0, &t->layout, t->params, m.coords, t->inference_samples, m.numsteps,
-                                            t->enc, t->inference_samples, t->dens, t->rows, t->batch_rows, m.counters + 3, m.counters + 2,
-                                            t->loss_scratch, t->loss_scratch_bytes, t->stream));
+    // one evaluation round when most rays outlived the first window in the previous step
+    // (the first steps: low densities stop few rays); the selection is the same either way
+    NGP_TRY(ngp_training_select_progressive_window(t->rays_per_batch, m.counters + 0, &t->layout, t->params, m.coords, t->inference_samples,
+                                                   m.numsteps, t->enc, t->inference_samples, t->dens, t->rows, t->batch_rows, m.counters + 3,
+                                                   m.counters + 2,
+                                            t->loss_scratch, t->loss_scratch_bytes, t->one_round ? 0xFFFFFFFFu : 48u, m.counters + 4, t->stream));
 #else
     NGP_TRY(ngp_training_compact_progressive(t->rays_per_batch, m.counters + 0, &t->layout, t->params, m.coords, t->inference_samples, m.numsteps,
                                              t->enc, t->inference_samples, t->dens, t->rows, t->ccoords, t->cenc, m.counters + 2, t->loss_scratch,
@@ -505,7 +509,7 @@ int train_step(ngp_trainer* t, bool premarch_next) {
 #endif
     // the step's counters are final here: the host reads them (for the next step's batch size)
     // while the rest of the step runs
-    NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, m.counters, 3 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
+    NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_counters, m.counters, 5 * sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read counters"));
     NGP_TRY(check_cuda(cudaEventRecord(t->ev_counts, t->stream), "record counters"));
     mark(t, 3);
     // the full network on the kept samples, then compositing, loss and padding (1944-1956)
@@ -543,6 +547,10 @@ int train_step(ngp_trainer* t, bool premarch_next) {
     const uint32_t c[3] = {t->host_counters[0], t->host_counters[1], t->host_counters[2]};
     t->measured_before  = c[1];
     t->measured         = c[2];
+    // rays still going after the first evaluation window (counter 4; 0 after a one-round step,
+    // which keeps the next step on one round only while at least 70 % of the rays outlived it)
+    if (!t->one_round) t->one_round = static_cast<uint64_t>(t->host_counters[4]) * 10u >= static_cast<uint64_t>(c[0]) * 7u && c[0] > 0;
+    else if (t->step % 16u == 15u) t->one_round = false;  // look again every 16 steps
     if (t->measured == 0u) {
         cudaMemcpy(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost);
         return fail(NGP_ERR_STATE, "Training stopped unexpectedly. density_grid_occupied_cells=" + std::to_string(t->occupied_cells));
@@ -772,7 +780,7 @@ extern "C" int ngp_trainer_create(const ngp_trainer_config* cfg, const ngp_split
 #endif
         NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_counts, cudaEventDisableTiming), "event"));
         NGP_TRY(check_cuda(cudaEventCreateWithFlags(&t->ev_march, cudaEventDisableTiming), "event"));
-        NGP_TRY(check_cuda(cudaMallocHost(&t->host_counters, 4 * sizeof(uint32_t)), "pinned counters"));
+        NGP_TRY(check_cuda(cudaMallocHost(&t->host_counters, 8 * sizeof(uint32_t)), "pinned counters"));
         NGP_TRY(check_cuda(cudaMallocHost(&t->host_loss, kNetworkBatch * sizeof(float)), "pinned loss"));
         NGP_TRY(upload_split(t->train, train, "train"));
         NGP_TRY(upload_split(t->val, validation, "validation"));

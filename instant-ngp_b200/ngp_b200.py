@@ -367,6 +367,19 @@ def training_select_progressive(rays_per_batch, ray_counter, layout, params, coo
            "ngp_training_select_progressive")
 
 
+def training_select_progressive_window(rays_per_batch, ray_counter, layout, params, coords, sample_bound, numsteps, enc, density, rows, batch_rows,
+                                       n_selected, compacted_counter, scratch, first_window, still_active=None, enc_stride=None,
+                                       stream=None) -> None:
+    """training_select_progressive with the first round's window (0xFFFFFFFF: one round)."""
+    _check(lib().ngp_training_select_progressive_window(_u32(rays_per_batch), _ptr(ray_counter), ctypes.byref(layout), _ptr(params), _ptr(coords),
+                                                        _u32(sample_bound), _ptr(numsteps), _ptr(enc),
+                                                        _u32(enc.shape[1] if enc_stride is None else enc_stride), _ptr(density), _ptr(rows),
+                                                        _ptr(batch_rows), _ptr(n_selected), _ptr(compacted_counter), _ptr(scratch),
+                                                        ctypes.c_size_t(scratch.numel() * scratch.element_size()), _u32(first_window),
+                                                        _ptr(still_active), _stream(stream)),
+           "ngp_training_select_progressive_window")
+
+
 def training_loss_selected_kind(rays_per_batch, step, ray_counter, pixels, frame_count, width, height, network_output, ray_indices, rays, numsteps,
                                 coords, dloss, loss_values, scratch, loss_kind, stream=None) -> None:
     _check(lib().ngp_training_loss_selected_kind(_u32(rays_per_batch), _u32(step), _ptr(ray_counter), _ptr(pixels), _u32(frame_count), _u32(width),

@@ -767,3 +767,48 @@ def test_density_forward_splat_equals_forward_then_splat(ngp):
     torch.cuda.synchronize()
     assert (a > 0).sum().item() > 0.3 * n
     assert a.cpu().numpy().tobytes() == b.cpu().numpy().tobytes()
+
+
+def test_selection_does_not_depend_on_the_first_window(ngp, small_scene, blob_bitfield):
+    """ngp_training_select_progressive_window: one round (window = all samples), the default 48
+    and a narrow 5-sample window select the same batch (rows, counts, compacted counter,
+    numsteps); still_active counts the rays that outlive the first window."""
+    import torch
+
+    pix, cam, tr = _scene_tensors(small_scene)
+    F, H, W = tr["pixels"].shape[:3]
+    bits = T(blob_bitfield)
+    n, limit, step = 12288, 1 << 21, 8
+    rows_n = ngp.compacted_rows()
+    (fx, fy), (cx, cy) = tr["focal"], tr["principal"]
+    layout = ngp.grid_layout(16, 2, 19, 16, math.log2(128.0) / 15.0)
+    _, table, _ = workloads.encode_inputs(1, layout.n_params, 16, 2, seed=4)
+    table = (table.astype(np.float32) * 2e4).astype(np.float16)
+    params = T(np.concatenate([workloads.xavier_mlp_params(9), table]).view(np.int16))
+    ns = torch.zeros((n, 2), dtype=torch.int32, device="cuda")
+    rays = torch.zeros((n, 6), dtype=torch.float32, device="cuda")
+    ridx = torch.zeros(n, dtype=torch.int32, device="cuda")
+    coords = torch.zeros((limit, 7), dtype=torch.float32, device="cuda")
+    msc = torch.zeros(ngp.march_scratch_words(n), dtype=torch.int32, device="cuda")
+    rc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ngp.march_training_rays(cam, F, W, H, fx, fy, cx, cy, step, n, limit, bits, coords, rays, ridx, ns, msc, rc, sc)
+    torch.cuda.synchronize()
+    m = (int(sc.item()) + 127) // 128 * 128
+    out = {}
+    for window in (0xFFFFFFFF, 48, 5):
+        z = lambda dtype, *shape: torch.zeros(shape, dtype=dtype, device="cuda")  # noqa: E731
+        ns_w, cc, nsel, active = ns.clone(), z(torch.int32, 1), z(torch.int32, 1), z(torch.int32, 1)
+        active.fill_(12345)
+        enc, dens, rows, brows = z(torch.float16, 32, m), z(torch.float16, m), z(torch.int32, m), z(torch.int32, rows_n)
+        scratch = z(torch.uint8, ngp.loss_scratch_bytes(n))
+        ngp.training_select_progressive_window(n, rc, layout, params, coords, m, ns_w, enc, dens, rows, brows, nsel, cc, scratch, window, active)
+        torch.cuda.synchronize()
+        out[window] = (ns_w.cpu().numpy(), int(cc.item()), int(nsel.item()), brows[: int(nsel.item())].cpu().numpy(), int(active.item()))
+    a = out[0xFFFFFFFF]
+    for window in (48, 5):
+        b = out[window]
+        assert (a[0] == b[0]).all() and a[1] == b[1] and a[2] == b[2] and np.array_equal(a[3], b[3])
+    assert a[4] == 0  # one round: nothing left for a second
+    rays_n = int(rc.item())
+    assert 0 < out[5][4] <= rays_n and out[48][4] <= out[5][4]
