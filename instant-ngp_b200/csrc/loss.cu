@@ -513,13 +513,17 @@ __global__ void __launch_bounds__(kCtaThreads) keep_round_kernel(const __grid_co
                 d            = v ? __half2float(dens[static_cast<uint64_t>(j) * p.density_stride]) : 0.0f;
                 dt           = v ? c[static_cast<uint64_t>(j) * 7u + 3u] : 0.0f;
             };
-            float d_next, dt_next;
-            load(lo + lane, d_next, dt_next);
+            // (three chunks in flight: a long ray's chunks are short to walk but far from the SM)
+            float d1, dt1, d2, dt2, d3, dt3;
+            load(lo + lane, d1, dt1);
+            load(lo + 32u + lane, d2, dt2);
+            load(lo + 64u + lane, d3, dt3);
             for (uint32_t c0 = lo; c0 < hi; c0 += 32u) {
                 const uint32_t j  = c0 + lane;
                 const bool valid  = j < hi;
-                const float d = d_next, dt = dt_next;
-                load(j + 32u, d_next, dt_next);
+                const float d = d1, dt = dt1;
+                d1 = d2, dt1 = dt2, d2 = d3, dt2 = dt3;
+                load(j + 96u, d3, dt3);
                 const float alpha = valid ? 1.0f - __expf(-expf(d) * dt) : 0.0f;
                 const float Tb    = prefix_transmittance(T, 1.0f - alpha, min(32u, hi - c0));
                 const bool keep   = valid && !(Tb < kTransmittanceEps);
