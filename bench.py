@@ -245,12 +245,17 @@ def train_roofline(phases: dict, grid: dict, peaks: dict, l2: dict | None) -> di
     return res
 
 
-def _trained_twin(ngp, ds, cfg, world, warmup):
-    """A trainer at step `warmup`: every twin built from the same dataset and config takes the same
-    steps (the training is deterministic), so timed, end-to-end and profiled runs cover equal work."""
+def _trained_twin(ngp, ds, cfg, world, warmup, run_ahead=False):
+    """A trainer at step `warmup`: every twin built from the same dataset and config runs the same
+    step schedule (grid updates, batch sizes; the values differ only by the order of fp32 atomic
+    sums), so timed, end-to-end and profiled runs cover equal work.  The device-timed twins run
+    without run-ahead, so that a train(K) call's events hold every kernel of its K steps; the
+    end-to-end twin keeps the library's default (run-ahead on)."""
     model = ngp.InstantNGP(ds, cfg)
     if world > 1:
         model.join_process_group()
+    if not run_ahead:
+        model.set_run_ahead(False)
     model.train(warmup)
     return model
 
@@ -315,7 +320,7 @@ def bench_train_ours(args, rank, world, local):
     model.close()
     # end to end through the public API, on a twin at the same steps: one train(1) call per step,
     # each reading back the step's counters and per-ray loss; wall clock, max over ranks
-    twin = _trained_twin(ngp, ds, cfg, world, args.warmup)
+    twin = _trained_twin(ngp, ds, cfg, world, args.warmup, run_ahead=True)
     torch.cuda.synchronize()
     barrier(world)
     t0 = time.perf_counter()

@@ -610,6 +610,15 @@ NGP_API int ngp_trainer_set_loss(ngp_trainer* t, int loss_kind);
  * 4 network backward, 5 encoding backward, 6 gradient exchange (fp16 conversion +
  * reduce-scatter), 7 Adam (+ all-gather of the fp16 parameters).  out_ms needs 8 floats;
  * out_mean_inference_samples = mean marched samples per step. */
+/* Run-ahead (on by default; no counterpart in the reference): when the step after a train call
+ * updates the density grid, the call leaves that update's first half (samples, encoding, density
+ * network and splat into internal scratch) running on the GPU when it returns, so the GPU is not
+ * idle while the host enters the next call; the next step completes the update.  Nothing a caller
+ * can observe changes before that step.  A call's elapsed_ms then covers its steps without the
+ * first half of its first step's update when the previous call ran it ahead: turn it off (which
+ * also drops work already run ahead) to time exactly the work of a call's steps. */
+NGP_API int ngp_trainer_set_run_ahead(ngp_trainer* t, int enable);
+
 NGP_API int ngp_trainer_set_profiling(ngp_trainer* t, int enable);
 NGP_API int ngp_trainer_phase_times(const ngp_trainer* t, float* out_ms, uint32_t n, uint32_t* out_steps, float* out_mean_inference_samples);
 /* Profiled grid updates (no reference counterpart; update_density_grid, ngp.train.cu:1526-1595,

@@ -29,6 +29,7 @@ using namespace ngp;
 
 namespace {
 
+constexpr uint32_t kNoStep     = 0xFFFFFFFFu;
 constexpr uint32_t kMlpParams  = 10240;
 constexpr int kTrainPhases     = 8;  // see ngp_trainer_phase_times
 constexpr int kGridPhases      = 5;  // see ngp_trainer_grid_phase_times
@@ -185,6 +186,9 @@ struct ngp_trainer {
     cudaEvent_t ev_counts = nullptr, ev_march = nullptr;
     uint32_t* host_counters = nullptr;  // pinned copy of counters 0..4
     bool one_round          = false;    // progressive evaluation in one round (see train_step)
+    uint32_t grid_begun     = 0xFFFFFFFFu;  // step whose grid update's first half is already enqueued
+    uint32_t grid_samples_pending = 0;      // samples of the update begun last
+    bool run_ahead          = true;         // see begin_next_grid_update
     float* host_loss        = nullptr;  // pinned copy of the last step's per-ray loss [BATCH]
     bool premarched         = false;    // step `step` was marched on march_stream
     // Adam: bias-corrected rate per step count, entries [1, lr_table_len] filled
@@ -313,21 +317,11 @@ void grid_mark(ngp_trainer* t, int k) {
     if (t->profiling) cudaEventRecord(t->grid_marks[k], t->stream);
 }
 
-// update_density_grid (ngp.train.cu:1526-1595).
-int update_grid(ngp_trainer* t) {
-    if (!grid_update_due(t->step)) return NGP_OK;
-    if (t->grid_events_used == t->grid_events.size()) {
-        cudaEvent_t e0 = nullptr, e1 = nullptr;
-        NGP_TRY(check_cuda(cudaEventCreate(&e0), "grid timing event"));
-        if (const int st = check_cuda(cudaEventCreate(&e1), "grid timing event"); st != NGP_OK) {
-            cudaEventDestroy(e0);
-            return st;
-        }
-        t->grid_events.emplace_back(e0, e1);
-    }
-    const auto& ev = t->grid_events[t->grid_events_used++];
-    cudaEventRecord(ev.first, t->stream);
-    grid_mark(t, 0);
+// First half of a grid update: the samples, their encodings and the density network with the
+// splat into the grid scratch.  It writes only internal buffers (encodings, cell indices, grid
+// samples and the scratch the previous update's bitfield pass cleared), so it can run ahead of
+// the step that completes the update (begin_next_grid_update).
+int grid_update_begin(ngp_trainer* t) {
     const Split& s = t->train;
     if (t->step == 0) {
         t->ema_step = 0;
@@ -354,11 +348,37 @@ int update_grid(ngp_trainer* t) {
     // density network with the splat (K3) in its epilogue: scratch[cell] = max(..., exp(d) * dt)
     NGP_TRY(ngp_density_forward_splat(n, t->params, t->enc, n, t->grid_indices, t->grid_scratch, t->stream));
     grid_mark(t, 3);
+    t->grid_samples_pending = n;
+    return NGP_OK;
+}
+
+// update_density_grid (ngp.train.cu:1526-1595).
+int update_grid(ngp_trainer* t) {
+    if (!grid_update_due(t->step)) return NGP_OK;
+    const bool begun = t->grid_begun == t->step;  // the first half ran at the end of the last train call
+    t->grid_begun    = kNoStep;
+    cudaEvent_t ev_end = nullptr;
+    if (!begun) {
+        if (t->grid_events_used == t->grid_events.size()) {
+            cudaEvent_t e0 = nullptr, e1 = nullptr;
+            NGP_TRY(check_cuda(cudaEventCreate(&e0), "grid timing event"));
+            if (const int st = check_cuda(cudaEventCreate(&e1), "grid timing event"); st != NGP_OK) {
+                cudaEventDestroy(e0);
+                return st;
+            }
+            t->grid_events.emplace_back(e0, e1);
+        }
+        const auto& ev = t->grid_events[t->grid_events_used++];
+        cudaEventRecord(ev.first, t->stream);
+        ev_end = ev.second;
+        grid_mark(t, 0);
+        NGP_TRY(grid_update_begin(t));
+    }
     grid_mark(t, 4);
     NGP_TRY(ngp_density_grid_update(t->grid_values, t->grid_scratch, 0.95f, t->grid_partial, t->grid_mean, t->bitfield, t->occupied, t->stream));
     grid_mark(t, 5);
     ++t->ema_step;
-    cudaEventRecord(ev.second, t->stream);
+    if (ev_end != nullptr) cudaEventRecord(ev_end, t->stream);
     if (t->profiling) {
         NGP_TRY(check_cuda(cudaEventSynchronize(t->grid_marks[kGridPhases]), "grid update"));
         for (int k = 0; k < kGridPhases; ++k) {
@@ -366,10 +386,29 @@ int update_grid(ngp_trainer* t) {
             cudaEventElapsedTime(&ms, t->grid_marks[k], t->grid_marks[k + 1]);
             t->grid_phase_ms[k] += ms;
         }
-        t->grid_samples_sum += n;
+        t->grid_samples_sum += t->grid_samples_pending;
         ++t->profiled_grid_updates;
     }
     return NGP_OK;
+}
+
+// At the end of a train call: when the next step updates the density grid, its first half goes
+// onto the stream now, behind the call's last optimizer step, so that the GPU has that work while
+// the host returns from this call and enters the next one.  Its results are consumed by the next
+// step; set_params discards them.  (Not while profiling: the phase marks time whole updates.)
+int begin_next_grid_update(ngp_trainer* t) {
+    if (!t->run_ahead || t->profiling || t->step == 0 || !grid_update_due(t->step) || t->grid_begun == t->step) return NGP_OK;
+    NGP_TRY(grid_update_begin(t));
+    t->grid_begun = t->step;
+    return NGP_OK;
+}
+
+// Drops a grid-update first half enqueued ahead (the parameters changed, or its phase marks are
+// wanted): the scratch it splatted into is cleared again, and the step redoes it.
+int discard_grid_begin(ngp_trainer* t) {
+    if (t->grid_begun == kNoStep) return NGP_OK;
+    t->grid_begun = kNoStep;
+    return check_cuda(cudaMemsetAsync(t->grid_scratch, 0, sizeof(float) * kGridCells, t->stream), "discard grid update");
 }
 
 // Adds the finished grid updates' durations to grid_update_ms.
@@ -1042,7 +1081,15 @@ extern "C" int ngp_trainer_train(ngp_trainer* t, int32_t iters, ngp_train_stats*
     cudaEventRecord(e1, t->stream);
     NGP_TRY(check_cuda(cudaMemcpyAsync(t->host_loss, t->loss_values, sizeof(float) * loss_rays, cudaMemcpyDeviceToHost, t->stream), "read loss"));
     NGP_TRY(check_cuda(cudaMemcpyAsync(&t->occupied_cells, t->occupied, sizeof(uint32_t), cudaMemcpyDeviceToHost, t->stream), "read occupied"));
-    NGP_TRY(wait_stream(t, t->stream, "train"));
+    cudaEvent_t e2 = nullptr;
+    NGP_TRY(check_cuda(cudaEventCreateWithFlags(&e2, cudaEventDisableTiming), "train event"));
+    cudaEventRecord(e2, t->stream);
+    // the next step's grid-update first half runs while the host returns (it is not waited for)
+    const int begun = begin_next_grid_update(t);
+    const int waited = wait_event(t, e2, "train");
+    cudaEventDestroy(e2);
+    NGP_TRY(begun);
+    NGP_TRY(waited);
     if (t->peer_exchange) {
         uint32_t status = 0;
         NGP_TRY(check_cuda(cudaMemcpy(&status, t->peer_status, sizeof(status), cudaMemcpyDeviceToHost), "peer exchange status"));
@@ -1173,6 +1220,13 @@ extern "C" int ngp_trainer_get_grid(const ngp_trainer* t, uint8_t* bitfield_host
     return NGP_OK;
 }
 
+extern "C" int ngp_trainer_set_run_ahead(ngp_trainer* t, int enable) {
+    clear_error();
+    if (t == nullptr) return fail(NGP_ERR_INVALID, "run ahead: null trainer");
+    t->run_ahead = enable != 0;
+    return enable ? NGP_OK : discard_grid_begin(t);
+}
+
 extern "C" int ngp_trainer_set_profiling(ngp_trainer* t, int enable) {
     clear_error();
     if (t == nullptr) return fail(NGP_ERR_INVALID, "profiling: null trainer");
@@ -1180,6 +1234,7 @@ extern "C" int ngp_trainer_set_profiling(ngp_trainer* t, int enable) {
         for (cudaEvent_t& e : t->marks) NGP_TRY(check_cuda(cudaEventCreate(&e), "profiling events"));
         for (cudaEvent_t& e : t->grid_marks) NGP_TRY(check_cuda(cudaEventCreate(&e), "profiling events"));
     }
+    if (enable) NGP_TRY(discard_grid_begin(t));  // profiled updates are timed whole
     t->profiling = enable != 0;
     for (double& v : t->phase_ms) v = 0.0;
     for (double& v : t->grid_phase_ms) v = 0.0;

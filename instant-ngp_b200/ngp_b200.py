@@ -689,6 +689,11 @@ class InstantNGP:
 
     PHASES = ("grid_update", "march", "inference_compact", "mlp_fwd_loss_pad", "mlp_bwd", "encode_bwd", "exchange", "adam")
 
+    def set_run_ahead(self, enable: bool = True) -> None:
+        """Run-ahead of the next step's grid-update first half when a train call returns (default
+        on); off: a call's elapsed_ms covers exactly the work of its steps."""
+        _check(lib().ngp_trainer_set_run_ahead(self.handle, ctypes.c_int(1 if enable else 0)), "ngp_trainer_set_run_ahead")
+
     def set_profiling(self, enable: bool = True) -> None:
         _check(lib().ngp_trainer_set_profiling(self.handle, ctypes.c_int(1 if enable else 0)), "ngp_trainer_set_profiling")
 

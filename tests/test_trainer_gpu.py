@@ -67,3 +67,24 @@ def test_comparison_image_and_render(ngp, scene):
     r = (rgb.cpu().numpy().reshape(128, 128, 3) * 255.0 + 0.5).astype(np.uint8)
     assert np.abs(r.astype(int) - img[:, 128:].astype(int)).max() <= 1
     m.close()
+
+
+def test_step_by_step_calls_match_one_call(ngp, scene):
+    """train(1) called 40 times (each call leaves the next step's grid-update first half running
+    when it returns; a test() between calls reads the grid and network in between) trains like
+    one train(40) call.  Training is not bitwise repeatable (fp32 atomics sum the grid gradients
+    in any order; two train(40) runs differ too), so the check is on the statistics and the test
+    PSNR."""
+    a = ngp.InstantNGP(scene, ngp.config0_trainer_config())
+    b = ngp.InstantNGP(scene, ngp.config0_trainer_config())
+    sa = a.train(40)
+    for k in range(40):
+        sb = b.train(1)
+        if k == 20:
+            b.test()
+    assert sa["step"] == sb["step"] == 40
+    assert sa["measured_sample_count"] == sb["measured_sample_count"]
+    assert abs(sa["density_grid_occupancy_ratio"] - sb["density_grid_occupancy_ratio"]) < 0.01
+    assert abs(a.test()["psnr"] - b.test()["psnr"]) < 0.5
+    a.close()
+    b.close()
