@@ -5,9 +5,11 @@ by oracle/train_replay.inc) runs once on the reference's ngp.train.cu and once o
 Sample placement differs (ray order vs atomic order) and gradients are summed in fp32 instead of
 fp16, so the runs are compared statistically:
 * on a small scene the adaptive batch settles to similar ray and sample counts (within 0.6-1.7x);
-* on the config-3 scene (100 train / 20 test views of 800 x 800), over three scenes (seeds) and
+* on the config-3 scene (100 train / 20 test views of 800 x 800), over five scenes (seeds) and
   2000 steps each, the drop-in layer's mean test PSNR is at least the reference's minus 0.2 dB
-  (north_star: final PSNR within 0.2 dB)."""
+  (north_star: final PSNR within 0.2 dB).  Neither run is bitwise repeatable (atomic sums in
+  any order), and single scenes differ by up to about 0.5 dB either way, so the bar is on the
+  mean over five scenes."""
 from __future__ import annotations
 
 import numpy as np
@@ -43,11 +45,11 @@ def test_reference_loop_on_drop_in_layer_settles_alike(reflib):
     assert our_psnr > 15.0
 
 
-def test_drop_in_layer_psnr_within_0p2_db_over_three_scenes(reflib):
+def test_drop_in_layer_psnr_within_0p2_db_over_five_scenes(reflib):
     from oracle import REF_SO, SHIM_REPLAY_SO
 
     ours, ref = [], []
-    for seed in (3, 13, 23):
+    for seed in (3, 13, 23, 33, 43):
         scene = workloads.procedural_dataset(n_train=100, n_test=20, width=800, height=800, seed=seed, device="cuda")
         ref.append(_replay(REF_SO, scene, 2000)[1])
         ours.append(_replay(SHIM_REPLAY_SO, scene, 2000)[1])
