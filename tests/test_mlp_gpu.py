@@ -234,3 +234,27 @@ def test_gradients_to_half_rounds_and_clears(ngp, n):
     assert rc == 0
     assert torch.equal(out.view(torch.int16), want.view(torch.int16))
     assert int(torch.count_nonzero(g)) == 0
+
+
+@pytest.mark.parametrize("rows", [False, True], ids=["contiguous", "row-list"])
+def test_density_forward_many_tiles_equals_full_network_channel(ngp, rows):
+    """The density network alone at 2^20 rows (many tiles per CTA: the input ring and the
+    register prefetch wrap around) equals channel 3 of the full network, bit for bit, for
+    contiguous rows and for a row list."""
+    import torch
+
+    n = 1 << 20
+    params = _t(workloads.xavier_mlp_params(7))
+    x_h, c_h, _ = workloads.mlp_inputs(n, seed=17)
+    x, coords = _t(x_h), _t(c_h)
+    full = torch.zeros((n, 16), dtype=torch.float16, device="cuda")
+    ngp.mlp_forward(params, x, coords, full)
+    dens = torch.zeros(n, dtype=torch.float16, device="cuda")
+    if rows:
+        perm = torch.randperm(n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3)).to(torch.int32)
+        cnt = torch.tensor([n], dtype=torch.int32, device="cuda")
+        ngp.density_forward_rows(n, perm, cnt, params, x, n, dens)
+    else:
+        ngp.density_forward(params, x, dens)
+    torch.cuda.synchronize()
+    assert torch.equal(dens.view(torch.int16), full[:, 3].contiguous().view(torch.int16))
